@@ -1,0 +1,326 @@
+"""Benchmark of the B200 Needle-3 token loop (one JSON line on rank 0).
+
+Workload (the reference's batched-decoding configuration): the synthetic
+depth-20 Needle-3 archive (seed 0), 256 independent sequences per GPU with
+prompt lengths uniform in [128, 1024] (seeded per rank), greedy decoding. A
+step is one batched decode step of every sequence on the GPU: tied logits,
+argmax, and the forward pass of the chosen tokens through all 20 layers with
+the paged int8 KV cache. Sequences are sharded across ranks with no
+collective on the data path (weak scaling).
+
+  value  tokens/s of the whole job, from CUDA events on the library's stream
+         around K device-resident steps (max over ranks)
+  e2e    the same through nb_batch_step with host buffers: per step the
+         host->device staging of the step's metadata and the device->host
+         read of the chosen tokens are inside the timed region
+  batch1 the batch-1 configuration: depth 20, a 512-token prompt (prefill ms)
+         and masked greedy steps (a seeded ~5% allowed bitset each step)
+  roofline  the attention kernel (the HBM-bound dominant kernel) against the
+         measured HBM copy bandwidth
+  cpu_baseline  the CPU restatement's float path (what the reference runs on
+         an x86 host) on a bounded sample of the same workload
+
+`--impl reference` times that CPU path alone on the host cores.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+SEQS_PER_GPU = 256
+PROMPT_RANGE = (128, 1024)
+DEPTH = 20
+METRIC = "decode tokens/s (depth-20 Needle-3, 256 sequences per GPU, greedy)"
+UNIT = "tokens/s"
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=32)
+    p.add_argument("--warmup", type=int, default=4)
+    p.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    p.add_argument("--seqs", type=int, default=SEQS_PER_GPU)
+    p.add_argument("--no-batch1", action="store_true")
+    p.add_argument("--no-cpu", action="store_true")
+    p.add_argument("--profile", action="store_true", help="small setup for ncu captures")
+    return p.parse_args()
+
+
+def prompts(rank: int, count: int):
+    rng = np.random.default_rng(1000 + rank)
+    lengths = rng.integers(PROMPT_RANGE[0], PROMPT_RANGE[1] + 1, count)
+    return [rng.integers(10, 8000, n).astype(np.uint32) for n in lengths]
+
+
+def measured_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return json.load(f), "measured"
+    except OSError:
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}, "fallback"
+
+
+class Clocks:
+    """nvidia-smi samples during the timed region."""
+
+    def __init__(self, device: int):
+        self.device = device
+        self.proc = None
+        self.path = tempfile.mktemp(suffix=".csv")
+
+    def __enter__(self):
+        query = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+                 "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+                 "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.out = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.device), f"--query-gpu={query}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"], stdout=self.out,
+                                         stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc:
+            time.sleep(0.25)
+            self.proc.terminate()
+            self.proc.wait()
+            self.out.close()
+
+    def summary(self):
+        if not self.proc:
+            return None
+        rows = []
+        with open(self.path) as f:
+            for line in f:
+                parts = [x.strip() for x in line.split(",")]
+                if len(parts) >= 9 and parts[1].isdigit():
+                    rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return None
+        sm = [int(r[1]) for r in rows]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": int(rows[0][2]), "reasons": reasons,
+                "samples": len(rows)}
+
+
+def launches_per_step(depth: int) -> int:
+    # logits prep + product, select, embed, 7 per layer, final norm, advance
+    return 2 + 1 + 1 + 7 * depth + 1 + 1
+
+
+def cpu_baseline(archive: str, rank_prompts, threads: int, steps: int = 2, sample: int = 8):
+    from oracle import oracle
+
+    model = oracle.Model.open(archive, oracle.MODE_FLOAT, threads)
+    sessions = []
+    for ids in rank_prompts[:sample]:
+        s = oracle.Session(model)
+        s.feed(ids)
+        sessions.append(s)
+    tokens = np.array([oracle.argmax(s.logits()) for s in sessions], dtype=np.uint32)
+    oracle.sessions_step(sessions, tokens, threads)  # warm-up step
+    start = time.perf_counter()
+    for _ in range(steps):
+        logits = oracle.sessions_step(sessions, tokens, threads)
+        tokens = np.argmax(logits, axis=1).astype(np.uint32)
+    elapsed = time.perf_counter() - start
+    return {"value": len(sessions) * steps / elapsed, "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"{len(sessions)} of the rank's sequences (prompts {min(len(p) for p in rank_prompts[:sample])}-"
+                      f"{max(len(p) for p in rank_prompts[:sample])} tokens, prefill untimed), {steps} decode steps each, "
+                      f"oracle FLOAT mode (the reference's x86 float kernels) with one sequence per thread"}
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from rustyneedle_b200 import synthetic
+
+    archive = synthetic.cached_archive(seed=0)
+    threads = os.cpu_count() or 1
+    from oracle import oracle
+
+    oracle.build()
+    model = oracle.Model.open(archive, oracle.MODE_FLOAT, threads)
+    sample = min(16, args.seqs)
+    sessions = []
+    for ids in prompts(0, args.seqs)[:sample]:
+        s = oracle.Session(model)
+        s.feed(ids)
+        sessions.append(s)
+    tokens = np.array([oracle.argmax(s.logits()) for s in sessions], dtype=np.uint32)
+    for _ in range(args.warmup):
+        tokens = np.argmax(oracle.sessions_step(sessions, tokens, threads), axis=1).astype(np.uint32)
+    start = time.perf_counter()
+    for _ in range(args.steps):
+        tokens = np.argmax(oracle.sessions_step(sessions, tokens, threads), axis=1).astype(np.uint32)
+    elapsed = time.perf_counter() - start
+    value = sample * args.steps / elapsed
+    line = {"metric": METRIC, "value": value, "unit": UNIT, "impl": "reference", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * elapsed / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic", "config": {"workload": "config2: depth-20 synthetic Needle-3, greedy decode",
+                                            "sequences_timed": sample, "prompt_tokens": list(PROMPT_RANGE)},
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
+                             "sample": f"{sample} sequences of the workload, one decode step of each per step, "
+                                       "prefill untimed; oracle FLOAT mode (the reference's x86 float kernels)"},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        return run_reference(args)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dist = None
+    if world > 1:
+        import torch
+        import torch.distributed as dist_mod
+        from datetime import timedelta
+
+        torch.cuda.set_device(local)
+        dist_mod.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=torch.device("cuda", local))
+        dist = dist_mod
+
+    import rustyneedle_b200 as nb
+    from rustyneedle_b200 import debug, synthetic
+
+    archive = synthetic.cached_archive(seed=0)
+    seqs = 8 if args.profile else args.seqs
+    model = nb.Model.open(archive, device=local, max_sessions=seqs + 2)
+    if DEPTH != model.config.num_layers:
+        model = model.with_depth(DEPTH)
+    rank_prompts = prompts(rank, seqs)
+    t0 = time.perf_counter()
+    sessions = []
+    for ids in rank_prompts:
+        s = nb.Session(model)
+        s.feed(ids)
+        sessions.append(s)
+    setup_s = time.perf_counter() - t0
+    batch = nb.Batch(model, sessions)
+
+    def barrier():
+        if dist:
+            dist.barrier()
+
+    def max_over_ranks(x: float) -> float:
+        if not dist:
+            return x
+        import torch
+
+        t = torch.tensor([x], dtype=torch.float64, device=f"cuda:{local}")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    batch.run(args.warmup)
+    barrier()
+    with Clocks(local) as clocks:
+        ms = batch.run(args.steps)
+    barrier()
+    ms = max_over_ranks(ms)
+    total_tokens = seqs * world * args.steps
+    value = total_tokens / (ms / 1000.0)
+
+    # end to end through the public C ABI with host buffers
+    batch.step()
+    barrier()
+    start = time.perf_counter()
+    for _ in range(args.steps):
+        batch.step()
+    e2e_s = max_over_ranks(time.perf_counter() - start)
+    e2e = {"value": seqs * world * args.steps / e2e_s, "unit": UNIT, "h2d_bytes_per_step": seqs * (16 + 4 + 4),
+           "d2h_bytes_per_step": seqs * 4}
+
+    att_ms, att_bytes = debug.time_attention(batch, reps=3)
+    peaks, peak_kind = measured_peaks()
+    achieved = att_bytes / (att_ms / 1000.0) / 1e9
+    traffic = None
+    try:
+        with open(os.path.join(ROOT, "profiles", "k_attend_traffic.json")) as f:
+            t = json.load(f)
+            traffic = t["dram_bytes_per_position"] * (att_bytes / t["algorithmic_bytes_per_position"])
+    except (OSError, KeyError, ZeroDivisionError):
+        traffic = None
+    roofline = {"kernel": "k_attend (paged int8 attention, one launch = one layer of the batch)", "bound": "hbm",
+                "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": traffic,
+                "peak_source": f"{peak_kind} hbm_gbs", "launch_ms": att_ms, "algorithmic_bytes": att_bytes}
+
+    line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "int8+f32", "data": "synthetic",
+            "config": {"workload": "config2: depth-20 synthetic Needle-3 (seed 0), 256 sequences per GPU, prompts "
+                                   "uniform in [128, 1024], greedy decode, paged int8 KV (64-token pages)",
+                       "sequences_per_gpu": seqs, "depth": DEPTH, "parallelism": f"dp{world} (sequences sharded)",
+                       "l2": "inputs larger than L2 (KV cache ~2 GB per GPU)", "setup_s": round(setup_s, 1)},
+            "e2e": e2e, "roofline": roofline, "gpu_launches": launches_per_step(DEPTH) * args.steps,
+            "clocks": clocks.summary()}
+
+    if not args.no_batch1 and rank == 0 and not args.profile:
+        line["batch1"] = batch1(nb, model)
+    if rank == 0 and world == 1 and not args.no_cpu and not args.profile:
+        from oracle import oracle
+
+        oracle.build()
+        line["cpu_baseline"] = cpu_baseline(archive, rank_prompts, os.cpu_count() or 1)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    batch.close()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def batch1(nb, model):
+    """Config 1: depth 20, batch 1, 512-token prompt, 256 masked greedy steps."""
+    rng = np.random.default_rng(7)
+    ids = rng.integers(10, 8000, 512).astype(np.uint32)
+    s = nb.Session(model)
+    start = time.perf_counter()
+    s.feed(ids)
+    prefill_ms = 1000 * (time.perf_counter() - start)
+    b = nb.Batch(model, [s])
+    words = model.config.output_vocab // 32
+    masks = []
+    for _ in range(256):
+        allowed = rng.random(model.config.output_vocab) < 0.05
+        allowed[rng.integers(0, model.config.output_vocab)] = True
+        masks.append(np.packbits(allowed.astype(np.uint8), bitorder="little").view(np.uint32)[:words].copy())
+    times = []
+    for m in masks:
+        t = time.perf_counter()
+        b.step(m)
+        times.append(1000 * (time.perf_counter() - t))
+    b.close()
+    times = times[4:]
+    return {"prefill_ms_512": round(prefill_ms, 2), "p50_ms_per_token": round(float(np.percentile(times, 50)), 4),
+            "p90_ms_per_token": round(float(np.percentile(times, 90)), 4),
+            "tokens_per_s": round(1000.0 / float(np.percentile(times, 50)), 1), "steps": len(times),
+            "note": "per-token latency through nb_batch_step (host mask in, token out), depth 20"}
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,154 @@
+/*
+ * needle_b200.h — C ABI of the B200-native Needle-3 token loop.
+ *
+ * This is the drop-in boundary for rustyneedle's model + generation layers.
+ * Each entry point names the reference interface it replaces (paths are
+ * inside the rustyneedle workspace). Plain pointers and sizes only; every
+ * call returns an nb_status and never aborts on bad input. The message of the
+ * last failure on the calling thread is returned by nb_last_error().
+ *
+ * Threading: an nb_model is immutable once opened and may be shared by host
+ * threads (the reference's Arc<Model>, docs/library.md:150). Sessions and
+ * batches are single-thread objects (Send, not Sync), like rustyneedle's
+ * Session. All device work of a model runs on that model's CUDA stream.
+ */
+#ifndef NEEDLE_B200_H
+#define NEEDLE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum nb_status {
+  NB_OK = 0,
+  NB_ERR_IO = -1,               /* CactError::Io (crates/cact/src/error.rs:6) */
+  NB_ERR_ARCHIVE = -2,          /* CactError::{Truncated, WrongTag, UnknownElementKind, BadLayout, OutOfBounds} */
+  NB_ERR_DEPTH = -3,            /* ModelError::Depth (crates/model/src/model.rs:15) */
+  NB_ERR_ARGUMENT = -4,         /* a null pointer, an out-of-range token id or size */
+  NB_ERR_UNSUPPORTED = -5,      /* an archive feature this build does not run (conv taps, engram, probe heads) */
+  NB_ERR_CUDA = -6,             /* a CUDA runtime failure; the message names the call */
+  NB_ERR_CONTEXT_OVERFLOW = -7, /* RawTurn.overflow (crates/generate/src/generator.rs:77-89) */
+  NB_ERR_KV_EXHAUSTED = -8,     /* the device KV page pool has no free page */
+  NB_ERR_TIMEOUT = -9,          /* a bounded device wait gave up */
+  NB_ERR_NO_DEVICE = -10        /* no CUDA device, or the library was built for another architecture */
+} nb_status;
+
+typedef struct nb_model nb_model;
+typedef struct nb_session nb_session;
+typedef struct nb_batch nb_batch;
+
+typedef struct nb_options {
+  int32_t device;          /* CUDA ordinal; -1 = the current device */
+  uint32_t max_sessions;   /* concurrent sessions on this model (0 = 256) */
+  uint32_t kv_pages;       /* 64-position KV pages in the pool (0 = enough for max_sessions at max_seq_len) */
+  uint32_t max_batch_tokens; /* tokens in one forward pass (prefill chunk; 0 = 1024) */
+} nb_options;
+
+typedef struct nb_model_config {
+  uint32_t vocab, output_vocab, d_model, num_heads, num_kv_heads, num_layers, head_dim, max_seq_len, hada_n, lanes;
+  uint32_t depth;          /* active layers */
+  int32_t active_layers[64];
+  float rope_theta;
+} nb_model_config;
+
+typedef struct nb_step_stats {
+  float probability;       /* allowed_statistics().probability (generator.rs:182-194) */
+  float mass;              /* allowed_statistics().mass */
+  int32_t status;          /* NB_OK or NB_ERR_CONTEXT_OVERFLOW for this sequence */
+} nb_step_stats;
+
+const char* nb_last_error(void);
+
+/* Model::open (crates/model/src/model.rs:52-56): reads the .cact archive
+ * (crates/cact/src/archive.rs:37-70, layout.rs:190-209), repacks every
+ * codebook-quantised matrix into its device layout and uploads it once.
+ * `options` may be NULL. */
+nb_status nb_model_open(const char* path, const nb_options* options, nb_model** out);
+
+/* Model::with_depth (model.rs:63-66, ladder.rs:22-29): a new handle over the
+ * same device weights running the first `depth` rungs of the bisection ladder.
+ * NB_ERR_DEPTH when depth is outside [2, layers]. */
+nb_status nb_model_with_depth(const nb_model* model, uint32_t depth, nb_model** out);
+
+/* Model::config (model.rs:80-82) and Model::active_layers (model.rs:76-78). */
+nb_status nb_model_get_config(const nb_model* model, nb_model_config* out);
+
+/* Drops one handle; device memory is freed with the last handle of a model. */
+void nb_model_release(nb_model* model);
+
+/* Session::new (crates/model/src/session.rs:30-42). */
+nb_status nb_session_create(nb_model* model, nb_session** out);
+
+/* Session: Clone — the prefix cache (generator.rs:36-47). KV pages are shared
+ * copy-on-write; the clone costs no device copy until one side appends into a
+ * shared partial page. */
+nb_status nb_session_clone(const nb_session* session, nb_session** out);
+
+void nb_session_release(nb_session* session);
+
+/* Session::feed (session.rs:56-70): the prompt runs as batched forward
+ * passes; results are bit-identical to pushing the tokens one at a time. */
+nb_status nb_session_feed(nb_session* session, const uint32_t* ids, size_t count);
+
+/* Session::push (session.rs:72-148): one token through every active layer. */
+nb_status nb_session_push(nb_session* session, uint32_t id);
+
+/* Session::logits (session.rs:166-177) into a caller-owned host buffer of
+ * at least output_vocab floats. */
+nb_status nb_session_logits(nb_session* session, float* out, size_t capacity);
+
+/* Session::len (session.rs:44-46). */
+size_t nb_session_len(const nb_session* session);
+
+/* Greedy selection of generator.rs:99-116 for one session: logits, the
+ * optional packed grammar bitset (V/32 words, bit set = allowed), argmax or
+ * argmax_allowed (generator.rs:147-165, falling back to the unrestricted
+ * argmax when nothing is allowed) and allowed_statistics; the chosen token is
+ * then pushed. `stats` may be NULL. */
+nb_status nb_session_step(nb_session* session, const uint32_t* mask_bits, uint32_t* next, nb_step_stats* stats);
+
+/* Batched decode (no reference equivalent: run_turn's loop,
+ * generator.rs:99-130, over B independent sessions). The batch owns a CUDA
+ * graph of one step; the sessions must all belong to `model`. */
+nb_status nb_batch_create(nb_model* model, nb_session* const* sessions, uint32_t count, nb_batch** out);
+void nb_batch_release(nb_batch* batch);
+
+/* One greedy step of every session in the batch, all on device: logits,
+ * mask, argmax, statistics and the push of the chosen tokens. mask_bits is
+ * count × (output_vocab/32) words or NULL (unconstrained); next receives
+ * count token ids; stats (count entries) may be NULL. A sequence whose context
+ * is full is not stepped: its stats.status is NB_ERR_CONTEXT_OVERFLOW and its
+ * next id is UINT32_MAX. */
+nb_status nb_batch_step(nb_batch* batch, const uint32_t* mask_bits, uint32_t* next, nb_step_stats* stats);
+
+/* Device-resident variant for callers that keep data on the GPU: mask_bits
+ * (may be NULL) and next (count uint32) are device pointers on the model's
+ * device. stats_device must be NULL: statistics come from nb_batch_step. */
+nb_status nb_batch_step_device(nb_batch* batch, const uint32_t* mask_bits_device, uint32_t* next_device,
+                               nb_step_stats* stats_device);
+
+/* `steps` greedy steps of the batch back to back on the device, without a
+ * host round trip between them (unconstrained, or under per-step device
+ * masks: steps × count × (output_vocab/32) words). tokens_device (steps ×
+ * count, may be NULL) receives the chosen ids; elapsed_ms (may be NULL) the
+ * device time of the run, measured with CUDA events on the model's stream.
+ * Fails with NB_ERR_CONTEXT_OVERFLOW, before any work, when a session cannot
+ * take `steps` more tokens. */
+nb_status nb_batch_run(nb_batch* batch, uint32_t steps, const uint32_t* mask_bits_device, uint32_t* tokens_device,
+                       float* elapsed_ms);
+
+/* Waits for the model's stream. */
+nb_status nb_model_synchronize(nb_model* model);
+
+/* Builds the table of inputs where this host's libm expf differs from the
+ * correctly rounded exponential (used by the device sigmoid to reproduce
+ * f32::exp exactly) and writes it to `path`. Runs on the host CPU. */
+nb_status nb_build_expf_table(const char* path);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

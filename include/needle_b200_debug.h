@@ -1,0 +1,46 @@
+/*
+ * needle_b200_debug.h — kernel-level test hooks of the B200 Needle-3 library.
+ *
+ * These entry points are not part of the drop-in boundary (needle_b200.h):
+ * the parity tests use them to compare single kernels with the CPU
+ * restatement. Buffers are host memory; each call synchronises.
+ */
+#ifndef NEEDLE_B200_DEBUG_H
+#define NEEDLE_B200_DEBUG_H
+
+#include "needle_b200.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Element-wise device math on the model's GPU: op 0 = f32::exp as the host
+ * libm computes it, 1 = sigmoid (crates/kernels/src/ops.rs:69-71),
+ * 2 = fast_exp (ops.rs:83-90), 3 = silu (ops.rs:74-76). */
+nb_status nb_debug_math(nb_model* model, int op, const float* in, float* out, size_t count);
+
+/* QuantisedMatrix::prepare + multiply_vector (crates/kernels/src/matrix.rs:123-165)
+ * of `count` inputs through one device matrix: which = 0 the fused
+ * q/k/v/gate rows of `layer`, 1 its out_proj, 2 the tied embedding (logits).
+ * in: count × columns floats; out: count × rows floats. */
+nb_status nb_debug_project(nb_model* model, int which, uint32_t layer, const float* in, size_t count, float* out);
+
+/* The session's final hidden state (session.rs:140-143): d_model floats. */
+nb_status nb_debug_hidden(nb_session* session, float* out);
+
+/* The int8 KV cache of one layer in the reference's layout
+ * (model/src/attention.rs:37-45): keys/values [len][kv_heads][64],
+ * scales [kv_heads][len]. */
+nb_status nb_debug_kv(nb_session* session, uint32_t layer, int8_t* keys, float* key_scales, int8_t* values,
+                      float* value_scales);
+
+/* Replays the attention kernel of every active layer over the batch's
+ * current positions `reps` times and reports the mean device time of one
+ * launch (CUDA events on the model's stream) and the KV bytes one launch
+ * must read (keys, values and their scales of every attended position). */
+nb_status nb_debug_time_attention(nb_batch* batch, uint32_t reps, float* ms_per_launch, double* bytes_per_launch);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,271 @@
+"""ctypes binding of include/needle_b200.h (the product's C ABI)."""
+
+from __future__ import annotations
+
+import ctypes
+import os
+from dataclasses import dataclass
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+_LIBRARY = os.path.join(HERE, "_native", "libneedle_b200.so")
+
+NB_OK = 0
+STATUS_NAMES = {
+    -1: "NB_ERR_IO", -2: "NB_ERR_ARCHIVE", -3: "NB_ERR_DEPTH", -4: "NB_ERR_ARGUMENT", -5: "NB_ERR_UNSUPPORTED",
+    -6: "NB_ERR_CUDA", -7: "NB_ERR_CONTEXT_OVERFLOW", -8: "NB_ERR_KV_EXHAUSTED", -9: "NB_ERR_TIMEOUT",
+    -10: "NB_ERR_NO_DEVICE",
+}
+
+
+class NeedleError(RuntimeError):
+    """A failed C-ABI call; `status` is the nb_status code."""
+
+    def __init__(self, status: int, message: str):
+        super().__init__(f"{STATUS_NAMES.get(status, status)}: {message}")
+        self.status = status
+        self.message = message
+
+
+class DepthError(NeedleError):
+    """ModelError::Depth (crates/model/src/model.rs:15)."""
+
+
+class ContextOverflow(NeedleError):
+    """The session would pass max_seq_len (crates/generate/src/generator.rs:77-89)."""
+
+
+class nb_options(ctypes.Structure):
+    _fields_ = [("device", ctypes.c_int32), ("max_sessions", ctypes.c_uint32), ("kv_pages", ctypes.c_uint32),
+                ("max_batch_tokens", ctypes.c_uint32)]
+
+
+class nb_model_config(ctypes.Structure):
+    _fields_ = [(name, ctypes.c_uint32) for name in
+                ("vocab", "output_vocab", "d_model", "num_heads", "num_kv_heads", "num_layers", "head_dim",
+                 "max_seq_len", "hada_n", "lanes", "depth")] + [("active_layers", ctypes.c_int32 * 64),
+                                                               ("rope_theta", ctypes.c_float)]
+
+
+class nb_step_stats(ctypes.Structure):
+    _fields_ = [("probability", ctypes.c_float), ("mass", ctypes.c_float), ("status", ctypes.c_int32)]
+
+
+_lib = None
+
+
+def library_path() -> str:
+    return _LIBRARY
+
+
+def lib() -> ctypes.CDLL:
+    """The loaded native library; raises when it has not been built."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(_LIBRARY):
+            raise ImportError(f"{_LIBRARY} is missing: run `python -m rustyneedle_b200.build` "
+                              "(or __graft_entry__.build()) first; there is no CPU fallback")
+        L = ctypes.CDLL(_LIBRARY)
+        P, U32, SZ, I = ctypes.c_void_p, ctypes.c_uint32, ctypes.c_size_t, ctypes.c_int
+        sig = {
+            "nb_last_error": (ctypes.c_char_p, []),
+            "nb_model_open": (I, [ctypes.c_char_p, ctypes.POINTER(nb_options), ctypes.POINTER(P)]),
+            "nb_model_with_depth": (I, [P, U32, ctypes.POINTER(P)]),
+            "nb_model_get_config": (I, [P, ctypes.POINTER(nb_model_config)]),
+            "nb_model_release": (None, [P]),
+            "nb_model_synchronize": (I, [P]),
+            "nb_session_create": (I, [P, ctypes.POINTER(P)]),
+            "nb_session_clone": (I, [P, ctypes.POINTER(P)]),
+            "nb_session_release": (None, [P]),
+            "nb_session_feed": (I, [P, P, SZ]),
+            "nb_session_push": (I, [P, U32]),
+            "nb_session_logits": (I, [P, P, SZ]),
+            "nb_session_len": (SZ, [P]),
+            "nb_session_step": (I, [P, P, ctypes.POINTER(U32), ctypes.POINTER(nb_step_stats)]),
+            "nb_batch_create": (I, [P, P, U32, ctypes.POINTER(P)]),
+            "nb_batch_release": (None, [P]),
+            "nb_batch_step": (I, [P, P, P, P]),
+            "nb_batch_step_device": (I, [P, P, P, P]),
+            "nb_batch_run": (I, [P, U32, P, P, ctypes.POINTER(ctypes.c_float)]),
+            "nb_build_expf_table": (I, [ctypes.c_char_p]),
+        }
+        for name, (res, args) in sig.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+def _check(status: int) -> None:
+    if status != NB_OK:
+        message = lib().nb_last_error().decode(errors="replace")
+        cls = DepthError if status == -3 else ContextOverflow if status == -7 else NeedleError
+        raise cls(status, message)
+
+
+def _ptr(a: np.ndarray) -> ctypes.c_void_p:
+    return ctypes.c_void_p(a.ctypes.data)
+
+
+@dataclass
+class ModelConfig:
+    vocab: int
+    output_vocab: int
+    d_model: int
+    num_heads: int
+    num_kv_heads: int
+    num_layers: int
+    head_dim: int
+    max_seq_len: int
+    hada_n: int
+    lanes: int
+    active_layers: list
+    rope_theta: float
+
+
+@dataclass
+class StepStats:
+    probability: float
+    mass: float
+    status: int
+
+
+class Model:
+    """Model::open / Model::with_depth. Handles share one set of device weights."""
+
+    def __init__(self, handle):
+        self._h = handle
+        c = nb_model_config()
+        _check(lib().nb_model_get_config(self._h, ctypes.byref(c)))
+        self.config = ModelConfig(c.vocab, c.output_vocab, c.d_model, c.num_heads, c.num_kv_heads, c.num_layers,
+                                  c.head_dim, c.max_seq_len, c.hada_n, c.lanes, list(c.active_layers[:c.depth]),
+                                  c.rope_theta)
+
+    @classmethod
+    def open(cls, path: str, device: int = -1, max_sessions: int = 0, kv_pages: int = 0,
+             max_batch_tokens: int = 0) -> "Model":
+        h = ctypes.c_void_p()
+        opts = nb_options(device, max_sessions, kv_pages, max_batch_tokens)
+        _check(lib().nb_model_open(os.fspath(path).encode(), ctypes.byref(opts), ctypes.byref(h)))
+        return cls(h)
+
+    def with_depth(self, depth: int) -> "Model":
+        h = ctypes.c_void_p()
+        _check(lib().nb_model_with_depth(self._h, depth, ctypes.byref(h)))
+        return Model(h)
+
+    def active_layers(self) -> list:
+        return list(self.config.active_layers)
+
+    def synchronize(self) -> None:
+        _check(lib().nb_model_synchronize(self._h))
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            lib().nb_model_release(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class Session:
+    """Session::new / feed / push / logits / len, plus Clone."""
+
+    def __init__(self, model: Model, handle=None):
+        self.model = model
+        if handle is None:
+            handle = ctypes.c_void_p()
+            _check(lib().nb_session_create(model._h, ctypes.byref(handle)))
+        self._h = handle
+
+    def clone(self) -> "Session":
+        h = ctypes.c_void_p()
+        _check(lib().nb_session_clone(self._h, ctypes.byref(h)))
+        return Session(self.model, h)
+
+    def __len__(self) -> int:
+        return int(lib().nb_session_len(self._h))
+
+    def feed(self, tokens) -> None:
+        t = np.ascontiguousarray(tokens, dtype=np.uint32)
+        _check(lib().nb_session_feed(self._h, _ptr(t), t.size))
+
+    def push(self, token: int) -> None:
+        _check(lib().nb_session_push(self._h, int(token)))
+
+    def logits(self) -> np.ndarray:
+        out = np.empty(self.model.config.output_vocab, dtype=np.float32)
+        _check(lib().nb_session_logits(self._h, _ptr(out), out.size))
+        return out
+
+    def step(self, mask_bits: np.ndarray | None = None, stats: bool = False):
+        """One greedy step: choose from the current logits (optionally under a
+        packed allowed-token bitset), push the choice, return it."""
+        nxt = ctypes.c_uint32()
+        st = nb_step_stats()
+        m = None if mask_bits is None else np.ascontiguousarray(mask_bits, dtype=np.uint32)
+        _check(lib().nb_session_step(self._h, None if m is None else _ptr(m), ctypes.byref(nxt),
+                                     ctypes.byref(st) if stats else None))
+        if stats:
+            return int(nxt.value), StepStats(st.probability, st.mass, st.status)
+        return int(nxt.value)
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            lib().nb_session_release(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class Batch:
+    """B sessions stepped together by one graph-captured device step."""
+
+    def __init__(self, model: Model, sessions: list):
+        self.model = model
+        self.sessions = list(sessions)
+        arr = (ctypes.c_void_p * len(sessions))(*[s._h.value if isinstance(s._h, ctypes.c_void_p) else s._h
+                                                   for s in sessions])
+        self._arr = arr
+        h = ctypes.c_void_p()
+        _check(lib().nb_batch_create(model._h, ctypes.cast(arr, ctypes.c_void_p), len(sessions), ctypes.byref(h)))
+        self._h = h
+        self._next = np.zeros(len(sessions), dtype=np.uint32)
+        self._stats = (nb_step_stats * len(sessions))()
+
+    def step(self, mask_bits: np.ndarray | None = None, stats: bool = False):
+        m = None if mask_bits is None else np.ascontiguousarray(mask_bits, dtype=np.uint32)
+        if m is not None and m.size != len(self.sessions) * (self.model.config.output_vocab // 32):
+            raise ValueError("mask_bits must hold count x output_vocab/32 words")
+        _check(lib().nb_batch_step(self._h, None if m is None else _ptr(m), _ptr(self._next),
+                                   ctypes.cast(self._stats, ctypes.c_void_p) if stats else None))
+        if stats:
+            return self._next.copy(), [StepStats(s.probability, s.mass, s.status) for s in self._stats]
+        return self._next.copy()
+
+    def run(self, steps: int, mask_bits_device: int | None = None, tokens_device: int | None = None) -> float:
+        """`steps` device-resident greedy steps; returns their device time in ms."""
+        ms = ctypes.c_float()
+        _check(lib().nb_batch_run(self._h, steps, mask_bits_device, tokens_device, ctypes.byref(ms)))
+        return float(ms.value)
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            lib().nb_batch_release(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

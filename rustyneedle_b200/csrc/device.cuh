@@ -1,0 +1,176 @@
+// device.cuh — device-side building blocks shared by the Needle-3 kernels.
+//
+// Every float operation is written with an explicitly rounded intrinsic so the
+// association order of the reference survives compilation (the library is also
+// built with -fmad=false). Reductions whose order the reference fixes (the
+// 8-lane sum of squares of crates/kernels/src/ops.rs:7-17, sequential sums) are
+// evaluated in that order; max and integer reductions, which are exact in any
+// order, use warp shuffles.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "exactmath.h"
+#include "layout.h"
+
+namespace nbk {
+
+constexpr unsigned FULL = 0xffffffffu;
+
+__device__ __forceinline__ float fmul(float a, float b) { return __fmul_rn(a, b); }
+__device__ __forceinline__ float fadd(float a, float b) { return __fadd_rn(a, b); }
+__device__ __forceinline__ float fsub(float a, float b) { return __fsub_rn(a, b); }
+__device__ __forceinline__ float fdiv(float a, float b) { return __fdiv_rn(a, b); }
+__device__ __forceinline__ float frcp(float a) { return __frcp_rn(a); }
+__device__ __forceinline__ float fsqrt(float a) { return __fsqrt_rn(a); }
+
+// Rust's float Iterator::sum starts from -0.0.
+constexpr float SUM_START = -0.0f;
+
+// Set per device by set_exp_constants (kernels.cu).
+__constant__ nbx::ExpConstants c_exp;
+__constant__ nbx::ExceptionSet c_exceptions;
+
+// f32::exp of the host libm (see exactmath.h).
+__device__ __forceinline__ float expf_libm(float x) {
+  if (isnan(x)) return x;
+  if (x > 89.0f) return INFINITY;
+  if (x < -110.0f) return 0.0f;
+  double y = nbx::exp_double_core(
+      x, c_exp, [](double a, double b) { return __dmul_rn(a, b); }, [](double a, double b) { return __dadd_rn(a, b); },
+      [](double a, double b, double c) { return __fma_rn(a, b, c); });
+  float f = __double2float_rn(y);
+  if (nbx::near_midpoint(y, f, c_exp.near_relative) && nbx::exception_contains(c_exceptions, nbx::float_bits(x)))
+    f = nbx::other_neighbour(y, f);
+  return f;
+}
+
+// crates/kernels/src/ops.rs:69-71
+__device__ __forceinline__ float sigmoid(float v) { return fdiv(1.0f, fadd(1.0f, expf_libm(-v))); }
+
+// crates/kernels/src/ops.rs:83-90: clamp, scale by log2(e), round half away
+// from zero, degree-5 polynomial of the fraction, then the power of two.
+__device__ __forceinline__ float fast_exp(float value) {
+  float c = value;
+  if (c < -87.0f) c = -87.0f;
+  if (c > 87.0f) c = 87.0f;
+  float scaled = fmul(c, 1.44269504088896341f);
+  float whole = roundf(scaled);
+  float f = fsub(scaled, whole);
+  float p = fmul(f, 0.0013333558f);
+  p = fadd(0.009618129f, p);
+  p = fmul(f, p);
+  p = fadd(0.05550411f, p);
+  p = fmul(f, p);
+  p = fadd(0.2402265f, p);
+  p = fmul(f, p);
+  p = fadd(0.69314718055994531f, p);
+  p = fmul(f, p);
+  p = fadd(1.0f, p);
+  int w = isnan(whole) ? 0 : (int)whole;
+  return fmul(p, __int_as_float((w + 127) << 23));
+}
+
+// crates/kernels/src/ops.rs:74-76
+__device__ __forceinline__ float silu(float v) { return fdiv(v, fadd(1.0f, fast_exp(-v))); }
+
+__device__ __forceinline__ float clampf(float x, float lo, float hi) { return x < lo ? lo : (x > hi ? hi : x); }
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int s = 16; s > 0; s >>= 1) v = fmaxf(v, __shfl_xor_sync(FULL, v, s));
+  return v;
+}
+
+__device__ __forceinline__ int warp_sum_int(int v) {
+#pragma unroll
+  for (int s = 16; s > 0; s >>= 1) v += __shfl_xor_sync(FULL, v, s);
+  return v;
+}
+
+// Max over a block; `scratch` holds one float per warp. All threads get the result.
+__device__ __forceinline__ float block_max(float v, float* scratch) {
+  v = warp_max(v);
+  int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, warps = blockDim.x >> 5;
+  __syncthreads();
+  if (lane == 0) scratch[warp] = v;
+  __syncthreads();
+  float r = scratch[0];
+  for (int i = 1; i < warps; ++i) r = fmaxf(r, scratch[i]);
+  return r;
+}
+
+// ops.rs:7-17 over n values in shared memory: eight running lanes (lane l
+// takes values l, l+8, ...), the lanes summed in order from -0.0, then the tail.
+// Called by one whole warp; every lane returns the sum.
+__device__ __forceinline__ float sum_of_squares_warp(const float* v, int n) {
+  int lane = threadIdx.x & 31;
+  int whole = n / 8 * 8;
+  float acc = 0.0f;
+  if (lane < 8)
+    for (int i = lane; i < whole; i += 8) acc = fadd(acc, fmul(v[i], v[i]));
+  float s = SUM_START;
+#pragma unroll
+  for (int l = 0; l < 8; ++l) s = fadd(s, __shfl_sync(FULL, acc, l));
+  float tail = SUM_START;
+  for (int i = whole; i < n; ++i) tail = fadd(tail, fmul(v[i], v[i]));
+  return fadd(s, tail);
+}
+
+// 1 / sqrt(mean_square + 1e-6) of ops.rs:44-66.
+__device__ __forceinline__ float inverse_rms(float sum_squares, int n) {
+  float ms = fdiv(sum_squares, (float)n);
+  return fdiv(1.0f, fsqrt(fadd(ms, 1e-6f)));
+}
+
+// The normalised Walsh–Hadamard transform of one 128-value group held by a
+// warp, four consecutive values per lane (walsh.rs:41-76): the radix-4 first
+// stage, then butterflies of span 4..64 (lane distance 1..16), then the scale.
+__device__ __forceinline__ void fwht128(float v[4], float inv_sqrt_group) {
+  int lane = threadIdx.x & 31;
+  float a = v[0], b = v[1], c = v[2], d = v[3];
+  float ls = fadd(a, b), ld = fsub(a, b), hs = fadd(c, d), hd = fsub(c, d);
+  v[0] = fadd(ls, hs);
+  v[1] = fadd(ld, hd);
+  v[2] = fsub(ls, hs);
+  v[3] = fsub(ld, hd);
+#pragma unroll
+  for (int s = 1; s < 32; s <<= 1) {
+    bool upper = lane & s;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float o = __shfl_xor_sync(FULL, v[j], s);
+      v[j] = upper ? fsub(o, v[j]) : fadd(v[j], o);
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < 4; ++j) v[j] = fmul(v[j], inv_sqrt_group);
+}
+
+// Per-group int8 activation of neon.rs:22-46 / panel.rs:46-65 for the 128
+// values a warp holds (4 per lane): scale = peak/127 (1 when the group is 0),
+// codes = round-half-even(x / scale) clamped to ±127. Returns the scale and
+// the lane's four codes packed little-endian.
+__device__ __forceinline__ float quantise_group(const float v[4], uint32_t& packed) {
+  float peak = 0.0f;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) peak = fmaxf(peak, fabsf(v[j]));
+  peak = warp_max(peak);
+  float scale = peak > 0.0f ? fdiv(peak, 127.0f) : 1.0f;
+  packed = 0;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    int q = (int)clampf(rintf(fdiv(v[j], scale)), -127.0f, 127.0f);
+    packed |= (uint32_t)(q & 0xff) << (8 * j);
+  }
+  return scale;
+}
+
+// fake_quantise_int8 element step (ops.rs:120-125) given the vector's scale.
+__device__ __forceinline__ float fake_quant(float v, float scale) { return fmul(clampf(rintf(fdiv(v, scale)), -128.0f, 127.0f), scale); }
+__device__ __forceinline__ float int8_scale_of(float peak) { return peak > 0.0f ? fdiv(peak, 127.0f) : 1.0f; }
+
+__device__ __forceinline__ int dp4a(uint32_t a, uint32_t b, int c) { return __dp4a((int)a, (int)b, c); }
+
+}  // namespace nbk

@@ -1,0 +1,31 @@
+// kernels.h — host launchers of the kernels in kernels.cu.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include "exactmath.h"
+#include "layout.h"
+
+namespace nbk {
+
+void set_exp_constants(const nbx::ExpConstants& constants, const nbx::ExceptionSet& exceptions, cudaStream_t stream);
+cudaError_t configure(const nbl::ModelDev& md, int t_cap);
+
+void launch_embed(const nbl::ModelDev& md, const nbl::Work& w, int M, cudaStream_t st);
+void launch_layer(const nbl::ModelDev& md, const nbl::LayerDev& L, const nbl::Work& w, const nbl::KvDev& kv, int M, int layer,
+                  int slot, int t_cap, cudaStream_t st);
+void launch_final(const nbl::ModelDev& md, const nbl::Work& w, float* hidden, int M, cudaStream_t st);
+void launch_logits(const nbl::ModelDev& md, const float* hidden, const int32_t* slots, int B, int8_t* act, float* act_scale,
+                   float* logits, cudaStream_t st);
+void launch_select(const float* logits, int V, const uint32_t* mask, const int32_t* active, uint32_t* next, float* peaks, int B,
+                   cudaStream_t st);
+void launch_stats(const float* logits, int V, const uint32_t* mask, const int32_t* active, const uint32_t* next,
+                  const float* peaks, float* stats, int stats_stride, int B, cudaStream_t st);
+void launch_advance(nbl::TokenMeta* meta, int B, cudaStream_t st);
+void launch_attend(const nbl::ModelDev& md, const nbl::LayerDev& L, const nbl::Work& w, const nbl::KvDev& kv, int M, int layer,
+                   int t_cap, cudaStream_t st);
+void launch_debug_math(int op, const float* in, float* out, int n, cudaStream_t st);
+void launch_debug_project(const nbl::ModelDev& md, const nbl::QMat& W, const float* in, int K, int M, int8_t* act,
+                          float* act_scale, float* out, int out_stride, cudaStream_t st);
+
+}  // namespace nbk

@@ -1,0 +1,135 @@
+// layout.h — device data layout of a loaded Needle-3 model, its KV pages and
+// the per-pass workspace. Shared by the host runtime and the kernels.
+//
+// Weights. Every codebook-quantised matrix (crates/cact/src/record.rs, kind 3)
+// is expanded once at load from its 2- or 4-bit indices to int8 through the
+// reference's integer level table (crates/kernels/src/neon.rs:114-123) and
+// stored lane-interleaved for the projection kernel: rows in blocks of 8, each
+// row's 128-column groups cut into 16-byte pieces, piece k of (row r, group g)
+// at ((block*KP + k)*32 + 4*r + g)*16 for K = 512 (KP = 8 pieces per group).
+// Per (row, group) scales are f32: for 2-bit matrices the product
+// norm*level_scale of the panel combine (panel.rs:184), for 4-bit matrices the
+// norm alone (the row combine multiplies by level_scale after the norm,
+// neon.rs:180).
+//
+// KV pages hold 64 positions of one layer of one sequence for every kv head:
+//   keys    [kv][64 positions][head_dim] int8            (position-major rows)
+//   values  [kv][16 blocks][head_dim][4 positions] int8  (the reference's
+//           4-position value panels, model/src/attention.rs:54-69)
+//   kscale  [kv][64] f32, vscale [kv][64] f32
+#pragma once
+
+#include <stdint.h>
+
+namespace nbl {
+
+constexpr int GROUP = 128;
+constexpr int HEAD_DIM = 64;
+constexpr int PAGE_POSITIONS = 64;
+constexpr int LANES = 4;
+constexpr int MAX_D = 1024;
+constexpr int MAX_HEADS = 16;
+constexpr int HADA_RIGHT = 32;
+constexpr int COND_RANK = 8;
+
+struct PageGeometry {
+  uint32_t kv_heads;
+  uint32_t key_bytes;     // kv * 64 * head_dim
+  uint32_t value_offset;  // == key_bytes
+  uint32_t kscale_offset; // 2 * key_bytes
+  uint32_t vscale_offset;
+  uint32_t page_bytes;
+};
+
+inline PageGeometry page_geometry(uint32_t kv_heads) {
+  PageGeometry p;
+  p.kv_heads = kv_heads;
+  p.key_bytes = kv_heads * PAGE_POSITIONS * HEAD_DIM;
+  p.value_offset = p.key_bytes;
+  p.kscale_offset = 2 * p.key_bytes;
+  p.vscale_offset = p.kscale_offset + kv_heads * PAGE_POSITIONS * 4;
+  p.page_bytes = p.vscale_offset + kv_heads * PAGE_POSITIONS * 4;
+  return p;
+}
+
+// A codebook-quantised matrix in device layout.
+struct QMat {
+  const int8_t* codes;   // lane-interleaved int8 (K = 512) or row-major int8 (other K)
+  const float* scales;   // [rows][groups]
+  float level_scale;     // IntegerLevels::scale
+  uint32_t rows, cols, groups;
+  int fused;             // 1: 2-bit panel combine (fma); 0: 4-bit row combine
+};
+
+struct HadamardDev {
+  const float *d1, *d2, *b2, *d3, *d4;
+  const float* left[3];   // left_size x left_size
+  const float* right[3];  // 32 x 32
+  const float *cond_v, *cond_u;
+};
+
+struct LayerDev {
+  QMat qkvg;  // q, k, v and gate_proj stacked row-wise (one fused product, matrix.rs:167-193)
+  QMat out;
+  const float *norm_in, *post_norm, *pre_hada, *q_norm, *k_norm;
+  float attn_gate;
+  HadamardDev hada;
+  int global;  // 1 when the layer attends to the whole context
+};
+
+struct ModelDev {
+  uint32_t d_model, heads, kv_heads, vocab, output_vocab, hada_n, hada_left, max_seq_len, num_layers;
+  uint32_t sliding_window;
+  float sqrt_d;          // (d_model as f32).sqrt()
+  float inv_sqrt_group;  // 1 / sqrt(128)
+  float inv_root_qk;     // 1 / sqrt(head_dim)
+  // embedding: packed 4-bit (or 2-bit) rows for the gather, int8 for logits
+  const uint8_t* embed_packed;
+  uint32_t embed_bits, embed_row_bytes;
+  const float* embed_levels;  // 16 float levels
+  const float* embed_norms;   // [vocab][groups]
+  QMat logits;                // the tied embedding as a product
+  // lanes (crates/model/src/lanes.rs)
+  QMat phi_pre, phi_post, phi_res;  // row-major int8, K = lanes * d_model
+  const float *a_pre, *a_post, *a_res, *b_pre, *b_post, *b_res;
+  const float* final_norm;
+  const int32_t* perm1;
+  const int32_t* perm2;
+  const float2* rotary;       // [max_seq_len][head_dim/2] (sin, cos)
+  PageGeometry page;
+};
+
+// Per-token metadata of one forward pass.
+struct TokenMeta {
+  int32_t slot;      // session slot (page table row)
+  int32_t position;  // absolute position of this token
+  int32_t last;      // 1 when this is the sequence's last token in the pass
+  int32_t pad;
+};
+
+// Device workspace of a forward pass over at most `capacity` tokens.
+struct Work {
+  uint32_t capacity;
+  const uint32_t* tokens;   // [M] token ids (device)
+  const TokenMeta* meta;    // [M]
+  float* stream;            // [M][4][d]
+  float* next_stream;       // [M][4][d]
+  float* x;                 // [M][d]      routing input, then the block's running value
+  float* route;             // [M][4 + 16] post gates and Sinkhorn residual weights
+  int8_t* act;              // [M][max(d, attention width)] int8 activations
+  float* act_scale;         // [M][groups]
+  float* proj;              // [M][q + k + v + gate]
+  int8_t* qcodes;           // [M][heads][64]
+  float* qscale;            // [M][heads]
+  float* attn;              // [M][heads * 64]
+  float* outp;              // [M][d]
+};
+
+struct KvDev {
+  uint8_t* pool;
+  const int32_t* page_table;  // [slots][layers][max_pages]
+  uint32_t max_pages;
+  uint32_t num_layers;
+};
+
+}  // namespace nbl

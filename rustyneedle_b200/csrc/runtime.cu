@@ -1,0 +1,1289 @@
+// runtime.cu — host runtime and C ABI of the B200 Needle-3 token loop.
+//
+// An Engine owns one opened archive on one GPU: the device weights, the KV
+// page pool, the session slots and the forward-pass workspace, all driven on
+// one CUDA stream. nb_model handles (Model::open, Model::with_depth) share an
+// Engine and differ only in their active layers; sessions are slots of the
+// Engine; batches capture one greedy decode step as a CUDA graph.
+#include <cuda_runtime.h>
+#include <dlfcn.h>
+
+#include <algorithm>
+#include <atomic>
+#include <cmath>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <map>
+#include <memory>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/needle_b200.h"
+#include "archive.h"
+#include "expf_table.h"
+#include "kernels.h"
+#include "layout.h"
+
+using namespace nbl;
+
+namespace nbr {
+
+thread_local std::string g_error;
+
+struct Failure {
+  nb_status status;
+  std::string message;
+};
+
+[[noreturn]] void fail(nb_status s, const std::string& m) { throw Failure{s, m}; }
+
+#define NB_CUDA(call)                                                                                          \
+  do {                                                                                                         \
+    cudaError_t e_ = (call);                                                                                   \
+    if (e_ != cudaSuccess) ::nbr::fail(NB_ERR_CUDA, std::string(#call) + ": " + cudaGetErrorString(e_));      \
+  } while (0)
+
+template <typename F>
+nb_status guard(F&& f) {
+  try {
+    f();
+    return NB_OK;
+  } catch (const Failure& e) {
+    g_error = e.message;
+    return e.status;
+  } catch (const nba::ArchiveError& e) {
+    g_error = e.message;
+    return (nb_status)e.status;
+  } catch (const std::bad_alloc&) {
+    g_error = "host allocation failed";
+    return NB_ERR_ARGUMENT;
+  } catch (const std::exception& e) {
+    g_error = e.what();
+    return NB_ERR_ARGUMENT;
+  }
+}
+
+// ------------------------------------------------------------ level tables
+// crates/kernels/src/codebook.rs:1-43 and matrix.rs:499-514
+struct Levels {
+  uint32_t bits = 0;  // lookup width (ternary crumbs read as 2 bits)
+  float values[16] = {0};
+  int8_t ints[16] = {0};  // IntegerLevels::table (neon.rs:114-123)
+  float int_scale = 1.0f;
+  bool fused = false;  // 2-bit panels: fma combine (panel.rs:184-187)
+};
+
+Levels levels_for(uint32_t record_bits, const std::vector<float>& cb, uint32_t group) {
+  Levels L;
+  auto copy = [&](size_t from, size_t n) {
+    if (cb.size() < from + n) fail(NB_ERR_ARCHIVE, "codebook is shorter than 28 values");
+    for (size_t i = 0; i < n; ++i) L.values[i] = cb[from + i];
+  };
+  switch (record_bits) {
+    case 2:
+      L.bits = 2;
+      copy(0, 4);
+      L.fused = group % 16 == 0;
+      break;
+    case 4:
+      L.bits = 4;
+      copy(12, 16);
+      break;
+    case 5: {
+      float level = 1.2240064f / std::sqrt((float)group);
+      L.bits = 2;
+      L.values[1] = level;
+      L.values[3] = -level;
+      break;
+    }
+    default:
+      fail(NB_ERR_UNSUPPORTED, "codebook width " + std::to_string(record_bits) +
+                                   " runs on the reference's float kernel, which this build does not implement");
+  }
+  if ((L.bits == 2 && group % 64 != 0) || (L.bits == 4 && group % 32 != 0))
+    fail(NB_ERR_UNSUPPORTED, "group size " + std::to_string(group) + " has no integer kernel in the reference");
+  uint32_t count = 1u << L.bits;
+  float peak = 0.0f;
+  for (uint32_t i = 0; i < count; ++i) peak = std::fmax(peak, std::fabs(L.values[i]));
+  L.int_scale = peak > 0.0f ? peak / 127.0f : 1.0f;
+  for (uint32_t i = 0; i < count; ++i) L.ints[i] = (int8_t)std::round(L.values[i] / L.int_scale);
+  return L;
+}
+
+static inline uint32_t code_at(const uint8_t* row, uint64_t i, uint32_t bits) {
+  uint64_t bit = i * bits, byte = bit >> 3, shift = bit & 7;
+  uint32_t raw = row[byte];
+  if (shift + bits > 8) raw |= (uint32_t)row[byte + 1] << 8;
+  return (raw >> shift) & ((1u << bits) - 1);
+}
+
+// ----------------------------------------------------------------- engine
+struct Engine;
+
+struct DeviceArena {
+  std::vector<void*> blocks;
+  ~DeviceArena() {
+    for (void* p : blocks) cudaFree(p);
+  }
+  template <typename T>
+  T* alloc(size_t count) {
+    void* p = nullptr;
+    size_t bytes = std::max<size_t>(count * sizeof(T), 16);
+    cudaError_t e = cudaMalloc(&p, bytes);
+    if (e != cudaSuccess) fail(NB_ERR_CUDA, "cudaMalloc(" + std::to_string(bytes) + "): " + cudaGetErrorString(e));
+    blocks.push_back(p);
+    return static_cast<T*>(p);
+  }
+  template <typename T>
+  T* upload(const std::vector<T>& v, cudaStream_t st) {
+    T* p = alloc<T>(v.size());
+    if (!v.empty()) NB_CUDA(cudaMemcpyAsync(p, v.data(), v.size() * sizeof(T), cudaMemcpyHostToDevice, st));
+    return p;
+  }
+};
+
+struct PinnedBuffer {
+  void* p = nullptr;
+  size_t bytes = 0;
+  ~PinnedBuffer() {
+    if (p) cudaFreeHost(p);
+  }
+  void ensure(size_t n) {
+    if (n <= bytes) return;
+    if (p) cudaFreeHost(p);
+    p = nullptr;
+    NB_CUDA(cudaMallocHost(&p, n));
+    bytes = n;
+  }
+  template <typename T>
+  T* as() {
+    return static_cast<T*>(p);
+  }
+};
+
+struct Engine {
+  int device = 0;
+  cudaStream_t stream = nullptr, side = nullptr;
+  std::mutex mutex;
+  nba::Geometry geo;
+  ModelDev md{};
+  std::vector<LayerDev> layers;
+  DeviceArena arena;
+  std::vector<uint32_t> exception_slots;
+  // sessions and KV pages
+  uint32_t max_sessions = 0, max_pages = 0, num_pages = 0;
+  uint8_t* pool = nullptr;
+  int32_t* d_page_table = nullptr;
+  PinnedBuffer h_table;               // pinned mirror: [slots][layers][max_pages] int32
+  bool copies_in_flight = false;      // asynchronous copies still read pinned staging memory
+  std::vector<uint32_t> refcount;     // per physical page
+  std::vector<uint32_t> free_pages;
+  std::vector<uint32_t> free_slots;
+  std::vector<uint8_t> slot_dirty;
+  float* d_hidden = nullptr;  // [slots][d]
+  // forward workspace
+  uint32_t capacity = 0;
+  Work work{};
+  uint32_t* d_tokens = nullptr;
+  TokenMeta* d_meta = nullptr;
+  PinnedBuffer h_tokens, h_meta, h_misc;
+  // logits of single-session calls
+  int8_t* d_logit_act = nullptr;
+  float* d_logit_scale = nullptr;
+  float* d_logits = nullptr;  // [max_sessions][V]
+  int32_t* d_slots = nullptr;
+  uint32_t* d_next = nullptr;
+  float* d_peaks = nullptr;
+  float* d_stats = nullptr;
+  uint32_t* d_mask = nullptr;
+  int32_t* d_active = nullptr;
+  int t_cap = 0;
+
+  KvDev kv() const { return KvDev{pool, d_page_table, max_pages, geo.num_layers}; }
+
+  ~Engine() {
+    if (device >= 0) cudaSetDevice(device);
+    if (stream) cudaStreamSynchronize(stream);
+    if (side) cudaStreamDestroy(side);
+    if (stream) cudaStreamDestroy(stream);
+  }
+
+  int32_t& page_entry(uint32_t slot, uint32_t layer, uint32_t index) {
+    return h_table.as<int32_t>()[((size_t)slot * geo.num_layers + layer) * max_pages + index];
+  }
+
+  // Waits until no queued copy still reads the pinned staging buffers, so the
+  // host may rewrite them.
+  void settle() {
+    if (copies_in_flight) {
+      NB_CUDA(cudaStreamSynchronize(stream));
+      copies_in_flight = false;
+    }
+  }
+
+  uint32_t take_page() {
+    if (free_pages.empty()) fail(NB_ERR_KV_EXHAUSTED, "the KV page pool is exhausted (" + std::to_string(num_pages) + " pages)");
+    uint32_t p = free_pages.back();
+    free_pages.pop_back();
+    refcount[p] = 1;
+    return p;
+  }
+
+  void drop_page(int32_t p) {
+    if (p < 0) return;
+    if (--refcount[p] == 0) free_pages.push_back((uint32_t)p);
+  }
+
+  // Makes the page that receives `position` of every active layer private to `slot`.
+  void prepare_append(uint32_t slot, const std::vector<int32_t>& active, uint32_t position) {
+    settle();
+    uint32_t index = position / PAGE_POSITIONS;
+    for (int32_t layer : active) {
+      int32_t& e = page_entry(slot, (uint32_t)layer, index);
+      if (e < 0) {
+        e = (int32_t)take_page();
+        slot_dirty[slot] = 1;
+      } else if (refcount[e] > 1) {
+        uint32_t fresh = take_page();
+        NB_CUDA(cudaMemcpyAsync(pool + (size_t)fresh * md.page.page_bytes, pool + (size_t)e * md.page.page_bytes, md.page.page_bytes,
+                                cudaMemcpyDeviceToDevice, stream));
+        --refcount[e];
+        e = (int32_t)fresh;
+        slot_dirty[slot] = 1;
+      }
+    }
+  }
+
+  void flush_page_tables() {
+    size_t row = (size_t)geo.num_layers * max_pages;
+    for (uint32_t s = 0; s < max_sessions; ++s) {
+      if (!slot_dirty[s]) continue;
+      NB_CUDA(cudaMemcpyAsync(d_page_table + s * row, h_table.as<int32_t>() + s * row, row * 4, cudaMemcpyHostToDevice, stream));
+      copies_in_flight = true;
+      slot_dirty[s] = 0;
+    }
+  }
+};
+
+// Path of the libm-exception table: $NEEDLE_B200_EXPF_TABLE, else beside this library.
+static std::string expf_table_path() {
+  if (const char* env = std::getenv("NEEDLE_B200_EXPF_TABLE")) return env;
+  Dl_info info;
+  if (dladdr(reinterpret_cast<void*>(&expf_table_path), &info) && info.dli_fname) {
+    std::string so = info.dli_fname;
+    size_t slash = so.rfind('/');
+    return (slash == std::string::npos ? std::string(".") : so.substr(0, slash)) + "/glibc_expf_exceptions.bin";
+  }
+  return "glibc_expf_exceptions.bin";
+}
+
+static std::mutex g_table_mutex;
+static std::shared_ptr<nbx::ExpfTable> g_table;
+
+static std::shared_ptr<nbx::ExpfTable> load_expf_table() {
+  std::lock_guard<std::mutex> lock(g_table_mutex);
+  if (g_table) return g_table;
+  auto table = std::make_shared<nbx::ExpfTable>();
+  std::string path = expf_table_path();
+  if (!nbx::read_expf_table(path.c_str(), *table) || !nbx::verify_expf_table(*table)) {
+    *table = nbx::scan_expf_exceptions(0);
+    if (table->unexplained) fail(NB_ERR_UNSUPPORTED, "the host expf has mismatches the device exponential cannot reproduce");
+    try {
+      nbx::write_expf_table(path.c_str(), *table);
+    } catch (...) {
+    }
+  }
+  g_table = table;
+  return table;
+}
+
+// Expands a codebook matrix to int8 through the integer level table, in the
+// projection kernel's lane-interleaved layout (K = 512 or 1024) or row-major.
+static void expand_matrix(const nba::Archive& a, uint32_t index, const Levels& lv, bool interleave, std::vector<int8_t>& codes,
+                          std::vector<float>& scales, uint32_t row_offset_codes, uint32_t row_offset_scales, uint32_t total_rows) {
+  const nba::Record& r = a.record(index);
+  uint64_t rows = r.rows(), cols = r.padded_columns(), groups = r.groups_per_row(), rb = r.packed_row_bytes();
+  const uint8_t* packed = a.data(index);
+  const uint8_t* norms = packed + r.packed_bytes();
+  if (r.packed_bytes() + rows * groups * 2 > r.byte_len) fail(NB_ERR_ARCHIVE, "codebook tensor " + std::to_string(index) + " is shorter than its shape");
+  uint32_t gk = (uint32_t)(cols / GROUP), RB = interleave ? 32 / gk : 1;
+  if (interleave) {
+    size_t blocks = (total_rows + RB - 1) / RB;
+    if (codes.size() < blocks * 4096) codes.resize(blocks * 4096, 0);
+  } else if (codes.size() < (size_t)total_rows * cols) {
+    codes.resize((size_t)total_rows * cols, 0);
+  }
+  if (scales.size() < (size_t)total_rows * groups) scales.resize((size_t)total_rows * groups, 0.0f);
+  for (uint64_t row = 0; row < rows; ++row) {
+    const uint8_t* src = packed + row * rb;
+    uint64_t out_row = row + row_offset_codes;
+    for (uint64_t c = 0; c < cols; ++c) {
+      int8_t v = lv.ints[code_at(src, c, lv.bits)];
+      if (interleave) {
+        uint64_t block = out_row / RB, rr = out_row % RB, g = c / GROUP, within = c % GROUP, k = within / 16, byte = within % 16;
+        uint64_t lane = rr * gk + g;
+        codes[((block * 8 + k) * 32 + lane) * 16 + byte] = v;
+      } else {
+        codes[out_row * cols + c] = v;
+      }
+    }
+    for (uint64_t g = 0; g < groups; ++g) {
+      uint16_t h;
+      std::memcpy(&h, norms + 2 * (row * groups + g), 2);
+      float norm = nba::half_to_f32(h);
+      scales[(row + row_offset_scales) * groups + g] = lv.fused ? norm * lv.int_scale : norm;
+    }
+  }
+}
+
+static void check_matrix(const nba::Archive& a, uint32_t index, uint64_t rows, uint64_t cols, const char* what) {
+  const nba::Record& r = a.record(index);
+  if (r.kind != nba::CODEBOOK) fail(NB_ERR_ARCHIVE, std::string(what) + " is not codebook-quantised");
+  if (r.rows() != rows || r.columns() != cols || r.group() != GROUP)
+    fail(NB_ERR_UNSUPPORTED, std::string(what) + " has shape " + std::to_string(r.rows()) + "x" + std::to_string(r.columns()) +
+                                 " group " + std::to_string(r.group_size));
+}
+
+static std::vector<float> floats_of(const nba::Archive& a, uint32_t index, size_t expected, const char* what) {
+  std::vector<float> v = a.floats(index);
+  if (expected && v.size() < expected) fail(NB_ERR_ARCHIVE, std::string(what) + " holds " + std::to_string(v.size()) + " values, expected " + std::to_string(expected));
+  return v;
+}
+
+std::shared_ptr<Engine> open_engine(const char* path, const nb_options* opt) {
+  nba::Archive a(path);
+  nba::Layout lay = a.resolve();
+  a.validate_tokenizer(lay.tokenizer);
+  const nba::Geometry& g = a.geometry();
+  if (g.qkv_conv_taps > 0) fail(NB_ERR_UNSUPPORTED, "qkv conv taps are not implemented by this build");
+  if (!g.engram_sites.empty()) fail(NB_ERR_UNSUPPORTED, "engram sites are not implemented by this build");
+  if (g.mhc_lanes != LANES) fail(NB_ERR_UNSUPPORTED, "only 4-lane models are implemented");
+  if (g.qk_head_dim != HEAD_DIM || g.v_head_dim != HEAD_DIM) fail(NB_ERR_UNSUPPORTED, "head dims other than 64 are not implemented");
+  if (g.d_model % GROUP || g.d_model > MAX_D || (g.d_model / GROUP != 4 && g.d_model / GROUP != 8))
+    fail(NB_ERR_UNSUPPORTED, "d_model " + std::to_string(g.d_model) + " is not implemented (512 or 1024)");
+  if (g.num_kv_heads == 0 || g.num_heads % g.num_kv_heads || g.num_heads / g.num_kv_heads > 4 ||
+      (g.num_heads / g.num_kv_heads == 3) || g.num_heads > MAX_HEADS || g.num_heads * HEAD_DIM != g.d_model)
+    fail(NB_ERR_UNSUPPORTED, "head layout is not implemented");
+  if (g.hada_n != 2048 && g.hada_n != 1024) fail(NB_ERR_UNSUPPORTED, "hada_n must be 1024 or 2048");
+  if (g.max_seq_len == 0 || g.max_seq_len > 8192) fail(NB_ERR_UNSUPPORTED, "max_seq_len must be in 1..8192");
+  if (g.output_vocab() > g.vocab || g.output_vocab() % 32 || g.output_vocab() > 8192)
+    fail(NB_ERR_UNSUPPORTED, "output vocab must be a multiple of 32 up to 8192");
+
+  auto E = std::make_shared<Engine>();
+  E->geo = g;
+  int device = opt && opt->device >= 0 ? opt->device : -1;
+  int count = 0;
+  if (cudaGetDeviceCount(&count) != cudaSuccess || count == 0) fail(NB_ERR_NO_DEVICE, "no CUDA device is visible");
+  if (device < 0) NB_CUDA(cudaGetDevice(&device));
+  if (device >= count) fail(NB_ERR_ARGUMENT, "device ordinal out of range");
+  E->device = device;
+  NB_CUDA(cudaSetDevice(device));
+  cudaDeviceProp prop;
+  NB_CUDA(cudaGetDeviceProperties(&prop, device));
+  if (prop.major != 10) fail(NB_ERR_NO_DEVICE, std::string("this build targets sm_100a; device is ") + prop.name);
+  NB_CUDA(cudaStreamCreateWithFlags(&E->stream, cudaStreamNonBlocking));
+  NB_CUDA(cudaStreamCreateWithFlags(&E->side, cudaStreamNonBlocking));
+  cudaStream_t st = E->stream;
+  DeviceArena& A = E->arena;
+
+  // libm-compatible exponential
+  auto table = load_expf_table();
+  uint32_t mask = 0;
+  E->exception_slots = nbx::hash_slots(*table, mask);
+  uint32_t* d_slots = A.upload(E->exception_slots, st);
+  nbx::ExpConstants constants = nbx::make_exp_constants();
+  nbk::set_exp_constants(constants, nbx::ExceptionSet{d_slots, mask}, st);
+  NB_CUDA(cudaGetLastError());
+
+  const uint32_t d = g.d_model, H = g.num_heads, KV = g.num_kv_heads, L = g.num_layers, N = g.hada_n;
+  const uint32_t qkvg_rows = 2 * H * HEAD_DIM + 2 * KV * HEAD_DIM;
+  ModelDev& md = E->md;
+  md.d_model = d;
+  md.heads = H;
+  md.kv_heads = KV;
+  md.vocab = g.vocab;
+  md.output_vocab = g.output_vocab();
+  md.hada_n = N;
+  md.hada_left = N / 32;
+  md.max_seq_len = g.max_seq_len;
+  md.num_layers = L;
+  md.sliding_window = g.sliding_window;
+  md.sqrt_d = std::sqrt((float)d);
+  md.inv_sqrt_group = 1.0f / std::sqrt((float)GROUP);
+  md.inv_root_qk = 1.0f / std::sqrt((float)HEAD_DIM);
+  md.page = page_geometry(KV);
+
+  // embedding: packed rows for the gather, int8 rows for the tied logits
+  check_matrix(a, lay.embedding, g.vocab, d, "the embedding");
+  const nba::Record& er = a.record(lay.embedding);
+  Levels elv = levels_for(er.bits, a.codebook(), er.group_size);
+  {
+    std::vector<uint8_t> packed(a.data(lay.embedding), a.data(lay.embedding) + er.packed_bytes());
+    md.embed_packed = A.upload(packed, st);
+    md.embed_bits = elv.bits;
+    md.embed_row_bytes = (uint32_t)er.packed_row_bytes();
+    md.embed_levels = A.upload(std::vector<float>(elv.values, elv.values + 16), st);
+    std::vector<float> norms((size_t)g.vocab * (d / GROUP));
+    const uint8_t* nb = a.data(lay.embedding) + er.packed_bytes();
+    for (size_t i = 0; i < norms.size(); ++i) {
+      uint16_t h;
+      std::memcpy(&h, nb + 2 * i, 2);
+      norms[i] = nba::half_to_f32(h);
+    }
+    md.embed_norms = A.upload(norms, st);
+    std::vector<int8_t> codes;
+    std::vector<float> scales;
+    expand_matrix(a, lay.embedding, elv, true, codes, scales, 0, 0, g.vocab);
+    // only the first output_vocab rows take part in the logits (session.rs:174-175)
+    md.logits = QMat{A.upload(codes, st), A.upload(scales, st), elv.int_scale, md.output_vocab, d, d / GROUP, elv.fused ? 1 : 0};
+  }
+  // lanes
+  {
+    const uint32_t n = LANES * d;
+    auto phi = [&](uint32_t index, uint32_t rows, const char* what) {
+      check_matrix(a, index, rows, n, what);
+      const nba::Record& r = a.record(index);
+      Levels lv = levels_for(r.bits, a.codebook(), r.group_size);
+      if (lv.fused) fail(NB_ERR_UNSUPPORTED, std::string(what) + " is 2-bit; the lane maps are implemented for 4-bit codes");
+      std::vector<int8_t> codes;
+      std::vector<float> scales;
+      expand_matrix(a, index, lv, false, codes, scales, 0, 0, rows);
+      return QMat{A.upload(codes, st), A.upload(scales, st), lv.int_scale, rows, n, n / GROUP, 0};
+    };
+    md.phi_pre = phi(lay.lanes.phi_pre, L * LANES, "phi_pre");
+    md.phi_post = phi(lay.lanes.phi_post, L * LANES, "phi_post");
+    md.phi_res = phi(lay.lanes.phi_res, L * LANES * LANES, "phi_res");
+    md.a_pre = A.upload(floats_of(a, lay.lanes.a_pre, L, "a_pre"), st);
+    md.a_post = A.upload(floats_of(a, lay.lanes.a_post, L, "a_post"), st);
+    md.a_res = A.upload(floats_of(a, lay.lanes.a_res, L, "a_res"), st);
+    md.b_pre = A.upload(floats_of(a, lay.lanes.b_pre, L * LANES, "b_pre"), st);
+    md.b_post = A.upload(floats_of(a, lay.lanes.b_post, L * LANES, "b_post"), st);
+    md.b_res = A.upload(floats_of(a, lay.lanes.b_res, L * LANES * LANES, "b_res"), st);
+  }
+  md.final_norm = A.upload(floats_of(a, lay.final_norm, d, "final_norm"), st);
+  for (int which = 0; which < 2; ++which) {
+    std::vector<float> p = floats_of(a, lay.perms[which], N, "hadamard permutation");
+    std::vector<int32_t> perm(N);
+    for (uint32_t i = 0; i < N; ++i) {
+      if (!(p[i] >= 0.0f) || p[i] >= (float)N) fail(NB_ERR_ARCHIVE, "hadamard permutation entry out of range");
+      perm[i] = (int32_t)p[i];
+    }
+    (which == 0 ? md.perm1 : md.perm2) = A.upload(perm, st);
+  }
+  // rotary table: angle = position as f32 * frequency (ops.rs:127-141), sin/cos of the host libm
+  {
+    std::vector<float> freq(HEAD_DIM / 2);
+    for (int i = 0; i < HEAD_DIM / 2; ++i) freq[i] = 1.0f / std::pow(g.rope_theta, 2.0f * (float)i / (float)HEAD_DIM);
+    std::vector<float2> rot((size_t)g.max_seq_len * (HEAD_DIM / 2));
+    for (uint32_t p = 0; p < g.max_seq_len; ++p)
+      for (int i = 0; i < HEAD_DIM / 2; ++i) {
+        float angle = (float)p * freq[i];
+        rot[(size_t)p * (HEAD_DIM / 2) + i] = make_float2(std::sin(angle), std::cos(angle));
+      }
+    md.rotary = A.upload(rot, st);
+  }
+  // layers
+  for (uint32_t l = 0; l < L; ++l) {
+    const nba::LayerIdx& t = lay.layers[l];
+    LayerDev D{};
+    check_matrix(a, t.q, H * HEAD_DIM, d, "q_proj");
+    check_matrix(a, t.k, KV * HEAD_DIM, d, "k_proj");
+    check_matrix(a, t.v, KV * HEAD_DIM, d, "v_proj");
+    check_matrix(a, t.gate, H * HEAD_DIM, d, "gate_proj");
+    check_matrix(a, t.out, d, H * HEAD_DIM, "out_proj");
+    Levels lq = levels_for(a.record(t.q).bits, a.codebook(), GROUP);
+    for (uint32_t m : {t.k, t.v, t.gate})
+      if (levels_for(a.record(m).bits, a.codebook(), GROUP).fused != lq.fused)
+        fail(NB_ERR_UNSUPPORTED, "q, k, v and gate projections must share one code width");
+    std::vector<int8_t> codes;
+    std::vector<float> scales;
+    uint32_t offset = 0;
+    for (uint32_t m : {t.q, t.k, t.v, t.gate}) {
+      Levels lv = levels_for(a.record(m).bits, a.codebook(), GROUP);
+      expand_matrix(a, m, lv, true, codes, scales, offset, offset, qkvg_rows);
+      offset += (uint32_t)a.record(m).rows();
+    }
+    D.qkvg = QMat{A.upload(codes, st), A.upload(scales, st), lq.int_scale, qkvg_rows, d, d / GROUP, lq.fused ? 1 : 0};
+    Levels lo = levels_for(a.record(t.out).bits, a.codebook(), GROUP);
+    codes.clear();
+    scales.clear();
+    expand_matrix(a, t.out, lo, true, codes, scales, 0, 0, d);
+    D.out = QMat{A.upload(codes, st), A.upload(scales, st), lo.int_scale, d, H * HEAD_DIM, (H * HEAD_DIM) / GROUP, lo.fused ? 1 : 0};
+    D.norm_in = A.upload(floats_of(a, t.norm_in, d, "norm_in"), st);
+    D.post_norm = A.upload(floats_of(a, t.post_norm, d, "post_norm"), st);
+    D.pre_hada = A.upload(floats_of(a, t.pre_hada, d, "pre_hada"), st);
+    D.q_norm = A.upload(floats_of(a, t.q_norm, HEAD_DIM, "q_norm"), st);
+    D.k_norm = A.upload(floats_of(a, t.k_norm, HEAD_DIM, "k_norm"), st);
+    D.attn_gate = floats_of(a, t.attn_gate, 1, "attn_gate")[0];
+    const nba::HadamardIdx& h = t.hada;
+    HadamardDev& HD = D.hada;
+    HD.d1 = A.upload(floats_of(a, h.d1, N, "d1"), st);
+    HD.d2 = A.upload(floats_of(a, h.d2, N, "d2"), st);
+    HD.b2 = A.upload(floats_of(a, h.b2, N, "b2"), st);
+    HD.d3 = A.upload(floats_of(a, h.d3, N, "d3"), st);
+    HD.d4 = A.upload(floats_of(a, h.d4, N, "d4"), st);
+    uint32_t pairs[3][2] = {{h.w1a, h.w1b}, {h.w2a, h.w2b}, {h.w3a, h.w3b}};
+    for (int i = 0; i < 3; ++i) {
+      std::vector<float> left = a.floats(pairs[i][0]), right = a.floats(pairs[i][1]);
+      size_t ls = (size_t)std::llround(std::sqrt((double)left.size())), rs = (size_t)std::llround(std::sqrt((double)right.size()));
+      if (rs != HADA_RIGHT || ls != md.hada_left || ls * rs != N)
+        fail(NB_ERR_UNSUPPORTED, "hadamard factors must be (hada_n/32)^2 and 32^2");
+      HD.left[i] = A.upload(left, st);
+      HD.right[i] = A.upload(right, st);
+    }
+    std::vector<float> cv = floats_of(a, h.cond_v, 0, "cond_v"), cu = floats_of(a, h.cond_u, 0, "cond_u");
+    if (cu.size() != (size_t)COND_RANK * N || cv.size() != (size_t)COND_RANK * d)
+      fail(NB_ERR_UNSUPPORTED, "the Hadamard condition must have rank 8");
+    HD.cond_v = A.upload(cv, st);
+    HD.cond_u = A.upload(cu, st);
+    D.global = (g.sliding_window == 0 || g.is_global_layer(l)) ? 1 : 0;
+    E->layers.push_back(D);
+  }
+
+  // sessions, KV pool, workspace
+  E->max_sessions = opt && opt->max_sessions ? opt->max_sessions : 256;
+  E->max_pages = (g.max_seq_len + PAGE_POSITIONS - 1) / PAGE_POSITIONS;
+  uint64_t default_pages = (uint64_t)E->max_sessions * L * E->max_pages;
+  size_t free_bytes = 0, total_bytes = 0;
+  NB_CUDA(cudaMemGetInfo(&free_bytes, &total_bytes));
+  uint64_t cap_pages = (uint64_t)(free_bytes * 0.6) / md.page.page_bytes;
+  E->num_pages = (uint32_t)(opt && opt->kv_pages ? opt->kv_pages : std::min<uint64_t>(default_pages, cap_pages));
+  if (E->num_pages == 0) fail(NB_ERR_ARGUMENT, "the KV pool holds no page");
+  E->pool = A.alloc<uint8_t>((size_t)E->num_pages * md.page.page_bytes);
+  E->refcount.assign(E->num_pages, 0);
+  for (uint32_t p = E->num_pages; p-- > 0;) E->free_pages.push_back(p);
+  const size_t table_entries = (size_t)E->max_sessions * L * E->max_pages;
+  E->h_table.ensure(table_entries * 4);
+  std::fill(E->h_table.as<int32_t>(), E->h_table.as<int32_t>() + table_entries, -1);
+  E->d_page_table = A.alloc<int32_t>(table_entries);
+  NB_CUDA(cudaMemcpyAsync(E->d_page_table, E->h_table.p, table_entries * 4, cudaMemcpyHostToDevice, st));
+  E->slot_dirty.assign(E->max_sessions, 0);
+  for (uint32_t s = E->max_sessions; s-- > 0;) E->free_slots.push_back(s);
+  E->d_hidden = A.alloc<float>((size_t)E->max_sessions * d);
+  NB_CUDA(cudaMemsetAsync(E->d_hidden, 0, (size_t)E->max_sessions * d * 4, st));
+
+  E->capacity = std::max<uint32_t>(opt && opt->max_batch_tokens ? opt->max_batch_tokens : 1024, E->max_sessions);
+  const uint32_t M = E->capacity, AW = H * HEAD_DIM, actw = std::max(d, AW);
+  Work& w = E->work;
+  w.capacity = M;
+  E->d_tokens = A.alloc<uint32_t>(M);
+  E->d_meta = A.alloc<TokenMeta>(M);
+  w.tokens = E->d_tokens;
+  w.meta = E->d_meta;
+  w.stream = A.alloc<float>((size_t)M * LANES * d);
+  w.next_stream = A.alloc<float>((size_t)M * LANES * d);
+  w.x = A.alloc<float>((size_t)M * d);
+  w.route = A.alloc<float>((size_t)M * (LANES + LANES * LANES));
+  w.act = A.alloc<int8_t>((size_t)M * actw);
+  w.act_scale = A.alloc<float>((size_t)M * (actw / GROUP));
+  w.proj = A.alloc<float>((size_t)M * qkvg_rows);
+  w.qcodes = A.alloc<int8_t>((size_t)M * H * HEAD_DIM);
+  w.qscale = A.alloc<float>((size_t)M * H);
+  w.attn = A.alloc<float>((size_t)M * AW);
+  w.outp = A.alloc<float>((size_t)M * d);
+  const uint32_t B = E->max_sessions, V = md.output_vocab;
+  E->d_logit_act = A.alloc<int8_t>((size_t)B * d);
+  E->d_logit_scale = A.alloc<float>((size_t)B * (d / GROUP));
+  E->d_logits = A.alloc<float>((size_t)B * V);
+  E->d_slots = A.alloc<int32_t>(B);
+  E->d_next = A.alloc<uint32_t>(B);
+  E->d_peaks = A.alloc<float>((size_t)2 * B);
+  E->d_stats = A.alloc<float>((size_t)2 * B);
+  E->d_mask = A.alloc<uint32_t>((size_t)B * (V / 32));
+  E->d_active = A.alloc<int32_t>(B);
+  E->h_tokens.ensure((size_t)M * 4);
+  E->h_meta.ensure((size_t)M * sizeof(TokenMeta));
+  E->t_cap = (int)((g.max_seq_len + 3) / 4 * 4);
+  NB_CUDA(nbk::configure(md, E->t_cap));
+  NB_CUDA(cudaStreamSynchronize(st));
+  return E;
+}
+
+// ------------------------------------------------------------ forward pass
+struct TokenSpec {
+  uint32_t token;
+  uint32_t slot;
+  uint32_t position;
+  bool last;
+};
+
+// Runs the forward pass of up to `capacity` tokens on the engine's stream
+// (embedding, every active layer, final norm into the sequences' hidden rows).
+void forward(Engine& E, const std::vector<int32_t>& active, const TokenSpec* specs, uint32_t count) {
+  E.settle();
+  for (uint32_t i = 0; i < count; ++i) E.prepare_append(specs[i].slot, active, specs[i].position);
+  E.flush_page_tables();
+  uint32_t* ht = E.h_tokens.as<uint32_t>();
+  TokenMeta* hm = E.h_meta.as<TokenMeta>();
+  for (uint32_t i = 0; i < count; ++i) {
+    ht[i] = specs[i].token;
+    hm[i] = TokenMeta{(int32_t)specs[i].slot, (int32_t)specs[i].position, specs[i].last ? 1 : 0, 0};
+  }
+  NB_CUDA(cudaMemcpyAsync(E.d_tokens, ht, count * 4, cudaMemcpyHostToDevice, E.stream));
+  NB_CUDA(cudaMemcpyAsync(E.d_meta, hm, count * sizeof(TokenMeta), cudaMemcpyHostToDevice, E.stream));
+  E.copies_in_flight = true;
+  Work w = E.work;
+  KvDev kv = E.kv();
+  nbk::launch_embed(E.md, w, (int)count, E.stream);
+  for (size_t slot = 0; slot < active.size(); ++slot) {
+    int layer = active[slot];
+    nbk::launch_layer(E.md, E.layers[layer], w, kv, (int)count, layer, (int)slot, E.t_cap, E.stream);
+    std::swap(w.stream, w.next_stream);
+  }
+  nbk::launch_final(E.md, w, E.d_hidden, (int)count, E.stream);
+  NB_CUDA(cudaGetLastError());
+  // the pass alternates stream buffers; keep the engine's pair consistent
+  E.work.stream = w.stream;
+  E.work.next_stream = w.next_stream;
+}
+
+}  // namespace nbr
+
+using namespace nbr;
+
+// ------------------------------------------------------------------- C ABI
+struct nb_model {
+  std::shared_ptr<Engine> engine;
+  std::vector<int32_t> active;
+};
+
+struct nb_session {
+  std::shared_ptr<Engine> engine;
+  std::vector<int32_t> active;
+  uint32_t slot = 0;
+  uint32_t length = 0;
+};
+
+struct nb_batch {
+  std::shared_ptr<Engine> engine;
+  std::vector<nb_session*> sessions;
+  std::vector<int32_t> active;
+  std::map<int, cudaGraphExec_t> graphs;  // key: mask | stats << 1
+  uint32_t* d_tokens = nullptr;           // the batch's token ids (= the chosen tokens)
+  TokenMeta* d_meta = nullptr;
+  PinnedBuffer h_meta, h_mask, h_next, h_stats, h_active;
+  DeviceArena arena;
+  cudaEvent_t fork = nullptr, join = nullptr;
+  bool use_graphs = true;
+  ~nb_batch() {
+    for (auto& kv : graphs) cudaGraphExecDestroy(kv.second);
+    if (fork) cudaEventDestroy(fork);
+    if (join) cudaEventDestroy(join);
+  }
+};
+
+extern "C" {
+
+const char* nb_last_error(void) { return g_error.c_str(); }
+
+nb_status nb_model_open(const char* path, const nb_options* options, nb_model** out) {
+  if (!out) return NB_ERR_ARGUMENT;
+  *out = nullptr;
+  return guard([&] {
+    if (!path) fail(NB_ERR_ARGUMENT, "path is null");
+    auto engine = open_engine(path, options);
+    auto* m = new nb_model();
+    m->engine = engine;
+    for (uint32_t l = 0; l < engine->geo.num_layers; ++l) m->active.push_back((int32_t)l);
+    *out = m;
+  });
+}
+
+// crates/model/src/ladder.rs:1-29
+static std::vector<int32_t> ladder_order(int layers) {
+  std::vector<int32_t> order;
+  if (layers <= 1) {
+    for (int i = 0; i < layers; ++i) order.push_back(i);
+    return order;
+  }
+  std::vector<int32_t> selected{0, layers - 1};
+  order = selected;
+  while ((int)order.size() < layers) {
+    std::sort(selected.begin(), selected.end());
+    int best_gap = -1, left = 0, right = 0;
+    for (size_t i = 0; i + 1 < selected.size(); ++i) {
+      int gap = selected[i + 1] - selected[i];
+      if (gap > 1 && (gap > best_gap || (gap == best_gap && selected[i] < left))) {
+        best_gap = gap;
+        left = selected[i];
+        right = selected[i + 1];
+      }
+    }
+    selected.push_back((left + right) / 2);
+    order.push_back((left + right) / 2);
+  }
+  return order;
+}
+
+nb_status nb_model_with_depth(const nb_model* model, uint32_t depth, nb_model** out) {
+  if (!model || !out) return NB_ERR_ARGUMENT;
+  *out = nullptr;
+  int layers = (int)model->engine->geo.num_layers;
+  if ((int)depth < std::min(2, layers) || (int)depth > layers) {
+    g_error = "depth " + std::to_string(depth) + " is outside the 2 to " + std::to_string(layers) + " layers this model offers";
+    return NB_ERR_DEPTH;
+  }
+  auto order = ladder_order(layers);
+  std::vector<int32_t> active(order.begin(), order.begin() + depth);
+  std::sort(active.begin(), active.end());
+  auto* m = new nb_model();
+  m->engine = model->engine;
+  m->active = active;
+  *out = m;
+  return NB_OK;
+}
+
+nb_status nb_model_get_config(const nb_model* model, nb_model_config* out) {
+  if (!model || !out) return NB_ERR_ARGUMENT;
+  const nba::Geometry& g = model->engine->geo;
+  std::memset(out, 0, sizeof *out);
+  out->vocab = g.vocab;
+  out->output_vocab = g.output_vocab();
+  out->d_model = g.d_model;
+  out->num_heads = g.num_heads;
+  out->num_kv_heads = g.num_kv_heads;
+  out->num_layers = g.num_layers;
+  out->head_dim = g.qk_head_dim;
+  out->max_seq_len = g.max_seq_len;
+  out->hada_n = g.hada_n;
+  out->lanes = g.mhc_lanes;
+  out->depth = (uint32_t)model->active.size();
+  for (size_t i = 0; i < model->active.size() && i < 64; ++i) out->active_layers[i] = model->active[i];
+  out->rope_theta = g.rope_theta;
+  return NB_OK;
+}
+
+void nb_model_release(nb_model* model) { delete model; }
+
+nb_status nb_model_synchronize(nb_model* model) {
+  if (!model) return NB_ERR_ARGUMENT;
+  return guard([&] {
+    NB_CUDA(cudaSetDevice(model->engine->device));
+    NB_CUDA(cudaStreamSynchronize(model->engine->stream));
+  });
+}
+
+nb_status nb_session_create(nb_model* model, nb_session** out) {
+  if (!model || !out) return NB_ERR_ARGUMENT;
+  *out = nullptr;
+  return guard([&] {
+    Engine& E = *model->engine;
+    std::lock_guard<std::mutex> lock(E.mutex);
+    if (E.free_slots.empty()) fail(NB_ERR_ARGUMENT, "every session slot is in use (max_sessions " + std::to_string(E.max_sessions) + ")");
+    NB_CUDA(cudaSetDevice(E.device));
+    auto* s = new nb_session();
+    s->engine = model->engine;
+    s->active = model->active;
+    s->slot = E.free_slots.back();
+    E.free_slots.pop_back();
+    NB_CUDA(cudaMemsetAsync(E.d_hidden + (size_t)s->slot * E.md.d_model, 0, E.md.d_model * 4, E.stream));
+    *out = s;
+  });
+}
+
+nb_status nb_session_clone(const nb_session* session, nb_session** out) {
+  if (!session || !out) return NB_ERR_ARGUMENT;
+  *out = nullptr;
+  return guard([&] {
+    Engine& E = *session->engine;
+    std::lock_guard<std::mutex> lock(E.mutex);
+    if (E.free_slots.empty()) fail(NB_ERR_ARGUMENT, "every session slot is in use");
+    NB_CUDA(cudaSetDevice(E.device));
+    E.settle();
+    auto* s = new nb_session(*session);
+    s->slot = E.free_slots.back();
+    E.free_slots.pop_back();
+    for (uint32_t l = 0; l < E.geo.num_layers; ++l)
+      for (uint32_t i = 0; i < E.max_pages; ++i) {
+        int32_t p = E.page_entry(session->slot, l, i);
+        E.page_entry(s->slot, l, i) = p;
+        if (p >= 0) ++E.refcount[p];
+      }
+    E.slot_dirty[s->slot] = 1;
+    NB_CUDA(cudaMemcpyAsync(E.d_hidden + (size_t)s->slot * E.md.d_model, E.d_hidden + (size_t)session->slot * E.md.d_model,
+                            E.md.d_model * 4, cudaMemcpyDeviceToDevice, E.stream));
+    *out = s;
+  });
+}
+
+void nb_session_release(nb_session* session) {
+  if (!session) return;
+  Engine& E = *session->engine;
+  {
+    std::lock_guard<std::mutex> lock(E.mutex);
+    cudaSetDevice(E.device);
+    try {
+      E.settle();
+    } catch (...) {
+    }
+    for (uint32_t l = 0; l < E.geo.num_layers; ++l)
+      for (uint32_t i = 0; i < E.max_pages; ++i) {
+        int32_t& p = E.page_entry(session->slot, l, i);
+        E.drop_page(p);
+        p = -1;
+      }
+    E.slot_dirty[session->slot] = 1;
+    E.free_slots.push_back(session->slot);
+  }
+  delete session;
+}
+
+size_t nb_session_len(const nb_session* session) { return session ? session->length : 0; }
+
+static void check_tokens(const Engine& E, const uint32_t* ids, size_t count) {
+  for (size_t i = 0; i < count; ++i)
+    if (ids[i] >= E.geo.vocab) fail(NB_ERR_ARGUMENT, "token id " + std::to_string(ids[i]) + " is outside the vocabulary");
+}
+
+static void run_tokens(nb_session* s, const uint32_t* ids, size_t count) {
+  Engine& E = *s->engine;
+  if (s->length + count > E.geo.max_seq_len)
+    fail(NB_ERR_CONTEXT_OVERFLOW, "the session would exceed max_seq_len " + std::to_string(E.geo.max_seq_len));
+  NB_CUDA(cudaSetDevice(E.device));
+  std::vector<TokenSpec> specs;
+  size_t done = 0;
+  while (done < count) {
+    size_t n = std::min<size_t>(E.capacity, count - done);
+    specs.resize(n);
+    for (size_t i = 0; i < n; ++i) specs[i] = TokenSpec{ids[done + i], s->slot, (uint32_t)(s->length + done + i), i + 1 == n};
+    forward(E, s->active, specs.data(), (uint32_t)n);
+    done += n;
+  }
+  NB_CUDA(cudaStreamSynchronize(E.stream));
+  s->length += (uint32_t)count;
+}
+
+nb_status nb_session_feed(nb_session* session, const uint32_t* ids, size_t count) {
+  if (!session || (!ids && count)) return NB_ERR_ARGUMENT;
+  return guard([&] {
+    Engine& E = *session->engine;
+    std::lock_guard<std::mutex> lock(E.mutex);
+    check_tokens(E, ids, count);
+    if (count) run_tokens(session, ids, count);
+  });
+}
+
+nb_status nb_session_push(nb_session* session, uint32_t id) {
+  if (!session) return NB_ERR_ARGUMENT;
+  return guard([&] {
+    Engine& E = *session->engine;
+    std::lock_guard<std::mutex> lock(E.mutex);
+    check_tokens(E, &id, 1);
+    run_tokens(session, &id, 1);
+  });
+}
+
+nb_status nb_session_logits(nb_session* session, float* out, size_t capacity) {
+  if (!session || !out) return NB_ERR_ARGUMENT;
+  return guard([&] {
+    Engine& E = *session->engine;
+    std::lock_guard<std::mutex> lock(E.mutex);
+    uint32_t V = E.md.output_vocab;
+    if (capacity < V) fail(NB_ERR_ARGUMENT, "the logits buffer holds fewer than output_vocab floats");
+    NB_CUDA(cudaSetDevice(E.device));
+    int32_t slot = (int32_t)session->slot;
+    NB_CUDA(cudaMemcpyAsync(E.d_slots, &slot, 4, cudaMemcpyHostToDevice, E.stream));
+    nbk::launch_logits(E.md, E.d_hidden, E.d_slots, 1, E.d_logit_act, E.d_logit_scale, E.d_logits, E.stream);
+    NB_CUDA(cudaGetLastError());
+    NB_CUDA(cudaMemcpyAsync(out, E.d_logits, (size_t)V * 4, cudaMemcpyDeviceToHost, E.stream));
+    NB_CUDA(cudaStreamSynchronize(E.stream));
+  });
+}
+
+// ------------------------------------------------------------------ batches
+static void build_step(nb_batch* b, bool masked, bool stats) {
+  Engine& E = *b->engine;
+  const int B = (int)b->sessions.size();
+  const uint32_t V = E.md.output_vocab;
+  cudaStream_t st = E.stream;
+  nbk::launch_logits(E.md, E.d_hidden, E.d_slots, B, E.d_logit_act, E.d_logit_scale, E.d_logits, st);
+  nbk::launch_select(E.d_logits, (int)V, masked ? E.d_mask : nullptr, E.d_active, b->d_tokens, E.d_peaks, B, st);
+  if (stats) {
+    NB_CUDA(cudaEventRecord(b->fork, st));
+    NB_CUDA(cudaStreamWaitEvent(E.side, b->fork, 0));
+    nbk::launch_stats(E.d_logits, (int)V, masked ? E.d_mask : nullptr, E.d_active, b->d_tokens, E.d_peaks, E.d_stats, 2, B, E.side);
+  }
+  Work w = E.work;
+  w.tokens = b->d_tokens;
+  w.meta = b->d_meta;
+  KvDev kv = E.kv();
+  nbk::launch_embed(E.md, w, B, st);
+  for (size_t slot = 0; slot < b->active.size(); ++slot) {
+    int layer = b->active[slot];
+    nbk::launch_layer(E.md, E.layers[layer], w, kv, B, layer, (int)slot, E.t_cap, st);
+    std::swap(w.stream, w.next_stream);
+  }
+  nbk::launch_final(E.md, w, E.d_hidden, B, st);
+  nbk::launch_advance(b->d_meta, B, st);
+  if (stats) {
+    NB_CUDA(cudaEventRecord(b->join, E.side));
+    NB_CUDA(cudaStreamWaitEvent(st, b->join, 0));
+  }
+}
+
+nb_status nb_batch_create(nb_model* model, nb_session* const* sessions, uint32_t count, nb_batch** out) {
+  if (!model || !out || (!sessions && count)) return NB_ERR_ARGUMENT;
+  *out = nullptr;
+  return guard([&] {
+    Engine& E = *model->engine;
+    std::lock_guard<std::mutex> lock(E.mutex);
+    if (count == 0 || count > E.max_sessions || count > E.capacity) fail(NB_ERR_ARGUMENT, "batch size must be in 1..max_sessions");
+    NB_CUDA(cudaSetDevice(E.device));
+    auto b = std::make_unique<nb_batch>();
+    b->engine = model->engine;
+    b->active = model->active;
+    for (uint32_t i = 0; i < count; ++i) {
+      if (!sessions[i] || sessions[i]->engine != model->engine) fail(NB_ERR_ARGUMENT, "every session must belong to the batch's model");
+      if (sessions[i]->active != model->active) fail(NB_ERR_ARGUMENT, "every session must run the batch model's depth");
+      for (uint32_t j = 0; j < i; ++j)
+        if (sessions[j] == sessions[i]) fail(NB_ERR_ARGUMENT, "a session appears twice in the batch");
+      b->sessions.push_back(sessions[i]);
+    }
+    b->d_tokens = b->arena.alloc<uint32_t>(count);
+    b->d_meta = b->arena.alloc<TokenMeta>(count);
+    b->h_meta.ensure(count * sizeof(TokenMeta));
+    b->h_next.ensure(count * 4);
+    b->h_stats.ensure(count * 8);
+    b->h_active.ensure(count * 4);
+    b->h_mask.ensure((size_t)count * (E.md.output_vocab / 32) * 4);
+    NB_CUDA(cudaEventCreateWithFlags(&b->fork, cudaEventDisableTiming));
+    NB_CUDA(cudaEventCreateWithFlags(&b->join, cudaEventDisableTiming));
+    *out = b.release();
+  });
+}
+
+void nb_batch_release(nb_batch* batch) {
+  if (!batch) return;
+  {
+    std::lock_guard<std::mutex> lock(batch->engine->mutex);
+    cudaSetDevice(batch->engine->device);
+    cudaStreamSynchronize(batch->engine->stream);
+  }
+  delete batch;
+}
+
+// Host part of a step: which sequences can grow, their pages, their metadata.
+static uint32_t stage_step(nb_batch* b) {
+  Engine& E = *b->engine;
+  E.settle();
+  const uint32_t B = (uint32_t)b->sessions.size();
+  TokenMeta* hm = b->h_meta.as<TokenMeta>();
+  int32_t* ha = b->h_active.as<int32_t>();
+  std::vector<int32_t> slots(B);
+  uint32_t live = 0;
+  for (uint32_t i = 0; i < B; ++i) {
+    nb_session* s = b->sessions[i];
+    slots[i] = (int32_t)s->slot;
+    // generator.rs:99: a step needs session.len() + 1 < max_seq_len
+    bool ok = s->length + 1 < E.geo.max_seq_len;
+    ha[i] = ok ? 1 : 0;
+    hm[i] = TokenMeta{ok ? (int32_t)s->slot : -1, (int32_t)s->length, 1, 0};
+    if (ok) {
+      E.prepare_append(s->slot, b->active, s->length);
+      ++live;
+    }
+  }
+  E.flush_page_tables();
+  E.h_misc.ensure(B * 4);
+  std::memcpy(E.h_misc.p, slots.data(), B * 4);
+  NB_CUDA(cudaMemcpyAsync(E.d_slots, E.h_misc.p, B * 4, cudaMemcpyHostToDevice, E.stream));
+  NB_CUDA(cudaMemcpyAsync(b->d_meta, hm, B * sizeof(TokenMeta), cudaMemcpyHostToDevice, E.stream));
+  NB_CUDA(cudaMemcpyAsync(E.d_active, ha, B * 4, cudaMemcpyHostToDevice, E.stream));
+  E.copies_in_flight = true;
+  return live;
+}
+
+static void launch_step(nb_batch* b, bool masked, bool stats) {
+  Engine& E = *b->engine;
+  if (!b->use_graphs) {
+    build_step(b, masked, stats);
+    NB_CUDA(cudaGetLastError());
+    return;
+  }
+  int key = (masked ? 1 : 0) | (stats ? 2 : 0);
+  auto it = b->graphs.find(key);
+  if (it == b->graphs.end()) {
+    cudaGraph_t graph;
+    NB_CUDA(cudaStreamBeginCapture(E.stream, cudaStreamCaptureModeThreadLocal));
+    try {
+      build_step(b, masked, stats);
+    } catch (...) {
+      cudaStreamEndCapture(E.stream, &graph);
+      throw;
+    }
+    NB_CUDA(cudaStreamEndCapture(E.stream, &graph));
+    cudaGraphExec_t exec;
+    cudaError_t e = cudaGraphInstantiate(&exec, graph, 0);
+    cudaGraphDestroy(graph);
+    if (e != cudaSuccess) fail(NB_ERR_CUDA, std::string("cudaGraphInstantiate: ") + cudaGetErrorString(e));
+    it = b->graphs.emplace(key, exec).first;
+  }
+  NB_CUDA(cudaGraphLaunch(it->second, E.stream));
+}
+
+static void finish_step(nb_batch* b) {
+  for (size_t i = 0; i < b->sessions.size(); ++i)
+    if (b->h_active.as<int32_t>()[i]) b->sessions[i]->length += 1;
+}
+
+nb_status nb_batch_step(nb_batch* batch, const uint32_t* mask_bits, uint32_t* next, nb_step_stats* stats) {
+  if (!batch || !next) return NB_ERR_ARGUMENT;
+  return guard([&] {
+    Engine& E = *batch->engine;
+    std::lock_guard<std::mutex> lock(E.mutex);
+    NB_CUDA(cudaSetDevice(E.device));
+    const uint32_t B = (uint32_t)batch->sessions.size(), words = E.md.output_vocab / 32;
+    stage_step(batch);
+    if (mask_bits) {
+      std::memcpy(batch->h_mask.p, mask_bits, (size_t)B * words * 4);
+      NB_CUDA(cudaMemcpyAsync(E.d_mask, batch->h_mask.p, (size_t)B * words * 4, cudaMemcpyHostToDevice, E.stream));
+    }
+    launch_step(batch, mask_bits != nullptr, stats != nullptr);
+    NB_CUDA(cudaMemcpyAsync(batch->h_next.p, batch->d_tokens, B * 4, cudaMemcpyDeviceToHost, E.stream));
+    if (stats) NB_CUDA(cudaMemcpyAsync(batch->h_stats.p, E.d_stats, (size_t)B * 8, cudaMemcpyDeviceToHost, E.stream));
+    NB_CUDA(cudaStreamSynchronize(E.stream));
+    const int32_t* ha = batch->h_active.as<int32_t>();
+    for (uint32_t i = 0; i < B; ++i) {
+      next[i] = ha[i] ? batch->h_next.as<uint32_t>()[i] : 0xffffffffu;
+      if (stats) {
+        stats[i].probability = ha[i] ? batch->h_stats.as<float>()[2 * i] : 0.0f;
+        stats[i].mass = ha[i] ? batch->h_stats.as<float>()[2 * i + 1] : 1.0f;
+        stats[i].status = ha[i] ? NB_OK : NB_ERR_CONTEXT_OVERFLOW;
+      }
+    }
+    finish_step(batch);
+  });
+}
+
+nb_status nb_batch_step_device(nb_batch* batch, const uint32_t* mask_bits_device, uint32_t* next_device, nb_step_stats* stats_device) {
+  if (!batch || !next_device || stats_device) {
+    g_error = "nb_batch_step_device takes device pointers for next and mask, and no stats";
+    return NB_ERR_ARGUMENT;
+  }
+  return guard([&] {
+    Engine& E = *batch->engine;
+    std::lock_guard<std::mutex> lock(E.mutex);
+    NB_CUDA(cudaSetDevice(E.device));
+    const uint32_t B = (uint32_t)batch->sessions.size(), words = E.md.output_vocab / 32;
+    stage_step(batch);
+    if (mask_bits_device)
+      NB_CUDA(cudaMemcpyAsync(E.d_mask, mask_bits_device, (size_t)B * words * 4, cudaMemcpyDeviceToDevice, E.stream));
+    launch_step(batch, mask_bits_device != nullptr, false);
+    NB_CUDA(cudaMemcpyAsync(next_device, batch->d_tokens, B * 4, cudaMemcpyDeviceToDevice, E.stream));
+    NB_CUDA(cudaStreamSynchronize(E.stream));
+    finish_step(batch);
+  });
+}
+
+nb_status nb_batch_run(nb_batch* batch, uint32_t steps, const uint32_t* mask_bits_device, uint32_t* tokens_device,
+                       float* elapsed_ms) {
+  if (!batch || steps == 0) return NB_ERR_ARGUMENT;
+  return guard([&] {
+    Engine& E = *batch->engine;
+    std::lock_guard<std::mutex> lock(E.mutex);
+    NB_CUDA(cudaSetDevice(E.device));
+    const uint32_t B = (uint32_t)batch->sessions.size(), words = E.md.output_vocab / 32;
+    for (nb_session* s : batch->sessions)
+      if (s->length + steps >= E.geo.max_seq_len)
+        fail(NB_ERR_CONTEXT_OVERFLOW, "a session of the batch cannot take " + std::to_string(steps) + " more tokens");
+    // pages for every position the run will write, then the usual staging
+    for (nb_session* s : batch->sessions)
+      for (uint32_t k = 1; k < steps; ++k)
+        if ((s->length + k) % PAGE_POSITIONS == 0) E.prepare_append(s->slot, batch->active, s->length + k);
+    stage_step(batch);
+    cudaEvent_t start, stop;
+    NB_CUDA(cudaEventCreate(&start));
+    NB_CUDA(cudaEventCreate(&stop));
+    NB_CUDA(cudaEventRecord(start, E.stream));
+    for (uint32_t k = 0; k < steps; ++k) {
+      if (mask_bits_device)
+        NB_CUDA(cudaMemcpyAsync(E.d_mask, mask_bits_device + (size_t)k * B * words, (size_t)B * words * 4, cudaMemcpyDeviceToDevice,
+                                E.stream));
+      launch_step(batch, mask_bits_device != nullptr, false);
+      if (tokens_device)
+        NB_CUDA(cudaMemcpyAsync(tokens_device + (size_t)k * B, batch->d_tokens, B * 4, cudaMemcpyDeviceToDevice, E.stream));
+    }
+    NB_CUDA(cudaEventRecord(stop, E.stream));
+    NB_CUDA(cudaEventSynchronize(stop));
+    float ms = 0.0f;
+    NB_CUDA(cudaEventElapsedTime(&ms, start, stop));
+    cudaEventDestroy(start);
+    cudaEventDestroy(stop);
+    if (elapsed_ms) *elapsed_ms = ms;
+    for (nb_session* s : batch->sessions) s->length += steps;
+  });
+}
+
+nb_status nb_session_step(nb_session* session, const uint32_t* mask_bits, uint32_t* next, nb_step_stats* stats) {
+  if (!session || !next) return NB_ERR_ARGUMENT;
+  nb_model m;
+  m.engine = session->engine;
+  m.active = session->active;
+  nb_batch* b = nullptr;
+  nb_status s = nb_batch_create(&m, &session, 1, &b);
+  if (s != NB_OK) return s;
+  b->use_graphs = false;
+  nb_step_stats st{};
+  s = nb_batch_step(b, mask_bits, next, stats ? &st : nullptr);
+  if (stats) *stats = st;
+  if (s == NB_OK && stats && st.status != NB_OK) {
+    g_error = "the session's context is full";
+    s = NB_ERR_CONTEXT_OVERFLOW;
+  }
+  nb_batch_release(b);
+  return s;
+}
+
+nb_status nb_build_expf_table(const char* path) {
+  if (!path) return NB_ERR_ARGUMENT;
+  return guard([&] {
+    nbx::ExpfTable table = nbx::scan_expf_exceptions(0);
+    if (table.unexplained) fail(NB_ERR_UNSUPPORTED, "the host expf has mismatches the device exponential cannot reproduce");
+    nbx::write_expf_table(path, table);
+  });
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------- test hooks
+#include "../../include/needle_b200_debug.h"
+
+namespace nbr {
+template <typename T>
+struct DeviceTemp {
+  T* p = nullptr;
+  explicit DeviceTemp(size_t n) { NB_CUDA(cudaMalloc(&p, std::max<size_t>(n * sizeof(T), 16))); }
+  ~DeviceTemp() { cudaFree(p); }
+};
+}  // namespace nbr
+
+extern "C" {
+
+nb_status nb_debug_math(nb_model* model, int op, const float* in, float* out, size_t count) {
+  if (!model || !in || !out || op < 0 || op > 3) return NB_ERR_ARGUMENT;
+  return guard([&] {
+    Engine& E = *model->engine;
+    std::lock_guard<std::mutex> lock(E.mutex);
+    NB_CUDA(cudaSetDevice(E.device));
+    E.settle();
+    DeviceTemp<float> din(count), dout(count);
+    NB_CUDA(cudaMemcpyAsync(din.p, in, count * 4, cudaMemcpyHostToDevice, E.stream));
+    nbk::launch_debug_math(op, din.p, dout.p, (int)count, E.stream);
+    NB_CUDA(cudaGetLastError());
+    NB_CUDA(cudaMemcpyAsync(out, dout.p, count * 4, cudaMemcpyDeviceToHost, E.stream));
+    NB_CUDA(cudaStreamSynchronize(E.stream));
+  });
+}
+
+nb_status nb_debug_project(nb_model* model, int which, uint32_t layer, const float* in, size_t count, float* out) {
+  if (!model || !in || !out || count == 0) return NB_ERR_ARGUMENT;
+  return guard([&] {
+    Engine& E = *model->engine;
+    std::lock_guard<std::mutex> lock(E.mutex);
+    if (layer >= E.layers.size() || which < 0 || which > 2) fail(NB_ERR_ARGUMENT, "no such matrix");
+    const QMat& W = which == 0 ? E.layers[layer].qkvg : which == 1 ? E.layers[layer].out : E.md.logits;
+    NB_CUDA(cudaSetDevice(E.device));
+    E.settle();
+    const uint32_t K = W.cols;
+    DeviceTemp<float> din(count * K), dout(count * W.rows), dscale(count * W.groups);
+    DeviceTemp<int8_t> dact(count * K);
+    NB_CUDA(cudaMemcpyAsync(din.p, in, count * K * 4, cudaMemcpyHostToDevice, E.stream));
+    nbk::launch_debug_project(E.md, W, din.p, (int)K, (int)count, dact.p, dscale.p, dout.p, (int)W.rows, E.stream);
+    NB_CUDA(cudaGetLastError());
+    NB_CUDA(cudaMemcpyAsync(out, dout.p, count * W.rows * 4, cudaMemcpyDeviceToHost, E.stream));
+    NB_CUDA(cudaStreamSynchronize(E.stream));
+  });
+}
+
+nb_status nb_debug_hidden(nb_session* session, float* out) {
+  if (!session || !out) return NB_ERR_ARGUMENT;
+  return guard([&] {
+    Engine& E = *session->engine;
+    std::lock_guard<std::mutex> lock(E.mutex);
+    NB_CUDA(cudaSetDevice(E.device));
+    NB_CUDA(cudaMemcpyAsync(out, E.d_hidden + (size_t)session->slot * E.md.d_model, E.md.d_model * 4, cudaMemcpyDeviceToHost,
+                            E.stream));
+    NB_CUDA(cudaStreamSynchronize(E.stream));
+  });
+}
+
+nb_status nb_debug_kv(nb_session* session, uint32_t layer, int8_t* keys, float* key_scales, int8_t* values, float* value_scales) {
+  if (!session) return NB_ERR_ARGUMENT;
+  return guard([&] {
+    Engine& E = *session->engine;
+    std::lock_guard<std::mutex> lock(E.mutex);
+    if (layer >= E.geo.num_layers) fail(NB_ERR_ARGUMENT, "no such layer");
+    NB_CUDA(cudaSetDevice(E.device));
+    E.settle();
+    const PageGeometry& pg = E.md.page;
+    const uint32_t n = session->length, KV = pg.kv_heads;
+    std::vector<uint8_t> page(pg.page_bytes);
+    for (uint32_t base = 0; base < n; base += PAGE_POSITIONS) {
+      int32_t p = E.page_entry(session->slot, layer, base / PAGE_POSITIONS);
+      if (p < 0) fail(NB_ERR_ARGUMENT, "the layer holds no page at this position");
+      NB_CUDA(cudaMemcpy(page.data(), E.pool + (size_t)p * pg.page_bytes, pg.page_bytes, cudaMemcpyDeviceToHost));
+      for (uint32_t i = 0; i < PAGE_POSITIONS && base + i < n; ++i) {
+        uint32_t pos = base + i;
+        for (uint32_t h = 0; h < KV; ++h) {
+          for (uint32_t dim = 0; dim < HEAD_DIM; ++dim) {
+            if (keys) keys[((size_t)pos * KV + h) * HEAD_DIM + dim] = (int8_t)page[((size_t)h * PAGE_POSITIONS + i) * HEAD_DIM + dim];
+            if (values)
+              values[((size_t)pos * KV + h) * HEAD_DIM + dim] =
+                  (int8_t)page[pg.value_offset + (size_t)h * PAGE_POSITIONS * HEAD_DIM + (i / 4) * (HEAD_DIM * 4) + dim * 4 + i % 4];
+          }
+          float ks, vs;
+          std::memcpy(&ks, &page[pg.kscale_offset + ((size_t)h * PAGE_POSITIONS + i) * 4], 4);
+          std::memcpy(&vs, &page[pg.vscale_offset + ((size_t)h * PAGE_POSITIONS + i) * 4], 4);
+          if (key_scales) key_scales[(size_t)h * n + pos] = ks;
+          if (value_scales) value_scales[(size_t)h * n + pos] = vs;
+        }
+      }
+    }
+  });
+}
+
+}  // extern "C"
+
+extern "C" nb_status nb_debug_time_attention(nb_batch* batch, uint32_t reps, float* ms_per_launch, double* bytes_per_launch) {
+  if (!batch || reps == 0 || !ms_per_launch) return NB_ERR_ARGUMENT;
+  return guard([&] {
+    Engine& E = *batch->engine;
+    std::lock_guard<std::mutex> lock(E.mutex);
+    NB_CUDA(cudaSetDevice(E.device));
+    E.settle();
+    const uint32_t B = (uint32_t)batch->sessions.size();
+    // the batch's current positions (the last step's tokens were appended at length-1)
+    TokenMeta* hm = batch->h_meta.as<TokenMeta>();
+    double bytes = 0.0;
+    const double per_position = (double)E.md.kv_heads * (2 * HEAD_DIM + 8);
+    for (uint32_t i = 0; i < B; ++i) {
+      nb_session* s = batch->sessions[i];
+      uint32_t pos = s->length ? s->length - 1 : 0;
+      hm[i] = TokenMeta{(int32_t)s->slot, (int32_t)pos, 1, 0};
+      bytes += (double)(pos + 1) * per_position;
+    }
+    NB_CUDA(cudaMemcpyAsync(batch->d_meta, hm, B * sizeof(TokenMeta), cudaMemcpyHostToDevice, E.stream));
+    Work w = E.work;
+    w.meta = batch->d_meta;
+    KvDev kv = E.kv();
+    cudaEvent_t start, stop;
+    NB_CUDA(cudaEventCreate(&start));
+    NB_CUDA(cudaEventCreate(&stop));
+    // one untimed round warms the caches the way the step does
+    for (int32_t layer : batch->active) nbk::launch_attend(E.md, E.layers[layer], w, kv, (int)B, layer, E.t_cap, E.stream);
+    NB_CUDA(cudaEventRecord(start, E.stream));
+    for (uint32_t r = 0; r < reps; ++r)
+      for (int32_t layer : batch->active) nbk::launch_attend(E.md, E.layers[layer], w, kv, (int)B, layer, E.t_cap, E.stream);
+    NB_CUDA(cudaEventRecord(stop, E.stream));
+    NB_CUDA(cudaEventSynchronize(stop));
+    NB_CUDA(cudaGetLastError());
+    float ms = 0.0f;
+    NB_CUDA(cudaEventElapsedTime(&ms, start, stop));
+    cudaEventDestroy(start);
+    cudaEventDestroy(stop);
+    *ms_per_launch = ms / (float)(reps * batch->active.size());
+    if (bytes_per_launch) *bytes_per_launch = bytes;
+  });
+}

@@ -1,0 +1,78 @@
+"""Kernel-level test hooks (include/needle_b200_debug.h): single kernels of the
+library run on their own so the tests can compare them with the CPU restatement."""
+
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+
+from ._native import Model, Session, _check, _ptr, lib
+
+OP_EXPF, OP_SIGMOID, OP_FAST_EXP, OP_SILU = 0, 1, 2, 3
+MATRIX_QKVG, MATRIX_OUT, MATRIX_LOGITS = 0, 1, 2
+
+_declared = False
+
+
+def _declare() -> None:
+    global _declared
+    if _declared:
+        return
+    L = lib()
+    P, SZ, U32, I = ctypes.c_void_p, ctypes.c_size_t, ctypes.c_uint32, ctypes.c_int
+    for name, args in {
+        "nb_debug_math": [P, I, P, P, SZ],
+        "nb_debug_project": [P, I, U32, P, SZ, P],
+        "nb_debug_hidden": [P, P],
+        "nb_debug_kv": [P, U32, P, P, P, P],
+        "nb_debug_time_attention": [P, U32, ctypes.POINTER(ctypes.c_float), ctypes.POINTER(ctypes.c_double)],
+    }.items():
+        fn = getattr(L, name)
+        fn.restype = I
+        fn.argtypes = args
+    _declared = True
+
+
+def math(model: Model, op: int, x: np.ndarray) -> np.ndarray:
+    _declare()
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    out = np.empty_like(x)
+    _check(lib().nb_debug_math(model._h, op, _ptr(x), _ptr(out), x.size))
+    return out
+
+
+def project(model: Model, which: int, layer: int, x: np.ndarray, rows: int) -> np.ndarray:
+    _declare()
+    x = np.ascontiguousarray(np.atleast_2d(x), dtype=np.float32)
+    out = np.empty((x.shape[0], rows), dtype=np.float32)
+    _check(lib().nb_debug_project(model._h, which, layer, _ptr(x), x.shape[0], _ptr(out)))
+    return out
+
+
+def hidden(session: Session) -> np.ndarray:
+    _declare()
+    out = np.empty(session.model.config.d_model, dtype=np.float32)
+    _check(lib().nb_debug_hidden(session._h, _ptr(out)))
+    return out
+
+
+def kv(session: Session, layer: int):
+    _declare()
+    c = session.model.config
+    n = len(session)
+    keys = np.zeros((n, c.num_kv_heads, c.head_dim), dtype=np.int8)
+    values = np.zeros_like(keys)
+    ks = np.zeros((c.num_kv_heads, n), dtype=np.float32)
+    vs = np.zeros_like(ks)
+    _check(lib().nb_debug_kv(session._h, layer, _ptr(keys), _ptr(ks), _ptr(values), _ptr(vs)))
+    return keys, ks, values, vs
+
+
+def time_attention(batch, reps: int = 5):
+    """Mean device ms of one attention launch over the batch's current
+    positions, and the KV bytes that launch reads."""
+    _declare()
+    ms, nbytes = ctypes.c_float(), ctypes.c_double()
+    _check(lib().nb_debug_time_attention(batch._h, reps, ctypes.byref(ms), ctypes.byref(nbytes)))
+    return float(ms.value), float(nbytes.value)

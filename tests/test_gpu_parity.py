@@ -1,0 +1,283 @@
+"""Parity of the sm_100a path with the CPU restatement (INT mode = the
+reference's integer kernels), called through the C ABI.
+
+The bar: integer work bit-exact; every float the reference fixes the order of
+(hidden states, logits, KV scales) bit-exact as well, so greedy tokens are
+identical. The sequential-sum statistics use the reference's order too and
+are held to 1e-6 relative."""
+
+import ctypes
+
+import numpy as np
+import pytest
+
+from tests.conftest import prompt_ids, random_mask
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def device_model(native_built, archive_path):
+    import rustyneedle_b200 as nb
+
+    return nb.Model.open(archive_path, max_sessions=64)
+
+
+@pytest.fixture(scope="module")
+def oracle_model(oracle_lib, archive_path):
+    return oracle_lib.Model.open(archive_path, oracle_lib.MODE_INT, 0)
+
+
+def _bits_equal(a, b):
+    a, b = np.asarray(a, dtype=np.float32), np.asarray(b, dtype=np.float32)
+    return a.shape == b.shape and np.array_equal(a.view(np.uint32), b.view(np.uint32))
+
+
+def _mismatch(a, b):
+    a, b = np.asarray(a, dtype=np.float32).ravel(), np.asarray(b, dtype=np.float32).ravel()
+    bad = np.nonzero(a.view(np.uint32) != b.view(np.uint32))[0]
+    if bad.size == 0:
+        return "equal"
+    i = bad[0]
+    rel = np.max(np.abs(a - b) / np.maximum(np.abs(b), 1e-30))
+    return f"{bad.size} of {a.size} differ; first at {i}: {a[i]!r} vs {b[i]!r}; max rel {rel:.3g}"
+
+
+# ------------------------------------------------------------------ kernels
+def test_device_exponential_reproduces_host_libm(device_model):
+    from rustyneedle_b200 import debug
+
+    libm = ctypes.CDLL("libm.so.6")
+    libm.expf.restype = ctypes.c_float
+    libm.expf.argtypes = [ctypes.c_float]
+    rng = np.random.default_rng(0)
+    x = np.concatenate([rng.uniform(-110, 89, 200_000), rng.standard_normal(200_000) * 4,
+                        [0.0, -0.0, 88.7, 88.73, 89.0, -103.9, -104.0, -110.0, 1e-30, -1e-30]]).astype(np.float32)
+    # inputs the libm rounds differently from the correctly rounded result
+    table = np.fromfile(__import__("rustyneedle_b200.build", fromlist=["x"]).EXPF_TABLE, dtype=np.uint32)[3:]
+    listed = table[rng.integers(0, table.size, 20_000)].view(np.float32)
+    x = np.concatenate([x, listed])
+    want = np.array([libm.expf(float(v)) for v in x], dtype=np.float32)
+    got = debug.math(device_model, debug.OP_EXPF, x)
+    assert _bits_equal(got, want), _mismatch(got, want)
+
+
+def test_device_sigmoid_fast_exp_silu_match_the_oracle(device_model, oracle_lib):
+    from rustyneedle_b200 import debug
+
+    rng = np.random.default_rng(1)
+    x = np.concatenate([rng.standard_normal(50_000) * 6, rng.uniform(-100, 100, 20_000)]).astype(np.float32)
+    sig = np.array([oracle_lib.sigmoid(v) for v in x], dtype=np.float32)
+    assert _bits_equal(debug.math(device_model, debug.OP_SIGMOID, x), sig)
+    fe = np.array([oracle_lib.fast_exp(v) for v in x], dtype=np.float32)
+    assert _bits_equal(debug.math(device_model, debug.OP_FAST_EXP, x), fe)
+
+
+def _tensor_index(oracle_model, want):
+    """Archive index of a tensor by its canonical position (layout.rs:190-230)."""
+    layers, per_layer = oracle_model.num_layers, 24
+    name, layer = want
+    offsets = {"q": 2, "k": 3, "v": 4, "gate": 7, "out": 8}
+    if name == "embedding":
+        return 0
+    return 1 + layer * per_layer + offsets[name] - 1
+
+
+@pytest.mark.parametrize("layer", [0, 7, 19])
+def test_fused_projection_matches_the_panel_kernel(device_model, oracle_model, layer):
+    from rustyneedle_b200 import debug
+
+    rng = np.random.default_rng(layer)
+    x = (rng.standard_normal((5, 512)) * rng.uniform(0.01, 3.0, (5, 1))).astype(np.float32)
+    x[4, :] = 0.0  # an all-zero input: every group scale falls back to 1
+    got = debug.project(device_model, debug.MATRIX_QKVG, layer, x, 1536)
+    start = 0
+    for name, rows in (("q", 512), ("k", 256), ("v", 256), ("gate", 512)):
+        tensor = _tensor_index(oracle_model, (name, layer))
+        for t in range(x.shape[0]):
+            want, _ = oracle_model.matrix_product(tensor, x[t])
+            assert _bits_equal(got[t, start:start + rows], want), (name, t, _mismatch(got[t, start:start + rows], want))
+        start += rows
+
+
+def test_out_projection_and_logit_rows_match(device_model, oracle_model):
+    from rustyneedle_b200 import debug
+
+    rng = np.random.default_rng(11)
+    x = rng.standard_normal((3, 512)).astype(np.float32)
+    got = debug.project(device_model, debug.MATRIX_OUT, 3, x, 512)
+    tensor = _tensor_index(oracle_model, ("out", 3))
+    for t in range(3):
+        want, _ = oracle_model.matrix_product(tensor, x[t])
+        assert _bits_equal(got[t], want), _mismatch(got[t], want)
+    got = debug.project(device_model, debug.MATRIX_LOGITS, 0, x, 8192)
+    for t in range(3):
+        want, _ = oracle_model.matrix_product(0, x[t])
+        assert _bits_equal(got[t], want), _mismatch(got[t], want)
+
+
+# ------------------------------------------------------------------- model
+def test_feed_matches_the_oracle_hidden_logits_and_cache(device_model, oracle_model, oracle_lib):
+    import rustyneedle_b200 as nb
+    from rustyneedle_b200 import debug
+
+    model = device_model.with_depth(2)
+    omodel = oracle_model.with_depth(2)
+    ids = prompt_ids(0, 32)
+    s = nb.Session(model)
+    s.feed(ids)
+    o = oracle_lib.Session(omodel)
+    o.feed(ids)
+    assert len(s) == len(o) == 32
+    for layer in model.active_layers():
+        keys, ks, values, vs = debug.kv(s, layer)
+        okeys, oks, ovalues, ovs = o.cache(layer)
+        assert np.array_equal(keys, okeys) and np.array_equal(values, ovalues), layer
+        assert _bits_equal(ks, oks) and _bits_equal(vs, ovs), layer
+    assert _bits_equal(debug.hidden(s), o.hidden()), _mismatch(debug.hidden(s), o.hidden())
+    assert _bits_equal(s.logits(), o.logits()), _mismatch(s.logits(), o.logits())
+
+
+def test_config0_greedy_tokens_are_identical(device_model, oracle_model, oracle_lib):
+    """Config 0: depth 2, 32 prompt ids, 64 greedy tokens, batch 1, unconstrained."""
+    import rustyneedle_b200 as nb
+
+    model = device_model.with_depth(2)
+    omodel = oracle_model.with_depth(2)
+    ids = prompt_ids(0, 32)
+    s = nb.Session(model)
+    s.feed(ids)
+    o = oracle_lib.Session(omodel)
+    o.feed(ids)
+    got, want = [], []
+    for _ in range(64):
+        got.append(s.step())
+        token = oracle_lib.argmax(o.logits())
+        o.push(token)
+        want.append(token)
+    assert got == want
+    assert _bits_equal(s.logits(), o.logits())
+
+
+def test_depth20_masked_steps_and_statistics(device_model, oracle_model, oracle_lib):
+    """Config-1 style: full depth, a grammar bitset (~5% allowed) every step."""
+    import rustyneedle_b200 as nb
+
+    ids = prompt_ids(5, 48)
+    s = nb.Session(device_model)
+    s.feed(ids)
+    o = oracle_lib.Session(oracle_model)
+    o.feed(ids)
+    rng = np.random.default_rng(9)
+    for step in range(12):
+        bits, allowed = random_mask(rng, 8192, 0.05)
+        token, stats = s.step(bits, stats=True)
+        logits = o.logits()
+        want = oracle_lib.argmax_allowed(logits, allowed)
+        assert token == want, step
+        p, m = oracle_lib.allowed_statistics(logits, want, allowed)
+        assert abs(stats.probability - p) <= 1e-6 * abs(p) and abs(stats.mass - m) <= 1e-6 * abs(m)
+        o.push(want)
+    assert _bits_equal(s.logits(), o.logits())
+
+
+def test_empty_mask_falls_back_to_the_unrestricted_argmax(device_model, oracle_model, oracle_lib):
+    import rustyneedle_b200 as nb
+
+    model = device_model.with_depth(2)
+    s = nb.Session(model)
+    s.feed(prompt_ids(2, 8))
+    o = oracle_lib.Session(oracle_model.with_depth(2))
+    o.feed(prompt_ids(2, 8))
+    token = s.step(np.zeros(8192 // 32, dtype=np.uint32))
+    assert token == oracle_lib.argmax(o.logits())
+
+
+def test_batched_decode_matches_single_sessions(device_model, oracle_model, oracle_lib):
+    import rustyneedle_b200 as nb
+
+    model = device_model.with_depth(4)
+    omodel = oracle_model.with_depth(4)
+    lengths = [3, 17, 64, 65, 130]
+    sessions, oracles = [], []
+    for i, n in enumerate(lengths):
+        ids = prompt_ids(100 + i, n)
+        s = nb.Session(model)
+        s.feed(ids)
+        sessions.append(s)
+        o = oracle_lib.Session(omodel)
+        o.feed(ids)
+        oracles.append(o)
+    batch = nb.Batch(model, sessions)
+    for _ in range(6):
+        got = batch.step()
+        want = []
+        for o in oracles:
+            token = oracle_lib.argmax(o.logits())
+            o.push(token)
+            want.append(token)
+        assert list(got) == want
+    for s, o in zip(sessions, oracles):
+        assert _bits_equal(s.logits(), o.logits())
+
+
+def test_clone_shares_the_prefix_copy_on_write(device_model, oracle_model, oracle_lib):
+    import rustyneedle_b200 as nb
+
+    model = device_model.with_depth(2)
+    base = nb.Session(model)
+    base.feed(prompt_ids(7, 70))  # ends inside a partly filled page
+    a, b = base.clone(), base.clone()
+    a.push(11)
+    b.push(12)
+    o = oracle_lib.Session(oracle_model.with_depth(2))
+    o.feed(prompt_ids(7, 70))
+    oa, ob = o.clone(), o.clone()
+    oa.push(11)
+    ob.push(12)
+    assert _bits_equal(a.logits(), oa.logits()) and _bits_equal(b.logits(), ob.logits())
+    assert _bits_equal(base.logits(), o.logits())
+
+
+def test_chunked_prefill_is_exact(archive_path, oracle_model, oracle_lib):
+    import rustyneedle_b200 as nb
+
+    model = nb.Model.open(archive_path, max_sessions=4, max_batch_tokens=96).with_depth(2)
+    ids = prompt_ids(21, 300)
+    s = nb.Session(model)
+    s.feed(ids)
+    stepped = nb.Session(model)
+    for t in ids[:40]:
+        stepped.push(int(t))
+    stepped.feed(ids[40:])
+    o = oracle_lib.Session(oracle_model.with_depth(2))
+    o.feed(ids)
+    assert _bits_equal(s.logits(), o.logits()) and _bits_equal(stepped.logits(), o.logits())
+
+
+# ------------------------------------------------------------------ errors
+def test_context_overflow_and_depth_errors(archive_path, device_model):
+    import rustyneedle_b200 as nb
+
+    with pytest.raises(nb.DepthError):
+        device_model.with_depth(1)
+    with pytest.raises(nb.DepthError):
+        device_model.with_depth(21)
+    model = device_model.with_depth(2)
+    s = nb.Session(model)
+    with pytest.raises(nb.ContextOverflow):
+        s.feed(np.full(model.config.max_seq_len + 1, 10, dtype=np.uint32))
+    assert len(s) == 0
+    with pytest.raises(nb.NeedleError):
+        s.push(model.config.vocab)
+
+
+def test_kv_pool_exhaustion_is_a_status(archive_path):
+    import rustyneedle_b200 as nb
+
+    model = nb.Model.open(archive_path, max_sessions=2, kv_pages=4).with_depth(2)
+    s = nb.Session(model)
+    s.feed(prompt_ids(1, 64))  # one page per active layer
+    with pytest.raises(nb.NeedleError) as err:
+        s.feed(prompt_ids(2, 128))
+    assert err.value.status == -8

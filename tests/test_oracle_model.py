@@ -1,0 +1,115 @@
+"""Model-level properties of the CPU restatement (restating the tolerances of
+the reference's golden tests as self-consistency checks)."""
+
+import numpy as np
+import pytest
+
+from tests.conftest import prompt_ids
+
+
+def _cos(a, b):
+    a, b = a.astype(np.float64), b.astype(np.float64)
+    return float(a @ b / np.sqrt((a @ a) * (b @ b)))
+
+
+def test_int_prefill_is_bit_identical_to_pushing(oracle_lib, small_archive_path):
+    m = oracle_lib.Model.open(small_archive_path, oracle_lib.MODE_INT, 0)
+    ids = prompt_ids(3, 40)
+    fed, pushed = oracle_lib.Session(m), oracle_lib.Session(m)
+    fed.feed(ids)
+    for t in ids:
+        pushed.push(int(t))
+    assert np.array_equal(fed.logits(), pushed.logits())
+
+
+def test_float_prefill_agrees_with_stepping(oracle_lib, small_archive_path, kats):
+    """crates/model/tests/prefill.rs: batched vs stepped cosine > 0.9995, same argmax."""
+    m = oracle_lib.Model.open(small_archive_path, oracle_lib.MODE_FLOAT, 0)
+    ids = prompt_ids(4, 40)
+    fed, pushed = oracle_lib.Session(m), oracle_lib.Session(m)
+    fed.feed(ids)
+    for t in ids:
+        pushed.push(int(t))
+    a, b = fed.logits(), pushed.logits()
+    assert _cos(a, b) > kats["prefill_cosine"]
+    assert oracle_lib.argmax(a) == oracle_lib.argmax(b)
+
+
+def test_full_depth_is_the_base_model(oracle_lib, small_archive_path, kats):
+    m = oracle_lib.Model.open(small_archive_path, oracle_lib.MODE_INT, 0)
+    full = m.with_depth(4)
+    a, b = oracle_lib.Session(m), oracle_lib.Session(full)
+    a.feed(prompt_ids(5, 12))
+    b.feed(prompt_ids(5, 12))
+    assert _cos(a.logits(), b.logits()) > kats["full_depth_cosine"]
+    assert np.array_equal(a.logits(), b.logits())
+
+
+def test_depths_outside_the_ladder_are_refused(oracle_lib, small_archive_path):
+    m = oracle_lib.Model.open(small_archive_path, oracle_lib.MODE_INT, 0)
+    for depth in (1, 5):
+        with pytest.raises(oracle_lib.OracleError) as e:
+            m.with_depth(depth)
+        assert e.value.status == -3
+    assert m.with_depth(2).active_layers() == [0, 3]
+
+
+def test_int_and_float_modes_agree_like_the_reference_documents(oracle_lib, small_archive_path):
+    """docs/parity.md:24: the int8 kernel is within ~0.7% rRMS of the float one."""
+    ids = prompt_ids(6, 24)
+    out = []
+    for mode in (oracle_lib.MODE_INT, oracle_lib.MODE_FLOAT):
+        s = oracle_lib.Session(oracle_lib.Model.open(small_archive_path, mode, 0))
+        s.feed(ids)
+        out.append(s.logits())
+    assert _cos(out[0], out[1]) > 0.999
+    rel = np.sqrt(np.mean((out[0] - out[1]) ** 2) / np.mean(out[1] ** 2))
+    assert rel < 0.05
+
+
+def test_clone_is_independent(oracle_lib, small_archive_path):
+    m = oracle_lib.Model.open(small_archive_path, oracle_lib.MODE_INT, 0)
+    base = oracle_lib.Session(m)
+    base.feed(prompt_ids(8, 10))
+    before = base.logits()
+    c = base.clone()
+    c.push(42)
+    assert np.array_equal(base.logits(), before) and len(c) == 11 and len(base) == 10
+
+
+def test_threads_do_not_change_results(oracle_lib, small_archive_path):
+    ids = prompt_ids(9, 20)
+    out = []
+    for threads in (1, 4):
+        s = oracle_lib.Session(oracle_lib.Model.open(small_archive_path, oracle_lib.MODE_FLOAT, threads))
+        s.feed(ids)
+        out.append(s.logits())
+    assert np.array_equal(out[0], out[1])
+
+
+def test_argmax_and_statistics_follow_the_generator(oracle_lib):
+    v = np.array([1.0, 3.0, 3.0, 2.0], dtype=np.float32)
+    assert oracle_lib.argmax(v) == 1
+    allowed = np.array([1, 0, 1, 1], dtype=np.uint8)
+    assert oracle_lib.argmax_allowed(v, allowed) == 2
+    assert oracle_lib.argmax_allowed(v, np.zeros(4, dtype=np.uint8)) == -1
+    p, m = oracle_lib.allowed_statistics(v, 2, allowed)
+    e = np.exp(v.astype(np.float64) - 3.0)
+    assert abs(p - e[2] / (e[0] + e[2] + e[3])) < 1e-5 and abs(m - (e[0] + e[2] + e[3]) / e.sum()) < 1e-5
+
+
+def test_synthetic_archive_is_deterministic(tmp_path):
+    from rustyneedle_b200 import synthetic
+
+    g = synthetic.Geometry(num_layers=2, vocab=512, out_vocab=512, max_seq_len=128)
+    a = synthetic.write_archive(str(tmp_path / "a.cact"), 3, g)
+    b = synthetic.write_archive(str(tmp_path / "b.cact"), 3, g)
+    assert open(a, "rb").read() == open(b, "rb").read()
+
+
+def test_synthetic_archive_resolves_in_the_oracle(oracle_lib, archive_path):
+    m = oracle_lib.Model.open(archive_path, oracle_lib.MODE_INT, 1)
+    assert (m.vocab, m.d_model, m.num_heads, m.num_kv_heads, m.num_layers, m.head_dim) == (8192, 512, 8, 4, 20, 64)
+    info = m.tensor_info(0)
+    assert info == dict(kind=3, rows=8192, columns=512, group=128, bits=4)
+    assert m.tensor_info(2)["bits"] == 2
