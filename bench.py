@@ -56,7 +56,8 @@ def parse():
     p.add_argument("--seqs", type=int, default=SEQS_PER_GPU)
     p.add_argument("--no-batch1", action="store_true")
     p.add_argument("--no-cpu", action="store_true")
-    p.add_argument("--profile", action="store_true", help="small setup for ncu captures")
+    p.add_argument("--profile", action="store_true", help="64 sequences, no extras: the small case for ncu captures")
+    p.add_argument("--batch1-only", action="store_true", help="only the batch-1 configuration (ncu launch lists)")
     return p.parse_args()
 
 
@@ -208,11 +209,16 @@ def main():
     from rustyneedle_b200 import debug, synthetic
 
     archive = synthetic.cached_archive(seed=0)
-    seqs = 8 if args.profile else args.seqs
-    model = nb.Model.open(archive, device=local, max_sessions=seqs + 2)
+    seqs = 64 if args.profile else args.seqs
+    rank_prompts = prompts(rank, seqs)
+    # KV pool sized to the run: every sequence's prompt plus the decode steps, plus the batch-1 session
+    pages = sum(-(-(len(p) + 2 * args.steps + 2 * args.warmup + 8) // 64) for p in rank_prompts) * DEPTH + 40 * DEPTH
+    model = nb.Model.open(archive, device=local, max_sessions=seqs + 2, kv_pages=pages)
     if DEPTH != model.config.num_layers:
         model = model.with_depth(DEPTH)
-    rank_prompts = prompts(rank, seqs)
+    if args.batch1_only:
+        print(json.dumps({"batch1": batch1(nb, model)}), flush=True)
+        return
     t0 = time.perf_counter()
     sessions = []
     for ids in rank_prompts:
@@ -280,6 +286,7 @@ def main():
             "clocks": clocks.summary()}
 
     if not args.no_batch1 and rank == 0 and not args.profile:
+        batch.close()
         line["batch1"] = batch1(nb, model)
     if rank == 0 and world == 1 and not args.no_cpu and not args.profile:
         from oracle import oracle

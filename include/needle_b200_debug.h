@@ -25,6 +25,10 @@ nb_status nb_debug_math(nb_model* model, int op, const float* in, float* out, si
  * in: count × columns floats; out: count × rows floats. */
 nb_status nb_debug_project(nb_model* model, int which, uint32_t layer, const float* in, size_t count, float* out);
 
+/* HadamardWeights::apply (crates/model/src/hadamard.rs:260-304) of one layer
+ * on `count` inputs of d_model values. */
+nb_status nb_debug_hadamard(nb_model* model, uint32_t layer, const float* in, size_t count, float* out);
+
 /* The session's final hidden state (session.rs:140-143): d_model floats. */
 nb_status nb_debug_hidden(nb_session* session, float* out);
 

@@ -35,6 +35,18 @@ __device__ __forceinline__ uint32_t code_at(const uint8_t* row, uint32_t i, uint
   return (raw >> shift) & ((1u << bits) - 1);
 }
 
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(s), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+// Copies `floats` (a multiple of 4, 16-byte aligned) from global to shared
+// memory, 16 bytes per request; completes at cp_async_wait_all().
+__device__ __forceinline__ void stage_async(float* dst, const float* src, int floats) {
+  for (int i = threadIdx.x; i < floats / 4; i += blockDim.x) cp_async16(dst + 4 * i, src + 4 * i);
+}
+
 __device__ __forceinline__ uint8_t* page_base(const KvDev& kv, const PageGeometry& pg, int slot, int layer, int position) {
   int page = kv.page_table[((size_t)slot * kv.num_layers + layer) * kv.max_pages + position / PAGE_POSITIONS];
   return kv.pool + (size_t)page * pg.page_bytes;
@@ -65,24 +77,38 @@ __global__ void __launch_bounds__(128) k_embed(ModelDev md, Work w, int M) {
 
 // ------------------------------------------------------------------- routing
 // grid M, block 256 (8 warps). Warp 7 finishes the Sinkhorn mixing weights
-// while warps 0-6 build the block input, norm it and quantise it.
+// while warps 0-6 build the block input, norm it and quantise it. Every
+// global operand the kernel needs is staged by one round of cp.async.
+constexpr int PHI_ROWS = LANES + LANES + LANES * LANES;
+
+__device__ __forceinline__ void phi_row(const ModelDev& md, int r, int layer, const QMat*& P, int& row) {
+  P = r < 4 ? &md.phi_pre : (r < 8 ? &md.phi_post : &md.phi_res);
+  row = r < 4 ? layer * LANES + r : (r < 8 ? layer * LANES + (r - 4) : layer * LANES * LANES + (r - 8));
+}
+
 __global__ void __launch_bounds__(256) k_route(ModelDev md, LayerDev L, Work w, int M, int layer, int slot) {
   extern __shared__ float sm[];
   int t = blockIdx.x;
   if (t >= M || w.meta[t].slot < 0) return;
   const int d = md.d_model, n = LANES * d, ng = n / GROUP;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  float* s_stream = sm;                               // n
-  float* s_work = sm + n;                             // n (normalised stream, later x)
+  float* s_stream = sm;                                     // n
+  float* s_work = sm + n;                                   // n: normalised stream, later x
   int8_t* s_codes = reinterpret_cast<int8_t*>(sm + 2 * n);  // n bytes
+  float* s_norms = sm + 2 * n + n / 4;                      // PHI_ROWS * ng phi norms
+  float* s_gain = s_norms + PHI_ROWS * ng;                  // d norm_in gains
   __shared__ float s_ascale[MAX_D * LANES / GROUP];
   __shared__ float s_red[8];
-  __shared__ float s_phi[LANES + LANES + LANES * LANES];
+  __shared__ float s_phi[PHI_ROWS];
   __shared__ float s_gate[LANES];
   __shared__ float s_inv;
 
-  const float4* src = reinterpret_cast<const float4*>(w.stream + (size_t)t * n);
-  for (int i = tid; i < n / 4; i += blockDim.x) reinterpret_cast<float4*>(s_stream)[i] = src[i];
+  stage_async(s_stream, w.stream + (size_t)t * n, n);
+  stage_async(s_norms, md.phi_pre.scales + (size_t)layer * LANES * ng, LANES * ng);
+  stage_async(s_norms + LANES * ng, md.phi_post.scales + (size_t)layer * LANES * ng, LANES * ng);
+  stage_async(s_norms + 2 * LANES * ng, md.phi_res.scales + (size_t)layer * LANES * LANES * ng, LANES * LANES * ng);
+  stage_async(s_gain, L.norm_in, d);
+  cp_async_wait_all();
   __syncthreads();
   // unit_rms over all lanes (ops.rs:60-66), then fake_quantise_int8 (ops.rs:120-125)
   if (warp == 0) {
@@ -97,12 +123,11 @@ __global__ void __launch_bounds__(256) k_route(ModelDev md, LayerDev L, Work w, 
     peak = fmaxf(peak, fabsf(v));
   }
   float scale = int8_scale_of(block_max(peak, s_red));
-  for (int i = tid; i < n; i += blockDim.x) s_work[i] = fake_quant(s_work[i], scale);
-  __syncthreads();
   // rotate and quantise per 128-group (QuantisedMatrix::prepare + PlaneInput)
   for (int g = warp; g < ng; g += 8) {
     float v[4];
-    *reinterpret_cast<float4*>(v) = *reinterpret_cast<const float4*>(s_work + g * GROUP + 4 * lane);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) v[j] = fake_quant(s_work[g * GROUP + 4 * lane + j], scale);
     fwht128(v, md.inv_sqrt_group);
     uint32_t packed;
     float sc = quantise_group(v, packed);
@@ -111,49 +136,90 @@ __global__ void __launch_bounds__(256) k_route(ModelDev md, LayerDev L, Work w, 
   }
   __syncthreads();
   // phi products: 4 pre rows, 4 post rows, 16 residual rows of this layer
-  // (lanes.rs:156-163), 4-bit row combine (neon.rs:164-183)
-  for (int r = warp; r < 24; r += 8) {
-    const QMat& P = r < 4 ? md.phi_pre : (r < 8 ? md.phi_post : md.phi_res);
-    int row = r < 4 ? layer * LANES + r : (r < 8 ? layer * LANES + (r - 4) : layer * LANES * LANES + (r - 8));
-    const uint32_t* wrow = reinterpret_cast<const uint32_t*>(P.codes + (size_t)row * n);
-    const uint32_t* arow = reinterpret_cast<const uint32_t*>(s_codes);
-    float total = 0.0f;
-    for (int g = 0; g < ng; ++g) {
-      int acc = dp4a(wrow[g * 32 + lane], arow[g * 32 + lane], 0);
-      acc = warp_sum_int(acc);
-      total = fadd(total, fmul(fmul(fmul((float)acc, P.scales[(size_t)row * ng + g]), P.level_scale), s_ascale[g]));
+  // (lanes.rs:156-163). Thread (group g, row r) forms the exact int32 sum of
+  // one 128-column group (two pairs per thread, loads issued together); one
+  // thread per row then combines the groups in order with the 4-bit row chain
+  // (neon.rs:164-183).
+  int* s_acc = reinterpret_cast<int*>(s_work);  // [ng][PHI_ROWS]; s_work is free again
+  {
+    const int pairs = PHI_ROWS * ng;
+    uint4 wr[2][8];
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const int pair = tid + u * 256;
+      if (pair < pairs) {
+        const int g = pair / PHI_ROWS;
+        const QMat* P;
+        int row;
+        phi_row(md, pair % PHI_ROWS, layer, P, row);
+        const uint4* wv = reinterpret_cast<const uint4*>(P->codes + (size_t)row * n + g * GROUP);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) wr[u][k] = wv[k];
+      }
     }
-    if (lane == 0) s_phi[r] = total;
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const int pair = tid + u * 256;
+      if (pair < pairs) {
+        const int g = pair / PHI_ROWS;
+        const uint4* av = reinterpret_cast<const uint4*>(s_codes + g * GROUP);
+        int acc[4] = {0, 0, 0, 0};
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          uint4 a = av[k];
+          acc[0] = dp4a(wr[u][k].x, a.x, acc[0]);
+          acc[1] = dp4a(wr[u][k].y, a.y, acc[1]);
+          acc[2] = dp4a(wr[u][k].z, a.z, acc[2]);
+          acc[3] = dp4a(wr[u][k].w, a.w, acc[3]);
+        }
+        s_acc[pair] = (acc[0] + acc[1]) + (acc[2] + acc[3]);
+      }
+    }
+  }
+  __syncthreads();
+  if (tid < PHI_ROWS) {
+    const QMat* P;
+    int row;
+    phi_row(md, tid, layer, P, row);
+    const float lscale = P->level_scale;
+    float total = 0.0f;
+    for (int g = 0; g < ng; ++g)
+      total = fadd(total, fmul(fmul(fmul((float)s_acc[g * PHI_ROWS + tid], s_norms[tid * ng + g]), lscale), s_ascale[g]));
+    s_phi[tid] = total;
   }
   __syncthreads();
   float* route_out = w.route + (size_t)t * (LANES + LANES * LANES);
   if (warp == 7) {
     // post gates and the Sinkhorn-normalised residual mixing (lanes.rs:166-179, ops.rs:198-217)
+    __shared__ float s_res[16];
     if (lane < LANES) {
       float off = lane == (slot % LANES) ? 0.0f : -4.0f;
       float p = fadd(fadd(fmul(md.a_post[layer], s_phi[4 + lane]), md.b_post[layer * LANES + lane]), off);
       route_out[lane] = fmul(2.0f, sigmoid(p));
     }
+    if (lane < 16) s_res[lane] = fadd(fmul(md.a_res[layer], s_phi[8 + lane]), md.b_res[layer * 16 + lane]);
+    __syncwarp();
+    if (lane < 16) {
+      const int r = lane / 4;
+      float pk = -INFINITY;
+      for (int c = 0; c < 4; ++c) pk = fmaxf(pk, s_res[r * 4 + c]);
+      float e = expf_libm(fsub(s_res[lane], pk));
+      __syncwarp(0xffffu);
+      s_res[lane] = e;
+    }
+    __syncwarp();
     if (lane == 0) {
       float x[16];
-      for (int i = 0; i < 16; ++i) x[i] = fadd(fmul(md.a_res[layer], s_phi[8 + i]), md.b_res[layer * 16 + i]);
-      for (int r = 0; r < 4; ++r) {
-        float pk = -INFINITY;
-        for (int c = 0; c < 4; ++c) pk = fmaxf(pk, x[r * 4 + c]);
-        for (int c = 0; c < 4; ++c) x[r * 4 + c] = expf_libm(fsub(x[r * 4 + c], pk));
-      }
+      for (int i = 0; i < 16; ++i) x[i] = s_res[i];
       const float MIN_POSITIVE = 1.17549435e-38f;
       for (int it = 0; it < 20; ++it) {
-        for (int r = 0; r < 4; ++r) {
-          float tot = fadd(fadd(fadd(fadd(SUM_START, x[r * 4]), x[r * 4 + 1]), x[r * 4 + 2]), x[r * 4 + 3]);
-          float iv = frcp(fmaxf(tot, MIN_POSITIVE));
-          for (int c = 0; c < 4; ++c) x[r * 4 + c] = fmul(x[r * 4 + c], iv);
-        }
-        for (int c = 0; c < 4; ++c) {
-          float tot = fadd(fadd(fadd(fadd(SUM_START, x[c]), x[4 + c]), x[8 + c]), x[12 + c]);
-          float iv = frcp(fmaxf(tot, MIN_POSITIVE));
-          for (int r = 0; r < 4; ++r) x[r * 4 + c] = fmul(x[r * 4 + c], iv);
-        }
+        float iv[4];
+        for (int r = 0; r < 4; ++r) iv[r] = frcp(fmaxf(fadd(fadd(fadd(fadd(SUM_START, x[r * 4]), x[r * 4 + 1]), x[r * 4 + 2]), x[r * 4 + 3]), MIN_POSITIVE));
+        for (int r = 0; r < 4; ++r)
+          for (int c = 0; c < 4; ++c) x[r * 4 + c] = fmul(x[r * 4 + c], iv[r]);
+        for (int c = 0; c < 4; ++c) iv[c] = frcp(fmaxf(fadd(fadd(fadd(fadd(SUM_START, x[c]), x[4 + c]), x[8 + c]), x[12 + c]), MIN_POSITIVE));
+        for (int r = 0; r < 4; ++r)
+          for (int c = 0; c < 4; ++c) x[r * 4 + c] = fmul(x[r * 4 + c], iv[c]);
       }
       for (int i = 0; i < 16; ++i) route_out[LANES + i] = x[i];
     }
@@ -166,7 +232,7 @@ __global__ void __launch_bounds__(256) k_route(ModelDev md, LayerDev L, Work w, 
     s_gate[tid] = sigmoid(fadd(fadd(fmul(md.a_pre[layer], s_phi[tid]), md.b_pre[layer * LANES + tid]), off));
   }
   named_barrier(1, nthreads);
-  float* s_x = s_work;  // reuse: the block input x (lanes.rs:169-171)
+  float* s_x = s_work;  // the block input x (lanes.rs:169-171)
   float* xg = w.x + (size_t)t * d;
   for (int i = tid; i < d; i += nthreads) {
     float acc = 0.0f;
@@ -182,11 +248,11 @@ __global__ void __launch_bounds__(256) k_route(ModelDev md, LayerDev L, Work w, 
   }
   named_barrier(1, nthreads);
   // zero_centred_norm (ops.rs:44-50) then fake_quantise_int8 (attention.rs:99-100)
-  float* s_y = s_stream;  // reuse
+  float* s_y = s_stream;
   inv = s_inv;
   peak = 0.0f;
   for (int i = tid; i < d; i += nthreads) {
-    float v = fmul(fmul(fadd(1.0f, L.norm_in[i]), s_x[i]), inv);
+    float v = fmul(fmul(fadd(1.0f, s_gain[i]), s_x[i]), inv);
     s_y[i] = v;
     peak = fmaxf(peak, fabsf(v));
   }
@@ -197,70 +263,184 @@ __global__ void __launch_bounds__(256) k_route(ModelDev md, LayerDev L, Work w, 
   for (int i = 1; i < 7; ++i) peak = fmaxf(peak, s_red[i]);
   scale = int8_scale_of(peak);
   const int dg = d / GROUP;
-  int8_t* act = w.act + (size_t)t * d;
   for (int g = warp; g < dg; g += 7) {
     float v[4];
+#pragma unroll
     for (int j = 0; j < 4; ++j) v[j] = fake_quant(s_y[g * GROUP + 4 * lane + j], scale);
     fwht128(v, md.inv_sqrt_group);
     uint32_t packed;
     float sc = quantise_group(v, packed);
-    *reinterpret_cast<uint32_t*>(act + g * GROUP + 4 * lane) = packed;
+    *reinterpret_cast<uint32_t*>(w.act + core_offset(t, g * GROUP + 4 * lane, d / 16)) = packed;
     if (lane == 0) w.act_scale[(size_t)t * dg + g] = sc;
   }
 }
 
-// --------------------------------------------------------------- projection
-// out[m][row] for rows of W and tokens m: per (row, 128-group) an exact int32
-// dot product, then the groups combined in order — fused for 2-bit matrices
-// (panel.rs:184-187), a product chain for 4-bit ones (neon.rs:180).
-// Lane (r, g) of a warp owns group g of row 8·warp + r and keeps its 128
-// weight codes in registers while it walks the tokens. grid (ceil(rows/64),
-// token chunks), block 256.
-template <int GK>
-__global__ void __launch_bounds__(256) k_project(QMat W, const int8_t* __restrict__ act, const float* __restrict__ act_scale,
-                                                 float* __restrict__ out, int M, int out_stride, int tokens_per_cta,
-                                                 const TokenMeta* __restrict__ meta) {
-  constexpr int RB = 32 / GK;
-  constexpr int K = GK * GROUP;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int rowblock = blockIdx.x * 8 + warp;
-  if (rowblock * RB >= (int)W.rows) return;
-  const int r = lane / GK, g = lane % GK;
-  const int row = rowblock * RB + r;
-  const bool valid = row < (int)W.rows;
-  uint4 wv[8];
-  const uint4* base = reinterpret_cast<const uint4*>(W.codes) + (size_t)rowblock * 8 * 32;
-#pragma unroll
-  for (int k = 0; k < 8; ++k) wv[k] = valid ? base[k * 32 + lane] : make_uint4(0, 0, 0, 0);
-  const float wscale = valid ? W.scales[(size_t)row * GK + g] : 0.0f;
-  const int m0 = blockIdx.y * tokens_per_cta, m1 = min(M, m0 + tokens_per_cta);
-  const int leader = r * GK;
-  for (int m = m0; m < m1; ++m) {
-    if (meta && meta[m].slot < 0) continue;
-    const uint4* a = reinterpret_cast<const uint4*>(act + (size_t)m * K + g * GROUP);
-    int acc = 0;
-#pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      uint4 av = a[k];
-      acc = dp4a(wv[k].x, av.x, acc);
-      acc = dp4a(wv[k].y, av.y, acc);
-      acc = dp4a(wv[k].z, av.z, acc);
-      acc = dp4a(wv[k].w, av.w, acc);
-    }
-    const float as = act_scale[(size_t)m * GK + g];
-    float total = 0.0f;
-#pragma unroll
-    for (int gg = 0; gg < GK; ++gg) {
-      int ag = __shfl_sync(FULL, acc, leader + gg);
-      float ws = __shfl_sync(FULL, wscale, leader + gg);
-      float asg = __shfl_sync(FULL, as, leader + gg);
-      if (W.fused)
-        total = __fmaf_rn((float)ag, fmul(ws, asg), total);
-      else
-        total = fadd(total, fmul(fmul(fmul((float)ag, ws), W.level_scale), asg));
-    }
-    if (g == 0 && valid) out[(size_t)m * out_stride + row] = total;
+// ------------------------------------------------------- tensor-core product
+// out[m][row] = Σ_g combine(acc_g[row][m]) for a K = 512 codebook matrix on
+// the 5th-generation tensor cores: tcgen05.mma kind::i8 with int32
+// accumulators in TMEM, one accumulator per 128-column group (the reference
+// scales every group separately, neon.rs:158 / panel.rs:184-187), four
+// K = 32 steps per group. Operands live in global memory in the canonical
+// K-major core-matrix layout (core_offset, layout.h) so a 128-row weight tile
+// and an NT-token activation tile are each one contiguous block, fetched by
+// cp.async.bulk onto an mbarrier. In the epilogue warp w reads TMEM lane
+// quadrant w%4 (thread = weight row) for its share of the tokens, each group's
+// accumulators with tcgen05.ld, and combines them in group order: fma for
+// 2-bit panels, the product chain for 4-bit rows. Small token tiles keep the
+// epilogue short and spread a projection over many CTAs.
+// grid (ceil(rows/128), ceil(M/NT)), block 8·NT (16 tokens per warp slice).
+constexpr int GEMM_ROWS = 128;
+constexpr int GEMM_K = 512;
+constexpr int GEMM_KC = GEMM_K / 16;  // 16-byte chunks per row
+constexpr uint32_t GEMM_WAIT_LIMIT = 1u << 24;
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t phase) {
+  for (uint32_t i = 0; i < GEMM_WAIT_LIMIT; ++i) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.b32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(bar), "r"(phase)
+        : "memory");
+    if (done) return true;
   }
+  return false;
+}
+
+// UMMA shared-memory descriptor (K-major, no swizzle): start address, the byte
+// offset between the two 16-byte K halves of a K = 32 step (LBO) and between
+// 8-row core-matrix groups (SBO), descriptor version 1.
+__device__ __forceinline__ uint64_t umma_desc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+  return (uint64_t)((addr >> 4) & 0x3fff) | ((uint64_t)((lbo >> 4) & 0x3fff) << 16) | ((uint64_t)((sbo >> 4) & 0x3fff) << 32) |
+         (1ull << 46);
+}
+
+template <int NT>
+__global__ void __launch_bounds__(8 * NT) k_gemm(QMat W, const int8_t* __restrict__ act, const float* __restrict__ act_scale,
+                                              float* __restrict__ out, int M, int out_stride, const TokenMeta* __restrict__ meta,
+                                              int* __restrict__ error) {
+  constexpr int GK = GEMM_K / GROUP;
+  constexpr uint32_t COLS = GK * NT;  // TMEM columns: one NT-wide accumulator per group
+  constexpr uint32_t A_BYTES = GEMM_ROWS * GEMM_K, B_BYTES = NT * GEMM_K;
+  // instruction descriptor: D s32, A and B s8, both K-major, N = NT, M = 128
+  constexpr uint32_t IDESC = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(NT >> 3) << 17) | ((uint32_t)(GEMM_ROWS >> 4) << 24);
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + A_BYTES;
+  __shared__ __align__(8) uint64_t bars[2];
+  __shared__ uint32_t s_tmem;
+  __shared__ float s_as[NT * GK];
+  __shared__ int s_fail;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int tile = blockIdx.x, m0 = blockIdx.y * NT, mcount = min(NT, M - m0);
+  const uint32_t bar_load = smem_u32(&bars[0]), bar_mma = smem_u32(&bars[1]);
+
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s_tmem)), "r"(COLS) : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  if (tid == 0) {
+    s_fail = 0;
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar_load), "r"(1) : "memory");
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar_mma), "r"(1) : "memory");
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  for (int i = tid; i < NT * GK; i += blockDim.x) s_as[i] = i / GK < mcount ? act_scale[(size_t)m0 * GK + i] : 0.0f;
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = s_tmem;
+
+  if (tid == 0) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar_load), "r"(A_BYTES + B_BYTES) : "memory");
+    const uint8_t* ga = reinterpret_cast<const uint8_t*>(W.codes) + (size_t)tile * A_BYTES;
+    const uint8_t* gb = reinterpret_cast<const uint8_t*>(act) + (size_t)(m0 / 8) * (8 * GEMM_K);
+    constexpr uint32_t PIECE = 16384;
+    for (uint32_t off = 0; off < A_BYTES; off += PIECE)
+      asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(sA + off)),
+                   "l"(ga + off), "r"(min(PIECE, A_BYTES - off)), "r"(bar_load)
+                   : "memory");
+    for (uint32_t off = 0; off < B_BYTES; off += PIECE)
+      asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(sB + off)),
+                   "l"(gb + off), "r"(min(PIECE, B_BYTES - off)), "r"(bar_load)
+                   : "memory");
+  }
+  bool ok = mbar_wait(bar_load, 0);
+  if (ok && warp == 0) {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    if (lane == 0) {
+      const uint32_t a0 = smem_u32(sA), b0 = smem_u32(sB);
+#pragma unroll
+      for (int g = 0; g < GK; ++g)
+#pragma unroll
+        for (int s = 0; s < 4; ++s) {
+          const int step = g * 4 + s;  // K bytes 32·step .. 32·step+31 = chunks 2·step, 2·step+1
+          const uint64_t da = umma_desc(a0 + step * 256, 128, GEMM_KC * 128);
+          const uint64_t db = umma_desc(b0 + step * 256, 128, GEMM_KC * 128);
+          const uint32_t d_tmem = tmem + g * NT, accumulate = s > 0 ? 1u : 0u;
+          asm volatile(
+              "{\n\t.reg .pred p;\n\t"
+              "setp.ne.b32 p, %4, 0;\n\t"
+              "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}" ::"r"(d_tmem),
+              "l"(da), "l"(db), "r"(IDESC), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
+              : "memory");
+        }
+      asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar_mma) : "memory");
+    }
+    __syncwarp();
+  }
+  if (ok) ok = mbar_wait(bar_mma, 0);
+  if (!ok) s_fail = 1;
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (!s_fail) {
+    const int quad = warp & 3, slice = warp >> 2;
+    const int row = tile * GEMM_ROWS + quad * 32 + lane;
+    const bool valid = row < (int)W.rows;
+    float ws[GK];
+#pragma unroll
+    for (int g = 0; g < GK; ++g) ws[g] = valid ? W.scales[(size_t)row * GK + g] : 0.0f;
+    const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16);
+    {
+      const int c0 = slice * 16;
+      uint32_t a[GK][16];
+#pragma unroll
+      for (int g = 0; g < GK; ++g)
+        asm volatile(
+            "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+            : "=r"(a[g][0]), "=r"(a[g][1]), "=r"(a[g][2]), "=r"(a[g][3]), "=r"(a[g][4]), "=r"(a[g][5]), "=r"(a[g][6]), "=r"(a[g][7]),
+              "=r"(a[g][8]), "=r"(a[g][9]), "=r"(a[g][10]), "=r"(a[g][11]), "=r"(a[g][12]), "=r"(a[g][13]), "=r"(a[g][14]), "=r"(a[g][15])
+            : "r"(lane_base + g * NT + c0));
+      asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const int n = c0 + j;
+        float total = 0.0f;
+#pragma unroll
+        for (int g = 0; g < GK; ++g) {
+          const float acc = (float)(int)a[g][j];
+          const float as = s_as[n * GK + g];
+          total = W.fused ? __fmaf_rn(acc, fmul(ws[g], as), total) : fadd(total, fmul(fmul(fmul(acc, ws[g]), W.level_scale), as));
+        }
+        if (valid && n < mcount && !(meta && meta[m0 + n].slot < 0)) out[(size_t)(m0 + n) * out_stride + row] = total;
+      }
+    }
+  } else if (tid == 0) {
+    atomicExch(error, 1);
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(COLS) : "memory");
+}
+
+template <int NT>
+constexpr size_t gemm_smem() {
+  return (size_t)GEMM_ROWS * GEMM_K + (size_t)NT * GEMM_K;
 }
 
 // ------------------------------------------------------------------- heads
@@ -269,16 +449,21 @@ __global__ void __launch_bounds__(256) k_project(QMat W, const int8_t* __restric
 __global__ void k_heads(ModelDev md, LayerDev L, Work w, KvDev kv, int M, int layer) {
   int t = blockIdx.x;
   if (t >= M) return;
-  TokenMeta meta = w.meta[t];
+  const TokenMeta meta = w.meta[t];
   if (meta.slot < 0) return;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int H = md.heads, KV = md.kv_heads;
-  // proj rows: q [H*64] | k [KV*64] | v [KV*64] | gate [H*64]
-  const float* row = w.proj + (size_t)t * (2 * H + 2 * KV) * HEAD_DIM;
   const int kind = warp < H ? 0 : (warp < H + KV ? 1 : 2);
   const int head = kind == 0 ? warp : (kind == 1 ? warp - H : warp - H - KV);
-  const float* src = row + (kind == 0 ? 0 : (kind == 1 ? H * HEAD_DIM : (H + KV) * HEAD_DIM)) + head * HEAD_DIM;
+  // proj rows: q [H*64] | k [KV*64] | v [KV*64] | gate [H*64]
+  const float* src = w.proj + (size_t)t * (2 * H + 2 * KV) * HEAD_DIM + (kind == 0 ? 0 : (kind == 1 ? H * HEAD_DIM : (H + KV) * HEAD_DIM)) +
+                     head * HEAD_DIM;
+  // every operand is requested before the first use
   float e0 = src[lane], e1 = src[lane + 32];
+  const float* gain = kind == 0 ? L.q_norm : L.k_norm;
+  const float g0 = gain[lane], g1 = gain[lane + 32];
+  const float2 sc = md.rotary[(size_t)meta.position * (HEAD_DIM / 2) + lane];
+  uint8_t* page = kind == 0 ? nullptr : page_base(kv, md.page, meta.slot, layer, meta.position);
   if (kind != 2) {
     // zero_centred_norm_in_place over the head (ops.rs:52-58): lane l < 8 runs
     // the chain over elements l, l+8, ..., l+56
@@ -298,10 +483,8 @@ __global__ void k_heads(ModelDev md, LayerDev L, Work w, KvDev kv, int M, int la
 #pragma unroll
     for (int l = 0; l < 8; ++l) s = fadd(s, __shfl_sync(FULL, acc, l));
     float inv = inverse_rms(s, HEAD_DIM);
-    const float* gain = kind == 0 ? L.q_norm : L.k_norm;
-    e0 = fmul(fmul(fadd(1.0f, gain[lane]), e0), inv);
-    e1 = fmul(fmul(fadd(1.0f, gain[lane + 32]), e1), inv);
-    float2 sc = md.rotary[(size_t)meta.position * (HEAD_DIM / 2) + lane];
+    e0 = fmul(fmul(fadd(1.0f, g0), e0), inv);
+    e1 = fmul(fmul(fadd(1.0f, g1), e1), inv);
     float a = e0, b = e1;
     e0 = fsub(fmul(a, sc.y), fmul(b, sc.x));
     e1 = fadd(fmul(b, sc.y), fmul(a, sc.x));
@@ -319,7 +502,6 @@ __global__ void k_heads(ModelDev md, LayerDev L, Work w, KvDev kv, int M, int la
     return;
   }
   const PageGeometry& pg = md.page;
-  uint8_t* page = page_base(kv, pg, meta.slot, layer, meta.position);
   int p = meta.position % PAGE_POSITIONS;
   if (kind == 1) {
     int8_t* key = reinterpret_cast<int8_t*>(page) + ((size_t)head * PAGE_POSITIONS + p) * HEAD_DIM;
@@ -335,15 +517,20 @@ __global__ void k_heads(ModelDev md, LayerDev L, Work w, KvDev kv, int M, int la
 }
 
 // ---------------------------------------------------------------- attention
-// grid (M, kv_heads), block 160: warps 0-3 score, weight and accumulate the
-// values of the kv head's query heads; warp 4 forms the softmax totals in the
+// grid (M, kv_heads), block 288: warps 0-7 score, weight and accumulate the
+// values of the kv head's query heads; warp 8 forms the softmax totals in the
 // reference's order (four running lanes, (l0+l1)+(l2+l3), then the tail;
-// neon.rs:277-307) while warps 0-3 accumulate.
-constexpr int ATT_THREADS = 128;
+// neon.rs:277-307) while warps 0-7 accumulate. Every KV byte is read once.
+constexpr int ATT_WORKERS = 256;
+constexpr int ATT_THREADS_ALL = ATT_WORKERS + 32;
 constexpr int MAX_GROUP = 4;
+constexpr int ATT_SLICES = ATT_WORKERS / 16;
+constexpr int ATT_UNROLL = 4;
+
+__host__ __device__ constexpr int att_wstride(int t_cap) { return t_cap / 4 + 2; }
 
 template <int G>
-__global__ void __launch_bounds__(160) k_attend(ModelDev md, Work w, KvDev kv, int M, int layer, int global, int t_cap) {
+__global__ void __launch_bounds__(ATT_THREADS_ALL, 3) k_attend(ModelDev md, Work w, KvDev kv, int M, int layer, int global, int t_cap) {
   extern __shared__ float sm[];
   const int t = blockIdx.x, kvh = blockIdx.y;
   if (t >= M) return;
@@ -355,17 +542,20 @@ __global__ void __launch_bounds__(160) k_attend(ModelDev md, Work w, KvDev kv, i
   if (md.sliding_window > 0 && !global) first = total > (int)md.sliding_window ? total - (int)md.sliding_window : 0;
   const int count = total - first;
   const int b0 = first / 4, nblk = (total - 1) / 4 - b0 + 1;
-  float* s_coef = sm;                                   // [G][t_cap]
-  float* s_e = sm + G * t_cap;                          // [G][t_cap]
-  uint32_t* s_whi = reinterpret_cast<uint32_t*>(sm + 2 * G * t_cap);  // [G][t_cap/4 + 2]
-  uint32_t* s_wlo = s_whi + G * (t_cap / 4 + 2);
-  int* s_pv = reinterpret_cast<int*>(s_wlo + G * (t_cap / 4 + 2));     // [8][G][64]
-  __shared__ uint32_t s_q[MAX_GROUP][16];
+  const int ws = att_wstride(t_cap);
+  float* s_e = sm;                                              // [G][t_cap] coefficients, then exponentials
+  float* s_vs = sm + G * t_cap;                                 // [t_cap] value scales
+  uint32_t* s_whi = reinterpret_cast<uint32_t*>(s_vs + t_cap);  // [G][ws]
+  uint32_t* s_wlo = s_whi + G * ws;                             // [G][ws]
+  int* s_pv = reinterpret_cast<int*>(s_wlo + G * ws);           // [ATT_SLICES][G][64]
+  __shared__ __align__(16) uint32_t s_q[MAX_GROUP][16];
+  __shared__ const uint8_t* s_page[128];
   __shared__ float s_qs[MAX_GROUP], s_peak[MAX_GROUP], s_scale2[MAX_GROUP], s_total[MAX_GROUP];
-  __shared__ float s_red[MAX_GROUP][4];
+  __shared__ float s_red[MAX_GROUP][ATT_WORKERS / 32];
   const PageGeometry& pg = md.page;
   const int* table = kv.page_table + ((size_t)meta.slot * kv.num_layers + layer) * kv.max_pages;
-
+  const int npages = (total - 1) / PAGE_POSITIONS + 1;
+  for (int i = tid; i < npages; i += blockDim.x) s_page[i] = kv.pool + (size_t)table[i] * pg.page_bytes;
   if (tid < G * 16) {
     int h = tid / 16, k = tid % 16;
     s_q[h][k] = reinterpret_cast<const uint32_t*>(w.qcodes + ((size_t)t * md.heads + kvh * G + h) * HEAD_DIM)[k];
@@ -373,56 +563,53 @@ __global__ void __launch_bounds__(160) k_attend(ModelDev md, Work w, KvDev kv, i
   if (tid < G) s_qs[tid] = fmul(w.qscale[(size_t)t * md.heads + kvh * G + tid], md.inv_root_qk);
   __syncthreads();
 
-  if (tid < ATT_THREADS) {
-    // pass 1: integer scores, coefficients (s · key_scale) · query_scale and their peak
+  if (tid < ATT_WORKERS) {
+    // pass 1: integer scores q·k, coefficients (s · key_scale) · query_scale, their
+    // peak; the value scales are staged for pass 2. Two positions per thread
+    // per round, both positions' loads in flight together.
     float lmax[G];
 #pragma unroll
     for (int h = 0; h < G; ++h) lmax[h] = -INFINITY;
-    for (int i = tid; i < count; i += ATT_THREADS) {
-      int p = first + i;
-      const uint8_t* page = kv.pool + (size_t)table[p / PAGE_POSITIONS] * pg.page_bytes;
-      const uint4* key = reinterpret_cast<const uint4*>(page + ((size_t)kvh * PAGE_POSITIONS + p % PAGE_POSITIONS) * HEAD_DIM);
-      uint4 k0 = key[0], k1 = key[1], k2 = key[2], k3 = key[3];
-      float ks = reinterpret_cast<const float*>(page + pg.kscale_offset)[kvh * PAGE_POSITIONS + p % PAGE_POSITIONS];
+    for (int i0 = tid; i0 < count; i0 += 2 * ATT_WORKERS) {
+      uint4 key[2][4];
+      float ks[2], vs[2];
 #pragma unroll
-      for (int h = 0; h < G; ++h) {
-        const uint32_t* q = s_q[h];
-        int s = 0;
-        s = dp4a(k0.x, q[0], s); s = dp4a(k0.y, q[1], s); s = dp4a(k0.z, q[2], s); s = dp4a(k0.w, q[3], s);
-        s = dp4a(k1.x, q[4], s); s = dp4a(k1.y, q[5], s); s = dp4a(k1.z, q[6], s); s = dp4a(k1.w, q[7], s);
-        s = dp4a(k2.x, q[8], s); s = dp4a(k2.y, q[9], s); s = dp4a(k2.z, q[10], s); s = dp4a(k2.w, q[11], s);
-        s = dp4a(k3.x, q[12], s); s = dp4a(k3.y, q[13], s); s = dp4a(k3.z, q[14], s); s = dp4a(k3.w, q[15], s);
-        float c = fmul(fmul((float)s, ks), s_qs[h]);
-        s_coef[h * t_cap + i] = c;
-        lmax[h] = fmaxf(lmax[h], c);
+      for (int u = 0; u < 2; ++u) {
+        const int i = min(i0 + u * ATT_WORKERS, count - 1);
+        const int p = first + i, within = p % PAGE_POSITIONS;
+        const uint8_t* page = s_page[p / PAGE_POSITIONS];
+        const uint4* kp = reinterpret_cast<const uint4*>(page + ((size_t)kvh * PAGE_POSITIONS + within) * HEAD_DIM);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) key[u][k] = kp[k];
+        ks[u] = reinterpret_cast<const float*>(page + pg.kscale_offset)[kvh * PAGE_POSITIONS + within];
+        vs[u] = reinterpret_cast<const float*>(page + pg.vscale_offset)[kvh * PAGE_POSITIONS + within];
+      }
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int i = i0 + u * ATT_WORKERS;
+        if (i < count) {
+          s_vs[i] = vs[u];
+#pragma unroll
+          for (int h = 0; h < G; ++h) {
+            const uint4* q = reinterpret_cast<const uint4*>(s_q[h]);
+            int part[4] = {0, 0, 0, 0};
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const uint4 qv = q[k];
+              part[0] = dp4a(key[u][k].x, qv.x, part[0]);
+              part[1] = dp4a(key[u][k].y, qv.y, part[1]);
+              part[2] = dp4a(key[u][k].z, qv.z, part[2]);
+              part[3] = dp4a(key[u][k].w, qv.w, part[3]);
+            }
+            const int s = (part[0] + part[1]) + (part[2] + part[3]);
+            float c = fmul(fmul((float)s, ks[u]), s_qs[h]);
+            s_e[h * t_cap + i] = c;
+            lmax[h] = fmaxf(lmax[h], c);
+          }
+        }
       }
     }
-    for (int h = 0; h < G; ++h) {
-      float m = warp_max(lmax[h]);
-      if (lane == 0) s_red[h][warp] = m;
-    }
-  }
-  __syncthreads();
-  if (tid < G) s_peak[tid] = fmaxf(fmaxf(s_red[tid][0], s_red[tid][1]), fmaxf(s_red[tid][2], s_red[tid][3]));
-  __syncthreads();
-  if (tid < ATT_THREADS) {
-    // pass 2: e = fast_exp(c - peak), weight = e · value_scale, and the weights' peak
-    float lmax[G];
 #pragma unroll
-    for (int h = 0; h < G; ++h) lmax[h] = 0.0f;
-    for (int i = tid; i < count; i += ATT_THREADS) {
-      int p = first + i;
-      const uint8_t* page = kv.pool + (size_t)table[p / PAGE_POSITIONS] * pg.page_bytes;
-      float vs = reinterpret_cast<const float*>(page + pg.vscale_offset)[kvh * PAGE_POSITIONS + p % PAGE_POSITIONS];
-#pragma unroll
-      for (int h = 0; h < G; ++h) {
-        float e = fast_exp(fsub(s_coef[h * t_cap + i], s_peak[h]));
-        s_e[h * t_cap + i] = e;
-        float c2 = fmul(e, vs);
-        s_coef[h * t_cap + i] = c2;
-        lmax[h] = fmaxf(lmax[h], fabsf(c2));
-      }
-    }
     for (int h = 0; h < G; ++h) {
       float m = warp_max(lmax[h]);
       if (lane == 0) s_red[h][warp] = m;
@@ -430,15 +617,43 @@ __global__ void __launch_bounds__(160) k_attend(ModelDev md, Work w, KvDev kv, i
   }
   __syncthreads();
   if (tid < G) {
-    float pk = fmaxf(fmaxf(s_red[tid][0], s_red[tid][1]), fmaxf(s_red[tid][2], s_red[tid][3]));
+    float m = s_red[tid][0];
+    for (int k = 1; k < ATT_WORKERS / 32; ++k) m = fmaxf(m, s_red[tid][k]);
+    s_peak[tid] = m;
+  }
+  __syncthreads();
+  if (tid < ATT_WORKERS) {
+    // pass 2: e = fast_exp(c - peak) and the peak of the weights e · value_scale
+    float lmax[G];
+#pragma unroll
+    for (int h = 0; h < G; ++h) lmax[h] = 0.0f;
+    for (int i = tid; i < count; i += ATT_WORKERS) {
+      const float vs = s_vs[i];
+#pragma unroll
+      for (int h = 0; h < G; ++h) {
+        float e = fast_exp(fsub(s_e[h * t_cap + i], s_peak[h]));
+        s_e[h * t_cap + i] = e;
+        lmax[h] = fmaxf(lmax[h], fabsf(fmul(e, vs)));
+      }
+    }
+#pragma unroll
+    for (int h = 0; h < G; ++h) {
+      float m = warp_max(lmax[h]);
+      if (lane == 0) s_red[h][warp] = m;
+    }
+  }
+  __syncthreads();
+  if (tid < G) {
+    float pk = s_red[tid][0];
+    for (int k = 1; k < ATT_WORKERS / 32; ++k) pk = fmaxf(pk, s_red[tid][k]);
     s_peak[tid] = pk;
     s_scale2[tid] = fdiv(pk, 2047.0f);
   }
   __syncthreads();
-  if (warp == 4) {
+  if (warp == ATT_WORKERS / 32) {
     // softmax totals in the order of neon.rs:294-305
-    int h = lane >> 2, j = lane & 3;
-    int vc = count - count % 4;
+    const int h = lane >> 2, j = lane & 3;
+    const int vc = count - count % 4;
     float acc = 0.0f;
     if (h < G)
       for (int i = j; i < vc; i += 4) acc = fadd(acc, s_e[h * t_cap + i]);
@@ -450,49 +665,66 @@ __global__ void __launch_bounds__(160) k_attend(ModelDev md, Work w, KvDev kv, i
       s_total[h] = tot;
     }
   } else {
-    // pass 3: 12-bit weights round(c / (peak / 2047)) (half away from zero),
-    // split into 6-bit halves per absolute 4-position block (neon.rs:348-365)
-    for (int b = tid; b < nblk; b += ATT_THREADS) {
-      int pbase = (b0 + b) * 4;
+    // pass 3: 12-bit weights round(c / (peak / 2047)) (half away from zero) of
+    // c = e · value_scale, split into 6-bit halves per absolute 4-position
+    // block (attention.rs:294-310, neon.rs:348-365)
+    for (int b = tid; b < nblk; b += ATT_WORKERS) {
+      const int pbase = (b0 + b) * 4;
+#pragma unroll
       for (int h = 0; h < G; ++h) {
         uint32_t hi = 0, lo = 0;
-        float sc = s_scale2[h];
-        bool live = s_peak[h] > 0.0f;
+        const float sc = s_scale2[h];
+        const bool live = s_peak[h] > 0.0f;
+#pragma unroll
         for (int j = 0; j < 4; ++j) {
-          int p = pbase + j;
+          const int p = pbase + j;
           int wgt = 0;
-          if (live && p >= first && p < total) wgt = (int)roundf(fdiv(s_coef[h * t_cap + (p - first)], sc));
+          if (live && p >= first && p < total) {
+            const int i = p - first;
+            wgt = (int)roundf(fdiv(fmul(s_e[h * t_cap + i], s_vs[i]), sc));
+          }
           hi |= (uint32_t)((wgt >> 6) & 0xff) << (8 * j);
           lo |= (uint32_t)((wgt & 63) & 0xff) << (8 * j);
         }
-        s_whi[h * (t_cap / 4 + 2) + b] = hi;
-        s_wlo[h * (t_cap / 4 + 2) + b] = lo;
+        s_whi[h * ws + b] = hi;
+        s_wlo[h * ws + b] = lo;
       }
     }
-    named_barrier(1, ATT_THREADS);
+    named_barrier(1, ATT_WORKERS);
     // pass 4: exact integer sums over the value panels; thread (dq, slice) owns
-    // four dimensions and every eighth block
+    // four dimensions and every ATT_SLICES-th block, ATT_UNROLL blocks per round
     const int dq = tid & 15, slice = tid >> 4;
     int hi_acc[G][4], lo_acc[G][4];
 #pragma unroll
     for (int h = 0; h < G; ++h)
-      for (int k = 0; k < 4; ++k) hi_acc[h][k] = lo_acc[h][k] = 0;
-    for (int b = slice; b < nblk; b += 8) {
-      int p = (b0 + b) * 4;
-      const uint8_t* page = kv.pool + (size_t)table[p / PAGE_POSITIONS] * pg.page_bytes;
-      uint4 v = *reinterpret_cast<const uint4*>(page + pg.value_offset + (size_t)kvh * PAGE_POSITIONS * HEAD_DIM +
-                                                ((p % PAGE_POSITIONS) / 4) * (HEAD_DIM * 4) + dq * 16);
 #pragma unroll
-      for (int h = 0; h < G; ++h) {
-        uint32_t whi = s_whi[h * (t_cap / 4 + 2) + b], wlo = s_wlo[h * (t_cap / 4 + 2) + b];
-        hi_acc[h][0] = dp4a(v.x, whi, hi_acc[h][0]);
-        hi_acc[h][1] = dp4a(v.y, whi, hi_acc[h][1]);
-        hi_acc[h][2] = dp4a(v.z, whi, hi_acc[h][2]);
-        hi_acc[h][3] = dp4a(v.w, whi, hi_acc[h][3]);
-        lo_acc[h][0] = dp4a(v.x, wlo, lo_acc[h][0]);
-        lo_acc[h][1] = dp4a(v.y, wlo, lo_acc[h][1]);
-        lo_acc[h][2] = dp4a(v.z, wlo, lo_acc[h][2]);
-        lo_acc[h][3] = dp4a(v.w, wlo, lo_acc[h][3]);
+      for (int k = 0; k < 4; ++k) hi_acc[h][k] = lo_acc[h][k] = 0;
+    const size_t vbase = pg.value_offset + (size_t)kvh * PAGE_POSITIONS * HEAD_DIM + dq * 16;
+    for (int bb = slice; bb < nblk; bb += ATT_UNROLL * ATT_SLICES) {
+      uint4 v[ATT_UNROLL];
+#pragma unroll
+      for (int u = 0; u < ATT_UNROLL; ++u) {
+        const int b = min(bb + u * ATT_SLICES, nblk - 1);
+        const int p = (b0 + b) * 4;
+        v[u] = *reinterpret_cast<const uint4*>(s_page[p / PAGE_POSITIONS] + vbase + ((p % PAGE_POSITIONS) / 4) * (HEAD_DIM * 4));
+      }
+#pragma unroll
+      for (int u = 0; u < ATT_UNROLL; ++u) {
+        const int b = bb + u * ATT_SLICES;
+        if (b < nblk) {
+#pragma unroll
+          for (int h = 0; h < G; ++h) {
+            const uint32_t whi = s_whi[h * ws + b], wlo = s_wlo[h * ws + b];
+            hi_acc[h][0] = dp4a(v[u].x, whi, hi_acc[h][0]);
+            hi_acc[h][1] = dp4a(v[u].y, whi, hi_acc[h][1]);
+            hi_acc[h][2] = dp4a(v[u].z, whi, hi_acc[h][2]);
+            hi_acc[h][3] = dp4a(v[u].w, whi, hi_acc[h][3]);
+            lo_acc[h][0] = dp4a(v[u].x, wlo, lo_acc[h][0]);
+            lo_acc[h][1] = dp4a(v[u].y, wlo, lo_acc[h][1]);
+            lo_acc[h][2] = dp4a(v[u].z, wlo, lo_acc[h][2]);
+            lo_acc[h][3] = dp4a(v[u].w, wlo, lo_acc[h][3]);
+          }
+        }
       }
     }
 #pragma unroll
@@ -501,192 +733,319 @@ __global__ void __launch_bounds__(160) k_attend(ModelDev md, Work w, KvDev kv, i
       for (int k = 0; k < 4; ++k) s_pv[(slice * G + h) * HEAD_DIM + dq * 4 + k] = (hi_acc[h][k] << 6) + lo_acc[h][k];
   }
   __syncthreads();
-  if (tid < ATT_THREADS) {
-    for (int o = tid; o < G * HEAD_DIM; o += ATT_THREADS) {
-      int h = o / HEAD_DIM, dim = o % HEAD_DIM;
-      int sum = 0;
-      for (int s = 0; s < 8; ++s) sum += s_pv[(s * G + h) * HEAD_DIM + dim];
-      float value = s_peak[h] > 0.0f ? fmul((float)sum, s_scale2[h]) : 0.0f;
-      float inverse = fdiv(1.0f, s_total[h]);
-      w.attn[(size_t)t * md.heads * HEAD_DIM + (kvh * G + h) * HEAD_DIM + dim] = fmul(value, inverse);
-    }
+  if (tid < G * HEAD_DIM) {
+    const int h = tid / HEAD_DIM, dim = tid % HEAD_DIM;
+    int sum = 0;
+#pragma unroll
+    for (int s = 0; s < ATT_SLICES; ++s) sum += s_pv[(s * G + h) * HEAD_DIM + dim];
+    const float value = s_peak[h] > 0.0f ? fmul((float)sum, s_scale2[h]) : 0.0f;
+    const float inverse = fdiv(1.0f, s_total[h]);
+    w.attn[(size_t)t * md.heads * HEAD_DIM + (kvh * G + h) * HEAD_DIM + dim] = fmul(value, inverse);
   }
 }
 
 // ------------------------------------------------------ int8 activation prep
-// in[m] (K values, optionally times sigmoid(gate[m])) → fake_quantise_int8 →
-// per-group rotation and int8 codes. Used for out_proj (attention.rs:145-150)
-// and the logits (session.rs:170-175). grid M, block 128.
+// in[m] (K values, optionally times sigmoid(gate[m])) → fake_quantise_int8
+// (when `fake`) → per-group rotation and int8 codes. Used for out_proj
+// (attention.rs:145-150) and the logits (session.rs:170-175). grid M, block
+// 128; four consecutive values per thread and pass.
 __global__ void __launch_bounds__(128) k_prep(const float* __restrict__ in, int in_stride, const int32_t* __restrict__ rows,
                                               const float* __restrict__ gate, int gate_stride, int K, int8_t* __restrict__ act,
                                               float* __restrict__ act_scale, int M, const TokenMeta* __restrict__ meta,
                                               float inv_sqrt_group, int fake) {
-  __shared__ float s_v[MAX_D];
+  __shared__ __align__(16) float s_v[MAX_D];
   __shared__ float s_red[4];
-  int t = blockIdx.x;
+  const int t = blockIdx.x;
   if (t >= M || (meta && meta[t].slot < 0)) return;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const float* src = in + (size_t)(rows ? rows[t] : t) * in_stride;
   float peak = 0.0f;
-  for (int i = tid; i < K; i += blockDim.x) {
-    float v = src[i];
-    if (gate) v = fmul(v, sigmoid(gate[(size_t)t * gate_stride + i]));
-    s_v[i] = v;
-    peak = fmaxf(peak, fabsf(v));
+  for (int i4 = tid; i4 < K / 4; i4 += blockDim.x) {
+    float4 v = reinterpret_cast<const float4*>(src)[i4];
+    if (gate) {
+      const float4 gv = reinterpret_cast<const float4*>(gate + (size_t)t * gate_stride)[i4];
+      v = make_float4(fmul(v.x, sigmoid(gv.x)), fmul(v.y, sigmoid(gv.y)), fmul(v.z, sigmoid(gv.z)), fmul(v.w, sigmoid(gv.w)));
+    }
+    reinterpret_cast<float4*>(s_v)[i4] = v;
+    peak = fmaxf(peak, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
   }
-  float scale = int8_scale_of(block_max(peak, s_red));
+  const float scale = int8_scale_of(block_max(peak, s_red));
   const int groups = K / GROUP;
   for (int g = warp; g < groups; g += blockDim.x >> 5) {
     float v[4];
-    for (int j = 0; j < 4; ++j) v[j] = fake ? fake_quant(s_v[g * GROUP + 4 * lane + j], scale) : s_v[g * GROUP + 4 * lane + j];
+    *reinterpret_cast<float4*>(v) = reinterpret_cast<const float4*>(s_v + g * GROUP)[lane];
+    if (fake)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) v[j] = fake_quant(v[j], scale);
     fwht128(v, inv_sqrt_group);
     uint32_t packed;
-    float sc = quantise_group(v, packed);
-    *reinterpret_cast<uint32_t*>(act + (size_t)t * K + g * GROUP + 4 * lane) = packed;
+    const float sc = quantise_group(v, packed);
+    *reinterpret_cast<uint32_t*>(act + core_offset(t, g * GROUP + 4 * lane, K / 16)) = packed;
     if (lane == 0) act_scale[(size_t)t * groups + g] = sc;
   }
 }
 
 // ------------------------------------------------------------ block finish
-// grid M, block 512. Post norm, gated residual (session.rs:121-125), the
+// grid M, block 128. Post norm, gated residual (session.rs:121-125), the
 // Hadamard MLP (hadamard.rs:260-304) and the lane combine (lanes.rs:183-204).
-template <int LEFT, bool FUSED32>
-__device__ __forceinline__ void kronecker(const float* __restrict__ X, const float* __restrict__ Lf, const float* __restrict__ R,
-                                          float* __restrict__ mixed, float* __restrict__ out) {
-  // ops.rs:143-164: mixed = X·R (sequential over j), out = Lᵀ·mixed (sequential over i).
-  // FUSED32 restates the aarch64 32×32 path, which fuses each step (ops.rs:219-299).
-  constexpr int PER = LEFT * HADA_RIGHT / 512;
-  const int tid = threadIdx.x, c = tid & 31, r0 = tid >> 5;
-  float acc[PER];
+//
+// Each Kronecker factor application K(x) = Lᵀ·(X·R) (ops.rs:143-164) runs as
+// two products C[r][c] = Σ_s A[s][r]·B[s][c] with s ascending, the reference's
+// summation order for every output. A thread owns a 4×4 output tile, so each
+// step reads one float4 of A and one of B from shared memory for 16
+// multiply-adds. The stage-A operand X enters transposed (XT[j][i]). Operands
+// arrive by cp.async, the next factor pair while the current stage's
+// elementwise pass runs.
+// Packed two-lane f32 arithmetic (PTX add/mul/fma .rn.f32x2): each component
+// rounded to nearest exactly as the scalar .rn instruction.
+__device__ __forceinline__ float2 add2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "mul.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return d;
+}
+
+template <int S, int R, bool FUSED32>
+__device__ __forceinline__ void tn_stage(const float* __restrict__ A, const float* __restrict__ B, float* __restrict__ C) {
+  // Two adjacent output columns share one packed f32x2 instruction.
+  const int tid = threadIdx.x;
+  if (tid < R * 2) {
+    const int r0 = (tid >> 3) * 4, c0 = (tid & 7) * 4;
+    float2 acc[4][2];
 #pragma unroll
-  for (int q = 0; q < PER; ++q) acc[q] = 0.0f;
-  for (int j = 0; j < HADA_RIGHT; ++j) {
-    float rv = R[j * HADA_RIGHT + c];
+    for (int i = 0; i < 4; ++i) acc[i][0] = acc[i][1] = make_float2(0.0f, 0.0f);
+#pragma unroll 8
+    for (int s = 0; s < S; ++s) {
+      const float4 a = *reinterpret_cast<const float4*>(A + s * R + r0);
+      const float4 b = *reinterpret_cast<const float4*>(B + s * HADA_RIGHT + c0);
+      const float av[4] = {a.x, a.y, a.z, a.w};
+      const float2 b01 = make_float2(b.x, b.y), b23 = make_float2(b.z, b.w);
 #pragma unroll
-    for (int q = 0; q < PER; ++q) {
-      float xv = X[(r0 + 16 * q) * HADA_RIGHT + j];
-      acc[q] = FUSED32 ? __fmaf_rn(rv, xv, acc[q]) : fadd(acc[q], fmul(xv, rv));
+      for (int i = 0; i < 4; ++i) {
+        const float2 ai = make_float2(av[i], av[i]);
+        if (FUSED32) {
+          acc[i][0] = fma2(ai, b01, acc[i][0]);
+          acc[i][1] = fma2(ai, b23, acc[i][1]);
+        } else {
+          // packed products, scalar sums: a packed multiply feeding a packed
+          // add is contracted to a packed fma by the backend even under
+          // -fmad=false, which the reference never does here
+          const float2 p01 = mul2(ai, b01), p23 = mul2(ai, b23);
+          acc[i][0] = make_float2(fadd(acc[i][0].x, p01.x), fadd(acc[i][0].y, p01.y));
+          acc[i][1] = make_float2(fadd(acc[i][1].x, p23.x), fadd(acc[i][1].y, p23.y));
+        }
+      }
     }
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      *reinterpret_cast<float4*>(C + (r0 + i) * HADA_RIGHT + c0) = make_float4(acc[i][0].x, acc[i][0].y, acc[i][1].x, acc[i][1].y);
   }
-#pragma unroll
-  for (int q = 0; q < PER; ++q) mixed[(r0 + 16 * q) * HADA_RIGHT + c] = acc[q];
-  __syncthreads();
-#pragma unroll
-  for (int q = 0; q < PER; ++q) acc[q] = 0.0f;
-  for (int i = 0; i < LEFT; ++i) {
-    float mv = mixed[i * HADA_RIGHT + c];
-#pragma unroll
-    for (int q = 0; q < PER; ++q) {
-      float lv = Lf[i * LEFT + r0 + 16 * q];
-      acc[q] = FUSED32 ? __fmaf_rn(mv, lv, acc[q]) : fadd(acc[q], fmul(lv, mv));
-    }
-  }
-#pragma unroll
-  for (int q = 0; q < PER; ++q) out[(r0 + 16 * q) * HADA_RIGHT + c] = acc[q];
   __syncthreads();
 }
 
+template <int LEFT, bool FUSED32>
+__device__ __forceinline__ void kronecker(float* xt, float* tmp, const float* left, const float* right, float* out) {
+  tn_stage<HADA_RIGHT, LEFT, FUSED32>(xt, right, tmp);
+  tn_stage<LEFT, LEFT, FUSED32>(left, tmp, out);
+}
+
+constexpr int BLOCK_THREADS = 128;
+
+// The stage-A operand position of element e of a LEFT×32 matrix.
 template <int LEFT>
-__global__ void __launch_bounds__(512) k_block(ModelDev md, LayerDev L, Work w, int M) {
+__device__ __forceinline__ int transposed(int e) { return (e % HADA_RIGHT) * LEFT + e / HADA_RIGHT; }
+
+// The Hadamard MLP of hadamard.rs:260-304 on the pre-normed input s_pre (d
+// values): rank-8 condition softmax, modulation, three Kronecker factor
+// applications with the two permutations and the SiLU gate. The result (before
+// the final d4 scale) is left in buf0. cond_v, left[0] and right[0] must
+// already be staged in s_condv, s_left and s_right.
+template <int LEFT>
+__device__ __forceinline__ void hadamard_core(const ModelDev& md, const HadamardDev& Hd, const int d, const float* s_pre, float* buf0,
+                                              float* buf1, float* s_mod, float* s_left, float* s_right, const float* s_condv) {
+  constexpr int N = LEFT * HADA_RIGHT;
+  constexpr int PER = N / (4 * BLOCK_THREADS);
+  constexpr bool FUSED32 = LEFT == 32;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  __shared__ float s_w[COND_RANK], s_chain[4][COND_RANK];
+  // condition weights: four chains of rank-8 partial sums (hadamard.rs:263-276)
+  if (warp == 0) {
+    int j = lane / COND_RANK, rr = lane % COND_RANK;
+    float acc = 0.0f;
+#pragma unroll 8
+    for (int g = 0; g < d / 4; ++g) acc = fadd(acc, fmul(s_pre[4 * g + j], s_condv[(4 * g + j) * COND_RANK + rr]));
+    s_chain[j][rr] = acc;
+    __syncwarp();
+    if (lane == 0) {
+      float wv[COND_RANK], peak = -INFINITY;
+      for (int r = 0; r < COND_RANK; ++r) {
+        wv[r] = fadd(fadd(fadd(fadd(0.0f, s_chain[0][r]), s_chain[1][r]), s_chain[2][r]), s_chain[3][r]);
+        peak = fmaxf(peak, wv[r]);
+      }
+      float total = 0.0f;
+      for (int r = 0; r < COND_RANK; ++r) {
+        wv[r] = fast_exp(fsub(wv[r], peak));
+        total = fadd(total, wv[r]);
+      }
+      float inverse = fdiv(1.0f, total);
+      for (int r = 0; r < COND_RANK; ++r) s_w[r] = fmul(wv[r], inverse);
+    }
+  }
+  __syncthreads();
+  // modulation = 1 + Σ_r w_r·cond_u[r] (sequential over r) and X = pad(x) ⊙ d1
+#pragma unroll 2
+  for (int q = 0; q < PER; ++q) {
+    const int i4 = tid + q * BLOCK_THREADS;
+    float4 u[COND_RANK];
+#pragma unroll
+    for (int r = 0; r < COND_RANK; ++r) u[r] = reinterpret_cast<const float4*>(Hd.cond_u + (size_t)r * N)[i4];
+    const float4 d1 = reinterpret_cast<const float4*>(Hd.d1)[i4];
+    float m[4] = {1.0f, 1.0f, 1.0f, 1.0f};
+#pragma unroll
+    for (int r = 0; r < COND_RANK; ++r) {
+      m[0] = fadd(m[0], fmul(s_w[r], u[r].x));
+      m[1] = fadd(m[1], fmul(s_w[r], u[r].y));
+      m[2] = fadd(m[2], fmul(s_w[r], u[r].z));
+      m[3] = fadd(m[3], fmul(s_w[r], u[r].w));
+    }
+    *reinterpret_cast<float4*>(s_mod + 4 * i4) = make_float4(m[0], m[1], m[2], m[3]);
+    const float dv[4] = {d1.x, d1.y, d1.z, d1.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      int i = 4 * i4 + e;
+      buf0[transposed<LEFT>(i)] = fmul(i < d ? s_pre[i] : 0.0f, dv[e]);
+    }
+  }
+  __syncthreads();
+  kronecker<LEFT, FUSED32>(buf0, buf1, s_left, s_right, buf0);  // first = K1(d1 ⊙ x)
+  stage_async(s_left, Hd.left[1], LEFT * LEFT);
+  stage_async(s_right, Hd.right[1], HADA_RIGHT * HADA_RIGHT);
+#pragma unroll
+  for (int q = 0; q < PER; ++q) {
+    const int i4 = tid + q * BLOCK_THREADS;
+    const int4 p = reinterpret_cast<const int4*>(md.perm1)[i4];
+    const float4 d2 = reinterpret_cast<const float4*>(Hd.d2)[i4];
+    const float4 b2 = reinterpret_cast<const float4*>(Hd.b2)[i4];
+    const float4 mo = *reinterpret_cast<const float4*>(s_mod + 4 * i4);
+    const int pv[4] = {p.x, p.y, p.z, p.w};
+    const float dv[4] = {d2.x, d2.y, d2.z, d2.w}, bv[4] = {b2.x, b2.y, b2.z, b2.w}, mv[4] = {mo.x, mo.y, mo.z, mo.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) buf1[transposed<LEFT>(4 * i4 + e)] = silu(fadd(fmul(fmul(dv[e], mv[e]), buf0[pv[e]]), bv[e]));
+  }
+  cp_async_wait_all();
+  __syncthreads();
+  kronecker<LEFT, FUSED32>(buf1, buf0, s_left, s_right, buf1);  // second
+  stage_async(s_left, Hd.left[2], LEFT * LEFT);
+  stage_async(s_right, Hd.right[2], HADA_RIGHT * HADA_RIGHT);
+#pragma unroll
+  for (int q = 0; q < PER; ++q) {
+    const int i4 = tid + q * BLOCK_THREADS;
+    const int4 p = reinterpret_cast<const int4*>(md.perm2)[i4];
+    const float4 d3 = reinterpret_cast<const float4*>(Hd.d3)[i4];
+    const int pv[4] = {p.x, p.y, p.z, p.w};
+    const float dv[4] = {d3.x, d3.y, d3.z, d3.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) buf0[transposed<LEFT>(4 * i4 + e)] = fmul(buf1[pv[e]], dv[e]);
+  }
+  cp_async_wait_all();
+  __syncthreads();
+  kronecker<LEFT, FUSED32>(buf0, buf1, s_left, s_right, buf0);  // third
+}
+
+template <int LEFT>
+__global__ void __launch_bounds__(BLOCK_THREADS) k_block(ModelDev md, LayerDev L, Work w, int M) {
   extern __shared__ float sm[];
   constexpr int N = LEFT * HADA_RIGHT;
+  constexpr int PER = N / (4 * BLOCK_THREADS);  // float4 chunks per thread
   constexpr bool FUSED32 = LEFT == 32;
   const int t = blockIdx.x;
   if (t >= M || w.meta[t].slot < 0) return;
   const int d = md.d_model, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  float* s_a = sm;               // d
-  float* s_x = sm + MAX_D;       // d
-  float* s_pre = sm + 2 * MAX_D; // d
-  float* s_buf0 = sm + 3 * MAX_D;       // N
-  float* s_buf1 = s_buf0 + N;           // N
-  float* s_mod = s_buf1 + N;            // N
-  float* s_left = s_mod + N;            // LEFT*LEFT
+  float* s_a = sm;                        // d: attention output, then the running block value
+  float* s_x = sm + MAX_D;                // d: the routing input
+  float* s_pre = sm + 2 * MAX_D;          // d: pre-Hadamard norm
+  float* buf0 = sm + 3 * MAX_D;           // N
+  float* buf1 = buf0 + N;                 // N
+  float* s_mod = buf1 + N;                // N
+  float* s_left = s_mod + N;              // LEFT*LEFT
   float* s_right = s_left + LEFT * LEFT;  // 32*32
-  __shared__ float s_inv, s_gate, s_w[COND_RANK], s_chain[4][COND_RANK];
-
-  for (int i = tid; i < d; i += blockDim.x) {
-    s_a[i] = w.outp[(size_t)t * d + i];
-    s_x[i] = w.x[(size_t)t * d + i];
-  }
-  if (tid == 0) s_gate = sigmoid(L.attn_gate);
-  __syncthreads();
-  if (warp == 0) {
-    float ss = sum_of_squares_warp(s_a, d);
-    if (lane == 0) s_inv = inverse_rms(ss, d);
-  }
-  __syncthreads();
-  for (int i = tid; i < d; i += blockDim.x) {
-    float a = fmul(fmul(fadd(1.0f, L.post_norm[i]), s_a[i]), s_inv);
-    s_a[i] = fadd(s_x[i], fmul(s_gate, a));  // s_a now holds the running block value
-  }
-  __syncthreads();
-  if (warp == 0) {
-    float ss = sum_of_squares_warp(s_a, d);
-    if (lane == 0) s_inv = inverse_rms(ss, d);
-  }
-  __syncthreads();
-  for (int i = tid; i < d; i += blockDim.x) s_pre[i] = fmul(fmul(fadd(1.0f, L.pre_hada[i]), s_a[i]), s_inv);
-  __syncthreads();
+  // d*8 condition values, consumed before the first Kronecker stage: they
+  // borrow buf1 and s_mod when they fit there
+  float* s_condv = d * COND_RANK <= 2 * N ? buf1 : s_right + HADA_RIGHT * HADA_RIGHT;
+  __shared__ float s_inv, s_gate;
   const HadamardDev& Hd = L.hada;
-  // condition weights: four chains of rank-8 partial sums (hadamard.rs:263-276)
-  if (tid < 4 * COND_RANK) {
-    int j = tid / COND_RANK, rr = tid % COND_RANK;
-    float acc = 0.0f;
-    for (int g = 0; 4 * g + j < d; ++g) acc = fadd(acc, fmul(s_pre[4 * g + j], Hd.cond_v[(4 * g + j) * COND_RANK + rr]));
-    s_chain[j][rr] = acc;
+
+  stage_async(s_a, w.outp + (size_t)t * d, d);
+  stage_async(s_x, w.x + (size_t)t * d, d);
+  stage_async(s_condv, Hd.cond_v, d * COND_RANK);
+  stage_async(s_left, Hd.left[0], LEFT * LEFT);
+  stage_async(s_right, Hd.right[0], HADA_RIGHT * HADA_RIGHT);
+  if (tid == 0) s_gate = sigmoid(L.attn_gate);
+  cp_async_wait_all();
+  __syncthreads();
+  if (warp == 0) {
+    float ss = sum_of_squares_warp(s_a, d);
+    if (lane == 0) s_inv = inverse_rms(ss, d);
   }
   __syncthreads();
-  if (tid == 0) {
-    float wv[COND_RANK], peak = -INFINITY;
-    for (int rr = 0; rr < COND_RANK; ++rr) {
-      wv[rr] = fadd(fadd(fadd(fadd(0.0f, s_chain[0][rr]), s_chain[1][rr]), s_chain[2][rr]), s_chain[3][rr]);
-      peak = fmaxf(peak, wv[rr]);
-    }
-    float total = 0.0f;
-    for (int rr = 0; rr < COND_RANK; ++rr) {
-      wv[rr] = fast_exp(fsub(wv[rr], peak));
-      total = fadd(total, wv[rr]);
-    }
-    float inverse = fdiv(1.0f, total);
-    for (int rr = 0; rr < COND_RANK; ++rr) s_w[rr] = fmul(wv[rr], inverse);
+  for (int i = tid; i < d; i += BLOCK_THREADS) {
+    float a = fmul(fmul(fadd(1.0f, L.post_norm[i]), s_a[i]), s_inv);
+    s_a[i] = fadd(s_x[i], fmul(s_gate, a));
   }
   __syncthreads();
-  for (int i = tid; i < N; i += blockDim.x) {
-    float m = 1.0f;
-    for (int rr = 0; rr < COND_RANK; ++rr) m = fadd(m, fmul(s_w[rr], Hd.cond_u[rr * N + i]));
-    s_mod[i] = m;
-    s_buf0[i] = fmul(i < d ? s_pre[i] : 0.0f, Hd.d1[i]);
+  if (warp == 0) {
+    float ss = sum_of_squares_warp(s_a, d);
+    if (lane == 0) s_inv = inverse_rms(ss, d);
   }
-  for (int i = tid; i < LEFT * LEFT; i += blockDim.x) s_left[i] = Hd.left[0][i];
-  for (int i = tid; i < HADA_RIGHT * HADA_RIGHT; i += blockDim.x) s_right[i] = Hd.right[0][i];
   __syncthreads();
-  kronecker<LEFT, FUSED32>(s_buf0, s_left, s_right, s_buf1, s_buf0);  // first = K1(d1 ⊙ x)
-  for (int i = tid; i < N; i += blockDim.x) {
-    float g = s_buf0[md.perm1[i]];
-    s_buf1[i] = silu(fadd(fmul(fmul(Hd.d2[i], s_mod[i]), g), Hd.b2[i]));
-  }
-  for (int i = tid; i < LEFT * LEFT; i += blockDim.x) s_left[i] = Hd.left[1][i];
-  for (int i = tid; i < HADA_RIGHT * HADA_RIGHT; i += blockDim.x) s_right[i] = Hd.right[1][i];
+  for (int i = tid; i < d; i += BLOCK_THREADS) s_pre[i] = fmul(fmul(fadd(1.0f, L.pre_hada[i]), s_a[i]), s_inv);
   __syncthreads();
-  kronecker<LEFT, FUSED32>(s_buf1, s_left, s_right, s_mod, s_buf1);  // second (s_mod is free now)
-  for (int i = tid; i < N; i += blockDim.x) s_buf0[i] = fmul(s_buf1[md.perm2[i]], Hd.d3[i]);
-  for (int i = tid; i < LEFT * LEFT; i += blockDim.x) s_left[i] = Hd.left[2][i];
-  for (int i = tid; i < HADA_RIGHT * HADA_RIGHT; i += blockDim.x) s_right[i] = Hd.right[2][i];
-  __syncthreads();
-  kronecker<LEFT, FUSED32>(s_buf0, s_left, s_right, s_buf1, s_buf0);  // third
+  hadamard_core<LEFT>(md, Hd, d, s_pre, buf0, buf1, s_mod, s_left, s_right, s_condv);
   // x += mlp; delta = x - input; next lanes (lanes.rs:183-204)
   const float* route = w.route + (size_t)t * (LANES + LANES * LANES);
+  float rw[LANES + LANES * LANES];
+#pragma unroll
+  for (int k = 0; k < LANES + LANES * LANES; ++k) rw[k] = route[k];
   const float* stream = w.stream + (size_t)t * LANES * d;
   float* next = w.next_stream + (size_t)t * LANES * d;
-  for (int i = tid; i < d; i += blockDim.x) {
-    float xv = fadd(s_a[i], fmul(s_buf0[i], Hd.d4[i]));
-    float delta = fsub(xv, s_x[i]);
+  for (int i4 = tid; i4 < d / 4; i4 += BLOCK_THREADS) {
+    const float4 d4 = reinterpret_cast<const float4*>(Hd.d4)[i4];
+    float4 sv[LANES];
+#pragma unroll
+    for (int s = 0; s < LANES; ++s) sv[s] = reinterpret_cast<const float4*>(stream + s * d)[i4];
+    const float dv[4] = {d4.x, d4.y, d4.z, d4.w};
+    float delta[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      int i = 4 * i4 + e;
+      delta[e] = fsub(fadd(s_a[i], fmul(buf0[i], dv[e])), s_x[i]);
+    }
 #pragma unroll
     for (int l = 0; l < LANES; ++l) {
-      float acc = 0.0f;
+      float o[4];
 #pragma unroll
-      for (int s = 0; s < LANES; ++s) acc = fadd(acc, fmul(route[LANES + l * LANES + s], stream[s * d + i]));
-      next[l * d + i] = fadd(acc, fmul(route[l], delta));
+      for (int e = 0; e < 4; ++e) {
+        float acc = 0.0f;
+#pragma unroll
+        for (int s = 0; s < LANES; ++s) acc = fadd(acc, fmul(rw[LANES + l * LANES + s], (&sv[s].x)[e]));
+        o[e] = fadd(acc, fmul(rw[l], delta[e]));
+      }
+      reinterpret_cast<float4*>(next + l * d)[i4] = make_float4(o[0], o[1], o[2], o[3]);
     }
   }
 }
@@ -695,19 +1054,27 @@ __global__ void __launch_bounds__(512) k_block(ModelDev md, LayerDev L, Work w, 
 // lane_mean (session.rs:192-200) and the final zero-centred norm into the
 // sequence's hidden state, for the last token of each sequence. grid M, block 128.
 __global__ void __launch_bounds__(128) k_final(ModelDev md, Work w, float* __restrict__ hidden, int M) {
-  __shared__ float s_mean[MAX_D];
+  __shared__ __align__(16) float s_mean[MAX_D];
   __shared__ float s_inv;
-  int t = blockIdx.x;
+  const int t = blockIdx.x;
   if (t >= M) return;
-  TokenMeta meta = w.meta[t];
+  const TokenMeta meta = w.meta[t];
   if (meta.slot < 0 || !meta.last) return;
   const int d = md.d_model, tid = threadIdx.x;
   const float* stream = w.stream + (size_t)t * LANES * d;
-  for (int i = tid; i < d; i += blockDim.x) {
-    float m = 0.0f;
+  for (int i4 = tid; i4 < d / 4; i4 += blockDim.x) {
+    float4 s[LANES];
 #pragma unroll
-    for (int l = 0; l < LANES; ++l) m = fadd(m, fdiv(stream[l * d + i], (float)LANES));
-    s_mean[i] = m;
+    for (int l = 0; l < LANES; ++l) s[l] = reinterpret_cast<const float4*>(stream + l * d)[i4];
+    float m[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      float acc = 0.0f;
+#pragma unroll
+      for (int l = 0; l < LANES; ++l) acc = fadd(acc, fdiv((&s[l].x)[e], (float)LANES));
+      m[e] = acc;
+    }
+    reinterpret_cast<float4*>(s_mean)[i4] = make_float4(m[0], m[1], m[2], m[3]);
   }
   __syncthreads();
   if (tid < 32) {
@@ -721,46 +1088,61 @@ __global__ void __launch_bounds__(128) k_final(ModelDev md, Work w, float* __res
 // ------------------------------------------------------------------ select
 // argmax / argmax_allowed (generator.rs:147-165): the first index holding the
 // maximum over the allowed ids, or over all ids when none is allowed.
-// grid B, block 256.
+// grid B, block 256; each thread keeps its 32 logits (8 float4) in registers.
+constexpr int SELECT_CHUNKS = 8;
+
 __global__ void __launch_bounds__(256) k_select(const float* __restrict__ logits, int V, const uint32_t* __restrict__ mask,
                                                 const int32_t* __restrict__ active, uint32_t* __restrict__ next,
                                                 float* __restrict__ peaks) {
   __shared__ float s_red[8];
   __shared__ int s_idx[8];
-  __shared__ int s_any;
+  __shared__ int s_any[8];
   const int b = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   if (active && active[b] == 0) {
     if (tid == 0) next[b] = 0xffffffffu;
     return;
   }
-  const float* v = logits + (size_t)b * V;
+  const float4* v4 = reinterpret_cast<const float4*>(logits + (size_t)b * V);
   const uint32_t* m = mask ? mask + (size_t)b * (V / 32) : nullptr;
+  float4 val[SELECT_CHUNKS];
+  uint32_t bits[SELECT_CHUNKS];
+#pragma unroll
+  for (int c = 0; c < SELECT_CHUNKS; ++c) {
+    const int i4 = c * blockDim.x + tid;
+    const bool in = i4 < V / 4;
+    val[c] = in ? v4[i4] : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+    bits[c] = in ? (m ? (m[i4 >> 3] >> ((i4 & 7) * 4)) & 15u : 15u) : 0u;
+  }
   float pk_all = -INFINITY, pk_allowed = -INFINITY;
   int any = 0;
-  for (int i = tid; i < V; i += blockDim.x) {
-    float x = v[i];
-    pk_all = fmaxf(pk_all, x);
-    bool ok = m ? ((m[i >> 5] >> (i & 31)) & 1u) : true;
-    if (ok) {
-      pk_allowed = fmaxf(pk_allowed, x);
-      any = 1;
+#pragma unroll
+  for (int c = 0; c < SELECT_CHUNKS; ++c)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float x = (&val[c].x)[e];
+      pk_all = fmaxf(pk_all, x);
+      if ((bits[c] >> e) & 1u) {
+        pk_allowed = fmaxf(pk_allowed, x);
+        any = 1;
+      }
     }
-  }
-  if (tid == 0) s_any = 0;
-  __syncthreads();
-  if (any) s_any = 1;
-  float all = block_max(pk_all, s_red);
-  float allowed = block_max(pk_allowed, s_red);
-  bool restricted = m && s_any;
-  float target = restricted ? allowed : all;
+  any = __any_sync(FULL, any);
+  if (lane == 0) s_any[warp] = any;
+  const float all = block_max(pk_all, s_red);
+  const float allowed = block_max(pk_allowed, s_red);
+  int anyb = 0;
+  for (int i = 0; i < (int)(blockDim.x >> 5); ++i) anyb |= s_any[i];
+  const bool restricted = m && anyb;
+  const float target = restricted ? allowed : all;
   int best = 0x7fffffff;
-  for (int i = tid; i < V; i += blockDim.x) {
-    bool ok = restricted ? ((m[i >> 5] >> (i & 31)) & 1u) : true;
-    if (ok && v[i] == target) {
-      best = i;
-      break;
+#pragma unroll
+  for (int c = 0; c < SELECT_CHUNKS; ++c)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int i = 4 * (c * (int)blockDim.x + tid) + e;
+      const bool ok = restricted ? ((bits[c] >> e) & 1u) : (i < V);
+      if (ok && (&val[c].x)[e] == target) best = min(best, i);
     }
-  }
   for (int s = 16; s > 0; s >>= 1) best = min(best, __shfl_xor_sync(FULL, best, s));
   __syncthreads();
   if (lane == 0) s_idx[warp] = best;
@@ -823,14 +1205,19 @@ void set_exp_constants(const nbx::ExpConstants& constants, const nbx::ExceptionS
   cudaMemcpyToSymbolAsync(c_exceptions, &exceptions, sizeof exceptions, 0, cudaMemcpyHostToDevice, stream);
 }
 
-size_t route_smem(const ModelDev& md) { return (size_t)LANES * md.d_model * 4 * 2 + LANES * md.d_model; }
+size_t route_smem(const ModelDev& md) {
+  const size_t n = (size_t)LANES * md.d_model, ng = n / GROUP;
+  return (2 * n + n / 4 + PHI_ROWS * ng + md.d_model) * 4;
+}
 size_t attend_smem(const ModelDev& md, int t_cap) {
   int G = md.heads / md.kv_heads;
-  return (size_t)2 * G * t_cap * 4 + 2 * (size_t)G * (t_cap / 4 + 2) * 4 + (size_t)8 * G * HEAD_DIM * 4;
+  return (size_t)(G + 1) * t_cap * 4 + 2 * (size_t)G * att_wstride(t_cap) * 4 + (size_t)ATT_SLICES * G * HEAD_DIM * 4;
 }
 size_t block_smem(const ModelDev& md) {
   int N = md.hada_left * HADA_RIGHT;
-  return (size_t)(3 * MAX_D + 3 * N + md.hada_left * md.hada_left + HADA_RIGHT * HADA_RIGHT) * 4;
+  size_t floats = 3 * MAX_D + 3 * N + md.hada_left * md.hada_left + HADA_RIGHT * HADA_RIGHT;
+  if ((int)md.d_model * COND_RANK > 2 * N) floats += (size_t)md.d_model * COND_RANK;
+  return floats * 4;
 }
 
 cudaError_t configure(const ModelDev& md, int t_cap) {
@@ -842,18 +1229,23 @@ cudaError_t configure(const ModelDev& md, int t_cap) {
   if ((e = cudaFuncSetAttribute(k_block<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)block_smem(md)))) return e;
   if ((e = cudaFuncSetAttribute(k_block<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)block_smem(md)))) return e;
   if ((e = cudaFuncSetAttribute(k_stats, cudaFuncAttributeMaxDynamicSharedMemorySize, 2 * 8192 * 4))) return e;
+  if ((e = cudaFuncSetAttribute(k_gemm<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gemm_smem<16>()))) return e;
+  if ((e = cudaFuncSetAttribute(k_gemm<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gemm_smem<32>()))) return e;
+
   return cudaSuccess;
 }
 
+static int* g_gemm_error = nullptr;
+
+void set_error_flag(int* flag) { g_gemm_error = flag; }
+
 static void project(const QMat& W, const int8_t* act, const float* act_scale, float* out, int M, int out_stride,
                     const TokenMeta* meta, cudaStream_t st) {
-  int rowblocks = (W.rows + 63) / 64;
-  int chunk = M <= 8 ? M : 16;
-  dim3 grid(rowblocks, (M + chunk - 1) / chunk);
-  if (W.groups == 4)
-    k_project<4><<<grid, 256, 0, st>>>(W, act, act_scale, out, M, out_stride, chunk, meta);
-  else if (W.groups == 8)
-    k_project<8><<<grid, 256, 0, st>>>(W, act, act_scale, out, M, out_stride, chunk, meta);
+  const int tiles = (W.rows + GEMM_ROWS - 1) / GEMM_ROWS;
+  if (M <= 16)
+    k_gemm<16><<<dim3(tiles, 1), 8 * 16, gemm_smem<16>(), st>>>(W, act, act_scale, out, M, out_stride, meta, g_gemm_error);
+  else
+    k_gemm<32><<<dim3(tiles, (M + 31) / 32), 8 * 32, gemm_smem<32>(), st>>>(W, act, act_scale, out, M, out_stride, meta, g_gemm_error);
 }
 
 void launch_embed(const ModelDev& md, const Work& w, int M, cudaStream_t st) { k_embed<<<M, 128, 0, st>>>(md, w, M); }
@@ -867,18 +1259,18 @@ void launch_layer(const ModelDev& md, const LayerDev& L, const Work& w, const Kv
   k_heads<<<M, 32 * (H + 2 * KV), 0, st>>>(md, L, w, kv, M, layer);
   const int G = H / KV;
   if (G == 1)
-    k_attend<1><<<dim3(M, KV), 160, attend_smem(md, t_cap), st>>>(md, w, kv, M, layer, L.global, t_cap);
+    k_attend<1><<<dim3(M, KV), ATT_THREADS_ALL, attend_smem(md, t_cap), st>>>(md, w, kv, M, layer, L.global, t_cap);
   else if (G == 2)
-    k_attend<2><<<dim3(M, KV), 160, attend_smem(md, t_cap), st>>>(md, w, kv, M, layer, L.global, t_cap);
+    k_attend<2><<<dim3(M, KV), ATT_THREADS_ALL, attend_smem(md, t_cap), st>>>(md, w, kv, M, layer, L.global, t_cap);
   else
-    k_attend<4><<<dim3(M, KV), 160, attend_smem(md, t_cap), st>>>(md, w, kv, M, layer, L.global, t_cap);
+    k_attend<4><<<dim3(M, KV), ATT_THREADS_ALL, attend_smem(md, t_cap), st>>>(md, w, kv, M, layer, L.global, t_cap);
   k_prep<<<M, 128, 0, st>>>(w.attn, H * HEAD_DIM, nullptr, w.proj + (H + 2 * KV) * HEAD_DIM, proj_stride, H * HEAD_DIM, w.act,
                             w.act_scale, M, w.meta, md.inv_sqrt_group, 1);
   project(L.out, w.act, w.act_scale, w.outp, M, d, w.meta, st);
   if (md.hada_left == 64)
-    k_block<64><<<M, 512, block_smem(md), st>>>(md, L, w, M);
+    k_block<64><<<M, BLOCK_THREADS, block_smem(md), st>>>(md, L, w, M);
   else
-    k_block<32><<<M, 512, block_smem(md), st>>>(md, L, w, M);
+    k_block<32><<<M, BLOCK_THREADS, block_smem(md), st>>>(md, L, w, M);
 }
 
 void launch_final(const ModelDev& md, const Work& w, float* hidden, int M, cudaStream_t st) { k_final<<<M, 128, 0, st>>>(md, w, hidden, M); }
@@ -904,11 +1296,11 @@ void launch_advance(TokenMeta* meta, int B, cudaStream_t st) { k_advance<<<(B + 
 void launch_attend(const ModelDev& md, const LayerDev& L, const Work& w, const KvDev& kv, int M, int layer, int t_cap, cudaStream_t st) {
   const int G = md.heads / md.kv_heads, KV = md.kv_heads;
   if (G == 1)
-    k_attend<1><<<dim3(M, KV), 160, attend_smem(md, t_cap), st>>>(md, w, kv, M, layer, L.global, t_cap);
+    k_attend<1><<<dim3(M, KV), ATT_THREADS_ALL, attend_smem(md, t_cap), st>>>(md, w, kv, M, layer, L.global, t_cap);
   else if (G == 2)
-    k_attend<2><<<dim3(M, KV), 160, attend_smem(md, t_cap), st>>>(md, w, kv, M, layer, L.global, t_cap);
+    k_attend<2><<<dim3(M, KV), ATT_THREADS_ALL, attend_smem(md, t_cap), st>>>(md, w, kv, M, layer, L.global, t_cap);
   else
-    k_attend<4><<<dim3(M, KV), 160, attend_smem(md, t_cap), st>>>(md, w, kv, M, layer, L.global, t_cap);
+    k_attend<4><<<dim3(M, KV), ATT_THREADS_ALL, attend_smem(md, t_cap), st>>>(md, w, kv, M, layer, L.global, t_cap);
 }
 
 // ------------------------------------------------------------------- debug
@@ -923,6 +1315,39 @@ __global__ void k_debug_math(int op, const float* in, float* out, int n) {
 
 void launch_debug_math(int op, const float* in, float* out, int n, cudaStream_t st) {
   k_debug_math<<<(n + 255) / 256, 256, 0, st>>>(op, in, out, n);
+}
+
+// HadamardWeights::apply (hadamard.rs:260-304) of one layer on `M` inputs.
+template <int LEFT>
+__global__ void __launch_bounds__(BLOCK_THREADS) k_debug_hadamard(ModelDev md, HadamardDev Hd, const float* in, float* out, int M) {
+  extern __shared__ float sm[];
+  constexpr int N = LEFT * HADA_RIGHT;
+  const int t = blockIdx.x, d = md.d_model;
+  float* s_pre = sm + 2 * MAX_D;
+  float* buf0 = sm + 3 * MAX_D;
+  float* buf1 = buf0 + N;
+  float* s_mod = buf1 + N;
+  float* s_left = s_mod + N;
+  float* s_right = s_left + LEFT * LEFT;
+  float* s_condv = d * COND_RANK <= 2 * N ? buf1 : s_right + HADA_RIGHT * HADA_RIGHT;
+  stage_async(s_condv, Hd.cond_v, d * COND_RANK);
+  stage_async(s_left, Hd.left[0], LEFT * LEFT);
+  stage_async(s_right, Hd.right[0], HADA_RIGHT * HADA_RIGHT);
+  stage_async(s_pre, in + (size_t)t * d, d);
+  cp_async_wait_all();
+  __syncthreads();
+  hadamard_core<LEFT>(md, Hd, d, s_pre, buf0, buf1, s_mod, s_left, s_right, s_condv);
+  for (int i = threadIdx.x; i < d; i += BLOCK_THREADS) out[(size_t)t * d + i] = fmul(buf0[i], Hd.d4[i]);
+}
+
+void launch_debug_hadamard(const ModelDev& md, const LayerDev& L, const float* in, float* out, int M, cudaStream_t st) {
+  if (md.hada_left == 64) {
+    cudaFuncSetAttribute(k_debug_hadamard<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)block_smem(md));
+    k_debug_hadamard<64><<<M, BLOCK_THREADS, block_smem(md), st>>>(md, L.hada, in, out, M);
+  } else {
+    cudaFuncSetAttribute(k_debug_hadamard<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)block_smem(md));
+    k_debug_hadamard<32><<<M, BLOCK_THREADS, block_smem(md), st>>>(md, L.hada, in, out, M);
+  }
 }
 
 // One codebook product of K-wide inputs (rotated and quantised per group,

@@ -10,6 +10,8 @@ namespace nbk {
 
 void set_exp_constants(const nbx::ExpConstants& constants, const nbx::ExceptionSet& exceptions, cudaStream_t stream);
 cudaError_t configure(const nbl::ModelDev& md, int t_cap);
+// Device flag the tensor-core product sets when a bounded wait gives up.
+void set_error_flag(int* flag);
 
 void launch_embed(const nbl::ModelDev& md, const nbl::Work& w, int M, cudaStream_t st);
 void launch_layer(const nbl::ModelDev& md, const nbl::LayerDev& L, const nbl::Work& w, const nbl::KvDev& kv, int M, int layer,
@@ -24,6 +26,7 @@ void launch_stats(const float* logits, int V, const uint32_t* mask, const int32_
 void launch_advance(nbl::TokenMeta* meta, int B, cudaStream_t st);
 void launch_attend(const nbl::ModelDev& md, const nbl::LayerDev& L, const nbl::Work& w, const nbl::KvDev& kv, int M, int layer,
                    int t_cap, cudaStream_t st);
+void launch_debug_hadamard(const nbl::ModelDev& md, const nbl::LayerDev& L, const float* in, float* out, int M, cudaStream_t st);
 void launch_debug_math(int op, const float* in, float* out, int n, cudaStream_t st);
 void launch_debug_project(const nbl::ModelDev& md, const nbl::QMat& W, const float* in, int K, int M, int8_t* act,
                           float* act_scale, float* out, int out_stride, cudaStream_t st);

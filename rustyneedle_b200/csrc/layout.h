@@ -3,10 +3,10 @@
 //
 // Weights. Every codebook-quantised matrix (crates/cact/src/record.rs, kind 3)
 // is expanded once at load from its 2- or 4-bit indices to int8 through the
-// reference's integer level table (crates/kernels/src/neon.rs:114-123) and
-// stored lane-interleaved for the projection kernel: rows in blocks of 8, each
-// row's 128-column groups cut into 16-byte pieces, piece k of (row r, group g)
-// at ((block*KP + k)*32 + 4*r + g)*16 for K = 512 (KP = 8 pieces per group).
+// reference's integer level table (crates/kernels/src/neon.rs:114-123). The
+// matrices of the tensor-core products (fused q/k/v/gate, out_proj, the tied
+// logits) are stored in the K-major core-matrix layout of core_offset() with
+// rows padded to whole 128-row tiles; the lane maps stay row-major.
 // Per (row, group) scales are f32: for 2-bit matrices the product
 // norm*level_scale of the panel combine (panel.rs:184), for 4-bit matrices the
 // norm alone (the row combine multiplies by level_scale after the norm,
@@ -19,7 +19,13 @@
 //   kscale  [kv][64] f32, vscale [kv][64] f32
 #pragma once
 
+#include <stddef.h>
 #include <stdint.h>
+
+#ifndef __CUDACC__
+#define __host__
+#define __device__
+#endif
 
 namespace nbl {
 
@@ -52,9 +58,17 @@ inline PageGeometry page_geometry(uint32_t kv_heads) {
   return p;
 }
 
+// Canonical K-major core-matrix layout of the tensor-core operands: element
+// (row r, byte k) of a matrix with `kchunks` 16-byte chunks per row sits in
+// the 8-row × 16-byte core matrix (r/8, k/16), rows 16 bytes apart. A group of
+// 8 rows is one contiguous block of kchunks·128 bytes.
+__host__ __device__ inline size_t core_offset(size_t r, uint32_t k, uint32_t kchunks) {
+  return ((r >> 3) * kchunks + (k >> 4)) * 128 + (r & 7) * 16 + (k & 15);
+}
+
 // A codebook-quantised matrix in device layout.
 struct QMat {
-  const int8_t* codes;   // lane-interleaved int8 (K = 512) or row-major int8 (other K)
+  const int8_t* codes;   // int8 in the core-matrix layout (K = 512, rows padded to 128) or row-major (lane maps)
   const float* scales;   // [rows][groups]
   float level_scale;     // IntegerLevels::scale
   uint32_t rows, cols, groups;
@@ -116,7 +130,7 @@ struct Work {
   float* next_stream;       // [M][4][d]
   float* x;                 // [M][d]      routing input, then the block's running value
   float* route;             // [M][4 + 16] post gates and Sinkhorn residual weights
-  int8_t* act;              // [M][max(d, attention width)] int8 activations
+  int8_t* act;              // int8 activations in the core-matrix layout (K = 512), capacity rounded to 128
   float* act_scale;         // [M][groups]
   float* proj;              // [M][q + k + v + gate]
   int8_t* qcodes;           // [M][heads][64]

@@ -199,6 +199,7 @@ struct Engine {
   float* d_stats = nullptr;
   uint32_t* d_mask = nullptr;
   int32_t* d_active = nullptr;
+  int* d_error = nullptr;  // set by a device wait that gave up
   int t_cap = 0;
 
   KvDev kv() const { return KvDev{pool, d_page_table, max_pages, geo.num_layers}; }
@@ -300,40 +301,29 @@ static std::shared_ptr<nbx::ExpfTable> load_expf_table() {
 }
 
 // Expands a codebook matrix to int8 through the integer level table, in the
-// projection kernel's lane-interleaved layout (K = 512 or 1024) or row-major.
-static void expand_matrix(const nba::Archive& a, uint32_t index, const Levels& lv, bool interleave, std::vector<int8_t>& codes,
-                          std::vector<float>& scales, uint32_t row_offset_codes, uint32_t row_offset_scales, uint32_t total_rows) {
+// tensor-core core-matrix layout (rows padded to 128-row tiles) or row-major.
+static void expand_matrix(const nba::Archive& a, uint32_t index, const Levels& lv, bool core, std::vector<int8_t>& codes,
+                          std::vector<float>& scales, uint32_t row_offset, uint32_t total_rows) {
   const nba::Record& r = a.record(index);
   uint64_t rows = r.rows(), cols = r.padded_columns(), groups = r.groups_per_row(), rb = r.packed_row_bytes();
   const uint8_t* packed = a.data(index);
   const uint8_t* norms = packed + r.packed_bytes();
   if (r.packed_bytes() + rows * groups * 2 > r.byte_len) fail(NB_ERR_ARCHIVE, "codebook tensor " + std::to_string(index) + " is shorter than its shape");
-  uint32_t gk = (uint32_t)(cols / GROUP), RB = interleave ? 32 / gk : 1;
-  if (interleave) {
-    size_t blocks = (total_rows + RB - 1) / RB;
-    if (codes.size() < blocks * 4096) codes.resize(blocks * 4096, 0);
-  } else if (codes.size() < (size_t)total_rows * cols) {
-    codes.resize((size_t)total_rows * cols, 0);
-  }
+  const uint64_t stored_rows = core ? (total_rows + 127) / 128 * 128 : total_rows;
+  if (codes.size() < stored_rows * cols) codes.resize(stored_rows * cols, 0);
   if (scales.size() < (size_t)total_rows * groups) scales.resize((size_t)total_rows * groups, 0.0f);
   for (uint64_t row = 0; row < rows; ++row) {
     const uint8_t* src = packed + row * rb;
-    uint64_t out_row = row + row_offset_codes;
+    const uint64_t out_row = row + row_offset;
     for (uint64_t c = 0; c < cols; ++c) {
       int8_t v = lv.ints[code_at(src, c, lv.bits)];
-      if (interleave) {
-        uint64_t block = out_row / RB, rr = out_row % RB, g = c / GROUP, within = c % GROUP, k = within / 16, byte = within % 16;
-        uint64_t lane = rr * gk + g;
-        codes[((block * 8 + k) * 32 + lane) * 16 + byte] = v;
-      } else {
-        codes[out_row * cols + c] = v;
-      }
+      codes[core ? core_offset(out_row, (uint32_t)c, (uint32_t)(cols / 16)) : out_row * cols + c] = v;
     }
     for (uint64_t g = 0; g < groups; ++g) {
       uint16_t h;
       std::memcpy(&h, norms + 2 * (row * groups + g), 2);
       float norm = nba::half_to_f32(h);
-      scales[(row + row_offset_scales) * groups + g] = lv.fused ? norm * lv.int_scale : norm;
+      scales[(row + row_offset) * groups + g] = lv.fused ? norm * lv.int_scale : norm;
     }
   }
 }
@@ -361,8 +351,8 @@ std::shared_ptr<Engine> open_engine(const char* path, const nb_options* opt) {
   if (!g.engram_sites.empty()) fail(NB_ERR_UNSUPPORTED, "engram sites are not implemented by this build");
   if (g.mhc_lanes != LANES) fail(NB_ERR_UNSUPPORTED, "only 4-lane models are implemented");
   if (g.qk_head_dim != HEAD_DIM || g.v_head_dim != HEAD_DIM) fail(NB_ERR_UNSUPPORTED, "head dims other than 64 are not implemented");
-  if (g.d_model % GROUP || g.d_model > MAX_D || (g.d_model / GROUP != 4 && g.d_model / GROUP != 8))
-    fail(NB_ERR_UNSUPPORTED, "d_model " + std::to_string(g.d_model) + " is not implemented (512 or 1024)");
+  if (g.d_model != 512)
+    fail(NB_ERR_UNSUPPORTED, "d_model " + std::to_string(g.d_model) + " is not implemented (the tensor-core products take K = 512)");
   if (g.num_kv_heads == 0 || g.num_heads % g.num_kv_heads || g.num_heads / g.num_kv_heads > 4 ||
       (g.num_heads / g.num_kv_heads == 3) || g.num_heads > MAX_HEADS || g.num_heads * HEAD_DIM != g.d_model)
     fail(NB_ERR_UNSUPPORTED, "head layout is not implemented");
@@ -435,7 +425,7 @@ std::shared_ptr<Engine> open_engine(const char* path, const nb_options* opt) {
     md.embed_norms = A.upload(norms, st);
     std::vector<int8_t> codes;
     std::vector<float> scales;
-    expand_matrix(a, lay.embedding, elv, true, codes, scales, 0, 0, g.vocab);
+    expand_matrix(a, lay.embedding, elv, true, codes, scales, 0, g.vocab);
     // only the first output_vocab rows take part in the logits (session.rs:174-175)
     md.logits = QMat{A.upload(codes, st), A.upload(scales, st), elv.int_scale, md.output_vocab, d, d / GROUP, elv.fused ? 1 : 0};
   }
@@ -449,7 +439,7 @@ std::shared_ptr<Engine> open_engine(const char* path, const nb_options* opt) {
       if (lv.fused) fail(NB_ERR_UNSUPPORTED, std::string(what) + " is 2-bit; the lane maps are implemented for 4-bit codes");
       std::vector<int8_t> codes;
       std::vector<float> scales;
-      expand_matrix(a, index, lv, false, codes, scales, 0, 0, rows);
+      expand_matrix(a, index, lv, false, codes, scales, 0, rows);
       return QMat{A.upload(codes, st), A.upload(scales, st), lv.int_scale, rows, n, n / GROUP, 0};
     };
     md.phi_pre = phi(lay.lanes.phi_pre, L * LANES, "phi_pre");
@@ -502,14 +492,14 @@ std::shared_ptr<Engine> open_engine(const char* path, const nb_options* opt) {
     uint32_t offset = 0;
     for (uint32_t m : {t.q, t.k, t.v, t.gate}) {
       Levels lv = levels_for(a.record(m).bits, a.codebook(), GROUP);
-      expand_matrix(a, m, lv, true, codes, scales, offset, offset, qkvg_rows);
+      expand_matrix(a, m, lv, true, codes, scales, offset, qkvg_rows);
       offset += (uint32_t)a.record(m).rows();
     }
     D.qkvg = QMat{A.upload(codes, st), A.upload(scales, st), lq.int_scale, qkvg_rows, d, d / GROUP, lq.fused ? 1 : 0};
     Levels lo = levels_for(a.record(t.out).bits, a.codebook(), GROUP);
     codes.clear();
     scales.clear();
-    expand_matrix(a, t.out, lo, true, codes, scales, 0, 0, d);
+    expand_matrix(a, t.out, lo, true, codes, scales, 0, d);
     D.out = QMat{A.upload(codes, st), A.upload(scales, st), lo.int_scale, d, H * HEAD_DIM, (H * HEAD_DIM) / GROUP, lo.fused ? 1 : 0};
     D.norm_in = A.upload(floats_of(a, t.norm_in, d, "norm_in"), st);
     D.post_norm = A.upload(floats_of(a, t.post_norm, d, "post_norm"), st);
@@ -576,7 +566,9 @@ std::shared_ptr<Engine> open_engine(const char* path, const nb_options* opt) {
   w.next_stream = A.alloc<float>((size_t)M * LANES * d);
   w.x = A.alloc<float>((size_t)M * d);
   w.route = A.alloc<float>((size_t)M * (LANES + LANES * LANES));
-  w.act = A.alloc<int8_t>((size_t)M * actw);
+  const size_t act_rows = ((size_t)M + 127) / 128 * 128;
+  w.act = A.alloc<int8_t>(act_rows * actw);
+  NB_CUDA(cudaMemsetAsync(w.act, 0, act_rows * actw, st));
   w.act_scale = A.alloc<float>((size_t)M * (actw / GROUP));
   w.proj = A.alloc<float>((size_t)M * qkvg_rows);
   w.qcodes = A.alloc<int8_t>((size_t)M * H * HEAD_DIM);
@@ -584,7 +576,12 @@ std::shared_ptr<Engine> open_engine(const char* path, const nb_options* opt) {
   w.attn = A.alloc<float>((size_t)M * AW);
   w.outp = A.alloc<float>((size_t)M * d);
   const uint32_t B = E->max_sessions, V = md.output_vocab;
-  E->d_logit_act = A.alloc<int8_t>((size_t)B * d);
+  const size_t logit_rows = ((size_t)B + 127) / 128 * 128;
+  E->d_logit_act = A.alloc<int8_t>(logit_rows * d);
+  NB_CUDA(cudaMemsetAsync(E->d_logit_act, 0, logit_rows * d, st));
+  E->d_error = A.alloc<int>(1);
+  NB_CUDA(cudaMemsetAsync(E->d_error, 0, sizeof(int), st));
+  nbk::set_error_flag(E->d_error);
   E->d_logit_scale = A.alloc<float>((size_t)B * (d / GROUP));
   E->d_logits = A.alloc<float>((size_t)B * V);
   E->d_slots = A.alloc<int32_t>(B);
@@ -1187,12 +1184,33 @@ nb_status nb_debug_project(nb_model* model, int which, uint32_t layer, const flo
     NB_CUDA(cudaSetDevice(E.device));
     E.settle();
     const uint32_t K = W.cols;
-    DeviceTemp<float> din(count * K), dout(count * W.rows), dscale(count * W.groups);
-    DeviceTemp<int8_t> dact(count * K);
+    // the tensor-core product reads whole 16..128-token tiles of activations
+    const size_t tile_rows = (count + 127) / 128 * 128;
+    DeviceTemp<float> din(count * K), dout(count * W.rows), dscale(tile_rows * W.groups);
+    DeviceTemp<int8_t> dact(tile_rows * K);
+    NB_CUDA(cudaMemsetAsync(dact.p, 0, tile_rows * K, E.stream));
     NB_CUDA(cudaMemcpyAsync(din.p, in, count * K * 4, cudaMemcpyHostToDevice, E.stream));
     nbk::launch_debug_project(E.md, W, din.p, (int)K, (int)count, dact.p, dscale.p, dout.p, (int)W.rows, E.stream);
     NB_CUDA(cudaGetLastError());
     NB_CUDA(cudaMemcpyAsync(out, dout.p, count * W.rows * 4, cudaMemcpyDeviceToHost, E.stream));
+    NB_CUDA(cudaStreamSynchronize(E.stream));
+  });
+}
+
+nb_status nb_debug_hadamard(nb_model* model, uint32_t layer, const float* in, size_t count, float* out) {
+  if (!model || !in || !out || count == 0) return NB_ERR_ARGUMENT;
+  return guard([&] {
+    Engine& E = *model->engine;
+    std::lock_guard<std::mutex> lock(E.mutex);
+    if (layer >= E.layers.size()) fail(NB_ERR_ARGUMENT, "no such layer");
+    NB_CUDA(cudaSetDevice(E.device));
+    E.settle();
+    const size_t d = E.md.d_model;
+    DeviceTemp<float> din(count * d), dout(count * d);
+    NB_CUDA(cudaMemcpyAsync(din.p, in, count * d * 4, cudaMemcpyHostToDevice, E.stream));
+    nbk::launch_debug_hadamard(E.md, E.layers[layer], din.p, dout.p, (int)count, E.stream);
+    NB_CUDA(cudaGetLastError());
+    NB_CUDA(cudaMemcpyAsync(out, dout.p, count * d * 4, cudaMemcpyDeviceToHost, E.stream));
     NB_CUDA(cudaStreamSynchronize(E.stream));
   });
 }

@@ -25,6 +25,7 @@ def _declare() -> None:
         "nb_debug_math": [P, I, P, P, SZ],
         "nb_debug_project": [P, I, U32, P, SZ, P],
         "nb_debug_hidden": [P, P],
+        "nb_debug_hadamard": [P, U32, P, SZ, P],
         "nb_debug_kv": [P, U32, P, P, P, P],
         "nb_debug_time_attention": [P, U32, ctypes.POINTER(ctypes.c_float), ctypes.POINTER(ctypes.c_double)],
     }.items():
@@ -47,6 +48,14 @@ def project(model: Model, which: int, layer: int, x: np.ndarray, rows: int) -> n
     x = np.ascontiguousarray(np.atleast_2d(x), dtype=np.float32)
     out = np.empty((x.shape[0], rows), dtype=np.float32)
     _check(lib().nb_debug_project(model._h, which, layer, _ptr(x), x.shape[0], _ptr(out)))
+    return out
+
+
+def hadamard(model: Model, layer: int, x: np.ndarray) -> np.ndarray:
+    _declare()
+    x = np.ascontiguousarray(np.atleast_2d(x), dtype=np.float32)
+    out = np.empty_like(x)
+    _check(lib().nb_debug_hadamard(model._h, layer, _ptr(x), x.shape[0], _ptr(out)))
     return out
 
 

@@ -100,6 +100,34 @@ def test_fused_projection_matches_the_panel_kernel(device_model, oracle_model, l
         start += rows
 
 
+@pytest.mark.parametrize("tokens", [17, 40, 300])
+def test_projection_over_many_token_tiles(device_model, oracle_model, tokens):
+    from rustyneedle_b200 import debug
+
+    rng = np.random.default_rng(tokens)
+    x = (rng.standard_normal((tokens, 512)) * rng.uniform(0.01, 3.0, (tokens, 1))).astype(np.float32)
+    got = debug.project(device_model, debug.MATRIX_QKVG, 4, x, 1536)
+    start = 0
+    for name, rows in (("q", 512), ("k", 256), ("v", 256), ("gate", 512)):
+        tensor = _tensor_index(oracle_model, (name, 4))
+        for t in range(0, tokens, 7):
+            want, _ = oracle_model.matrix_product(tensor, x[t])
+            assert _bits_equal(got[t, start:start + rows], want), (name, t, _mismatch(got[t, start:start + rows], want))
+        start += rows
+
+
+@pytest.mark.parametrize("layer", [0, 11])
+def test_hadamard_mlp_matches(device_model, oracle_model, layer):
+    from rustyneedle_b200 import debug
+
+    rng = np.random.default_rng(50 + layer)
+    x = rng.standard_normal((6, 512)).astype(np.float32)
+    got = debug.hadamard(device_model, layer, x)
+    for t in range(6):
+        want = oracle_model.hadamard(layer, x[t])
+        assert _bits_equal(got[t], want), (t, _mismatch(got[t], want))
+
+
 def test_out_projection_and_logit_rows_match(device_model, oracle_model):
     from rustyneedle_b200 import debug
 
