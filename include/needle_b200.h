@@ -148,6 +148,23 @@ nb_status nb_model_synchronize(nb_model* model);
  * f32::exp exactly) and writes it to `path`. Runs on the host CPU. */
 nb_status nb_build_expf_table(const char* path);
 
+/* Allocation-free codebook product. It has no counterpart in the reference:
+ * it serves callers that may not allocate device memory — a host that has
+ * given all of the GPU's memory to its own pool, or a thread that must not
+ * take the device-wide synchronisation cudaMalloc/cudaFree imply — with the
+ * same result as QuantisedMatrix::prepare + multiply_vector
+ * (crates/kernels/src/matrix.rs:123-165) through one device matrix: which = 0
+ * the fused q/k/v/gate rows of `layer`, 1 its out_proj, 2 the tied embedding.
+ * in_device: count × 512 floats (16-byte aligned), out_device: count × rows
+ * floats, both device memory of the model's GPU; stream: a cudaStream_t of that
+ * GPU, or NULL for the model's stream. Returns when the product is complete.
+ * Its scratch is a fixed array of the library, one per GPU, that holds at most
+ * 256 tokens: a larger count fails with NB_ERR_ARGUMENT, before any work. The
+ * first call on a GPU looks the array up (make it before any stream capture).
+ * Every call shares the array: calls that overlap in time race on it. */
+nb_status nb_model_project_static(nb_model* model, int which, uint32_t layer, const float* in_device, uint32_t count,
+                                  float* out_device, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

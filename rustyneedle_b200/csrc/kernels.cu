@@ -18,6 +18,8 @@
 // logits product and k_select (generator.rs:147-194).
 #include <cuda_runtime.h>
 
+#include <mutex>
+
 #include "device.cuh"
 #include "kernels.h"
 
@@ -1357,6 +1359,60 @@ void launch_debug_project(const ModelDev& md, const QMat& W, const float* in, in
                           float* out, int out_stride, cudaStream_t st) {
   k_prep<<<M, 128, 0, st>>>(in, K, nullptr, nullptr, 0, K, act, act_scale, M, nullptr, md.inv_sqrt_group, 0);
   project(W, act, act_scale, out, M, out_stride, nullptr, st);
+}
+
+// ------------------------------------------------ allocation-free product
+// The one codebook product above for callers that may not allocate device
+// memory: a host that has handed all of the GPU's memory to its own pool, or
+// a thread that must not take the implicit device-wide synchronisation of
+// cudaMalloc/cudaFree. Its scratch — the int8 activations in the
+// core-matrix layout, their per-group scales and the flag of a bounded wait
+// that gave up — is this file-scope array, one per device, shared by every
+// call: two calls that overlap in time (on any streams or threads) race on it.
+// Nothing in it has to start at zero except the flag, which each call clears;
+// the product reads the unused token rows of its last tile but stores none of
+// their columns.
+constexpr size_t STATIC_ACT_BYTES = (size_t)STATIC_MAX_TOKENS * GEMM_K;
+constexpr size_t STATIC_SCALE_BYTES = (size_t)STATIC_MAX_TOKENS * (GEMM_K / GROUP) * sizeof(float);
+constexpr size_t STATIC_SCRATCH_BYTES = STATIC_ACT_BYTES + STATIC_SCALE_BYTES + 256;
+static_assert(STATIC_MAX_TOKENS % 32 == 0, "the scratch must hold whole 32-token tiles");
+static __device__ __align__(256) uint8_t g_static_scratch[STATIC_SCRATCH_BYTES];
+
+constexpr int STATIC_MAX_DEVICES = 64;
+static uint8_t* g_static_address[STATIC_MAX_DEVICES];
+static std::mutex g_static_mutex;
+
+cudaError_t static_scratch_setup(int device) {
+  if (device < 0 || device >= STATIC_MAX_DEVICES) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lock(g_static_mutex);
+  if (g_static_address[device]) return cudaSuccess;
+  cudaError_t e = cudaSetDevice(device);
+  if (e != cudaSuccess) return e;
+  void* p = nullptr;
+  e = cudaGetSymbolAddress(&p, g_static_scratch);
+  if (e != cudaSuccess) return e;
+  g_static_address[device] = static_cast<uint8_t*>(p);
+  return cudaSuccess;
+}
+
+cudaError_t launch_static_project(int device, const ModelDev& md, const QMat& W, const float* in, int M, float* out,
+                                  cudaStream_t st, int* wait_failed) {
+  uint8_t* base = g_static_address[device];
+  int8_t* act = reinterpret_cast<int8_t*>(base);
+  float* act_scale = reinterpret_cast<float*>(base + STATIC_ACT_BYTES);
+  int* flag = reinterpret_cast<int*>(base + STATIC_ACT_BYTES + STATIC_SCALE_BYTES);
+  cudaError_t e = cudaMemsetAsync(flag, 0, sizeof(int), st);
+  if (e != cudaSuccess) return e;
+  const int K = GEMM_K, tiles = (W.rows + GEMM_ROWS - 1) / GEMM_ROWS;
+  k_prep<<<M, 128, 0, st>>>(in, K, nullptr, nullptr, 0, K, act, act_scale, M, nullptr, md.inv_sqrt_group, 0);
+  if (M <= 16)
+    k_gemm<16><<<dim3(tiles, 1), 8 * 16, gemm_smem<16>(), st>>>(W, act, act_scale, out, M, (int)W.rows, nullptr, flag);
+  else
+    k_gemm<32><<<dim3(tiles, (M + 31) / 32), 8 * 32, gemm_smem<32>(), st>>>(W, act, act_scale, out, M, (int)W.rows, nullptr, flag);
+  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  *wait_failed = 0;
+  if ((e = cudaMemcpyAsync(wait_failed, flag, sizeof(int), cudaMemcpyDeviceToHost, st)) != cudaSuccess) return e;
+  return cudaStreamSynchronize(st);
 }
 
 }  // namespace nbk

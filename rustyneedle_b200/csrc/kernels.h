@@ -31,4 +31,16 @@ void launch_debug_math(int op, const float* in, float* out, int n, cudaStream_t 
 void launch_debug_project(const nbl::ModelDev& md, const nbl::QMat& W, const float* in, int K, int M, int8_t* act,
                           float* act_scale, float* out, int out_stride, cudaStream_t st);
 
+// The allocation-free product: tokens per call the file-scope scratch holds.
+constexpr int STATIC_MAX_TOKENS = 256;
+// Looks up this device's copy of the scratch once (cudaGetSymbolAddress with
+// the device current; it may load the module, so it belongs before any stream
+// capture). Later calls return at once.
+cudaError_t static_scratch_setup(int device);
+// k_prep + the tensor-core product of M ≤ STATIC_MAX_TOKENS inputs (K = 512,
+// 16-byte aligned) into out [M][W.rows]; synchronises `st` and reports in
+// *wait_failed whether a bounded wait of the product gave up.
+cudaError_t launch_static_project(int device, const nbl::ModelDev& md, const nbl::QMat& W, const float* in, int M, float* out,
+                                  cudaStream_t st, int* wait_failed);
+
 }  // namespace nbk

@@ -1133,6 +1133,30 @@ nb_status nb_session_step(nb_session* session, const uint32_t* mask_bits, uint32
   return s;
 }
 
+// Allocates nothing on the device (its scratch is the file-scope array of
+// kernels.cu) and, on success, nothing on the host either; see the header
+// for the callers it serves.
+nb_status nb_model_project_static(nb_model* model, int which, uint32_t layer, const float* in_device, uint32_t count,
+                                  float* out_device, void* stream) {
+  if (!model || !in_device || !out_device || count == 0 || which < 0 || which > 2) return NB_ERR_ARGUMENT;
+  return guard([&] {
+    Engine& E = *model->engine;
+    if (which < 2 && layer >= E.layers.size()) fail(NB_ERR_ARGUMENT, "no such layer");
+    if (count > (uint32_t)nbk::STATIC_MAX_TOKENS)
+      fail(NB_ERR_ARGUMENT, "count " + std::to_string(count) + " is above the " + std::to_string(nbk::STATIC_MAX_TOKENS) +
+                                " tokens the static scratch holds");
+    if (reinterpret_cast<uintptr_t>(in_device) % 16 || reinterpret_cast<uintptr_t>(out_device) % 4)
+      fail(NB_ERR_ARGUMENT, "in_device must be 16-byte and out_device 4-byte aligned");
+    const QMat& W = which == 0 ? E.layers[layer].qkvg : which == 1 ? E.layers[layer].out : E.md.logits;
+    NB_CUDA(cudaSetDevice(E.device));
+    NB_CUDA(nbk::static_scratch_setup(E.device));
+    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : E.stream;
+    int wait_failed = 0;
+    NB_CUDA(nbk::launch_static_project(E.device, E.md, W, in_device, (int)count, out_device, st, &wait_failed));
+    if (wait_failed) fail(NB_ERR_TIMEOUT, "a bounded wait of the tensor-core product gave up");
+  });
+}
+
 nb_status nb_build_expf_table(const char* path) {
   if (!path) return NB_ERR_ARGUMENT;
   return guard([&] {
