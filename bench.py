@@ -62,9 +62,9 @@ def parse():
 
 
 def prompts(rank: int, count: int):
-    rng = np.random.default_rng(1000 + rank)
-    lengths = rng.integers(PROMPT_RANGE[0], PROMPT_RANGE[1] + 1, count)
-    return [rng.integers(10, 8000, n).astype(np.uint32) for n in lengths]
+    from rustyneedle_b200 import dp
+
+    return dp.shard_prompts(rank, count, PROMPT_RANGE[0], PROMPT_RANGE[1])
 
 
 def measured_peaks():
@@ -192,27 +192,18 @@ def main():
     args = parse()
     if args.impl == "reference":
         return run_reference(args)
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    dist = None
-    if world > 1:
-        import torch
-        import torch.distributed as dist_mod
-        from datetime import timedelta
-
-        torch.cuda.set_device(local)
-        dist_mod.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=torch.device("cuda", local))
-        dist = dist_mod
-
     import rustyneedle_b200 as nb
-    from rustyneedle_b200 import debug, synthetic
+    from rustyneedle_b200 import debug, dp, synthetic
+
+    ranks = dp.ranks_from_env()
+    rank, world, local = ranks.rank, ranks.world, ranks.local
+    dist = dp.init_group(ranks, "nccl")
 
     archive = synthetic.cached_archive(seed=0)
     seqs = 64 if args.profile else args.seqs
     rank_prompts = prompts(rank, seqs)
     # KV pool sized to the run: every sequence's prompt plus the decode steps, plus the batch-1 session
-    pages = sum(-(-(len(p) + 2 * args.steps + 2 * args.warmup + 8) // 64) for p in rank_prompts) * DEPTH + 40 * DEPTH
+    pages = dp.kv_pages_for(rank_prompts, 2 * args.steps + 2 * args.warmup + 8, DEPTH)
     model = nb.Model.open(archive, device=local, max_sessions=seqs + 2, kv_pages=pages)
     if DEPTH != model.config.num_layers:
         model = model.with_depth(DEPTH)
@@ -229,17 +220,10 @@ def main():
     batch = nb.Batch(model, sessions)
 
     def barrier():
-        if dist:
-            dist.barrier()
+        dp.barrier(dist)
 
     def max_over_ranks(x: float) -> float:
-        if not dist:
-            return x
-        import torch
-
-        t = torch.tensor([x], dtype=torch.float64, device=f"cuda:{local}")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+        return dp.max_over_ranks(dist, x, f"cuda:{local}")
 
     batch.run(args.warmup)
     barrier()
@@ -267,7 +251,8 @@ def main():
     try:
         with open(os.path.join(ROOT, "profiles", "k_attend_traffic.json")) as f:
             t = json.load(f)
-            traffic = t["dram_bytes_per_position"] * (att_bytes / t["algorithmic_bytes_per_position"])
+            # the captured launch's DRAM bytes per algorithmic byte, scaled to this launch
+            traffic = round(t["dram_bytes"] / t["algorithmic_bytes"] * att_bytes)
     except (OSError, KeyError, ZeroDivisionError):
         traffic = None
     roofline = {"kernel": "k_attend (paged int8 attention, one launch = one layer of the batch)", "bound": "hbm",
@@ -296,9 +281,7 @@ def main():
     if rank == 0:
         print(json.dumps(line), flush=True)
     batch.close()
-    if dist:
-        dist.barrier()
-        dist.destroy_process_group()
+    dp.close_group(dist)
 
 
 def batch1(nb, model):
