@@ -25,6 +25,17 @@ __device__ __forceinline__ float fdiv(float a, float b) { return __fdiv_rn(a, b)
 __device__ __forceinline__ float frcp(float a) { return __frcp_rn(a); }
 __device__ __forceinline__ float fsqrt(float a) { return __fsqrt_rn(a); }
 
+// Programmatic dependent launch. Every kernel of the token loop is launched
+// with programmatic stream serialisation: it may start while its predecessor
+// on the stream still runs. pdl_trigger() (first thing in every CTA) lets the
+// successor start once all of this grid's CTAs are resident; pdl_wait()
+// blocks until the predecessor grid has completed and its writes are
+// visible. Before pdl_wait() a kernel only reads the model's constant weights
+// and writes nothing to global memory; every CTA passes pdl_wait() before it
+// exits, so completion stays transitive along the stream.
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // Rust's float Iterator::sum starts from -0.0.
 constexpr float SUM_START = -0.0f;
 
@@ -108,8 +119,21 @@ __device__ __forceinline__ float sum_of_squares_warp(const float* v, int n) {
   int lane = threadIdx.x & 31;
   int whole = n / 8 * 8;
   float acc = 0.0f;
-  if (lane < 8)
-    for (int i = lane; i < whole; i += 8) acc = fadd(acc, fmul(v[i], v[i]));
+  if (lane < 8) {
+    int i = lane;
+    // sixteen loads in flight per batch; the running sum itself stays one ordered chain
+    for (; i + 8 * 15 < whole; i += 8 * 16) {
+      float sq[16];
+#pragma unroll
+      for (int k = 0; k < 16; ++k) {
+        const float x = v[i + 8 * k];
+        sq[k] = fmul(x, x);
+      }
+#pragma unroll
+      for (int k = 0; k < 16; ++k) acc = fadd(acc, sq[k]);
+    }
+    for (; i < whole; i += 8) acc = fadd(acc, fmul(v[i], v[i]));
+  }
   float s = SUM_START;
 #pragma unroll
   for (int l = 0; l < 8; ++l) s = fadd(s, __shfl_sync(FULL, acc, l));

@@ -18,7 +18,9 @@
 // logits product and k_select (generator.rs:147-194).
 #include <cuda_runtime.h>
 
+#include <cstdlib>
 #include <mutex>
+#include <utility>
 
 #include "device.cuh"
 #include "kernels.h"
@@ -58,6 +60,7 @@ __device__ __forceinline__ uint8_t* page_base(const KvDev& kv, const PageGeometr
 // QuantisedMatrix::dequantise_row (matrix.rs:140-153) times sqrt(d), copied
 // into every lane (session.rs:84-90). grid M, block 128.
 __global__ void __launch_bounds__(128) k_embed(ModelDev md, Work w, int M) {
+  pdl_wait();
   int t = blockIdx.x;
   if (t >= M || w.meta[t].slot < 0) return;
   uint32_t token = w.tokens[t];
@@ -91,7 +94,6 @@ __device__ __forceinline__ void phi_row(const ModelDev& md, int r, int layer, co
 __global__ void __launch_bounds__(256) k_route(ModelDev md, LayerDev L, Work w, int M, int layer, int slot) {
   extern __shared__ float sm[];
   int t = blockIdx.x;
-  if (t >= M || w.meta[t].slot < 0) return;
   const int d = md.d_model, n = LANES * d, ng = n / GROUP;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   float* s_stream = sm;                                     // n
@@ -105,11 +107,17 @@ __global__ void __launch_bounds__(256) k_route(ModelDev md, LayerDev L, Work w, 
   __shared__ float s_gate[LANES];
   __shared__ float s_inv;
 
-  stage_async(s_stream, w.stream + (size_t)t * n, n);
+  // the layer's constant weights first, then (once the previous kernel is done) the token's stream
   stage_async(s_norms, md.phi_pre.scales + (size_t)layer * LANES * ng, LANES * ng);
   stage_async(s_norms + LANES * ng, md.phi_post.scales + (size_t)layer * LANES * ng, LANES * ng);
   stage_async(s_norms + 2 * LANES * ng, md.phi_res.scales + (size_t)layer * LANES * LANES * ng, LANES * LANES * ng);
   stage_async(s_gain, L.norm_in, d);
+  pdl_wait();
+  if (t >= M || w.meta[t].slot < 0) {
+    cp_async_wait_all();
+    return;
+  }
+  stage_async(s_stream, w.stream + (size_t)t * n, n);
   cp_async_wait_all();
   __syncthreads();
   // unit_rms over all lanes (ops.rs:60-66), then fake_quantise_int8 (ops.rs:120-125)
@@ -139,10 +147,10 @@ __global__ void __launch_bounds__(256) k_route(ModelDev md, LayerDev L, Work w, 
   __syncthreads();
   // phi products: 4 pre rows, 4 post rows, 16 residual rows of this layer
   // (lanes.rs:156-163). Thread (group g, row r) forms the exact int32 sum of
-  // one 128-column group (two pairs per thread, loads issued together); one
-  // thread per row then combines the groups in order with the 4-bit row chain
-  // (neon.rs:164-183).
-  int* s_acc = reinterpret_cast<int*>(s_work);  // [ng][PHI_ROWS]; s_work is free again
+  // one 128-column group (two pairs per thread, loads issued together) and its
+  // scaled term acc·norm·level_scale·act_scale; one thread per row then adds
+  // the terms in group order, the 4-bit row chain (neon.rs:164-183).
+  float* s_term = s_work;  // [ng][PHI_ROWS]; s_work is free again
   {
     const int pairs = PHI_ROWS * ng;
     uint4 wr[2][8];
@@ -174,19 +182,20 @@ __global__ void __launch_bounds__(256) k_route(ModelDev md, LayerDev L, Work w, 
           acc[2] = dp4a(wr[u][k].z, a.z, acc[2]);
           acc[3] = dp4a(wr[u][k].w, a.w, acc[3]);
         }
-        s_acc[pair] = (acc[0] + acc[1]) + (acc[2] + acc[3]);
+        const int r = pair % PHI_ROWS;
+        const QMat* P;
+        int row;
+        phi_row(md, r, layer, P, row);
+        const float sum = (float)((acc[0] + acc[1]) + (acc[2] + acc[3]));
+        s_term[pair] = fmul(fmul(fmul(sum, s_norms[r * ng + g]), P->level_scale), s_ascale[g]);
       }
     }
   }
   __syncthreads();
   if (tid < PHI_ROWS) {
-    const QMat* P;
-    int row;
-    phi_row(md, tid, layer, P, row);
-    const float lscale = P->level_scale;
     float total = 0.0f;
-    for (int g = 0; g < ng; ++g)
-      total = fadd(total, fmul(fmul(fmul((float)s_acc[g * PHI_ROWS + tid], s_norms[tid * ng + g]), lscale), s_ascale[g]));
+#pragma unroll 16
+    for (int g = 0; g < ng; ++g) total = fadd(total, s_term[g * PHI_ROWS + tid]);
     s_phi[tid] = total;
   }
   __syncthreads();
@@ -264,6 +273,7 @@ __global__ void __launch_bounds__(256) k_route(ModelDev md, LayerDev L, Work w, 
   peak = s_red[0];
   for (int i = 1; i < 7; ++i) peak = fmaxf(peak, s_red[i]);
   scale = int8_scale_of(peak);
+  pdl_trigger();  // the tail of the kernel overlaps the next one's prologue
   const int dg = d / GROUP;
   for (int g = warp; g < dg; g += 7) {
     float v[4];
@@ -345,12 +355,35 @@ __global__ void __launch_bounds__(8 * NT) k_gemm(QMat W, const int8_t* __restric
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s_tmem)), "r"(COLS) : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
+  constexpr uint32_t PIECE = 16384;
   if (tid == 0) {
     s_fail = 0;
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar_load), "r"(1) : "memory");
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar_mma), "r"(1) : "memory");
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    // the weight tile is constant: its copy starts before the previous kernel has finished
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar_load), "r"(A_BYTES + B_BYTES) : "memory");
+    const uint8_t* ga = reinterpret_cast<const uint8_t*>(W.codes) + (size_t)tile * A_BYTES;
+    for (uint32_t off = 0; off < A_BYTES; off += PIECE)
+      asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(sA + off)),
+                   "l"(ga + off), "r"(min(PIECE, A_BYTES - off)), "r"(bar_load)
+                   : "memory");
+  }
+  // this thread's output row and its per-group weight scales (constant)
+  const int quad = warp & 3, slice = warp >> 2;
+  const int row = tile * GEMM_ROWS + quad * 32 + lane;
+  const bool valid = row < (int)W.rows;
+  float ws[GK];
+#pragma unroll
+  for (int g = 0; g < GK; ++g) ws[g] = valid ? W.scales[(size_t)row * GK + g] : 0.0f;
+  pdl_wait();
+  if (tid == 0) {
+    const uint8_t* gb = reinterpret_cast<const uint8_t*>(act) + (size_t)(m0 / 8) * (8 * GEMM_K);
+    for (uint32_t off = 0; off < B_BYTES; off += PIECE)
+      asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(sB + off)),
+                   "l"(gb + off), "r"(min(PIECE, B_BYTES - off)), "r"(bar_load)
+                   : "memory");
   }
   for (int i = tid; i < NT * GK; i += blockDim.x) s_as[i] = i / GK < mcount ? act_scale[(size_t)m0 * GK + i] : 0.0f;
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -358,20 +391,6 @@ __global__ void __launch_bounds__(8 * NT) k_gemm(QMat W, const int8_t* __restric
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem = s_tmem;
 
-  if (tid == 0) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar_load), "r"(A_BYTES + B_BYTES) : "memory");
-    const uint8_t* ga = reinterpret_cast<const uint8_t*>(W.codes) + (size_t)tile * A_BYTES;
-    const uint8_t* gb = reinterpret_cast<const uint8_t*>(act) + (size_t)(m0 / 8) * (8 * GEMM_K);
-    constexpr uint32_t PIECE = 16384;
-    for (uint32_t off = 0; off < A_BYTES; off += PIECE)
-      asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(sA + off)),
-                   "l"(ga + off), "r"(min(PIECE, A_BYTES - off)), "r"(bar_load)
-                   : "memory");
-    for (uint32_t off = 0; off < B_BYTES; off += PIECE)
-      asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(sB + off)),
-                   "l"(gb + off), "r"(min(PIECE, B_BYTES - off)), "r"(bar_load)
-                   : "memory");
-  }
   bool ok = mbar_wait(bar_load, 0);
   if (ok && warp == 0) {
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
@@ -398,15 +417,10 @@ __global__ void __launch_bounds__(8 * NT) k_gemm(QMat W, const int8_t* __restric
   }
   if (ok) ok = mbar_wait(bar_mma, 0);
   if (!ok) s_fail = 1;
+  pdl_trigger();  // the epilogue overlaps the next kernel's prologue
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   __syncthreads();
   if (!s_fail) {
-    const int quad = warp & 3, slice = warp >> 2;
-    const int row = tile * GEMM_ROWS + quad * 32 + lane;
-    const bool valid = row < (int)W.rows;
-    float ws[GK];
-#pragma unroll
-    for (int g = 0; g < GK; ++g) ws[g] = valid ? W.scales[(size_t)row * GK + g] : 0.0f;
     const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16);
     {
       const int c0 = slice * 16;
@@ -440,6 +454,75 @@ __global__ void __launch_bounds__(8 * NT) k_gemm(QMat W, const int8_t* __restric
   if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(COLS) : "memory");
 }
 
+// -------------------------------------------------------------------- gemv
+// The same product for a few tokens (decode at small batch) as a memory-bound
+// int8 GEMV on the CUDA cores. A warp owns one 8-row block of the
+// core-matrix layout (4 KB contiguous: eight coalesced 16-byte loads per
+// lane). Lane l serves row l%8 and the 16-byte chunks c = 4j + l/8, so the
+// exact int32 sum of each 128-column group (chunks 8g..8g+7) is two dp4a
+// chains per lane, reduced over the row's four lanes. Every token's
+// activations sit in shared memory; the output is the ordered per-group
+// combine of k_gemm's epilogue.
+constexpr int GEMV_WARPS = 2;
+constexpr int GEMV_MAX_TOKENS = 8;
+
+__global__ void __launch_bounds__(GEMV_WARPS * 32) k_gemv(QMat W, const int8_t* __restrict__ act, const float* __restrict__ act_scale,
+                                                        float* __restrict__ out, int M, int out_stride,
+                                                        const TokenMeta* __restrict__ meta) {
+  constexpr int GK = GEMM_K / GROUP;
+  __shared__ __align__(16) uint8_t s_act[GEMV_MAX_TOKENS][GEMM_K];
+  __shared__ float s_as[GEMV_MAX_TOKENS][GK];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int block = blockIdx.x * GEMV_WARPS + warp;
+  const int row = block * 8 + (lane & 7), q = lane >> 3;
+  const bool live = block * 8 < (int)W.rows;  // storage rows are padded to 128, so a live block is whole
+  uint4 wv[8];
+  float ws[GK];
+  if (live) {
+    const uint4* src = reinterpret_cast<const uint4*>(W.codes + (size_t)block * 8 * GEMM_K);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) wv[j] = src[j * 32 + lane];
+  }
+#pragma unroll
+  for (int g = 0; g < GK; ++g) ws[g] = row < (int)W.rows ? W.scales[(size_t)row * GK + g] : 0.0f;
+  pdl_wait();
+  for (int i = threadIdx.x; i < M * GEMM_KC; i += blockDim.x) {
+    const int t = i / GEMM_KC, c = i % GEMM_KC;
+    *reinterpret_cast<uint4*>(&s_act[t][c * 16]) = *reinterpret_cast<const uint4*>(act + core_offset(t, c * 16, GEMM_KC));
+  }
+  for (int i = threadIdx.x; i < M * GK; i += blockDim.x) s_as[i / GK][i % GK] = act_scale[i];
+  __syncthreads();
+  if (!live) return;
+  for (int t = 0; t < M; ++t) {
+    int acc[GK];
+#pragma unroll
+    for (int g = 0; g < GK; ++g) acc[g] = 0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const uint4 a = *reinterpret_cast<const uint4*>(&s_act[t][(4 * j + q) * 16]);
+      const int g = j >> 1;
+      acc[g] = dp4a(wv[j].x, a.x, acc[g]);
+      acc[g] = dp4a(wv[j].y, a.y, acc[g]);
+      acc[g] = dp4a(wv[j].z, a.z, acc[g]);
+      acc[g] = dp4a(wv[j].w, a.w, acc[g]);
+    }
+#pragma unroll
+    for (int g = 0; g < GK; ++g) {
+      acc[g] += __shfl_xor_sync(FULL, acc[g], 8);
+      acc[g] += __shfl_xor_sync(FULL, acc[g], 16);
+    }
+    if (q == 0 && row < (int)W.rows && !(meta && meta[t].slot < 0)) {
+      float total = 0.0f;
+#pragma unroll
+      for (int g = 0; g < GK; ++g) {
+        const float a = (float)acc[g], as = s_as[t][g];
+        total = W.fused ? __fmaf_rn(a, fmul(ws[g], as), total) : fadd(total, fmul(fmul(fmul(a, ws[g]), W.level_scale), as));
+      }
+      out[(size_t)t * out_stride + row] = total;
+    }
+  }
+}
+
 template <int NT>
 constexpr size_t gemm_smem() {
   return (size_t)GEMM_ROWS * GEMM_K + (size_t)NT * GEMM_K;
@@ -449,6 +532,7 @@ constexpr size_t gemm_smem() {
 // grid M, block 32·(heads + 2·kv_heads). One warp per q, k or v head; lane l
 // holds elements l and l+32, the two halves rotary pairs (ops.rs:131-141).
 __global__ void k_heads(ModelDev md, LayerDev L, Work w, KvDev kv, int M, int layer) {
+  pdl_wait();
   int t = blockIdx.x;
   if (t >= M) return;
   const TokenMeta meta = w.meta[t];
@@ -533,9 +617,10 @@ __host__ __device__ constexpr int att_wstride(int t_cap) { return t_cap / 4 + 2;
 
 template <int G>
 __global__ void __launch_bounds__(ATT_THREADS_ALL, 3) k_attend(ModelDev md, Work w, KvDev kv, int M, int layer, int global, int t_cap) {
+  pdl_wait();
   extern __shared__ float sm[];
-  const int t = blockIdx.x, kvh = blockIdx.y;
-  if (t >= M) return;
+  if ((int)blockIdx.x >= M) return;
+  const int t = w.order ? w.order[blockIdx.x] : (int)blockIdx.x, kvh = blockIdx.y;
   const TokenMeta meta = w.meta[t];
   if (meta.slot < 0) return;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -657,8 +742,19 @@ __global__ void __launch_bounds__(ATT_THREADS_ALL, 3) k_attend(ModelDev md, Work
     const int h = lane >> 2, j = lane & 3;
     const int vc = count - count % 4;
     float acc = 0.0f;
-    if (h < G)
-      for (int i = j; i < vc; i += 4) acc = fadd(acc, s_e[h * t_cap + i]);
+    if (h < G) {
+      const float* e = s_e + h * t_cap;
+      int i = j;
+      // sixteen loads in flight per batch; the running sum stays one ordered chain per lane
+      for (; i + 4 * 15 < vc; i += 4 * 16) {
+        float v[16];
+#pragma unroll
+        for (int k = 0; k < 16; ++k) v[k] = e[i + 4 * k];
+#pragma unroll
+        for (int k = 0; k < 16; ++k) acc = fadd(acc, v[k]);
+      }
+      for (; i < vc; i += 4) acc = fadd(acc, e[i]);
+    }
     float l0 = __shfl_sync(FULL, acc, (lane & ~3) + 0), l1 = __shfl_sync(FULL, acc, (lane & ~3) + 1);
     float l2 = __shfl_sync(FULL, acc, (lane & ~3) + 2), l3 = __shfl_sync(FULL, acc, (lane & ~3) + 3);
     if (h < G && j == 0) {
@@ -735,6 +831,7 @@ __global__ void __launch_bounds__(ATT_THREADS_ALL, 3) k_attend(ModelDev md, Work
       for (int k = 0; k < 4; ++k) s_pv[(slice * G + h) * HEAD_DIM + dq * 4 + k] = (hi_acc[h][k] << 6) + lo_acc[h][k];
   }
   __syncthreads();
+  pdl_trigger();  // the output rows overlap the next kernel's prologue
   if (tid < G * HEAD_DIM) {
     const int h = tid / HEAD_DIM, dim = tid % HEAD_DIM;
     int sum = 0;
@@ -755,6 +852,7 @@ __global__ void __launch_bounds__(128) k_prep(const float* __restrict__ in, int 
                                               const float* __restrict__ gate, int gate_stride, int K, int8_t* __restrict__ act,
                                               float* __restrict__ act_scale, int M, const TokenMeta* __restrict__ meta,
                                               float inv_sqrt_group, int fake) {
+  pdl_wait();
   __shared__ __align__(16) float s_v[MAX_D];
   __shared__ float s_red[4];
   const int t = blockIdx.x;
@@ -824,38 +922,36 @@ __device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
 
 template <int S, int R, bool FUSED32>
 __device__ __forceinline__ void tn_stage(const float* __restrict__ A, const float* __restrict__ B, float* __restrict__ C) {
-  // Two adjacent output columns share one packed f32x2 instruction.
+  // A thread owns a 4-row × 2-column tile: per step one float4 of A, one
+  // float2 of B, and the two columns of a row share one packed f32x2 product.
+  constexpr int TILES = (R / 4) * (HADA_RIGHT / 2);
   const int tid = threadIdx.x;
-  if (tid < R * 2) {
-    const int r0 = (tid >> 3) * 4, c0 = (tid & 7) * 4;
-    float2 acc[4][2];
+  if (tid < TILES) {
+    const int r0 = (tid / (HADA_RIGHT / 2)) * 4, c0 = (tid % (HADA_RIGHT / 2)) * 2;
+    float2 acc[4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) acc[i][0] = acc[i][1] = make_float2(0.0f, 0.0f);
+    for (int i = 0; i < 4; ++i) acc[i] = make_float2(0.0f, 0.0f);
 #pragma unroll 8
     for (int s = 0; s < S; ++s) {
       const float4 a = *reinterpret_cast<const float4*>(A + s * R + r0);
-      const float4 b = *reinterpret_cast<const float4*>(B + s * HADA_RIGHT + c0);
+      const float2 b = *reinterpret_cast<const float2*>(B + s * HADA_RIGHT + c0);
       const float av[4] = {a.x, a.y, a.z, a.w};
-      const float2 b01 = make_float2(b.x, b.y), b23 = make_float2(b.z, b.w);
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         const float2 ai = make_float2(av[i], av[i]);
         if (FUSED32) {
-          acc[i][0] = fma2(ai, b01, acc[i][0]);
-          acc[i][1] = fma2(ai, b23, acc[i][1]);
+          acc[i] = fma2(ai, b, acc[i]);
         } else {
           // packed products, scalar sums: a packed multiply feeding a packed
           // add is contracted to a packed fma by the backend even under
           // -fmad=false, which the reference never does here
-          const float2 p01 = mul2(ai, b01), p23 = mul2(ai, b23);
-          acc[i][0] = make_float2(fadd(acc[i][0].x, p01.x), fadd(acc[i][0].y, p01.y));
-          acc[i][1] = make_float2(fadd(acc[i][1].x, p23.x), fadd(acc[i][1].y, p23.y));
+          const float2 p = mul2(ai, b);
+          acc[i] = make_float2(fadd(acc[i].x, p.x), fadd(acc[i].y, p.y));
         }
       }
     }
 #pragma unroll
-    for (int i = 0; i < 4; ++i)
-      *reinterpret_cast<float4*>(C + (r0 + i) * HADA_RIGHT + c0) = make_float4(acc[i][0].x, acc[i][0].y, acc[i][1].x, acc[i][1].y);
+    for (int i = 0; i < 4; ++i) *reinterpret_cast<float2*>(C + (r0 + i) * HADA_RIGHT + c0) = acc[i];
   }
   __syncthreads();
 }
@@ -866,7 +962,7 @@ __device__ __forceinline__ void kronecker(float* xt, float* tmp, const float* le
   tn_stage<LEFT, LEFT, FUSED32>(left, tmp, out);
 }
 
-constexpr int BLOCK_THREADS = 128;
+constexpr int BLOCK_THREADS = 256;
 
 // The stage-A operand position of element e of a LEFT×32 matrix.
 template <int LEFT>
@@ -879,18 +975,31 @@ __device__ __forceinline__ int transposed(int e) { return (e % HADA_RIGHT) * LEF
 // already be staged in s_condv, s_left and s_right.
 template <int LEFT>
 __device__ __forceinline__ void hadamard_core(const ModelDev& md, const HadamardDev& Hd, const int d, const float* s_pre, float* buf0,
-                                              float* buf1, float* s_mod, float* s_left, float* s_right, const float* s_condv) {
+                                              float* buf1, float* s_mod, float* s_left, float* s_right, float* s_condv) {
   constexpr int N = LEFT * HADA_RIGHT;
   constexpr int PER = N / (4 * BLOCK_THREADS);
   constexpr bool FUSED32 = LEFT == 32;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   __shared__ float s_w[COND_RANK], s_chain[4][COND_RANK];
-  // condition weights: four chains of rank-8 partial sums (hadamard.rs:263-276)
+  // condition weights: four chains of rank-8 partial sums (hadamard.rs:263-276).
+  // Chain (j, r) adds x[4g+j]·cond_v[4g+j][r] over g in order; the products
+  // are formed in place by the whole block (element 32g + 8j + r of cond_v
+  // meets x[4g + j]), then lane 8j + r of warp 0 runs the ordered sum.
+  for (int i = tid; i < d * COND_RANK; i += BLOCK_THREADS) s_condv[i] = fmul(s_pre[i >> 3], s_condv[i]);
+  __syncthreads();
   if (warp == 0) {
     int j = lane / COND_RANK, rr = lane % COND_RANK;
     float acc = 0.0f;
-#pragma unroll 8
-    for (int g = 0; g < d / 4; ++g) acc = fadd(acc, fmul(s_pre[4 * g + j], s_condv[(4 * g + j) * COND_RANK + rr]));
+    const int G = d / 4;
+    int g = 0;
+    for (; g + 15 < G; g += 16) {
+      float p[16];
+#pragma unroll
+      for (int k = 0; k < 16; ++k) p[k] = s_condv[32 * (g + k) + lane];
+#pragma unroll
+      for (int k = 0; k < 16; ++k) acc = fadd(acc, p[k]);
+    }
+    for (; g < G; ++g) acc = fadd(acc, s_condv[32 * g + lane]);
     s_chain[j][rr] = acc;
     __syncwarp();
     if (lane == 0) {
@@ -973,10 +1082,7 @@ template <int LEFT>
 __global__ void __launch_bounds__(BLOCK_THREADS) k_block(ModelDev md, LayerDev L, Work w, int M) {
   extern __shared__ float sm[];
   constexpr int N = LEFT * HADA_RIGHT;
-  constexpr int PER = N / (4 * BLOCK_THREADS);  // float4 chunks per thread
-  constexpr bool FUSED32 = LEFT == 32;
   const int t = blockIdx.x;
-  if (t >= M || w.meta[t].slot < 0) return;
   const int d = md.d_model, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   float* s_a = sm;                        // d: attention output, then the running block value
   float* s_x = sm + MAX_D;                // d: the routing input
@@ -992,12 +1098,18 @@ __global__ void __launch_bounds__(BLOCK_THREADS) k_block(ModelDev md, LayerDev L
   __shared__ float s_inv, s_gate;
   const HadamardDev& Hd = L.hada;
 
-  stage_async(s_a, w.outp + (size_t)t * d, d);
-  stage_async(s_x, w.x + (size_t)t * d, d);
+  // the layer's constant weights first, then (once the previous kernel is done) the token's rows
   stage_async(s_condv, Hd.cond_v, d * COND_RANK);
   stage_async(s_left, Hd.left[0], LEFT * LEFT);
   stage_async(s_right, Hd.right[0], HADA_RIGHT * HADA_RIGHT);
   if (tid == 0) s_gate = sigmoid(L.attn_gate);
+  pdl_wait();
+  if (t >= M || w.meta[t].slot < 0) {
+    cp_async_wait_all();
+    return;
+  }
+  stage_async(s_a, w.outp + (size_t)t * d, d);
+  stage_async(s_x, w.x + (size_t)t * d, d);
   cp_async_wait_all();
   __syncthreads();
   if (warp == 0) {
@@ -1018,6 +1130,7 @@ __global__ void __launch_bounds__(BLOCK_THREADS) k_block(ModelDev md, LayerDev L
   for (int i = tid; i < d; i += BLOCK_THREADS) s_pre[i] = fmul(fmul(fadd(1.0f, L.pre_hada[i]), s_a[i]), s_inv);
   __syncthreads();
   hadamard_core<LEFT>(md, Hd, d, s_pre, buf0, buf1, s_mod, s_left, s_right, s_condv);
+  pdl_trigger();  // the lane combine overlaps the next kernel's prologue
   // x += mlp; delta = x - input; next lanes (lanes.rs:183-204)
   const float* route = w.route + (size_t)t * (LANES + LANES * LANES);
   float rw[LANES + LANES * LANES];
@@ -1056,6 +1169,7 @@ __global__ void __launch_bounds__(BLOCK_THREADS) k_block(ModelDev md, LayerDev L
 // lane_mean (session.rs:192-200) and the final zero-centred norm into the
 // sequence's hidden state, for the last token of each sequence. grid M, block 128.
 __global__ void __launch_bounds__(128) k_final(ModelDev md, Work w, float* __restrict__ hidden, int M) {
+  pdl_wait();
   __shared__ __align__(16) float s_mean[MAX_D];
   __shared__ float s_inv;
   const int t = blockIdx.x;
@@ -1096,6 +1210,7 @@ constexpr int SELECT_CHUNKS = 8;
 __global__ void __launch_bounds__(256) k_select(const float* __restrict__ logits, int V, const uint32_t* __restrict__ mask,
                                                 const int32_t* __restrict__ active, uint32_t* __restrict__ next,
                                                 float* __restrict__ peaks) {
+  pdl_wait();
   __shared__ float s_red[8];
   __shared__ int s_idx[8];
   __shared__ int s_any[8];
@@ -1166,6 +1281,7 @@ __global__ void __launch_bounds__(256) k_select(const float* __restrict__ logits
 __global__ void __launch_bounds__(256) k_stats(const float* __restrict__ logits, int V, const uint32_t* __restrict__ mask,
                                                const int32_t* __restrict__ active, const uint32_t* __restrict__ next,
                                                const float* __restrict__ peaks, float* __restrict__ stats, int stats_stride) {
+  pdl_wait();
   extern __shared__ float sm[];
   const int b = blockIdx.x, tid = threadIdx.x;
   if (active && active[b] == 0) return;
@@ -1196,6 +1312,7 @@ __global__ void __launch_bounds__(256) k_stats(const float* __restrict__ logits,
 
 // After a decode pass: the chosen token becomes the next input at the next position.
 __global__ void k_advance(TokenMeta* meta, int B) {
+  pdl_wait();
   int b = blockIdx.x * blockDim.x + threadIdx.x;
   if (b >= B || meta[b].slot < 0) return;
   meta[b].position += 1;
@@ -1241,68 +1358,115 @@ static int* g_gemm_error = nullptr;
 
 void set_error_flag(int* flag) { g_gemm_error = flag; }
 
+// Passes over at most this many tokens launch their kernels with
+// programmatic stream serialisation: each kernel's prologue (constant weight
+// loads, tensor-memory allocation) overlaps the tail of its predecessor; see
+// pdl_wait in device.cuh. Larger passes fill the SMs by themselves, and the
+// early-resident successor CTAs only take room from the running kernel, so
+// they launch plainly. $NEEDLE_B200_PDL=0 turns the overlap off.
+constexpr int PDL_MAX_TOKENS = 32;
+static thread_local int t_pass_tokens = 0;
+
+static bool pdl_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("NEEDLE_B200_PDL");
+    return !(e && e[0] == '0');
+  }();
+  return on && t_pass_tokens <= PDL_MAX_TOKENS;
+}
+
+template <typename... P, typename... A>
+static void launch(void (*kernel)(P...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, A&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaLaunchKernelEx(&cfg, kernel, std::forward<A>(args)...);
+}
+
 static void project(const QMat& W, const int8_t* act, const float* act_scale, float* out, int M, int out_stride,
                     const TokenMeta* meta, cudaStream_t st) {
   const int tiles = (W.rows + GEMM_ROWS - 1) / GEMM_ROWS;
-  if (M <= 16)
-    k_gemm<16><<<dim3(tiles, 1), 8 * 16, gemm_smem<16>(), st>>>(W, act, act_scale, out, M, out_stride, meta, g_gemm_error);
+  if (M <= GEMV_MAX_TOKENS) {
+    const int blocks = (W.rows + 7) / 8;
+    launch(k_gemv, (blocks + GEMV_WARPS - 1) / GEMV_WARPS, GEMV_WARPS * 32, 0, st, W, act, act_scale, out, M, out_stride, meta);
+  } else if (M <= 16)
+    launch(k_gemm<16>, dim3(tiles, 1), 8 * 16, gemm_smem<16>(), st, W, act, act_scale, out, M, out_stride, meta, g_gemm_error);
   else
-    k_gemm<32><<<dim3(tiles, (M + 31) / 32), 8 * 32, gemm_smem<32>(), st>>>(W, act, act_scale, out, M, out_stride, meta, g_gemm_error);
+    launch(k_gemm<32>, dim3(tiles, (M + 31) / 32), 8 * 32, gemm_smem<32>(), st, W, act, act_scale, out, M, out_stride, meta,
+           g_gemm_error);
 }
 
-void launch_embed(const ModelDev& md, const Work& w, int M, cudaStream_t st) { k_embed<<<M, 128, 0, st>>>(md, w, M); }
+void launch_embed(const ModelDev& md, const Work& w, int M, cudaStream_t st) {
+  t_pass_tokens = M;
+  launch(k_embed, M, 128, 0, st, md, w, M);
+}
 
 void launch_layer(const ModelDev& md, const LayerDev& L, const Work& w, const KvDev& kv, int M, int layer, int slot, int t_cap,
                   cudaStream_t st) {
+  t_pass_tokens = M;
   const int d = md.d_model, H = md.heads, KV = md.kv_heads;
   const int proj_stride = (2 * H + 2 * KV) * HEAD_DIM;
-  k_route<<<M, 256, route_smem(md), st>>>(md, L, w, M, layer, slot);
+  launch(k_route, M, 256, route_smem(md), st, md, L, w, M, layer, slot);
   project(L.qkvg, w.act, w.act_scale, w.proj, M, proj_stride, w.meta, st);
-  k_heads<<<M, 32 * (H + 2 * KV), 0, st>>>(md, L, w, kv, M, layer);
-  const int G = H / KV;
-  if (G == 1)
-    k_attend<1><<<dim3(M, KV), ATT_THREADS_ALL, attend_smem(md, t_cap), st>>>(md, w, kv, M, layer, L.global, t_cap);
-  else if (G == 2)
-    k_attend<2><<<dim3(M, KV), ATT_THREADS_ALL, attend_smem(md, t_cap), st>>>(md, w, kv, M, layer, L.global, t_cap);
-  else
-    k_attend<4><<<dim3(M, KV), ATT_THREADS_ALL, attend_smem(md, t_cap), st>>>(md, w, kv, M, layer, L.global, t_cap);
-  k_prep<<<M, 128, 0, st>>>(w.attn, H * HEAD_DIM, nullptr, w.proj + (H + 2 * KV) * HEAD_DIM, proj_stride, H * HEAD_DIM, w.act,
-                            w.act_scale, M, w.meta, md.inv_sqrt_group, 1);
+  launch(k_heads, M, 32 * (H + 2 * KV), 0, st, md, L, w, kv, M, layer);
+  launch_attend(md, L, w, kv, M, layer, t_cap, st);
+  launch(k_prep, M, 128, 0, st, (const float*)w.attn, H * HEAD_DIM, (const int32_t*)nullptr,
+         (const float*)(w.proj + (H + 2 * KV) * HEAD_DIM), proj_stride, H * HEAD_DIM, w.act, w.act_scale, M, w.meta,
+         md.inv_sqrt_group, 1);
   project(L.out, w.act, w.act_scale, w.outp, M, d, w.meta, st);
   if (md.hada_left == 64)
-    k_block<64><<<M, BLOCK_THREADS, block_smem(md), st>>>(md, L, w, M);
+    launch(k_block<64>, M, BLOCK_THREADS, block_smem(md), st, md, L, w, M);
   else
-    k_block<32><<<M, BLOCK_THREADS, block_smem(md), st>>>(md, L, w, M);
+    launch(k_block<32>, M, BLOCK_THREADS, block_smem(md), st, md, L, w, M);
 }
 
-void launch_final(const ModelDev& md, const Work& w, float* hidden, int M, cudaStream_t st) { k_final<<<M, 128, 0, st>>>(md, w, hidden, M); }
+void launch_final(const ModelDev& md, const Work& w, float* hidden, int M, cudaStream_t st) {
+  t_pass_tokens = M;
+  launch(k_final, M, 128, 0, st, md, w, hidden, M);
+}
 
 void launch_logits(const ModelDev& md, const float* hidden, const int32_t* slots, int B, int8_t* act, float* act_scale, float* logits,
                    cudaStream_t st) {
-  k_prep<<<B, 128, 0, st>>>(hidden, md.d_model, slots, nullptr, 0, md.d_model, act, act_scale, B, nullptr, md.inv_sqrt_group, 1);
+  t_pass_tokens = B;
+  launch(k_prep, B, 128, 0, st, hidden, (int)md.d_model, slots, (const float*)nullptr, 0, (int)md.d_model, act, act_scale, B,
+         (const TokenMeta*)nullptr, md.inv_sqrt_group, 1);
   project(md.logits, act, act_scale, logits, B, md.output_vocab, nullptr, st);
 }
 
 void launch_select(const float* logits, int V, const uint32_t* mask, const int32_t* active, uint32_t* next, float* peaks, int B,
                    cudaStream_t st) {
-  k_select<<<B, 256, 0, st>>>(logits, V, mask, active, next, peaks);
+  t_pass_tokens = B;
+  launch(k_select, B, 256, 0, st, logits, V, mask, active, next, peaks);
 }
 
 void launch_stats(const float* logits, int V, const uint32_t* mask, const int32_t* active, const uint32_t* next, const float* peaks,
                   float* stats, int stats_stride, int B, cudaStream_t st) {
-  k_stats<<<B, 256, (size_t)2 * V * 4, st>>>(logits, V, mask, active, next, peaks, stats, stats_stride);
+  t_pass_tokens = B;
+  launch(k_stats, B, 256, (size_t)2 * V * 4, st, logits, V, mask, active, next, peaks, stats, stats_stride);
 }
 
-void launch_advance(TokenMeta* meta, int B, cudaStream_t st) { k_advance<<<(B + 127) / 128, 128, 0, st>>>(meta, B); }
+void launch_advance(TokenMeta* meta, int B, cudaStream_t st) {
+  t_pass_tokens = B;
+  launch(k_advance, (B + 127) / 128, 128, 0, st, meta, B);
+}
 
 void launch_attend(const ModelDev& md, const LayerDev& L, const Work& w, const KvDev& kv, int M, int layer, int t_cap, cudaStream_t st) {
+  t_pass_tokens = M;
   const int G = md.heads / md.kv_heads, KV = md.kv_heads;
+  const size_t smem = attend_smem(md, t_cap);
   if (G == 1)
-    k_attend<1><<<dim3(M, KV), ATT_THREADS_ALL, attend_smem(md, t_cap), st>>>(md, w, kv, M, layer, L.global, t_cap);
+    launch(k_attend<1>, dim3(M, KV), ATT_THREADS_ALL, smem, st, md, w, kv, M, layer, L.global, t_cap);
   else if (G == 2)
-    k_attend<2><<<dim3(M, KV), ATT_THREADS_ALL, attend_smem(md, t_cap), st>>>(md, w, kv, M, layer, L.global, t_cap);
+    launch(k_attend<2>, dim3(M, KV), ATT_THREADS_ALL, smem, st, md, w, kv, M, layer, L.global, t_cap);
   else
-    k_attend<4><<<dim3(M, KV), ATT_THREADS_ALL, attend_smem(md, t_cap), st>>>(md, w, kv, M, layer, L.global, t_cap);
+    launch(k_attend<4>, dim3(M, KV), ATT_THREADS_ALL, smem, st, md, w, kv, M, layer, L.global, t_cap);
 }
 
 // ------------------------------------------------------------------- debug

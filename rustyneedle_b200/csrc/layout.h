@@ -126,6 +126,7 @@ struct Work {
   uint32_t capacity;
   const uint32_t* tokens;   // [M] token ids (device)
   const TokenMeta* meta;    // [M]
+  const int32_t* order;     // [M] attention CTA row i serves token order[i] (longest contexts first); null = i
   float* stream;            // [M][4][d]
   float* next_stream;       // [M][4][d]
   float* x;                 // [M][d]      routing input, then the block's running value

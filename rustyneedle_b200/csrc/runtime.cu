@@ -163,9 +163,16 @@ struct PinnedBuffer {
   }
 };
 
+// A batched step splits its sequences into up to this many groups whose
+// forward passes run as independent chains of the step's graph: every kernel
+// of the pass is a short per-token latency chain, so two or more chains
+// overlap on the SMs where one alone leaves them waiting.
+constexpr int MAX_STEP_GROUPS = 8;
+
 struct Engine {
   int device = 0;
   cudaStream_t stream = nullptr, side = nullptr;
+  cudaStream_t group_streams[MAX_STEP_GROUPS] = {};
   std::mutex mutex;
   nba::Geometry geo;
   ModelDev md{};
@@ -208,6 +215,8 @@ struct Engine {
     if (device >= 0) cudaSetDevice(device);
     if (stream) cudaStreamSynchronize(stream);
     if (side) cudaStreamDestroy(side);
+    for (cudaStream_t g : group_streams)
+      if (g) cudaStreamDestroy(g);
     if (stream) cudaStreamDestroy(stream);
   }
 
@@ -375,6 +384,7 @@ std::shared_ptr<Engine> open_engine(const char* path, const nb_options* opt) {
   if (prop.major != 10) fail(NB_ERR_NO_DEVICE, std::string("this build targets sm_100a; device is ") + prop.name);
   NB_CUDA(cudaStreamCreateWithFlags(&E->stream, cudaStreamNonBlocking));
   NB_CUDA(cudaStreamCreateWithFlags(&E->side, cudaStreamNonBlocking));
+  for (cudaStream_t& g : E->group_streams) NB_CUDA(cudaStreamCreateWithFlags(&g, cudaStreamNonBlocking));
   cudaStream_t st = E->stream;
   DeviceArena& A = E->arena;
 
@@ -660,14 +670,17 @@ struct nb_batch {
   std::map<int, cudaGraphExec_t> graphs;  // key: mask | stats << 1
   uint32_t* d_tokens = nullptr;           // the batch's token ids (= the chosen tokens)
   TokenMeta* d_meta = nullptr;
+  int32_t* d_order = nullptr;             // per group: its sequences by decreasing context length
   PinnedBuffer h_meta, h_mask, h_next, h_stats, h_active;
   DeviceArena arena;
-  cudaEvent_t fork = nullptr, join = nullptr;
+  cudaEvent_t fork = nullptr, join[MAX_STEP_GROUPS] = {};
+  int groups = 1;  // independent chains of the step (sequences split in runs of whole 32-row tiles)
   bool use_graphs = true;
   ~nb_batch() {
     for (auto& kv : graphs) cudaGraphExecDestroy(kv.second);
     if (fork) cudaEventDestroy(fork);
-    if (join) cudaEventDestroy(join);
+    for (cudaEvent_t e : join)
+      if (e) cudaEventDestroy(e);
   }
 };
 
@@ -890,34 +903,88 @@ nb_status nb_session_logits(nb_session* session, float* out, size_t capacity) {
 }
 
 // ------------------------------------------------------------------ batches
-static void build_step(nb_batch* b, bool masked, bool stats) {
+// The workspace rows [b0, capacity) as a workspace of their own. b0 is a
+// multiple of 32, so the int8 activations (core-matrix layout, 8-row blocks
+// of K bytes; K = d_model for both products that read them) start on a whole
+// 32-token tile of the tensor-core product.
+static Work work_rows(const Engine& E, const Work& w, uint32_t b0) {
+  const size_t d = E.md.d_model, H = E.md.heads, KV = E.md.kv_heads, actw = d;
+  Work s = w;
+  s.capacity = w.capacity - b0;
+  s.tokens = w.tokens + b0;
+  s.meta = w.meta + b0;
+  s.order = w.order ? w.order + b0 : nullptr;
+  s.stream = w.stream + b0 * LANES * d;
+  s.next_stream = w.next_stream + b0 * LANES * d;
+  s.x = w.x + b0 * d;
+  s.route = w.route + b0 * (LANES + LANES * LANES);
+  s.act = w.act + b0 * actw;
+  s.act_scale = w.act_scale + b0 * (actw / GROUP);
+  s.proj = w.proj + b0 * (2 * H + 2 * KV) * HEAD_DIM;
+  s.qcodes = w.qcodes + b0 * H * HEAD_DIM;
+  s.qscale = w.qscale + b0 * H;
+  s.attn = w.attn + b0 * H * HEAD_DIM;
+  s.outp = w.outp + b0 * d;
+  return s;
+}
+
+// Sequences [b0, b0 + count) of the step: tied logits, selection (and
+// statistics), then the forward pass of the chosen tokens, on stream `st`.
+static void build_group(nb_batch* b, bool masked, bool stats, uint32_t b0, uint32_t count, cudaStream_t st) {
   Engine& E = *b->engine;
-  const int B = (int)b->sessions.size();
-  const uint32_t V = E.md.output_vocab;
-  cudaStream_t st = E.stream;
-  nbk::launch_logits(E.md, E.d_hidden, E.d_slots, B, E.d_logit_act, E.d_logit_scale, E.d_logits, st);
-  nbk::launch_select(E.d_logits, (int)V, masked ? E.d_mask : nullptr, E.d_active, b->d_tokens, E.d_peaks, B, st);
-  if (stats) {
-    NB_CUDA(cudaEventRecord(b->fork, st));
-    NB_CUDA(cudaStreamWaitEvent(E.side, b->fork, 0));
-    nbk::launch_stats(E.d_logits, (int)V, masked ? E.d_mask : nullptr, E.d_active, b->d_tokens, E.d_peaks, E.d_stats, 2, B, E.side);
-  }
-  Work w = E.work;
-  w.tokens = b->d_tokens;
-  w.meta = b->d_meta;
+  const uint32_t V = E.md.output_vocab, d = E.md.d_model;
+  const int n = (int)count;
+  uint32_t* mask = masked ? E.d_mask + (size_t)b0 * (V / 32) : nullptr;
+  nbk::launch_logits(E.md, E.d_hidden, E.d_slots + b0, n, E.d_logit_act + (size_t)b0 * d, E.d_logit_scale + (size_t)b0 * (d / GROUP),
+                     E.d_logits + (size_t)b0 * V, st);
+  nbk::launch_select(E.d_logits + (size_t)b0 * V, (int)V, mask, E.d_active + b0, b->d_tokens + b0, E.d_peaks + 2 * b0, n, st);
+  if (stats)
+    nbk::launch_stats(E.d_logits + (size_t)b0 * V, (int)V, mask, E.d_active + b0, b->d_tokens + b0, E.d_peaks + 2 * b0,
+                      E.d_stats + 2 * b0, 2, n, st);
+  Work base = E.work;
+  base.tokens = b->d_tokens;
+  base.meta = b->d_meta;
+  base.order = b->d_order;
+  Work w = work_rows(E, base, b0);
   KvDev kv = E.kv();
-  nbk::launch_embed(E.md, w, B, st);
+  nbk::launch_embed(E.md, w, n, st);
   for (size_t slot = 0; slot < b->active.size(); ++slot) {
     int layer = b->active[slot];
-    nbk::launch_layer(E.md, E.layers[layer], w, kv, B, layer, (int)slot, E.t_cap, st);
+    nbk::launch_layer(E.md, E.layers[layer], w, kv, n, layer, (int)slot, E.t_cap, st);
     std::swap(w.stream, w.next_stream);
   }
-  nbk::launch_final(E.md, w, E.d_hidden, B, st);
-  nbk::launch_advance(b->d_meta, B, st);
-  if (stats) {
-    NB_CUDA(cudaEventRecord(b->join, E.side));
-    NB_CUDA(cudaStreamWaitEvent(st, b->join, 0));
+  nbk::launch_final(E.md, w, E.d_hidden, n, st);
+  nbk::launch_advance(b->d_meta + b0, n, st);
+}
+
+// Sequences per group: whole 32-sequence tiles.
+static uint32_t group_rows(uint32_t B, int groups) { return groups <= 1 ? B : std::min(B, ((B + groups - 1) / groups + 31) / 32 * 32); }
+
+static void build_step(nb_batch* b, bool masked, bool stats) {
+  Engine& E = *b->engine;
+  const uint32_t B = (uint32_t)b->sessions.size();
+  const uint32_t per = group_rows(B, b->groups);
+  if (per >= B) {
+    build_group(b, masked, stats, 0, B, E.stream);
+    return;
   }
+  NB_CUDA(cudaEventRecord(b->fork, E.stream));
+  int g = 0;
+  for (uint32_t b0 = 0; b0 < B; b0 += per, ++g) {
+    cudaStream_t st = E.group_streams[g];
+    NB_CUDA(cudaStreamWaitEvent(st, b->fork, 0));
+    build_group(b, masked, stats, b0, std::min(per, B - b0), st);
+    NB_CUDA(cudaEventRecord(b->join[g], st));
+  }
+  for (int i = 0; i < g; ++i) NB_CUDA(cudaStreamWaitEvent(E.stream, b->join[i], 0));
+}
+
+// Chains per step: one below 64 sequences, then one per 64 sequences up to
+// MAX_STEP_GROUPS; $NEEDLE_B200_STEP_GROUPS overrides (1 = a single chain).
+static int step_groups(uint32_t count) {
+  int groups = (int)std::min<uint32_t>(std::max<uint32_t>(count / 64, 1), 4);
+  if (const char* env = std::getenv("NEEDLE_B200_STEP_GROUPS")) groups = std::atoi(env);
+  return std::max(1, std::min(groups, MAX_STEP_GROUPS));
 }
 
 nb_status nb_batch_create(nb_model* model, nb_session* const* sessions, uint32_t count, nb_batch** out) {
@@ -946,7 +1013,24 @@ nb_status nb_batch_create(nb_model* model, nb_session* const* sessions, uint32_t
     b->h_active.ensure(count * 4);
     b->h_mask.ensure((size_t)count * (E.md.output_vocab / 32) * 4);
     NB_CUDA(cudaEventCreateWithFlags(&b->fork, cudaEventDisableTiming));
-    NB_CUDA(cudaEventCreateWithFlags(&b->join, cudaEventDisableTiming));
+    for (cudaEvent_t& e : b->join) NB_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+    b->groups = step_groups(count);
+    // attention CTAs of each group in decreasing context length: the longest
+    // sequences start first and the last wave holds the short ones (every
+    // sequence advances one position per step, so the order holds)
+    {
+      const uint32_t per = group_rows(count, b->groups);
+      std::vector<int32_t> order(count);
+      for (uint32_t g0 = 0; g0 < count; g0 += per) {
+        const uint32_t n = std::min(per, count - g0);
+        for (uint32_t i = 0; i < n; ++i) order[g0 + i] = (int32_t)i;
+        std::stable_sort(order.begin() + g0, order.begin() + g0 + n, [&](int32_t a, int32_t c) {
+          return b->sessions[g0 + a]->length > b->sessions[g0 + c]->length;
+        });
+      }
+      b->d_order = b->arena.alloc<int32_t>(count);
+      NB_CUDA(cudaMemcpy(b->d_order, order.data(), count * 4, cudaMemcpyHostToDevice));
+    }
     *out = b.release();
   });
 }
