@@ -91,23 +91,45 @@ __device__ __forceinline__ void phi_row(const ModelDev& md, int r, int layer, co
   row = r < 4 ? layer * LANES + r : (r < 8 ? layer * LANES + (r - 4) : layer * LANES * LANES + (r - 8));
 }
 
+// Shared memory of k_route, in floats: this layer's phi rows (PHI_ROWS × n
+// bytes, the 16-byte chunk c of row r stored at chunk c ^ (r % 8) so that the
+// eight rows a quarter-warp reads fall in distinct banks), the stream, a work
+// row, the squares in chain-major order (8 chains of n/8, stride n/8 + 4),
+// the int8 codes, the phi norms and the norm_in gains.
+__host__ __device__ inline size_t route_floats(int d) {
+  const size_t n = (size_t)LANES * d, ng = n / GROUP;
+  return PHI_ROWS * n / 4 + 2 * n + 8 * (n / 8 + 4) + n / 4 + PHI_ROWS * ng + d;
+}
+
 __global__ void __launch_bounds__(256) k_route(ModelDev md, LayerDev L, Work w, int M, int layer, int slot) {
-  extern __shared__ float sm[];
-  int t = blockIdx.x;
-  const int d = md.d_model, n = LANES * d, ng = n / GROUP;
+  extern __shared__ __align__(16) float sm[];
+  const int t = blockIdx.x;
+  const int d = md.d_model, n = LANES * d, ng = n / GROUP, sqs = n / 8 + 4;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  float* s_stream = sm;                                     // n
-  float* s_work = sm + n;                                   // n: normalised stream, later x
-  int8_t* s_codes = reinterpret_cast<int8_t*>(sm + 2 * n);  // n bytes
-  float* s_norms = sm + 2 * n + n / 4;                      // PHI_ROWS * ng phi norms
-  float* s_gain = s_norms + PHI_ROWS * ng;                  // d norm_in gains
+  uint8_t* s_phiw = reinterpret_cast<uint8_t*>(sm);              // PHI_ROWS × n bytes
+  float* s_stream = sm + PHI_ROWS * n / 4;                       // n
+  float* s_work = s_stream + n;                                  // n: later x and the phi terms
+  float* s_sq = s_work + n;                                      // 8 × sqs
+  int8_t* s_codes = reinterpret_cast<int8_t*>(s_sq + 8 * sqs);  // n bytes
+  float* s_norms = s_sq + 8 * sqs + n / 4;                       // PHI_ROWS × ng phi norms
+  float* s_gain = s_norms + PHI_ROWS * ng;                       // d norm_in gains
   __shared__ float s_ascale[MAX_D * LANES / GROUP];
   __shared__ float s_red[8];
   __shared__ float s_phi[PHI_ROWS];
   __shared__ float s_gate[LANES];
-  __shared__ float s_inv;
+  __shared__ float s_inv, s_peak;
 
   // the layer's constant weights first, then (once the previous kernel is done) the token's stream
+  {
+    const int chunks = n / 16;
+    for (int i = tid; i < PHI_ROWS * chunks; i += blockDim.x) {
+      const int r = i / chunks, c = i % chunks;
+      const QMat* P;
+      int row;
+      phi_row(md, r, layer, P, row);
+      cp_async16(s_phiw + (size_t)r * n + (size_t)(c ^ (r & 7)) * 16, P->codes + (size_t)row * n + (size_t)c * 16);
+    }
+  }
   stage_async(s_norms, md.phi_pre.scales + (size_t)layer * LANES * ng, LANES * ng);
   stage_async(s_norms + LANES * ng, md.phi_post.scales + (size_t)layer * LANES * ng, LANES * ng);
   stage_async(s_norms + 2 * LANES * ng, md.phi_res.scales + (size_t)layer * LANES * LANES * ng, LANES * LANES * ng);
@@ -120,24 +142,52 @@ __global__ void __launch_bounds__(256) k_route(ModelDev md, LayerDev L, Work w, 
   stage_async(s_stream, w.stream + (size_t)t * n, n);
   cp_async_wait_all();
   __syncthreads();
-  // unit_rms over all lanes (ops.rs:60-66), then fake_quantise_int8 (ops.rs:120-125)
-  if (warp == 0) {
-    float ss = sum_of_squares_warp(s_stream, n);
-    if (lane == 0) s_inv = inverse_rms(ss, n);
+  // unit_rms over all lanes (ops.rs:60-66): the squares, placed chain-major
+  // (value v joins chain v % 8 at place v / 8), and the peak |x|, which the
+  // positive scale keeps: max |x·inv| = max|x| · inv
+  {
+    float pk = 0.0f;
+    for (int v = tid; v < n; v += blockDim.x) {
+      const float x = s_stream[v];
+      s_sq[(v & 7) * sqs + (v >> 3)] = fmul(x, x);
+      pk = fmaxf(pk, fabsf(x));
+    }
+    pk = warp_max(pk);
+    if (lane == 0) s_red[warp] = pk;
   }
   __syncthreads();
-  float inv = s_inv, peak = 0.0f;
-  for (int i = tid; i < n; i += blockDim.x) {
-    float v = fmul(s_stream[i], inv);
-    s_work[i] = v;
-    peak = fmaxf(peak, fabsf(v));
-  }
-  float scale = int8_scale_of(block_max(peak, s_red));
-  // rotate and quantise per 128-group (QuantisedMatrix::prepare + PlaneInput)
-  for (int g = warp; g < ng; g += 8) {
-    float v[4];
+  if (warp == 0) {
+    // eight ordered chains over n/8 squares each, then the lanes in order from -0.0 (ops.rs:7-17)
+    float acc = 0.0f;
+    if (lane < 8) {
+      const float4* q = reinterpret_cast<const float4*>(s_sq + lane * sqs);
+      for (int m = 0; m < n / 32; m += 8) {
+        float4 b[8];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) v[j] = fake_quant(s_work[g * GROUP + 4 * lane + j], scale);
+        for (int k = 0; k < 8; ++k) b[k] = q[m + k];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) acc = fadd(fadd(fadd(fadd(acc, b[k].x), b[k].y), b[k].z), b[k].w);
+      }
+    }
+    float ss = SUM_START;
+#pragma unroll
+    for (int l = 0; l < 8; ++l) ss = fadd(ss, __shfl_sync(FULL, acc, l));
+    if (lane == 0) {
+      float pk = s_red[0];
+      for (int i = 1; i < 8; ++i) pk = fmaxf(pk, s_red[i]);
+      s_inv = inverse_rms(ss, n);
+      s_peak = pk;
+    }
+  }
+  __syncthreads();
+  // fake_quantise_int8 (ops.rs:120-125) of the normalised stream, then rotate
+  // and quantise per 128-group (QuantisedMatrix::prepare + PlaneInput)
+  const float inv = s_inv;
+  float scale = int8_scale_of(fmul(s_peak, inv));
+  for (int g = warp; g < ng; g += 8) {
+    const float4 x = reinterpret_cast<const float4*>(s_stream + g * GROUP)[lane];
+    float v[4] = {fake_quant(fmul(x.x, inv), scale), fake_quant(fmul(x.y, inv), scale), fake_quant(fmul(x.z, inv), scale),
+                  fake_quant(fmul(x.w, inv), scale)};
     fwht128(v, md.inv_sqrt_group);
     uint32_t packed;
     float sc = quantise_group(v, packed);
@@ -158,13 +208,10 @@ __global__ void __launch_bounds__(256) k_route(ModelDev md, LayerDev L, Work w, 
     for (int u = 0; u < 2; ++u) {
       const int pair = tid + u * 256;
       if (pair < pairs) {
-        const int g = pair / PHI_ROWS;
-        const QMat* P;
-        int row;
-        phi_row(md, pair % PHI_ROWS, layer, P, row);
-        const uint4* wv = reinterpret_cast<const uint4*>(P->codes + (size_t)row * n + g * GROUP);
+        const int g = pair / PHI_ROWS, r = pair % PHI_ROWS;
+        const uint4* wv = reinterpret_cast<const uint4*>(s_phiw + (size_t)r * n);
 #pragma unroll
-        for (int k = 0; k < 8; ++k) wr[u][k] = wv[k];
+        for (int k = 0; k < 8; ++k) wr[u][k] = wv[(g * 8 + k) ^ (r & 7)];
       }
     }
 #pragma unroll
@@ -260,10 +307,10 @@ __global__ void __launch_bounds__(256) k_route(ModelDev md, LayerDev L, Work w, 
   named_barrier(1, nthreads);
   // zero_centred_norm (ops.rs:44-50) then fake_quantise_int8 (attention.rs:99-100)
   float* s_y = s_stream;
-  inv = s_inv;
-  peak = 0.0f;
+  const float inv_x = s_inv;
+  float peak = 0.0f;
   for (int i = tid; i < d; i += nthreads) {
-    float v = fmul(fmul(fadd(1.0f, s_gain[i]), s_x[i]), inv);
+    float v = fmul(fmul(fadd(1.0f, s_gain[i]), s_x[i]), inv_x);
     s_y[i] = v;
     peak = fmaxf(peak, fabsf(v));
   }
@@ -886,29 +933,22 @@ __global__ void __launch_bounds__(128) k_prep(const float* __restrict__ in, int 
 }
 
 // ------------------------------------------------------------ block finish
-// grid M, block 128. Post norm, gated residual (session.rs:121-125), the
+// grid M, block 256. Post norm, gated residual (session.rs:121-125), the
 // Hadamard MLP (hadamard.rs:260-304) and the lane combine (lanes.rs:183-204).
 //
 // Each Kronecker factor application K(x) = Lᵀ·(X·R) (ops.rs:143-164) runs as
 // two products C[r][c] = Σ_s A[s][r]·B[s][c] with s ascending, the reference's
-// summation order for every output. A thread owns a 4×4 output tile, so each
-// step reads one float4 of A and one of B from shared memory for 16
-// multiply-adds. The stage-A operand X enters transposed (XT[j][i]). Operands
-// arrive by cp.async, the next factor pair while the current stage's
-// elementwise pass runs.
-// Packed two-lane f32 arithmetic (PTX add/mul/fma .rn.f32x2): each component
+// summation order for every output. A thread owns a 4×2 output tile: each
+// step reads one float4 of A and one float2 of B from shared memory for 8
+// multiply-adds, two columns per packed instruction. The stage-A operand X
+// enters transposed (XT[j][i]). Operands arrive by cp.async, the next factor
+// pair while the current stage's elementwise pass runs.
+// Packed two-lane f32 arithmetic (PTX add/fma .rn.f32x2): each component
 // rounded to nearest exactly as the scalar .rn instruction.
 __device__ __forceinline__ float2 add2(float2 a, float2 b) {
   float2 d;
   asm("{\n\t.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
       "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
-      : "=f"(d.x), "=f"(d.y) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
-  return d;
-}
-__device__ __forceinline__ float2 mul2(float2 a, float2 b) {
-  float2 d;
-  asm("{\n\t.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
-      "mul.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
       : "=f"(d.x), "=f"(d.y) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
   return d;
 }
@@ -920,8 +960,14 @@ __device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
   return d;
 }
 
+// -0.0 in both lanes, read from memory so the compiler cannot see the value:
+// fma(a, b, -0.0) is a·b rounded once, exactly mul.rn, and a packed fma is
+// never merged with the packed add that follows it (a visible packed multiply
+// would be, into one fused multiply-add the reference never performs).
+__device__ float2 g_negzero = {-0.0f, -0.0f};
+
 template <int S, int R, bool FUSED32>
-__device__ __forceinline__ void tn_stage(const float* __restrict__ A, const float* __restrict__ B, float* __restrict__ C) {
+__device__ __forceinline__ void tn_stage(const float* __restrict__ A, const float* __restrict__ B, float* __restrict__ C, float2 nz) {
   // A thread owns a 4-row × 2-column tile: per step one float4 of A, one
   // float2 of B, and the two columns of a row share one packed f32x2 product.
   constexpr int TILES = (R / 4) * (HADA_RIGHT / 2);
@@ -939,15 +985,10 @@ __device__ __forceinline__ void tn_stage(const float* __restrict__ A, const floa
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         const float2 ai = make_float2(av[i], av[i]);
-        if (FUSED32) {
+        if (FUSED32)
           acc[i] = fma2(ai, b, acc[i]);
-        } else {
-          // packed products, scalar sums: a packed multiply feeding a packed
-          // add is contracted to a packed fma by the backend even under
-          // -fmad=false, which the reference never does here
-          const float2 p = mul2(ai, b);
-          acc[i] = make_float2(fadd(acc[i].x, p.x), fadd(acc[i].y, p.y));
-        }
+        else
+          acc[i] = add2(acc[i], fma2(ai, b, nz));  // product rounded, then the sum rounded
       }
     }
 #pragma unroll
@@ -957,9 +998,9 @@ __device__ __forceinline__ void tn_stage(const float* __restrict__ A, const floa
 }
 
 template <int LEFT, bool FUSED32>
-__device__ __forceinline__ void kronecker(float* xt, float* tmp, const float* left, const float* right, float* out) {
-  tn_stage<HADA_RIGHT, LEFT, FUSED32>(xt, right, tmp);
-  tn_stage<LEFT, LEFT, FUSED32>(left, tmp, out);
+__device__ __forceinline__ void kronecker(float* xt, float* tmp, const float* left, const float* right, float* out, float2 nz) {
+  tn_stage<HADA_RIGHT, LEFT, FUSED32>(xt, right, tmp, nz);
+  tn_stage<LEFT, LEFT, FUSED32>(left, tmp, out, nz);
 }
 
 constexpr int BLOCK_THREADS = 256;
@@ -980,6 +1021,7 @@ __device__ __forceinline__ void hadamard_core(const ModelDev& md, const Hadamard
   constexpr int PER = N / (4 * BLOCK_THREADS);
   constexpr bool FUSED32 = LEFT == 32;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const float2 nz = g_negzero;
   __shared__ float s_w[COND_RANK], s_chain[4][COND_RANK];
   // condition weights: four chains of rank-8 partial sums (hadamard.rs:263-276).
   // Chain (j, r) adds x[4g+j]·cond_v[4g+j][r] over g in order; the products
@@ -1043,39 +1085,54 @@ __device__ __forceinline__ void hadamard_core(const ModelDev& md, const Hadamard
     }
   }
   __syncthreads();
-  kronecker<LEFT, FUSED32>(buf0, buf1, s_left, s_right, buf0);  // first = K1(d1 ⊙ x)
+  // the next elementwise pass's constants are loaded into registers before
+  // each Kronecker application, so their latency hides behind it
+  int4 p1[PER];
+  float4 d2v[PER], b2v[PER];
+#pragma unroll
+  for (int q = 0; q < PER; ++q) {
+    const int i4 = tid + q * BLOCK_THREADS;
+    p1[q] = reinterpret_cast<const int4*>(md.perm1)[i4];
+    d2v[q] = reinterpret_cast<const float4*>(Hd.d2)[i4];
+    b2v[q] = reinterpret_cast<const float4*>(Hd.b2)[i4];
+  }
+  kronecker<LEFT, FUSED32>(buf0, buf1, s_left, s_right, buf0, nz);  // first = K1(d1 ⊙ x)
   stage_async(s_left, Hd.left[1], LEFT * LEFT);
   stage_async(s_right, Hd.right[1], HADA_RIGHT * HADA_RIGHT);
 #pragma unroll
   for (int q = 0; q < PER; ++q) {
     const int i4 = tid + q * BLOCK_THREADS;
-    const int4 p = reinterpret_cast<const int4*>(md.perm1)[i4];
-    const float4 d2 = reinterpret_cast<const float4*>(Hd.d2)[i4];
-    const float4 b2 = reinterpret_cast<const float4*>(Hd.b2)[i4];
     const float4 mo = *reinterpret_cast<const float4*>(s_mod + 4 * i4);
-    const int pv[4] = {p.x, p.y, p.z, p.w};
-    const float dv[4] = {d2.x, d2.y, d2.z, d2.w}, bv[4] = {b2.x, b2.y, b2.z, b2.w}, mv[4] = {mo.x, mo.y, mo.z, mo.w};
+    const int pv[4] = {p1[q].x, p1[q].y, p1[q].z, p1[q].w};
+    const float dv[4] = {d2v[q].x, d2v[q].y, d2v[q].z, d2v[q].w}, bv[4] = {b2v[q].x, b2v[q].y, b2v[q].z, b2v[q].w},
+                mv[4] = {mo.x, mo.y, mo.z, mo.w};
 #pragma unroll
     for (int e = 0; e < 4; ++e) buf1[transposed<LEFT>(4 * i4 + e)] = silu(fadd(fmul(fmul(dv[e], mv[e]), buf0[pv[e]]), bv[e]));
   }
+  int4 p2[PER];
+  float4 d3v[PER];
+#pragma unroll
+  for (int q = 0; q < PER; ++q) {
+    const int i4 = tid + q * BLOCK_THREADS;
+    p2[q] = reinterpret_cast<const int4*>(md.perm2)[i4];
+    d3v[q] = reinterpret_cast<const float4*>(Hd.d3)[i4];
+  }
   cp_async_wait_all();
   __syncthreads();
-  kronecker<LEFT, FUSED32>(buf1, buf0, s_left, s_right, buf1);  // second
+  kronecker<LEFT, FUSED32>(buf1, buf0, s_left, s_right, buf1, nz);  // second
   stage_async(s_left, Hd.left[2], LEFT * LEFT);
   stage_async(s_right, Hd.right[2], HADA_RIGHT * HADA_RIGHT);
 #pragma unroll
   for (int q = 0; q < PER; ++q) {
     const int i4 = tid + q * BLOCK_THREADS;
-    const int4 p = reinterpret_cast<const int4*>(md.perm2)[i4];
-    const float4 d3 = reinterpret_cast<const float4*>(Hd.d3)[i4];
-    const int pv[4] = {p.x, p.y, p.z, p.w};
-    const float dv[4] = {d3.x, d3.y, d3.z, d3.w};
+    const int pv[4] = {p2[q].x, p2[q].y, p2[q].z, p2[q].w};
+    const float dv[4] = {d3v[q].x, d3v[q].y, d3v[q].z, d3v[q].w};
 #pragma unroll
     for (int e = 0; e < 4; ++e) buf0[transposed<LEFT>(4 * i4 + e)] = fmul(buf1[pv[e]], dv[e]);
   }
   cp_async_wait_all();
   __syncthreads();
-  kronecker<LEFT, FUSED32>(buf0, buf1, s_left, s_right, buf0);  // third
+  kronecker<LEFT, FUSED32>(buf0, buf1, s_left, s_right, buf0, nz);  // third
 }
 
 template <int LEFT>
@@ -1095,6 +1152,8 @@ __global__ void __launch_bounds__(BLOCK_THREADS) k_block(ModelDev md, LayerDev L
   // d*8 condition values, consumed before the first Kronecker stage: they
   // borrow buf1 and s_mod when they fit there
   float* s_condv = d * COND_RANK <= 2 * N ? buf1 : s_right + HADA_RIGHT * HADA_RIGHT;
+  float* s_gpost = s_right + HADA_RIGHT * HADA_RIGHT + (d * COND_RANK <= 2 * N ? 0 : d * COND_RANK);  // d post_norm gains
+  float* s_gpre = s_gpost + MAX_D;                                                                     // d pre_hada gains
   __shared__ float s_inv, s_gate;
   const HadamardDev& Hd = L.hada;
 
@@ -1102,6 +1161,8 @@ __global__ void __launch_bounds__(BLOCK_THREADS) k_block(ModelDev md, LayerDev L
   stage_async(s_condv, Hd.cond_v, d * COND_RANK);
   stage_async(s_left, Hd.left[0], LEFT * LEFT);
   stage_async(s_right, Hd.right[0], HADA_RIGHT * HADA_RIGHT);
+  stage_async(s_gpost, L.post_norm, d);
+  stage_async(s_gpre, L.pre_hada, d);
   if (tid == 0) s_gate = sigmoid(L.attn_gate);
   pdl_wait();
   if (t >= M || w.meta[t].slot < 0) {
@@ -1118,7 +1179,7 @@ __global__ void __launch_bounds__(BLOCK_THREADS) k_block(ModelDev md, LayerDev L
   }
   __syncthreads();
   for (int i = tid; i < d; i += BLOCK_THREADS) {
-    float a = fmul(fmul(fadd(1.0f, L.post_norm[i]), s_a[i]), s_inv);
+    float a = fmul(fmul(fadd(1.0f, s_gpost[i]), s_a[i]), s_inv);
     s_a[i] = fadd(s_x[i], fmul(s_gate, a));
   }
   __syncthreads();
@@ -1127,22 +1188,27 @@ __global__ void __launch_bounds__(BLOCK_THREADS) k_block(ModelDev md, LayerDev L
     if (lane == 0) s_inv = inverse_rms(ss, d);
   }
   __syncthreads();
-  for (int i = tid; i < d; i += BLOCK_THREADS) s_pre[i] = fmul(fmul(fadd(1.0f, L.pre_hada[i]), s_a[i]), s_inv);
-  __syncthreads();
-  hadamard_core<LEFT>(md, Hd, d, s_pre, buf0, buf1, s_mod, s_left, s_right, s_condv);
-  pdl_trigger();  // the lane combine overlaps the next kernel's prologue
-  // x += mlp; delta = x - input; next lanes (lanes.rs:183-204)
+  for (int i = tid; i < d; i += BLOCK_THREADS) s_pre[i] = fmul(fmul(fadd(1.0f, s_gpre[i]), s_a[i]), s_inv);
+  // the lane combine's operands (routing weights, this token's lanes, d4) load
+  // while the Hadamard MLP runs; one float4 column per thread (d <= 4 · 256)
   const float* route = w.route + (size_t)t * (LANES + LANES * LANES);
   float rw[LANES + LANES * LANES];
 #pragma unroll
   for (int k = 0; k < LANES + LANES * LANES; ++k) rw[k] = route[k];
   const float* stream = w.stream + (size_t)t * LANES * d;
   float* next = w.next_stream + (size_t)t * LANES * d;
-  for (int i4 = tid; i4 < d / 4; i4 += BLOCK_THREADS) {
-    const float4 d4 = reinterpret_cast<const float4*>(Hd.d4)[i4];
-    float4 sv[LANES];
+  const int i4 = tid;
+  float4 sv[LANES], d4 = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+  if (i4 < d / 4) {
+    d4 = reinterpret_cast<const float4*>(Hd.d4)[i4];
 #pragma unroll
     for (int s = 0; s < LANES; ++s) sv[s] = reinterpret_cast<const float4*>(stream + s * d)[i4];
+  }
+  __syncthreads();
+  hadamard_core<LEFT>(md, Hd, d, s_pre, buf0, buf1, s_mod, s_left, s_right, s_condv);
+  pdl_trigger();  // the lane combine overlaps the next kernel's prologue
+  // x += mlp; delta = x - input; next lanes (lanes.rs:183-204)
+  if (i4 < d / 4) {
     const float dv[4] = {d4.x, d4.y, d4.z, d4.w};
     float delta[4];
 #pragma unroll
@@ -1324,17 +1390,14 @@ void set_exp_constants(const nbx::ExpConstants& constants, const nbx::ExceptionS
   cudaMemcpyToSymbolAsync(c_exceptions, &exceptions, sizeof exceptions, 0, cudaMemcpyHostToDevice, stream);
 }
 
-size_t route_smem(const ModelDev& md) {
-  const size_t n = (size_t)LANES * md.d_model, ng = n / GROUP;
-  return (2 * n + n / 4 + PHI_ROWS * ng + md.d_model) * 4;
-}
+size_t route_smem(const ModelDev& md) { return route_floats((int)md.d_model) * 4; }
 size_t attend_smem(const ModelDev& md, int t_cap) {
   int G = md.heads / md.kv_heads;
   return (size_t)(G + 1) * t_cap * 4 + 2 * (size_t)G * att_wstride(t_cap) * 4 + (size_t)ATT_SLICES * G * HEAD_DIM * 4;
 }
 size_t block_smem(const ModelDev& md) {
   int N = md.hada_left * HADA_RIGHT;
-  size_t floats = 3 * MAX_D + 3 * N + md.hada_left * md.hada_left + HADA_RIGHT * HADA_RIGHT;
+  size_t floats = 3 * MAX_D + 3 * N + md.hada_left * md.hada_left + HADA_RIGHT * HADA_RIGHT + 2 * MAX_D;
   if ((int)md.d_model * COND_RANK > 2 * N) floats += (size_t)md.d_model * COND_RANK;
   return floats * 4;
 }
