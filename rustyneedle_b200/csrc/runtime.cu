@@ -163,10 +163,9 @@ struct PinnedBuffer {
   }
 };
 
-// A batched step splits its sequences into up to this many groups whose
-// forward passes run as independent chains of the step's graph: every kernel
-// of the pass is a short per-token latency chain, so two or more chains
-// overlap on the SMs where one alone leaves them waiting.
+// A batched step can split its sequences into up to this many groups whose
+// forward passes run as independent chains of the step's graph (see
+// step_groups for the default).
 constexpr int MAX_STEP_GROUPS = 8;
 
 struct Engine {
@@ -979,10 +978,11 @@ static void build_step(nb_batch* b, bool masked, bool stats) {
   for (int i = 0; i < g; ++i) NB_CUDA(cudaStreamWaitEvent(E.stream, b->join[i], 0));
 }
 
-// Chains per step: one below 64 sequences, then one per 64 sequences up to
-// MAX_STEP_GROUPS; $NEEDLE_B200_STEP_GROUPS overrides (1 = a single chain).
-static int step_groups(uint32_t count) {
-  int groups = (int)std::min<uint32_t>(std::max<uint32_t>(count / 64, 1), 4);
+// Chains per step: one by default (measured on B200: a single chain of 256
+// sequences steps as fast as four concurrent chains of 64);
+// $NEEDLE_B200_STEP_GROUPS sets another count.
+static int step_groups(uint32_t) {
+  int groups = 1;
   if (const char* env = std::getenv("NEEDLE_B200_STEP_GROUPS")) groups = std::atoi(env);
   return std::max(1, std::min(groups, MAX_STEP_GROUPS));
 }
