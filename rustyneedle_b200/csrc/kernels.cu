@@ -16,6 +16,7 @@
 //                 (model/src/session.rs:121-137, hadamard.rs:260-304)
 // then k_final (lane mean and final norm) and, per generated token, the tied
 // logits product and k_select (generator.rs:147-194).
+#include <cooperative_groups.h>
 #include <cuda_runtime.h>
 
 #include <cstdlib>
@@ -659,17 +660,26 @@ constexpr int ATT_THREADS_ALL = ATT_WORKERS + 32;
 constexpr int MAX_GROUP = 4;
 constexpr int ATT_SLICES = ATT_WORKERS / 16;
 constexpr int ATT_UNROLL = 4;
+constexpr int ATT_MAX_KV = 8;
 
 __host__ __device__ constexpr int att_wstride(int t_cap) { return t_cap / 4 + 2; }
 
-template <int G>
+// With PREP (G * 64 values per CTA, whole 128-value groups) the kernel also
+// does k_prep's work for the output projection: the CTAs of one token form a
+// cluster over the kv heads, exchange the peak of their gated outputs in
+// distributed shared memory and each quantises its own groups.
+__device__ __forceinline__ void cluster_arrive_relaxed() { asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory"); }
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.aligned;" ::: "memory"); }
+
+template <int G, bool PREP>
 __global__ void __launch_bounds__(ATT_THREADS_ALL, 3) k_attend(ModelDev md, Work w, KvDev kv, int M, int layer, int global, int t_cap) {
   pdl_wait();
   extern __shared__ float sm[];
-  if ((int)blockIdx.x >= M) return;
+  if ((int)blockIdx.x >= M) return;  // the whole cluster shares the token
   const int t = w.order ? w.order[blockIdx.x] : (int)blockIdx.x, kvh = blockIdx.y;
   const TokenMeta meta = w.meta[t];
   if (meta.slot < 0) return;
+  if (PREP) cluster_arrive_relaxed();  // paired with the wait before the first remote access
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int total = meta.position + 1;
   int first = 0;
@@ -879,6 +889,7 @@ __global__ void __launch_bounds__(ATT_THREADS_ALL, 3) k_attend(ModelDev md, Work
   }
   __syncthreads();
   pdl_trigger();  // the output rows overlap the next kernel's prologue
+  float out = 0.0f;
   if (tid < G * HEAD_DIM) {
     const int h = tid / HEAD_DIM, dim = tid % HEAD_DIM;
     int sum = 0;
@@ -886,7 +897,48 @@ __global__ void __launch_bounds__(ATT_THREADS_ALL, 3) k_attend(ModelDev md, Work
     for (int s = 0; s < ATT_SLICES; ++s) sum += s_pv[(s * G + h) * HEAD_DIM + dim];
     const float value = s_peak[h] > 0.0f ? fmul((float)sum, s_scale2[h]) : 0.0f;
     const float inverse = fdiv(1.0f, s_total[h]);
-    w.attn[(size_t)t * md.heads * HEAD_DIM + (kvh * G + h) * HEAD_DIM + dim] = fmul(value, inverse);
+    out = fmul(value, inverse);
+    if (!PREP) w.attn[(size_t)t * md.heads * HEAD_DIM + (kvh * G + h) * HEAD_DIM + dim] = out;
+  }
+  if (PREP) {
+    // k_prep (attention.rs:145-150): the output gated by sigmoid(gate), the
+    // peak over the token's whole vector (all kv heads of the cluster), the
+    // fake quantisation, then per 128-group rotation and int8 codes
+    namespace cg = cooperative_groups;
+    cg::cluster_group cluster = cg::this_cluster();
+    __shared__ __align__(16) float s_o[MAX_GROUP * HEAD_DIM];
+    __shared__ float s_cpeak[ATT_MAX_KV];
+    const int H = md.heads, KV = md.kv_heads, proj_stride = (2 * H + 2 * KV) * HEAD_DIM;
+    float mag = 0.0f;
+    if (tid < G * HEAD_DIM) {
+      const float gate = w.proj[(size_t)t * proj_stride + (H + 2 * KV) * HEAD_DIM + kvh * G * HEAD_DIM + tid];
+      const float v = fmul(out, sigmoid(gate));
+      s_o[tid] = v;
+      mag = fabsf(v);
+    }
+    mag = warp_max(mag);
+    if (lane == 0 && warp < G * 2) s_red[0][warp] = mag;
+    __syncthreads();
+    cluster_wait();  // every CTA of the cluster runs: distributed shared memory is usable
+    if (tid == 0) {
+      float pk = s_red[0][0];
+      for (int i = 1; i < G * 2; ++i) pk = fmaxf(pk, s_red[0][i]);
+      for (int r = 0; r < KV; ++r) *cluster.map_shared_rank(&s_cpeak[kvh], r) = pk;
+    }
+    cluster.sync();
+    float peak = s_cpeak[0];
+    for (int r = 1; r < KV; ++r) peak = fmaxf(peak, s_cpeak[r]);
+    const float scale = int8_scale_of(peak);
+    if (warp < G / 2) {
+      const float4 x = reinterpret_cast<const float4*>(s_o + warp * GROUP)[lane];
+      float v[4] = {fake_quant(x.x, scale), fake_quant(x.y, scale), fake_quant(x.z, scale), fake_quant(x.w, scale)};
+      fwht128(v, md.inv_sqrt_group);
+      uint32_t packed;
+      const float sc = quantise_group(v, packed);
+      const int K = H * HEAD_DIM, group = kvh * (G / 2) + warp;
+      *reinterpret_cast<uint32_t*>(w.act + core_offset(t, group * GROUP + 4 * lane, K / 16)) = packed;
+      if (lane == 0) w.act_scale[(size_t)t * (K / GROUP) + group] = sc;
+    }
   }
 }
 
@@ -1405,9 +1457,12 @@ size_t block_smem(const ModelDev& md) {
 cudaError_t configure(const ModelDev& md, int t_cap) {
   cudaError_t e;
   if ((e = cudaFuncSetAttribute(k_route, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)route_smem(md)))) return e;
-  if ((e = cudaFuncSetAttribute(k_attend<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)attend_smem(md, t_cap)))) return e;
-  if ((e = cudaFuncSetAttribute(k_attend<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)attend_smem(md, t_cap)))) return e;
-  if ((e = cudaFuncSetAttribute(k_attend<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)attend_smem(md, t_cap)))) return e;
+  const int att_smem = (int)attend_smem(md, t_cap);
+  if ((e = cudaFuncSetAttribute(k_attend<1, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, att_smem))) return e;
+  if ((e = cudaFuncSetAttribute(k_attend<2, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, att_smem))) return e;
+  if ((e = cudaFuncSetAttribute(k_attend<4, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, att_smem))) return e;
+  if ((e = cudaFuncSetAttribute(k_attend<2, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, att_smem))) return e;
+  if ((e = cudaFuncSetAttribute(k_attend<4, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, att_smem))) return e;
   if ((e = cudaFuncSetAttribute(k_block<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)block_smem(md)))) return e;
   if ((e = cudaFuncSetAttribute(k_block<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)block_smem(md)))) return e;
   if ((e = cudaFuncSetAttribute(k_stats, cudaFuncAttributeMaxDynamicSharedMemorySize, 2 * 8192 * 4))) return e;
@@ -1439,18 +1494,30 @@ static bool pdl_enabled() {
 }
 
 template <typename... P, typename... A>
-static void launch(void (*kernel)(P...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, A&&... args) {
+static void launch_clustered(void (*kernel)(P...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, dim3 cluster, A&&... args) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = block;
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  if (cluster.x * cluster.y * cluster.z > 1) {
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = cluster.x;
+    attr[1].val.clusterDim.y = cluster.y;
+    attr[1].val.clusterDim.z = cluster.z;
+    cfg.numAttrs = 2;
+  }
   cudaLaunchKernelEx(&cfg, kernel, std::forward<A>(args)...);
+}
+
+template <typename... P, typename... A>
+static void launch(void (*kernel)(P...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, A&&... args) {
+  launch_clustered(kernel, grid, block, smem, st, dim3(1, 1, 1), std::forward<A>(args)...);
 }
 
 static void project(const QMat& W, const int8_t* act, const float* act_scale, float* out, int M, int out_stride,
@@ -1479,10 +1546,12 @@ void launch_layer(const ModelDev& md, const LayerDev& L, const Work& w, const Kv
   launch(k_route, M, 256, route_smem(md), st, md, L, w, M, layer, slot);
   project(L.qkvg, w.act, w.act_scale, w.proj, M, proj_stride, w.meta, st);
   launch(k_heads, M, 32 * (H + 2 * KV), 0, st, md, L, w, kv, M, layer);
-  launch_attend(md, L, w, kv, M, layer, t_cap, st);
-  launch(k_prep, M, 128, 0, st, (const float*)w.attn, H * HEAD_DIM, (const int32_t*)nullptr,
-         (const float*)(w.proj + (H + 2 * KV) * HEAD_DIM), proj_stride, H * HEAD_DIM, w.act, w.act_scale, M, w.meta,
-         md.inv_sqrt_group, 1);
+  if (!launch_attend_prep(md, L, w, kv, M, layer, t_cap, st)) {
+    launch_attend(md, L, w, kv, M, layer, t_cap, st);
+    launch(k_prep, M, 128, 0, st, (const float*)w.attn, H * HEAD_DIM, (const int32_t*)nullptr,
+           (const float*)(w.proj + (H + 2 * KV) * HEAD_DIM), proj_stride, H * HEAD_DIM, w.act, w.act_scale, M, w.meta,
+           md.inv_sqrt_group, 1);
+  }
   project(L.out, w.act, w.act_scale, w.outp, M, d, w.meta, st);
   if (md.hada_left == 64)
     launch(k_block<64>, M, BLOCK_THREADS, block_smem(md), st, md, L, w, M);
@@ -1525,11 +1594,37 @@ void launch_attend(const ModelDev& md, const LayerDev& L, const Work& w, const K
   const int G = md.heads / md.kv_heads, KV = md.kv_heads;
   const size_t smem = attend_smem(md, t_cap);
   if (G == 1)
-    launch(k_attend<1>, dim3(M, KV), ATT_THREADS_ALL, smem, st, md, w, kv, M, layer, L.global, t_cap);
+    launch(k_attend<1, false>, dim3(M, KV), ATT_THREADS_ALL, smem, st, md, w, kv, M, layer, L.global, t_cap);
   else if (G == 2)
-    launch(k_attend<2>, dim3(M, KV), ATT_THREADS_ALL, smem, st, md, w, kv, M, layer, L.global, t_cap);
+    launch(k_attend<2, false>, dim3(M, KV), ATT_THREADS_ALL, smem, st, md, w, kv, M, layer, L.global, t_cap);
   else
-    launch(k_attend<4>, dim3(M, KV), ATT_THREADS_ALL, smem, st, md, w, kv, M, layer, L.global, t_cap);
+    launch(k_attend<4, false>, dim3(M, KV), ATT_THREADS_ALL, smem, st, md, w, kv, M, layer, L.global, t_cap);
+}
+
+// Attention with the output projection's activation step fused in (whole
+// 128-value groups per CTA: 2 or 4 query heads per kv head, at most 8 kv
+// heads), for passes of at most FUSE_PREP_MAX_TOKENS tokens, where it saves a
+// launch on the latency path; larger passes keep k_prep, since the cluster
+// over kv heads costs the attention more CTA scheduling freedom than k_prep
+// costs on B200. False when the separate kernel must run.
+// $NEEDLE_B200_FUSE_PREP=0 keeps it always.
+constexpr int FUSE_PREP_MAX_TOKENS = 64;
+bool launch_attend_prep(const ModelDev& md, const LayerDev& L, const Work& w, const KvDev& kv, int M, int layer, int t_cap,
+                        cudaStream_t st) {
+  static const bool off = [] {
+    const char* e = std::getenv("NEEDLE_B200_FUSE_PREP");
+    return e && e[0] == '0';
+  }();
+  const int G = md.heads / md.kv_heads, KV = md.kv_heads;
+  if (off || M > FUSE_PREP_MAX_TOKENS || (G != 2 && G != 4) || KV > ATT_MAX_KV || md.heads * HEAD_DIM != md.d_model) return false;
+  t_pass_tokens = M;
+  const size_t smem = attend_smem(md, t_cap);
+  const dim3 cluster(1, KV, 1);
+  if (G == 2)
+    launch_clustered(k_attend<2, true>, dim3(M, KV), ATT_THREADS_ALL, smem, st, cluster, md, w, kv, M, layer, L.global, t_cap);
+  else
+    launch_clustered(k_attend<4, true>, dim3(M, KV), ATT_THREADS_ALL, smem, st, cluster, md, w, kv, M, layer, L.global, t_cap);
+  return true;
 }
 
 // ------------------------------------------------------------------- debug

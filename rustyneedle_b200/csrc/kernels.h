@@ -26,6 +26,8 @@ void launch_stats(const float* logits, int V, const uint32_t* mask, const int32_
 void launch_advance(nbl::TokenMeta* meta, int B, cudaStream_t st);
 void launch_attend(const nbl::ModelDev& md, const nbl::LayerDev& L, const nbl::Work& w, const nbl::KvDev& kv, int M, int layer,
                    int t_cap, cudaStream_t st);
+bool launch_attend_prep(const nbl::ModelDev& md, const nbl::LayerDev& L, const nbl::Work& w, const nbl::KvDev& kv, int M, int layer,
+                        int t_cap, cudaStream_t st);
 void launch_debug_hadamard(const nbl::ModelDev& md, const nbl::LayerDev& L, const float* in, float* out, int M, cudaStream_t st);
 void launch_debug_math(int op, const float* in, float* out, int n, cudaStream_t st);
 void launch_debug_project(const nbl::ModelDev& md, const nbl::QMat& W, const float* in, int K, int M, int8_t* act,

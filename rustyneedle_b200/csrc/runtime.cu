@@ -1393,15 +1393,21 @@ extern "C" nb_status nb_debug_time_attention(nb_batch* batch, uint32_t reps, flo
     NB_CUDA(cudaMemcpyAsync(batch->d_meta, hm, B * sizeof(TokenMeta), cudaMemcpyHostToDevice, E.stream));
     Work w = E.work;
     w.meta = batch->d_meta;
+    if (batch->groups == 1) w.order = batch->d_order;  // the step's launch order (per group otherwise)
     KvDev kv = E.kv();
+    // the attention kernel the step runs (with the output projection's activation step fused in where it is)
+    auto attend = [&](int32_t layer) {
+      if (!nbk::launch_attend_prep(E.md, E.layers[layer], w, kv, (int)B, layer, E.t_cap, E.stream))
+        nbk::launch_attend(E.md, E.layers[layer], w, kv, (int)B, layer, E.t_cap, E.stream);
+    };
     cudaEvent_t start, stop;
     NB_CUDA(cudaEventCreate(&start));
     NB_CUDA(cudaEventCreate(&stop));
     // one untimed round warms the caches the way the step does
-    for (int32_t layer : batch->active) nbk::launch_attend(E.md, E.layers[layer], w, kv, (int)B, layer, E.t_cap, E.stream);
+    for (int32_t layer : batch->active) attend(layer);
     NB_CUDA(cudaEventRecord(start, E.stream));
     for (uint32_t r = 0; r < reps; ++r)
-      for (int32_t layer : batch->active) nbk::launch_attend(E.md, E.layers[layer], w, kv, (int)B, layer, E.t_cap, E.stream);
+      for (int32_t layer : batch->active) attend(layer);
     NB_CUDA(cudaEventRecord(stop, E.stream));
     NB_CUDA(cudaEventSynchronize(stop));
     NB_CUDA(cudaGetLastError());
