@@ -58,6 +58,8 @@ def parse():
     p.add_argument("--no-cpu", action="store_true")
     p.add_argument("--profile", action="store_true", help="64 sequences, no extras: the small case for ncu captures")
     p.add_argument("--batch1-only", action="store_true", help="only the batch-1 configuration (ncu launch lists)")
+    p.add_argument("--products", action="store_true",
+                   help="the product microbenchmark (config 3) instead of decoding: one JSON line of GOP/s per shape")
     return p.parse_args()
 
 
@@ -188,10 +190,39 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+PRODUCT_SHAPES = [(512, 2048, 2), (2048, 512, 2), (512, 8192, 4)]  # (K, N, code bits)
+PRODUCT_TOKENS = [1, 8, 64, 256, 4096]
+
+
+def products(args):
+    """Config 3: int8 codebook products M x K -> N through nb_debug_product,
+    the product kernel alone timed with CUDA events (activations quantised and
+    resident), against twice the measured bf16 tensor peak (int8 dense rate)."""
+    from rustyneedle_b200 import debug, synthetic
+
+    peaks, peak_kind = measured_peaks()
+    int8_peak = 2.0 * peaks["bf16_tflops"]
+    rows = []
+    for cols, n, bits in PRODUCT_SHAPES:
+        packed, levels, norms = synthetic.product_matrix(seed=cols + n, rows=n, columns=cols, bits=bits)
+        for m in PRODUCT_TOKENS:
+            x = np.random.default_rng(m).standard_normal((m, cols)).astype(np.float32)
+            _, ms = debug.product(bits, packed, levels, norms, n, cols, x, reps=max(3, args.steps))
+            tops = 2.0 * m * cols * n / (ms / 1000.0) / 1e12
+            weight_gbs = n * cols / (ms / 1000.0) / 1e9  # int8 weight bytes per product
+            rows.append({"M": m, "K": cols, "N": n, "bits": bits, "us": round(ms * 1000.0, 2), "TOP/s": round(tops, 2),
+                         "frac_int8_tensor": round(tops / int8_peak, 4), "weight_GB/s": round(weight_gbs, 1)})
+    print(json.dumps({"metric": "codebook int8 product throughput (config 3)", "unit": "TOP/s", "impl": "b200",
+                      "peak": {"int8_tensor_TOPs": int8_peak, "source": f"2 x {peak_kind} bf16_tflops"},
+                      "data": "synthetic", "products": rows}), flush=True)
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         return run_reference(args)
+    if args.products:
+        return products(args)
     import rustyneedle_b200 as nb
     from rustyneedle_b200 import debug, dp, synthetic
 

@@ -29,6 +29,17 @@ nb_status nb_debug_project(nb_model* model, int which, uint32_t layer, const flo
  * on `count` inputs of d_model values. */
 nb_status nb_debug_hadamard(nb_model* model, uint32_t layer, const float* in, size_t count, float* out);
 
+/* The product microbenchmark (no model): QuantisedMatrix::prepare +
+ * multiply_vector (crates/kernels/src/matrix.rs:123-165) of `count` inputs
+ * through a matrix given in the archive's representation — packed bits-wide
+ * indices per row (rows × cols·bits/8 bytes, matrix.rs:622-631), the 2^bits
+ * codebook levels and fp16 norms per 128-column group — on device `device`.
+ * bits 2 or 4, cols 512 or 2048. in: count × cols floats; out: count × rows
+ * floats. With reps > 0, *ms_per_product (may be NULL) receives the mean device
+ * time of the product kernel alone, activations already quantised. */
+nb_status nb_debug_product(int device, uint32_t bits, const uint8_t* packed, const float* levels, const uint16_t* norms, uint32_t rows,
+                           uint32_t cols, const float* in, uint32_t count, float* out, uint32_t reps, float* ms_per_product);
+
 /* The session's final hidden state (session.rs:140-143): d_model floats. */
 nb_status nb_debug_hidden(nb_session* session, float* out);
 

@@ -1619,6 +1619,38 @@ int nbo_matrix_product(const nbo_model* model, int tensor, const float* input, s
   });
 }
 
+// The product of a matrix given in the archive's representation (packed
+// bits-wide indices per row, the 2^bits codebook levels, fp16 norms per
+// 128-column group) through the same QMatrix code as the archive path.
+int nbo_product_raw(int mode, uint32_t bits, const uint8_t* packed, const float* levels, const uint16_t* norms, size_t rows,
+                    size_t cols, const float* input, float* out, int32_t* sums) {
+  return guard([&] {
+    if ((bits != 2 && bits != 4) || cols % 128 != 0 || !packed || !levels || !norms || !input || !out)
+      throw Failure(ERR_ARGUMENT, "a raw product takes 2- or 4-bit codes and a multiple of 128 columns");
+    std::vector<float> cb(28, 0.0f);
+    for (uint32_t i = 0; i < (1u << bits); ++i) cb[(bits == 2 ? 0 : 12) + i] = levels[i];
+    QMatrix m;
+    m.packed = packed;
+    m.rows = rows;
+    m.columns = m.padded = cols;
+    m.group = 128;
+    m.record_bits = bits;
+    m.row_bytes = cols * bits / 8;
+    m.groups = cols / 128;
+    m.table = lookup_table(bits, cb, 128);
+    m.ilevels = integer_levels(m.table);
+    m.norms.resize(rows * m.groups);
+    for (size_t i = 0; i < m.norms.size(); ++i) m.norms[i] = half_to_f32(norms[i]);
+    std::vector<float> rotated = m.prepare(input);
+    if (mode == NBO_MODE_INT && m.integer_path(NBO_MODE_INT)) {
+      GroupInput in = quantise_groups(rotated.data(), m.padded, m.group);
+      for (size_t r = 0; r < rows; ++r) out[r] = m.row_integer(r, in, sums ? sums + r * m.groups : nullptr);
+    } else {
+      for (size_t r = 0; r < rows; ++r) out[r] = m.row_float(r, rotated.data());
+    }
+  });
+}
+
 int nbo_matrix_dequantise_row(const nbo_model* model, int tensor, size_t row, float* out) {
   return guard([&] {
     QMatrix m = load_matrix(*model->archive, (size_t)tensor);

@@ -99,6 +99,13 @@ int nbo_matrix_product(const nbo_model* model, int tensor, const float* input, s
 int nbo_matrix_dequantise_row(const nbo_model* model, int tensor, size_t row, float* out);
 /* Shape of archive tensor `tensor`: kind, rows, columns, group, bits. */
 int nbo_tensor_info(const nbo_model* model, int tensor, int64_t* out5);
+/* A codebook product of one input through a matrix given in the archive's
+ * representation (QuantisedMatrix, crates/kernels/src/matrix.rs:123-165):
+ * packed bits-wide indices (rows × cols·bits/8 bytes), the 2^bits levels and
+ * fp16 norms per 128-column group; mode NBO_MODE_INT or NBO_MODE_FLOAT.
+ * sums (may be NULL) receives the INT path's per-group int32 sums. */
+int nbo_product_raw(int mode, uint32_t bits, const uint8_t* packed, const float* levels, const uint16_t* norms, size_t rows,
+                    size_t cols, const float* input, float* out, int32_t* sums);
 /* HadamardWeights::apply of one layer (crates/model/src/hadamard.rs:260-304). */
 int nbo_hadamard_apply(const nbo_model* model, int layer, const float* input, float* out);
 

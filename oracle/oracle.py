@@ -78,6 +78,7 @@ def _declare(L: ctypes.CDLL) -> None:
         "nbo_half_to_f32": (F, [ctypes.c_uint16]),
         "nbo_matrix_product": (I, [P, I, P, SZ, SZ, P, P]),
         "nbo_matrix_dequantise_row": (I, [P, I, SZ, P]),
+        "nbo_product_raw": (I, [I, U32, P, P, P, SZ, SZ, P, P, P]),
         "nbo_tensor_info": (I, [P, I, P]),
         "nbo_hadamard_apply": (I, [P, I, P, P]),
     }
@@ -227,6 +228,21 @@ def sessions_step(sessions: list[Session], tokens, threads: int = 0, want_logits
     vocab = sessions[0].model.output_vocab
     out = np.zeros((len(sessions), vocab), dtype=np.float32) if want_logits else None
     lib().nbo_sessions_step(handles, len(sessions), _ptr(t), _ptr(out) if out is not None else None, threads)
+    return out
+
+
+def product_raw(mode: int, bits: int, packed: np.ndarray, levels: np.ndarray, norms: np.ndarray, rows: int, cols: int,
+                x: np.ndarray) -> np.ndarray:
+    """A codebook product through a matrix in the archive's representation
+    (packed indices, levels, fp16 norms as uint16) for one input row."""
+    p = np.ascontiguousarray(packed, dtype=np.uint8)
+    lv = np.ascontiguousarray(levels, dtype=np.float32)
+    nm = np.ascontiguousarray(norms, dtype=np.uint16)
+    xv = np.ascontiguousarray(x, dtype=np.float32)
+    out = np.zeros(rows, dtype=np.float32)
+    status = lib().nbo_product_raw(mode, bits, _ptr(p), _ptr(lv), _ptr(nm), rows, cols, _ptr(xv), _ptr(out), None)
+    if status != 0:
+        raise RuntimeError(lib().nbo_last_error().decode())
     return out
 
 

@@ -19,6 +19,7 @@
 #include <cooperative_groups.h>
 #include <cuda_runtime.h>
 
+#include <cmath>
 #include <cstdlib>
 #include <mutex>
 #include <utility>
@@ -379,11 +380,15 @@ __device__ __forceinline__ uint64_t umma_desc(uint32_t addr, uint32_t lbo, uint3
          (1ull << 46);
 }
 
-template <int NT>
+// K = 512 · KCH (KCH chunks of the K-chunk-major layout, one after another:
+// the weight tile and the activation block of chunk c are copied, its 16 MMAs
+// accumulate groups 4c..4c+3, and the next chunk's copy starts once they have
+// completed). The epilogue combines the groups in order.
+template <int NT, int KCH>
 __global__ void __launch_bounds__(8 * NT) k_gemm(QMat W, const int8_t* __restrict__ act, const float* __restrict__ act_scale,
                                               float* __restrict__ out, int M, int out_stride, const TokenMeta* __restrict__ meta,
-                                              int* __restrict__ error) {
-  constexpr int GK = GEMM_K / GROUP;
+                                              int* __restrict__ error, int act_rows) {
+  constexpr int GK = KCH * (GEMM_K / GROUP);
   constexpr uint32_t COLS = GK * NT;  // TMEM columns: one NT-wide accumulator per group
   constexpr uint32_t A_BYTES = GEMM_ROWS * GEMM_K, B_BYTES = NT * GEMM_K;
   // instruction descriptor: D s32, A and B s8, both K-major, N = NT, M = 128
@@ -398,12 +403,23 @@ __global__ void __launch_bounds__(8 * NT) k_gemm(QMat W, const int8_t* __restric
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int tile = blockIdx.x, m0 = blockIdx.y * NT, mcount = min(NT, M - m0);
   const uint32_t bar_load = smem_u32(&bars[0]), bar_mma = smem_u32(&bars[1]);
+  const size_t rows_cap = ((size_t)W.rows + GEMM_ROWS - 1) / GEMM_ROWS * GEMM_ROWS;
+  constexpr uint32_t PIECE = 16384;
+  auto copy = [&](uint8_t* dst, const uint8_t* src, uint32_t bytes) {
+    for (uint32_t off = 0; off < bytes; off += PIECE)
+      asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(dst + off)),
+                   "l"(src + off), "r"(min(PIECE, bytes - off)), "r"(bar_load)
+                   : "memory");
+  };
+  auto weights = [&](int c) { return reinterpret_cast<const uint8_t*>(W.codes) + (size_t)c * rows_cap * GEMM_K + (size_t)tile * A_BYTES; };
+  auto tokens = [&](int c) {
+    return reinterpret_cast<const uint8_t*>(act) + (size_t)c * act_rows * GEMM_K + (size_t)(m0 / 8) * (8 * GEMM_K);
+  };
 
   if (warp == 0) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s_tmem)), "r"(COLS) : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
-  constexpr uint32_t PIECE = 16384;
   if (tid == 0) {
     s_fail = 0;
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar_load), "r"(1) : "memory");
@@ -412,11 +428,7 @@ __global__ void __launch_bounds__(8 * NT) k_gemm(QMat W, const int8_t* __restric
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     // the weight tile is constant: its copy starts before the previous kernel has finished
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar_load), "r"(A_BYTES + B_BYTES) : "memory");
-    const uint8_t* ga = reinterpret_cast<const uint8_t*>(W.codes) + (size_t)tile * A_BYTES;
-    for (uint32_t off = 0; off < A_BYTES; off += PIECE)
-      asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(sA + off)),
-                   "l"(ga + off), "r"(min(PIECE, A_BYTES - off)), "r"(bar_load)
-                   : "memory");
+    copy(sA, weights(0), A_BYTES);
   }
   // this thread's output row and its per-group weight scales (constant)
   const int quad = warp & 3, slice = warp >> 2;
@@ -426,73 +438,78 @@ __global__ void __launch_bounds__(8 * NT) k_gemm(QMat W, const int8_t* __restric
 #pragma unroll
   for (int g = 0; g < GK; ++g) ws[g] = valid ? W.scales[(size_t)row * GK + g] : 0.0f;
   pdl_wait();
-  if (tid == 0) {
-    const uint8_t* gb = reinterpret_cast<const uint8_t*>(act) + (size_t)(m0 / 8) * (8 * GEMM_K);
-    for (uint32_t off = 0; off < B_BYTES; off += PIECE)
-      asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(sB + off)),
-                   "l"(gb + off), "r"(min(PIECE, B_BYTES - off)), "r"(bar_load)
-                   : "memory");
-  }
+  if (tid == 0) copy(sB, tokens(0), B_BYTES);
   for (int i = tid; i < NT * GK; i += blockDim.x) s_as[i] = i / GK < mcount ? act_scale[(size_t)m0 * GK + i] : 0.0f;
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem = s_tmem;
 
-  bool ok = mbar_wait(bar_load, 0);
-  if (ok && warp == 0) {
-    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    if (lane == 0) {
-      const uint32_t a0 = smem_u32(sA), b0 = smem_u32(sB);
-#pragma unroll
-      for (int g = 0; g < GK; ++g)
-#pragma unroll
-        for (int s = 0; s < 4; ++s) {
-          const int step = g * 4 + s;  // K bytes 32·step .. 32·step+31 = chunks 2·step, 2·step+1
-          const uint64_t da = umma_desc(a0 + step * 256, 128, GEMM_KC * 128);
-          const uint64_t db = umma_desc(b0 + step * 256, 128, GEMM_KC * 128);
-          const uint32_t d_tmem = tmem + g * NT, accumulate = s > 0 ? 1u : 0u;
-          asm volatile(
-              "{\n\t.reg .pred p;\n\t"
-              "setp.ne.b32 p, %4, 0;\n\t"
-              "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}" ::"r"(d_tmem),
-              "l"(da), "l"(db), "r"(IDESC), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
-              : "memory");
-        }
-      asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar_mma) : "memory");
+  bool ok = true;
+#pragma unroll 1
+  for (int c = 0; c < KCH; ++c) {
+    if (c > 0 && tid == 0) {
+      // chunk c - 1's MMAs have completed (every thread waited for them): its smem is free
+      asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar_load), "r"(A_BYTES + B_BYTES) : "memory");
+      copy(sA, weights(c), A_BYTES);
+      copy(sB, tokens(c), B_BYTES);
     }
-    __syncwarp();
+    if (ok) ok = mbar_wait(bar_load, c & 1);
+    if (ok && warp == 0) {
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      if (lane == 0) {
+        const uint32_t a0 = smem_u32(sA), b0 = smem_u32(sB);
+#pragma unroll
+        for (int g = 0; g < GEMM_K / GROUP; ++g)
+#pragma unroll
+          for (int s = 0; s < 4; ++s) {
+            const int step = g * 4 + s;  // K bytes 32·step .. 32·step+31 = chunks 2·step, 2·step+1
+            const uint64_t da = umma_desc(a0 + step * 256, 128, GEMM_KC * 128);
+            const uint64_t db = umma_desc(b0 + step * 256, 128, GEMM_KC * 128);
+            const uint32_t d_tmem = tmem + (c * (GEMM_K / GROUP) + g) * NT, accumulate = s > 0 ? 1u : 0u;
+            asm volatile(
+                "{\n\t.reg .pred p;\n\t"
+                "setp.ne.b32 p, %4, 0;\n\t"
+                "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}" ::"r"(d_tmem),
+                "l"(da), "l"(db), "r"(IDESC), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
+                : "memory");
+          }
+        asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar_mma) : "memory");
+      }
+      __syncwarp();
+    }
+    if (ok) ok = mbar_wait(bar_mma, c & 1);
   }
-  if (ok) ok = mbar_wait(bar_mma, 0);
   if (!ok) s_fail = 1;
   pdl_trigger();  // the epilogue overlaps the next kernel's prologue
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   __syncthreads();
   if (!s_fail) {
     const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16);
-    {
-      const int c0 = slice * 16;
-      uint32_t a[GK][16];
+    const int c0 = slice * 16;
+    float total[16];
 #pragma unroll
-      for (int g = 0; g < GK; ++g)
-        asm volatile(
-            "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
-            : "=r"(a[g][0]), "=r"(a[g][1]), "=r"(a[g][2]), "=r"(a[g][3]), "=r"(a[g][4]), "=r"(a[g][5]), "=r"(a[g][6]), "=r"(a[g][7]),
-              "=r"(a[g][8]), "=r"(a[g][9]), "=r"(a[g][10]), "=r"(a[g][11]), "=r"(a[g][12]), "=r"(a[g][13]), "=r"(a[g][14]), "=r"(a[g][15])
-            : "r"(lane_base + g * NT + c0));
+    for (int j = 0; j < 16; ++j) total[j] = 0.0f;
+#pragma unroll
+    for (int g = 0; g < GK; ++g) {
+      uint32_t a[16];
+      asm volatile(
+          "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+          : "=r"(a[0]), "=r"(a[1]), "=r"(a[2]), "=r"(a[3]), "=r"(a[4]), "=r"(a[5]), "=r"(a[6]), "=r"(a[7]), "=r"(a[8]), "=r"(a[9]),
+            "=r"(a[10]), "=r"(a[11]), "=r"(a[12]), "=r"(a[13]), "=r"(a[14]), "=r"(a[15])
+          : "r"(lane_base + g * NT + c0));
       asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
-        const int n = c0 + j;
-        float total = 0.0f;
-#pragma unroll
-        for (int g = 0; g < GK; ++g) {
-          const float acc = (float)(int)a[g][j];
-          const float as = s_as[n * GK + g];
-          total = W.fused ? __fmaf_rn(acc, fmul(ws[g], as), total) : fadd(total, fmul(fmul(fmul(acc, ws[g]), W.level_scale), as));
-        }
-        if (valid && n < mcount && !(meta && meta[m0 + n].slot < 0)) out[(size_t)(m0 + n) * out_stride + row] = total;
+        const float acc = (float)(int)a[j];
+        const float as = s_as[(c0 + j) * GK + g];
+        total[j] = W.fused ? __fmaf_rn(acc, fmul(ws[g], as), total[j]) : fadd(total[j], fmul(fmul(fmul(acc, ws[g]), W.level_scale), as));
       }
+    }
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const int n = c0 + j;
+      if (valid && n < mcount && !(meta && meta[m0 + n].slot < 0)) out[(size_t)(m0 + n) * out_stride + row] = total[j];
     }
   } else if (tid == 0) {
     atomicExch(error, 1);
@@ -505,25 +522,30 @@ __global__ void __launch_bounds__(8 * NT) k_gemm(QMat W, const int8_t* __restric
 // -------------------------------------------------------------------- gemv
 // The same product for a few tokens (decode at small batch) as a memory-bound
 // int8 GEMV on the CUDA cores. A warp owns one 8-row block of the
-// core-matrix layout (4 KB contiguous: eight coalesced 16-byte loads per
-// lane). Lane l serves row l%8 and the 16-byte chunks c = 4j + l/8, so the
-// exact int32 sum of each 128-column group (chunks 8g..8g+7) is two dp4a
-// chains per lane, reduced over the row's four lanes. Every token's
-// activations sit in shared memory; the output is the ordered per-group
-// combine of k_gemm's epilogue.
+// core-matrix layout (4 KB contiguous per 512-column chunk: eight coalesced
+// 16-byte loads per lane). Lane l serves row l%8 and the 16-byte chunks
+// c = 4j + l/8, so the exact int32 sum of each 128-column group (chunks
+// 8g..8g+7) is two dp4a chains per lane, reduced over the row's four lanes.
+// Every token's activations sit in shared memory; the output is the ordered
+// per-group combine of k_gemm's epilogue (carried across chunks in shared
+// memory when K > 512).
 constexpr int GEMV_WARPS = 2;
 constexpr int GEMV_MAX_TOKENS = 8;
 
+template <int KCH>
 __global__ void __launch_bounds__(GEMV_WARPS * 32) k_gemv(QMat W, const int8_t* __restrict__ act, const float* __restrict__ act_scale,
                                                         float* __restrict__ out, int M, int out_stride,
-                                                        const TokenMeta* __restrict__ meta) {
-  constexpr int GK = GEMM_K / GROUP;
-  __shared__ __align__(16) uint8_t s_act[GEMV_MAX_TOKENS][GEMM_K];
+                                                        const TokenMeta* __restrict__ meta, int act_rows) {
+  constexpr int GC = GEMM_K / GROUP;  // groups per chunk
+  constexpr int GK = KCH * GC;
+  __shared__ __align__(16) uint8_t s_act[GEMV_MAX_TOKENS][KCH * GEMM_K];
   __shared__ float s_as[GEMV_MAX_TOKENS][GK];
+  __shared__ float s_tot[KCH > 1 ? GEMV_MAX_TOKENS : 1][GEMV_WARPS * 8];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int block = blockIdx.x * GEMV_WARPS + warp;
   const int row = block * 8 + (lane & 7), q = lane >> 3;
   const bool live = block * 8 < (int)W.rows;  // storage rows are padded to 128, so a live block is whole
+  const size_t rows_cap = ((size_t)W.rows + GEMM_ROWS - 1) / GEMM_ROWS * GEMM_ROWS;
   uint4 wv[8];
   float ws[GK];
   if (live) {
@@ -534,39 +556,50 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32) k_gemv(QMat W, const int8_t* 
 #pragma unroll
   for (int g = 0; g < GK; ++g) ws[g] = row < (int)W.rows ? W.scales[(size_t)row * GK + g] : 0.0f;
   pdl_wait();
-  for (int i = threadIdx.x; i < M * GEMM_KC; i += blockDim.x) {
-    const int t = i / GEMM_KC, c = i % GEMM_KC;
-    *reinterpret_cast<uint4*>(&s_act[t][c * 16]) = *reinterpret_cast<const uint4*>(act + core_offset(t, c * 16, GEMM_KC));
+  for (int i = threadIdx.x; i < M * KCH * GEMM_KC; i += blockDim.x) {
+    const int t = i / (KCH * GEMM_KC), k = (i % (KCH * GEMM_KC)) * 16;
+    *reinterpret_cast<uint4*>(&s_act[t][k]) = *reinterpret_cast<const uint4*>(act + chunked_offset(t, k, act_rows));
   }
   for (int i = threadIdx.x; i < M * GK; i += blockDim.x) s_as[i / GK][i % GK] = act_scale[i];
   __syncthreads();
   if (!live) return;
-  for (int t = 0; t < M; ++t) {
-    int acc[GK];
+#pragma unroll 1
+  for (int c = 0; c < KCH; ++c) {
+    if (c > 0) {
+      const uint4* src = reinterpret_cast<const uint4*>(W.codes + (size_t)c * rows_cap * GEMM_K + (size_t)block * 8 * GEMM_K);
 #pragma unroll
-    for (int g = 0; g < GK; ++g) acc[g] = 0;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const uint4 a = *reinterpret_cast<const uint4*>(&s_act[t][(4 * j + q) * 16]);
-      const int g = j >> 1;
-      acc[g] = dp4a(wv[j].x, a.x, acc[g]);
-      acc[g] = dp4a(wv[j].y, a.y, acc[g]);
-      acc[g] = dp4a(wv[j].z, a.z, acc[g]);
-      acc[g] = dp4a(wv[j].w, a.w, acc[g]);
+      for (int j = 0; j < 8; ++j) wv[j] = src[j * 32 + lane];
     }
+    for (int t = 0; t < M; ++t) {
+      int acc[GC];
 #pragma unroll
-    for (int g = 0; g < GK; ++g) {
-      acc[g] += __shfl_xor_sync(FULL, acc[g], 8);
-      acc[g] += __shfl_xor_sync(FULL, acc[g], 16);
-    }
-    if (q == 0 && row < (int)W.rows && !(meta && meta[t].slot < 0)) {
-      float total = 0.0f;
+      for (int g = 0; g < GC; ++g) acc[g] = 0;
 #pragma unroll
-      for (int g = 0; g < GK; ++g) {
-        const float a = (float)acc[g], as = s_as[t][g];
-        total = W.fused ? __fmaf_rn(a, fmul(ws[g], as), total) : fadd(total, fmul(fmul(fmul(a, ws[g]), W.level_scale), as));
+      for (int j = 0; j < 8; ++j) {
+        const uint4 a = *reinterpret_cast<const uint4*>(&s_act[t][c * GEMM_K + (4 * j + q) * 16]);
+        const int g = j >> 1;
+        acc[g] = dp4a(wv[j].x, a.x, acc[g]);
+        acc[g] = dp4a(wv[j].y, a.y, acc[g]);
+        acc[g] = dp4a(wv[j].z, a.z, acc[g]);
+        acc[g] = dp4a(wv[j].w, a.w, acc[g]);
       }
-      out[(size_t)t * out_stride + row] = total;
+#pragma unroll
+      for (int g = 0; g < GC; ++g) {
+        acc[g] += __shfl_xor_sync(FULL, acc[g], 8);
+        acc[g] += __shfl_xor_sync(FULL, acc[g], 16);
+      }
+      if (q == 0 && row < (int)W.rows) {
+        float total = KCH > 1 && c > 0 ? s_tot[KCH > 1 ? t : 0][warp * 8 + lane] : 0.0f;
+#pragma unroll
+        for (int g = 0; g < GC; ++g) {
+          const float a = (float)acc[g], as = s_as[t][c * GC + g], w = ws[c * GC + g];
+          total = W.fused ? __fmaf_rn(a, fmul(w, as), total) : fadd(total, fmul(fmul(fmul(a, w), W.level_scale), as));
+        }
+        if (c + 1 < KCH)
+          s_tot[KCH > 1 ? t : 0][warp * 8 + lane] = total;
+        else if (!(meta && meta[t].slot < 0))
+          out[(size_t)t * out_stride + row] = total;
+      }
     }
   }
 }
@@ -947,12 +980,14 @@ __global__ void __launch_bounds__(ATT_THREADS_ALL, 3) k_attend(ModelDev md, Work
 // (when `fake`) → per-group rotation and int8 codes. Used for out_proj
 // (attention.rs:145-150) and the logits (session.rs:170-175). grid M, block
 // 128; four consecutive values per thread and pass.
+constexpr int PREP_MAX_K = 2048;
+
 __global__ void __launch_bounds__(128) k_prep(const float* __restrict__ in, int in_stride, const int32_t* __restrict__ rows,
                                               const float* __restrict__ gate, int gate_stride, int K, int8_t* __restrict__ act,
                                               float* __restrict__ act_scale, int M, const TokenMeta* __restrict__ meta,
-                                              float inv_sqrt_group, int fake) {
+                                              float inv_sqrt_group, int fake, int act_rows) {
   pdl_wait();
-  __shared__ __align__(16) float s_v[MAX_D];
+  __shared__ __align__(16) float s_v[PREP_MAX_K];
   __shared__ float s_red[4];
   const int t = blockIdx.x;
   if (t >= M || (meta && meta[t].slot < 0)) return;
@@ -979,7 +1014,7 @@ __global__ void __launch_bounds__(128) k_prep(const float* __restrict__ in, int 
     fwht128(v, inv_sqrt_group);
     uint32_t packed;
     const float sc = quantise_group(v, packed);
-    *reinterpret_cast<uint32_t*>(act + core_offset(t, g * GROUP + 4 * lane, K / 16)) = packed;
+    *reinterpret_cast<uint32_t*>(act + chunked_offset(t, g * GROUP + 4 * lane, act_rows)) = packed;
     if (lane == 0) act_scale[(size_t)t * groups + g] = sc;
   }
 }
@@ -1466,8 +1501,10 @@ cudaError_t configure(const ModelDev& md, int t_cap) {
   if ((e = cudaFuncSetAttribute(k_block<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)block_smem(md)))) return e;
   if ((e = cudaFuncSetAttribute(k_block<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)block_smem(md)))) return e;
   if ((e = cudaFuncSetAttribute(k_stats, cudaFuncAttributeMaxDynamicSharedMemorySize, 2 * 8192 * 4))) return e;
-  if ((e = cudaFuncSetAttribute(k_gemm<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gemm_smem<16>()))) return e;
-  if ((e = cudaFuncSetAttribute(k_gemm<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gemm_smem<32>()))) return e;
+  if ((e = cudaFuncSetAttribute(k_gemm<16, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gemm_smem<16>()))) return e;
+  if ((e = cudaFuncSetAttribute(k_gemm<32, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gemm_smem<32>()))) return e;
+  if ((e = cudaFuncSetAttribute(k_gemm<16, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gemm_smem<16>()))) return e;
+  if ((e = cudaFuncSetAttribute(k_gemm<32, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gemm_smem<32>()))) return e;
 
   return cudaSuccess;
 }
@@ -1520,17 +1557,28 @@ static void launch(void (*kernel)(P...), dim3 grid, dim3 block, size_t smem, cud
   launch_clustered(kernel, grid, block, smem, st, dim3(1, 1, 1), std::forward<A>(args)...);
 }
 
+// One codebook product of M tokens through W (K = W.cols: 512, or 2048 in the
+// product benchmark): the CUDA-core GEMV for a few tokens, else tcgen05 tiles
+// of 16 or 32 tokens. act_rows is the row capacity of the activation buffer
+// (it places the chunks of K > 512).
 static void project(const QMat& W, const int8_t* act, const float* act_scale, float* out, int M, int out_stride,
-                    const TokenMeta* meta, cudaStream_t st) {
+                    const TokenMeta* meta, cudaStream_t st, int act_rows = 0, int* error = nullptr) {
+  if (!error) error = g_gemm_error;
   const int tiles = (W.rows + GEMM_ROWS - 1) / GEMM_ROWS;
+  const bool wide = W.cols == 4 * GEMM_K;
   if (M <= GEMV_MAX_TOKENS) {
-    const int blocks = (W.rows + 7) / 8;
-    launch(k_gemv, (blocks + GEMV_WARPS - 1) / GEMV_WARPS, GEMV_WARPS * 32, 0, st, W, act, act_scale, out, M, out_stride, meta);
-  } else if (M <= 16)
-    launch(k_gemm<16>, dim3(tiles, 1), 8 * 16, gemm_smem<16>(), st, W, act, act_scale, out, M, out_stride, meta, g_gemm_error);
-  else
-    launch(k_gemm<32>, dim3(tiles, (M + 31) / 32), 8 * 32, gemm_smem<32>(), st, W, act, act_scale, out, M, out_stride, meta,
-           g_gemm_error);
+    const int ctas = ((W.rows + 7) / 8 + GEMV_WARPS - 1) / GEMV_WARPS;
+    if (wide)
+      launch(k_gemv<4>, ctas, GEMV_WARPS * 32, 0, st, W, act, act_scale, out, M, out_stride, meta, act_rows);
+    else
+      launch(k_gemv<1>, ctas, GEMV_WARPS * 32, 0, st, W, act, act_scale, out, M, out_stride, meta, act_rows);
+  } else if (M <= 16) {
+    auto k = wide ? k_gemm<16, 4> : k_gemm<16, 1>;
+    launch(k, dim3(tiles, 1), 8 * 16, gemm_smem<16>(), st, W, act, act_scale, out, M, out_stride, meta, error, act_rows);
+  } else {
+    auto k = wide ? k_gemm<32, 4> : k_gemm<32, 1>;
+    launch(k, dim3(tiles, (M + 31) / 32), 8 * 32, gemm_smem<32>(), st, W, act, act_scale, out, M, out_stride, meta, error, act_rows);
+  }
 }
 
 void launch_embed(const ModelDev& md, const Work& w, int M, cudaStream_t st) {
@@ -1550,7 +1598,7 @@ void launch_layer(const ModelDev& md, const LayerDev& L, const Work& w, const Kv
     launch_attend(md, L, w, kv, M, layer, t_cap, st);
     launch(k_prep, M, 128, 0, st, (const float*)w.attn, H * HEAD_DIM, (const int32_t*)nullptr,
            (const float*)(w.proj + (H + 2 * KV) * HEAD_DIM), proj_stride, H * HEAD_DIM, w.act, w.act_scale, M, w.meta,
-           md.inv_sqrt_group, 1);
+           md.inv_sqrt_group, 1, 0);
   }
   project(L.out, w.act, w.act_scale, w.outp, M, d, w.meta, st);
   if (md.hada_left == 64)
@@ -1568,7 +1616,7 @@ void launch_logits(const ModelDev& md, const float* hidden, const int32_t* slots
                    cudaStream_t st) {
   t_pass_tokens = B;
   launch(k_prep, B, 128, 0, st, hidden, (int)md.d_model, slots, (const float*)nullptr, 0, (int)md.d_model, act, act_scale, B,
-         (const TokenMeta*)nullptr, md.inv_sqrt_group, 1);
+         (const TokenMeta*)nullptr, md.inv_sqrt_group, 1, 0);
   project(md.logits, act, act_scale, logits, B, md.output_vocab, nullptr, st);
 }
 
@@ -1679,8 +1727,40 @@ void launch_debug_hadamard(const ModelDev& md, const LayerDev& L, const float* i
 // multiply_vector (matrix.rs:123-165).
 void launch_debug_project(const ModelDev& md, const QMat& W, const float* in, int K, int M, int8_t* act, float* act_scale,
                           float* out, int out_stride, cudaStream_t st) {
-  k_prep<<<M, 128, 0, st>>>(in, K, nullptr, nullptr, 0, K, act, act_scale, M, nullptr, md.inv_sqrt_group, 0);
+  k_prep<<<M, 128, 0, st>>>(in, K, nullptr, nullptr, 0, K, act, act_scale, M, nullptr, md.inv_sqrt_group, 0, 0);
   project(W, act, act_scale, out, M, out_stride, nullptr, st);
+}
+
+// The product benchmark of the test hooks: k_prep (rotation and per-group
+// int8 activations, no fake quantisation) then the product; with reps > 0
+// the product alone is replayed reps times between CUDA events.
+cudaError_t launch_product_bench(const QMat& W, const float* in, int M, int8_t* act, float* act_scale, int act_rows, float* out,
+                                 int* error, int reps, float* ms, cudaStream_t st) {
+  cudaError_t e;
+  if ((e = cudaFuncSetAttribute(k_gemm<16, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gemm_smem<16>()))) return e;
+  if ((e = cudaFuncSetAttribute(k_gemm<32, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gemm_smem<32>()))) return e;
+  if ((e = cudaFuncSetAttribute(k_gemm<16, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gemm_smem<16>()))) return e;
+  if ((e = cudaFuncSetAttribute(k_gemm<32, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gemm_smem<32>()))) return e;
+  t_pass_tokens = M;
+  const int K = (int)W.cols;
+  k_prep<<<M, 128, 0, st>>>(in, K, nullptr, nullptr, 0, K, act, act_scale, M, nullptr, 1.0f / std::sqrt((float)GROUP), 0, act_rows);
+  project(W, act, act_scale, out, M, (int)W.rows, nullptr, st, act_rows, error);
+  if ((e = cudaGetLastError())) return e;
+  *ms = 0.0f;
+  if (reps <= 0) return cudaSuccess;
+  cudaEvent_t start, stop;
+  if ((e = cudaEventCreate(&start))) return e;
+  if ((e = cudaEventCreate(&stop))) return e;
+  cudaEventRecord(start, st);
+  for (int r = 0; r < reps; ++r) project(W, act, act_scale, out, M, (int)W.rows, nullptr, st, act_rows, error);
+  cudaEventRecord(stop, st);
+  e = cudaEventSynchronize(stop);
+  float total = 0.0f;
+  if (e == cudaSuccess) e = cudaEventElapsedTime(&total, start, stop);
+  cudaEventDestroy(start);
+  cudaEventDestroy(stop);
+  *ms = total / (float)reps;
+  return e;
 }
 
 // ------------------------------------------------ allocation-free product
@@ -1726,11 +1806,11 @@ cudaError_t launch_static_project(int device, const ModelDev& md, const QMat& W,
   cudaError_t e = cudaMemsetAsync(flag, 0, sizeof(int), st);
   if (e != cudaSuccess) return e;
   const int K = GEMM_K, tiles = (W.rows + GEMM_ROWS - 1) / GEMM_ROWS;
-  k_prep<<<M, 128, 0, st>>>(in, K, nullptr, nullptr, 0, K, act, act_scale, M, nullptr, md.inv_sqrt_group, 0);
+  k_prep<<<M, 128, 0, st>>>(in, K, nullptr, nullptr, 0, K, act, act_scale, M, nullptr, md.inv_sqrt_group, 0, 0);
   if (M <= 16)
-    k_gemm<16><<<dim3(tiles, 1), 8 * 16, gemm_smem<16>(), st>>>(W, act, act_scale, out, M, (int)W.rows, nullptr, flag);
+    k_gemm<16, 1><<<dim3(tiles, 1), 8 * 16, gemm_smem<16>(), st>>>(W, act, act_scale, out, M, (int)W.rows, nullptr, flag, 0);
   else
-    k_gemm<32><<<dim3(tiles, (M + 31) / 32), 8 * 32, gemm_smem<32>(), st>>>(W, act, act_scale, out, M, (int)W.rows, nullptr, flag);
+    k_gemm<32, 1><<<dim3(tiles, (M + 31) / 32), 8 * 32, gemm_smem<32>(), st>>>(W, act, act_scale, out, M, (int)W.rows, nullptr, flag, 0);
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
   *wait_failed = 0;
   if ((e = cudaMemcpyAsync(wait_failed, flag, sizeof(int), cudaMemcpyDeviceToHost, st)) != cudaSuccess) return e;

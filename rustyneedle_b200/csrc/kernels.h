@@ -33,6 +33,9 @@ void launch_debug_math(int op, const float* in, float* out, int n, cudaStream_t 
 void launch_debug_project(const nbl::ModelDev& md, const nbl::QMat& W, const float* in, int K, int M, int8_t* act,
                           float* act_scale, float* out, int out_stride, cudaStream_t st);
 
+cudaError_t launch_product_bench(const nbl::QMat& W, const float* in, int M, int8_t* act, float* act_scale, int act_rows, float* out,
+                                 int* error, int reps, float* ms, cudaStream_t st);
+
 // The allocation-free product: tokens per call the file-scope scratch holds.
 constexpr int STATIC_MAX_TOKENS = 256;
 // Looks up this device's copy of the scratch once (cudaGetSymbolAddress with

@@ -66,9 +66,18 @@ __host__ __device__ inline size_t core_offset(size_t r, uint32_t k, uint32_t kch
   return ((r >> 3) * kchunks + (k >> 4)) * 128 + (r & 7) * 16 + (k & 15);
 }
 
+// Operands wider than 512 columns are stored K-chunk-major: chunk c (columns
+// 512c .. 512c+511) of all rows (padded to rows_cap) is one block in the
+// core-matrix layout above, so a 128-row tile of one chunk is 64 KB
+// contiguous. For K = 512 this is the plain core-matrix layout.
+constexpr uint32_t KCHUNK = 512;
+__host__ __device__ inline size_t chunked_offset(size_t r, uint32_t k, size_t rows_cap) {
+  return (size_t)(k / KCHUNK) * rows_cap * KCHUNK + core_offset(r, k % KCHUNK, KCHUNK / 16);
+}
+
 // A codebook-quantised matrix in device layout.
 struct QMat {
-  const int8_t* codes;   // int8 in the core-matrix layout (K = 512, rows padded to 128) or row-major (lane maps)
+  const int8_t* codes;   // int8, K-chunk-major core-matrix layout (rows padded to 128), or row-major (lane maps)
   const float* scales;   // [rows][groups]
   float level_scale;     // IntegerLevels::scale
   uint32_t rows, cols, groups;

@@ -325,7 +325,7 @@ static void expand_matrix(const nba::Archive& a, uint32_t index, const Levels& l
     const uint64_t out_row = row + row_offset;
     for (uint64_t c = 0; c < cols; ++c) {
       int8_t v = lv.ints[code_at(src, c, lv.bits)];
-      codes[core ? core_offset(out_row, (uint32_t)c, (uint32_t)(cols / 16)) : out_row * cols + c] = v;
+      codes[core ? chunked_offset(out_row, (uint32_t)c, stored_rows) : out_row * cols + c] = v;
     }
     for (uint64_t g = 0; g < groups; ++g) {
       uint16_t h;
@@ -1320,6 +1320,52 @@ nb_status nb_debug_hadamard(nb_model* model, uint32_t layer, const float* in, si
     NB_CUDA(cudaGetLastError());
     NB_CUDA(cudaMemcpyAsync(out, dout.p, count * d * 4, cudaMemcpyDeviceToHost, E.stream));
     NB_CUDA(cudaStreamSynchronize(E.stream));
+  });
+}
+
+nb_status nb_debug_product(int device, uint32_t bits, const uint8_t* packed, const float* levels, const uint16_t* norms, uint32_t rows,
+                           uint32_t cols, const float* in, uint32_t count, float* out, uint32_t reps, float* ms_per_product) {
+  if (!packed || !levels || !norms || !in || !out || rows == 0 || count == 0 || (cols != 512 && cols != 2048) || (bits != 2 && bits != 4))
+    return NB_ERR_ARGUMENT;
+  return guard([&] {
+    int devices = 0;
+    if (cudaGetDeviceCount(&devices) != cudaSuccess || devices == 0) fail(NB_ERR_NO_DEVICE, "no CUDA device");
+    NB_CUDA(cudaSetDevice(device));
+    std::vector<float> cb(28, 0.0f);
+    for (uint32_t i = 0; i < (1u << bits); ++i) cb[(bits == 2 ? 0 : 12) + i] = levels[i];
+    const Levels lv = levels_for(bits, cb, GROUP);
+    const size_t rows_cap = ((size_t)rows + 127) / 128 * 128, groups = cols / GROUP, act_rows = ((size_t)count + 127) / 128 * 128;
+    const size_t rb = (size_t)cols * bits / 8;
+    std::vector<int8_t> codes(rows_cap * cols, 0);
+    std::vector<float> scales((size_t)rows * groups);
+    for (size_t r = 0; r < rows; ++r) {
+      for (uint32_t c = 0; c < cols; ++c) codes[chunked_offset(r, c, rows_cap)] = lv.ints[code_at(packed + r * rb, c, lv.bits)];
+      for (size_t g = 0; g < groups; ++g) {
+        const float norm = nba::half_to_f32(norms[r * groups + g]);
+        scales[r * groups + g] = lv.fused ? norm * lv.int_scale : norm;
+      }
+    }
+    DeviceTemp<int8_t> dcodes(codes.size()), dact(act_rows * cols);
+    DeviceTemp<float> dscales(scales.size()), din((size_t)count * cols), dact_scale((size_t)count * groups), dout((size_t)count * rows);
+    DeviceTemp<int> derr(1);
+    cudaStream_t st;
+    NB_CUDA(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking));
+    NB_CUDA(cudaMemcpyAsync(dcodes.p, codes.data(), codes.size(), cudaMemcpyHostToDevice, st));
+    NB_CUDA(cudaMemcpyAsync(dscales.p, scales.data(), scales.size() * 4, cudaMemcpyHostToDevice, st));
+    NB_CUDA(cudaMemcpyAsync(din.p, in, (size_t)count * cols * 4, cudaMemcpyHostToDevice, st));
+    NB_CUDA(cudaMemsetAsync(dact.p, 0, act_rows * cols, st));
+    NB_CUDA(cudaMemsetAsync(derr.p, 0, sizeof(int), st));
+    const QMat W{dcodes.p, dscales.p, lv.int_scale, rows, cols, (uint32_t)groups, lv.fused ? 1 : 0};
+    float ms = 0.0f;
+    cudaError_t e = nbk::launch_product_bench(W, din.p, (int)count, dact.p, dact_scale.p, (int)act_rows, dout.p, derr.p, (int)reps, &ms, st);
+    int err = 0;
+    if (e == cudaSuccess) e = cudaMemcpyAsync(out, dout.p, (size_t)count * rows * 4, cudaMemcpyDeviceToHost, st);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(&err, derr.p, sizeof(int), cudaMemcpyDeviceToHost, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    cudaStreamDestroy(st);
+    NB_CUDA(e);
+    if (err) fail(NB_ERR_TIMEOUT, "a bounded wait of the tensor-core product gave up");
+    if (ms_per_product) *ms_per_product = ms;
   });
 }
 

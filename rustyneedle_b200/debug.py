@@ -28,6 +28,7 @@ def _declare() -> None:
         "nb_debug_hadamard": [P, U32, P, SZ, P],
         "nb_debug_kv": [P, U32, P, P, P, P],
         "nb_debug_time_attention": [P, U32, ctypes.POINTER(ctypes.c_float), ctypes.POINTER(ctypes.c_double)],
+        "nb_debug_product": [I, U32, P, P, P, U32, U32, P, U32, P, U32, ctypes.POINTER(ctypes.c_float)],
     }.items():
         fn = getattr(L, name)
         fn.restype = I
@@ -85,3 +86,19 @@ def time_attention(batch, reps: int = 5):
     ms, nbytes = ctypes.c_float(), ctypes.c_double()
     _check(lib().nb_debug_time_attention(batch._h, reps, ctypes.byref(ms), ctypes.byref(nbytes)))
     return float(ms.value), float(nbytes.value)
+
+
+def product(bits: int, packed: np.ndarray, levels: np.ndarray, norms: np.ndarray, rows: int, cols: int, x: np.ndarray,
+            reps: int = 0, device: int = 0):
+    """The product microbenchmark: outputs (count × rows) and, with reps > 0,
+    the mean device milliseconds of the product kernel alone."""
+    _declare()
+    p = np.ascontiguousarray(packed, dtype=np.uint8)
+    lv = np.ascontiguousarray(levels, dtype=np.float32)
+    nm = np.ascontiguousarray(norms, dtype=np.uint16)
+    xv = np.ascontiguousarray(np.atleast_2d(x), dtype=np.float32)
+    out = np.empty((xv.shape[0], rows), dtype=np.float32)
+    ms = ctypes.c_float()
+    _check(lib().nb_debug_product(device, bits, _ptr(p), _ptr(lv), _ptr(nm), rows, cols, _ptr(xv), xv.shape[0], _ptr(out), reps,
+                                  ctypes.byref(ms)))
+    return out, float(ms.value)

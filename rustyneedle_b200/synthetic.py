@@ -92,11 +92,7 @@ class _Writer:
         return self.add(KIND_SINGLE, values.shape, values.tobytes())
 
     def codebook_matrix(self, rng: np.random.Generator, rows: int, columns: int, bits: int, group: int) -> int:
-        padded = -(-columns // group) * group
-        groups = padded // group
-        packed = rng.integers(0, 256, size=rows * padded * bits // 8, dtype=np.uint8)
-        norm = np.exp(rng.uniform(np.log(1e-3), np.log(1e-2), size=rows)).astype(np.float16)
-        norms = np.repeat(norm, groups)
+        packed, norms = _codebook_rows(rng, rows, columns, bits, group)
         return self.add(KIND_CODEBOOK, (rows, columns), packed.tobytes() + norms.tobytes(), group, bits)
 
     def finish(self, path: str, header_fields: list[int], rope_theta: float, codebook: np.ndarray) -> None:
@@ -119,6 +115,41 @@ class _Writer:
                 f.write(b"\0" * (at - position))
                 f.write(blob)
                 position = at + len(blob)
+
+
+def _codebook_rows(rng: np.random.Generator, rows: int, columns: int, bits: int, group: int):
+    """The draws of _Writer.codebook_matrix: packed indices and fp16 norms (as uint16)."""
+    padded = -(-columns // group) * group
+    groups = padded // group
+    packed = rng.integers(0, 256, size=rows * padded * bits // 8, dtype=np.uint8)
+    norm = np.exp(rng.uniform(np.log(1e-3), np.log(1e-2), size=rows)).astype(np.float16)
+    return packed, np.repeat(norm, groups).view(np.uint16)
+
+
+def _levels(codebook: np.ndarray, bits: int) -> np.ndarray:
+    start = {2: 0, 3: 4, 4: 12}[bits]
+    return codebook[start:start + (1 << bits)].copy()
+
+
+def embedding_raw(seed: int = 0, geometry: Geometry | None = None):
+    """The embedding tensor of write_archive(seed, geometry) in the archive's
+    representation: (packed indices, codebook levels, fp16 norms as uint16)."""
+    g = geometry or Geometry()
+    rng = np.random.default_rng(seed)
+    codebook = _codebook(rng, g.group)
+    packed, norms = _codebook_rows(rng, g.vocab, g.d_model, g.embedding_bits, g.group)
+    return packed, _levels(codebook, g.embedding_bits), norms
+
+
+def product_matrix(seed: int, rows: int, columns: int, bits: int, group: int = 128):
+    """A codebook-quantised matrix for the product microbenchmark, drawn like
+    the archive's: Lloyd-Max-shaped levels, uniform indices, one log-uniform
+    [1e-3, 1e-2] fp16 norm per row repeated over its groups. Returns (packed
+    indices, levels, fp16 norms as uint16)."""
+    rng = np.random.default_rng(seed)
+    codebook = _codebook(rng, group)
+    packed, norms = _codebook_rows(rng, rows, columns, bits, group)
+    return packed, _levels(codebook, bits), norms
 
 
 def tokenizer_blob(vocab: int) -> bytes:

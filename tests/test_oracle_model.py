@@ -113,3 +113,19 @@ def test_synthetic_archive_resolves_in_the_oracle(oracle_lib, archive_path):
     info = m.tensor_info(0)
     assert info == dict(kind=3, rows=8192, columns=512, group=128, bits=4)
     assert m.tensor_info(2)["bits"] == 2
+
+
+def test_raw_product_is_the_archive_product(oracle_lib, archive_path):
+    """nbo_product_raw (the product microbenchmark's checker) runs the archive
+    path's code: on the embedding's own codes it gives the same bits."""
+    from rustyneedle_b200 import synthetic
+
+    packed, levels, norms = synthetic.embedding_raw(seed=0)
+    rows, cols = 8192, 512
+    model = oracle_lib.Model.open(archive_path, oracle_lib.MODE_INT, 0)
+    rng = np.random.default_rng(3)
+    for _ in range(2):
+        x = rng.standard_normal(cols).astype(np.float32)
+        got = oracle_lib.product_raw(oracle_lib.MODE_INT, 4, packed, levels, norms, rows, cols, x)
+        want, _ = model.matrix_product(0, x)
+        assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
