@@ -692,7 +692,7 @@ constexpr int ATT_WORKERS = 256;
 constexpr int ATT_THREADS_ALL = ATT_WORKERS + 32;
 constexpr int MAX_GROUP = 4;
 constexpr int ATT_SLICES = ATT_WORKERS / 16;
-constexpr int ATT_UNROLL = 4;
+constexpr int ATT_UNROLL = 8;
 constexpr int ATT_MAX_KV = 8;
 
 __host__ __device__ constexpr int att_wstride(int t_cap) { return t_cap / 4 + 2; }
