@@ -239,7 +239,7 @@ def main():
     if DEPTH != model.config.num_layers:
         model = model.with_depth(DEPTH)
     if args.batch1_only:
-        print(json.dumps({"batch1": batch1(nb, model)}), flush=True)
+        print(json.dumps({"batch1": batch1(nb, model, local)}), flush=True)
         return
     t0 = time.perf_counter()
     sessions = []
@@ -303,7 +303,7 @@ def main():
 
     if not args.no_batch1 and rank == 0 and not args.profile:
         batch.close()
-        line["batch1"] = batch1(nb, model)
+        line["batch1"] = batch1(nb, model, local)
     if rank == 0 and world == 1 and not args.no_cpu and not args.profile:
         from oracle import oracle
 
@@ -315,7 +315,7 @@ def main():
     dp.close_group(dist)
 
 
-def batch1(nb, model):
+def batch1(nb, model, device: int = 0):
     """Config 1: depth 20, batch 1, 512-token prompt, 256 masked greedy steps."""
     rng = np.random.default_rng(7)
     ids = rng.integers(10, 8000, 512).astype(np.uint32)
@@ -331,15 +331,17 @@ def batch1(nb, model):
         allowed[rng.integers(0, model.config.output_vocab)] = True
         masks.append(np.packbits(allowed.astype(np.uint8), bitorder="little").view(np.uint32)[:words].copy())
     times = []
-    for m in masks:
-        t = time.perf_counter()
-        b.step(m)
-        times.append(1000 * (time.perf_counter() - t))
+    with Clocks(device) as clocks:
+        for m in masks:
+            t = time.perf_counter()
+            b.step(m)
+            times.append(1000 * (time.perf_counter() - t))
     b.close()
     times = times[4:]
     return {"prefill_ms_512": round(prefill_ms, 2), "p50_ms_per_token": round(float(np.percentile(times, 50)), 4),
             "p90_ms_per_token": round(float(np.percentile(times, 90)), 4),
             "tokens_per_s": round(1000.0 / float(np.percentile(times, 50)), 1), "steps": len(times),
+            "clocks": clocks.summary(),
             "note": "per-token latency through nb_batch_step (host mask in, token out), depth 20"}
 
 

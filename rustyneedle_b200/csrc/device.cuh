@@ -36,6 +36,42 @@ __device__ __forceinline__ float fsqrt(float a) { return __fsqrt_rn(a); }
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
+// Bounded mbarrier waits: a wait that gives up returns false, and its caller
+// raises the device error flag and skips the work instead of hanging.
+constexpr uint32_t MBAR_WAIT_LIMIT = 1u << 24;
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t phase) {
+  for (uint32_t i = 0; i < MBAR_WAIT_LIMIT; ++i) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.b32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(bar), "r"(phase)
+        : "memory");
+    if (done) return true;
+  }
+  return false;
+}
+
+// Bulk copies (cp.async.bulk) of contiguous global ranges into shared memory,
+// completing on one mbarrier: one thread initialises the barrier, announces
+// the bytes and issues every copy; addresses and sizes are 16-byte multiples.
+__device__ __forceinline__ void bulk_start(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(1) : "memory");
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void bulk_copy(void* dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(dst)), "l"(src),
+               "r"(bytes), "r"(bar)
+               : "memory");
+}
+
 // Rust's float Iterator::sum starts from -0.0.
 constexpr float SUM_START = -0.0f;
 

@@ -94,16 +94,14 @@ __device__ __forceinline__ void phi_row(const ModelDev& md, int r, int layer, co
 }
 
 // Shared memory of k_route, in floats: this layer's phi rows (PHI_ROWS × n
-// bytes, the 16-byte chunk c of row r stored at chunk c ^ (r % 8) so that the
-// eight rows a quarter-warp reads fall in distinct banks), the stream, a work
-// row, the squares in chain-major order (8 chains of n/8, stride n/8 + 4),
-// the int8 codes, the phi norms and the norm_in gains.
+// bytes), the stream, a work row, the squares in chain-major order (8 chains
+// of n/8, stride n/8 + 4), the int8 codes, the phi norms and the norm_in gains.
 __host__ __device__ inline size_t route_floats(int d) {
   const size_t n = (size_t)LANES * d, ng = n / GROUP;
   return PHI_ROWS * n / 4 + 2 * n + 8 * (n / 8 + 4) + n / 4 + PHI_ROWS * ng + d;
 }
 
-__global__ void __launch_bounds__(256) k_route(ModelDev md, LayerDev L, Work w, int M, int layer, int slot) {
+__global__ void __launch_bounds__(256) k_route(ModelDev md, LayerDev L, Work w, int M, int layer, int slot, int* error) {
   extern __shared__ __align__(16) float sm[];
   const int t = blockIdx.x;
   const int d = md.d_model, n = LANES * d, ng = n / GROUP, sqs = n / 8 + 4;
@@ -120,25 +118,33 @@ __global__ void __launch_bounds__(256) k_route(ModelDev md, LayerDev L, Work w, 
   __shared__ float s_phi[PHI_ROWS];
   __shared__ float s_gate[LANES];
   __shared__ float s_inv, s_peak;
+  __shared__ __align__(8) uint64_t s_bar;
+  const uint32_t bar = smem_u32(&s_bar);
 
-  // the layer's constant weights first, then (once the previous kernel is done) the token's stream
-  {
-    const int chunks = n / 16;
-    for (int i = tid; i < PHI_ROWS * chunks; i += blockDim.x) {
-      const int r = i / chunks, c = i % chunks;
+  // the layer's constant weights first (bulk copies: lane 0 of warp 0 arms
+  // the barrier, each lane issues one copy), then (once the previous kernel
+  // is done) the token's stream
+  if (warp == 0) {
+    if (lane == 0) bulk_start(bar, PHI_ROWS * n + (PHI_ROWS * ng + d) * 4);
+    __syncwarp();
+    if (lane < PHI_ROWS) {
       const QMat* P;
       int row;
-      phi_row(md, r, layer, P, row);
-      cp_async16(s_phiw + (size_t)r * n + (size_t)(c ^ (r & 7)) * 16, P->codes + (size_t)row * n + (size_t)c * 16);
+      phi_row(md, lane, layer, P, row);
+      bulk_copy(s_phiw + (size_t)lane * n, P->codes + (size_t)row * n, n, bar);
+    } else if (lane == PHI_ROWS) {
+      bulk_copy(s_norms, md.phi_pre.scales + (size_t)layer * LANES * ng, LANES * ng * 4, bar);
+    } else if (lane == PHI_ROWS + 1) {
+      bulk_copy(s_norms + LANES * ng, md.phi_post.scales + (size_t)layer * LANES * ng, LANES * ng * 4, bar);
+    } else if (lane == PHI_ROWS + 2) {
+      bulk_copy(s_norms + 2 * LANES * ng, md.phi_res.scales + (size_t)layer * LANES * LANES * ng, LANES * LANES * ng * 4, bar);
+    } else if (lane == PHI_ROWS + 3) {
+      bulk_copy(s_gain, L.norm_in, d * 4, bar);
     }
   }
-  stage_async(s_norms, md.phi_pre.scales + (size_t)layer * LANES * ng, LANES * ng);
-  stage_async(s_norms + LANES * ng, md.phi_post.scales + (size_t)layer * LANES * ng, LANES * ng);
-  stage_async(s_norms + 2 * LANES * ng, md.phi_res.scales + (size_t)layer * LANES * LANES * ng, LANES * LANES * ng);
-  stage_async(s_gain, L.norm_in, d);
   pdl_wait();
   if (t >= M || w.meta[t].slot < 0) {
-    cp_async_wait_all();
+    if (tid == 0 && !mbar_wait(bar, 0)) atomicExch(error, 1);  // no copy outlives the CTA
     return;
   }
   stage_async(s_stream, w.stream + (size_t)t * n, n);
@@ -196,47 +202,38 @@ __global__ void __launch_bounds__(256) k_route(ModelDev md, LayerDev L, Work w, 
     *reinterpret_cast<uint32_t*>(s_codes + g * GROUP + 4 * lane) = packed;
     if (lane == 0) s_ascale[g] = sc;
   }
+  if (!mbar_wait(bar, 0) && tid == 0) atomicExch(error, 1);  // the phi rows, norms and gains
   __syncthreads();
   // phi products: 4 pre rows, 4 post rows, 16 residual rows of this layer
-  // (lanes.rs:156-163). Thread (group g, row r) forms the exact int32 sum of
-  // one 128-column group (two pairs per thread, loads issued together) and its
-  // scaled term acc·norm·level_scale·act_scale; one thread per row then adds
-  // the terms in group order, the 4-bit row chain (neon.rs:164-183).
+  // (lanes.rs:156-163). Each (row r, group g) pair takes eight lanes, lane k
+  // its 16-byte chunk k of the group (a quarter-warp reads 128 contiguous
+  // bytes); the exact int32 sum is reduced over the eight lanes, and lane 0
+  // forms the scaled term acc·norm·level_scale·act_scale. One thread per row
+  // then adds the terms in group order, the 4-bit row chain (neon.rs:164-183).
   float* s_term = s_work;  // [ng][PHI_ROWS]; s_work is free again
   {
-    const int pairs = PHI_ROWS * ng;
-    uint4 wr[2][8];
-#pragma unroll
-    for (int u = 0; u < 2; ++u) {
-      const int pair = tid + u * 256;
-      if (pair < pairs) {
-        const int g = pair / PHI_ROWS, r = pair % PHI_ROWS;
-        const uint4* wv = reinterpret_cast<const uint4*>(s_phiw + (size_t)r * n);
-#pragma unroll
-        for (int k = 0; k < 8; ++k) wr[u][k] = wv[(g * 8 + k) ^ (r & 7)];
+    const int tasks = PHI_ROWS * ng * 8;
+    for (int base = 0; base < tasks; base += blockDim.x) {
+      const int task = base + tid, pair = task >> 3, k = task & 7;
+      const bool live = task < tasks;
+      const int g = pair / PHI_ROWS, r = pair % PHI_ROWS;
+      int acc = 0;
+      if (live) {
+        const uint4 wv = *reinterpret_cast<const uint4*>(s_phiw + (size_t)r * n + g * GROUP + k * 16);
+        const uint4 a = *reinterpret_cast<const uint4*>(s_codes + g * GROUP + k * 16);
+        acc = dp4a(wv.x, a.x, acc);
+        acc = dp4a(wv.y, a.y, acc);
+        acc = dp4a(wv.z, a.z, acc);
+        acc = dp4a(wv.w, a.w, acc);
       }
-    }
-#pragma unroll
-    for (int u = 0; u < 2; ++u) {
-      const int pair = tid + u * 256;
-      if (pair < pairs) {
-        const int g = pair / PHI_ROWS;
-        const uint4* av = reinterpret_cast<const uint4*>(s_codes + g * GROUP);
-        int acc[4] = {0, 0, 0, 0};
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          uint4 a = av[k];
-          acc[0] = dp4a(wr[u][k].x, a.x, acc[0]);
-          acc[1] = dp4a(wr[u][k].y, a.y, acc[1]);
-          acc[2] = dp4a(wr[u][k].z, a.z, acc[2]);
-          acc[3] = dp4a(wr[u][k].w, a.w, acc[3]);
-        }
-        const int r = pair % PHI_ROWS;
+      acc += __shfl_xor_sync(FULL, acc, 1);
+      acc += __shfl_xor_sync(FULL, acc, 2);
+      acc += __shfl_xor_sync(FULL, acc, 4);
+      if (live && k == 0) {
         const QMat* P;
         int row;
         phi_row(md, r, layer, P, row);
-        const float sum = (float)((acc[0] + acc[1]) + (acc[2] + acc[3]));
-        s_term[pair] = fmul(fmul(fmul(sum, s_norms[r * ng + g]), P->level_scale), s_ascale[g]);
+        s_term[pair] = fmul(fmul(fmul((float)acc, s_norms[r * ng + g]), P->level_scale), s_ascale[g]);
       }
     }
   }
@@ -250,46 +247,46 @@ __global__ void __launch_bounds__(256) k_route(ModelDev md, LayerDev L, Work w, 
   __syncthreads();
   float* route_out = w.route + (size_t)t * (LANES + LANES * LANES);
   if (warp == 7) {
-    // post gates and the Sinkhorn-normalised residual mixing (lanes.rs:166-179, ops.rs:198-217)
-    __shared__ float s_res[16];
-    if (lane < LANES) {
-      float off = lane == (slot % LANES) ? 0.0f : -4.0f;
-      float p = fadd(fadd(fmul(md.a_post[layer], s_phi[4 + lane]), md.b_post[layer * LANES + lane]), off);
-      route_out[lane] = fmul(2.0f, sigmoid(p));
-    }
-    if (lane < 16) s_res[lane] = fadd(fmul(md.a_res[layer], s_phi[8 + lane]), md.b_res[layer * 16 + lane]);
-    __syncwarp();
+    // the Sinkhorn-normalised residual mixing (lanes.rs:166-179, ops.rs:198-217):
+    // lane 4r + c holds element (r, c); every row or column total is the
+    // reference's ordered sum from -0.0, gathered by shuffles in its order
     if (lane < 16) {
-      const int r = lane / 4;
+      constexpr unsigned M16 = 0xffffu;
+      const int r = lane / 4, c = lane % 4;
+      const float v = fadd(fmul(md.a_res[layer], s_phi[8 + lane]), md.b_res[layer * 16 + lane]);
       float pk = -INFINITY;
-      for (int c = 0; c < 4; ++c) pk = fmaxf(pk, s_res[r * 4 + c]);
-      float e = expf_libm(fsub(s_res[lane], pk));
-      __syncwarp(0xffffu);
-      s_res[lane] = e;
-    }
-    __syncwarp();
-    if (lane == 0) {
-      float x[16];
-      for (int i = 0; i < 16; ++i) x[i] = s_res[i];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) pk = fmaxf(pk, __shfl_sync(M16, v, 4 * r + k));
+      float x = expf_libm(fsub(v, pk));
       const float MIN_POSITIVE = 1.17549435e-38f;
       for (int it = 0; it < 20; ++it) {
-        float iv[4];
-        for (int r = 0; r < 4; ++r) iv[r] = frcp(fmaxf(fadd(fadd(fadd(fadd(SUM_START, x[r * 4]), x[r * 4 + 1]), x[r * 4 + 2]), x[r * 4 + 3]), MIN_POSITIVE));
-        for (int r = 0; r < 4; ++r)
-          for (int c = 0; c < 4; ++c) x[r * 4 + c] = fmul(x[r * 4 + c], iv[r]);
-        for (int c = 0; c < 4; ++c) iv[c] = frcp(fmaxf(fadd(fadd(fadd(fadd(SUM_START, x[c]), x[4 + c]), x[8 + c]), x[12 + c]), MIN_POSITIVE));
-        for (int r = 0; r < 4; ++r)
-          for (int c = 0; c < 4; ++c) x[r * 4 + c] = fmul(x[r * 4 + c], iv[c]);
+        float total = SUM_START;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) total = fadd(total, __shfl_sync(M16, x, 4 * r + k));
+        x = fmul(x, frcp(fmaxf(total, MIN_POSITIVE)));
+        total = SUM_START;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) total = fadd(total, __shfl_sync(M16, x, 4 * k + c));
+        x = fmul(x, frcp(fmaxf(total, MIN_POSITIVE)));
       }
-      for (int i = 0; i < 16; ++i) route_out[LANES + i] = x[i];
+      route_out[LANES + lane] = x;
     }
     return;
   }
-  // warps 0-6 (224 threads) from here on
+  // warps 0-6 (224 threads) from here on; threads 0-3 form the pre gates,
+  // threads 4-7 the post gates (2 · sigmoid, lanes.rs:166-179)
   const int nthreads = 224;
-  if (tid < LANES) {
-    float off = tid == (slot % LANES) ? 8.0f + -4.0f : -4.0f;
-    s_gate[tid] = sigmoid(fadd(fadd(fmul(md.a_pre[layer], s_phi[tid]), md.b_pre[layer * LANES + tid]), off));
+  if (tid < 2 * LANES) {
+    const int l = tid % LANES;
+    const bool pre = tid < LANES;
+    const float off = pre ? (l == (slot % LANES) ? 8.0f + -4.0f : -4.0f) : (l == (slot % LANES) ? 0.0f : -4.0f);
+    const float a = pre ? md.a_pre[layer] : md.a_post[layer];
+    const float bias = pre ? md.b_pre[layer * LANES + l] : md.b_post[layer * LANES + l];
+    const float g = sigmoid(fadd(fadd(fmul(a, s_phi[pre ? l : 4 + l]), bias), off));
+    if (pre)
+      s_gate[l] = g;
+    else
+      route_out[l] = fmul(2.0f, g);
   }
   named_barrier(1, nthreads);
   float* s_x = s_work;  // the block input x (lanes.rs:169-171)
@@ -353,24 +350,6 @@ __global__ void __launch_bounds__(256) k_route(ModelDev md, LayerDev L, Work w, 
 constexpr int GEMM_ROWS = 128;
 constexpr int GEMM_K = 512;
 constexpr int GEMM_KC = GEMM_K / 16;  // 16-byte chunks per row
-constexpr uint32_t GEMM_WAIT_LIMIT = 1u << 24;
-
-__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
-
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t phase) {
-  for (uint32_t i = 0; i < GEMM_WAIT_LIMIT; ++i) {
-    uint32_t done;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.b32 %0, 1, 0, p;\n\t}"
-        : "=r"(done)
-        : "r"(bar), "r"(phase)
-        : "memory");
-    if (done) return true;
-  }
-  return false;
-}
 
 // UMMA shared-memory descriptor (K-major, no swizzle): start address, the byte
 // offset between the two 16-byte K halves of a K = 32 step (LBO) and between
@@ -1223,7 +1202,7 @@ __device__ __forceinline__ void hadamard_core(const ModelDev& md, const Hadamard
 }
 
 template <int LEFT>
-__global__ void __launch_bounds__(BLOCK_THREADS) k_block(ModelDev md, LayerDev L, Work w, int M) {
+__global__ void __launch_bounds__(BLOCK_THREADS) k_block(ModelDev md, LayerDev L, Work w, int M, int* error) {
   extern __shared__ float sm[];
   constexpr int N = LEFT * HADA_RIGHT;
   const int t = blockIdx.x;
@@ -1242,23 +1221,31 @@ __global__ void __launch_bounds__(BLOCK_THREADS) k_block(ModelDev md, LayerDev L
   float* s_gpost = s_right + HADA_RIGHT * HADA_RIGHT + (d * COND_RANK <= 2 * N ? 0 : d * COND_RANK);  // d post_norm gains
   float* s_gpre = s_gpost + MAX_D;                                                                     // d pre_hada gains
   __shared__ float s_inv, s_gate;
+  __shared__ __align__(8) uint64_t s_bar;
+  const uint32_t bar = smem_u32(&s_bar);
   const HadamardDev& Hd = L.hada;
 
-  // the layer's constant weights first, then (once the previous kernel is done) the token's rows
-  stage_async(s_condv, Hd.cond_v, d * COND_RANK);
-  stage_async(s_left, Hd.left[0], LEFT * LEFT);
-  stage_async(s_right, Hd.right[0], HADA_RIGHT * HADA_RIGHT);
-  stage_async(s_gpost, L.post_norm, d);
-  stage_async(s_gpre, L.pre_hada, d);
-  if (tid == 0) s_gate = sigmoid(L.attn_gate);
+  // the layer's constant weights first (bulk copies, one thread), then (once
+  // the previous kernel is done) the token's rows
+  if (warp == 0) {
+    if (lane == 0) bulk_start(bar, (d * COND_RANK + LEFT * LEFT + HADA_RIGHT * HADA_RIGHT + 2 * d) * 4);
+    __syncwarp();
+    if (lane == 0) bulk_copy(s_condv, Hd.cond_v, d * COND_RANK * 4, bar);
+    if (lane == 1) bulk_copy(s_left, Hd.left[0], LEFT * LEFT * 4, bar);
+    if (lane == 2) bulk_copy(s_right, Hd.right[0], HADA_RIGHT * HADA_RIGHT * 4, bar);
+    if (lane == 3) bulk_copy(s_gpost, L.post_norm, d * 4, bar);
+    if (lane == 4) bulk_copy(s_gpre, L.pre_hada, d * 4, bar);
+  }
+  if (tid == 32) s_gate = sigmoid(L.attn_gate);
   pdl_wait();
   if (t >= M || w.meta[t].slot < 0) {
-    cp_async_wait_all();
+    if (tid == 0 && !mbar_wait(bar, 0)) atomicExch(error, 1);  // no copy outlives the CTA
     return;
   }
   stage_async(s_a, w.outp + (size_t)t * d, d);
   stage_async(s_x, w.x + (size_t)t * d, d);
   cp_async_wait_all();
+  if (!mbar_wait(bar, 0) && tid == 0) atomicExch(error, 1);
   __syncthreads();
   if (warp == 0) {
     float ss = sum_of_squares_warp(s_a, d);
@@ -1591,7 +1578,7 @@ void launch_layer(const ModelDev& md, const LayerDev& L, const Work& w, const Kv
   t_pass_tokens = M;
   const int d = md.d_model, H = md.heads, KV = md.kv_heads;
   const int proj_stride = (2 * H + 2 * KV) * HEAD_DIM;
-  launch(k_route, M, 256, route_smem(md), st, md, L, w, M, layer, slot);
+  launch(k_route, M, 256, route_smem(md), st, md, L, w, M, layer, slot, g_gemm_error);
   project(L.qkvg, w.act, w.act_scale, w.proj, M, proj_stride, w.meta, st);
   launch(k_heads, M, 32 * (H + 2 * KV), 0, st, md, L, w, kv, M, layer);
   if (!launch_attend_prep(md, L, w, kv, M, layer, t_cap, st)) {
@@ -1602,9 +1589,9 @@ void launch_layer(const ModelDev& md, const LayerDev& L, const Work& w, const Kv
   }
   project(L.out, w.act, w.act_scale, w.outp, M, d, w.meta, st);
   if (md.hada_left == 64)
-    launch(k_block<64>, M, BLOCK_THREADS, block_smem(md), st, md, L, w, M);
+    launch(k_block<64>, M, BLOCK_THREADS, block_smem(md), st, md, L, w, M, g_gemm_error);
   else
-    launch(k_block<32>, M, BLOCK_THREADS, block_smem(md), st, md, L, w, M);
+    launch(k_block<32>, M, BLOCK_THREADS, block_smem(md), st, md, L, w, M, g_gemm_error);
 }
 
 void launch_final(const ModelDev& md, const Work& w, float* hidden, int M, cudaStream_t st) {
