@@ -121,26 +121,19 @@ __global__ void __launch_bounds__(256) k_route(ModelDev md, LayerDev L, Work w, 
   __shared__ __align__(8) uint64_t s_bar;
   const uint32_t bar = smem_u32(&s_bar);
 
-  // the layer's constant weights first (bulk copies: lane 0 of warp 0 arms
-  // the barrier, each lane issues one copy), then (once the previous kernel
-  // is done) the token's stream
-  if (warp == 0) {
-    if (lane == 0) bulk_start(bar, PHI_ROWS * n + (PHI_ROWS * ng + d) * 4);
-    __syncwarp();
-    if (lane < PHI_ROWS) {
-      const QMat* P;
-      int row;
-      phi_row(md, lane, layer, P, row);
-      bulk_copy(s_phiw + (size_t)lane * n, P->codes + (size_t)row * n, n, bar);
-    } else if (lane == PHI_ROWS) {
-      bulk_copy(s_norms, md.phi_pre.scales + (size_t)layer * LANES * ng, LANES * ng * 4, bar);
-    } else if (lane == PHI_ROWS + 1) {
-      bulk_copy(s_norms + LANES * ng, md.phi_post.scales + (size_t)layer * LANES * ng, LANES * ng * 4, bar);
-    } else if (lane == PHI_ROWS + 2) {
-      bulk_copy(s_norms + 2 * LANES * ng, md.phi_res.scales + (size_t)layer * LANES * LANES * ng, LANES * LANES * ng * 4, bar);
-    } else if (lane == PHI_ROWS + 3) {
-      bulk_copy(s_gain, L.norm_in, d * 4, bar);
-    }
+  // the layer's constant weights first, then (once the previous kernel is
+  // done) the token's stream. One thread arms the barrier and issues the bulk
+  // copies: the pre, post and residual rows of this layer are contiguous in
+  // their matrices (rows 4l.., 4l.., 16l..), so seven copies in all.
+  if (tid == 0) {
+    bulk_start(bar, PHI_ROWS * n + (PHI_ROWS * ng + d) * 4);
+    bulk_copy(s_phiw, md.phi_pre.codes + (size_t)layer * LANES * n, LANES * n, bar);
+    bulk_copy(s_phiw + (size_t)LANES * n, md.phi_post.codes + (size_t)layer * LANES * n, LANES * n, bar);
+    bulk_copy(s_phiw + (size_t)2 * LANES * n, md.phi_res.codes + (size_t)layer * LANES * LANES * n, LANES * LANES * n, bar);
+    bulk_copy(s_norms, md.phi_pre.scales + (size_t)layer * LANES * ng, LANES * ng * 4, bar);
+    bulk_copy(s_norms + LANES * ng, md.phi_post.scales + (size_t)layer * LANES * ng, LANES * ng * 4, bar);
+    bulk_copy(s_norms + 2 * LANES * ng, md.phi_res.scales + (size_t)layer * LANES * LANES * ng, LANES * LANES * ng * 4, bar);
+    bulk_copy(s_gain, L.norm_in, d * 4, bar);
   }
   pdl_wait();
   if (t >= M || w.meta[t].slot < 0) {
@@ -1227,14 +1220,13 @@ __global__ void __launch_bounds__(BLOCK_THREADS) k_block(ModelDev md, LayerDev L
 
   // the layer's constant weights first (bulk copies, one thread), then (once
   // the previous kernel is done) the token's rows
-  if (warp == 0) {
-    if (lane == 0) bulk_start(bar, (d * COND_RANK + LEFT * LEFT + HADA_RIGHT * HADA_RIGHT + 2 * d) * 4);
-    __syncwarp();
-    if (lane == 0) bulk_copy(s_condv, Hd.cond_v, d * COND_RANK * 4, bar);
-    if (lane == 1) bulk_copy(s_left, Hd.left[0], LEFT * LEFT * 4, bar);
-    if (lane == 2) bulk_copy(s_right, Hd.right[0], HADA_RIGHT * HADA_RIGHT * 4, bar);
-    if (lane == 3) bulk_copy(s_gpost, L.post_norm, d * 4, bar);
-    if (lane == 4) bulk_copy(s_gpre, L.pre_hada, d * 4, bar);
+  if (tid == 0) {  // one thread arms the barrier and issues every copy
+    bulk_start(bar, (d * COND_RANK + LEFT * LEFT + HADA_RIGHT * HADA_RIGHT + 2 * d) * 4);
+    bulk_copy(s_condv, Hd.cond_v, d * COND_RANK * 4, bar);
+    bulk_copy(s_left, Hd.left[0], LEFT * LEFT * 4, bar);
+    bulk_copy(s_right, Hd.right[0], HADA_RIGHT * HADA_RIGHT * 4, bar);
+    bulk_copy(s_gpost, L.post_norm, d * 4, bar);
+    bulk_copy(s_gpre, L.pre_hada, d * 4, bar);
   }
   if (tid == 32) s_gate = sigmoid(L.attn_gate);
   pdl_wait();
@@ -1514,7 +1506,11 @@ static bool pdl_enabled() {
     const char* e = std::getenv("NEEDLE_B200_PDL");
     return !(e && e[0] == '0');
   }();
-  return on && t_pass_tokens <= PDL_MAX_TOKENS;
+  static const int max_tokens = [] {
+    const char* e = std::getenv("NEEDLE_B200_PDL_TOKENS");
+    return e ? std::atoi(e) : PDL_MAX_TOKENS;
+  }();
+  return on && t_pass_tokens <= max_tokens;
 }
 
 template <typename... P, typename... A>
