@@ -1229,6 +1229,7 @@ __global__ void __launch_bounds__(BLOCK_THREADS) k_block(ModelDev md, LayerDev L
     bulk_copy(s_gpre, L.pre_hada, d * 4, bar);
   }
   if (tid == 32) s_gate = sigmoid(L.attn_gate);
+  __syncthreads();  // the barrier is initialised before any thread waits on it
   pdl_wait();
   if (t >= M || w.meta[t].slot < 0) {
     if (tid == 0 && !mbar_wait(bar, 0)) atomicExch(error, 1);  // no copy outlives the CTA
