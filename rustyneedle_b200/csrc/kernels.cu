@@ -1228,8 +1228,8 @@ __global__ void __launch_bounds__(BLOCK_THREADS) k_block(ModelDev md, LayerDev L
     bulk_copy(s_gpost, L.post_norm, d * 4, bar);
     bulk_copy(s_gpre, L.pre_hada, d * 4, bar);
   }
-  if (tid == 32) s_gate = sigmoid(L.attn_gate);
   __syncthreads();  // the barrier is initialised before any thread waits on it
+  if (tid == 32) s_gate = sigmoid(L.attn_gate);
   pdl_wait();
   if (t >= M || w.meta[t].slot < 0) {
     if (tid == 0 && !mbar_wait(bar, 0)) atomicExch(error, 1);  // no copy outlives the CTA
@@ -1493,13 +1493,13 @@ static int* g_gemm_error = nullptr;
 
 void set_error_flag(int* flag) { g_gemm_error = flag; }
 
-// Passes over at most this many tokens launch their kernels with
-// programmatic stream serialisation: each kernel's prologue (constant weight
-// loads, tensor-memory allocation) overlaps the tail of its predecessor; see
-// pdl_wait in device.cuh. Larger passes fill the SMs by themselves, and the
-// early-resident successor CTAs only take room from the running kernel, so
-// they launch plainly. $NEEDLE_B200_PDL=0 turns the overlap off.
-constexpr int PDL_MAX_TOKENS = 32;
+// Every kernel of a pass launches with programmatic stream serialisation:
+// its prologue (constant weight loads, tensor-memory allocation) overlaps the
+// tail of its predecessor; see pdl_wait in device.cuh. On B200 this pays at
+// every pass size (decode batches of 1..256, prefill passes of 1024 tokens).
+// $NEEDLE_B200_PDL=0 turns the overlap off; $NEEDLE_B200_PDL_TOKENS=N keeps it
+// to passes of at most N tokens.
+constexpr int PDL_MAX_TOKENS = 1 << 30;
 static thread_local int t_pass_tokens = 0;
 
 static bool pdl_enabled() {
