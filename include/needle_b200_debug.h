@@ -16,7 +16,9 @@ extern "C" {
 
 /* Element-wise device math on the model's GPU: op 0 = f32::exp as the host
  * libm computes it, 1 = sigmoid (crates/kernels/src/ops.rs:69-71),
- * 2 = fast_exp (ops.rs:83-90), 3 = silu (ops.rs:74-76). */
+ * 2 = fast_exp (ops.rs:83-90), 3 = silu (ops.rs:74-76), 4 = the Sinkhorn
+ * reciprocal 1 / max(x, f32::MIN_POSITIVE) (ops.rs:206, 211) for x <= 4 (the
+ * row and column totals never exceed 4). */
 nb_status nb_debug_math(nb_model* model, int op, const float* in, float* out, size_t count);
 
 /* QuantisedMatrix::prepare + multiply_vector (crates/kernels/src/matrix.rs:123-165)

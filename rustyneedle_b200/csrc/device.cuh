@@ -75,22 +75,65 @@ __device__ __forceinline__ void bulk_copy(void* dst, const void* src, uint32_t b
 // Rust's float Iterator::sum starts from -0.0.
 constexpr float SUM_START = -0.0f;
 
-// Set per device by set_exp_constants (kernels.cu).
+// Set per device by set_exp_constants (kernels.cu). The 2^(j/64) table is
+// also held in global memory: lanes index it with their own j, which the
+// constant cache would serve one address at a time; L1 serves a warp's reads
+// of the 512-byte table in at most four wavefronts.
 __constant__ nbx::ExpConstants c_exp;
 __constant__ nbx::ExceptionSet c_exceptions;
+__device__ double g_exp_table[64];
 
-// f32::exp of the host libm (see exactmath.h).
+// f32::exp of the host libm (see exactmath.h): the same double-precision
+// evaluation as nbx::exp_double_core, written out for the device. 2^m is
+// applied as a multiply by an exactly built power of two (m ∈ [-159, 128], so
+// y·2^m is a normal double, the same value ldexp gives), and the
+// near-midpoint test uses the result's positive sign (e^x > 0).
 __device__ __forceinline__ float expf_libm(float x) {
   if (isnan(x)) return x;
   if (x > 89.0f) return INFINITY;
   if (x < -110.0f) return 0.0f;
-  double y = nbx::exp_double_core(
-      x, c_exp, [](double a, double b) { return __dmul_rn(a, b); }, [](double a, double b) { return __dadd_rn(a, b); },
-      [](double a, double b, double c) { return __fma_rn(a, b, c); });
+  const double xd = (double)x;
+  const double kd = rint(__dmul_rn(xd, c_exp.inv_step));
+  const int k = (int)kd;
+  const double t = __ldg(&g_exp_table[k & 63]);
+  double r = __dadd_rn(xd, -__dmul_rn(kd, c_exp.step_hi));
+  r = __dadd_rn(r, -__dmul_rn(kd, c_exp.step_lo));
+  double p = 1.0 / 5040.0;
+  p = __fma_rn(p, r, 1.0 / 720.0);
+  p = __fma_rn(p, r, 1.0 / 120.0);
+  p = __fma_rn(p, r, 1.0 / 24.0);
+  p = __fma_rn(p, r, 1.0 / 6.0);
+  p = __fma_rn(p, r, 0.5);
+  p = __fma_rn(p, r, 1.0);
+  p = __fma_rn(p, r, 1.0);
+  const double scale = __longlong_as_double((long long)((k >> 6) + 1023) << 52);  // 2^m, m = (k - (k & 63)) / 64
+  const double y = __dmul_rn(__dmul_rn(t, p), scale);
   float f = __double2float_rn(y);
-  if (nbx::near_midpoint(y, f, c_exp.near_relative) && nbx::exception_contains(c_exceptions, nbx::float_bits(x)))
-    f = nbx::other_neighbour(y, f);
+  if ((double)f != y) {
+    // the other binary32 neighbour of y, and whether y lies within
+    // near_relative·y of their midpoint (nbx::near_midpoint for y > 0)
+    const float other = __int_as_float(__float_as_int(f) + ((double)f < y ? 1 : -1));
+    const double mid = __dmul_rn(__dadd_rn((double)f, (double)other), 0.5);
+    if (fabs(__dadd_rn(y, -mid)) <= __dmul_rn(y, c_exp.near_relative) && !isinf(f) &&
+        nbx::exception_contains(c_exceptions, nbx::float_bits(x)))
+      f = other;
+  }
   return f;
+}
+
+// 1/b correctly rounded, for a positive normal b below 2^126 (so 1/b is
+// normal too), by Markstein's refinement of the hardware approximation
+// (P. W. Markstein, "Computation of elementary functions on the IBM RISC
+// System/6000 processor", IBM J. Res. Develop. 34(1), 1990): y0 =
+// rcp.approx(b) lies within an ulp of 1/b, so e = 1 - b·y0 is exact in one
+// fma, and y0 + y0·e is rounded once. Straight-line code (no slow path), so
+// independent reciprocals overlap. Compared bit for bit with __frcp_rn over
+// every b in [2^-126, 2^126) on B200: no difference.
+__device__ __forceinline__ float rcp_positive(float b) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(b));
+  const float e = __fmaf_rn(-b, y, 1.0f);
+  return __fmaf_rn(e, y, y);
 }
 
 // crates/kernels/src/ops.rs:69-71

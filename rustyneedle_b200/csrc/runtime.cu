@@ -1267,7 +1267,7 @@ struct DeviceTemp {
 extern "C" {
 
 nb_status nb_debug_math(nb_model* model, int op, const float* in, float* out, size_t count) {
-  if (!model || !in || !out || op < 0 || op > 3) return NB_ERR_ARGUMENT;
+  if (!model || !in || !out || op < 0 || op > 4) return NB_ERR_ARGUMENT;
   return guard([&] {
     Engine& E = *model->engine;
     std::lock_guard<std::mutex> lock(E.mutex);

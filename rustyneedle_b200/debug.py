@@ -9,7 +9,7 @@ import numpy as np
 
 from ._native import Model, Session, _check, _ptr, lib
 
-OP_EXPF, OP_SIGMOID, OP_FAST_EXP, OP_SILU = 0, 1, 2, 3
+OP_EXPF, OP_SIGMOID, OP_FAST_EXP, OP_SILU, OP_SINKHORN_RCP = 0, 1, 2, 3, 4
 MATRIX_QKVG, MATRIX_OUT, MATRIX_LOGITS = 0, 1, 2
 
 _declared = False

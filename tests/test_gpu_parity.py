@@ -73,6 +73,19 @@ def test_device_sigmoid_fast_exp_silu_match_the_oracle(device_model, oracle_lib)
     assert _bits_equal(debug.math(device_model, debug.OP_FAST_EXP, x), fe)
 
 
+def test_sinkhorn_reciprocal_is_correctly_rounded(device_model):
+    """The Sinkhorn's 1 / max(total, f32::MIN_POSITIVE) (ops.rs:206, 211) over every
+    64th binary32 in [2^-126, 4] plus zeros, negatives and NaN (-> MIN_POSITIVE);
+    numpy's float32 division is the IEEE correctly rounded quotient."""
+    from rustyneedle_b200 import debug
+
+    bits = np.arange(0x00800000, 0x40800001, 64, dtype=np.uint32)
+    x = np.concatenate([bits.view(np.float32), np.array([0.0, -0.0, -1.0, np.nan, 4.0], dtype=np.float32)])
+    want = (np.float32(1.0) / np.maximum(np.nan_to_num(x, nan=0.0), np.finfo(np.float32).tiny)).astype(np.float32)
+    got = debug.math(device_model, debug.OP_SINKHORN_RCP, x)
+    assert _bits_equal(got, want), _mismatch(got, want)
+
+
 def _tensor_index(oracle_model, want):
     """Archive index of a tensor by its canonical position (layout.rs:190-230)."""
     layers, per_layer = oracle_model.num_layers, 24
