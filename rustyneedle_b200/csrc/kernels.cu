@@ -1058,12 +1058,14 @@ __device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
 __device__ float2 g_negzero = {-0.0f, -0.0f};
 
 template <int S, int R, bool FUSED32>
-__device__ __forceinline__ void tn_stage(const float* __restrict__ A, const float* __restrict__ B, float* __restrict__ C, float2 nz) {
+__device__ __forceinline__ void tn_stage(const float* __restrict__ A, const float* __restrict__ B, float* __restrict__ C, float2 nz,
+                                         int rows = R) {
   // A thread owns a 4-row × 2-column tile: per step one float4 of A, one
   // float2 of B, and the two columns of a row share one packed f32x2 product.
-  constexpr int TILES = (R / 4) * (HADA_RIGHT / 2);
+  // Only the first `rows` output rows (a multiple of 4) are formed.
+  const int tiles = (rows / 4) * (HADA_RIGHT / 2);
   const int tid = threadIdx.x;
-  if (tid < TILES) {
+  if (tid < tiles) {
     const int r0 = (tid / (HADA_RIGHT / 2)) * 4, c0 = (tid % (HADA_RIGHT / 2)) * 2;
     float2 acc[4];
 #pragma unroll
@@ -1088,10 +1090,13 @@ __device__ __forceinline__ void tn_stage(const float* __restrict__ A, const floa
   __syncthreads();
 }
 
+// One Kronecker factor application; out_rows limits the second product to
+// the output rows that are read afterwards.
 template <int LEFT, bool FUSED32>
-__device__ __forceinline__ void kronecker(float* xt, float* tmp, const float* left, const float* right, float* out, float2 nz) {
+__device__ __forceinline__ void kronecker(float* xt, float* tmp, const float* left, const float* right, float* out, float2 nz,
+                                          int out_rows = LEFT) {
   tn_stage<HADA_RIGHT, LEFT, FUSED32>(xt, right, tmp, nz);
-  tn_stage<LEFT, LEFT, FUSED32>(left, tmp, out, nz);
+  tn_stage<LEFT, LEFT, FUSED32>(left, tmp, out, nz, out_rows);
 }
 
 constexpr int BLOCK_THREADS = 256;
@@ -1100,19 +1105,23 @@ constexpr int BLOCK_THREADS = 256;
 template <int LEFT>
 __device__ __forceinline__ int transposed(int e) { return (e % HADA_RIGHT) * LEFT + e / HADA_RIGHT; }
 
-// The Hadamard MLP of hadamard.rs:260-304 on the pre-normed input s_pre (d
-// values): rank-8 condition softmax, modulation, three Kronecker factor
-// applications with the two permutations and the SiLU gate. The result (before
-// the final d4 scale) is left in buf0. cond_v, left[0] and right[0] must
-// already be staged in s_condv, s_left and s_right.
+// Rows of the last application's result that hold the d outputs (the rest
+// is padding the reference drops): ceil(d / 32), rounded up to whole 4-row tiles.
 template <int LEFT>
-__device__ __forceinline__ void hadamard_core(const ModelDev& md, const HadamardDev& Hd, const int d, const float* s_pre, float* buf0,
-                                              float* buf1, float* s_mod, float* s_left, float* s_right, float* s_condv) {
+__device__ __forceinline__ int output_rows(int d) {
+  return min(LEFT, (d / HADA_RIGHT + 3) / 4 * 4);
+}
+
+// The front of the Hadamard MLP (hadamard.rs:260-283) on the pre-normed
+// input s_pre (d values): the rank-8 condition softmax, the modulation
+// 1 + Σ_r w_r·cond_u[r] into s_mod and X = pad(x) ⊙ d1, transposed, into xt.
+// cond_v must already be staged in s_condv (it is overwritten).
+template <int LEFT>
+__device__ __forceinline__ void hada_prepare(const HadamardDev& Hd, const int d, const float* s_pre, float* xt, float* s_mod,
+                                             float* s_condv) {
   constexpr int N = LEFT * HADA_RIGHT;
   constexpr int PER = N / (4 * BLOCK_THREADS);
-  constexpr bool FUSED32 = LEFT == 32;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const float2 nz = g_negzero;
   __shared__ float s_w[COND_RANK];
   // condition weights: four chains of rank-8 partial sums (hadamard.rs:263-276).
   // Chain (j, r) adds x[4g+j]·cond_v[4g+j][r] over g in order; the products
@@ -1170,86 +1179,114 @@ __device__ __forceinline__ void hadamard_core(const ModelDev& md, const Hadamard
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
       int i = 4 * i4 + e;
-      buf0[transposed<LEFT>(i)] = fmul(i < d ? s_pre[i] : 0.0f, dv[e]);
+      xt[transposed<LEFT>(i)] = fmul(i < d ? s_pre[i] : 0.0f, dv[e]);
     }
   }
   __syncthreads();
-  // the next elementwise pass's constants are loaded into registers before
-  // each Kronecker application, so their latency hides behind it
+}
+
+// The operands of the two elementwise passes, loaded into registers ahead of
+// the Kronecker application they follow so their latency hides behind it.
+template <int LEFT>
+struct HadaPass1 {
+  static constexpr int PER = LEFT * HADA_RIGHT / (4 * BLOCK_THREADS);
   int4 p1[PER];
   float4 d2v[PER], b2v[PER];
+  __device__ __forceinline__ void load(const ModelDev& md, const HadamardDev& Hd) {
 #pragma unroll
-  for (int q = 0; q < PER; ++q) {
-    const int i4 = tid + q * BLOCK_THREADS;
-    p1[q] = reinterpret_cast<const int4*>(md.perm1)[i4];
-    d2v[q] = reinterpret_cast<const float4*>(Hd.d2)[i4];
-    b2v[q] = reinterpret_cast<const float4*>(Hd.b2)[i4];
+    for (int q = 0; q < PER; ++q) {
+      const int i4 = threadIdx.x + q * BLOCK_THREADS;
+      p1[q] = reinterpret_cast<const int4*>(md.perm1)[i4];
+      d2v[q] = reinterpret_cast<const float4*>(Hd.d2)[i4];
+      b2v[q] = reinterpret_cast<const float4*>(Hd.b2)[i4];
+    }
   }
+  // xt[transposed(i)] = silu(d2 ⊙ modulation ⊙ in[perm1[i]] + b2)  (hadamard.rs:288-294)
+  __device__ __forceinline__ void run(const float* s_mod, const float* in, float* xt) const {
+#pragma unroll
+    for (int q = 0; q < PER; ++q) {
+      const int i4 = threadIdx.x + q * BLOCK_THREADS;
+      const float4 mo = *reinterpret_cast<const float4*>(s_mod + 4 * i4);
+      const int pv[4] = {p1[q].x, p1[q].y, p1[q].z, p1[q].w};
+      const float dv[4] = {d2v[q].x, d2v[q].y, d2v[q].z, d2v[q].w}, bv[4] = {b2v[q].x, b2v[q].y, b2v[q].z, b2v[q].w},
+                  mv[4] = {mo.x, mo.y, mo.z, mo.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) xt[transposed<LEFT>(4 * i4 + e)] = silu(fadd(fmul(fmul(dv[e], mv[e]), in[pv[e]]), bv[e]));
+    }
+  }
+};
+
+template <int LEFT>
+struct HadaPass2 {
+  static constexpr int PER = LEFT * HADA_RIGHT / (4 * BLOCK_THREADS);
+  int4 p2[PER];
+  float4 d3v[PER];
+  __device__ __forceinline__ void load(const ModelDev& md, const HadamardDev& Hd) {
+#pragma unroll
+    for (int q = 0; q < PER; ++q) {
+      const int i4 = threadIdx.x + q * BLOCK_THREADS;
+      p2[q] = reinterpret_cast<const int4*>(md.perm2)[i4];
+      d3v[q] = reinterpret_cast<const float4*>(Hd.d3)[i4];
+    }
+  }
+  // xt[transposed(i)] = in[perm2[i]] ⊙ d3  (hadamard.rs:296-300)
+  __device__ __forceinline__ void run(const float* in, float* xt) const {
+#pragma unroll
+    for (int q = 0; q < PER; ++q) {
+      const int i4 = threadIdx.x + q * BLOCK_THREADS;
+      const int pv[4] = {p2[q].x, p2[q].y, p2[q].z, p2[q].w};
+      const float dv[4] = {d3v[q].x, d3v[q].y, d3v[q].z, d3v[q].w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) xt[transposed<LEFT>(4 * i4 + e)] = fmul(in[pv[e]], dv[e]);
+    }
+  }
+};
+
+// The Hadamard MLP of hadamard.rs:260-304 on the pre-normed input s_pre (d
+// values): rank-8 condition softmax, modulation, three Kronecker factor
+// applications with the two permutations and the SiLU gate. The result (before
+// the final d4 scale) is left in buf0[0..d). cond_v, left[0] and right[0] must
+// already be staged in s_condv, s_left and s_right.
+template <int LEFT>
+__device__ __forceinline__ void hadamard_core(const ModelDev& md, const HadamardDev& Hd, const int d, const float* s_pre, float* buf0,
+                                              float* buf1, float* s_mod, float* s_left, float* s_right, float* s_condv) {
+  constexpr bool FUSED32 = LEFT == 32;
+  const float2 nz = g_negzero;
+  hada_prepare<LEFT>(Hd, d, s_pre, buf0, s_mod, s_condv);
+  HadaPass1<LEFT> pass1;
+  pass1.load(md, Hd);
   kronecker<LEFT, FUSED32>(buf0, buf1, s_left, s_right, buf0, nz);  // first = K1(d1 ⊙ x)
   stage_async(s_left, Hd.left[1], LEFT * LEFT);
   stage_async(s_right, Hd.right[1], HADA_RIGHT * HADA_RIGHT);
-#pragma unroll
-  for (int q = 0; q < PER; ++q) {
-    const int i4 = tid + q * BLOCK_THREADS;
-    const float4 mo = *reinterpret_cast<const float4*>(s_mod + 4 * i4);
-    const int pv[4] = {p1[q].x, p1[q].y, p1[q].z, p1[q].w};
-    const float dv[4] = {d2v[q].x, d2v[q].y, d2v[q].z, d2v[q].w}, bv[4] = {b2v[q].x, b2v[q].y, b2v[q].z, b2v[q].w},
-                mv[4] = {mo.x, mo.y, mo.z, mo.w};
-#pragma unroll
-    for (int e = 0; e < 4; ++e) buf1[transposed<LEFT>(4 * i4 + e)] = silu(fadd(fmul(fmul(dv[e], mv[e]), buf0[pv[e]]), bv[e]));
-  }
-  int4 p2[PER];
-  float4 d3v[PER];
-#pragma unroll
-  for (int q = 0; q < PER; ++q) {
-    const int i4 = tid + q * BLOCK_THREADS;
-    p2[q] = reinterpret_cast<const int4*>(md.perm2)[i4];
-    d3v[q] = reinterpret_cast<const float4*>(Hd.d3)[i4];
-  }
+  pass1.run(s_mod, buf0, buf1);
+  HadaPass2<LEFT> pass2;
+  pass2.load(md, Hd);
   cp_async_wait_all();
   __syncthreads();
   kronecker<LEFT, FUSED32>(buf1, buf0, s_left, s_right, buf1, nz);  // second
   stage_async(s_left, Hd.left[2], LEFT * LEFT);
   stage_async(s_right, Hd.right[2], HADA_RIGHT * HADA_RIGHT);
-#pragma unroll
-  for (int q = 0; q < PER; ++q) {
-    const int i4 = tid + q * BLOCK_THREADS;
-    const int pv[4] = {p2[q].x, p2[q].y, p2[q].z, p2[q].w};
-    const float dv[4] = {d3v[q].x, d3v[q].y, d3v[q].z, d3v[q].w};
-#pragma unroll
-    for (int e = 0; e < 4; ++e) buf0[transposed<LEFT>(4 * i4 + e)] = fmul(buf1[pv[e]], dv[e]);
-  }
+  pass2.run(buf1, buf0);
   cp_async_wait_all();
   __syncthreads();
-  kronecker<LEFT, FUSED32>(buf0, buf1, s_left, s_right, buf0, nz);  // third
+  kronecker<LEFT, FUSED32>(buf0, buf1, s_left, s_right, buf0, nz, output_rows<LEFT>(d));  // third
 }
 
+// The front of the block finish (session.rs:121-137): the layer's constant
+// operands (cond_v, the first Kronecker factors, the two norm gains) by bulk
+// copy, then (once the previous kernel is done) the token's rows, the post
+// norm and gated residual into s_a, and the pre-Hadamard norm into s_pre.
+// False when the token is not live: the CTA has then waited for its copies
+// and returns.
 template <int LEFT>
-__global__ void __launch_bounds__(BLOCK_THREADS) k_block(ModelDev md, LayerDev L, Work w, int M, int* error) {
-  extern __shared__ float sm[];
-  constexpr int N = LEFT * HADA_RIGHT;
-  const int t = blockIdx.x;
-  const int d = md.d_model, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  float* s_a = sm;                        // d: attention output, then the running block value
-  float* s_x = sm + MAX_D;                // d: the routing input
-  float* s_pre = sm + 2 * MAX_D;          // d: pre-Hadamard norm
-  float* buf0 = sm + 3 * MAX_D;           // N
-  float* buf1 = buf0 + N;                 // N
-  float* s_mod = buf1 + N;                // N
-  float* s_left = s_mod + N;              // LEFT*LEFT
-  float* s_right = s_left + LEFT * LEFT;  // 32*32
-  // d*8 condition values, consumed before the first Kronecker stage: they
-  // borrow buf1 and s_mod when they fit there
-  float* s_condv = d * COND_RANK <= 2 * N ? buf1 : s_right + HADA_RIGHT * HADA_RIGHT;
-  float* s_gpost = s_right + HADA_RIGHT * HADA_RIGHT + (d * COND_RANK <= 2 * N ? 0 : d * COND_RANK);  // d post_norm gains
-  float* s_gpre = s_gpost + MAX_D;                                                                     // d pre_hada gains
+__device__ __forceinline__ bool block_front(const LayerDev& L, const Work& w, int M, int t, int d, int* error, float* s_a, float* s_x,
+                                            float* s_pre, float* s_condv, float* s_left, float* s_right, float* s_gpost,
+                                            float* s_gpre) {
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   __shared__ float s_inv, s_gate;
   __shared__ __align__(8) uint64_t s_bar;
   const uint32_t bar = smem_u32(&s_bar);
   const HadamardDev& Hd = L.hada;
-
-  // the layer's constant weights first (bulk copies, one thread), then (once
-  // the previous kernel is done) the token's rows
   if (tid == 0) {  // one thread arms the barrier and issues every copy
     bulk_start(bar, (d * COND_RANK + LEFT * LEFT + HADA_RIGHT * HADA_RIGHT + 2 * d) * 4);
     bulk_copy(s_condv, Hd.cond_v, d * COND_RANK * 4, bar);
@@ -1262,7 +1299,7 @@ __global__ void __launch_bounds__(BLOCK_THREADS) k_block(ModelDev md, LayerDev L
   pdl_wait();
   if (t >= M || w.meta[t].slot < 0) {
     if (tid == 0 && !mbar_wait(bar, 0)) atomicExch(error, 1);  // no copy outlives the CTA
-    return;
+    return false;
   }
   stage_async(s_a, w.outp + (size_t)t * d, d);
   stage_async(s_x, w.x + (size_t)t * d, d);
@@ -1287,6 +1324,42 @@ __global__ void __launch_bounds__(BLOCK_THREADS) k_block(ModelDev md, LayerDev L
   }
   __syncthreads();
   for (int i = tid; i < d; i += BLOCK_THREADS) s_pre[i] = fmul(fmul(fadd(1.0f, s_gpre[i]), s_a[i]), s_inv);
+  return true;
+}
+
+// x += mlp · d4; delta = x - input; next lane l = Σ_s res[l][s]·lane_s + post[l]·delta
+// (lanes.rs:183-204) for element i.
+__device__ __forceinline__ float lane_out(const float* rw, const float* sv, int l, float delta) {
+  float acc = 0.0f;
+#pragma unroll
+  for (int s = 0; s < LANES; ++s) acc = fadd(acc, fmul(rw[LANES + l * LANES + s], sv[s]));
+  return fadd(acc, fmul(rw[l], delta));
+}
+
+// grid M, block 256. Post norm, gated residual (session.rs:121-125), the
+// Hadamard MLP (hadamard.rs:260-304) and the lane combine (lanes.rs:183-204).
+template <int LEFT>
+__global__ void __launch_bounds__(BLOCK_THREADS) k_block(ModelDev md, LayerDev L, Work w, int M, int* error) {
+  extern __shared__ float sm[];
+  constexpr int N = LEFT * HADA_RIGHT;
+  const int t = blockIdx.x;
+  const int d = md.d_model, tid = threadIdx.x;
+  float* s_a = sm;                        // d: attention output, then the running block value
+  float* s_x = sm + MAX_D;                // d: the routing input
+  float* s_pre = sm + 2 * MAX_D;          // d: pre-Hadamard norm
+  float* buf0 = sm + 3 * MAX_D;           // N
+  float* buf1 = buf0 + N;                 // N
+  float* s_mod = buf1 + N;                // N
+  float* s_left = s_mod + N;              // LEFT*LEFT
+  float* s_right = s_left + LEFT * LEFT;  // 32*32
+  // d*8 condition values, consumed before the first Kronecker stage: they
+  // borrow buf1 and s_mod when they fit there
+  float* s_condv = d * COND_RANK <= 2 * N ? buf1 : s_right + HADA_RIGHT * HADA_RIGHT;
+  float* s_gpost = s_right + HADA_RIGHT * HADA_RIGHT + (d * COND_RANK <= 2 * N ? 0 : d * COND_RANK);  // d post_norm gains
+  float* s_gpre = s_gpost + MAX_D;                                                                     // d pre_hada gains
+  const HadamardDev& Hd = L.hada;
+
+  if (!block_front<LEFT>(L, w, M, t, d, error, s_a, s_x, s_pre, s_condv, s_left, s_right, s_gpost, s_gpre)) return;
   // the lane combine's operands (routing weights, this token's lanes, d4) load
   // while the Hadamard MLP runs; one float4 column per thread (d <= 4 · 256)
   const float* route = w.route + (size_t)t * (LANES + LANES * LANES);
@@ -1305,7 +1378,6 @@ __global__ void __launch_bounds__(BLOCK_THREADS) k_block(ModelDev md, LayerDev L
   __syncthreads();
   hadamard_core<LEFT>(md, Hd, d, s_pre, buf0, buf1, s_mod, s_left, s_right, s_condv);
   pdl_trigger();  // the lane combine overlaps the next kernel's prologue
-  // x += mlp; delta = x - input; next lanes (lanes.rs:183-204)
   if (i4 < d / 4) {
     const float dv[4] = {d4.x, d4.y, d4.z, d4.w};
     float delta[4];
@@ -1319,13 +1391,136 @@ __global__ void __launch_bounds__(BLOCK_THREADS) k_block(ModelDev md, LayerDev L
       float o[4];
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        float acc = 0.0f;
-#pragma unroll
-        for (int s = 0; s < LANES; ++s) acc = fadd(acc, fmul(rw[LANES + l * LANES + s], (&sv[s].x)[e]));
-        o[e] = fadd(acc, fmul(rw[l], delta[e]));
+        const float lanes_e[LANES] = {(&sv[0].x)[e], (&sv[1].x)[e], (&sv[2].x)[e], (&sv[3].x)[e]};
+        o[e] = lane_out(rw, lanes_e, l, delta[e]);
       }
       reinterpret_cast<float4*>(next + l * d)[i4] = make_float4(o[0], o[1], o[2], o[3]);
     }
+  }
+}
+
+// ------------------------------------------------ block finish over a cluster
+// For small passes the three Kronecker applications are split over a cluster
+// of CL CTAs by output column: column c of K(x) = Lᵀ·(X·R) depends only on
+// column c of R, so CTA q forms columns [q·W, (q+1)·W) of both products of
+// every application (one row and two columns per thread, the same ordered
+// sums), then stores its slice into every CTA's copy of the result through
+// distributed shared memory, since the elementwise pass after an application
+// permutes the whole vector. The norms, condition softmax, modulation and
+// elementwise passes run in every CTA of the cluster; the last application
+// and the lane combine stay split by column.
+template <int LEFT>
+struct BlockSplit {
+  static constexpr int W = 2 * BLOCK_THREADS / LEFT;  // columns per CTA: LEFT rows × W/2 column pairs = 256 threads
+  static constexpr int CL = HADA_RIGHT / W;           // CTAs per token: 4 (LEFT 64) or 2 (LEFT 32)
+};
+
+// Σ_s A[s][r]·B[s][c..c+1] over s ascending, from +0.0 (as tn_stage).
+template <int S, int R, bool FUSED32>
+__device__ __forceinline__ float2 col_pair(const float* __restrict__ A, const float* __restrict__ B, int bstride, int r, int c,
+                                           float2 nz) {
+  float2 acc = make_float2(0.0f, 0.0f);
+#pragma unroll 8
+  for (int s = 0; s < S; ++s) {
+    const float a = A[s * R + r];
+    const float2 b = *reinterpret_cast<const float2*>(B + s * bstride + c);
+    const float2 ai = make_float2(a, a);
+    acc = FUSED32 ? fma2(ai, b, acc) : add2(acc, fma2(ai, b, nz));
+  }
+  return acc;
+}
+
+template <int LEFT>
+__global__ void __launch_bounds__(BLOCK_THREADS) k_block_split(ModelDev md, LayerDev L, Work w, int M, int* error) {
+  namespace cg = cooperative_groups;
+  extern __shared__ float sm[];
+  constexpr int N = LEFT * HADA_RIGHT, W = BlockSplit<LEFT>::W, CL = BlockSplit<LEFT>::CL;
+  constexpr bool FUSED32 = LEFT == 32;
+  cg::cluster_group cluster = cg::this_cluster();
+  const int q = (int)cluster.block_rank(), t = blockIdx.x / CL;
+  const int d = md.d_model, tid = threadIdx.x;
+  const int cq = q * W;                                           // this CTA's first column
+  const int r = tid / (W / 2), cl = 2 * (tid % (W / 2));          // this thread's row and column pair (within the slice)
+  float* s_a = sm;                                                // d
+  float* s_x = sm + MAX_D;                                        // d
+  float* s_pre = sm + 2 * MAX_D;                                  // d
+  float* xa = sm + 3 * MAX_D;                                     // N: first and third applications' input (transposed)
+  float* xb = xa + N;                                             // N: the second's; then the third's slice of results
+  float* f1 = xb + N;                                             // N: the first application's result, all columns
+  float* f2 = f1 + N;                                             // N: the second's
+  float* s_mod = f2 + N;                                          // N
+  float* s_t = s_mod + N;                                         // LEFT × W: this CTA's columns of X·R
+  float* s_left = s_t + LEFT * W;                                 // LEFT*LEFT
+  float* s_right = s_left + LEFT * LEFT;                          // 32*32
+  // cond_v borrows f2 and s_mod: both stay untouched until the condition
+  // weights are formed (f2 is written by the cluster only after the first
+  // application, which every CTA reaches after its own condition softmax)
+  float* s_condv = d * COND_RANK <= 2 * N ? f2 : s_right + HADA_RIGHT * HADA_RIGHT;
+  float* s_gpost = s_right + HADA_RIGHT * HADA_RIGHT + (d * COND_RANK <= 2 * N ? 0 : d * COND_RANK);
+  float* s_gpre = s_gpost + MAX_D;
+  const HadamardDev& Hd = L.hada;
+  const float2 nz = g_negzero;
+
+  if (!block_front<LEFT>(L, w, M, t, d, error, s_a, s_x, s_pre, s_condv, s_left, s_right, s_gpost, s_gpre)) return;
+  cluster_arrive_relaxed();  // paired with the wait before the first remote store
+  // this CTA's elements of the lane combine: rows 0..d/32-1 of its columns
+  const int rows_d = d / HADA_RIGHT, own = rows_d * W;
+  const int ei = (tid / W) * HADA_RIGHT + cq + tid % W;
+  const float* route = w.route + (size_t)t * (LANES + LANES * LANES);
+  float rw[LANES + LANES * LANES], sv[LANES], d4 = 0.0f;
+#pragma unroll
+  for (int k = 0; k < LANES + LANES * LANES; ++k) rw[k] = route[k];
+  if (tid < own) {
+    d4 = Hd.d4[ei];
+#pragma unroll
+    for (int s = 0; s < LANES; ++s) sv[s] = w.stream[((size_t)t * LANES + s) * d + ei];
+  }
+  __syncthreads();
+  hada_prepare<LEFT>(Hd, d, s_pre, xa, s_mod, s_condv);
+  HadaPass1<LEFT> pass1;
+  pass1.load(md, Hd);
+
+  // application 1: this CTA's columns, then every CTA's copy of f1
+  float2 v;
+  *reinterpret_cast<float2*>(s_t + r * W + cl) = col_pair<HADA_RIGHT, LEFT, FUSED32>(xa, s_right + cq, HADA_RIGHT, r, cl, nz);
+  __syncthreads();
+  v = col_pair<LEFT, LEFT, FUSED32>(s_left, s_t, W, r, cl, nz);
+  cluster_wait();  // every CTA of the cluster runs: distributed shared memory is usable
+#pragma unroll
+  for (int p = 0; p < CL; ++p) *reinterpret_cast<float2*>(cluster.map_shared_rank(f1 + r * HADA_RIGHT + cq + cl, p)) = v;
+  cluster.sync();  // f1 is whole in every CTA; every local read of s_left and s_right is done
+  stage_async(s_left, Hd.left[1], LEFT * LEFT);
+  stage_async(s_right, Hd.right[1], HADA_RIGHT * HADA_RIGHT);
+  pass1.run(s_mod, f1, xb);
+  HadaPass2<LEFT> pass2;
+  pass2.load(md, Hd);
+  cp_async_wait_all();
+  __syncthreads();
+
+  // application 2
+  *reinterpret_cast<float2*>(s_t + r * W + cl) = col_pair<HADA_RIGHT, LEFT, FUSED32>(xb, s_right + cq, HADA_RIGHT, r, cl, nz);
+  __syncthreads();
+  v = col_pair<LEFT, LEFT, FUSED32>(s_left, s_t, W, r, cl, nz);
+#pragma unroll
+  for (int p = 0; p < CL; ++p) *reinterpret_cast<float2*>(cluster.map_shared_rank(f2 + r * HADA_RIGHT + cq + cl, p)) = v;
+  cluster.sync();  // f2 is whole; no remote access follows, so CTAs may leave independently
+  stage_async(s_left, Hd.left[2], LEFT * LEFT);
+  stage_async(s_right, Hd.right[2], HADA_RIGHT * HADA_RIGHT);
+  pass2.run(f2, xa);
+  cp_async_wait_all();
+  __syncthreads();
+
+  // application 3: only the rows that hold the d outputs, kept in this CTA
+  *reinterpret_cast<float2*>(s_t + r * W + cl) = col_pair<HADA_RIGHT, LEFT, FUSED32>(xa, s_right + cq, HADA_RIGHT, r, cl, nz);
+  __syncthreads();
+  if (r < rows_d) *reinterpret_cast<float2*>(xb + r * HADA_RIGHT + cq + cl) = col_pair<LEFT, LEFT, FUSED32>(s_left, s_t, W, r, cl, nz);
+  __syncthreads();
+  pdl_trigger();  // the lane combine overlaps the next kernel's prologue
+  if (tid < own) {
+    const float delta = fsub(fadd(s_a[ei], fmul(xb[ei], d4)), s_x[ei]);
+    float* next = w.next_stream + (size_t)t * LANES * d;
+#pragma unroll
+    for (int l = 0; l < LANES; ++l) next[l * d + ei] = lane_out(rw, sv, l, delta);
   }
 }
 
@@ -1500,6 +1695,12 @@ size_t block_smem(const ModelDev& md) {
   if ((int)md.d_model * COND_RANK > 2 * N) floats += (size_t)md.d_model * COND_RANK;
   return floats * 4;
 }
+size_t block_split_smem(const ModelDev& md) {
+  const int left = md.hada_left, N = left * HADA_RIGHT, W = 2 * BLOCK_THREADS / left;
+  size_t floats = 3 * MAX_D + 5 * N + left * W + left * left + HADA_RIGHT * HADA_RIGHT + 2 * MAX_D;
+  if ((int)md.d_model * COND_RANK > 2 * N) floats += (size_t)md.d_model * COND_RANK;
+  return floats * 4;
+}
 
 cudaError_t configure(const ModelDev& md, int t_cap) {
   cudaError_t e;
@@ -1512,6 +1713,8 @@ cudaError_t configure(const ModelDev& md, int t_cap) {
   if ((e = cudaFuncSetAttribute(k_attend<4, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, att_smem))) return e;
   if ((e = cudaFuncSetAttribute(k_block<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)block_smem(md)))) return e;
   if ((e = cudaFuncSetAttribute(k_block<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)block_smem(md)))) return e;
+  if ((e = cudaFuncSetAttribute(k_block_split<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)block_split_smem(md)))) return e;
+  if ((e = cudaFuncSetAttribute(k_block_split<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)block_split_smem(md)))) return e;
   if ((e = cudaFuncSetAttribute(k_stats, cudaFuncAttributeMaxDynamicSharedMemorySize, 2 * 8192 * 4))) return e;
   if ((e = cudaFuncSetAttribute(k_gemm<16, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gemm_smem<16>()))) return e;
   if ((e = cudaFuncSetAttribute(k_gemm<32, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gemm_smem<32>()))) return e;
@@ -1602,6 +1805,30 @@ void launch_embed(const ModelDev& md, const Work& w, int M, cudaStream_t st) {
   launch(k_embed, M, 128, 0, st, md, w, M);
 }
 
+// The block finish: split over a cluster by Kronecker output column for
+// passes of at most BLOCK_SPLIT_MAX_TOKENS tokens, where one CTA per token
+// leaves most SMs idle and the FP32 products set the latency; one CTA per
+// token above, where the whole GPU is busy and the split's repeated front
+// (norms, softmax, elementwise passes in every CTA of a cluster) would cost
+// throughput. $NEEDLE_B200_BLOCK_SPLIT=N sets the threshold (0: never).
+constexpr int BLOCK_SPLIT_MAX_TOKENS = 64;
+static void launch_block(const ModelDev& md, const LayerDev& L, const Work& w, int M, cudaStream_t st) {
+  static const int max_tokens = [] {
+    const char* e = std::getenv("NEEDLE_B200_BLOCK_SPLIT");
+    return e ? std::atoi(e) : BLOCK_SPLIT_MAX_TOKENS;
+  }();
+  const int left = md.hada_left, W = 2 * BLOCK_THREADS / left, CL = HADA_RIGHT / W;
+  // every thread of a CTA takes at most one element of the lane combine
+  const bool split = M <= max_tokens && ((int)md.d_model / HADA_RIGHT) * W <= BLOCK_THREADS;
+  if (split) {
+    auto k = left == 64 ? k_block_split<64> : k_block_split<32>;
+    launch_clustered(k, dim3(M * CL), BLOCK_THREADS, block_split_smem(md), st, dim3(CL, 1, 1), md, L, w, M, g_gemm_error);
+  } else {
+    auto k = left == 64 ? k_block<64> : k_block<32>;
+    launch(k, M, BLOCK_THREADS, block_smem(md), st, md, L, w, M, g_gemm_error);
+  }
+}
+
 void launch_layer(const ModelDev& md, const LayerDev& L, const Work& w, const KvDev& kv, int M, int layer, int slot, int t_cap,
                   cudaStream_t st) {
   t_pass_tokens = M;
@@ -1617,10 +1844,7 @@ void launch_layer(const ModelDev& md, const LayerDev& L, const Work& w, const Kv
            md.inv_sqrt_group, 1, 0);
   }
   project(L.out, w.act, w.act_scale, w.outp, M, d, w.meta, st);
-  if (md.hada_left == 64)
-    launch(k_block<64>, M, BLOCK_THREADS, block_smem(md), st, md, L, w, M, g_gemm_error);
-  else
-    launch(k_block<32>, M, BLOCK_THREADS, block_smem(md), st, md, L, w, M, g_gemm_error);
+  launch_block(md, L, w, M, st);
 }
 
 void launch_final(const ModelDev& md, const Work& w, float* hidden, int M, cudaStream_t st) {
