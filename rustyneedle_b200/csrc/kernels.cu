@@ -616,16 +616,15 @@ constexpr size_t gemm_smem() {
 // ------------------------------------------------------------------- heads
 // grid M, block 32·(heads + 2·kv_heads). One warp per q, k or v head; lane l
 // holds elements l and l+32, the two halves rotary pairs (ops.rs:131-141).
-__global__ void k_heads(ModelDev md, LayerDev L, Work w, KvDev kv, int M, int layer) {
-  pdl_wait();
-  int t = blockIdx.x;
-  if (t >= M) return;
-  const TokenMeta meta = w.meta[t];
-  if (meta.slot < 0) return;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+// One head of one token, one warp (attention.rs:118-143): zero-centred norm
+// and rotary for query and key heads, then quantise_int8 (ops.rs:112-118).
+// kind 0 = query head `head`: its 64 codes go to q_out and the scale is
+// returned; 1 = key head, 2 = value head: codes and scale go into the token's
+// slot of its KV page.
+__device__ __forceinline__ float head_codes(const ModelDev& md, const LayerDev& L, const Work& w, const KvDev& kv, int t,
+                                            const TokenMeta& meta, int layer, int kind, int head, int8_t* q_out) {
+  const int lane = threadIdx.x & 31;
   const int H = md.heads, KV = md.kv_heads;
-  const int kind = warp < H ? 0 : (warp < H + KV ? 1 : 2);
-  const int head = kind == 0 ? warp : (kind == 1 ? warp - H : warp - H - KV);
   // proj rows: q [H*64] | k [KV*64] | v [KV*64] | gate [H*64]
   const float* src = w.proj + (size_t)t * (2 * H + 2 * KV) * HEAD_DIM + (kind == 0 ? 0 : (kind == 1 ? H * HEAD_DIM : (H + KV) * HEAD_DIM)) +
                      head * HEAD_DIM;
@@ -666,11 +665,9 @@ __global__ void k_heads(ModelDev md, LayerDev L, Work w, KvDev kv, int M, int la
   int8_t c0 = (int8_t)clampf(rintf(fdiv(e0, scale)), -128.0f, 127.0f);
   int8_t c1 = (int8_t)clampf(rintf(fdiv(e1, scale)), -128.0f, 127.0f);
   if (kind == 0) {
-    int8_t* q = w.qcodes + ((size_t)t * H + head) * HEAD_DIM;
-    q[lane] = c0;
-    q[lane + 32] = c1;
-    if (lane == 0) w.qscale[(size_t)t * H + head] = scale;
-    return;
+    q_out[lane] = c0;
+    q_out[lane + 32] = c1;
+    return scale;
   }
   const PageGeometry& pg = md.page;
   int p = meta.position % PAGE_POSITIONS;
@@ -684,6 +681,59 @@ __global__ void k_heads(ModelDev md, LayerDev L, Work w, KvDev kv, int M, int la
     panel[lane * 4] = c0;
     panel[(lane + 32) * 4] = c1;
     if (lane == 0) reinterpret_cast<float*>(page + pg.vscale_offset)[head * PAGE_POSITIONS + p] = scale;
+  }
+  return scale;
+}
+
+// grid M, block 32·(H + 2·KV): one warp per query, key and value head.
+__global__ void k_heads(ModelDev md, LayerDev L, Work w, KvDev kv, int M, int layer) {
+  pdl_wait();
+  int t = blockIdx.x;
+  if (t >= M) return;
+  const TokenMeta meta = w.meta[t];
+  if (meta.slot < 0) return;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int H = md.heads, KV = md.kv_heads;
+  const int kind = warp < H ? 0 : (warp < H + KV ? 1 : 2);
+  const int head = kind == 0 ? warp : (kind == 1 ? warp - H : warp - H - KV);
+  const float scale = head_codes(md, L, w, kv, t, meta, layer, kind, head, w.qcodes + ((size_t)t * H + head) * HEAD_DIM);
+  if (kind == 0 && lane == 0) w.qscale[(size_t)t * H + head] = scale;
+}
+
+// ------------------------------------------------------ int8 activation prep
+// in (K values, optionally times sigmoid(gate)) → fake_quantise_int8 (when
+// `fake`) → per-group rotation and int8 codes of row t, by the whole block;
+// s_v holds K floats, s_red one float per warp. Used for out_proj
+// (attention.rs:145-150) and the logits (session.rs:170-175). The inputs are
+// read from L2 (another CTA of the same kernel may have written them).
+constexpr int PREP_MAX_K = 2048;
+
+__device__ __forceinline__ void prep_token(const float* src, const float* gate, int K, int8_t* act, float* act_scale, int t,
+                                           float inv_sqrt_group, int fake, int act_rows, float* s_v, float* s_red) {
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  float peak = 0.0f;
+  for (int i4 = tid; i4 < K / 4; i4 += blockDim.x) {
+    float4 v = __ldcg(reinterpret_cast<const float4*>(src) + i4);
+    if (gate) {
+      const float4 gv = __ldcg(reinterpret_cast<const float4*>(gate) + i4);
+      v = make_float4(fmul(v.x, sigmoid(gv.x)), fmul(v.y, sigmoid(gv.y)), fmul(v.z, sigmoid(gv.z)), fmul(v.w, sigmoid(gv.w)));
+    }
+    reinterpret_cast<float4*>(s_v)[i4] = v;
+    peak = fmaxf(peak, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+  }
+  const float scale = int8_scale_of(block_max(peak, s_red));
+  const int groups = K / GROUP;
+  for (int g = warp; g < groups; g += blockDim.x >> 5) {
+    float v[4];
+    *reinterpret_cast<float4*>(v) = reinterpret_cast<const float4*>(s_v + g * GROUP)[lane];
+    if (fake)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) v[j] = fake_quant(v[j], scale);
+    fwht128(v, inv_sqrt_group);
+    uint32_t packed;
+    const float sc = quantise_group(v, packed);
+    *reinterpret_cast<uint32_t*>(act + chunked_offset(t, g * GROUP + 4 * lane, act_rows)) = packed;
+    if (lane == 0) act_scale[(size_t)t * groups + g] = sc;
   }
 }
 
@@ -701,15 +751,25 @@ constexpr int ATT_MAX_KV = 8;
 
 __host__ __device__ constexpr int att_wstride(int t_cap) { return t_cap / 4 + 2; }
 
-// With PREP (G * 64 values per CTA, whole 128-value groups) the kernel also
-// does k_prep's work for the output projection: the CTAs of one token form a
-// cluster over the kv heads, exchange the peak of their gated outputs in
-// distributed shared memory and each quantises its own groups.
+// The epilogue (EPI) either writes the output rows (ATT_ROWS; k_prep then
+// prepares the output projection's activations), or does k_prep's work
+// itself: with ATT_CLUSTER (G * 64 values per CTA, whole 128-value groups)
+// the CTAs of one token form a cluster over the kv heads, exchange the peak
+// of their gated outputs in distributed shared memory and each quantises its
+// own groups; with ATT_LAST every CTA writes its rows and counts itself in
+// w.arrivals[t], and the token's last CTA prepares the whole row.
+// With HEADS (a pass whose tokens all belong to different sequences) the CTA
+// first does k_heads' work for its kv head: its query heads' codes go
+// straight to shared memory, the key and value into the token's page slot,
+// which only this CTA reads in this pass.
+constexpr int ATT_ROWS = 0, ATT_CLUSTER = 1, ATT_LAST = 2;
 __device__ __forceinline__ void cluster_arrive_relaxed() { asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory"); }
 __device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.aligned;" ::: "memory"); }
 
-template <int G, bool PREP>
-__global__ void __launch_bounds__(ATT_THREADS_ALL, 3) k_attend(ModelDev md, Work w, KvDev kv, int M, int layer, int global, int t_cap) {
+template <int G, int EPI, bool HEADS>
+__global__ void __launch_bounds__(ATT_THREADS_ALL, 3) k_attend(ModelDev md, LayerDev L, Work w, KvDev kv, int M, int layer, int t_cap) {
+  constexpr bool PREP = EPI == ATT_CLUSTER;
+  const int global = L.global;
   pdl_wait();
   extern __shared__ float sm[];
   if ((int)blockIdx.x >= M) return;  // the whole cluster shares the token
@@ -737,12 +797,22 @@ __global__ void __launch_bounds__(ATT_THREADS_ALL, 3) k_attend(ModelDev md, Work
   const int* table = kv.page_table + ((size_t)meta.slot * kv.num_layers + layer) * kv.max_pages;
   const int npages = (total - 1) / PAGE_POSITIONS + 1;
   for (int i = tid; i < npages; i += blockDim.x) s_page[i] = kv.pool + (size_t)table[i] * pg.page_bytes;
-  if (tid < G * 16) {
-    int h = tid / 16, k = tid % 16;
-    s_q[h][k] = reinterpret_cast<const uint32_t*>(w.qcodes + ((size_t)t * md.heads + kvh * G + h) * HEAD_DIM)[k];
+  if (HEADS) {
+    // warps 0..G-1: query heads kvh·G + warp; warp G: key head kvh; warp G+1: value head kvh
+    if (warp < G + 2) {
+      const int kind = warp < G ? 0 : warp - G + 1;
+      const float sc = head_codes(md, L, w, kv, t, meta, layer, kind, kind == 0 ? kvh * G + warp : kvh,
+                                  reinterpret_cast<int8_t*>(s_q[kind == 0 ? warp : 0]));
+      if (kind == 0 && lane == 0) s_qs[warp] = fmul(sc, md.inv_root_qk);
+    }
+  } else {
+    if (tid < G * 16) {
+      int h = tid / 16, k = tid % 16;
+      s_q[h][k] = reinterpret_cast<const uint32_t*>(w.qcodes + ((size_t)t * md.heads + kvh * G + h) * HEAD_DIM)[k];
+    }
+    if (tid < G) s_qs[tid] = fmul(w.qscale[(size_t)t * md.heads + kvh * G + tid], md.inv_root_qk);
   }
-  if (tid < G) s_qs[tid] = fmul(w.qscale[(size_t)t * md.heads + kvh * G + tid], md.inv_root_qk);
-  __syncthreads();
+  __syncthreads();  // the query codes, and with HEADS this position's key and value, are in place
 
   if (tid < ATT_WORKERS) {
     // pass 1: integer scores q·k, coefficients (s · key_scale) · query_scale, their
@@ -937,6 +1007,23 @@ __global__ void __launch_bounds__(ATT_THREADS_ALL, 3) k_attend(ModelDev md, Work
     out = fmul(value, inverse);
     if (!PREP) w.attn[(size_t)t * md.heads * HEAD_DIM + (kvh * G + h) * HEAD_DIM + dim] = out;
   }
+  if (EPI == ATT_LAST) {
+    // the last of the token's kv-head CTAs prepares the output projection's
+    // activations for the whole row (the fence orders every CTA's rows
+    // before its count; the reader fences again before reading them)
+    __shared__ int s_last;
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) s_last = atomicAdd(&w.arrivals[t], 1) == (int)gridDim.y - 1;
+    __syncthreads();
+    if (s_last) {
+      __threadfence();
+      const int H = md.heads, KV = md.kv_heads, K = H * HEAD_DIM;
+      prep_token(w.attn + (size_t)t * K, w.proj + (size_t)t * (2 * H + 2 * KV) * HEAD_DIM + (H + 2 * KV) * HEAD_DIM, K, w.act,
+                 w.act_scale, t, md.inv_sqrt_group, 1, 0, s_e, &s_red[0][0]);
+      if (tid == 0) w.arrivals[t] = 0;  // ready for the next layer's attention
+    }
+  }
   if (PREP) {
     // k_prep (attention.rs:145-150): the output gated by sigmoid(gate), the
     // peak over the token's whole vector (all kv heads of the cluster), the
@@ -980,12 +1067,7 @@ __global__ void __launch_bounds__(ATT_THREADS_ALL, 3) k_attend(ModelDev md, Work
 }
 
 // ------------------------------------------------------ int8 activation prep
-// in[m] (K values, optionally times sigmoid(gate[m])) → fake_quantise_int8
-// (when `fake`) → per-group rotation and int8 codes. Used for out_proj
-// (attention.rs:145-150) and the logits (session.rs:170-175). grid M, block
-// 128; four consecutive values per thread and pass.
-constexpr int PREP_MAX_K = 2048;
-
+// prep_token for M rows (row rows[m] of `in` when rows is given). grid M, block 128.
 __global__ void __launch_bounds__(128) k_prep(const float* __restrict__ in, int in_stride, const int32_t* __restrict__ rows,
                                               const float* __restrict__ gate, int gate_stride, int K, int8_t* __restrict__ act,
                                               float* __restrict__ act_scale, int M, const TokenMeta* __restrict__ meta,
@@ -995,32 +1077,8 @@ __global__ void __launch_bounds__(128) k_prep(const float* __restrict__ in, int 
   __shared__ float s_red[4];
   const int t = blockIdx.x;
   if (t >= M || (meta && meta[t].slot < 0)) return;
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const float* src = in + (size_t)(rows ? rows[t] : t) * in_stride;
-  float peak = 0.0f;
-  for (int i4 = tid; i4 < K / 4; i4 += blockDim.x) {
-    float4 v = reinterpret_cast<const float4*>(src)[i4];
-    if (gate) {
-      const float4 gv = reinterpret_cast<const float4*>(gate + (size_t)t * gate_stride)[i4];
-      v = make_float4(fmul(v.x, sigmoid(gv.x)), fmul(v.y, sigmoid(gv.y)), fmul(v.z, sigmoid(gv.z)), fmul(v.w, sigmoid(gv.w)));
-    }
-    reinterpret_cast<float4*>(s_v)[i4] = v;
-    peak = fmaxf(peak, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
-  }
-  const float scale = int8_scale_of(block_max(peak, s_red));
-  const int groups = K / GROUP;
-  for (int g = warp; g < groups; g += blockDim.x >> 5) {
-    float v[4];
-    *reinterpret_cast<float4*>(v) = reinterpret_cast<const float4*>(s_v + g * GROUP)[lane];
-    if (fake)
-#pragma unroll
-      for (int j = 0; j < 4; ++j) v[j] = fake_quant(v[j], scale);
-    fwht128(v, inv_sqrt_group);
-    uint32_t packed;
-    const float sc = quantise_group(v, packed);
-    *reinterpret_cast<uint32_t*>(act + chunked_offset(t, g * GROUP + 4 * lane, act_rows)) = packed;
-    if (lane == 0) act_scale[(size_t)t * groups + g] = sc;
-  }
+  prep_token(in + (size_t)(rows ? rows[t] : t) * in_stride, gate ? gate + (size_t)t * gate_stride : nullptr, K, act, act_scale, t,
+             inv_sqrt_group, fake, act_rows, s_v, s_red);
 }
 
 // ------------------------------------------------------------ block finish
@@ -1702,15 +1760,21 @@ size_t block_split_smem(const ModelDev& md) {
   return floats * 4;
 }
 
+template <int G, int EPI>
+static cudaError_t attend_attributes(int smem) {
+  cudaError_t e = cudaFuncSetAttribute(k_attend<G, EPI, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  return e ? e : cudaFuncSetAttribute(k_attend<G, EPI, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+}
+
 cudaError_t configure(const ModelDev& md, int t_cap) {
   cudaError_t e;
   if ((e = cudaFuncSetAttribute(k_route, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)route_smem(md)))) return e;
   const int att_smem = (int)attend_smem(md, t_cap);
-  if ((e = cudaFuncSetAttribute(k_attend<1, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, att_smem))) return e;
-  if ((e = cudaFuncSetAttribute(k_attend<2, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, att_smem))) return e;
-  if ((e = cudaFuncSetAttribute(k_attend<4, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, att_smem))) return e;
-  if ((e = cudaFuncSetAttribute(k_attend<2, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, att_smem))) return e;
-  if ((e = cudaFuncSetAttribute(k_attend<4, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, att_smem))) return e;
+  if ((e = attend_attributes<1, ATT_ROWS>(att_smem)) || (e = attend_attributes<1, ATT_LAST>(att_smem)) ||
+      (e = attend_attributes<2, ATT_ROWS>(att_smem)) || (e = attend_attributes<2, ATT_CLUSTER>(att_smem)) ||
+      (e = attend_attributes<2, ATT_LAST>(att_smem)) || (e = attend_attributes<4, ATT_ROWS>(att_smem)) ||
+      (e = attend_attributes<4, ATT_CLUSTER>(att_smem)) || (e = attend_attributes<4, ATT_LAST>(att_smem)))
+    return e;
   if ((e = cudaFuncSetAttribute(k_block<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)block_smem(md)))) return e;
   if ((e = cudaFuncSetAttribute(k_block<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)block_smem(md)))) return e;
   if ((e = cudaFuncSetAttribute(k_block_split<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)block_split_smem(md)))) return e;
@@ -1830,19 +1894,24 @@ static void launch_block(const ModelDev& md, const LayerDev& L, const Work& w, i
 }
 
 void launch_layer(const ModelDev& md, const LayerDev& L, const Work& w, const KvDev& kv, int M, int layer, int slot, int t_cap,
-                  cudaStream_t st) {
+                  bool distinct, cudaStream_t st) {
   t_pass_tokens = M;
   const int d = md.d_model, H = md.heads, KV = md.kv_heads;
   const int proj_stride = (2 * H + 2 * KV) * HEAD_DIM;
   launch(k_route, M, 256, route_smem(md), st, md, L, w, M, layer, slot, g_gemm_error);
   project(L.qkvg, w.act, w.act_scale, w.proj, M, proj_stride, w.meta, st);
-  launch(k_heads, M, 32 * (H + 2 * KV), 0, st, md, L, w, kv, M, layer);
-  if (!launch_attend_prep(md, L, w, kv, M, layer, t_cap, st)) {
-    launch_attend(md, L, w, kv, M, layer, t_cap, st);
+  // the head step runs inside the attention when each token of the pass
+  // belongs to a different sequence; $NEEDLE_B200_FUSE_HEADS=0 keeps k_heads
+  static const bool heads_off = [] {
+    const char* e = std::getenv("NEEDLE_B200_FUSE_HEADS");
+    return e && e[0] == '0';
+  }();
+  const bool heads = distinct && !heads_off;
+  if (!heads) launch(k_heads, M, 32 * (H + 2 * KV), 0, st, md, L, w, kv, M, layer);
+  if (!launch_attention(md, L, w, kv, M, layer, t_cap, heads, st))
     launch(k_prep, M, 128, 0, st, (const float*)w.attn, H * HEAD_DIM, (const int32_t*)nullptr,
            (const float*)(w.proj + (H + 2 * KV) * HEAD_DIM), proj_stride, H * HEAD_DIM, w.act, w.act_scale, M, w.meta,
            md.inv_sqrt_group, 1, 0);
-  }
   project(L.out, w.act, w.act_scale, w.outp, M, d, w.meta, st);
   launch_block(md, L, w, M, st);
 }
@@ -1877,42 +1946,59 @@ void launch_advance(TokenMeta* meta, int B, cudaStream_t st) {
   launch(k_advance, (B + 127) / 128, 128, 0, st, meta, B);
 }
 
-void launch_attend(const ModelDev& md, const LayerDev& L, const Work& w, const KvDev& kv, int M, int layer, int t_cap, cudaStream_t st) {
-  t_pass_tokens = M;
-  const int G = md.heads / md.kv_heads, KV = md.kv_heads;
+// The attention of a pass with its neighbours fused in where the shapes
+// allow: the head step when `heads`, and the output projection's activation
+// step, by the cluster epilogue for passes of at most FUSE_PREP_MAX_TOKENS
+// tokens (a launch saved on the latency path) and by the last-CTA epilogue
+// above (the cluster over kv heads would cost the attention CTA scheduling
+// freedom there). False when k_prep must still run.
+// $NEEDLE_B200_FUSE_PREP=0 always leaves the activation step to k_prep.
+constexpr int FUSE_PREP_MAX_TOKENS = 64;
+
+template <int G, int EPI>
+static void attend_variant(bool heads, const ModelDev& md, const LayerDev& L, const Work& w, const KvDev& kv, int M, int layer,
+                           int t_cap, cudaStream_t st) {
+  const dim3 grid(M, md.kv_heads), cluster(1, EPI == ATT_CLUSTER ? md.kv_heads : 1, 1);
   const size_t smem = attend_smem(md, t_cap);
-  if (G == 1)
-    launch(k_attend<1, false>, dim3(M, KV), ATT_THREADS_ALL, smem, st, md, w, kv, M, layer, L.global, t_cap);
-  else if (G == 2)
-    launch(k_attend<2, false>, dim3(M, KV), ATT_THREADS_ALL, smem, st, md, w, kv, M, layer, L.global, t_cap);
+  if (heads)
+    launch_clustered(k_attend<G, EPI, true>, grid, ATT_THREADS_ALL, smem, st, cluster, md, L, w, kv, M, layer, t_cap);
   else
-    launch(k_attend<4, false>, dim3(M, KV), ATT_THREADS_ALL, smem, st, md, w, kv, M, layer, L.global, t_cap);
+    launch_clustered(k_attend<G, EPI, false>, grid, ATT_THREADS_ALL, smem, st, cluster, md, L, w, kv, M, layer, t_cap);
 }
 
-// Attention with the output projection's activation step fused in (whole
-// 128-value groups per CTA: 2 or 4 query heads per kv head, at most 8 kv
-// heads), for passes of at most FUSE_PREP_MAX_TOKENS tokens, where it saves a
-// launch on the latency path; larger passes keep k_prep, since the cluster
-// over kv heads costs the attention more CTA scheduling freedom than k_prep
-// costs on B200. False when the separate kernel must run.
-// $NEEDLE_B200_FUSE_PREP=0 keeps it always.
-constexpr int FUSE_PREP_MAX_TOKENS = 64;
-bool launch_attend_prep(const ModelDev& md, const LayerDev& L, const Work& w, const KvDev& kv, int M, int layer, int t_cap,
-                        cudaStream_t st) {
-  static const bool off = [] {
+bool launch_attention(const ModelDev& md, const LayerDev& L, const Work& w, const KvDev& kv, int M, int layer, int t_cap, bool heads,
+                      cudaStream_t st) {
+  static const bool prep_off = [] {
     const char* e = std::getenv("NEEDLE_B200_FUSE_PREP");
     return e && e[0] == '0';
   }();
-  const int G = md.heads / md.kv_heads, KV = md.kv_heads;
-  if (off || M > FUSE_PREP_MAX_TOKENS || (G != 2 && G != 4) || KV > ATT_MAX_KV || md.heads * HEAD_DIM != md.d_model) return false;
   t_pass_tokens = M;
-  const size_t smem = attend_smem(md, t_cap);
-  const dim3 cluster(1, KV, 1);
-  if (G == 2)
-    launch_clustered(k_attend<2, true>, dim3(M, KV), ATT_THREADS_ALL, smem, st, cluster, md, w, kv, M, layer, L.global, t_cap);
-  else
-    launch_clustered(k_attend<4, true>, dim3(M, KV), ATT_THREADS_ALL, smem, st, cluster, md, w, kv, M, layer, L.global, t_cap);
-  return true;
+  const int G = md.heads / md.kv_heads, K = md.heads * HEAD_DIM;
+  int epi = ATT_ROWS;
+  if (!prep_off) {
+    const bool whole_groups = (G == 2 || G == 4) && md.kv_heads <= ATT_MAX_KV && K == (int)md.d_model;
+    if (M <= FUSE_PREP_MAX_TOKENS && whole_groups)
+      epi = ATT_CLUSTER;
+    else if (K <= PREP_MAX_K && (size_t)G * t_cap >= (size_t)K && w.arrivals)
+      epi = ATT_LAST;
+  }
+  if (G == 1) {
+    if (epi == ATT_LAST)
+      attend_variant<1, ATT_LAST>(heads, md, L, w, kv, M, layer, t_cap, st);
+    else
+      attend_variant<1, ATT_ROWS>(heads, md, L, w, kv, M, layer, t_cap, st);
+    return epi == ATT_LAST;
+  }
+  if (G == 2) {
+    if (epi == ATT_CLUSTER) attend_variant<2, ATT_CLUSTER>(heads, md, L, w, kv, M, layer, t_cap, st);
+    if (epi == ATT_LAST) attend_variant<2, ATT_LAST>(heads, md, L, w, kv, M, layer, t_cap, st);
+    if (epi == ATT_ROWS) attend_variant<2, ATT_ROWS>(heads, md, L, w, kv, M, layer, t_cap, st);
+  } else {
+    if (epi == ATT_CLUSTER) attend_variant<4, ATT_CLUSTER>(heads, md, L, w, kv, M, layer, t_cap, st);
+    if (epi == ATT_LAST) attend_variant<4, ATT_LAST>(heads, md, L, w, kv, M, layer, t_cap, st);
+    if (epi == ATT_ROWS) attend_variant<4, ATT_ROWS>(heads, md, L, w, kv, M, layer, t_cap, st);
+  }
+  return epi != ATT_ROWS;
 }
 
 // ------------------------------------------------------------------- debug

@@ -14,8 +14,10 @@ cudaError_t configure(const nbl::ModelDev& md, int t_cap);
 void set_error_flag(int* flag);
 
 void launch_embed(const nbl::ModelDev& md, const nbl::Work& w, int M, cudaStream_t st);
+// One decoder layer of M tokens. `distinct`: every token of the pass belongs
+// to a different sequence (a decode step, or a one-token feed).
 void launch_layer(const nbl::ModelDev& md, const nbl::LayerDev& L, const nbl::Work& w, const nbl::KvDev& kv, int M, int layer,
-                  int slot, int t_cap, cudaStream_t st);
+                  int slot, int t_cap, bool distinct, cudaStream_t st);
 void launch_final(const nbl::ModelDev& md, const nbl::Work& w, float* hidden, int M, cudaStream_t st);
 void launch_logits(const nbl::ModelDev& md, const float* hidden, const int32_t* slots, int B, int8_t* act, float* act_scale,
                    float* logits, cudaStream_t st);
@@ -24,10 +26,11 @@ void launch_select(const float* logits, int V, const uint32_t* mask, const int32
 void launch_stats(const float* logits, int V, const uint32_t* mask, const int32_t* active, const uint32_t* next,
                   const float* peaks, float* stats, int stats_stride, int B, cudaStream_t st);
 void launch_advance(nbl::TokenMeta* meta, int B, cudaStream_t st);
-void launch_attend(const nbl::ModelDev& md, const nbl::LayerDev& L, const nbl::Work& w, const nbl::KvDev& kv, int M, int layer,
-                   int t_cap, cudaStream_t st);
-bool launch_attend_prep(const nbl::ModelDev& md, const nbl::LayerDev& L, const nbl::Work& w, const nbl::KvDev& kv, int M, int layer,
-                        int t_cap, cudaStream_t st);
+// The attention of a pass (with the head step when `heads`, and the output
+// projection's activation step where the shapes allow); false when k_prep
+// must still run.
+bool launch_attention(const nbl::ModelDev& md, const nbl::LayerDev& L, const nbl::Work& w, const nbl::KvDev& kv, int M, int layer,
+                      int t_cap, bool heads, cudaStream_t st);
 void launch_debug_hadamard(const nbl::ModelDev& md, const nbl::LayerDev& L, const float* in, float* out, int M, cudaStream_t st);
 void launch_debug_math(int op, const float* in, float* out, int n, cudaStream_t st);
 void launch_debug_project(const nbl::ModelDev& md, const nbl::QMat& W, const float* in, int K, int M, int8_t* act,

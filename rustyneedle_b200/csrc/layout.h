@@ -147,6 +147,7 @@ struct Work {
   float* qscale;            // [M][heads]
   float* attn;              // [M][heads * 64]
   float* outp;              // [M][d]
+  int* arrivals;            // [M] attention CTAs done per token (zero between passes)
 };
 
 struct KvDev {

@@ -584,6 +584,8 @@ std::shared_ptr<Engine> open_engine(const char* path, const nb_options* opt) {
   w.qscale = A.alloc<float>((size_t)M * H);
   w.attn = A.alloc<float>((size_t)M * AW);
   w.outp = A.alloc<float>((size_t)M * d);
+  w.arrivals = A.alloc<int>(M);
+  NB_CUDA(cudaMemsetAsync(w.arrivals, 0, (size_t)M * sizeof(int), st));
   const uint32_t B = E->max_sessions, V = md.output_vocab;
   const size_t logit_rows = ((size_t)B + 127) / 128 * 128;
   E->d_logit_act = A.alloc<int8_t>(logit_rows * d);
@@ -632,10 +634,17 @@ void forward(Engine& E, const std::vector<int32_t>& active, const TokenSpec* spe
   E.copies_in_flight = true;
   Work w = E.work;
   KvDev kv = E.kv();
+  // one token per sequence: the attention may do the head step itself
+  bool distinct = true;
+  std::vector<char> seen(E.max_sessions, 0);
+  for (uint32_t i = 0; i < count && distinct; ++i) {
+    distinct = !seen[specs[i].slot];
+    seen[specs[i].slot] = 1;
+  }
   nbk::launch_embed(E.md, w, (int)count, E.stream);
   for (size_t slot = 0; slot < active.size(); ++slot) {
     int layer = active[slot];
-    nbk::launch_layer(E.md, E.layers[layer], w, kv, (int)count, layer, (int)slot, E.t_cap, E.stream);
+    nbk::launch_layer(E.md, E.layers[layer], w, kv, (int)count, layer, (int)slot, E.t_cap, distinct, E.stream);
     std::swap(w.stream, w.next_stream);
   }
   nbk::launch_final(E.md, w, E.d_hidden, (int)count, E.stream);
@@ -924,6 +933,7 @@ static Work work_rows(const Engine& E, const Work& w, uint32_t b0) {
   s.qscale = w.qscale + b0 * H;
   s.attn = w.attn + b0 * H * HEAD_DIM;
   s.outp = w.outp + b0 * d;
+  s.arrivals = w.arrivals + b0;
   return s;
 }
 
@@ -949,7 +959,7 @@ static void build_group(nb_batch* b, bool masked, bool stats, uint32_t b0, uint3
   nbk::launch_embed(E.md, w, n, st);
   for (size_t slot = 0; slot < b->active.size(); ++slot) {
     int layer = b->active[slot];
-    nbk::launch_layer(E.md, E.layers[layer], w, kv, n, layer, (int)slot, E.t_cap, st);
+    nbk::launch_layer(E.md, E.layers[layer], w, kv, n, layer, (int)slot, E.t_cap, true, st);
     std::swap(w.stream, w.next_stream);
   }
   nbk::launch_final(E.md, w, E.d_hidden, n, st);
@@ -1441,10 +1451,11 @@ extern "C" nb_status nb_debug_time_attention(nb_batch* batch, uint32_t reps, flo
     w.meta = batch->d_meta;
     if (batch->groups == 1) w.order = batch->d_order;  // the step's launch order (per group otherwise)
     KvDev kv = E.kv();
-    // the attention kernel the step runs (with the output projection's activation step fused in where it is)
+    // the attention kernel the step runs, with the output projection's
+    // activation step fused in where it is; the head step (which the step
+    // also fuses in) is left out, since replaying it would rewrite the cache
     auto attend = [&](int32_t layer) {
-      if (!nbk::launch_attend_prep(E.md, E.layers[layer], w, kv, (int)B, layer, E.t_cap, E.stream))
-        nbk::launch_attend(E.md, E.layers[layer], w, kv, (int)B, layer, E.t_cap, E.stream);
+      nbk::launch_attention(E.md, E.layers[layer], w, kv, (int)B, layer, E.t_cap, false, E.stream);
     };
     cudaEvent_t start, stop;
     NB_CUDA(cudaEventCreate(&start));
