@@ -404,6 +404,7 @@ __global__ void __launch_bounds__(8 * NT) k_gemm(QMat W, const int8_t* __restric
   __shared__ uint32_t s_tmem;
   __shared__ float s_as[NT * GK];
   __shared__ int s_fail;
+  __shared__ bool s_live[NT];  // output column n is stored (a live token of the pass)
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int tile = blockIdx.x, m0 = blockIdx.y * NT, mcount = min(NT, M - m0);
   const uint32_t bar_load = smem_u32(&bars[0]), bar_mma = smem_u32(&bars[1]);
@@ -444,6 +445,7 @@ __global__ void __launch_bounds__(8 * NT) k_gemm(QMat W, const int8_t* __restric
   pdl_wait();
   if (tid == 0) copy(sB, tokens(0), B_BYTES);
   for (int i = tid; i < NT * GK; i += blockDim.x) s_as[i] = i / GK < mcount ? act_scale[(size_t)m0 * GK + i] : 0.0f;
+  if (tid < NT) s_live[tid] = tid < mcount && !(meta && meta[m0 + tid].slot < 0);
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
@@ -494,26 +496,35 @@ __global__ void __launch_bounds__(8 * NT) k_gemm(QMat W, const int8_t* __restric
     float total[16];
 #pragma unroll
     for (int j = 0; j < 16; ++j) total[j] = 0.0f;
+    // four groups' accumulators per batch, loaded together and waited for once
 #pragma unroll
-    for (int g = 0; g < GK; ++g) {
-      uint32_t a[16];
-      asm volatile(
-          "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
-          : "=r"(a[0]), "=r"(a[1]), "=r"(a[2]), "=r"(a[3]), "=r"(a[4]), "=r"(a[5]), "=r"(a[6]), "=r"(a[7]), "=r"(a[8]), "=r"(a[9]),
-            "=r"(a[10]), "=r"(a[11]), "=r"(a[12]), "=r"(a[13]), "=r"(a[14]), "=r"(a[15])
-          : "r"(lane_base + g * NT + c0));
+    for (int g0 = 0; g0 < GK; g0 += 4) {
+      uint32_t a[4][16];
+#pragma unroll
+      for (int gi = 0; gi < 4; ++gi)
+        asm volatile(
+            "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+            : "=r"(a[gi][0]), "=r"(a[gi][1]), "=r"(a[gi][2]), "=r"(a[gi][3]), "=r"(a[gi][4]), "=r"(a[gi][5]), "=r"(a[gi][6]),
+              "=r"(a[gi][7]), "=r"(a[gi][8]), "=r"(a[gi][9]), "=r"(a[gi][10]), "=r"(a[gi][11]), "=r"(a[gi][12]), "=r"(a[gi][13]),
+              "=r"(a[gi][14]), "=r"(a[gi][15])
+            : "r"(lane_base + (g0 + gi) * NT + c0));
       asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        const float acc = (float)(int)a[j];
-        const float as = s_as[(c0 + j) * GK + g];
-        total[j] = W.fused ? __fmaf_rn(acc, fmul(ws[g], as), total[j]) : fadd(total[j], fmul(fmul(fmul(acc, ws[g]), W.level_scale), as));
+      for (int gi = 0; gi < 4; ++gi) {
+        const int g = g0 + gi;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const float acc = (float)(int)a[gi][j];
+          const float as = s_as[(c0 + j) * GK + g];
+          total[j] =
+              W.fused ? __fmaf_rn(acc, fmul(ws[g], as), total[j]) : fadd(total[j], fmul(fmul(fmul(acc, ws[g]), W.level_scale), as));
+        }
       }
     }
 #pragma unroll
     for (int j = 0; j < 16; ++j) {
       const int n = c0 + j;
-      if (valid && n < mcount && !(meta && meta[m0 + n].slot < 0)) out[(size_t)(m0 + n) * out_stride + row] = total[j];
+      if (valid && s_live[n]) out[(size_t)(m0 + n) * out_stride + row] = total[j];
     }
   } else if (tid == 0) {
     atomicExch(error, 1);
@@ -793,6 +804,7 @@ __global__ void __launch_bounds__(ATT_THREADS_ALL, 3) k_attend(ModelDev md, Laye
   __shared__ const uint8_t* s_page[128];
   __shared__ float s_qs[MAX_GROUP], s_peak[MAX_GROUP], s_scale2[MAX_GROUP], s_total[MAX_GROUP];
   __shared__ float s_red[MAX_GROUP][ATT_WORKERS / 32];
+  __shared__ float s_gsig[EPI == ATT_ROWS ? 1 : MAX_GROUP * HEAD_DIM];  // sigmoid of this CTA's gate values
   const PageGeometry& pg = md.page;
   const int* table = kv.page_table + ((size_t)meta.slot * kv.num_layers + layer) * kv.max_pages;
   const int npages = (total - 1) / PAGE_POSITIONS + 1;
@@ -811,6 +823,13 @@ __global__ void __launch_bounds__(ATT_THREADS_ALL, 3) k_attend(ModelDev md, Laye
       s_q[h][k] = reinterpret_cast<const uint32_t*>(w.qcodes + ((size_t)t * md.heads + kvh * G + h) * HEAD_DIM)[k];
     }
     if (tid < G) s_qs[tid] = fmul(w.qscale[(size_t)t * md.heads + kvh * G + tid], md.inv_root_qk);
+  }
+  if (EPI != ATT_ROWS) {
+    // the output gate sigmoid(gate) of this CTA's G·64 values (attention.rs:145-150),
+    // by the warps the head step leaves idle
+    const int H = md.heads, KV = md.kv_heads, first_thread = HEADS ? (G + 2) * 32 : 0;
+    const float* gsrc = w.proj + (size_t)t * (2 * H + 2 * KV) * HEAD_DIM + (H + 2 * KV) * HEAD_DIM + kvh * G * HEAD_DIM;
+    for (int i = tid - first_thread; i >= 0 && i < G * HEAD_DIM; i += ATT_THREADS_ALL - first_thread) s_gsig[i] = sigmoid(gsrc[i]);
   }
   __syncthreads();  // the query codes, and with HEADS this position's key and value, are in place
 
@@ -1005,7 +1024,8 @@ __global__ void __launch_bounds__(ATT_THREADS_ALL, 3) k_attend(ModelDev md, Laye
     const float value = s_peak[h] > 0.0f ? fmul((float)sum, s_scale2[h]) : 0.0f;
     const float inverse = fdiv(1.0f, s_total[h]);
     out = fmul(value, inverse);
-    if (!PREP) w.attn[(size_t)t * md.heads * HEAD_DIM + (kvh * G + h) * HEAD_DIM + dim] = out;
+    // with ATT_LAST the rows are stored gated, ready for the last CTA's prep
+    if (!PREP) w.attn[(size_t)t * md.heads * HEAD_DIM + (kvh * G + h) * HEAD_DIM + dim] = EPI == ATT_LAST ? fmul(out, s_gsig[tid]) : out;
   }
   if (EPI == ATT_LAST) {
     // the last of the token's kv-head CTAs prepares the output projection's
@@ -1018,9 +1038,8 @@ __global__ void __launch_bounds__(ATT_THREADS_ALL, 3) k_attend(ModelDev md, Laye
     __syncthreads();
     if (s_last) {
       __threadfence();
-      const int H = md.heads, KV = md.kv_heads, K = H * HEAD_DIM;
-      prep_token(w.attn + (size_t)t * K, w.proj + (size_t)t * (2 * H + 2 * KV) * HEAD_DIM + (H + 2 * KV) * HEAD_DIM, K, w.act,
-                 w.act_scale, t, md.inv_sqrt_group, 1, 0, s_e, &s_red[0][0]);
+      const int K = md.heads * HEAD_DIM;
+      prep_token(w.attn + (size_t)t * K, nullptr, K, w.act, w.act_scale, t, md.inv_sqrt_group, 1, 0, s_e, &s_red[0][0]);
       if (tid == 0) w.arrivals[t] = 0;  // ready for the next layer's attention
     }
   }
@@ -1032,11 +1051,10 @@ __global__ void __launch_bounds__(ATT_THREADS_ALL, 3) k_attend(ModelDev md, Laye
     cg::cluster_group cluster = cg::this_cluster();
     __shared__ __align__(16) float s_o[MAX_GROUP * HEAD_DIM];
     __shared__ float s_cpeak[ATT_MAX_KV];
-    const int H = md.heads, KV = md.kv_heads, proj_stride = (2 * H + 2 * KV) * HEAD_DIM;
+    const int H = md.heads, KV = md.kv_heads;
     float mag = 0.0f;
     if (tid < G * HEAD_DIM) {
-      const float gate = w.proj[(size_t)t * proj_stride + (H + 2 * KV) * HEAD_DIM + kvh * G * HEAD_DIM + tid];
-      const float v = fmul(out, sigmoid(gate));
+      const float v = fmul(out, s_gsig[tid]);
       s_o[tid] = v;
       mag = fabsf(v);
     }
