@@ -371,7 +371,7 @@ __global__ void __launch_bounds__(256) k_route(ModelDev md, LayerDev L, Work w, 
 // accumulators with tcgen05.ld, and combines them in group order: fma for
 // 2-bit panels, the product chain for 4-bit rows. Small token tiles keep the
 // epilogue short and spread a projection over many CTAs.
-// grid (ceil(rows/128), ceil(M/NT)), block 8·NT (16 tokens per warp slice).
+// grid (ceil(rows/128), ceil(M/NT)), block 16·NT (8 tokens per warp slice).
 constexpr int GEMM_ROWS = 128;
 constexpr int GEMM_K = 512;
 constexpr int GEMM_KC = GEMM_K / 16;  // 16-byte chunks per row
@@ -388,8 +388,10 @@ __device__ __forceinline__ uint64_t umma_desc(uint32_t addr, uint32_t lbo, uint3
 // the weight tile and the activation block of chunk c are copied, its 16 MMAs
 // accumulate groups 4c..4c+3, and the next chunk's copy starts once they have
 // completed). The epilogue combines the groups in order.
+constexpr int GEMM_THREADS_PER_TOKEN = 16;  // 4 TMEM lane quadrants × NT/8 token slices of 32 threads
+
 template <int NT, int KCH>
-__global__ void __launch_bounds__(8 * NT) k_gemm(QMat W, const int8_t* __restrict__ act, const float* __restrict__ act_scale,
+__global__ void __launch_bounds__(GEMM_THREADS_PER_TOKEN * NT) k_gemm(QMat W, const int8_t* __restrict__ act, const float* __restrict__ act_scale,
                                               float* __restrict__ out, int M, int out_stride, const TokenMeta* __restrict__ meta,
                                               int* __restrict__ error, int act_rows) {
   constexpr int GK = KCH * (GEMM_K / GROUP);
@@ -492,28 +494,26 @@ __global__ void __launch_bounds__(8 * NT) k_gemm(QMat W, const int8_t* __restric
   __syncthreads();
   if (!s_fail) {
     const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16);
-    const int c0 = slice * 16;
-    float total[16];
+    const int c0 = slice * 8;
+    float total[8];
 #pragma unroll
-    for (int j = 0; j < 16; ++j) total[j] = 0.0f;
+    for (int j = 0; j < 8; ++j) total[j] = 0.0f;
     // four groups' accumulators per batch, loaded together and waited for once
 #pragma unroll
     for (int g0 = 0; g0 < GK; g0 += 4) {
-      uint32_t a[4][16];
+      uint32_t a[4][8];
 #pragma unroll
       for (int gi = 0; gi < 4; ++gi)
-        asm volatile(
-            "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
-            : "=r"(a[gi][0]), "=r"(a[gi][1]), "=r"(a[gi][2]), "=r"(a[gi][3]), "=r"(a[gi][4]), "=r"(a[gi][5]), "=r"(a[gi][6]),
-              "=r"(a[gi][7]), "=r"(a[gi][8]), "=r"(a[gi][9]), "=r"(a[gi][10]), "=r"(a[gi][11]), "=r"(a[gi][12]), "=r"(a[gi][13]),
-              "=r"(a[gi][14]), "=r"(a[gi][15])
-            : "r"(lane_base + (g0 + gi) * NT + c0));
+        asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+                     : "=r"(a[gi][0]), "=r"(a[gi][1]), "=r"(a[gi][2]), "=r"(a[gi][3]), "=r"(a[gi][4]), "=r"(a[gi][5]), "=r"(a[gi][6]),
+                       "=r"(a[gi][7])
+                     : "r"(lane_base + (g0 + gi) * NT + c0));
       asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
       for (int gi = 0; gi < 4; ++gi) {
         const int g = g0 + gi;
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
+        for (int j = 0; j < 8; ++j) {
           const float acc = (float)(int)a[gi][j];
           const float as = s_as[(c0 + j) * GK + g];
           total[j] =
@@ -522,7 +522,7 @@ __global__ void __launch_bounds__(8 * NT) k_gemm(QMat W, const int8_t* __restric
       }
     }
 #pragma unroll
-    for (int j = 0; j < 16; ++j) {
+    for (int j = 0; j < 8; ++j) {
       const int n = c0 + j;
       if (valid && s_live[n]) out[(size_t)(m0 + n) * out_stride + row] = total[j];
     }
@@ -1322,30 +1322,37 @@ struct HadaPass2 {
 // values): rank-8 condition softmax, modulation, three Kronecker factor
 // applications with the two permutations and the SiLU gate. The result (before
 // the final d4 scale) is left in buf0[0..d). cond_v, left[0] and right[0] must
-// already be staged in s_condv, s_left and s_right.
-template <int LEFT>
+// already be staged in s_condv, s_left and s_right; with RESIDENT all three
+// factor pairs are (factor k at s_left + k·LEFT², s_right + k·32²), else the
+// next pair is staged into the same place while an elementwise pass runs.
+template <int LEFT, bool RESIDENT>
 __device__ __forceinline__ void hadamard_core(const ModelDev& md, const HadamardDev& Hd, const int d, const float* s_pre, float* buf0,
                                               float* buf1, float* s_mod, float* s_left, float* s_right, float* s_condv) {
   constexpr bool FUSED32 = LEFT == 32;
+  constexpr int LS = RESIDENT ? LEFT * LEFT : 0, RS = RESIDENT ? HADA_RIGHT * HADA_RIGHT : 0;
   const float2 nz = g_negzero;
   hada_prepare<LEFT>(Hd, d, s_pre, buf0, s_mod, s_condv);
   HadaPass1<LEFT> pass1;
   pass1.load(md, Hd);
   kronecker<LEFT, FUSED32>(buf0, buf1, s_left, s_right, buf0, nz);  // first = K1(d1 ⊙ x)
-  stage_async(s_left, Hd.left[1], LEFT * LEFT);
-  stage_async(s_right, Hd.right[1], HADA_RIGHT * HADA_RIGHT);
+  if (!RESIDENT) {
+    stage_async(s_left, Hd.left[1], LEFT * LEFT);
+    stage_async(s_right, Hd.right[1], HADA_RIGHT * HADA_RIGHT);
+  }
   pass1.run(s_mod, buf0, buf1);
   HadaPass2<LEFT> pass2;
   pass2.load(md, Hd);
-  cp_async_wait_all();
+  if (!RESIDENT) cp_async_wait_all();
   __syncthreads();
-  kronecker<LEFT, FUSED32>(buf1, buf0, s_left, s_right, buf1, nz);  // second
-  stage_async(s_left, Hd.left[2], LEFT * LEFT);
-  stage_async(s_right, Hd.right[2], HADA_RIGHT * HADA_RIGHT);
+  kronecker<LEFT, FUSED32>(buf1, buf0, s_left + LS, s_right + RS, buf1, nz);  // second
+  if (!RESIDENT) {
+    stage_async(s_left, Hd.left[2], LEFT * LEFT);
+    stage_async(s_right, Hd.right[2], HADA_RIGHT * HADA_RIGHT);
+  }
   pass2.run(buf1, buf0);
-  cp_async_wait_all();
+  if (!RESIDENT) cp_async_wait_all();
   __syncthreads();
-  kronecker<LEFT, FUSED32>(buf0, buf1, s_left, s_right, buf0, nz, output_rows<LEFT>(d));  // third
+  kronecker<LEFT, FUSED32>(buf0, buf1, s_left + 2 * LS, s_right + 2 * RS, buf0, nz, output_rows<LEFT>(d));  // third
 }
 
 // The front of the block finish (session.rs:121-137): the layer's constant
@@ -1353,8 +1360,9 @@ __device__ __forceinline__ void hadamard_core(const ModelDev& md, const Hadamard
 // copy, then (once the previous kernel is done) the token's rows, the post
 // norm and gated residual into s_a, and the pre-Hadamard norm into s_pre.
 // False when the token is not live: the CTA has then waited for its copies
-// and returns.
-template <int LEFT>
+// and returns. FACTORS Kronecker factor pairs are copied (k-th at
+// s_left + k·LEFT², s_right + k·32²).
+template <int LEFT, int FACTORS>
 __device__ __forceinline__ bool block_front(const LayerDev& L, const Work& w, int M, int t, int d, int* error, float* s_a, float* s_x,
                                             float* s_pre, float* s_condv, float* s_left, float* s_right, float* s_gpost,
                                             float* s_gpre) {
@@ -1364,10 +1372,12 @@ __device__ __forceinline__ bool block_front(const LayerDev& L, const Work& w, in
   const uint32_t bar = smem_u32(&s_bar);
   const HadamardDev& Hd = L.hada;
   if (tid == 0) {  // one thread arms the barrier and issues every copy
-    bulk_start(bar, (d * COND_RANK + LEFT * LEFT + HADA_RIGHT * HADA_RIGHT + 2 * d) * 4);
+    bulk_start(bar, (d * COND_RANK + FACTORS * (LEFT * LEFT + HADA_RIGHT * HADA_RIGHT) + 2 * d) * 4);
     bulk_copy(s_condv, Hd.cond_v, d * COND_RANK * 4, bar);
-    bulk_copy(s_left, Hd.left[0], LEFT * LEFT * 4, bar);
-    bulk_copy(s_right, Hd.right[0], HADA_RIGHT * HADA_RIGHT * 4, bar);
+    for (int k = 0; k < FACTORS; ++k) {
+      bulk_copy(s_left + k * LEFT * LEFT, Hd.left[k], LEFT * LEFT * 4, bar);
+      bulk_copy(s_right + k * HADA_RIGHT * HADA_RIGHT, Hd.right[k], HADA_RIGHT * HADA_RIGHT * 4, bar);
+    }
     bulk_copy(s_gpost, L.post_norm, d * 4, bar);
     bulk_copy(s_gpre, L.pre_hada, d * 4, bar);
   }
@@ -1426,16 +1436,16 @@ __global__ void __launch_bounds__(BLOCK_THREADS) k_block(ModelDev md, LayerDev L
   float* buf0 = sm + 3 * MAX_D;           // N
   float* buf1 = buf0 + N;                 // N
   float* s_mod = buf1 + N;                // N
-  float* s_left = s_mod + N;              // LEFT*LEFT
-  float* s_right = s_left + LEFT * LEFT;  // 32*32
+  float* s_left = s_mod + N;                  // 3 × LEFT*LEFT: the three left factors
+  float* s_right = s_left + 3 * LEFT * LEFT;  // 3 × 32*32: the three right factors
   // d*8 condition values, consumed before the first Kronecker stage: they
   // borrow buf1 and s_mod when they fit there
-  float* s_condv = d * COND_RANK <= 2 * N ? buf1 : s_right + HADA_RIGHT * HADA_RIGHT;
-  float* s_gpost = s_right + HADA_RIGHT * HADA_RIGHT + (d * COND_RANK <= 2 * N ? 0 : d * COND_RANK);  // d post_norm gains
-  float* s_gpre = s_gpost + MAX_D;                                                                     // d pre_hada gains
+  float* s_condv = d * COND_RANK <= 2 * N ? buf1 : s_right + 3 * HADA_RIGHT * HADA_RIGHT;
+  float* s_gpost = s_right + 3 * HADA_RIGHT * HADA_RIGHT + (d * COND_RANK <= 2 * N ? 0 : d * COND_RANK);  // d post_norm gains
+  float* s_gpre = s_gpost + MAX_D;                                                                         // d pre_hada gains
   const HadamardDev& Hd = L.hada;
 
-  if (!block_front<LEFT>(L, w, M, t, d, error, s_a, s_x, s_pre, s_condv, s_left, s_right, s_gpost, s_gpre)) return;
+  if (!block_front<LEFT, 3>(L, w, M, t, d, error, s_a, s_x, s_pre, s_condv, s_left, s_right, s_gpost, s_gpre)) return;
   // the lane combine's operands (routing weights, this token's lanes, d4) load
   // while the Hadamard MLP runs; one float4 column per thread (d <= 4 · 256)
   const float* route = w.route + (size_t)t * (LANES + LANES * LANES);
@@ -1452,7 +1462,7 @@ __global__ void __launch_bounds__(BLOCK_THREADS) k_block(ModelDev md, LayerDev L
     for (int s = 0; s < LANES; ++s) sv[s] = reinterpret_cast<const float4*>(stream + s * d)[i4];
   }
   __syncthreads();
-  hadamard_core<LEFT>(md, Hd, d, s_pre, buf0, buf1, s_mod, s_left, s_right, s_condv);
+  hadamard_core<LEFT, true>(md, Hd, d, s_pre, buf0, buf1, s_mod, s_left, s_right, s_condv);
   pdl_trigger();  // the lane combine overlaps the next kernel's prologue
   if (i4 < d / 4) {
     const float dv[4] = {d4.x, d4.y, d4.z, d4.w};
@@ -1537,7 +1547,7 @@ __global__ void __launch_bounds__(BLOCK_THREADS) k_block_split(ModelDev md, Laye
   const HadamardDev& Hd = L.hada;
   const float2 nz = g_negzero;
 
-  if (!block_front<LEFT>(L, w, M, t, d, error, s_a, s_x, s_pre, s_condv, s_left, s_right, s_gpost, s_gpre)) return;
+  if (!block_front<LEFT, 1>(L, w, M, t, d, error, s_a, s_x, s_pre, s_condv, s_left, s_right, s_gpost, s_gpre)) return;
   cluster_arrive_relaxed();  // paired with the wait before the first remote store
   // this CTA's elements of the lane combine: rows 0..d/32-1 of its columns
   const int rows_d = d / HADA_RIGHT, own = rows_d * W;
@@ -1767,7 +1777,7 @@ size_t attend_smem(const ModelDev& md, int t_cap) {
 }
 size_t block_smem(const ModelDev& md) {
   int N = md.hada_left * HADA_RIGHT;
-  size_t floats = 3 * MAX_D + 3 * N + md.hada_left * md.hada_left + HADA_RIGHT * HADA_RIGHT + 2 * MAX_D;
+  size_t floats = 3 * MAX_D + 3 * N + 3 * (md.hada_left * md.hada_left + HADA_RIGHT * HADA_RIGHT) + 2 * MAX_D;
   if ((int)md.d_model * COND_RANK > 2 * N) floats += (size_t)md.d_model * COND_RANK;
   return floats * 4;
 }
@@ -1875,10 +1885,11 @@ static void project(const QMat& W, const int8_t* act, const float* act_scale, fl
       launch(k_gemv<1>, ctas, GEMV_WARPS * 32, 0, st, W, act, act_scale, out, M, out_stride, meta, act_rows);
   } else if (M <= 16) {
     auto k = wide ? k_gemm<16, 4> : k_gemm<16, 1>;
-    launch(k, dim3(tiles, 1), 8 * 16, gemm_smem<16>(), st, W, act, act_scale, out, M, out_stride, meta, error, act_rows);
+    launch(k, dim3(tiles, 1), GEMM_THREADS_PER_TOKEN * 16, gemm_smem<16>(), st, W, act, act_scale, out, M, out_stride, meta, error, act_rows);
   } else {
     auto k = wide ? k_gemm<32, 4> : k_gemm<32, 1>;
-    launch(k, dim3(tiles, (M + 31) / 32), 8 * 32, gemm_smem<32>(), st, W, act, act_scale, out, M, out_stride, meta, error, act_rows);
+    launch(k, dim3(tiles, (M + 31) / 32), GEMM_THREADS_PER_TOKEN * 32, gemm_smem<32>(), st, W, act, act_scale, out, M, out_stride, meta, error,
+           act_rows);
   }
 }
 
@@ -2057,7 +2068,7 @@ __global__ void __launch_bounds__(BLOCK_THREADS) k_debug_hadamard(ModelDev md, H
   stage_async(s_pre, in + (size_t)t * d, d);
   cp_async_wait_all();
   __syncthreads();
-  hadamard_core<LEFT>(md, Hd, d, s_pre, buf0, buf1, s_mod, s_left, s_right, s_condv);
+  hadamard_core<LEFT, false>(md, Hd, d, s_pre, buf0, buf1, s_mod, s_left, s_right, s_condv);
   for (int i = threadIdx.x; i < d; i += BLOCK_THREADS) out[(size_t)t * d + i] = fmul(buf0[i], Hd.d4[i]);
 }
 
@@ -2157,9 +2168,9 @@ cudaError_t launch_static_project(int device, const ModelDev& md, const QMat& W,
   const int K = GEMM_K, tiles = (W.rows + GEMM_ROWS - 1) / GEMM_ROWS;
   k_prep<<<M, 128, 0, st>>>(in, K, nullptr, nullptr, 0, K, act, act_scale, M, nullptr, md.inv_sqrt_group, 0, 0);
   if (M <= 16)
-    k_gemm<16, 1><<<dim3(tiles, 1), 8 * 16, gemm_smem<16>(), st>>>(W, act, act_scale, out, M, (int)W.rows, nullptr, flag, 0);
+    k_gemm<16, 1><<<dim3(tiles, 1), GEMM_THREADS_PER_TOKEN * 16, gemm_smem<16>(), st>>>(W, act, act_scale, out, M, (int)W.rows, nullptr, flag, 0);
   else
-    k_gemm<32, 1><<<dim3(tiles, (M + 31) / 32), 8 * 32, gemm_smem<32>(), st>>>(W, act, act_scale, out, M, (int)W.rows, nullptr, flag, 0);
+    k_gemm<32, 1><<<dim3(tiles, (M + 31) / 32), GEMM_THREADS_PER_TOKEN * 32, gemm_smem<32>(), st>>>(W, act, act_scale, out, M, (int)W.rows, nullptr, flag, 0);
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
   *wait_failed = 0;
   if ((e = cudaMemcpyAsync(wait_failed, flag, sizeof(int), cudaMemcpyDeviceToHost, st)) != cudaSuccess) return e;
