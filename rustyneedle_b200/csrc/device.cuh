@@ -27,12 +27,15 @@ __device__ __forceinline__ float fsqrt(float a) { return __fsqrt_rn(a); }
 
 // Programmatic dependent launch. Every kernel of the token loop is launched
 // with programmatic stream serialisation: it may start while its predecessor
-// on the stream still runs. pdl_trigger() (first thing in every CTA) lets the
-// successor start once all of this grid's CTAs are resident; pdl_wait()
-// blocks until the predecessor grid has completed and its writes are
-// visible. Before pdl_wait() a kernel only reads the model's constant weights
-// and writes nothing to global memory; every CTA passes pdl_wait() before it
-// exits, so completion stays transitive along the stream.
+// on the stream still runs. pdl_wait() blocks until the predecessor grid has
+// completed and its writes are visible; pdl_trigger() lets the successor
+// start once every CTA of this grid has triggered or exited. Every CTA passes
+// pdl_wait() before it triggers or exits, so when a kernel starts, every
+// launch before its immediate predecessor has completed. Before pdl_wait() a
+// kernel therefore writes nothing to global memory and reads only the
+// model's constant weights and data that launches at least two back (or the
+// host, before the pass) produced; it reads the latter through L2
+// (ld.global.cg), never through a possibly stale L1 line.
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 

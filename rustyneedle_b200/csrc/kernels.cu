@@ -54,8 +54,14 @@ __device__ __forceinline__ void stage_async(float* dst, const float* src, int fl
 }
 
 __device__ __forceinline__ uint8_t* page_base(const KvDev& kv, const PageGeometry& pg, int slot, int layer, int position) {
-  int page = kv.page_table[((size_t)slot * kv.num_layers + layer) * kv.max_pages + position / PAGE_POSITIONS];
+  int page = __ldcg(kv.page_table + ((size_t)slot * kv.num_layers + layer) * kv.max_pages + position / PAGE_POSITIONS);
   return kv.pool + (size_t)page * pg.page_bytes;
+}
+
+// A token's meta through L2 (it may be read before pdl_wait; see device.cuh).
+__device__ __forceinline__ TokenMeta load_meta(const TokenMeta* meta, int t) {
+  const int4 m = __ldcg(reinterpret_cast<const int4*>(meta + t));
+  return TokenMeta{m.x, m.y, m.z, m.w};
 }
 
 // ----------------------------------------------------------------- embedding
@@ -444,10 +450,11 @@ __global__ void __launch_bounds__(GEMM_THREADS_PER_TOKEN * NT) k_gemm(QMat W, co
   float ws[GK];
 #pragma unroll
   for (int g = 0; g < GK; ++g) ws[g] = valid ? W.scales[(size_t)row * GK + g] : 0.0f;
+  // the pass's token meta comes from launches before the predecessor
+  if (tid < NT) s_live[tid] = tid < mcount && !(meta && __ldcg(&meta[m0 + tid].slot) < 0);
   pdl_wait();
   if (tid == 0) copy(sB, tokens(0), B_BYTES);
   for (int i = tid; i < NT * GK; i += blockDim.x) s_as[i] = i / GK < mcount ? act_scale[(size_t)m0 * GK + i] : 0.0f;
-  if (tid < NT) s_live[tid] = tid < mcount && !(meta && meta[m0 + tid].slot < 0);
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
@@ -632,19 +639,37 @@ constexpr size_t gemm_smem() {
 // kind 0 = query head `head`: its 64 codes go to q_out and the scale is
 // returned; 1 = key head, 2 = value head: codes and scale go into the token's
 // slot of its KV page.
-__device__ __forceinline__ float head_codes(const ModelDev& md, const LayerDev& L, const Work& w, const KvDev& kv, int t,
-                                            const TokenMeta& meta, int layer, int kind, int head, int8_t* q_out) {
+// The head step's operands that do not come from the projection (the norm
+// gains and rotary row are constants, the page slot comes from the host's
+// page table): they may be loaded before pdl_wait.
+struct HeadPre {
+  float g0, g1;
+  float2 sc;
+  uint8_t* page;
+};
+__device__ __forceinline__ HeadPre head_prefetch(const ModelDev& md, const LayerDev& L, const KvDev& kv, const TokenMeta& meta, int layer,
+                                                 int kind) {
+  const int lane = threadIdx.x & 31;
+  const float* gain = kind == 0 ? L.q_norm : L.k_norm;
+  HeadPre p;
+  p.g0 = gain[lane];
+  p.g1 = gain[lane + 32];
+  p.sc = md.rotary[(size_t)meta.position * (HEAD_DIM / 2) + lane];
+  p.page = kind == 0 ? nullptr : page_base(kv, md.page, meta.slot, layer, meta.position);
+  return p;
+}
+
+__device__ __forceinline__ float head_codes(const ModelDev& md, const Work& w, int t, const TokenMeta& meta, int kind, int head,
+                                            const HeadPre& pre, int8_t* q_out) {
   const int lane = threadIdx.x & 31;
   const int H = md.heads, KV = md.kv_heads;
   // proj rows: q [H*64] | k [KV*64] | v [KV*64] | gate [H*64]
   const float* src = w.proj + (size_t)t * (2 * H + 2 * KV) * HEAD_DIM + (kind == 0 ? 0 : (kind == 1 ? H * HEAD_DIM : (H + KV) * HEAD_DIM)) +
                      head * HEAD_DIM;
-  // every operand is requested before the first use
   float e0 = src[lane], e1 = src[lane + 32];
-  const float* gain = kind == 0 ? L.q_norm : L.k_norm;
-  const float g0 = gain[lane], g1 = gain[lane + 32];
-  const float2 sc = md.rotary[(size_t)meta.position * (HEAD_DIM / 2) + lane];
-  uint8_t* page = kind == 0 ? nullptr : page_base(kv, md.page, meta.slot, layer, meta.position);
+  const float g0 = pre.g0, g1 = pre.g1;
+  const float2 sc = pre.sc;
+  uint8_t* page = pre.page;
   if (kind != 2) {
     // zero_centred_norm_in_place over the head (ops.rs:52-58): lane l < 8 runs
     // the chain over elements l, l+8, ..., l+56
@@ -707,7 +732,8 @@ __global__ void k_heads(ModelDev md, LayerDev L, Work w, KvDev kv, int M, int la
   const int H = md.heads, KV = md.kv_heads;
   const int kind = warp < H ? 0 : (warp < H + KV ? 1 : 2);
   const int head = kind == 0 ? warp : (kind == 1 ? warp - H : warp - H - KV);
-  const float scale = head_codes(md, L, w, kv, t, meta, layer, kind, head, w.qcodes + ((size_t)t * H + head) * HEAD_DIM);
+  const float scale = head_codes(md, w, t, meta, kind, head, head_prefetch(md, L, kv, meta, layer, kind),
+                                 w.qcodes + ((size_t)t * H + head) * HEAD_DIM);
   if (kind == 0 && lane == 0) w.qscale[(size_t)t * H + head] = scale;
 }
 
@@ -781,14 +807,30 @@ template <int G, int EPI, bool HEADS>
 __global__ void __launch_bounds__(ATT_THREADS_ALL, 3) k_attend(ModelDev md, LayerDev L, Work w, KvDev kv, int M, int layer, int t_cap) {
   constexpr bool PREP = EPI == ATT_CLUSTER;
   const int global = L.global;
-  pdl_wait();
   extern __shared__ float sm[];
-  if ((int)blockIdx.x >= M) return;  // the whole cluster shares the token
-  const int t = w.order ? w.order[blockIdx.x] : (int)blockIdx.x, kvh = blockIdx.y;
-  const TokenMeta meta = w.meta[t];
-  if (meta.slot < 0) return;
-  if (PREP) cluster_arrive_relaxed();  // paired with the wait before the first remote access
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  // the token's meta, its page pointers and (HEADS) the head step's constant
+  // operands come from launches before the predecessor: they load while the
+  // predecessor finishes
+  const int kvh = blockIdx.y;
+  int t = 0;
+  TokenMeta meta{-1, 0, 0, 0};
+  if ((int)blockIdx.x < M) {
+    t = w.order ? __ldcg(w.order + blockIdx.x) : (int)blockIdx.x;
+    meta = load_meta(w.meta, t);
+  }
+  __shared__ const uint8_t* s_page[128];
+  if (meta.slot >= 0) {
+    const int* table = kv.page_table + ((size_t)meta.slot * kv.num_layers + layer) * kv.max_pages;
+    const int npages = meta.position / PAGE_POSITIONS + 1;
+    for (int i = tid; i < npages; i += blockDim.x) s_page[i] = kv.pool + (size_t)__ldcg(table + i) * md.page.page_bytes;
+  }
+  HeadPre hpre{};
+  const int hkind = warp < G ? 0 : warp - G + 1;  // HEADS: warps 0..G-1 query heads, G key, G+1 value
+  if (HEADS && meta.slot >= 0 && warp < G + 2) hpre = head_prefetch(md, L, kv, meta, layer, hkind);
+  pdl_wait();
+  if (meta.slot < 0) return;  // also past the last token; the whole cluster shares the token
+  if (PREP) cluster_arrive_relaxed();  // paired with the wait before the first remote access
   const int total = meta.position + 1;
   int first = 0;
   if (md.sliding_window > 0 && !global) first = total > (int)md.sliding_window ? total - (int)md.sliding_window : 0;
@@ -801,21 +843,15 @@ __global__ void __launch_bounds__(ATT_THREADS_ALL, 3) k_attend(ModelDev md, Laye
   uint32_t* s_wlo = s_whi + G * ws;                             // [G][ws]
   int* s_pv = reinterpret_cast<int*>(s_wlo + G * ws);           // [ATT_SLICES][G][64]
   __shared__ __align__(16) uint32_t s_q[MAX_GROUP][16];
-  __shared__ const uint8_t* s_page[128];
   __shared__ float s_qs[MAX_GROUP], s_peak[MAX_GROUP], s_scale2[MAX_GROUP], s_total[MAX_GROUP];
   __shared__ float s_red[MAX_GROUP][ATT_WORKERS / 32];
   __shared__ float s_gsig[EPI == ATT_ROWS ? 1 : MAX_GROUP * HEAD_DIM];  // sigmoid of this CTA's gate values
   const PageGeometry& pg = md.page;
-  const int* table = kv.page_table + ((size_t)meta.slot * kv.num_layers + layer) * kv.max_pages;
-  const int npages = (total - 1) / PAGE_POSITIONS + 1;
-  for (int i = tid; i < npages; i += blockDim.x) s_page[i] = kv.pool + (size_t)table[i] * pg.page_bytes;
   if (HEADS) {
-    // warps 0..G-1: query heads kvh·G + warp; warp G: key head kvh; warp G+1: value head kvh
     if (warp < G + 2) {
-      const int kind = warp < G ? 0 : warp - G + 1;
-      const float sc = head_codes(md, L, w, kv, t, meta, layer, kind, kind == 0 ? kvh * G + warp : kvh,
-                                  reinterpret_cast<int8_t*>(s_q[kind == 0 ? warp : 0]));
-      if (kind == 0 && lane == 0) s_qs[warp] = fmul(sc, md.inv_root_qk);
+      const float sc = head_codes(md, w, t, meta, hkind, hkind == 0 ? kvh * G + warp : kvh, hpre,
+                                  reinterpret_cast<int8_t*>(s_q[hkind == 0 ? warp : 0]));
+      if (hkind == 0 && lane == 0) s_qs[warp] = fmul(sc, md.inv_root_qk);
     }
   } else {
     if (tid < G * 16) {
@@ -1382,13 +1418,16 @@ __device__ __forceinline__ bool block_front(const LayerDev& L, const Work& w, in
     bulk_copy(s_gpre, L.pre_hada, d * 4, bar);
   }
   if (tid == 32) s_gate = sigmoid(L.attn_gate);
+  // the routing input (k_route, launches earlier) and the token's meta load
+  // while the predecessor finishes
+  const bool live = t < M && load_meta(w.meta, t).slot >= 0;
+  if (live) stage_async(s_x, w.x + (size_t)t * d, d);
   pdl_wait();
-  if (t >= M || w.meta[t].slot < 0) {
+  if (!live) {
     if (tid == 0 && !mbar_wait(bar, 0)) atomicExch(error, 1);  // no copy outlives the CTA
     return false;
   }
   stage_async(s_a, w.outp + (size_t)t * d, d);
-  stage_async(s_x, w.x + (size_t)t * d, d);
   cp_async_wait_all();
   // the staged rows, the gate and the barrier's initialisation are visible to
   // every thread past this point; then each thread waits for the bulk copies
@@ -1445,13 +1484,13 @@ __global__ void __launch_bounds__(BLOCK_THREADS) k_block(ModelDev md, LayerDev L
   float* s_gpre = s_gpost + MAX_D;                                                                         // d pre_hada gains
   const HadamardDev& Hd = L.hada;
 
-  if (!block_front<LEFT, 3>(L, w, M, t, d, error, s_a, s_x, s_pre, s_condv, s_left, s_right, s_gpost, s_gpre)) return;
-  // the lane combine's operands (routing weights, this token's lanes, d4) load
-  // while the Hadamard MLP runs; one float4 column per thread (d <= 4 · 256)
+  // the lane combine's operands (routing weights and this token's lanes, from
+  // launches before the predecessor; d4) load first, and stay in registers
+  // through the Hadamard MLP; one float4 column per thread (d <= 4 · 256)
   const float* route = w.route + (size_t)t * (LANES + LANES * LANES);
   float rw[LANES + LANES * LANES];
 #pragma unroll
-  for (int k = 0; k < LANES + LANES * LANES; ++k) rw[k] = route[k];
+  for (int k = 0; k < LANES + LANES * LANES; ++k) rw[k] = __ldcg(route + k);
   const float* stream = w.stream + (size_t)t * LANES * d;
   float* next = w.next_stream + (size_t)t * LANES * d;
   const int i4 = tid;
@@ -1459,8 +1498,9 @@ __global__ void __launch_bounds__(BLOCK_THREADS) k_block(ModelDev md, LayerDev L
   if (i4 < d / 4) {
     d4 = reinterpret_cast<const float4*>(Hd.d4)[i4];
 #pragma unroll
-    for (int s = 0; s < LANES; ++s) sv[s] = reinterpret_cast<const float4*>(stream + s * d)[i4];
+    for (int s = 0; s < LANES; ++s) sv[s] = __ldcg(reinterpret_cast<const float4*>(stream + s * d) + i4);
   }
+  if (!block_front<LEFT, 3>(L, w, M, t, d, error, s_a, s_x, s_pre, s_condv, s_left, s_right, s_gpost, s_gpre)) return;
   __syncthreads();
   hadamard_core<LEFT, true>(md, Hd, d, s_pre, buf0, buf1, s_mod, s_left, s_right, s_condv);
   pdl_trigger();  // the lane combine overlaps the next kernel's prologue
@@ -1547,20 +1587,21 @@ __global__ void __launch_bounds__(BLOCK_THREADS) k_block_split(ModelDev md, Laye
   const HadamardDev& Hd = L.hada;
   const float2 nz = g_negzero;
 
-  if (!block_front<LEFT, 1>(L, w, M, t, d, error, s_a, s_x, s_pre, s_condv, s_left, s_right, s_gpost, s_gpre)) return;
-  cluster_arrive_relaxed();  // paired with the wait before the first remote store
-  // this CTA's elements of the lane combine: rows 0..d/32-1 of its columns
+  // this CTA's elements of the lane combine: rows 0..d/32-1 of its columns;
+  // their operands (from launches before the predecessor; d4) load first
   const int rows_d = d / HADA_RIGHT, own = rows_d * W;
   const int ei = (tid / W) * HADA_RIGHT + cq + tid % W;
   const float* route = w.route + (size_t)t * (LANES + LANES * LANES);
   float rw[LANES + LANES * LANES], sv[LANES], d4 = 0.0f;
 #pragma unroll
-  for (int k = 0; k < LANES + LANES * LANES; ++k) rw[k] = route[k];
+  for (int k = 0; k < LANES + LANES * LANES; ++k) rw[k] = __ldcg(route + k);
   if (tid < own) {
     d4 = Hd.d4[ei];
 #pragma unroll
-    for (int s = 0; s < LANES; ++s) sv[s] = w.stream[((size_t)t * LANES + s) * d + ei];
+    for (int s = 0; s < LANES; ++s) sv[s] = __ldcg(w.stream + ((size_t)t * LANES + s) * d + ei);
   }
+  if (!block_front<LEFT, 1>(L, w, M, t, d, error, s_a, s_x, s_pre, s_condv, s_left, s_right, s_gpost, s_gpre)) return;
+  cluster_arrive_relaxed();  // paired with the wait before the first remote store
   __syncthreads();
   hada_prepare<LEFT>(Hd, d, s_pre, xa, s_mod, s_condv);
   HadaPass1<LEFT> pass1;
