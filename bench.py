@@ -58,6 +58,8 @@ def parse():
     p.add_argument("--no-cpu", action="store_true")
     p.add_argument("--profile", action="store_true", help="64 sequences, no extras: the small case for ncu captures")
     p.add_argument("--batch1-only", action="store_true", help="only the batch-1 configuration (ncu launch lists)")
+    p.add_argument("--ncu-range", action="store_true",
+                   help="bracket the timed steps with cudaProfilerStart/Stop (ncu --profile-from-start off)")
     p.add_argument("--products", action="store_true",
                    help="the product microbenchmark (config 3) instead of decoding: one JSON line of GOP/s per shape")
     return p.parse_args()
@@ -123,11 +125,6 @@ class Clocks:
         reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": int(rows[0][2]), "reasons": reasons,
                 "samples": len(rows)}
-
-
-def launches_per_step(depth: int) -> int:
-    # logits prep + product, select, embed, 7 per layer, final norm, advance
-    return 2 + 1 + 1 + 7 * depth + 1 + 1
 
 
 def cpu_baseline(archive: str, rank_prompts, threads: int, steps: int = 2, sample: int = 8):
@@ -258,8 +255,16 @@ def main():
 
     batch.run(args.warmup)
     barrier()
+    if args.ncu_range:
+        import torch
+
+        torch.cuda.cudart().cudaProfilerStart()
     with Clocks(local) as clocks:
         ms = batch.run(args.steps)
+    if args.ncu_range:
+        import torch
+
+        torch.cuda.cudart().cudaProfilerStop()
     barrier()
     ms = max_over_ranks(ms)
     total_tokens = seqs * world * args.steps
@@ -298,7 +303,7 @@ def main():
                                    "uniform in [128, 1024], greedy decode, paged int8 KV (64-token pages)",
                        "sequences_per_gpu": seqs, "depth": DEPTH, "parallelism": f"dp{world} (sequences sharded)",
                        "l2": "inputs larger than L2 (KV cache ~2 GB per GPU)", "setup_s": round(setup_s, 1)},
-            "e2e": e2e, "roofline": roofline, "gpu_launches": launches_per_step(DEPTH) * args.steps,
+            "e2e": e2e, "roofline": roofline, "gpu_launches": debug.step_kernels(batch) * args.steps,
             "clocks": clocks.summary()}
 
     if not args.no_batch1 and rank == 0 and not args.profile:

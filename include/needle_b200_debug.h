@@ -57,6 +57,10 @@ nb_status nb_debug_kv(nb_session* session, uint32_t layer, int8_t* keys, float* 
  * must read (keys, values and their scales of every attended position). */
 nb_status nb_debug_time_attention(nb_batch* batch, uint32_t reps, float* ms_per_launch, double* bytes_per_launch);
 
+/* Kernels in the batch's step graph (the last one recorded; 0 before the
+ * first step). No reference counterpart: the bench's launch count. */
+nb_status nb_debug_step_kernels(nb_batch* batch, uint32_t* kernels);
+
 #ifdef __cplusplus
 }
 #endif

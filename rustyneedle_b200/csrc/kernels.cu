@@ -1857,9 +1857,6 @@ cudaError_t configure(const ModelDev& md, int t_cap) {
   return cudaSuccess;
 }
 
-static int* g_gemm_error = nullptr;
-
-void set_error_flag(int* flag) { g_gemm_error = flag; }
 
 // Every kernel of a pass launches with programmatic stream serialisation:
 // its prologue (constant weight loads, tensor-memory allocation) overlaps the
@@ -1882,8 +1879,12 @@ static bool pdl_enabled() {
   return on && t_pass_tokens <= max_tokens;
 }
 
+static thread_local long t_launches = 0;  // kernels this thread has launched (or recorded into a graph)
+long launch_counter() { return t_launches; }
+
 template <typename... P, typename... A>
 static void launch_clustered(void (*kernel)(P...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, dim3 cluster, A&&... args) {
+  ++t_launches;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = block;
@@ -1914,8 +1915,7 @@ static void launch(void (*kernel)(P...), dim3 grid, dim3 block, size_t smem, cud
 // of 16 or 32 tokens. act_rows is the row capacity of the activation buffer
 // (it places the chunks of K > 512).
 static void project(const QMat& W, const int8_t* act, const float* act_scale, float* out, int M, int out_stride,
-                    const TokenMeta* meta, cudaStream_t st, int act_rows = 0, int* error = nullptr) {
-  if (!error) error = g_gemm_error;
+                    const TokenMeta* meta, cudaStream_t st, int* error, int act_rows = 0) {
   const int tiles = (W.rows + GEMM_ROWS - 1) / GEMM_ROWS;
   const bool wide = W.cols == 4 * GEMM_K;
   if (M <= GEMV_MAX_TOKENS) {
@@ -1956,10 +1956,10 @@ static void launch_block(const ModelDev& md, const LayerDev& L, const Work& w, i
   const bool split = M <= max_tokens && ((int)md.d_model / HADA_RIGHT) * W <= BLOCK_THREADS;
   if (split) {
     auto k = left == 64 ? k_block_split<64> : k_block_split<32>;
-    launch_clustered(k, dim3(M * CL), BLOCK_THREADS, block_split_smem(md), st, dim3(CL, 1, 1), md, L, w, M, g_gemm_error);
+    launch_clustered(k, dim3(M * CL), BLOCK_THREADS, block_split_smem(md), st, dim3(CL, 1, 1), md, L, w, M, md.error);
   } else {
     auto k = left == 64 ? k_block<64> : k_block<32>;
-    launch(k, M, BLOCK_THREADS, block_smem(md), st, md, L, w, M, g_gemm_error);
+    launch(k, M, BLOCK_THREADS, block_smem(md), st, md, L, w, M, md.error);
   }
 }
 
@@ -1968,8 +1968,8 @@ void launch_layer(const ModelDev& md, const LayerDev& L, const Work& w, const Kv
   t_pass_tokens = M;
   const int d = md.d_model, H = md.heads, KV = md.kv_heads;
   const int proj_stride = (2 * H + 2 * KV) * HEAD_DIM;
-  launch(k_route, M, 256, route_smem(md), st, md, L, w, M, layer, slot, g_gemm_error);
-  project(L.qkvg, w.act, w.act_scale, w.proj, M, proj_stride, w.meta, st);
+  launch(k_route, M, 256, route_smem(md), st, md, L, w, M, layer, slot, md.error);
+  project(L.qkvg, w.act, w.act_scale, w.proj, M, proj_stride, w.meta, st, md.error);
   // the head step runs inside the attention when each token of the pass
   // belongs to a different sequence; $NEEDLE_B200_FUSE_HEADS=0 keeps k_heads
   static const bool heads_off = [] {
@@ -1982,7 +1982,7 @@ void launch_layer(const ModelDev& md, const LayerDev& L, const Work& w, const Kv
     launch(k_prep, M, 128, 0, st, (const float*)w.attn, H * HEAD_DIM, (const int32_t*)nullptr,
            (const float*)(w.proj + (H + 2 * KV) * HEAD_DIM), proj_stride, H * HEAD_DIM, w.act, w.act_scale, M, w.meta,
            md.inv_sqrt_group, 1, 0);
-  project(L.out, w.act, w.act_scale, w.outp, M, d, w.meta, st);
+  project(L.out, w.act, w.act_scale, w.outp, M, d, w.meta, st, md.error);
   launch_block(md, L, w, M, st);
 }
 
@@ -1996,7 +1996,7 @@ void launch_logits(const ModelDev& md, const float* hidden, const int32_t* slots
   t_pass_tokens = B;
   launch(k_prep, B, 128, 0, st, hidden, (int)md.d_model, slots, (const float*)nullptr, 0, (int)md.d_model, act, act_scale, B,
          (const TokenMeta*)nullptr, md.inv_sqrt_group, 1, 0);
-  project(md.logits, act, act_scale, logits, B, md.output_vocab, nullptr, st);
+  project(md.logits, act, act_scale, logits, B, md.output_vocab, nullptr, st, md.error);
 }
 
 void launch_select(const float* logits, int V, const uint32_t* mask, const int32_t* active, uint32_t* next, float* peaks, int B,
@@ -2129,7 +2129,7 @@ void launch_debug_hadamard(const ModelDev& md, const LayerDev& L, const float* i
 void launch_debug_project(const ModelDev& md, const QMat& W, const float* in, int K, int M, int8_t* act, float* act_scale,
                           float* out, int out_stride, cudaStream_t st) {
   k_prep<<<M, 128, 0, st>>>(in, K, nullptr, nullptr, 0, K, act, act_scale, M, nullptr, md.inv_sqrt_group, 0, 0);
-  project(W, act, act_scale, out, M, out_stride, nullptr, st);
+  project(W, act, act_scale, out, M, out_stride, nullptr, st, md.error);
 }
 
 // The product benchmark of the test hooks: k_prep (rotation and per-group
@@ -2145,7 +2145,7 @@ cudaError_t launch_product_bench(const QMat& W, const float* in, int M, int8_t* 
   t_pass_tokens = M;
   const int K = (int)W.cols;
   k_prep<<<M, 128, 0, st>>>(in, K, nullptr, nullptr, 0, K, act, act_scale, M, nullptr, 1.0f / std::sqrt((float)GROUP), 0, act_rows);
-  project(W, act, act_scale, out, M, (int)W.rows, nullptr, st, act_rows, error);
+  project(W, act, act_scale, out, M, (int)W.rows, nullptr, st, error, act_rows);
   if ((e = cudaGetLastError())) return e;
   *ms = 0.0f;
   if (reps <= 0) return cudaSuccess;
@@ -2153,7 +2153,7 @@ cudaError_t launch_product_bench(const QMat& W, const float* in, int M, int8_t* 
   if ((e = cudaEventCreate(&start))) return e;
   if ((e = cudaEventCreate(&stop))) return e;
   cudaEventRecord(start, st);
-  for (int r = 0; r < reps; ++r) project(W, act, act_scale, out, M, (int)W.rows, nullptr, st, act_rows, error);
+  for (int r = 0; r < reps; ++r) project(W, act, act_scale, out, M, (int)W.rows, nullptr, st, error, act_rows);
   cudaEventRecord(stop, st);
   e = cudaEventSynchronize(stop);
   float total = 0.0f;

@@ -10,8 +10,9 @@ namespace nbk {
 
 void set_exp_constants(const nbx::ExpConstants& constants, const nbx::ExceptionSet& exceptions, cudaStream_t stream);
 cudaError_t configure(const nbl::ModelDev& md, int t_cap);
-// Device flag the tensor-core product sets when a bounded wait gives up.
-void set_error_flag(int* flag);
+// Kernels the calling thread has launched or recorded into a graph so far
+// (the token loop's launchers; the test hooks are not counted).
+long launch_counter();
 
 void launch_embed(const nbl::ModelDev& md, const nbl::Work& w, int M, cudaStream_t st);
 // One decoder layer of M tokens. `distinct`: every token of the pass belongs

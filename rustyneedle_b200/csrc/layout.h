@@ -120,6 +120,7 @@ struct ModelDev {
   const int32_t* perm2;
   const float2* rotary;       // [max_seq_len][head_dim/2] (sin, cos)
   PageGeometry page;
+  int* error;                 // the engine's device flag: set when a bounded device wait gave up
 };
 
 // Per-token metadata of one forward pass.

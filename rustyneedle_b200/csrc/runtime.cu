@@ -177,7 +177,6 @@ struct Engine {
   ModelDev md{};
   std::vector<LayerDev> layers;
   DeviceArena arena;
-  std::vector<uint32_t> exception_slots;
   // sessions and KV pages
   uint32_t max_sessions = 0, max_pages = 0, num_pages = 0;
   uint8_t* pool = nullptr;
@@ -194,7 +193,7 @@ struct Engine {
   Work work{};
   uint32_t* d_tokens = nullptr;
   TokenMeta* d_meta = nullptr;
-  PinnedBuffer h_tokens, h_meta, h_misc;
+  PinnedBuffer h_tokens, h_meta, h_misc, h_error;
   // logits of single-session calls
   int8_t* d_logit_act = nullptr;
   float* d_logit_scale = nullptr;
@@ -290,6 +289,7 @@ static std::string expf_table_path() {
 
 static std::mutex g_table_mutex;
 static std::shared_ptr<nbx::ExpfTable> g_table;
+static std::map<int, nbx::ExceptionSet> g_device_exceptions;  // never freed: a device constant points at it
 
 static std::shared_ptr<nbx::ExpfTable> load_expf_table() {
   std::lock_guard<std::mutex> lock(g_table_mutex);
@@ -306,6 +306,22 @@ static std::shared_ptr<nbx::ExpfTable> load_expf_table() {
   }
   g_table = table;
   return table;
+}
+
+// The exception set's hash slots on `device` (uploaded once per process).
+static nbx::ExceptionSet device_exception_set(int device) {
+  auto table = load_expf_table();
+  std::lock_guard<std::mutex> lock(g_table_mutex);
+  auto it = g_device_exceptions.find(device);
+  if (it != g_device_exceptions.end()) return it->second;
+  uint32_t mask = 0;
+  const std::vector<uint32_t> slots = nbx::hash_slots(*table, mask);
+  uint32_t* d_slots = nullptr;
+  NB_CUDA(cudaMalloc(&d_slots, slots.size() * 4));
+  NB_CUDA(cudaMemcpy(d_slots, slots.data(), slots.size() * 4, cudaMemcpyHostToDevice));
+  const nbx::ExceptionSet set{d_slots, mask};
+  g_device_exceptions.emplace(device, set);
+  return set;
 }
 
 // Expands a codebook matrix to int8 through the integer level table, in the
@@ -387,13 +403,12 @@ std::shared_ptr<Engine> open_engine(const char* path, const nb_options* opt) {
   cudaStream_t st = E->stream;
   DeviceArena& A = E->arena;
 
-  // libm-compatible exponential
-  auto table = load_expf_table();
-  uint32_t mask = 0;
-  E->exception_slots = nbx::hash_slots(*table, mask);
-  uint32_t* d_slots = A.upload(E->exception_slots, st);
+  // libm-compatible exponential: the kernels read the exception set through a
+  // per-device constant, so its device copy is one per device for the whole
+  // process (every engine on the device uses the same table)
+  const nbx::ExceptionSet exceptions = device_exception_set(device);
   nbx::ExpConstants constants = nbx::make_exp_constants();
-  nbk::set_exp_constants(constants, nbx::ExceptionSet{d_slots, mask}, st);
+  nbk::set_exp_constants(constants, exceptions, st);
   NB_CUDA(cudaGetLastError());
 
   const uint32_t d = g.d_model, H = g.num_heads, KV = g.num_kv_heads, L = g.num_layers, N = g.hada_n;
@@ -592,7 +607,8 @@ std::shared_ptr<Engine> open_engine(const char* path, const nb_options* opt) {
   NB_CUDA(cudaMemsetAsync(E->d_logit_act, 0, logit_rows * d, st));
   E->d_error = A.alloc<int>(1);
   NB_CUDA(cudaMemsetAsync(E->d_error, 0, sizeof(int), st));
-  nbk::set_error_flag(E->d_error);
+  E->md.error = E->d_error;
+  E->h_error.ensure(sizeof(int));
   E->d_logit_scale = A.alloc<float>((size_t)B * (d / GROUP));
   E->d_logits = A.alloc<float>((size_t)B * V);
   E->d_slots = A.alloc<int32_t>(B);
@@ -683,6 +699,7 @@ struct nb_batch {
   DeviceArena arena;
   cudaEvent_t fork = nullptr, join[MAX_STEP_GROUPS] = {};
   int groups = 1;  // independent chains of the step (sequences split in runs of whole 32-row tiles)
+  uint32_t step_kernels = 0;  // kernels in the last step graph recorded
   bool use_graphs = true;
   ~nb_batch() {
     for (auto& kv : graphs) cudaGraphExecDestroy(kv.second);
@@ -855,6 +872,19 @@ static void check_tokens(const Engine& E, const uint32_t* ids, size_t count) {
     if (ids[i] >= E.geo.vocab) fail(NB_ERR_ARGUMENT, "token id " + std::to_string(ids[i]) + " is outside the vocabulary");
 }
 
+// The engine's device error flag (a bounded device wait gave up): its read is
+// queued with a pass's results and checked once the stream has synchronised.
+static void queue_error_read(Engine& E) {
+  NB_CUDA(cudaMemcpyAsync(E.h_error.p, E.d_error, sizeof(int), cudaMemcpyDeviceToHost, E.stream));
+}
+static void raise_device_error(Engine& E) {
+  if (*E.h_error.as<int>()) {
+    *E.h_error.as<int>() = 0;
+    NB_CUDA(cudaMemsetAsync(E.d_error, 0, sizeof(int), E.stream));
+    fail(NB_ERR_TIMEOUT, "a bounded device wait gave up");
+  }
+}
+
 static void run_tokens(nb_session* s, const uint32_t* ids, size_t count) {
   Engine& E = *s->engine;
   if (s->length + count > E.geo.max_seq_len)
@@ -869,7 +899,9 @@ static void run_tokens(nb_session* s, const uint32_t* ids, size_t count) {
     forward(E, s->active, specs.data(), (uint32_t)n);
     done += n;
   }
+  queue_error_read(E);
   NB_CUDA(cudaStreamSynchronize(E.stream));
+  raise_device_error(E);
   s->length += (uint32_t)count;
 }
 
@@ -906,7 +938,9 @@ nb_status nb_session_logits(nb_session* session, float* out, size_t capacity) {
     nbk::launch_logits(E.md, E.d_hidden, E.d_slots, 1, E.d_logit_act, E.d_logit_scale, E.d_logits, E.stream);
     NB_CUDA(cudaGetLastError());
     NB_CUDA(cudaMemcpyAsync(out, E.d_logits, (size_t)V * 4, cudaMemcpyDeviceToHost, E.stream));
+    queue_error_read(E);
     NB_CUDA(cudaStreamSynchronize(E.stream));
+    raise_device_error(E);
   });
 }
 
@@ -1098,12 +1132,14 @@ static void launch_step(nb_batch* b, bool masked, bool stats) {
   if (it == b->graphs.end()) {
     cudaGraph_t graph;
     NB_CUDA(cudaStreamBeginCapture(E.stream, cudaStreamCaptureModeThreadLocal));
+    const long before = nbk::launch_counter();
     try {
       build_step(b, masked, stats);
     } catch (...) {
       cudaStreamEndCapture(E.stream, &graph);
       throw;
     }
+    b->step_kernels = (uint32_t)(nbk::launch_counter() - before);
     NB_CUDA(cudaStreamEndCapture(E.stream, &graph));
     cudaGraphExec_t exec;
     cudaError_t e = cudaGraphInstantiate(&exec, graph, 0);
@@ -1134,7 +1170,9 @@ nb_status nb_batch_step(nb_batch* batch, const uint32_t* mask_bits, uint32_t* ne
     launch_step(batch, mask_bits != nullptr, stats != nullptr);
     NB_CUDA(cudaMemcpyAsync(batch->h_next.p, batch->d_tokens, B * 4, cudaMemcpyDeviceToHost, E.stream));
     if (stats) NB_CUDA(cudaMemcpyAsync(batch->h_stats.p, E.d_stats, (size_t)B * 8, cudaMemcpyDeviceToHost, E.stream));
+    queue_error_read(E);
     NB_CUDA(cudaStreamSynchronize(E.stream));
+    raise_device_error(E);
     const int32_t* ha = batch->h_active.as<int32_t>();
     for (uint32_t i = 0; i < B; ++i) {
       next[i] = ha[i] ? batch->h_next.as<uint32_t>()[i] : 0xffffffffu;
@@ -1163,7 +1201,9 @@ nb_status nb_batch_step_device(nb_batch* batch, const uint32_t* mask_bits_device
       NB_CUDA(cudaMemcpyAsync(E.d_mask, mask_bits_device, (size_t)B * words * 4, cudaMemcpyDeviceToDevice, E.stream));
     launch_step(batch, mask_bits_device != nullptr, false);
     NB_CUDA(cudaMemcpyAsync(next_device, batch->d_tokens, B * 4, cudaMemcpyDeviceToDevice, E.stream));
+    queue_error_read(E);
     NB_CUDA(cudaStreamSynchronize(E.stream));
+    raise_device_error(E);
     finish_step(batch);
   });
 }
@@ -1197,11 +1237,14 @@ nb_status nb_batch_run(nb_batch* batch, uint32_t steps, const uint32_t* mask_bit
         NB_CUDA(cudaMemcpyAsync(tokens_device + (size_t)k * B, batch->d_tokens, B * 4, cudaMemcpyDeviceToDevice, E.stream));
     }
     NB_CUDA(cudaEventRecord(stop, E.stream));
+    queue_error_read(E);  // after the timed region
     NB_CUDA(cudaEventSynchronize(stop));
     float ms = 0.0f;
     NB_CUDA(cudaEventElapsedTime(&ms, start, stop));
     cudaEventDestroy(start);
     cudaEventDestroy(stop);
+    NB_CUDA(cudaStreamSynchronize(E.stream));
+    raise_device_error(E);
     if (elapsed_ms) *elapsed_ms = ms;
     for (nb_session* s : batch->sessions) s->length += steps;
   });
@@ -1427,6 +1470,12 @@ nb_status nb_debug_kv(nb_session* session, uint32_t layer, int8_t* keys, float* 
 }
 
 }  // extern "C"
+
+extern "C" nb_status nb_debug_step_kernels(nb_batch* batch, uint32_t* kernels) {
+  if (!batch || !kernels) return NB_ERR_ARGUMENT;
+  *kernels = batch->step_kernels;
+  return NB_OK;
+}
 
 extern "C" nb_status nb_debug_time_attention(nb_batch* batch, uint32_t reps, float* ms_per_launch, double* bytes_per_launch) {
   if (!batch || reps == 0 || !ms_per_launch) return NB_ERR_ARGUMENT;

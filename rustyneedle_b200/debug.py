@@ -28,6 +28,7 @@ def _declare() -> None:
         "nb_debug_hadamard": [P, U32, P, SZ, P],
         "nb_debug_kv": [P, U32, P, P, P, P],
         "nb_debug_time_attention": [P, U32, ctypes.POINTER(ctypes.c_float), ctypes.POINTER(ctypes.c_double)],
+        "nb_debug_step_kernels": [P, ctypes.POINTER(ctypes.c_uint32)],
         "nb_debug_product": [I, U32, P, P, P, U32, U32, P, U32, P, U32, ctypes.POINTER(ctypes.c_float)],
     }.items():
         fn = getattr(L, name)
@@ -86,6 +87,14 @@ def time_attention(batch, reps: int = 5):
     ms, nbytes = ctypes.c_float(), ctypes.c_double()
     _check(lib().nb_debug_time_attention(batch._h, reps, ctypes.byref(ms), ctypes.byref(nbytes)))
     return float(ms.value), float(nbytes.value)
+
+
+def step_kernels(batch) -> int:
+    """Kernels in the batch's step graph (0 before its first step)."""
+    _declare()
+    n = ctypes.c_uint32()
+    _check(lib().nb_debug_step_kernels(batch._h, ctypes.byref(n)))
+    return int(n.value)
 
 
 def product(bits: int, packed: np.ndarray, levels: np.ndarray, norms: np.ndarray, rows: int, cols: int, x: np.ndarray,

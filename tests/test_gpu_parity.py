@@ -262,6 +262,41 @@ def test_batched_decode_matches_single_sessions(device_model, oracle_model, orac
         assert _bits_equal(s.logits(), o.logits())
 
 
+def test_wide_batch_decode_matches_the_oracle(archive_path, oracle_model, oracle_lib):
+    """A decode step over more than 64 sequences: the attention does the head step
+    itself and prepares the out projection in its last CTA per token, the block
+    finish runs one CTA per token, the products run on the tensor cores."""
+    import rustyneedle_b200 as nb
+
+    model = nb.Model.open(archive_path, max_sessions=80).with_depth(4)
+    omodel = oracle_model.with_depth(4)
+    lengths = [5, 33, 64, 97, 130, 190] * 12  # 72 sequences
+    sessions, oracles = [], []
+    for i, n in enumerate(lengths):
+        ids = prompt_ids(500 + i, n)
+        s = nb.Session(model)
+        s.feed(ids)
+        sessions.append(s)
+        o = oracle_lib.Session(omodel)
+        o.feed(ids)
+        oracles.append(o)
+    batch = nb.Batch(model, sessions)
+    for _ in range(3):
+        got = batch.step()
+        want = []
+        for o in oracles:
+            token = oracle_lib.argmax(o.logits())
+            o.push(token)
+            want.append(token)
+        assert list(got) == want
+    for s, o in zip(sessions, oracles):
+        assert _bits_equal(s.logits(), o.logits())
+    batch.close()
+    for s in sessions:
+        s.close()
+    model.close()
+
+
 def test_clone_shares_the_prefix_copy_on_write(device_model, oracle_model, oracle_lib):
     import rustyneedle_b200 as nb
 
