@@ -236,7 +236,7 @@ def main():
     if DEPTH != model.config.num_layers:
         model = model.with_depth(DEPTH)
     if args.batch1_only:
-        print(json.dumps({"batch1": batch1(nb, model, local)}), flush=True)
+        print(json.dumps({"batch1": batch1(nb, model, local, args.ncu_range)}), flush=True)
         return
     t0 = time.perf_counter()
     sessions = []
@@ -320,8 +320,9 @@ def main():
     dp.close_group(dist)
 
 
-def batch1(nb, model, device: int = 0):
-    """Config 1: depth 20, batch 1, 512-token prompt, 256 masked greedy steps."""
+def batch1(nb, model, device: int = 0, ncu_range: bool = False):
+    """Config 1: depth 20, batch 1, 512-token prompt, 256 masked greedy steps
+    (with ncu_range, steps 64 and 65 are bracketed by cudaProfilerStart/Stop)."""
     rng = np.random.default_rng(7)
     ids = rng.integers(10, 8000, 512).astype(np.uint32)
     s = nb.Session(model)
@@ -337,7 +338,11 @@ def batch1(nb, model, device: int = 0):
         masks.append(np.packbits(allowed.astype(np.uint8), bitorder="little").view(np.uint32)[:words].copy())
     times = []
     with Clocks(device) as clocks:
-        for m in masks:
+        for k, m in enumerate(masks):
+            if ncu_range and k in (64, 66):
+                import torch
+
+                (torch.cuda.cudart().cudaProfilerStart if k == 64 else torch.cuda.cudart().cudaProfilerStop)()
             t = time.perf_counter()
             b.step(m)
             times.append(1000 * (time.perf_counter() - t))
