@@ -179,6 +179,19 @@ def test_feed_matches_the_oracle_hidden_logits_and_cache(device_model, oracle_mo
     assert _bits_equal(s.logits(), o.logits()), _mismatch(s.logits(), o.logits())
 
 
+def test_long_prefill_matches_the_oracle(device_model, oracle_model, oracle_lib):
+    """A 600-token prompt in one pass (19 token blocks of the tcgen05 product, the last ragged)."""
+    import rustyneedle_b200 as nb
+
+    ids = prompt_ids(11, 600)
+    s = nb.Session(device_model.with_depth(2))
+    s.feed(ids)
+    o = oracle_lib.Session(oracle_model.with_depth(2))
+    o.feed(ids)
+    assert _bits_equal(s.logits(), o.logits()), _mismatch(s.logits(), o.logits())
+    s.close()
+
+
 def test_config0_greedy_tokens_are_identical(device_model, oracle_model, oracle_lib):
     """Config 0: depth 2, 32 prompt ids, 64 greedy tokens, batch 1, unconstrained."""
     import rustyneedle_b200 as nb

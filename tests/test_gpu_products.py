@@ -3,7 +3,8 @@
 nb_debug_product, bit-exact against the CPU restatement's INT product
 (QuantisedMatrix::prepare + multiply_vector, crates/kernels/src/matrix.rs:123-165).
 Token counts cover the CUDA-core GEMV (<= 8), the 16-token and 32-token
-tensor-core tiles, and K = 2048 (four 512-column chunks)."""
+tensor-core tiles, large passes with a ragged last block (600 and 2100
+tokens), and K = 2048 (four 512-column chunks)."""
 
 import numpy as np
 import pytest
@@ -14,7 +15,7 @@ SHAPES = [(512, 2048, 2), (2048, 512, 2), (2048, 512, 4), (512, 8192, 4)]
 
 
 @pytest.mark.parametrize("cols,rows,bits", SHAPES)
-@pytest.mark.parametrize("tokens", [1, 8, 13, 40, 256])
+@pytest.mark.parametrize("tokens", [1, 8, 13, 40, 256, 600, 2100])
 def test_product_matches_the_integer_restatement(native_built, oracle_lib, cols, rows, bits, tokens):
     from rustyneedle_b200 import debug, synthetic
 
