@@ -9,7 +9,8 @@ from dataclasses import dataclass
 import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-_LIBRARY = os.path.join(HERE, "_native", "libneedle_b200.so")
+# $NEEDLE_B200_LIBRARY selects another build of the library (same ABI)
+_LIBRARY = os.environ.get("NEEDLE_B200_LIBRARY") or os.path.join(HERE, "_native", "libneedle_b200.so")
 
 NB_OK = 0
 STATUS_NAMES = {
