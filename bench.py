@@ -239,11 +239,8 @@ def main():
         print(json.dumps({"batch1": batch1(nb, model, local, args.ncu_range)}), flush=True)
         return
     t0 = time.perf_counter()
-    sessions = []
-    for ids in rank_prompts:
-        s = nb.Session(model)
-        s.feed(ids)
-        sessions.append(s)
+    sessions = [nb.Session(model) for _ in rank_prompts]
+    nb.feed_many(sessions, rank_prompts)  # the prompts packed into shared prefill passes
     setup_s = time.perf_counter() - t0
     batch = nb.Batch(model, sessions)
 

@@ -93,6 +93,15 @@ void nb_session_release(nb_session* session);
  * passes; results are bit-identical to pushing the tokens one at a time. */
 nb_status nb_session_feed(nb_session* session, const uint32_t* ids, size_t count);
 
+/* Several sessions' Session::feed (session.rs:56-70) in one call: their
+ * prompts are packed, in session order, into shared forward passes of up to
+ * the model's batch-token capacity (options.max_batch_tokens); each session's
+ * state is bit-identical to feeding it alone. ids[i] holds counts[i] tokens
+ * of sessions[i]. The sessions must be distinct and belong to one model with
+ * the same active layers. No reference counterpart: the reference prefills
+ * one session at a time (prefill.rs:10-99). */
+nb_status nb_sessions_feed(nb_session* const* sessions, const uint32_t* const* ids, const size_t* counts, size_t n);
+
 /* Session::push (session.rs:72-148): one token through every active layer. */
 nb_status nb_session_push(nb_session* session, uint32_t id);
 

@@ -23,8 +23,9 @@ from ._native import (  # noqa: F401
     NeedleError,
     Session,
     StepStats,
+    feed_many,
     library_path,
 )
 
 __all__ = ["Model", "Session", "Batch", "ModelConfig", "StepStats", "NeedleError", "DepthError", "ContextOverflow",
-           "library_path"]
+           "feed_many", "library_path"]

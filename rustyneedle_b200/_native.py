@@ -80,6 +80,7 @@ def lib() -> ctypes.CDLL:
             "nb_session_clone": (I, [P, ctypes.POINTER(P)]),
             "nb_session_release": (None, [P]),
             "nb_session_feed": (I, [P, P, SZ]),
+            "nb_sessions_feed": (I, [P, P, P, SZ]),
             "nb_session_push": (I, [P, U32]),
             "nb_session_logits": (I, [P, P, SZ]),
             "nb_session_len": (SZ, [P]),
@@ -227,6 +228,22 @@ class Session:
             self.close()
         except Exception:
             pass
+
+
+def feed_many(sessions, prompts) -> None:
+    """Feeds every session its prompt in shared forward passes (nb_sessions_feed);
+    each session ends as if fed alone."""
+    sessions = list(sessions)
+    if len(sessions) != len(prompts):
+        raise ValueError("one prompt per session")
+    if not sessions:
+        return
+    arrays = [np.ascontiguousarray(p, dtype=np.uint32) for p in prompts]
+    n = len(sessions)
+    handles = (ctypes.c_void_p * n)(*[s._h for s in sessions])
+    ids = (ctypes.c_void_p * n)(*[a.ctypes.data if a.size else None for a in arrays])
+    counts = (ctypes.c_size_t * n)(*[a.size for a in arrays])
+    _check(lib().nb_sessions_feed(handles, ids, counts, n))
 
 
 class Batch:

@@ -915,6 +915,52 @@ nb_status nb_session_feed(nb_session* session, const uint32_t* ids, size_t count
   });
 }
 
+nb_status nb_sessions_feed(nb_session* const* sessions, const uint32_t* const* ids, const size_t* counts, size_t n) {
+  if (n == 0) return NB_OK;
+  if (!sessions || !ids || !counts || !sessions[0]) return NB_ERR_ARGUMENT;
+  return guard([&] {
+    Engine& E = *sessions[0]->engine;
+    std::lock_guard<std::mutex> lock(E.mutex);
+    for (size_t i = 0; i < n; ++i) {
+      nb_session* s = sessions[i];
+      if (!s || s->engine.get() != &E) fail(NB_ERR_ARGUMENT, "the sessions must belong to one model");
+      if (s->active != sessions[0]->active) fail(NB_ERR_ARGUMENT, "the sessions must share the model's active layers");
+      for (size_t j = 0; j < i; ++j)
+        if (sessions[j] == s) fail(NB_ERR_ARGUMENT, "a session appears twice");
+      if (!ids[i] && counts[i]) fail(NB_ERR_ARGUMENT, "a session's ids are null");
+      check_tokens(E, ids[i], counts[i]);
+      if (s->length + counts[i] > E.geo.max_seq_len)
+        fail(NB_ERR_CONTEXT_OVERFLOW, "a session would exceed max_seq_len " + std::to_string(E.geo.max_seq_len));
+    }
+    NB_CUDA(cudaSetDevice(E.device));
+    // the prompts in session order, packed into passes of up to the engine's
+    // capacity; a prompt may continue into the next pass (exact, as chunked
+    // feeding is), and each pass marks the last token of every sequence in it
+    std::vector<TokenSpec> specs;
+    specs.reserve(E.capacity);
+    size_t si = 0, done = 0;
+    while (si < n) {
+      specs.clear();
+      while (si < n && specs.size() < E.capacity) {
+        nb_session* s = sessions[si];
+        const size_t take = std::min<size_t>(E.capacity - specs.size(), counts[si] - done);
+        for (size_t k = 0; k < take; ++k)
+          specs.push_back(TokenSpec{ids[si][done + k], s->slot, (uint32_t)(s->length + done + k), k + 1 == take});
+        done += take;
+        if (done == counts[si]) {
+          ++si;
+          done = 0;
+        }
+      }
+      if (!specs.empty()) forward(E, sessions[0]->active, specs.data(), (uint32_t)specs.size());
+    }
+    queue_error_read(E);
+    NB_CUDA(cudaStreamSynchronize(E.stream));
+    raise_device_error(E);
+    for (size_t i = 0; i < n; ++i) sessions[i]->length += (uint32_t)counts[i];
+  });
+}
+
 nb_status nb_session_push(nb_session* session, uint32_t id) {
   if (!session) return NB_ERR_ARGUMENT;
   return guard([&] {

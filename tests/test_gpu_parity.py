@@ -275,6 +275,32 @@ def test_batched_decode_matches_single_sessions(device_model, oracle_model, orac
         assert _bits_equal(s.logits(), o.logits())
 
 
+def test_feeding_many_sessions_at_once_matches_feeding_each(device_model):
+    """nb_sessions_feed packs several prompts into shared passes (one prompt
+    spans a pass boundary): every session ends bit-identical to feeding it alone."""
+    import rustyneedle_b200 as nb
+
+    model = device_model.with_depth(3)
+    lengths = [40, 700, 1, 300, 90]  # 1131 tokens: two passes of up to 1024
+    prompts = [prompt_ids(900 + i, n) for i, n in enumerate(lengths)]
+    together = [nb.Session(model) for _ in lengths]
+    nb.feed_many(together, prompts)
+    for s, ids in zip(together, prompts):
+        alone = nb.Session(model)
+        alone.feed(ids)
+        assert len(s) == len(alone) == len(ids)
+        assert _bits_equal(s.logits(), alone.logits()), _mismatch(s.logits(), alone.logits())
+        alone.close()
+    # both continue alike
+    a, b = together[1], nb.Session(model)
+    b.feed(prompts[1])
+    a.push(7)
+    b.push(7)
+    assert _bits_equal(a.logits(), b.logits())
+    for s in together + [b]:
+        s.close()
+
+
 def test_wide_batch_decode_matches_the_oracle(archive_path, oracle_model, oracle_lib):
     """A decode step over more than 64 sequences: the attention does the head step
     itself and prepares the out projection in its last CTA per token, the block
