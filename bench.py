@@ -288,7 +288,8 @@ def main():
             traffic = round(t["dram_bytes"] / t["algorithmic_bytes"] * att_bytes)
     except (OSError, KeyError, ZeroDivisionError):
         traffic = None
-    roofline = {"kernel": "k_attend (paged int8 attention, one launch = one layer of the batch)", "bound": "hbm",
+    roofline = {"kernel": "k_attend (paged int8 attention; one layer of the batch: the step's launches, one per group of 128 sequences)",
+                "bound": "hbm",
                 "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                 "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": traffic,
                 "peak_source": f"{peak_kind} hbm_gbs", "launch_ms": att_ms, "algorithmic_bytes": att_bytes}

@@ -51,9 +51,10 @@ nb_status nb_debug_hidden(nb_session* session, float* out);
 nb_status nb_debug_kv(nb_session* session, uint32_t layer, int8_t* keys, float* key_scales, int8_t* values,
                       float* value_scales);
 
-/* Replays the attention kernel of every active layer over the batch's
- * current positions `reps` times and reports the mean device time of one
- * launch (CUDA events on the model's stream) and the KV bytes one launch
+/* Replays the attention of every active layer over the batch's current
+ * positions `reps` times (per layer the step's launches, one per group of
+ * sequences, one after another) and reports the mean device time of one
+ * layer's attention (CUDA events on the model's stream) and the KV bytes it
  * must read (keys, values and their scales of every attended position). */
 nb_status nb_debug_time_attention(nb_batch* batch, uint32_t reps, float* ms_per_launch, double* bytes_per_launch);
 

@@ -1071,8 +1071,14 @@ static void build_step(nb_batch* b, bool masked, bool stats) {
 // Chains per step: one by default (measured on B200: a single chain of 256
 // sequences steps as fast as four concurrent chains of 64);
 // $NEEDLE_B200_STEP_GROUPS sets another count.
-static int step_groups(uint32_t) {
-  int groups = 1;
+// Two independent chains when each keeps at least STEP_GROUP_MIN sequences:
+// one group's HBM-bound attention then runs beside the other's FP32-bound
+// block finish (B = 256: 177k vs 172k tokens/s on one B200). Smaller groups
+// would fall to the small-pass kernels (four groups of 64: 110k).
+// $NEEDLE_B200_STEP_GROUPS=N forces N.
+constexpr uint32_t STEP_GROUP_MIN = 128;
+static int step_groups(uint32_t count) {
+  int groups = count >= 2 * STEP_GROUP_MIN ? 2 : 1;
   if (const char* env = std::getenv("NEEDLE_B200_STEP_GROUPS")) groups = std::atoi(env);
   return std::max(1, std::min(groups, MAX_STEP_GROUPS));
 }
@@ -1542,15 +1548,20 @@ extern "C" nb_status nb_debug_time_attention(nb_batch* batch, uint32_t reps, flo
       bytes += (double)(pos + 1) * per_position;
     }
     NB_CUDA(cudaMemcpyAsync(batch->d_meta, hm, B * sizeof(TokenMeta), cudaMemcpyHostToDevice, E.stream));
-    Work w = E.work;
-    w.meta = batch->d_meta;
-    if (batch->groups == 1) w.order = batch->d_order;  // the step's launch order (per group otherwise)
+    Work base = E.work;
+    base.meta = batch->d_meta;
+    base.order = batch->d_order;
     KvDev kv = E.kv();
-    // the attention kernel the step runs, with the output projection's
+    // the attention launches the step runs (one per group of sequences, each
+    // over its rows in its launch order), with the output projection's
     // activation step fused in where it is; the head step (which the step
     // also fuses in) is left out, since replaying it would rewrite the cache
+    const uint32_t per = group_rows(B, batch->groups);
     auto attend = [&](int32_t layer) {
-      nbk::launch_attention(E.md, E.layers[layer], w, kv, (int)B, layer, E.t_cap, false, E.stream);
+      for (uint32_t b0 = 0; b0 < B; b0 += per) {
+        const Work w = work_rows(E, base, b0);
+        nbk::launch_attention(E.md, E.layers[layer], w, kv, (int)std::min(per, B - b0), layer, E.t_cap, false, E.stream);
+      }
     };
     cudaEvent_t start, stop;
     NB_CUDA(cudaEventCreate(&start));
