@@ -1068,9 +1068,6 @@ static void build_step(nb_batch* b, bool masked, bool stats) {
   for (int i = 0; i < g; ++i) NB_CUDA(cudaStreamWaitEvent(E.stream, b->join[i], 0));
 }
 
-// Chains per step: one by default (measured on B200: a single chain of 256
-// sequences steps as fast as four concurrent chains of 64);
-// $NEEDLE_B200_STEP_GROUPS sets another count.
 // Two independent chains when each keeps at least STEP_GROUP_MIN sequences:
 // one group's HBM-bound attention then runs beside the other's FP32-bound
 // block finish (B = 256: 177k vs 172k tokens/s on one B200). Smaller groups
