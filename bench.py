@@ -307,15 +307,57 @@ def main():
     if not args.no_batch1 and rank == 0 and not args.profile:
         batch.close()
         line["batch1"] = batch1(nb, model, local)
+        line["config0"] = config0(nb, model)
     if rank == 0 and world == 1 and not args.no_cpu and not args.profile:
         from oracle import oracle
 
         oracle.build()
         line["cpu_baseline"] = cpu_baseline(archive, rank_prompts, os.cpu_count() or 1)
+        if "config0" in line:
+            line["config0"]["cpu"] = config0_cpu(archive)
     if rank == 0:
         print(json.dumps(line), flush=True)
     batch.close()
     dp.close_group(dist)
+
+
+def config0(nb, model):
+    """Config 0: depth 2, batch 1, 32 prompt ids, 64 unconstrained greedy tokens."""
+    rng = np.random.default_rng(3)
+    shallow = model.with_depth(2)
+    s = nb.Session(shallow)
+    s.feed(rng.integers(10, 8000, 32).astype(np.uint32))
+    b = nb.Batch(shallow, [s])
+    times = []
+    for _ in range(64):
+        t = time.perf_counter()
+        b.step()
+        times.append(1000 * (time.perf_counter() - t))
+    b.close()
+    s.close()
+    shallow.close()
+    times = times[4:]
+    p50 = float(np.percentile(times, 50))
+    return {"p50_ms_per_token": round(p50, 4), "tokens_per_s": round(1000.0 / p50, 1), "steps": len(times),
+            "note": "depth 2, 32-token prompt, greedy through nb_batch_step (token out), unconstrained"}
+
+
+def config0_cpu(archive: str):
+    """Config 0 on the CPU oracle (FLOAT mode, one thread): the same prompt and 64 greedy tokens."""
+    from oracle import oracle
+
+    rng = np.random.default_rng(3)
+    model = oracle.Model.open(archive, oracle.MODE_FLOAT, 1).with_depth(2)
+    s = oracle.Session(model)
+    s.feed(rng.integers(10, 8000, 32).astype(np.uint32))
+    times = []
+    for _ in range(64):
+        t = time.perf_counter()
+        s.push(oracle.argmax(s.logits()))
+        times.append(1000 * (time.perf_counter() - t))
+    p50 = float(np.percentile(times[4:], 50))
+    return {"p50_ms_per_token": round(p50, 4), "tokens_per_s": round(1000.0 / p50, 1), "cores": 1,
+            "kind": "port", "sample": "60 timed greedy tokens after 4 untimed"}
 
 
 def batch1(nb, model, device: int = 0, ncu_range: bool = False):
