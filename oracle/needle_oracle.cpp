@@ -22,6 +22,7 @@
 #include <cmath>
 #include <cstdio>
 #include <cstring>
+#include <deque>
 #include <fstream>
 #include <memory>
 #include <stdexcept>
@@ -800,6 +801,7 @@ struct LayerW {
   std::vector<float> norm_in, post_norm, pre_hada, q_norm, k_norm;
   float attention_gate = 0.0f;
   QMatrix q, k, v, gate, out;
+  std::vector<float> taps[3];  // q, k, v causal convolution gains [tap][width]; empty without taps
   Hadamard hada;
 };
 
@@ -929,7 +931,6 @@ std::vector<float> hadamard_apply(const Hadamard& h, const float* input, size_t 
 
 std::shared_ptr<Weights> load_weights(const Archive& a, const Layout& L) {
   const Geometry& g = a.geo;
-  if (g.qkv_conv_taps > 0) throw Failure(ERR_UNSUPPORTED, "qkv conv taps are not restated by this oracle");
   if (!g.engram_sites.empty()) throw Failure(ERR_UNSUPPORTED, "engram sites are not restated by this oracle");
   if (g.num_heads % std::max<size_t>(g.num_kv_heads, 1) != 0) throw Failure(ERR_ARCHIVE, "query heads are not a multiple of kv heads");
   auto w = std::make_shared<Weights>();
@@ -951,6 +952,14 @@ std::shared_ptr<Weights> load_weights(const Archive& a, const Layout& L) {
     lw.v = load_matrix(a, t.v);
     lw.gate = load_matrix(a, t.gate);
     lw.out = load_matrix(a, t.out);
+    if (t.has_taps) {
+      // model/src/attention.rs:30 (floats of the three tap tensors)
+      const size_t widths[3] = {lw.q.rows, lw.k.rows, lw.v.rows};
+      for (int i = 0; i < 3; ++i) {
+        lw.taps[i] = floats(a, t.taps[i]);
+        if (lw.taps[i].size() < g.qkv_conv_taps * widths[i]) throw Failure(ERR_ARCHIVE, "conv tap tensor is shorter than taps x width");
+      }
+    }
     lw.q_norm = floats(a, t.q_norm);
     lw.k_norm = floats(a, t.k_norm);
     lw.post_norm = floats(a, t.post_norm);
@@ -1051,7 +1060,20 @@ void multiply_batch_float(const QMatrix& m, const float* rotated, size_t count, 
 struct Cache {
   std::vector<int8_t> keys, values;               // [position][kv][dim]
   std::vector<std::vector<float>> key_scales, value_scales;  // [kv][position]
+  std::deque<std::vector<float>> raw_history[3];  // q, k, v projections before the taps, newest first
 };
+
+// model/src/attention.rs:83-93 (mix_taps): Σ over tap < min(taps, position + 1)
+// of gain[tap] · history[tap], from +0.0, one multiply and one add per term.
+void mix_taps(const std::vector<float>& gains, const std::deque<std::vector<float>>& history, size_t taps, size_t position,
+              float* out, size_t width) {
+  for (size_t i = 0; i < width; ++i) out[i] = 0.0f;
+  for (size_t tap = 0; tap < std::min(taps, position + 1); ++tap) {
+    const float* g = &gains[tap * width];
+    const std::vector<float>& sample = history.at(tap);
+    for (size_t i = 0; i < width; ++i) out[i] += g[i] * sample[i];
+  }
+}
 
 // crates/kernels/src/attention.rs:251-280 for one head over positions [first, total).
 void attend_head(const int8_t* query, float query_scale, const Cache& cache, size_t kv, size_t kv_heads, size_t qk, size_t vd,
@@ -1248,6 +1270,16 @@ std::vector<float> attend(const nbo_model* M, const LayerW& W, size_t layer, Cac
   std::vector<float> q(W.q.rows), k(W.k.rows), v(W.v.rows), gate(W.gate.rows);
   std::vector<Job> jobs{{&W.q, 0, q.data(), W.q.rows}, {&W.k, 0, k.data(), W.k.rows}, {&W.v, 0, v.data(), W.v.rows}, {&W.gate, 0, gate.data(), W.gate.rows}};
   multiply_jobs(jobs, rotated.data(), M->mode, M->threads);
+  if (!W.taps[0].empty()) {
+    // attention.rs:105-111: the raw rows join the history, then each is mixed
+    size_t taps = g.qkv_conv_taps;
+    std::vector<float>* rows[3] = {&q, &k, &v};
+    for (int i = 0; i < 3; ++i) {
+      cache.raw_history[i].push_front(*rows[i]);
+      while (cache.raw_history[i].size() > taps) cache.raw_history[i].pop_back();
+    }
+    for (int i = 0; i < 3; ++i) mix_taps(W.taps[i], cache.raw_history[i], taps, position, rows[i]->data(), rows[i]->size());
+  }
   std::vector<int8_t> qcodes;
   std::vector<float> qscales;
   heads_and_cache(M, W, cache, freq, position, q.data(), k.data(), v.data(), qcodes, qscales);
@@ -1359,6 +1391,30 @@ void prefill_float(nbo_session* s, const uint32_t* tokens, size_t count) {
     multiply_batch_float(W.k, rotated.data(), count, k.data(), M->threads);
     multiply_batch_float(W.v, rotated.data(), count, v.data(), M->threads);
     multiply_batch_float(W.gate, rotated.data(), count, gate.data(), M->threads);
+    if (!W.taps[0].empty()) {
+      // attention.rs:243-276: token t's tap j reads row t - j of this chunk, or
+      // the history before it; the history keeps the newest rows
+      size_t taps = g.qkv_conv_taps;
+      std::vector<float>* rows[3] = {&q, &k, &v};
+      for (int i = 0; i < 3; ++i) {
+        size_t width = rows[i]->size() / count;
+        std::vector<float> mixed(count * width, 0.0f);
+        const std::deque<std::vector<float>> previous = cache.raw_history[i];
+        for (size_t t = 0; t < count; ++t) {
+          size_t position = first + t;
+          for (size_t tap = 0; tap < std::min(taps, position + 1); ++tap) {
+            const float* src = tap <= t ? &(*rows[i])[(t - tap) * width] : previous.at(tap - t - 1).data();
+            const float* gn = &W.taps[i][tap * width];
+            for (size_t c = 0; c < width; ++c) mixed[t * width + c] += gn[c] * src[c];
+          }
+        }
+        size_t newest = std::min(count, taps);
+        for (size_t t = count - newest; t < count; ++t)
+          cache.raw_history[i].push_front(std::vector<float>(rows[i]->begin() + t * width, rows[i]->begin() + (t + 1) * width));
+        while (cache.raw_history[i].size() > taps) cache.raw_history[i].pop_back();
+        *rows[i] = std::move(mixed);
+      }
+    }
     std::vector<int8_t> qcodes(count * H * qk);
     std::vector<float> qscales(count * H);
     for (size_t t = 0; t < count; ++t) {

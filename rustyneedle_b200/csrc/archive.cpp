@@ -197,9 +197,7 @@ Layout Archive::resolve() const {
     t.v = take();
     if (geo_.qkv_conv_taps > 0) {
       t.has_taps = true;
-      take();
-      take();
-      take();
+      for (uint32_t& x : t.taps) x = take();
     }
     t.q_norm = take();
     t.k_norm = take();

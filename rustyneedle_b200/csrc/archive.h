@@ -48,6 +48,7 @@ struct HadamardIdx { uint32_t d1, d2, b2, d3, d4, w1a, w1b, w2a, w2b, w3a, w3b, 
 struct LayerIdx {
   uint32_t norm_in, q, k, v, q_norm, k_norm, gate, out, post_norm, attn_gate, pre_hada;
   bool has_taps = false;
+  uint32_t taps[3]{};  // q, k, v causal convolution gains (when has_taps)
   HadamardIdx hada;
 };
 struct LanesIdx { uint32_t a_pre, a_post, a_res, b_pre, b_post, b_res, phi_pre, phi_post, phi_res; };

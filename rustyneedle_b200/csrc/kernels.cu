@@ -646,6 +646,8 @@ struct HeadPre {
   float g0, g1;
   float2 sc;
   uint8_t* page;
+  const float* taps;  // the layer's convolution gains (null without taps)
+  int layer;
 };
 __device__ __forceinline__ HeadPre head_prefetch(const ModelDev& md, const LayerDev& L, const KvDev& kv, const TokenMeta& meta, int layer,
                                                  int kind) {
@@ -656,7 +658,34 @@ __device__ __forceinline__ HeadPre head_prefetch(const ModelDev& md, const Layer
   p.g1 = gain[lane + 32];
   p.sc = md.rotary[(size_t)meta.position * (HEAD_DIM / 2) + lane];
   p.page = kind == 0 ? nullptr : page_base(kv, md.page, meta.slot, layer, meta.position);
+  p.taps = L.taps;
+  p.layer = layer;
   return p;
+}
+
+// QKV causal convolution of one projection column (model/src/attention.rs:83-93
+// for a single token, 243-276 for a chunk): Σ over tap < min(taps, position + 1)
+// of gain[tap] · raw[position - tap], from +0.0 in tap order. The raw value of
+// an earlier position is this pass's row `tap` places up when that row holds
+// the same sequence (a pass keeps each sequence's tokens contiguous and in
+// order), else the ring row an earlier pass left.
+__device__ __forceinline__ float conv_column(const ModelDev& md, const Work& w, const float* taps, int layer, int t,
+                                             const TokenMeta& meta, int col) {
+  const int qkvg = (2 * md.heads + 2 * md.kv_heads) * HEAD_DIM, width = (int)md.qkv_width, R = (int)md.conv_taps - 1;
+  const int n = min((int)md.conv_taps, meta.position + 1);
+  float acc = 0.0f;
+  for (int tap = 0; tap < n; ++tap) {
+    const int p = meta.position - tap;
+    bool here = tap == 0;
+    if (!here && t - tap >= 0) {
+      const TokenMeta o = load_meta(w.meta, t - tap);
+      here = o.slot == meta.slot && o.position == p;
+    }
+    const float x = here ? __ldcg(w.proj + (size_t)(t - tap) * qkvg + col)
+                         : __ldcg(md.conv_ring + (((size_t)meta.slot * md.num_layers + layer) * R + p % R) * width + col);
+    acc = fadd(acc, fmul(__ldg(taps + (size_t)tap * width + col), x));
+  }
+  return acc;
 }
 
 __device__ __forceinline__ float head_codes(const ModelDev& md, const Work& w, int t, const TokenMeta& meta, int kind, int head,
@@ -664,9 +693,16 @@ __device__ __forceinline__ float head_codes(const ModelDev& md, const Work& w, i
   const int lane = threadIdx.x & 31;
   const int H = md.heads, KV = md.kv_heads;
   // proj rows: q [H*64] | k [KV*64] | v [KV*64] | gate [H*64]
-  const float* src = w.proj + (size_t)t * (2 * H + 2 * KV) * HEAD_DIM + (kind == 0 ? 0 : (kind == 1 ? H * HEAD_DIM : (H + KV) * HEAD_DIM)) +
-                     head * HEAD_DIM;
-  float e0 = src[lane], e1 = src[lane + 32];
+  const int col = (kind == 0 ? 0 : (kind == 1 ? H * HEAD_DIM : (H + KV) * HEAD_DIM)) + head * HEAD_DIM + lane;
+  const float* src = w.proj + (size_t)t * (2 * H + 2 * KV) * HEAD_DIM + col;
+  float e0, e1;
+  if (pre.taps) {
+    e0 = conv_column(md, w, pre.taps, pre.layer, t, meta, col);
+    e1 = conv_column(md, w, pre.taps, pre.layer, t, meta, col + 32);
+  } else {
+    e0 = src[0];
+    e1 = src[32];
+  }
   const float g0 = pre.g0, g1 = pre.g1;
   const float2 sc = pre.sc;
   uint8_t* page = pre.page;
@@ -1398,10 +1434,28 @@ __device__ __forceinline__ void hadamard_core(const ModelDev& md, const Hadamard
 // False when the token is not live: the CTA has then waited for its copies
 // and returns. FACTORS Kronecker factor pairs are copied (k-th at
 // s_left + k·LEFT², s_right + k·32²).
+// With QKV convolution taps, the block finish also keeps the ring (the
+// attention's head step, launches earlier, has read it): each of the last
+// taps - 1 tokens of a sequence in this pass stores its raw q | k | v row at
+// ring row position % (taps - 1). `part` of `parts` CTAs of the token copies
+// its share.
+__device__ __forceinline__ void conv_ring_store(const ModelDev& md, const LayerDev& L, const Work& w, int M, int t, int part, int parts) {
+  const int R = (int)md.conv_taps - 1, width = (int)md.qkv_width;
+  const TokenMeta meta = load_meta(w.meta, t);
+  if (t + R < M) {
+    const TokenMeta o = load_meta(w.meta, t + R);
+    if (o.slot == meta.slot && o.position == meta.position + R) return;  // a later token of the pass holds this ring row
+  }
+  const float* src = w.proj + (size_t)t * (2 * md.heads + 2 * md.kv_heads) * HEAD_DIM;
+  float* dst = md.conv_ring + (((size_t)meta.slot * md.num_layers + L.index) * R + meta.position % R) * width;
+  const int share = width / parts;
+  for (int i = part * share + (int)threadIdx.x; i < (part + 1) * share; i += blockDim.x) dst[i] = __ldcg(src + i);
+}
+
 template <int LEFT, int FACTORS>
-__device__ __forceinline__ bool block_front(const LayerDev& L, const Work& w, int M, int t, int d, int* error, float* s_a, float* s_x,
-                                            float* s_pre, float* s_condv, float* s_left, float* s_right, float* s_gpost,
-                                            float* s_gpre) {
+__device__ __forceinline__ bool block_front(const ModelDev& md, const LayerDev& L, const Work& w, int M, int t, int d, int* error,
+                                            float* s_a, float* s_x, float* s_pre, float* s_condv, float* s_left, float* s_right,
+                                            float* s_gpost, float* s_gpre, int part, int parts) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   __shared__ float s_inv, s_gate;
   __shared__ __align__(8) uint64_t s_bar;
@@ -1428,6 +1482,7 @@ __device__ __forceinline__ bool block_front(const LayerDev& L, const Work& w, in
     return false;
   }
   stage_async(s_a, w.outp + (size_t)t * d, d);
+  if (md.conv_ring) conv_ring_store(md, L, w, M, t, part, parts);
   cp_async_wait_all();
   // the staged rows, the gate and the barrier's initialisation are visible to
   // every thread past this point; then each thread waits for the bulk copies
@@ -1500,7 +1555,7 @@ __global__ void __launch_bounds__(BLOCK_THREADS) k_block(ModelDev md, LayerDev L
 #pragma unroll
     for (int s = 0; s < LANES; ++s) sv[s] = __ldcg(reinterpret_cast<const float4*>(stream + s * d) + i4);
   }
-  if (!block_front<LEFT, 3>(L, w, M, t, d, error, s_a, s_x, s_pre, s_condv, s_left, s_right, s_gpost, s_gpre)) return;
+  if (!block_front<LEFT, 3>(md, L, w, M, t, d, error, s_a, s_x, s_pre, s_condv, s_left, s_right, s_gpost, s_gpre, 0, 1)) return;
   __syncthreads();
   hadamard_core<LEFT, true>(md, Hd, d, s_pre, buf0, buf1, s_mod, s_left, s_right, s_condv);
   pdl_trigger();  // the lane combine overlaps the next kernel's prologue
@@ -1600,7 +1655,7 @@ __global__ void __launch_bounds__(BLOCK_THREADS) k_block_split(ModelDev md, Laye
 #pragma unroll
     for (int s = 0; s < LANES; ++s) sv[s] = __ldcg(w.stream + ((size_t)t * LANES + s) * d + ei);
   }
-  if (!block_front<LEFT, 1>(L, w, M, t, d, error, s_a, s_x, s_pre, s_condv, s_left, s_right, s_gpost, s_gpre)) return;
+  if (!block_front<LEFT, 1>(md, L, w, M, t, d, error, s_a, s_x, s_pre, s_condv, s_left, s_right, s_gpost, s_gpre, q, CL)) return;
   cluster_arrive_relaxed();  // paired with the wait before the first remote store
   __syncthreads();
   hada_prepare<LEFT>(Hd, d, s_pre, xa, s_mod, s_condv);

@@ -17,6 +17,12 @@
 //   values  [kv][16 blocks][head_dim][4 positions] int8  (the reference's
 //           4-position value panels, model/src/attention.rs:54-69)
 //   kscale  [kv][64] f32, vscale [kv][64] f32
+//
+// QKV causal convolution (models with qkv_conv_taps > 0): each layer's gains
+// are [tap][q | k | v] (tap 0 = the current position), and the ring
+// conv_ring[slot][layer][taps - 1][q | k | v] keeps a sequence's raw
+// (pre-convolution) projections of its last taps - 1 positions, row
+// position % (taps - 1).
 #pragma once
 
 #include <stddef.h>
@@ -98,6 +104,8 @@ struct LayerDev {
   float attn_gate;
   HadamardDev hada;
   int global;  // 1 when the layer attends to the whole context
+  int index;   // the layer's index in the archive
+  const float* taps;  // [conv_taps][q | k | v] causal convolution gains; null without taps
 };
 
 struct ModelDev {
@@ -121,6 +129,9 @@ struct ModelDev {
   const float2* rotary;       // [max_seq_len][head_dim/2] (sin, cos)
   PageGeometry page;
   int* error;                 // the engine's device flag: set when a bounded device wait gave up
+  uint32_t conv_taps;         // QKV causal convolution taps (0 = none)
+  uint32_t qkv_width;         // (heads + 2 kv_heads) * head_dim: the convolved part of a projection row
+  float* conv_ring;           // [slots][layers][conv_taps - 1][qkv_width]; null when conv_taps < 2
 };
 
 // Per-token metadata of one forward pass.

@@ -188,6 +188,7 @@ struct Engine {
   std::vector<uint32_t> free_slots;
   std::vector<uint8_t> slot_dirty;
   float* d_hidden = nullptr;  // [slots][d]
+  size_t conv_ring_floats = 0;  // per slot: md.conv_ring's [layers][taps - 1][q | k | v]
   // forward workspace
   uint32_t capacity = 0;
   Work work{};
@@ -371,7 +372,7 @@ std::shared_ptr<Engine> open_engine(const char* path, const nb_options* opt) {
   nba::Layout lay = a.resolve();
   a.validate_tokenizer(lay.tokenizer);
   const nba::Geometry& g = a.geometry();
-  if (g.qkv_conv_taps > 0) fail(NB_ERR_UNSUPPORTED, "qkv conv taps are not implemented by this build");
+  if (g.qkv_conv_taps > 64) fail(NB_ERR_UNSUPPORTED, "more than 64 qkv conv taps are not implemented");
   if (!g.engram_sites.empty()) fail(NB_ERR_UNSUPPORTED, "engram sites are not implemented by this build");
   if (g.mhc_lanes != LANES) fail(NB_ERR_UNSUPPORTED, "only 4-lane models are implemented");
   if (g.qk_head_dim != HEAD_DIM || g.v_head_dim != HEAD_DIM) fail(NB_ERR_UNSUPPORTED, "head dims other than 64 are not implemented");
@@ -424,6 +425,8 @@ std::shared_ptr<Engine> open_engine(const char* path, const nb_options* opt) {
   md.max_seq_len = g.max_seq_len;
   md.num_layers = L;
   md.sliding_window = g.sliding_window;
+  md.conv_taps = g.qkv_conv_taps;
+  md.qkv_width = (H + 2 * KV) * HEAD_DIM;
   md.sqrt_d = std::sqrt((float)d);
   md.inv_sqrt_group = 1.0f / std::sqrt((float)GROUP);
   md.inv_root_qk = 1.0f / std::sqrt((float)HEAD_DIM);
@@ -553,6 +556,21 @@ std::shared_ptr<Engine> open_engine(const char* path, const nb_options* opt) {
     HD.cond_v = A.upload(cv, st);
     HD.cond_u = A.upload(cu, st);
     D.global = (g.sliding_window == 0 || g.is_global_layer(l)) ? 1 : 0;
+    D.index = (int)l;
+    if (t.has_taps) {
+      // model/src/attention.rs:30: the q, k and v gains, [tap][width] each,
+      // interleaved into [tap][q | k | v] to match a projection row
+      const uint32_t widths[3] = {H * HEAD_DIM, KV * HEAD_DIM, KV * HEAD_DIM}, T = g.qkv_conv_taps;
+      std::vector<float> taps((size_t)T * md.qkv_width);
+      uint32_t at = 0;
+      for (int i = 0; i < 3; ++i) {
+        std::vector<float> gains = floats_of(a, t.taps[i], (size_t)T * widths[i], "conv taps");
+        for (uint32_t k = 0; k < T; ++k)
+          std::copy(gains.begin() + (size_t)k * widths[i], gains.begin() + (size_t)(k + 1) * widths[i], taps.begin() + (size_t)k * md.qkv_width + at);
+        at += widths[i];
+      }
+      D.taps = A.upload(taps, st);
+    }
     E->layers.push_back(D);
   }
 
@@ -577,6 +595,11 @@ std::shared_ptr<Engine> open_engine(const char* path, const nb_options* opt) {
   for (uint32_t s = E->max_sessions; s-- > 0;) E->free_slots.push_back(s);
   E->d_hidden = A.alloc<float>((size_t)E->max_sessions * d);
   NB_CUDA(cudaMemsetAsync(E->d_hidden, 0, (size_t)E->max_sessions * d * 4, st));
+  if (g.qkv_conv_taps > 1) {
+    E->conv_ring_floats = (size_t)L * (g.qkv_conv_taps - 1) * md.qkv_width;  // per slot
+    md.conv_ring = A.alloc<float>(E->max_sessions * E->conv_ring_floats);
+    NB_CUDA(cudaMemsetAsync(md.conv_ring, 0, E->max_sessions * E->conv_ring_floats * 4, st));
+  }
 
   E->capacity = std::max<uint32_t>(opt && opt->max_batch_tokens ? opt->max_batch_tokens : 1024, E->max_sessions);
   const uint32_t M = E->capacity, AW = H * HEAD_DIM, actw = std::max(d, AW);
@@ -839,6 +862,9 @@ nb_status nb_session_clone(const nb_session* session, nb_session** out) {
     E.slot_dirty[s->slot] = 1;
     NB_CUDA(cudaMemcpyAsync(E.d_hidden + (size_t)s->slot * E.md.d_model, E.d_hidden + (size_t)session->slot * E.md.d_model,
                             E.md.d_model * 4, cudaMemcpyDeviceToDevice, E.stream));
+    if (E.conv_ring_floats)  // the convolution history is part of the session (attention.rs:45, AttentionCache is Clone)
+      NB_CUDA(cudaMemcpyAsync(E.md.conv_ring + s->slot * E.conv_ring_floats, E.md.conv_ring + session->slot * E.conv_ring_floats,
+                              E.conv_ring_floats * 4, cudaMemcpyDeviceToDevice, E.stream));
     *out = s;
   });
 }

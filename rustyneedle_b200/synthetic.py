@@ -6,7 +6,7 @@ reference's own (a 196-byte header of 48 u32 fields and an f32 rope_theta, the
 28-value codebook, 44-byte tensor records, 64-byte aligned blobs; see
 crates/cact/src/geometry.rs:41-115, record.rs:38-51, docs/format.md), and the
 tensors follow the canonical positional order of crates/cact/src/layout.rs:190-230:
-embedding; per layer norm_in, q, k, v, q_norm, k_norm, gate_proj, out_proj,
+embedding; per layer norm_in, q, k, v, [q, k, v conv taps], q_norm, k_norm, gate_proj, out_proj,
 post_norm, attn_gate, pre_hada and 13 Hadamard tensors; nine lane tensors; two
 Hadamard permutations; final_norm; the tokenizer blob.
 
@@ -63,6 +63,10 @@ class Geometry:
     embedding_bits: int = 4
     phi_bits: int = 4
     rank: int = 8
+    # optional Needle-3 features (0 = absent; the defaults write none of them)
+    sliding_window: int = 0   # window of the non-global layers
+    global_layers: int = 0    # bit l set: layer l attends to the whole context
+    conv_taps: int = 0        # causal convolution taps on q, k and v
     extra: dict = field(default_factory=dict)
 
 
@@ -183,6 +187,15 @@ def write_archive(path: str, seed: int = 0, geometry: Geometry | None = None) ->
         w.codebook_matrix(rng, H * hd, d, g.projection_bits, g.group)  # q
         w.codebook_matrix(rng, KV * hd, d, g.projection_bits, g.group)  # k
         w.codebook_matrix(rng, KV * hd, d, g.projection_bits, g.group)  # v
+        if g.conv_taps > 0:  # q, k, v taps [tap][width]: tap 0 near 1, older taps smaller
+            for width in (H * hd, KV * hd, KV * hd):
+                if g.extra.get("identity_taps"):  # tap 0 = 1, the rest 0, drawing nothing
+                    taps = np.zeros((g.conv_taps, width))
+                    taps[0] = 1.0
+                else:
+                    taps = 0.3 * rng.standard_normal((g.conv_taps, width))
+                    taps[0] += 1.0
+                w.single(taps)
         w.single(zeros(hd))  # q_norm
         w.single(zeros(hd))  # k_norm
         w.codebook_matrix(rng, H * hd, d, g.projection_bits, g.group)  # gate_proj
@@ -216,7 +229,8 @@ def write_archive(path: str, seed: int = 0, geometry: Geometry | None = None) ->
     w.add(KIND_RAW, (0,), tokenizer_blob(g.vocab))
 
     header = [FORMAT_TAG, len(w.records), codebook.size, 0, 8, g.vocab, g.out_vocab, d, H, KV, L, hd, hd,
-              g.max_seq_len, n, lanes, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0] + [0] * 16
+              g.max_seq_len, n, lanes, g.sliding_window, g.global_layers & 0xFFFFFFFF, g.global_layers >> 32, g.conv_taps,
+              0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0] + [0] * 16
     assert len(header) == 48
     w.finish(path, header, g.rope_theta, codebook)
     return path

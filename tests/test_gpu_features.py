@@ -1,0 +1,173 @@
+"""Parity of the archive features the default synthetic geometry leaves out:
+QKV causal convolution taps (model/src/attention.rs:83-117, 243-276) and the
+sliding window with global layers (attention.rs:171-177). The archive is a
+6-layer synthetic model with 3 taps, a 40-position window and layers 0 and 5
+global; every case is bit-exact against the CPU restatement in INT mode."""
+
+import numpy as np
+import pytest
+
+from tests.conftest import prompt_ids
+
+pytestmark = pytest.mark.gpu
+
+WINDOW = 40
+
+
+def _bits_equal(a, b):
+    a, b = np.asarray(a, dtype=np.float32), np.asarray(b, dtype=np.float32)
+    return a.shape == b.shape and np.array_equal(a.view(np.uint32), b.view(np.uint32))
+
+
+def _mismatch(a, b):
+    a, b = np.asarray(a, dtype=np.float32).ravel(), np.asarray(b, dtype=np.float32).ravel()
+    bad = np.nonzero(a.view(np.uint32) != b.view(np.uint32))[0]
+    if bad.size == 0:
+        return "equal"
+    i = bad[0]
+    return f"{bad.size} of {a.size} differ; first at {i}: {a[i]!r} vs {b[i]!r}"
+
+
+def _geometry(taps: int = 3):
+    from rustyneedle_b200 import synthetic
+
+    return synthetic.Geometry(num_layers=6, max_seq_len=512, conv_taps=taps, sliding_window=WINDOW, global_layers=0b100001)
+
+
+@pytest.fixture(scope="module")
+def features_path():
+    from rustyneedle_b200 import synthetic
+
+    return synthetic.cached_archive(seed=7, geometry=_geometry())
+
+
+@pytest.fixture(scope="module")
+def features_model(native_built, features_path):
+    import rustyneedle_b200 as nb
+
+    return nb.Model.open(features_path, max_sessions=96)
+
+
+@pytest.fixture(scope="module")
+def features_oracle(oracle_lib, features_path):
+    return oracle_lib.Model.open(features_path, oracle_lib.MODE_INT, 0)
+
+
+def test_windowed_prefill_matches_hidden_logits_and_cache(features_model, features_oracle, oracle_lib):
+    """One 150-token pass: every position past the first mixes same-pass rows;
+    the windowed layers attend to their last 40 positions only."""
+    import rustyneedle_b200 as nb
+    from rustyneedle_b200 import debug
+
+    ids = prompt_ids(31, 150)
+    s = nb.Session(features_model)
+    s.feed(ids)
+    o = oracle_lib.Session(features_oracle)
+    o.feed(ids)
+    for layer in features_model.active_layers():
+        keys, ks, values, vs = debug.kv(s, layer)
+        okeys, oks, ovalues, ovs = o.cache(layer)
+        assert np.array_equal(keys, okeys) and np.array_equal(values, ovalues), layer
+        assert _bits_equal(ks, oks) and _bits_equal(vs, ovs), layer
+    assert _bits_equal(debug.hidden(s), o.hidden()), _mismatch(debug.hidden(s), o.hidden())
+    assert _bits_equal(s.logits(), o.logits()), _mismatch(s.logits(), o.logits())
+    s.close()
+
+
+def test_ragged_feeds_then_greedy_steps(features_model, features_oracle, oracle_lib):
+    """Feeds of 1, 2, 5, 64, 1 and 3 tokens (the convolution reads across every
+    pass boundary, from the ring), then 12 greedy steps past the window."""
+    import rustyneedle_b200 as nb
+
+    s = nb.Session(features_model)
+    o = oracle_lib.Session(features_oracle)
+    at = 0
+    ids = prompt_ids(32, 76)
+    for n in (1, 2, 5, 64, 1, 3):
+        s.feed(ids[at:at + n])
+        o.feed(ids[at:at + n])
+        at += n
+        assert _bits_equal(s.logits(), o.logits()), (at, _mismatch(s.logits(), o.logits()))
+    for _ in range(12):
+        token = oracle_lib.argmax(o.logits())
+        o.push(token)
+        assert s.step() == token
+    assert _bits_equal(s.logits(), o.logits())
+    s.close()
+
+
+def test_small_passes_split_a_prompt_anywhere(native_built, features_path, features_oracle, oracle_lib):
+    """max_batch_tokens 7: a 90-token prompt runs as 13 passes, so the taps of
+    the first rows of every pass come from the previous pass's ring rows."""
+    import rustyneedle_b200 as nb
+
+    model = nb.Model.open(features_path, max_sessions=4, max_batch_tokens=7)
+    ids = prompt_ids(33, 90)
+    s = nb.Session(model)
+    s.feed(ids)
+    o = oracle_lib.Session(features_oracle)
+    o.feed(ids)
+    assert _bits_equal(s.logits(), o.logits()), _mismatch(s.logits(), o.logits())
+    s.close()
+    model.close()
+
+
+@pytest.mark.parametrize("count", [6, 72])
+def test_batched_decode_with_taps_and_window(features_model, features_oracle, oracle_lib, count):
+    """Batched steps (6 sequences: cluster kernels; 72: one CTA per token), some
+    sequences shorter than the taps, with a clone forked mid-way."""
+    import rustyneedle_b200 as nb
+
+    base = [1, 2, 3, 39, 41, 120]
+    lengths = (base * (count // len(base) + 1))[:count]
+    sessions, oracles = [], []
+    for i, n in enumerate(lengths):
+        ids = prompt_ids(700 + i, n)
+        s = nb.Session(features_model)
+        s.feed(ids)
+        sessions.append(s)
+        o = oracle_lib.Session(features_oracle)
+        o.feed(ids)
+        oracles.append(o)
+    batch = nb.Batch(features_model, sessions)
+    for _ in range(3):
+        got = batch.step()
+        want = []
+        for o in oracles:
+            token = oracle_lib.argmax(o.logits())
+            o.push(token)
+            want.append(token)
+        assert list(got) == want
+    batch.close()
+    # a clone carries the convolution history with it
+    c, oc = sessions[4].clone(), oracles[4].clone()
+    sessions[4].push(17)
+    oracles[4].push(17)
+    c.push(18)
+    oc.push(18)
+    assert _bits_equal(sessions[4].logits(), oracles[4].logits())
+    assert _bits_equal(c.logits(), oc.logits()), _mismatch(c.logits(), oc.logits())
+    for s in sessions + [c]:
+        s.close()
+
+
+@pytest.mark.parametrize("taps", [1, 2])
+def test_short_tap_counts(native_built, oracle_lib, taps):
+    """One tap (no history) and two taps (a one-row ring)."""
+    import rustyneedle_b200 as nb
+    from rustyneedle_b200 import synthetic
+
+    path = synthetic.cached_archive(seed=8, geometry=_geometry(taps))
+    model = nb.Model.open(path, max_sessions=4)
+    omodel = oracle_lib.Model.open(path, oracle_lib.MODE_INT, 0)
+    s = nb.Session(model)
+    o = oracle_lib.Session(omodel)
+    ids = prompt_ids(34, 50)
+    s.feed(ids[:45])
+    o.feed(ids[:45])
+    for t in ids[45:]:
+        s.push(int(t))
+        o.push(int(t))
+    assert _bits_equal(s.logits(), o.logits()), _mismatch(s.logits(), o.logits())
+    s.close()
+    model.close()

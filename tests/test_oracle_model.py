@@ -129,3 +129,47 @@ def test_raw_product_is_the_archive_product(oracle_lib, archive_path):
         got = oracle_lib.product_raw(oracle_lib.MODE_INT, 4, packed, levels, norms, rows, cols, x)
         want, _ = model.matrix_product(0, x)
         assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
+def _features(**kw):
+    from rustyneedle_b200 import synthetic
+
+    return synthetic.Geometry(num_layers=4, max_seq_len=256, **kw)
+
+
+def test_identity_taps_and_an_unreached_window_change_nothing(oracle_lib):
+    """Taps (1, 0, 0) reproduce the model without taps bit for bit, and so does a
+    window longer than the context; a shorter window changes the result."""
+    from rustyneedle_b200 import synthetic
+
+    plain = synthetic.cached_archive(seed=9, geometry=_features())
+    identity = synthetic.cached_archive(seed=9, geometry=_features(conv_taps=3, extra={"identity_taps": True}))
+    windowed = synthetic.cached_archive(seed=9, geometry=_features(sliding_window=64, global_layers=0b0001))
+    ids = prompt_ids(5, 50)
+
+    def logits(path, n):
+        s = oracle_lib.Session(oracle_lib.Model.open(path, oracle_lib.MODE_INT, 0))
+        s.feed(ids[:n])
+        return s.logits()
+
+    assert np.array_equal(logits(plain, 50).view(np.uint32), logits(identity, 50).view(np.uint32))
+    assert np.array_equal(logits(plain, 50).view(np.uint32), logits(windowed, 50).view(np.uint32))
+    ids = prompt_ids(5, 90)
+    assert not np.array_equal(logits(plain, 90), logits(windowed, 90))
+
+
+def test_taps_and_window_prefill_agree_with_stepping(oracle_lib, kats):
+    """The batched convolution (attention.rs:243-276) against the per-token one
+    (attention.rs:83-111), in FLOAT mode: cosine > 0.9995, same argmax."""
+    from rustyneedle_b200 import synthetic
+
+    path = synthetic.cached_archive(seed=10, geometry=_features(conv_taps=3, sliding_window=24, global_layers=0b1000))
+    m = oracle_lib.Model.open(path, oracle_lib.MODE_FLOAT, 0)
+    ids = prompt_ids(6, 60)
+    fed, pushed = oracle_lib.Session(m), oracle_lib.Session(m)
+    fed.feed(ids)
+    for t in ids:
+        pushed.push(int(t))
+    a, b = fed.logits(), pushed.logits()
+    assert _cos(a, b) > kats["prefill_cosine"]
+    assert oracle_lib.argmax(a) == oracle_lib.argmax(b)
