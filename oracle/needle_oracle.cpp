@@ -18,6 +18,7 @@
 #include <omp.h>
 
 #include <algorithm>
+#include <array>
 #include <cfenv>
 #include <cmath>
 #include <cstdio>
@@ -215,6 +216,7 @@ struct Layout {
   LanesT lanes;
   size_t perms[2];
   size_t engram_count = 0;
+  std::vector<std::array<size_t, 4>> engrams;  // tables, key_proj, value_proj, taps per site
   size_t final_norm;
   size_t head_count = 0;
   bool audio = false;
@@ -265,7 +267,9 @@ Layout resolve_layout(const Archive& a) {
   L.perms[0] = take();
   L.perms[1] = take();
   for (size_t s = 0; s < a.geo.engram_sites.size(); ++s) {
-    for (int i = 0; i < 4; ++i) take();
+    std::array<size_t, 4> e;
+    for (size_t& i : e) i = take();
+    L.engrams.push_back(e);
     L.engram_count++;
   }
   L.final_norm = take();
@@ -811,10 +815,17 @@ struct LanesW {
   QMatrix phi_pre, phi_post, phi_res;
 };
 
+// model/src/engram.rs:12-28
+struct EngramW {
+  QMatrix tables, key_proj, value_proj;
+  std::vector<float> taps;  // [conv_taps][d]
+};
+
 struct Weights {
   QMatrix embedding;
   std::vector<LayerW> layers;
   LanesW lanes;
+  std::vector<EngramW> engrams;  // one per engram site
   std::vector<float> final_norm;
   std::vector<size_t> perm1, perm2;
 };
@@ -931,7 +942,9 @@ std::vector<float> hadamard_apply(const Hadamard& h, const float* input, size_t 
 
 std::shared_ptr<Weights> load_weights(const Archive& a, const Layout& L) {
   const Geometry& g = a.geo;
-  if (!g.engram_sites.empty()) throw Failure(ERR_UNSUPPORTED, "engram sites are not restated by this oracle");
+  if (!g.engram_sites.empty() && (g.engram_orders.empty() || g.engram_tables % g.engram_orders.size() != 0 || g.engram_slots == 0))
+    throw Failure(ERR_ARCHIVE, "engram tables are not a multiple of the orders");
+  if (!g.engram_sites.empty() && g.engram_conv_taps == 0) throw Failure(ERR_UNSUPPORTED, "engram sites without value taps");
   if (g.num_heads % std::max<size_t>(g.num_kv_heads, 1) != 0) throw Failure(ERR_ARCHIVE, "query heads are not a multiple of kv heads");
   auto w = std::make_shared<Weights>();
   auto perm = [&](size_t index) {
@@ -979,6 +992,18 @@ std::shared_ptr<Weights> load_weights(const Archive& a, const Layout& L) {
   ln.phi_pre = load_matrix(a, L.lanes.phi_pre);
   ln.phi_post = load_matrix(a, L.lanes.phi_post);
   ln.phi_res = load_matrix(a, L.lanes.phi_res);
+  for (const auto& e : L.engrams) {  // engram.rs:19-28
+    EngramW ew;
+    ew.tables = load_matrix(a, e[0]);
+    ew.key_proj = load_matrix(a, e[1]);
+    ew.value_proj = load_matrix(a, e[2]);
+    ew.taps = floats(a, e[3]);
+    if (ew.tables.rows < g.engram_tables * g.engram_slots || ew.tables.columns != g.engram_sub_dim ||
+        ew.key_proj.columns != g.engram_tables * g.engram_sub_dim || ew.value_proj.columns != ew.key_proj.columns ||
+        ew.key_proj.rows != g.d_model || ew.value_proj.rows != g.d_model || ew.taps.size() < g.engram_conv_taps * g.d_model)
+      throw Failure(ERR_ARCHIVE, "engram tensors do not match the header");
+    w->engrams.push_back(std::move(ew));
+  }
   w->final_norm = floats(a, L.final_norm);
   return w;
 }
@@ -1154,6 +1179,7 @@ struct nbo_session {
   const nbo_model* model;
   std::vector<uint32_t> tokens;
   std::vector<nbo::Cache> caches;
+  std::vector<std::deque<std::vector<float>>> engram_history;  // per site: raw values, newest first (engram.rs:45-48)
   std::vector<float> frequencies;
   std::vector<float> hidden;
 };
@@ -1311,6 +1337,96 @@ void finish_block(const nbo_model* M, const LayerW& W, const Routing& r, std::ve
   combine_into(r, stream, delta.data(), d, lanes, next);
 }
 
+// ---------------------------------------------------------------- engram sites
+// engram.rs:30-46: per (order, head) table a multiplicative hash of the last
+// `order` token ids (0 before the start), xor-shifted, modulo the slots.
+std::vector<size_t> table_indices(const Geometry& g, const std::vector<uint32_t>& tokens, size_t position) {
+  const uint32_t HASH_SEED = 0x9E3779B9u, HASH_PRIME = 0x01000193u;
+  const size_t hpo = g.engram_tables / g.engram_orders.size();
+  const size_t stride = g.engram_seed_heads == 0 ? hpo : g.engram_seed_heads;
+  std::vector<size_t> out;
+  for (size_t oi = 0; oi < g.engram_orders.size(); ++oi)
+    for (size_t head = 0; head < hpo; ++head) {
+      uint32_t acc = HASH_SEED * (uint32_t)(oi * stride + head + 1);
+      for (size_t back = 0; back < g.engram_orders[oi]; ++back) {
+        uint32_t token = position >= back ? tokens[position - back] : 0u;
+        acc = (acc ^ token) * HASH_PRIME;
+      }
+      acc ^= acc >> 15;
+      out.push_back(acc % (uint32_t)g.engram_slots);
+    }
+  return out;
+}
+
+// engram.rs:72-83: table t's row, or zeros while the position is shorter
+// than the table's order, concatenated and fake-quantised.
+std::vector<float> engram_gather(const nbo_model* M, const EngramW& E, const std::vector<size_t>& idx, size_t position) {
+  const Geometry& g = M->archive->geo;
+  const size_t sub = g.engram_sub_dim, hpo = g.engram_tables / g.engram_orders.size();
+  std::vector<float> gathered(g.engram_tables * sub, 0.0f);
+  for (size_t t = 0; t < g.engram_tables; ++t)
+    if (position + 1 >= g.engram_orders[t / hpo]) {
+      std::vector<float> row = E.tables.dequantise_row(t * g.engram_slots + idx[t]);
+      std::copy(row.begin(), row.end(), gathered.begin() + t * sub);
+    }
+  fake_quantise_int8(gathered.data(), gathered.size());
+  return gathered;
+}
+
+// Σ over taps whose reach (tap · dilation) the position covers of
+// gain[tap] · raw[position - tap · dilation], from +0.0 (engram.rs:92-103).
+template <typename Source>
+void engram_conv(const Geometry& g, const EngramW& E, size_t position, size_t width, Source&& raw_at, float* value) {
+  for (size_t i = 0; i < width; ++i) value[i] = 0.0f;
+  for (size_t tap = 0; tap < g.engram_conv_taps; ++tap) {
+    size_t back = tap * g.engram_conv_dilation;
+    if (position < back) continue;
+    const float* past = raw_at(back);
+    const float* gn = &E.taps[tap * width];
+    for (size_t i = 0; i < width; ++i) value[i] += gn[i] * past[i];
+  }
+}
+
+size_t engram_keep(const Geometry& g) { return (g.engram_conv_taps - 1) * g.engram_conv_dilation + 1; }
+
+// EngramSiteState::contribute (engram.rs:68-105) for one token.
+void engram_contribute(const nbo_model* M, size_t site, std::deque<std::vector<float>>& history, const std::vector<size_t>& idx,
+                       size_t position, std::vector<float>& key, std::vector<float>& value) {
+  const Geometry& g = M->archive->geo;
+  const EngramW& E = M->weights->engrams[site];
+  std::vector<float> gathered = engram_gather(M, E, idx, position);
+  std::vector<float> rotated = E.key_proj.prepare(gathered.data());
+  key.assign(E.key_proj.rows, 0.0f);
+  std::vector<float> raw(E.value_proj.rows, 0.0f);
+  std::vector<Job> jobs{{&E.key_proj, 0, key.data(), E.key_proj.rows}, {&E.value_proj, 0, raw.data(), E.value_proj.rows}};
+  multiply_jobs(jobs, rotated.data(), M->mode, M->threads);
+  const size_t width = raw.size();
+  history.push_front(raw);
+  while (history.size() > engram_keep(g)) history.pop_back();
+  value.assign(width, 0.0f);
+  engram_conv(g, E, position, width, [&](size_t back) { return history.at(back).data(); }, value.data());
+}
+
+// session.rs:180-190
+void add_engram(float* x, const float* key, const float* value, size_t width) {
+  std::vector<float> ux(width), uk(width);
+  unit_rms(x, ux.data(), width);
+  unit_rms(key, uk.data(), width);
+  float dot = -0.0f;  // Iterator::sum
+  for (size_t i = 0; i < width; ++i) dot += ux[i] * uk[i];
+  float alpha = sigmoid(dot / std::sqrt((float)width));
+  for (size_t i = 0; i < width; ++i) x[i] += alpha * value[i];
+}
+
+// ModelConfig::engram_site_at (config.rs:87-89): the first site on the layer.
+int engram_site_at(const Geometry& g, size_t layer) {
+  for (size_t i = 0; i < g.engram_sites.size(); ++i)
+    if (g.engram_sites[i] == layer) return (int)i;
+  return -1;
+}
+
+bool layer_active(const nbo_model* M, size_t layer) { return std::find(M->active.begin(), M->active.end(), layer) != M->active.end(); }
+
 std::vector<float> embed(const nbo_model* M, uint32_t token) {
   const Geometry& g = M->archive->geo;
   if (token >= M->weights->embedding.rows) throw Failure(ERR_ARGUMENT, "token id outside the embedding");
@@ -1330,6 +1446,14 @@ void push(nbo_session* s, uint32_t token, float* trace) {
   size_t position = s->tokens.size();
   std::vector<float> stream = embed(M, token);
   s->tokens.push_back(token);
+  // session.rs:93-102: every site on an active layer contributes
+  const size_t sites = g.engram_sites.size();
+  std::vector<std::vector<float>> ekey(sites), evalue(sites);
+  if (sites) {
+    std::vector<size_t> idx = table_indices(g, s->tokens, position);
+    for (size_t i = 0; i < sites; ++i)
+      if (layer_active(M, g.engram_sites[i])) engram_contribute(M, i, s->engram_history[i], idx, position, ekey[i], evalue[i]);
+  }
   std::vector<float> next(stream.size());
   std::vector<float> normed(d);
   for (size_t slot = 0; slot < M->active.size(); ++slot) {
@@ -1337,6 +1461,8 @@ void push(nbo_session* s, uint32_t token, float* trace) {
     const LayerW& W = M->weights->layers[layer];
     Routing r = route(M, layer, slot, stream.data(), d);
     std::vector<float> x = r.input;
+    const int site = engram_site_at(g, layer);
+    if (site >= 0 && !ekey[site].empty()) add_engram(x.data(), ekey[site].data(), evalue[site].data(), d);
     zero_centred_norm(x.data(), W.norm_in.data(), normed.data(), d);
     std::vector<float> attended = attend(M, W, layer, s->caches[layer], s->frequencies.data(), position, normed.data());
     finish_block(M, W, r, x, attended, stream.data(), next.data());
@@ -1366,15 +1492,45 @@ void prefill_float(nbo_session* s, const uint32_t* tokens, size_t count) {
     std::vector<float> e = embed(M, tokens[t]);
     std::memcpy(&stream[t * frame], e.data(), frame * sizeof(float));
   });
+  // EngramSiteState::contribute_batch (engram.rs:112-160) per active site
+  const size_t sites = g.engram_sites.size();
+  std::vector<std::vector<float>> ekeys(sites), evalues(sites);
+  for (size_t i = 0; i < sites; ++i) {
+    if (!layer_active(M, g.engram_sites[i])) continue;
+    const EngramW& E = M->weights->engrams[i];
+    const size_t padded = E.key_proj.padded, kw = E.key_proj.rows, vw = E.value_proj.rows;
+    std::vector<float> rotated(count * padded);
+    fork(M->threads, count, true, [&](size_t t) {
+      std::vector<float> gathered = engram_gather(M, E, table_indices(g, s->tokens, first + t), first + t);
+      std::vector<float> r = E.key_proj.prepare(gathered.data());
+      std::memcpy(&rotated[t * padded], r.data(), padded * sizeof(float));
+    });
+    ekeys[i].assign(count * kw, 0.0f);
+    std::vector<float> raw(count * vw);
+    multiply_batch_float(E.key_proj, rotated.data(), count, ekeys[i].data(), M->threads);
+    multiply_batch_float(E.value_proj, rotated.data(), count, raw.data(), M->threads);
+    const std::deque<std::vector<float>> previous = s->engram_history[i];
+    evalues[i].assign(count * vw, 0.0f);
+    fork(M->threads, count, true, [&](size_t t) {
+      engram_conv(g, E, first + t, vw,
+                  [&](size_t back) { return back <= t ? &raw[(t - back) * vw] : previous.at(back - t - 1).data(); }, &evalues[i][t * vw]);
+    });
+    const size_t keep = engram_keep(g);
+    for (size_t t = count > keep ? count - keep : 0; t < count; ++t)
+      s->engram_history[i].push_front(std::vector<float>(raw.begin() + t * vw, raw.begin() + (t + 1) * vw));
+    while (s->engram_history[i].size() > keep) s->engram_history[i].pop_back();
+  }
   for (size_t slot = 0; slot < M->active.size(); ++slot) {
     size_t layer = M->active[slot];
     const LayerW& W = M->weights->layers[layer];
     Cache& cache = s->caches[layer];
     std::vector<Routing> routings(count);
     std::vector<float> x(count * d), normed(count * d);
+    const int site = engram_site_at(g, layer);
     fork(M->threads, count, true, [&](size_t t) {
       routings[t] = route(M, layer, slot, &stream[t * frame], d);
       std::memcpy(&x[t * d], routings[t].input.data(), d * sizeof(float));
+      if (site >= 0 && !ekeys[site].empty()) add_engram(&x[t * d], &ekeys[site][t * d], &evalues[site][t * d], d);
       zero_centred_norm(&x[t * d], W.norm_in.data(), &normed[t * d], d);
     });
     // attend_batch: fake-quantise, rotate and multiply every token at once.
@@ -1561,6 +1717,7 @@ nbo_session* nbo_session_new(const nbo_model* model) {
   auto* s = new nbo_session();
   s->model = model;
   s->caches.resize(model->archive->geo.num_layers);
+  s->engram_history.resize(model->archive->geo.engram_sites.size());
   s->frequencies = rotary_frequencies(model->archive->geo.qk_head_dim, model->archive->geo.rope_theta);
   return s;
 }

@@ -215,7 +215,9 @@ Layout Archive::resolve() const {
   L.perms[0] = take();
   L.perms[1] = take();
   for (size_t s = 0; s < geo_.engram_sites.size(); ++s) {
-    for (int i = 0; i < 4; ++i) take();
+    std::array<uint32_t, 4> e;
+    for (uint32_t& i : e) i = take();
+    L.engrams.push_back(e);
     L.engram_sites++;
   }
   L.final_norm = take();

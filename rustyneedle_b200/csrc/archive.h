@@ -7,6 +7,7 @@
 
 #include <cstdint>
 #include <string>
+#include <array>
 #include <vector>
 
 namespace nba {
@@ -59,6 +60,7 @@ struct Layout {
   LanesIdx lanes{};
   uint32_t perms[2]{};
   uint32_t engram_sites = 0;
+  std::vector<std::array<uint32_t, 4>> engrams;  // per site: tables, key_proj, value_proj, taps
   uint32_t final_norm = 0;
   uint32_t probe_heads = 0;
   bool audio = false;

@@ -88,6 +88,140 @@ __global__ void __launch_bounds__(128) k_embed(ModelDev md, Work w, int M) {
   }
 }
 
+// -------------------------------------------------------------- engram sites
+// The token id at `position` of row t's sequence: this pass's row when the
+// pass holds it (a pass keeps each sequence's tokens contiguous and in
+// order), else the sequence's token ring.
+__device__ __forceinline__ uint32_t token_at(const ModelDev& md, const Work& w, int t, const TokenMeta& meta, int position) {
+  const int back = meta.position - position;
+  if (back == 0) return __ldcg(w.tokens + t);
+  if (t - back >= 0) {
+    const TokenMeta o = load_meta(w.meta, t - back);
+    if (o.slot == meta.slot && o.position == position) return __ldcg(w.tokens + t - back);
+  }
+  return __ldcg(md.token_ring + (size_t)meta.slot * md.token_rows + position % md.token_rows);
+}
+
+// grid M, block 128. A site's gathered table rows for token t (engram.rs:30-46,
+// 68-83): table i hashes the last order(i) token ids (0 before the start),
+// xor-shifts and takes the slot modulo; its row is dequantised like the
+// embedding (level · norm, the normalised Walsh transform per 128-group,
+// matrix.rs:140-153), or zeros while the position is shorter than the order.
+// Then fake_quantise_int8 over the whole vector and the product's per-group
+// rotation and int8 codes (QuantisedMatrix::prepare); groups past
+// tables · sub_dim up to the padded K stay zero.
+constexpr int ENGRAM_MAX_K = 2048, ENGRAM_MAX_TABLES = 16, ENGRAM_MAX_TAPS = 16;
+__global__ void __launch_bounds__(128) k_engram_gather(ModelDev md, EngramDev E, Work w, int M) {
+  __shared__ __align__(16) float s_g[ENGRAM_MAX_K];
+  __shared__ uint32_t s_row[ENGRAM_MAX_TABLES];
+  __shared__ float s_red[4];
+  const int t = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  pdl_wait();
+  if (t >= M) return;
+  const TokenMeta meta = load_meta(w.meta, t);
+  if (meta.slot < 0) return;
+  const int tables = (int)md.engram_tables, sub = (int)md.engram_sub_dim, K = tables * sub, gpt = sub / GROUP;
+  if (tid < tables) {
+    const int oi = tid / (int)md.engram_heads_per_order, head = tid % (int)md.engram_heads_per_order, order = (int)md.engram_order[oi];
+    uint32_t acc = 0x9E3779B9u * (uint32_t)(oi * (int)md.engram_stride + head + 1);
+    for (int back = 0; back < order; ++back) {
+      const uint32_t token = meta.position >= back ? token_at(md, w, t, meta, meta.position - back) : 0u;
+      acc = (acc ^ token) * 0x01000193u;
+    }
+    acc ^= acc >> 15;
+    s_row[tid] = meta.position + 1 >= order ? (uint32_t)tid * md.engram_slots + acc % md.engram_slots : 0xffffffffu;
+  }
+  __syncthreads();
+  float peak = 0.0f;
+  for (int pair = warp; pair < tables * gpt; pair += 4) {
+    const int tb = pair / gpt, g = pair % gpt;
+    const uint32_t row = s_row[tb];
+    float v[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    if (row != 0xffffffffu) {
+      const uint8_t* codes = E.packed + (size_t)row * E.row_bytes;
+      const float norm = E.norms[(size_t)row * gpt + g];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) v[j] = fmul(E.levels[code_at(codes, g * GROUP + 4 * lane + j, E.bits)], norm);
+      fwht128(v, md.inv_sqrt_group);
+    }
+    *reinterpret_cast<float4*>(s_g + tb * sub + g * GROUP + 4 * lane) = make_float4(v[0], v[1], v[2], v[3]);
+    peak = fmaxf(peak, fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3]))));
+  }
+  peak = warp_max(peak);
+  if (lane == 0) s_red[warp] = peak;
+  __syncthreads();
+  const float scale = int8_scale_of(fmaxf(fmaxf(s_red[0], s_red[1]), fmaxf(s_red[2], s_red[3])));
+  pdl_trigger();
+  const int groups = (int)md.engram_k / GROUP;
+  for (int g = warp; g < groups; g += 4) {
+    uint32_t packed = 0;
+    float sc = 0.0f;
+    if (g * GROUP < K) {
+      const float4 x = reinterpret_cast<const float4*>(s_g + g * GROUP)[lane];
+      float v[4] = {fake_quant(x.x, scale), fake_quant(x.y, scale), fake_quant(x.z, scale), fake_quant(x.w, scale)};
+      fwht128(v, md.inv_sqrt_group);
+      sc = quantise_group(v, packed);
+    }
+    *reinterpret_cast<uint32_t*>(w.act + chunked_offset(t, g * GROUP + 4 * lane, w.act_rows)) = packed;
+    if (lane == 0) w.act_scale[(size_t)t * groups + g] = sc;
+  }
+}
+
+// At an engram site layer, k_route's x (the routing input, s_x) takes the
+// site's term (session.rs:180-190): alpha = sigmoid(Σ unit_rms(x)·unit_rms(key)
+// / sqrt(d)), the dot an ordered sum from -0.0, then x += alpha · value, the
+// value the dilated causal convolution of the raw values (engram.rs:92-103,
+// 146-159: this pass's rows, else the site's ring). Threads 0..nthreads-1 of
+// the CTA; s_key and s_prod are d floats of free shared memory.
+__device__ __forceinline__ void engram_add(const ModelDev& md, const EngramDev& E, const Work& w, int t, int nthreads, float* s_x,
+                                           float* s_key, float* s_prod, float* xg) {
+  __shared__ float s_e[2];
+  __shared__ const float* s_src[ENGRAM_MAX_TAPS];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, d = (int)md.d_model;
+  const TokenMeta meta = load_meta(w.meta, t);
+  const float* kv = w.engram_kv + (size_t)t * 2 * d;
+  for (int i = tid; i < d; i += nthreads) s_key[i] = __ldcg(kv + i);
+  if (tid < (int)md.engram_conv_taps) {  // each tap's raw value row (null: the position is too short)
+    const int back = tid * (int)md.engram_dilation, R = (int)md.engram_ring_rows;
+    const float* src = nullptr;
+    if (meta.position >= back) {
+      bool here = back == 0;
+      if (!here && t - back >= 0) {
+        const TokenMeta o = load_meta(w.meta, t - back);
+        here = o.slot == meta.slot && o.position == meta.position - back;
+      }
+      src = here ? w.engram_kv + (size_t)(t - back) * 2 * d + d : E.ring + ((size_t)meta.slot * R + (meta.position - back) % R) * d;
+    }
+    s_src[tid] = src;
+  }
+  named_barrier(1, nthreads);
+  if (warp < 2) {
+    const float ss = sum_of_squares_warp(warp == 0 ? s_x : s_key, d);
+    if (lane == 0) s_e[warp] = inverse_rms(ss, d);
+  }
+  named_barrier(1, nthreads);
+  const float inv_x = s_e[0], inv_k = s_e[1];
+  for (int i = tid; i < d; i += nthreads) s_prod[i] = fmul(fmul(s_x[i], inv_x), fmul(s_key[i], inv_k));
+  named_barrier(1, nthreads);
+  if (tid == 0) {
+    float dot = SUM_START;
+    for (int i = 0; i < d; ++i) dot = fadd(dot, s_prod[i]);
+    s_e[0] = sigmoid(fdiv(dot, md.sqrt_d));
+  }
+  named_barrier(1, nthreads);
+  const float alpha = s_e[0];
+  for (int i = tid; i < d; i += nthreads) {
+    float value = 0.0f;
+    for (int tap = 0; tap < (int)md.engram_conv_taps; ++tap) {
+      const float* src = s_src[tap];
+      if (src) value = fadd(value, fmul(__ldg(E.taps + (size_t)tap * d + i), __ldcg(src + i)));
+    }
+    const float x = fadd(s_x[i], fmul(alpha, value));
+    s_x[i] = x;
+    xg[i] = x;
+  }
+}
+
 // ------------------------------------------------------------------- routing
 // grid M, block 256 (8 warps). Warp 7 finishes the Sinkhorn mixing weights
 // while warps 0-6 build the block input, norm it and quantise it. Every
@@ -322,14 +456,20 @@ __global__ void __launch_bounds__(256) k_route(ModelDev md, LayerDev L, Work w, 
   named_barrier(1, nthreads);
   float* s_x = s_work;  // the block input x (lanes.rs:169-171)
   float* xg = w.x + (size_t)t * d;
+  const bool engram = L.engram_site >= 0;
+  float* xin = engram ? w.xin + (size_t)t * d : xg;  // the routing input; x adds the engram term to it
   for (int i = tid; i < d; i += nthreads) {
     float acc = 0.0f;
 #pragma unroll
     for (int l = 0; l < LANES; ++l) acc = fadd(acc, fmul(s_gate[l], s_stream[l * d + i]));
     s_x[i] = acc;
-    xg[i] = acc;
+    xin[i] = acc;
   }
   named_barrier(1, nthreads);
+  if (engram) {
+    engram_add(md, L.engram, w, t, nthreads, s_x, s_stream, s_stream + d, xg);  // the lanes are no longer needed
+    named_barrier(1, nthreads);
+  }
   if (warp == 0) {
     float ss = sum_of_squares_warp(s_x, d);
     if (lane == 0) s_inv = inverse_rms(ss, d);
@@ -1452,6 +1592,22 @@ __device__ __forceinline__ void conv_ring_store(const ModelDev& md, const LayerD
   for (int i = part * share + (int)threadIdx.x; i < (part + 1) * share; i += blockDim.x) dst[i] = __ldcg(src + i);
 }
 
+// At an engram site layer the last (taps - 1) · dilation tokens of a sequence
+// in this pass store their raw values in the site's ring (k_route, launches
+// earlier, has read it).
+__device__ __forceinline__ void engram_ring_store(const ModelDev& md, const EngramDev& E, const Work& w, int M, int t, int part, int parts) {
+  const int R = (int)md.engram_ring_rows, d = (int)md.d_model;
+  const TokenMeta meta = load_meta(w.meta, t);
+  if (t + R < M) {
+    const TokenMeta o = load_meta(w.meta, t + R);
+    if (o.slot == meta.slot && o.position == meta.position + R) return;
+  }
+  const float* src = w.engram_kv + (size_t)t * 2 * d + d;
+  float* dst = E.ring + ((size_t)meta.slot * R + meta.position % R) * d;
+  const int share = d / parts;
+  for (int i = part * share + (int)threadIdx.x; i < (part + 1) * share; i += blockDim.x) dst[i] = __ldcg(src + i);
+}
+
 template <int LEFT, int FACTORS>
 __device__ __forceinline__ bool block_front(const ModelDev& md, const LayerDev& L, const Work& w, int M, int t, int d, int* error,
                                             float* s_a, float* s_x, float* s_pre, float* s_condv, float* s_left, float* s_right,
@@ -1483,6 +1639,7 @@ __device__ __forceinline__ bool block_front(const ModelDev& md, const LayerDev& 
   }
   stage_async(s_a, w.outp + (size_t)t * d, d);
   if (md.conv_ring) conv_ring_store(md, L, w, M, t, part, parts);
+  if (L.engram_site >= 0 && L.engram.ring) engram_ring_store(md, L.engram, w, M, t, part, parts);
   cp_async_wait_all();
   // the staged rows, the gate and the barrier's initialisation are visible to
   // every thread past this point; then each thread waits for the bulk copies
@@ -1561,11 +1718,13 @@ __global__ void __launch_bounds__(BLOCK_THREADS) k_block(ModelDev md, LayerDev L
   pdl_trigger();  // the lane combine overlaps the next kernel's prologue
   if (i4 < d / 4) {
     const float dv[4] = {d4.x, d4.y, d4.z, d4.w};
+    // delta = x - routing input (lanes.rs:100-104); at an engram site x started from input + engram term
+    const float* xin = L.engram_site >= 0 ? w.xin + (size_t)t * d : nullptr;
     float delta[4];
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
       int i = 4 * i4 + e;
-      delta[e] = fsub(fadd(s_a[i], fmul(buf0[i], dv[e])), s_x[i]);
+      delta[e] = fsub(fadd(s_a[i], fmul(buf0[i], dv[e])), xin ? __ldcg(xin + i) : s_x[i]);
     }
 #pragma unroll
     for (int l = 0; l < LANES; ++l) {
@@ -1699,7 +1858,8 @@ __global__ void __launch_bounds__(BLOCK_THREADS) k_block_split(ModelDev md, Laye
   __syncthreads();
   pdl_trigger();  // the lane combine overlaps the next kernel's prologue
   if (tid < own) {
-    const float delta = fsub(fadd(s_a[ei], fmul(xb[ei], d4)), s_x[ei]);
+    const float input = L.engram_site >= 0 ? __ldcg(w.xin + (size_t)t * d + ei) : s_x[ei];
+    const float delta = fsub(fadd(s_a[ei], fmul(xb[ei], d4)), input);
     float* next = w.next_stream + (size_t)t * LANES * d;
 #pragma unroll
     for (int l = 0; l < LANES; ++l) next[l * d + ei] = lane_out(rw, sv, l, delta);
@@ -1716,7 +1876,18 @@ __global__ void __launch_bounds__(128) k_final(ModelDev md, Work w, float* __res
   const int t = blockIdx.x;
   if (t >= M) return;
   const TokenMeta meta = w.meta[t];
-  if (meta.slot < 0 || !meta.last) return;
+  if (meta.slot < 0) return;
+  if (md.token_ring && threadIdx.x == 0) {
+    // the last token_rows token ids of each sequence in the pass join its token ring
+    const int R = (int)md.token_rows;
+    bool newest = true;
+    if (t + R < M) {
+      const TokenMeta o = w.meta[t + R];
+      newest = !(o.slot == meta.slot && o.position == meta.position + R);
+    }
+    if (newest) md.token_ring[(size_t)meta.slot * R + meta.position % R] = w.tokens[t];
+  }
+  if (!meta.last) return;
   const int d = md.d_model, tid = threadIdx.x;
   const float* stream = w.stream + (size_t)t * LANES * d;
   for (int i4 = tid; i4 < d / 4; i4 += blockDim.x) {
@@ -2023,6 +2194,10 @@ void launch_layer(const ModelDev& md, const LayerDev& L, const Work& w, const Kv
   t_pass_tokens = M;
   const int d = md.d_model, H = md.heads, KV = md.kv_heads;
   const int proj_stride = (2 * H + 2 * KV) * HEAD_DIM;
+  if (L.engram_site >= 0) {  // the site's key and raw value rows (engram.rs:84-90)
+    launch(k_engram_gather, M, 128, 0, st, md, L.engram, w, M);
+    project(L.engram.kv, w.act, w.act_scale, w.engram_kv, M, 2 * d, w.meta, st, md.error, (int)w.act_rows);
+  }
   launch(k_route, M, 256, route_smem(md), st, md, L, w, M, layer, slot, md.error);
   project(L.qkvg, w.act, w.act_scale, w.proj, M, proj_stride, w.meta, st, md.error);
   // the head step runs inside the attention when each token of the pass

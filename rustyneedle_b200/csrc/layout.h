@@ -23,6 +23,14 @@
 // conv_ring[slot][layer][taps - 1][q | k | v] keeps a sequence's raw
 // (pre-convolution) projections of its last taps - 1 positions, row
 // position % (taps - 1).
+//
+// Engram sites (models/src/engram.rs): per site the hashed tables (packed
+// code rows, dequantised on gather like the embedding), key_proj and
+// value_proj stacked into one 2d-row product whose K (tables · sub_dim) is
+// zero-padded to 512 or 2048, and the value convolution gains. A sequence's
+// raw values of its last (taps - 1) · dilation positions sit in the site's
+// ring [slots][rows][d] at row position % rows; its last (max order - 1)
+// token ids in token_ring[slots][rows] at position % rows.
 #pragma once
 
 #include <stddef.h>
@@ -97,6 +105,16 @@ struct HadamardDev {
   const float *cond_v, *cond_u;
 };
 
+struct EngramDev {
+  const uint8_t* packed;   // tables · slots rows of packed codes
+  uint32_t row_bytes, bits;
+  const float* levels;     // 2^bits levels
+  const float* norms;      // [rows][sub_dim / 128]
+  QMat kv;                 // key_proj rows, then value_proj rows
+  const float* taps;       // [conv_taps][d]
+  float* ring;             // [slots][ring_rows][d]; null when ring_rows == 0
+};
+
 struct LayerDev {
   QMat qkvg;  // q, k, v and gate_proj stacked row-wise (one fused product, matrix.rs:167-193)
   QMat out;
@@ -106,6 +124,8 @@ struct LayerDev {
   int global;  // 1 when the layer attends to the whole context
   int index;   // the layer's index in the archive
   const float* taps;  // [conv_taps][q | k | v] causal convolution gains; null without taps
+  int engram_site;    // the engram site on this layer (the first listed), -1 for none
+  EngramDev engram;   // that site's weights and ring
 };
 
 struct ModelDev {
@@ -132,6 +152,12 @@ struct ModelDev {
   uint32_t conv_taps;         // QKV causal convolution taps (0 = none)
   uint32_t qkv_width;         // (heads + 2 kv_heads) * head_dim: the convolved part of a projection row
   float* conv_ring;           // [slots][layers][conv_taps - 1][qkv_width]; null when conv_taps < 2
+  // engram configuration (config.rs:4-14)
+  uint32_t engram_slots, engram_sub_dim, engram_tables, engram_orders, engram_heads_per_order, engram_stride;
+  uint32_t engram_order[4];
+  uint32_t engram_conv_taps, engram_dilation, engram_ring_rows, engram_k;  // engram_k: the padded product K
+  uint32_t* token_ring;       // [slots][token_rows]; null when token_rows == 0
+  uint32_t token_rows;        // max order - 1
 };
 
 // Per-token metadata of one forward pass.
@@ -160,6 +186,9 @@ struct Work {
   float* attn;              // [M][heads * 64]
   float* outp;              // [M][d]
   int* arrivals;            // [M] attention CTAs done per token (zero between passes)
+  float* engram_kv;         // [M][2d] an engram site's key and raw value rows (null without sites)
+  float* xin;               // [M][d] the routing input at an engram site layer (x holds it plus the engram term)
+  uint32_t act_rows;        // rows of the activation buffer's K-chunk-major layout
 };
 
 struct KvDev {

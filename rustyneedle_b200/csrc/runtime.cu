@@ -189,6 +189,8 @@ struct Engine {
   std::vector<uint8_t> slot_dirty;
   float* d_hidden = nullptr;  // [slots][d]
   size_t conv_ring_floats = 0;  // per slot: md.conv_ring's [layers][taps - 1][q | k | v]
+  std::vector<EngramDev> engram_sites;
+  uint32_t act_groups = 0;  // act_scale floats per token: the widest product's groups
   // forward workspace
   uint32_t capacity = 0;
   Work work{};
@@ -373,7 +375,19 @@ std::shared_ptr<Engine> open_engine(const char* path, const nb_options* opt) {
   a.validate_tokenizer(lay.tokenizer);
   const nba::Geometry& g = a.geometry();
   if (g.qkv_conv_taps > 64) fail(NB_ERR_UNSUPPORTED, "more than 64 qkv conv taps are not implemented");
-  if (!g.engram_sites.empty()) fail(NB_ERR_UNSUPPORTED, "engram sites are not implemented by this build");
+  uint32_t max_order = 0;
+  if (!g.engram_sites.empty()) {
+    if (g.engram_orders.empty() || g.engram_tables == 0 || g.engram_tables % g.engram_orders.size() || g.engram_slots == 0)
+      fail(NB_ERR_ARCHIVE, "engram tables are not a whole number per order");
+    if (g.engram_tables > 16) fail(NB_ERR_UNSUPPORTED, "more than 16 engram tables are not implemented");
+    if (g.engram_sub_dim == 0 || g.engram_sub_dim % GROUP || g.engram_tables * g.engram_sub_dim > 2048)
+      fail(NB_ERR_UNSUPPORTED, "engram rows must be whole 128-groups, at most 2048 values in all");
+    if (g.engram_conv_taps == 0 || g.engram_conv_taps > 16) fail(NB_ERR_UNSUPPORTED, "engram value taps must number 1 to 16");
+    for (uint32_t o : g.engram_orders) max_order = std::max(max_order, o);
+    if (max_order > 64) fail(NB_ERR_UNSUPPORTED, "engram orders above 64 are not implemented");
+    for (uint32_t site : g.engram_sites)
+      if (site >= g.num_layers) fail(NB_ERR_ARCHIVE, "an engram site names a layer the model does not have");
+  }
   if (g.mhc_lanes != LANES) fail(NB_ERR_UNSUPPORTED, "only 4-lane models are implemented");
   if (g.qk_head_dim != HEAD_DIM || g.v_head_dim != HEAD_DIM) fail(NB_ERR_UNSUPPORTED, "head dims other than 64 are not implemented");
   if (g.d_model != 512)
@@ -427,6 +441,20 @@ std::shared_ptr<Engine> open_engine(const char* path, const nb_options* opt) {
   md.sliding_window = g.sliding_window;
   md.conv_taps = g.qkv_conv_taps;
   md.qkv_width = (H + 2 * KV) * HEAD_DIM;
+  if (!g.engram_sites.empty()) {
+    md.engram_slots = g.engram_slots;
+    md.engram_sub_dim = g.engram_sub_dim;
+    md.engram_tables = g.engram_tables;
+    md.engram_orders = (uint32_t)g.engram_orders.size();
+    md.engram_heads_per_order = g.engram_tables / md.engram_orders;
+    md.engram_stride = g.engram_seed_heads ? g.engram_seed_heads : md.engram_heads_per_order;
+    for (uint32_t i = 0; i < md.engram_orders; ++i) md.engram_order[i] = g.engram_orders[i];
+    md.engram_conv_taps = g.engram_conv_taps;
+    md.engram_dilation = g.engram_conv_dilation;
+    md.engram_ring_rows = (g.engram_conv_taps - 1) * g.engram_conv_dilation;
+    md.engram_k = g.engram_tables * g.engram_sub_dim <= 512 ? 512 : 2048;
+    md.token_rows = max_order - 1;
+  }
   md.sqrt_d = std::sqrt((float)d);
   md.inv_sqrt_group = 1.0f / std::sqrt((float)GROUP);
   md.inv_root_qk = 1.0f / std::sqrt((float)HEAD_DIM);
@@ -574,6 +602,53 @@ std::shared_ptr<Engine> open_engine(const char* path, const nb_options* opt) {
     E->layers.push_back(D);
   }
 
+  // engram sites (engram.rs:19-28): tables as packed rows for the gather,
+  // key_proj and value_proj as one product, value taps
+  std::vector<EngramDev> sites;
+  for (size_t si = 0; si < g.engram_sites.size(); ++si) {
+    const std::array<uint32_t, 4>& e = lay.engrams.at(si);
+    EngramDev S{};
+    const nba::Record& tr = a.record(e[0]);
+    if (tr.kind != nba::CODEBOOK || tr.rows() < (uint64_t)g.engram_tables * g.engram_slots || tr.columns() != g.engram_sub_dim ||
+        tr.group() != GROUP)
+      fail(NB_ERR_UNSUPPORTED, "engram tables must be codebook rows of sub_dim values in 128-groups, tables x slots of them");
+    Levels tl = levels_for(tr.bits, a.codebook(), GROUP);
+    S.packed = A.upload(std::vector<uint8_t>(a.data(e[0]), a.data(e[0]) + tr.packed_bytes()), st);
+    S.row_bytes = (uint32_t)tr.packed_row_bytes();
+    S.bits = tl.bits;
+    S.levels = A.upload(std::vector<float>(tl.values, tl.values + 16), st);
+    {
+      const uint64_t n = tr.rows() * tr.groups_per_row();
+      if (tr.packed_bytes() + n * 2 > tr.byte_len) fail(NB_ERR_ARCHIVE, "engram tables are shorter than their shape");
+      std::vector<float> norms(n);
+      const uint8_t* nb = a.data(e[0]) + tr.packed_bytes();
+      for (uint64_t i = 0; i < n; ++i) {
+        uint16_t h;
+        std::memcpy(&h, nb + 2 * i, 2);
+        norms[i] = nba::half_to_f32(h);
+      }
+      S.norms = A.upload(norms, st);
+    }
+    const uint32_t K = g.engram_tables * g.engram_sub_dim, KP = md.engram_k, kg = K / GROUP, pg = KP / GROUP;
+    check_matrix(a, e[1], d, K, "engram key_proj");
+    check_matrix(a, e[2], d, K, "engram value_proj");
+    Levels lk = levels_for(a.record(e[1]).bits, a.codebook(), GROUP);
+    if (levels_for(a.record(e[2]).bits, a.codebook(), GROUP).fused != lk.fused)
+      fail(NB_ERR_UNSUPPORTED, "engram key_proj and value_proj must share one code width");
+    // K-chunk-major codes do not depend on the total K, so the padded columns
+    // simply stay zero; the scales are re-strided to the padded groups
+    std::vector<int8_t> codes((size_t)((2 * d + 127) / 128 * 128) * KP, 0);
+    std::vector<float> scales;
+    expand_matrix(a, e[1], lk, true, codes, scales, 0, 2 * d);
+    expand_matrix(a, e[2], levels_for(a.record(e[2]).bits, a.codebook(), GROUP), true, codes, scales, d, 2 * d);
+    std::vector<float> padded((size_t)2 * d * pg, 0.0f);
+    for (uint32_t r = 0; r < 2 * d; ++r)
+      for (uint32_t gi = 0; gi < kg; ++gi) padded[(size_t)r * pg + gi] = scales[(size_t)r * kg + gi];
+    S.kv = QMat{A.upload(codes, st), A.upload(padded, st), lk.int_scale, 2 * d, KP, pg, lk.fused ? 1 : 0};
+    S.taps = A.upload(floats_of(a, e[3], (size_t)g.engram_conv_taps * d, "engram taps"), st);
+    sites.push_back(S);
+  }
+
   // sessions, KV pool, workspace
   E->max_sessions = opt && opt->max_sessions ? opt->max_sessions : 256;
   E->max_pages = (g.max_seq_len + PAGE_POSITIONS - 1) / PAGE_POSITIONS;
@@ -595,6 +670,24 @@ std::shared_ptr<Engine> open_engine(const char* path, const nb_options* opt) {
   for (uint32_t s = E->max_sessions; s-- > 0;) E->free_slots.push_back(s);
   E->d_hidden = A.alloc<float>((size_t)E->max_sessions * d);
   NB_CUDA(cudaMemsetAsync(E->d_hidden, 0, (size_t)E->max_sessions * d * 4, st));
+  for (EngramDev& S : sites)
+    if (md.engram_ring_rows) {
+      S.ring = A.alloc<float>((size_t)E->max_sessions * md.engram_ring_rows * d);
+      NB_CUDA(cudaMemsetAsync(S.ring, 0, (size_t)E->max_sessions * md.engram_ring_rows * d * 4, st));
+    }
+  if (md.token_rows) {
+    md.token_ring = A.alloc<uint32_t>((size_t)E->max_sessions * md.token_rows);
+    NB_CUDA(cudaMemsetAsync(md.token_ring, 0, (size_t)E->max_sessions * md.token_rows * 4, st));
+  }
+  for (uint32_t l = 0; l < L; ++l) {  // ModelConfig::engram_site_at: the first site listed on the layer
+    E->layers[l].engram_site = -1;
+    for (size_t si = 0; si < sites.size() && E->layers[l].engram_site < 0; ++si)
+      if (g.engram_sites[si] == l) {
+        E->layers[l].engram_site = (int)si;
+        E->layers[l].engram = sites[si];
+      }
+  }
+  E->engram_sites = sites;
   if (g.qkv_conv_taps > 1) {
     E->conv_ring_floats = (size_t)L * (g.qkv_conv_taps - 1) * md.qkv_width;  // per slot
     md.conv_ring = A.alloc<float>(E->max_sessions * E->conv_ring_floats);
@@ -602,7 +695,8 @@ std::shared_ptr<Engine> open_engine(const char* path, const nb_options* opt) {
   }
 
   E->capacity = std::max<uint32_t>(opt && opt->max_batch_tokens ? opt->max_batch_tokens : 1024, E->max_sessions);
-  const uint32_t M = E->capacity, AW = H * HEAD_DIM, actw = std::max(d, AW);
+  const uint32_t M = E->capacity, AW = H * HEAD_DIM, actw = std::max({d, AW, md.engram_k});
+  E->act_groups = actw / GROUP;
   Work& w = E->work;
   w.capacity = M;
   E->d_tokens = A.alloc<uint32_t>(M);
@@ -614,6 +708,11 @@ std::shared_ptr<Engine> open_engine(const char* path, const nb_options* opt) {
   w.x = A.alloc<float>((size_t)M * d);
   w.route = A.alloc<float>((size_t)M * (LANES + LANES * LANES));
   const size_t act_rows = ((size_t)M + 127) / 128 * 128;
+  w.act_rows = (uint32_t)act_rows;
+  if (!sites.empty()) {
+    w.engram_kv = A.alloc<float>((size_t)M * 2 * d);
+    w.xin = A.alloc<float>((size_t)M * d);
+  }
   w.act = A.alloc<int8_t>(act_rows * actw);
   NB_CUDA(cudaMemsetAsync(w.act, 0, act_rows * actw, st));
   w.act_scale = A.alloc<float>((size_t)M * (actw / GROUP));
@@ -862,6 +961,14 @@ nb_status nb_session_clone(const nb_session* session, nb_session** out) {
     E.slot_dirty[s->slot] = 1;
     NB_CUDA(cudaMemcpyAsync(E.d_hidden + (size_t)s->slot * E.md.d_model, E.d_hidden + (size_t)session->slot * E.md.d_model,
                             E.md.d_model * 4, cudaMemcpyDeviceToDevice, E.stream));
+    const size_t d = E.md.d_model;
+    for (const EngramDev& S : E.engram_sites)  // EngramSiteState is part of the session (session.rs:22)
+      if (S.ring)
+        NB_CUDA(cudaMemcpyAsync(S.ring + (size_t)s->slot * E.md.engram_ring_rows * d, S.ring + (size_t)session->slot * E.md.engram_ring_rows * d,
+                                (size_t)E.md.engram_ring_rows * d * 4, cudaMemcpyDeviceToDevice, E.stream));
+    if (E.md.token_ring)
+      NB_CUDA(cudaMemcpyAsync(E.md.token_ring + (size_t)s->slot * E.md.token_rows, E.md.token_ring + (size_t)session->slot * E.md.token_rows,
+                              E.md.token_rows * 4, cudaMemcpyDeviceToDevice, E.stream));
     if (E.conv_ring_floats)  // the convolution history is part of the session (attention.rs:45, AttentionCache is Clone)
       NB_CUDA(cudaMemcpyAsync(E.md.conv_ring + s->slot * E.conv_ring_floats, E.md.conv_ring + session->slot * E.conv_ring_floats,
                               E.conv_ring_floats * 4, cudaMemcpyDeviceToDevice, E.stream));
@@ -1022,7 +1129,7 @@ nb_status nb_session_logits(nb_session* session, float* out, size_t capacity) {
 // of K bytes; K = d_model for both products that read them) start on a whole
 // 32-token tile of the tensor-core product.
 static Work work_rows(const Engine& E, const Work& w, uint32_t b0) {
-  const size_t d = E.md.d_model, H = E.md.heads, KV = E.md.kv_heads, actw = d;
+  const size_t d = E.md.d_model, H = E.md.heads, KV = E.md.kv_heads, actw = d;  // act: the K-chunk-major chunk 0 block
   Work s = w;
   s.capacity = w.capacity - b0;
   s.tokens = w.tokens + b0;
@@ -1033,7 +1140,9 @@ static Work work_rows(const Engine& E, const Work& w, uint32_t b0) {
   s.x = w.x + b0 * d;
   s.route = w.route + b0 * (LANES + LANES * LANES);
   s.act = w.act + b0 * actw;
-  s.act_scale = w.act_scale + b0 * (actw / GROUP);
+  s.act_scale = w.act_scale + b0 * E.act_groups;
+  s.engram_kv = w.engram_kv ? w.engram_kv + b0 * 2 * d : nullptr;
+  s.xin = w.xin ? w.xin + b0 * d : nullptr;
   s.proj = w.proj + b0 * (2 * H + 2 * KV) * HEAD_DIM;
   s.qcodes = w.qcodes + b0 * H * HEAD_DIM;
   s.qscale = w.qscale + b0 * H;

@@ -8,7 +8,8 @@ crates/cact/src/geometry.rs:41-115, record.rs:38-51, docs/format.md), and the
 tensors follow the canonical positional order of crates/cact/src/layout.rs:190-230:
 embedding; per layer norm_in, q, k, v, [q, k, v conv taps], q_norm, k_norm, gate_proj, out_proj,
 post_norm, attn_gate, pre_hada and 13 Hadamard tensors; nine lane tensors; two
-Hadamard permutations; final_norm; the tokenizer blob.
+Hadamard permutations; [per engram site: tables, key_proj, value_proj, taps];
+final_norm; the tokenizer blob.
 
 Weights are codebook-quantised (kind 3): uniform indices, packed least
 significant bit first, and one fp16 norm per row drawn log-uniform in
@@ -67,6 +68,14 @@ class Geometry:
     sliding_window: int = 0   # window of the non-global layers
     global_layers: int = 0    # bit l set: layer l attends to the whole context
     conv_taps: int = 0        # causal convolution taps on q, k and v
+    engram_sites: tuple = ()  # layers that add the hashed n-gram memory
+    engram_slots: int = 4096  # rows per table
+    engram_sub_dim: int = 128
+    engram_orders: tuple = (2, 3)
+    engram_heads_per_order: int = 2
+    engram_conv_taps: int = 3
+    engram_dilation: int = 2
+    engram_seed_heads: int = 0
     extra: dict = field(default_factory=dict)
 
 
@@ -225,12 +234,29 @@ def write_archive(path: str, seed: int = 0, geometry: Geometry | None = None) ->
     w.codebook_matrix(rng, L * lanes * lanes, lanes * d, g.phi_bits, g.group)  # phi_res
     w.single(rng.permutation(n).astype(np.float32))
     w.single(rng.permutation(n).astype(np.float32))
+    tables = len(g.engram_orders) * g.engram_heads_per_order
+    for _ in g.engram_sites:  # crates/cact/src/layout.rs:231-234: tables, key_proj, value_proj, taps
+        w.codebook_matrix(rng, tables * g.engram_slots, g.engram_sub_dim, g.projection_bits, g.group)
+        w.codebook_matrix(rng, d, tables * g.engram_sub_dim, g.projection_bits, g.group)
+        w.codebook_matrix(rng, d, tables * g.engram_sub_dim, g.projection_bits, g.group)
+        if g.extra.get("zero_engram_taps"):  # the value convolution adds nothing, drawing nothing
+            w.single(np.zeros((g.engram_conv_taps, d)))
+        else:
+            taps = 0.5 * rng.standard_normal((g.engram_conv_taps, d))
+            taps[0] += 1.0
+            w.single(taps)
     w.single(zeros(d))  # final_norm
     w.add(KIND_RAW, (0,), tokenizer_blob(g.vocab))
 
     header = [FORMAT_TAG, len(w.records), codebook.size, 0, 8, g.vocab, g.out_vocab, d, H, KV, L, hd, hd,
-              g.max_seq_len, n, lanes, g.sliding_window, g.global_layers & 0xFFFFFFFF, g.global_layers >> 32, g.conv_taps,
-              0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0] + [0] * 16
+              g.max_seq_len, n, lanes, g.sliding_window, g.global_layers & 0xFFFFFFFF, g.global_layers >> 32, g.conv_taps]
+    if g.engram_sites:
+        orders = list(g.engram_orders) + [0] * (4 - len(g.engram_orders))
+        sites = list(g.engram_sites) + [0] * (16 - len(g.engram_sites))
+        header += [g.engram_slots, g.engram_sub_dim, tables, g.engram_conv_taps, g.engram_dilation, g.engram_seed_heads,
+                   len(g.engram_orders)] + orders + [len(g.engram_sites)] + sites
+    else:
+        header += [0] * 28
     assert len(header) == 48
     w.finish(path, header, g.rope_theta, codebook)
     return path

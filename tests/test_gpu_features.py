@@ -1,8 +1,10 @@
 """Parity of the archive features the default synthetic geometry leaves out:
-QKV causal convolution taps (model/src/attention.rs:83-117, 243-276) and the
-sliding window with global layers (attention.rs:171-177). The archive is a
-6-layer synthetic model with 3 taps, a 40-position window and layers 0 and 5
-global; every case is bit-exact against the CPU restatement in INT mode."""
+QKV causal convolution taps (model/src/attention.rs:83-117, 243-276), the
+sliding window with global layers (attention.rs:171-177) and engram sites
+(model/src/engram.rs, session.rs:93-113, 180-190). The archives are 6-layer
+synthetic models with 3 taps, a 40-position window and layers 0 and 5
+global, plus engram sites for the second half; every case is bit-exact
+against the CPU restatement in INT mode."""
 
 import numpy as np
 import pytest
@@ -170,4 +172,172 @@ def test_short_tap_counts(native_built, oracle_lib, taps):
         o.push(int(t))
     assert _bits_equal(s.logits(), o.logits()), _mismatch(s.logits(), o.logits())
     s.close()
+    model.close()
+
+
+# ------------------------------------------------------------- engram sites
+def _engram_geometry(**kw):
+    from rustyneedle_b200 import synthetic
+
+    base = dict(num_layers=6, max_seq_len=512, conv_taps=3, sliding_window=WINDOW, global_layers=0b100001, engram_sites=(1, 4),
+                engram_slots=512, engram_orders=(2, 3), engram_heads_per_order=2, engram_conv_taps=3, engram_dilation=2)
+    base.update(kw)
+    return synthetic.Geometry(**base)
+
+
+@pytest.fixture(scope="module")
+def engram_path():
+    from rustyneedle_b200 import synthetic
+
+    return synthetic.cached_archive(seed=11, geometry=_engram_geometry())
+
+
+@pytest.fixture(scope="module")
+def engram_model(native_built, engram_path):
+    import rustyneedle_b200 as nb
+
+    return nb.Model.open(engram_path, max_sessions=96)
+
+
+@pytest.fixture(scope="module")
+def engram_oracle(oracle_lib, engram_path):
+    return oracle_lib.Model.open(engram_path, oracle_lib.MODE_INT, 0)
+
+
+def test_engram_prefill_and_ragged_feeds(engram_model, engram_oracle, oracle_lib):
+    """Two engram sites (orders 2 and 3, value taps 3 at dilation 2) with the
+    QKV taps and the window: one 100-token pass, then ragged feeds whose hashes
+    and value taps read across pass boundaries, then greedy steps."""
+    import rustyneedle_b200 as nb
+    from rustyneedle_b200 import debug
+
+    ids = prompt_ids(41, 100)
+    s = nb.Session(engram_model)
+    s.feed(ids)
+    o = oracle_lib.Session(engram_oracle)
+    o.feed(ids)
+    assert _bits_equal(debug.hidden(s), o.hidden()), _mismatch(debug.hidden(s), o.hidden())
+    more = prompt_ids(42, 40)
+    at = 0
+    for n in (1, 2, 5, 30, 1, 1):
+        s.feed(more[at:at + n])
+        o.feed(more[at:at + n])
+        at += n
+        assert _bits_equal(s.logits(), o.logits()), (at, _mismatch(s.logits(), o.logits()))
+    for _ in range(10):
+        token = oracle_lib.argmax(o.logits())
+        o.push(token)
+        assert s.step() == token
+    s.close()
+
+
+def test_engram_small_passes_and_clone(native_built, engram_path, engram_oracle, oracle_lib):
+    """max_batch_tokens 5: the token and value rings carry every pass boundary;
+    a clone carries both rings."""
+    import rustyneedle_b200 as nb
+
+    model = nb.Model.open(engram_path, max_sessions=4, max_batch_tokens=5)
+    ids = prompt_ids(43, 61)
+    s = nb.Session(model)
+    s.feed(ids)
+    o = oracle_lib.Session(engram_oracle)
+    o.feed(ids)
+    assert _bits_equal(s.logits(), o.logits()), _mismatch(s.logits(), o.logits())
+    c, oc = s.clone(), o.clone()
+    for t in (5, 6, 7):
+        c.push(t)
+        oc.push(t)
+    s.push(9)
+    o.push(9)
+    assert _bits_equal(c.logits(), oc.logits()) and _bits_equal(s.logits(), o.logits())
+    for x in (s, c):
+        x.close()
+    model.close()
+
+
+@pytest.mark.parametrize("count", [6, 72])
+def test_engram_batched_decode(engram_model, engram_oracle, oracle_lib, count):
+    import rustyneedle_b200 as nb
+
+    base = [1, 2, 3, 5, 8, 60]
+    lengths = (base * (count // len(base) + 1))[:count]
+    sessions, oracles = [], []
+    for i, n in enumerate(lengths):
+        ids = prompt_ids(800 + i, n)
+        s = nb.Session(engram_model)
+        s.feed(ids)
+        sessions.append(s)
+        o = oracle_lib.Session(engram_oracle)
+        o.feed(ids)
+        oracles.append(o)
+    batch = nb.Batch(engram_model, sessions)
+    for _ in range(4):
+        got = batch.step()
+        want = []
+        for o in oracles:
+            token = oracle_lib.argmax(o.logits())
+            o.push(token)
+            want.append(token)
+        assert list(got) == want
+    batch.close()
+    for s, o in zip(sessions, oracles):
+        assert _bits_equal(s.logits(), o.logits())
+        s.close()
+
+
+def test_engram_depth_without_a_site(engram_model, engram_oracle, oracle_lib):
+    """Depth 5 (layers 0, 1, 2, 3, 5) keeps the site on layer 1 and skips the one
+    on layer 4: that site neither contributes nor keeps history."""
+    import rustyneedle_b200 as nb
+
+    model, omodel = engram_model.with_depth(5), engram_oracle.with_depth(5)
+    assert model.active_layers() == [0, 1, 2, 3, 5]
+    ids = prompt_ids(44, 70)
+    s = nb.Session(model)
+    s.feed(ids)
+    o = oracle_lib.Session(omodel)
+    o.feed(ids)
+    s.push(3)
+    o.push(3)
+    assert _bits_equal(s.logits(), o.logits()), (model.active_layers(), _mismatch(s.logits(), o.logits()))
+    s.close()
+
+
+@pytest.mark.parametrize("variant", ["k256", "k2048_seed", "dilation1_taps1"])
+def test_engram_variants(native_built, oracle_lib, variant):
+    """Tables x sub_dim 256 (padded to a 512 product), 1024 (padded to 2048,
+    four orders, seed heads 3, stepped as a 256-sequence batch: two step
+    groups), and one value tap (no ring)."""
+    import rustyneedle_b200 as nb
+    from rustyneedle_b200 import synthetic
+
+    kw = {"k256": dict(engram_orders=(2,), engram_heads_per_order=2, engram_sites=(2,)),
+          "k2048_seed": dict(engram_orders=(1, 2, 3, 4), engram_heads_per_order=2, engram_seed_heads=3, engram_sites=(0, 3, 5)),
+          "dilation1_taps1": dict(engram_conv_taps=1, engram_dilation=1)}[variant]
+    path = synthetic.cached_archive(seed=12, geometry=_engram_geometry(**kw))
+    sequences = 256 if variant == "k2048_seed" else 4
+    model = nb.Model.open(path, max_sessions=sequences)
+    omodel = oracle_lib.Model.open(path, oracle_lib.MODE_INT, 0)
+    sessions, oracles = [], []
+    for i in range(sequences):
+        ids = prompt_ids(900 + i, 1 + i % 7 if sequences > 4 else 30 + i)
+        s = nb.Session(model)
+        s.feed(ids)
+        sessions.append(s)
+        o = oracle_lib.Session(omodel)
+        o.feed(ids)
+        oracles.append(o)
+    batch = nb.Batch(model, sessions)
+    for _ in range(2):
+        got = batch.step()
+        want = []
+        for o in oracles:
+            token = oracle_lib.argmax(o.logits())
+            o.push(token)
+            want.append(token)
+        assert list(got) == want
+    batch.close()
+    for s, o in zip(sessions, oracles):
+        assert _bits_equal(s.logits(), o.logits())
+        s.close()
     model.close()

@@ -173,3 +173,39 @@ def test_taps_and_window_prefill_agree_with_stepping(oracle_lib, kats):
     a, b = fed.logits(), pushed.logits()
     assert _cos(a, b) > kats["prefill_cosine"]
     assert oracle_lib.argmax(a) == oracle_lib.argmax(b)
+
+
+def test_engram_with_zero_value_taps_changes_nothing(oracle_lib):
+    """Engram value taps of zero add alpha · 0 (session.rs:187-189): the result is
+    the model without sites, bit for bit (the site tensors follow every layer's
+    draws, so the layers are the same)."""
+    from rustyneedle_b200 import synthetic
+
+    plain = synthetic.cached_archive(seed=13, geometry=_features())
+    zero = synthetic.cached_archive(seed=13, geometry=_features(engram_sites=(1, 2), engram_slots=256, extra={"zero_engram_taps": True}))
+    live = synthetic.cached_archive(seed=13, geometry=_features(engram_sites=(1, 2), engram_slots=256))
+    ids = prompt_ids(7, 30)
+    out = []
+    for path in (plain, zero, live):
+        s = oracle_lib.Session(oracle_lib.Model.open(path, oracle_lib.MODE_INT, 0))
+        s.feed(ids)
+        out.append(s.logits())
+    assert np.array_equal(out[0].view(np.uint32), out[1].view(np.uint32))
+    assert not np.array_equal(out[0], out[2])
+
+
+def test_engram_prefill_agrees_with_stepping(oracle_lib, kats):
+    """contribute_batch (engram.rs:108-160) against contribute (engram.rs:68-105)
+    in FLOAT mode: cosine > 0.9995, same argmax."""
+    from rustyneedle_b200 import synthetic
+
+    path = synthetic.cached_archive(seed=14, geometry=_features(conv_taps=2, engram_sites=(0, 3), engram_slots=256))
+    m = oracle_lib.Model.open(path, oracle_lib.MODE_FLOAT, 0)
+    ids = prompt_ids(8, 50)
+    fed, pushed = oracle_lib.Session(m), oracle_lib.Session(m)
+    fed.feed(ids)
+    for t in ids:
+        pushed.push(int(t))
+    a, b = fed.logits(), pushed.logits()
+    assert _cos(a, b) > kats["prefill_cosine"]
+    assert oracle_lib.argmax(a) == oracle_lib.argmax(b)
