@@ -109,6 +109,18 @@ nb_status nb_session_push(nb_session* session, uint32_t id);
  * at least output_vocab floats. */
 nb_status nb_session_logits(nb_session* session, float* out, size_t capacity);
 
+/* Session::head_output (session.rs:150-154): the probe head `code`'s
+ * projection of its pooled readout (ProbeHead::pooled and ::project,
+ * heads.rs:85-125), observed over every token the session has fed. Writes
+ * min(capacity, n) floats to `out` and n to *count (may be NULL).
+ * NB_ERR_ARGUMENT when the model has no head with that code (the reference's
+ * None). */
+nb_status nb_session_head_output(nb_session* session, uint32_t code, float* out, size_t capacity, size_t* count);
+
+/* Session::pooled_readout (session.rs:156-160): the pooled readout itself,
+ * queries x d_model floats (Engine::embed reads head 3's, engine.rs:113-123). */
+nb_status nb_session_pooled_readout(nb_session* session, uint32_t code, float* out, size_t capacity, size_t* count);
+
 /* Session::len (session.rs:44-46). */
 size_t nb_session_len(const nb_session* session);
 

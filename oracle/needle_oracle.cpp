@@ -219,6 +219,8 @@ struct Layout {
   std::vector<std::array<size_t, 4>> engrams;  // tables, key_proj, value_proj, taps per site
   size_t final_norm;
   size_t head_count = 0;
+  struct HeadT { uint8_t code; size_t probes, gain, query, row_bias, proj, bias; };
+  std::vector<HeadT> heads;
   bool audio = false;
   size_t tokenizer;
 };
@@ -280,8 +282,16 @@ Layout resolve_layout(const Archive& a) {
     for (size_t i = 0; i < r.byte_len / 2; ++i) {
       int code = (int)std::round(half_to_f32(codes[i]));
       if (code < 1 || code > 3) throw Failure(ERR_ARCHIVE, "unexpected tensor layout: unrecognised head manifest code");
-      for (int j = 0; j < 6; ++j) take();
-      if (code == 3) take();
+      Layout::HeadT h;
+      h.code = (uint8_t)code;
+      h.probes = take();
+      h.gain = take();
+      h.query = take();
+      h.row_bias = take();
+      h.proj = take();
+      h.bias = take();
+      if (code == 3) take();  // calibration: not read by the model crate
+      L.heads.push_back(h);
       L.head_count++;
     }
   }
@@ -364,6 +374,19 @@ float sum_of_squares(const float* v, size_t n) {
     for (size_t l = 0; l < LANES8; ++l) lanes[l] += v[c + l] * v[c + l];
   float tail = RUST_SUM_START;
   for (size_t i = whole; i < n; ++i) tail += v[i] * v[i];
+  float s = RUST_SUM_START;
+  for (size_t l = 0; l < LANES8; ++l) s += lanes[l];
+  return s + tail;
+}
+
+// ops.rs:19-30
+float dot_product(const float* a, const float* b, size_t n) {
+  float lanes[LANES8] = {0};
+  size_t whole = n / LANES8 * LANES8;
+  for (size_t c = 0; c < whole; c += LANES8)
+    for (size_t l = 0; l < LANES8; ++l) lanes[l] += a[c + l] * b[c + l];
+  float tail = RUST_SUM_START;
+  for (size_t i = whole; i < n; ++i) tail += a[i] * b[i];
   float s = RUST_SUM_START;
   for (size_t l = 0; l < LANES8; ++l) s += lanes[l];
   return s + tail;
@@ -821,11 +844,21 @@ struct EngramW {
   std::vector<float> taps;  // [conv_taps][d]
 };
 
+// model/src/heads.rs:6-18, loaded for every row (the embedding cell and one
+// cell per layer); a depth selects rows (ProbeHead::with_rows, heads.rs:52-78).
+struct ProbeHeadW {
+  uint8_t code = 0;
+  size_t rows = 0, ppl = 0, queries = 0, width = 0;
+  std::vector<float> probes, gain, query, row_bias, bias;  // probes [rows][ppl][width], query [queries][width]
+  QMatrix projection;
+};
+
 struct Weights {
   QMatrix embedding;
   std::vector<LayerW> layers;
   LanesW lanes;
   std::vector<EngramW> engrams;  // one per engram site
+  std::vector<ProbeHeadW> heads;
   std::vector<float> final_norm;
   std::vector<size_t> perm1, perm2;
 };
@@ -1004,6 +1037,32 @@ std::shared_ptr<Weights> load_weights(const Archive& a, const Layout& L) {
       throw Failure(ERR_ARCHIVE, "engram tensors do not match the header");
     w->engrams.push_back(std::move(ew));
   }
+  for (const Layout::HeadT& h : L.heads) {  // heads.rs:29-50
+    ProbeHeadW hw;
+    hw.code = h.code;
+    QMatrix probes = load_matrix(a, h.probes), query = load_matrix(a, h.query);
+    hw.rows = g.num_layers + 1;
+    hw.width = probes.columns;
+    hw.ppl = probes.rows / hw.rows;
+    hw.queries = query.rows;
+    for (size_t r = 0; r < probes.rows; ++r) {  // dense() (heads.rs:20-28)
+      std::vector<float> row = probes.dequantise_row(r);
+      hw.probes.insert(hw.probes.end(), row.begin(), row.end());
+    }
+    for (size_t r = 0; r < query.rows; ++r) {
+      std::vector<float> row = query.dequantise_row(r);
+      hw.query.insert(hw.query.end(), row.begin(), row.end());
+    }
+    hw.gain = floats(a, h.gain);
+    hw.row_bias = floats(a, h.row_bias);
+    hw.projection = load_matrix(a, h.proj);
+    hw.bias = floats(a, h.bias);
+    const size_t slots = hw.rows * hw.ppl;
+    if (hw.ppl == 0 || hw.gain.size() < slots || hw.row_bias.size() < hw.queries * slots || query.columns != hw.width ||
+        hw.projection.columns != hw.queries * hw.width || hw.bias.size() < hw.projection.rows)
+      throw Failure(ERR_ARCHIVE, "probe head tensors do not match one another");
+    w->heads.push_back(std::move(hw));
+  }
   w->final_norm = floats(a, L.final_norm);
   return w;
 }
@@ -1180,6 +1239,8 @@ struct nbo_session {
   std::vector<uint32_t> tokens;
   std::vector<nbo::Cache> caches;
   std::vector<std::deque<std::vector<float>>> engram_history;  // per site: raw values, newest first (engram.rs:45-48)
+  struct Accumulator { std::vector<float> peak, total, weighted; };  // heads.rs:151-156
+  std::vector<Accumulator> accumulators;                            // per probe head
   std::vector<float> frequencies;
   std::vector<float> hidden;
 };
@@ -1427,6 +1488,69 @@ int engram_site_at(const Geometry& g, size_t layer) {
 
 bool layer_active(const nbo_model* M, size_t layer) { return std::find(M->active.begin(), M->active.end(), layer) != M->active.end(); }
 
+// ---------------------------------------------------------------- probe heads
+// The head's rows for this model: the embedding cell and one per active layer
+// (model.rs:69-70).
+std::vector<size_t> head_rows(const nbo_model* M) {
+  std::vector<size_t> rows{0};
+  for (size_t l : M->active) rows.push_back(l + 1);
+  return rows;
+}
+
+// ProbeHead::observe (heads.rs:127-148): per (cell, probe) an online softmax
+// pool of the cells, weighted by exp(score - running peak).
+void observe(const ProbeHeadW& h, const std::vector<size_t>& rows, nbo_session::Accumulator& acc, const std::vector<std::vector<float>>& cells) {
+  const size_t width = h.width;
+  const float root = std::sqrt((float)width);
+  for (size_t c = 0; c < cells.size(); ++c)
+    for (size_t k = 0; k < h.ppl; ++k) {
+      const size_t slot = c * h.ppl + k;
+      const float* direction = &h.probes[(rows[c] * h.ppl + k) * width];
+      const float score = dot_product(cells[c].data(), direction, width) / root;
+      const float peak = std::fmax(acc.peak[slot], score);
+      const float rescale = acc.peak[slot] == -INFINITY ? 0.0f : std::exp(acc.peak[slot] - peak);
+      const float weight = std::exp(score - peak);
+      acc.total[slot] = acc.total[slot] * rescale + weight;
+      float* target = &acc.weighted[slot * width];
+      for (size_t i = 0; i < width; ++i) target[i] = target[i] * rescale + weight * cells[c][i];
+      acc.peak[slot] = peak;
+    }
+}
+
+// ProbeHead::pooled (heads.rs:85-115)
+std::vector<float> pooled(const ProbeHeadW& h, const std::vector<size_t>& rows, const nbo_session::Accumulator& acc) {
+  const size_t width = h.width, slots = rows.size() * h.ppl, all = h.rows * h.ppl;
+  std::vector<float> readouts(slots * width), averaged(width);
+  for (size_t slot = 0; slot < slots; ++slot) {
+    const float inverse = 1.0f / acc.total[slot];
+    for (size_t i = 0; i < width; ++i) averaged[i] = acc.weighted[slot * width + i] * inverse;
+    unit_rms(averaged.data(), &readouts[slot * width], width);
+    const float gain = h.gain[rows[slot / h.ppl] * h.ppl + slot % h.ppl];
+    for (size_t i = 0; i < width; ++i) readouts[slot * width + i] *= gain;
+  }
+  const float root = std::sqrt((float)width);
+  std::vector<float> out(h.queries * width, 0.0f), weights(slots);
+  for (size_t q = 0; q < h.queries; ++q) {
+    for (size_t slot = 0; slot < slots; ++slot)
+      weights[slot] = dot_product(&readouts[slot * width], &h.query[q * width], width) / root +
+                      h.row_bias[q * all + rows[slot / h.ppl] * h.ppl + slot % h.ppl];
+    softmax_in_place(weights.data(), slots);
+    for (size_t slot = 0; slot < slots; ++slot)
+      for (size_t i = 0; i < width; ++i) out[q * width + i] += weights[slot] * readouts[slot * width + i];
+  }
+  return out;
+}
+
+// ProbeHead::project (heads.rs:117-125)
+std::vector<float> project_head(const nbo_model* M, const ProbeHeadW& h, const std::vector<float>& pooled_values) {
+  std::vector<float> rotated = h.projection.prepare(pooled_values.data());
+  std::vector<float> out(h.projection.rows, 0.0f);
+  std::vector<Job> jobs{{&h.projection, 0, out.data(), h.projection.rows}};
+  multiply_jobs(jobs, rotated.data(), M->mode, M->threads);
+  for (size_t i = 0; i < out.size(); ++i) out[i] += h.bias[i];
+  return out;
+}
+
 std::vector<float> embed(const nbo_model* M, uint32_t token) {
   const Geometry& g = M->archive->geo;
   if (token >= M->weights->embedding.rows) throw Failure(ERR_ARGUMENT, "token id outside the embedding");
@@ -1456,6 +1580,7 @@ void push(nbo_session* s, uint32_t token, float* trace) {
   }
   std::vector<float> next(stream.size());
   std::vector<float> normed(d);
+  std::vector<std::vector<float>> cells{lane_mean(stream.data(), d, lanes)};  // session.rs:91-92, 139
   for (size_t slot = 0; slot < M->active.size(); ++slot) {
     size_t layer = M->active[slot];
     const LayerW& W = M->weights->layers[layer];
@@ -1468,10 +1593,13 @@ void push(nbo_session* s, uint32_t token, float* trace) {
     finish_block(M, W, r, x, attended, stream.data(), next.data());
     std::swap(stream, next);
     if (trace) std::memcpy(trace + slot * lanes * d, stream.data(), lanes * d * sizeof(float));
+    if (!M->weights->heads.empty()) cells.push_back(lane_mean(stream.data(), d, lanes));
   }
   std::vector<float> mean = lane_mean(stream.data(), d, lanes);
   s->hidden.assign(d, 0.0f);
   zero_centred_norm(mean.data(), M->weights->final_norm.data(), s->hidden.data(), d);
+  const std::vector<size_t> rows = head_rows(M);
+  for (size_t h = 0; h < M->weights->heads.size(); ++h) observe(M->weights->heads[h], rows, s->accumulators[h], cells);  // session.rs:144-146
 }
 
 // crates/model/src/prefill.rs:10-99 with the non-aarch64 attend_batch
@@ -1520,6 +1648,10 @@ void prefill_float(nbo_session* s, const uint32_t* tokens, size_t count) {
       s->engram_history[i].push_front(std::vector<float>(raw.begin() + t * vw, raw.begin() + (t + 1) * vw));
     while (s->engram_history[i].size() > keep) s->engram_history[i].pop_back();
   }
+  const bool heads = !M->weights->heads.empty();
+  std::vector<std::vector<std::vector<float>>> cells(count);  // prefill.rs:31, 86-88
+  if (heads)
+    for (size_t t = 0; t < count; ++t) cells[t].push_back(lane_mean(&stream[t * frame], d, lanes));
   for (size_t slot = 0; slot < M->active.size(); ++slot) {
     size_t layer = M->active[slot];
     const LayerW& W = M->weights->layers[layer];
@@ -1606,7 +1738,12 @@ void prefill_float(nbo_session* s, const uint32_t* tokens, size_t count) {
       finish_block(M, W, routings[t], xt, at, &stream[t * frame], &next[t * frame]);
     });
     std::swap(stream, next);
+    if (heads)
+      for (size_t t = 0; t < count; ++t) cells[t].push_back(lane_mean(&stream[t * frame], d, lanes));
   }
+  const std::vector<size_t> rows = head_rows(M);
+  for (size_t t = 0; t < count && heads; ++t)  // prefill.rs:90-94
+    for (size_t h = 0; h < M->weights->heads.size(); ++h) observe(M->weights->heads[h], rows, s->accumulators[h], cells[t]);
   std::vector<float> mean = lane_mean(&stream[(count - 1) * frame], d, lanes);
   s->hidden.assign(d, 0.0f);
   zero_centred_norm(mean.data(), M->weights->final_norm.data(), s->hidden.data(), d);
@@ -1718,6 +1855,10 @@ nbo_session* nbo_session_new(const nbo_model* model) {
   s->model = model;
   s->caches.resize(model->archive->geo.num_layers);
   s->engram_history.resize(model->archive->geo.engram_sites.size());
+  for (const nbo::ProbeHeadW& h : model->weights->heads) {  // ProbeHead::accumulator (heads.rs:80-83)
+    const size_t slots = (model->active.size() + 1) * h.ppl;
+    s->accumulators.push_back({std::vector<float>(slots, -INFINITY), std::vector<float>(slots, 0.0f), std::vector<float>(slots * h.width, 0.0f)});
+  }
   s->frequencies = rotary_frequencies(model->archive->geo.qk_head_dim, model->archive->geo.rope_theta);
   return s;
 }
@@ -1725,6 +1866,22 @@ nbo_session* nbo_session_new(const nbo_model* model) {
 nbo_session* nbo_session_clone(const nbo_session* s) { return new nbo_session(*s); }
 void nbo_session_free(nbo_session* s) { delete s; }
 size_t nbo_session_len(const nbo_session* s) { return s->tokens.size(); }
+
+// Session::head_output / pooled_readout (session.rs:150-160): the values
+// written (at most `cap`), or -1 when the model has no head with `code`.
+static long head_values(const nbo_session* s, int code, float* out, size_t cap, bool project) {
+  const nbo_model* M = s->model;
+  for (size_t h = 0; h < M->weights->heads.size(); ++h)
+    if (M->weights->heads[h].code == code) {
+      std::vector<float> v = nbo::pooled(M->weights->heads[h], nbo::head_rows(M), s->accumulators[h]);
+      if (project) v = nbo::project_head(M, M->weights->heads[h], v);
+      std::memcpy(out, v.data(), std::min(cap, v.size()) * sizeof(float));
+      return (long)v.size();
+    }
+  return -1;
+}
+long nbo_session_head_output(const nbo_session* s, int code, float* out, size_t cap) { return head_values(s, code, out, cap, true); }
+long nbo_session_pooled_readout(const nbo_session* s, int code, float* out, size_t cap) { return head_values(s, code, out, cap, false); }
 
 void nbo_session_push(nbo_session* s, uint32_t token) { guard([&] { push(s, token, nullptr); }); }
 void nbo_session_push_traced(nbo_session* s, uint32_t token, float* trace) { guard([&] { push(s, token, trace); }); }

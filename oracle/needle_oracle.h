@@ -51,6 +51,9 @@ nbo_session* nbo_session_new(const nbo_model* model);
 nbo_session* nbo_session_clone(const nbo_session* session);
 void nbo_session_free(nbo_session* session);
 size_t nbo_session_len(const nbo_session* session);
+// Session::head_output / pooled_readout: values written (at most cap), -1 without a head `code`.
+long nbo_session_head_output(const nbo_session* session, int code, float* out, size_t cap);
+long nbo_session_pooled_readout(const nbo_session* session, int code, float* out, size_t cap);
 void nbo_session_push(nbo_session* session, uint32_t token);
 /* push that also records the lane stream after every active layer:
  * trace holds depth × lanes × d_model floats. */

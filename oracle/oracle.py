@@ -53,6 +53,8 @@ def _declare(L: ctypes.CDLL) -> None:
         "nbo_session_clone": (P, [P]),
         "nbo_session_free": (None, [P]),
         "nbo_session_len": (SZ, [P]),
+        "nbo_session_head_output": (ctypes.c_long, [P, ctypes.c_int, P, SZ]),
+        "nbo_session_pooled_readout": (ctypes.c_long, [P, ctypes.c_int, P, SZ]),
         "nbo_session_push": (None, [P, U32]),
         "nbo_session_push_traced": (None, [P, U32, P]),
         "nbo_session_feed": (None, [P, P, SZ]),
@@ -182,6 +184,19 @@ class Session:
 
     def __len__(self) -> int:
         return int(lib().nbo_session_len(self._h))
+
+    def _head(self, fn, code: int):
+        out = np.empty(1 << 14, dtype=np.float32)
+        n = fn(self._h, int(code), _ptr(out), out.size)
+        return None if n < 0 else out[:n].copy()
+
+    def head_output(self, code: int):
+        """Session::head_output (session.rs:150-154); None without that head."""
+        return self._head(lib().nbo_session_head_output, code)
+
+    def pooled_readout(self, code: int):
+        """Session::pooled_readout (session.rs:156-160); None without that head."""
+        return self._head(lib().nbo_session_pooled_readout, code)
 
     def push(self, token: int) -> None:
         lib().nbo_session_push(self._h, int(token))

@@ -83,6 +83,8 @@ def lib() -> ctypes.CDLL:
             "nb_sessions_feed": (I, [P, P, P, SZ]),
             "nb_session_push": (I, [P, U32]),
             "nb_session_logits": (I, [P, P, SZ]),
+            "nb_session_head_output": (I, [P, U32, P, SZ, ctypes.POINTER(SZ)]),
+            "nb_session_pooled_readout": (I, [P, U32, P, SZ, ctypes.POINTER(SZ)]),
             "nb_session_len": (SZ, [P]),
             "nb_session_step": (I, [P, P, ctypes.POINTER(U32), ctypes.POINTER(nb_step_stats)]),
             "nb_batch_create": (I, [P, P, U32, ctypes.POINTER(P)]),
@@ -205,6 +207,23 @@ class Session:
         out = np.empty(self.model.config.output_vocab, dtype=np.float32)
         _check(lib().nb_session_logits(self._h, _ptr(out), out.size))
         return out
+
+    def _head(self, fn, code: int):
+        out = np.empty(1 << 14, dtype=np.float32)
+        n = ctypes.c_size_t()
+        status = fn(self._h, int(code), _ptr(out), out.size, ctypes.byref(n))
+        if status == -4:  # NB_ERR_ARGUMENT: the model has no head with that code (the reference's None)
+            return None
+        _check(status)
+        return out[:n.value].copy()
+
+    def head_output(self, code: int):
+        """Session::head_output: the probe head's projection, or None without that head."""
+        return self._head(lib().nb_session_head_output, code)
+
+    def pooled_readout(self, code: int):
+        """Session::pooled_readout: the head's pooled readout, or None without that head."""
+        return self._head(lib().nb_session_pooled_readout, code)
 
     def step(self, mask_bits: np.ndarray | None = None, stats: bool = False):
         """One greedy step: choose from the current logits (optionally under a

@@ -229,8 +229,16 @@ Layout Archive::resolve() const {
       std::memcpy(&h, data(manifest) + 2 * i, 2);
       long code = std::lround(half_to_f32(h));
       if (code < 1 || code > 3) fail(NB_ERR_ARCHIVE, "unexpected tensor layout: unrecognised head manifest code");
-      for (int k = 0; k < 6; ++k) take();
-      if (code == 3) take();
+      Layout::HeadIdx hi;
+      hi.code = (uint32_t)code;
+      hi.probes = take();
+      hi.gain = take();
+      hi.query = take();
+      hi.row_bias = take();
+      hi.proj = take();
+      hi.bias = take();
+      if (code == 3) take();  // calibration: not read by the model crate
+      L.heads.push_back(hi);
       L.probe_heads++;
     }
   }

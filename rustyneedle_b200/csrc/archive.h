@@ -63,6 +63,8 @@ struct Layout {
   std::vector<std::array<uint32_t, 4>> engrams;  // per site: tables, key_proj, value_proj, taps
   uint32_t final_norm = 0;
   uint32_t probe_heads = 0;
+  struct HeadIdx { uint32_t code, probes, gain, query, row_bias, proj, bias; };
+  std::vector<HeadIdx> heads;  // crates/cact/src/layout.rs:236-254
   bool audio = false;
   uint32_t tokenizer = 0;
 };

@@ -224,6 +224,29 @@ __device__ __forceinline__ float sum_of_squares_warp(const float* v, int n) {
   return fadd(s, tail);
 }
 
+// dot_product (ops.rs:19-30) of two n-vectors, n a multiple of 8, the same
+// lane structure as sum_of_squares_warp. Called by one whole warp; every lane
+// returns the sum.
+__device__ __forceinline__ float dot_product_warp(const float* a, const float* b, int n) {
+  const int lane = threadIdx.x & 31;
+  float acc = 0.0f;
+  if (lane < 8) {
+    int i = lane;
+    for (; i + 8 * 15 < n; i += 8 * 16) {
+      float p[16];
+#pragma unroll
+      for (int k = 0; k < 16; ++k) p[k] = fmul(a[i + 8 * k], b[i + 8 * k]);
+#pragma unroll
+      for (int k = 0; k < 16; ++k) acc = fadd(acc, p[k]);
+    }
+    for (; i < n; i += 8) acc = fadd(acc, fmul(a[i], b[i]));
+  }
+  float s = SUM_START;
+#pragma unroll
+  for (int l = 0; l < 8; ++l) s = fadd(s, __shfl_sync(FULL, acc, l));
+  return fadd(s, SUM_START);  // the empty tail
+}
+
 // 1 / sqrt(mean_square + 1e-6) of ops.rs:44-66.
 __device__ __forceinline__ float inverse_rms(float sum_squares, int n) {
   float ms = fdiv(sum_squares, (float)n);

@@ -1913,6 +1913,165 @@ __global__ void __launch_bounds__(128) k_final(ModelDev md, Work w, float* __res
   for (int i = tid; i < d; i += blockDim.x) hidden[(size_t)meta.slot * d + i] = fmul(fmul(fadd(1.0f, md.final_norm[i]), s_mean[i]), s_inv);
 }
 
+// -------------------------------------------------------------- probe heads
+// ProbeHead::observe (heads.rs:127-148) of one cell row (0: the embedding,
+// layer + 1: after that layer) for every token of the pass. grid M, block 128.
+// Each CTA forms its token's cell (lane_mean, session.rs:192-200) and its
+// scores dot(cell, direction) / sqrt(d) for every head and probe; the last
+// CTA of a sequence's run to arrive (a counter per run: fence, then atomic)
+// then runs the online softmax over the run's tokens in position order:
+// peak' = max(peak, score), rescale = exp(peak - peak') (0 while peak is
+// -inf), weight = exp(score - peak'), total = total·rescale + weight,
+// weighted = weighted·rescale + weight·cell, each product separately
+// rounded, exp the libm one.
+__global__ void __launch_bounds__(128) k_observe(ModelDev md, Work w, const float* __restrict__ stream, int M, int row) {
+  __shared__ __align__(16) float s_cell[MAX_D];
+  __shared__ int s_final;
+  pdl_wait();
+  const int t = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, d = (int)md.d_model;
+  if (t >= M) return;
+  const TokenMeta meta = load_meta(w.meta, t);
+  if (meta.slot < 0) return;
+  const float* lanes_t = stream + (size_t)t * LANES * d;
+  for (int i = tid; i < d; i += blockDim.x) {
+    float acc = 0.0f;
+#pragma unroll
+    for (int l = 0; l < LANES; ++l) acc = fadd(acc, fdiv(__ldcg(lanes_t + l * d + i), (float)LANES));
+    s_cell[i] = acc;
+    w.cells[(size_t)t * d + i] = acc;
+  }
+  __syncthreads();
+  int pairs = 0;
+  for (uint32_t h = 0; h < md.num_heads; ++h) pairs += (int)md.head[h].probes;
+  const float root = md.sqrt_d;
+  for (int p = warp; p < pairs; p += blockDim.x >> 5) {
+    int h = 0, k = p;
+    while (k >= (int)md.head[h].probes) k -= (int)md.head[h++].probes;
+    const HeadDev& H = md.head[h];
+    const float dot = dot_product_warp(s_cell, H.directions + ((size_t)row * H.probes + k) * d, d);
+    if (lane == 0) w.scores[(size_t)t * pairs + p] = fdiv(dot, root);
+  }
+  const int run = meta.run & 0xffff, len = meta.run >> 16, first = t - run;
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) s_final = atomicAdd(&w.arrivals[first], 1) == len - 1;
+  __syncthreads();
+  if (!s_final) return;
+  __threadfence();
+  // the scalar recurrence per (head, probe), token by token
+  for (int p = tid; p < pairs; p += blockDim.x) {
+    int h = 0, k = p;
+    while (k >= (int)md.head[h].probes) k -= (int)md.head[h++].probes;
+    const HeadDev& H = md.head[h];
+    const size_t slot = (size_t)meta.slot * (md.num_layers + 1) * H.probes + (size_t)row * H.probes + k;
+    float peak = H.peak[slot], total = H.total[slot];
+    for (int r = 0; r < len; ++r) {
+      const float score = __ldcg(w.scores + (size_t)(first + r) * pairs + p);
+      const float next = fmaxf(peak, score);
+      const float rescale = peak == -INFINITY ? 0.0f : expf_libm(fsub(peak, next));
+      const float weight = expf_libm(fsub(score, next));
+      total = fadd(fmul(total, rescale), weight);
+      w.scan[((size_t)(first + r) * pairs + p) * 2] = rescale;
+      w.scan[((size_t)(first + r) * pairs + p) * 2 + 1] = weight;
+      peak = next;
+    }
+    H.peak[slot] = peak;
+    H.total[slot] = total;
+  }
+  __syncthreads();
+  // the weighted cells, element by element, token by token
+  for (int e = tid; e < pairs * d; e += blockDim.x) {
+    const int p = e / d, i = e % d;
+    int h = 0, k = p;
+    while (k >= (int)md.head[h].probes) k -= (int)md.head[h++].probes;
+    const HeadDev& H = md.head[h];
+    float* target = H.weighted + ((size_t)meta.slot * (md.num_layers + 1) * H.probes + (size_t)row * H.probes + k) * d + i;
+    float v = *target;
+    for (int r = 0; r < len; ++r) {
+      const float* rw = w.scan + ((size_t)(first + r) * pairs + p) * 2;
+      v = fadd(fmul(v, rw[0]), fmul(rw[1], __ldcg(w.cells + (size_t)(first + r) * d + i)));
+    }
+    *target = v;
+  }
+  if (tid == 0) w.arrivals[first] = 0;  // ready for the next use
+}
+
+// ProbeHead::pooled (heads.rs:85-115) of one session's head h over the model's
+// rows (the embedding cell and its active layers): readouts unit_rms(weighted
+// / total) · gain into `readouts`, then per query the softmax (ops.rs:92-101)
+// of dot(readout, query) / sqrt(d) + row bias over the slots, and the
+// weighted sum of the readouts in slot order into `pooled`. One CTA of 256.
+__global__ void __launch_bounds__(256) k_head_pool(ModelDev md, int h, int slot, const int32_t* __restrict__ rows, int nrows,
+                                                   float* __restrict__ readouts, float* __restrict__ weights, float* __restrict__ pooled) {
+  const HeadDev& H = md.head[h];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, d = (int)md.d_model, P = (int)H.probes, slots = nrows * P;
+  const int all = (int)(md.num_layers + 1) * P;
+  const size_t base = (size_t)slot * all;
+  // readouts: averaged = weighted · (1 / total), then unit_rms and the gain
+  for (int s = warp; s < slots; s += 8) {
+    const int a = rows[s / P] * P + s % P;
+    const float inverse = fdiv(1.0f, H.total[base + a]);
+    float* out = readouts + (size_t)s * d;
+    for (int i = lane; i < d; i += 32) out[i] = fmul(H.weighted[(base + a) * d + i], inverse);
+    __syncwarp();
+    const float inv = inverse_rms(sum_of_squares_warp(out, d), d);
+    const float gain = H.gain[a];
+    for (int i = lane; i < d; i += 32) out[i] = fmul(fmul(out[i], inv), gain);
+  }
+  __syncthreads();
+  for (int q = 0; q < (int)H.queries; ++q) {
+    for (int s = warp; s < slots; s += 8) {
+      const float dot = dot_product_warp(readouts + (size_t)s * d, H.query + (size_t)q * d, d);
+      if (lane == 0) weights[s] = fadd(fdiv(dot, md.sqrt_d), H.row_bias[(size_t)q * all + rows[s / P] * P + s % P]);
+    }
+    __syncthreads();
+    if (tid == 0) {  // softmax_in_place: peak, fast_exp and the total in order, then 1 / total
+      float peak = -INFINITY;
+      for (int s = 0; s < slots; ++s) peak = fmaxf(peak, weights[s]);
+      float total = 0.0f;
+      for (int s = 0; s < slots; ++s) {
+        weights[s] = fast_exp(fsub(weights[s], peak));
+        total = fadd(total, weights[s]);
+      }
+      const float inverse = fdiv(1.0f, total);
+      for (int s = 0; s < slots; ++s) weights[s] = fmul(weights[s], inverse);
+    }
+    __syncthreads();
+    for (int i = tid; i < d; i += blockDim.x) {
+      float acc = 0.0f;
+      for (int s = 0; s < slots; ++s) acc = fadd(acc, fmul(weights[s], readouts[(size_t)s * d + i]));
+      pooled[(size_t)q * d + i] = acc;
+    }
+    __syncthreads();
+  }
+}
+
+// out[i] += bias[i] (heads.rs:121-123). One CTA.
+__global__ void k_add_bias(float* __restrict__ out, const float* __restrict__ bias, int n) {
+  for (int i = threadIdx.x; i < n; i += blockDim.x) out[i] = fadd(out[i], bias[i]);
+}
+
+// dense() (heads.rs:20-28): rows of a codebook matrix dequantised to f32 like
+// QuantisedMatrix::dequantise_row (matrix.rs:140-153). grid rows, block 128.
+__global__ void __launch_bounds__(128) k_dense_rows(const uint8_t* __restrict__ packed, uint32_t row_bytes, uint32_t bits,
+                                                    const float* __restrict__ levels, const float* __restrict__ norms, int cols,
+                                                    float inv_sqrt_group, float* __restrict__ out) {
+  const int r = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31, groups = cols / GROUP;
+  const uint8_t* row = packed + (size_t)r * row_bytes;
+  for (int g = warp; g < groups; g += 4) {
+    const float norm = norms[(size_t)r * groups + g];
+    float v[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) v[j] = fmul(levels[code_at(row, g * GROUP + 4 * lane + j, bits)], norm);
+    fwht128(v, inv_sqrt_group);
+    *reinterpret_cast<float4*>(out + (size_t)r * cols + g * GROUP + 4 * lane) = make_float4(v[0], v[1], v[2], v[3]);
+  }
+}
+
+__global__ void k_fill(float* __restrict__ p, size_t n, float value) {
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) p[i] = value;
+}
+
 // ------------------------------------------------------------------ select
 // argmax / argmax_allowed (generator.rs:147-165): the first index holding the
 // maximum over the allowed ids, or over all ids when none is allowed.
@@ -2214,6 +2373,34 @@ void launch_layer(const ModelDev& md, const LayerDev& L, const Work& w, const Kv
            md.inv_sqrt_group, 1, 0);
   project(L.out, w.act, w.act_scale, w.outp, M, d, w.meta, st, md.error);
   launch_block(md, L, w, M, st);
+}
+
+void launch_observe(const ModelDev& md, const Work& w, const float* stream, int M, int row, cudaStream_t st) {
+  t_pass_tokens = M;
+  launch(k_observe, M, 128, 0, st, md, w, stream, M, row);
+}
+
+void head_output(const ModelDev& md, int h, int slot, const int32_t* rows, int nrows, float* readouts, float* weights, float* pooled,
+                 int8_t* act, float* act_scale, int act_rows, float* out, bool project_out, cudaStream_t st) {
+  const HeadDev& H = md.head[h];
+  k_head_pool<<<1, 256, 0, st>>>(md, h, slot, rows, nrows, readouts, weights, pooled);
+  if (!project_out) return;
+  // ProbeHead::project (heads.rs:117-125): rotate and quantise per group (no
+  // fake quantisation), the product, then the bias
+  const int K = (int)H.queries * (int)md.d_model;
+  k_prep<<<1, 128, 0, st>>>(pooled, K, (const int32_t*)nullptr, (const float*)nullptr, 0, K, act, act_scale, 1, (const TokenMeta*)nullptr,
+                            md.inv_sqrt_group, 0, act_rows);
+  project(H.proj, act, act_scale, out, 1, (int)H.proj.rows, nullptr, st, md.error, act_rows);
+  k_add_bias<<<1, 128, 0, st>>>(out, H.bias, (int)H.outputs);
+}
+
+void dense_rows(const uint8_t* packed, uint32_t row_bytes, uint32_t bits, const float* levels, const float* norms, int rows, int cols,
+                float inv_sqrt_group, float* out, cudaStream_t st) {
+  k_dense_rows<<<rows, 128, 0, st>>>(packed, row_bytes, bits, levels, norms, cols, inv_sqrt_group, out);
+}
+
+void fill(float* p, size_t n, float value, cudaStream_t st) {
+  if (n) k_fill<<<(unsigned)std::min<size_t>((n + 255) / 256, 1184), 256, 0, st>>>(p, n, value);
 }
 
 void launch_final(const ModelDev& md, const Work& w, float* hidden, int M, cudaStream_t st) {

@@ -31,6 +31,14 @@
 // raw values of its last (taps - 1) · dilation positions sit in the site's
 // ring [slots][rows][d] at row position % rows; its last (max order - 1)
 // token ids in token_ring[slots][rows] at position % rows.
+//
+// Probe heads (models/src/heads.rs): per head the probe directions and query
+// rows dequantised to f32 ([rows = layers + 1][probes][d], [queries][d]), the
+// gains and row biases, the projection as a product (K = queries · d
+// zero-padded to 512 or 2048), and per session slot the online-softmax
+// accumulators peak, total [rows][probes] and weighted [rows][probes][d], all
+// indexed by the archive row (0 = the embedding cell, layer + 1), so every
+// depth uses its subset.
 #pragma once
 
 #include <stddef.h>
@@ -115,6 +123,19 @@ struct EngramDev {
   float* ring;             // [slots][ring_rows][d]; null when ring_rows == 0
 };
 
+struct HeadDev {
+  int code;
+  uint32_t probes, queries, outputs;  // probes per row
+  const float* directions;  // [layers + 1][probes][d]
+  const float* gain;        // [layers + 1][probes]
+  const float* query;       // [queries][d]
+  const float* row_bias;    // [queries][(layers + 1) · probes]
+  QMat proj;                // outputs × queries · d (padded)
+  const float* bias;        // [outputs]
+  float *peak, *total, *weighted;  // per slot: [(layers + 1) · probes], the same, × d
+};
+constexpr int MAX_PROBE_HEADS = 4;
+
 struct LayerDev {
   QMat qkvg;  // q, k, v and gate_proj stacked row-wise (one fused product, matrix.rs:167-193)
   QMat out;
@@ -158,6 +179,9 @@ struct ModelDev {
   uint32_t engram_conv_taps, engram_dilation, engram_ring_rows, engram_k;  // engram_k: the padded product K
   uint32_t* token_ring;       // [slots][token_rows]; null when token_rows == 0
   uint32_t token_rows;        // max order - 1
+  // probe heads
+  uint32_t num_heads;
+  HeadDev head[MAX_PROBE_HEADS];
 };
 
 // Per-token metadata of one forward pass.
@@ -165,7 +189,7 @@ struct TokenMeta {
   int32_t slot;      // session slot (page table row)
   int32_t position;  // absolute position of this token
   int32_t last;      // 1 when this is the sequence's last token in the pass
-  int32_t pad;
+  int32_t run;       // bits 0-15: the token's index in its sequence's run of this pass; 16-31: the run's length
 };
 
 // Device workspace of a forward pass over at most `capacity` tokens.
@@ -188,6 +212,9 @@ struct Work {
   int* arrivals;            // [M] attention CTAs done per token (zero between passes)
   float* engram_kv;         // [M][2d] an engram site's key and raw value rows (null without sites)
   float* xin;               // [M][d] the routing input at an engram site layer (x holds it plus the engram term)
+  float* cells;             // [M][d] a layer's lane means (probe heads)
+  float* scores;            // [M][heads · probes] their probe scores / sqrt(d)
+  float* scan;              // [M][heads · probes][2] the run's rescale and weight per token
   uint32_t act_rows;        // rows of the activation buffer's K-chunk-major layout
 };
 

@@ -191,6 +191,13 @@ struct Engine {
   size_t conv_ring_floats = 0;  // per slot: md.conv_ring's [layers][taps - 1][q | k | v]
   std::vector<EngramDev> engram_sites;
   uint32_t act_groups = 0;  // act_scale floats per token: the widest product's groups
+  // probe heads: (head, probe) pairs, the widest projection K, the most slots per session
+  uint32_t head_pairs = 0, head_k = 0;
+  size_t head_slots = 0;
+  int32_t* d_head_rows = nullptr;
+  float *d_head_readouts = nullptr, *d_head_weights = nullptr, *d_head_pooled = nullptr, *d_head_scale = nullptr, *d_head_out = nullptr;
+  int8_t* d_head_act = nullptr;
+  PinnedBuffer h_head;
   // forward workspace
   uint32_t capacity = 0;
   Work work{};
@@ -649,6 +656,62 @@ std::shared_ptr<Engine> open_engine(const char* path, const nb_options* opt) {
     sites.push_back(S);
   }
 
+  // probe heads (heads.rs:29-50): directions and queries dequantised to f32
+  // on the device, gains and biases, the projection as a product
+  if (lay.heads.size() > (size_t)MAX_PROBE_HEADS) fail(NB_ERR_UNSUPPORTED, "more than 4 probe heads are not implemented");
+  md.num_heads = (uint32_t)lay.heads.size();
+  for (size_t hi = 0; hi < lay.heads.size(); ++hi) {
+    const nba::Layout::HeadIdx& t = lay.heads[hi];
+    HeadDev& H = md.head[hi];
+    H.code = (int)t.code;
+    auto dense = [&](uint32_t index, const char* what) {
+      const nba::Record& r = a.record(index);
+      if (r.kind != nba::CODEBOOK || r.columns() != d || r.group() != GROUP)
+        fail(NB_ERR_UNSUPPORTED, std::string("probe head ") + what + " must be codebook rows of d_model values in 128-groups");
+      Levels lv = levels_for(r.bits, a.codebook(), GROUP);
+      const uint64_t n = r.rows() * r.groups_per_row();
+      if (r.packed_bytes() + n * 2 > r.byte_len) fail(NB_ERR_ARCHIVE, std::string("probe head ") + what + " is shorter than its shape");
+      std::vector<float> norms(n);
+      const uint8_t* nb = a.data(index) + r.packed_bytes();
+      for (uint64_t i = 0; i < n; ++i) {
+        uint16_t h;
+        std::memcpy(&h, nb + 2 * i, 2);
+        norms[i] = nba::half_to_f32(h);
+      }
+      const uint8_t* packed = A.upload(std::vector<uint8_t>(a.data(index), a.data(index) + r.packed_bytes()), st);
+      const float* levels = A.upload(std::vector<float>(lv.values, lv.values + 16), st);
+      float* out = A.alloc<float>((size_t)r.rows() * d);
+      nbk::dense_rows(packed, (uint32_t)r.packed_row_bytes(), lv.bits, levels, A.upload(norms, st), (int)r.rows(), (int)d, md.inv_sqrt_group,
+                      out, st);
+      return std::make_pair(out, (uint32_t)r.rows());
+    };
+    auto probes = dense(t.probes, "probes");
+    if (probes.second % (L + 1)) fail(NB_ERR_ARCHIVE, "probe head rows are not a whole number per layer");
+    H.probes = probes.second / (L + 1);
+    H.directions = probes.first;
+    auto query = dense(t.query, "query");
+    H.queries = query.second;
+    H.query = query.first;
+    const uint32_t all = (L + 1) * H.probes, K = H.queries * d;
+    H.gain = A.upload(floats_of(a, t.gain, all, "probe head gain"), st);
+    H.row_bias = A.upload(floats_of(a, t.row_bias, (size_t)H.queries * all, "probe head row_bias"), st);
+    const nba::Record& pr = a.record(t.proj);
+    if (pr.kind != nba::CODEBOOK || pr.columns() != K || pr.group() != GROUP || K > 2048)
+      fail(NB_ERR_UNSUPPORTED, "probe head projection must take queries x d_model <= 2048 columns in 128-groups");
+    H.outputs = (uint32_t)pr.rows();
+    if (H.outputs == 0 || H.outputs > 4096) fail(NB_ERR_UNSUPPORTED, "probe head projections of more than 4096 outputs are not implemented");
+    Levels lp = levels_for(pr.bits, a.codebook(), GROUP);
+    const uint32_t KP = K <= 512 ? 512 : 2048, kg = K / GROUP, pg = KP / GROUP;
+    std::vector<int8_t> codes((size_t)((H.outputs + 127) / 128 * 128) * KP, 0);
+    std::vector<float> scales;
+    expand_matrix(a, t.proj, lp, true, codes, scales, 0, H.outputs);
+    std::vector<float> padded((size_t)H.outputs * pg, 0.0f);
+    for (uint32_t r = 0; r < H.outputs; ++r)
+      for (uint32_t gi = 0; gi < kg; ++gi) padded[(size_t)r * pg + gi] = scales[(size_t)r * kg + gi];
+    H.proj = QMat{A.upload(codes, st), A.upload(padded, st), lp.int_scale, H.outputs, KP, pg, lp.fused ? 1 : 0};
+    H.bias = A.upload(floats_of(a, t.bias, H.outputs, "probe head bias"), st);
+  }
+
   // sessions, KV pool, workspace
   E->max_sessions = opt && opt->max_sessions ? opt->max_sessions : 256;
   E->max_pages = (g.max_seq_len + PAGE_POSITIONS - 1) / PAGE_POSITIONS;
@@ -670,6 +733,28 @@ std::shared_ptr<Engine> open_engine(const char* path, const nb_options* opt) {
   for (uint32_t s = E->max_sessions; s-- > 0;) E->free_slots.push_back(s);
   E->d_hidden = A.alloc<float>((size_t)E->max_sessions * d);
   NB_CUDA(cudaMemsetAsync(E->d_hidden, 0, (size_t)E->max_sessions * d * 4, st));
+  for (uint32_t hi = 0; hi < md.num_heads; ++hi) {  // ProbeAccumulator (heads.rs:151-156) per slot
+    HeadDev& H = md.head[hi];
+    const size_t all = (size_t)(L + 1) * H.probes;
+    H.peak = A.alloc<float>(E->max_sessions * all);
+    H.total = A.alloc<float>(E->max_sessions * all);
+    H.weighted = A.alloc<float>(E->max_sessions * all * d);
+    E->head_pairs += H.probes;
+    E->head_k = std::max<uint32_t>(E->head_k, H.proj.cols);
+    E->head_slots = std::max<size_t>(E->head_slots, all);
+  }
+  if (md.num_heads) {
+    E->d_head_rows = A.alloc<int32_t>(L + 1);
+    E->d_head_readouts = A.alloc<float>(E->head_slots * d);
+    E->d_head_weights = A.alloc<float>(E->head_slots);
+    E->d_head_pooled = A.alloc<float>(E->head_k);
+    E->d_head_act = A.alloc<int8_t>((size_t)128 * E->head_k);
+    NB_CUDA(cudaMemsetAsync(E->d_head_act, 0, (size_t)128 * E->head_k, st));
+    E->d_head_scale = A.alloc<float>(E->head_k / GROUP);
+    NB_CUDA(cudaMemsetAsync(E->d_head_scale, 0, (E->head_k / GROUP) * 4, st));
+    E->d_head_out = A.alloc<float>(std::max<size_t>(E->head_k, 4096));
+    E->h_head.ensure(std::max<size_t>(E->head_k, 4096) * 4);
+  }
   for (EngramDev& S : sites)
     if (md.engram_ring_rows) {
       S.ring = A.alloc<float>((size_t)E->max_sessions * md.engram_ring_rows * d);
@@ -712,6 +797,12 @@ std::shared_ptr<Engine> open_engine(const char* path, const nb_options* opt) {
   if (!sites.empty()) {
     w.engram_kv = A.alloc<float>((size_t)M * 2 * d);
     w.xin = A.alloc<float>((size_t)M * d);
+  }
+  if (md.num_heads) {
+    if (M > 0xffff) fail(NB_ERR_ARGUMENT, "passes of more than 65535 tokens are not supported with probe heads");
+    w.cells = A.alloc<float>((size_t)M * d);
+    w.scores = A.alloc<float>((size_t)M * E->head_pairs);
+    w.scan = A.alloc<float>((size_t)M * E->head_pairs * 2);
   }
   w.act = A.alloc<int8_t>(act_rows * actw);
   NB_CUDA(cudaMemsetAsync(w.act, 0, act_rows * actw, st));
@@ -765,7 +856,14 @@ void forward(Engine& E, const std::vector<int32_t>& active, const TokenSpec* spe
   TokenMeta* hm = E.h_meta.as<TokenMeta>();
   for (uint32_t i = 0; i < count; ++i) {
     ht[i] = specs[i].token;
-    hm[i] = TokenMeta{(int32_t)specs[i].slot, (int32_t)specs[i].position, specs[i].last ? 1 : 0, 0};
+    const bool continues = i > 0 && specs[i - 1].slot == specs[i].slot && specs[i - 1].position + 1 == specs[i].position;
+    const int32_t run = continues ? (hm[i - 1].run & 0xffff) + 1 : 0;
+    hm[i] = TokenMeta{(int32_t)specs[i].slot, (int32_t)specs[i].position, specs[i].last ? 1 : 0, run};
+  }
+  for (uint32_t i = count; i-- > 0;) {  // the run's length into every token of it
+    const bool ends = i + 1 == count || (hm[i + 1].run & 0xffff) == 0;
+    const int32_t len = ends ? (hm[i].run & 0xffff) + 1 : hm[i + 1].run >> 16;
+    hm[i].run = (hm[i].run & 0xffff) | (len << 16);
   }
   NB_CUDA(cudaMemcpyAsync(E.d_tokens, ht, count * 4, cudaMemcpyHostToDevice, E.stream));
   NB_CUDA(cudaMemcpyAsync(E.d_meta, hm, count * sizeof(TokenMeta), cudaMemcpyHostToDevice, E.stream));
@@ -780,10 +878,12 @@ void forward(Engine& E, const std::vector<int32_t>& active, const TokenSpec* spe
     seen[specs[i].slot] = 1;
   }
   nbk::launch_embed(E.md, w, (int)count, E.stream);
+  if (E.md.num_heads) nbk::launch_observe(E.md, w, w.stream, (int)count, 0, E.stream);
   for (size_t slot = 0; slot < active.size(); ++slot) {
     int layer = active[slot];
     nbk::launch_layer(E.md, E.layers[layer], w, kv, (int)count, layer, (int)slot, E.t_cap, distinct, E.stream);
     std::swap(w.stream, w.next_stream);
+    if (E.md.num_heads) nbk::launch_observe(E.md, w, w.stream, (int)count, layer + 1, E.stream);
   }
   nbk::launch_final(E.md, w, E.d_hidden, (int)count, E.stream);
   NB_CUDA(cudaGetLastError());
@@ -936,6 +1036,13 @@ nb_status nb_session_create(nb_model* model, nb_session** out) {
     s->slot = E.free_slots.back();
     E.free_slots.pop_back();
     NB_CUDA(cudaMemsetAsync(E.d_hidden + (size_t)s->slot * E.md.d_model, 0, E.md.d_model * 4, E.stream));
+    for (uint32_t h = 0; h < E.md.num_heads; ++h) {  // ProbeHead::accumulator (heads.rs:80-83)
+      const HeadDev& H = E.md.head[h];
+      const size_t all = (size_t)(E.md.num_layers + 1) * H.probes;
+      nbk::fill(H.peak + s->slot * all, all, -INFINITY, E.stream);
+      NB_CUDA(cudaMemsetAsync(H.total + s->slot * all, 0, all * 4, E.stream));
+      NB_CUDA(cudaMemsetAsync(H.weighted + s->slot * all * E.md.d_model, 0, all * E.md.d_model * 4, E.stream));
+    }
     *out = s;
   });
 }
@@ -962,6 +1069,14 @@ nb_status nb_session_clone(const nb_session* session, nb_session** out) {
     NB_CUDA(cudaMemcpyAsync(E.d_hidden + (size_t)s->slot * E.md.d_model, E.d_hidden + (size_t)session->slot * E.md.d_model,
                             E.md.d_model * 4, cudaMemcpyDeviceToDevice, E.stream));
     const size_t d = E.md.d_model;
+    for (uint32_t h = 0; h < E.md.num_heads; ++h) {  // the probe accumulators are part of the session (session.rs:26)
+      const HeadDev& H = E.md.head[h];
+      const size_t all = (size_t)(E.md.num_layers + 1) * H.probes;
+      NB_CUDA(cudaMemcpyAsync(H.peak + s->slot * all, H.peak + session->slot * all, all * 4, cudaMemcpyDeviceToDevice, E.stream));
+      NB_CUDA(cudaMemcpyAsync(H.total + s->slot * all, H.total + session->slot * all, all * 4, cudaMemcpyDeviceToDevice, E.stream));
+      NB_CUDA(cudaMemcpyAsync(H.weighted + s->slot * all * d, H.weighted + session->slot * all * d, all * d * 4, cudaMemcpyDeviceToDevice,
+                              E.stream));
+    }
     for (const EngramDev& S : E.engram_sites)  // EngramSiteState is part of the session (session.rs:22)
       if (S.ring)
         NB_CUDA(cudaMemcpyAsync(S.ring + (size_t)s->slot * E.md.engram_ring_rows * d, S.ring + (size_t)session->slot * E.md.engram_ring_rows * d,
@@ -1016,6 +1131,45 @@ static void raise_device_error(Engine& E) {
     NB_CUDA(cudaMemsetAsync(E.d_error, 0, sizeof(int), E.stream));
     fail(NB_ERR_TIMEOUT, "a bounded device wait gave up");
   }
+}
+
+// Session::head_output / pooled_readout (session.rs:150-160).
+static nb_status head_values(nb_session* session, uint32_t code, float* out, size_t capacity, size_t* count, bool project_out) {
+  if (!session || (!out && capacity)) return NB_ERR_ARGUMENT;
+  return guard([&] {
+    Engine& E = *session->engine;
+    std::lock_guard<std::mutex> lock(E.mutex);
+    int h = -1;
+    for (uint32_t i = 0; i < E.md.num_heads && h < 0; ++i)
+      if ((uint32_t)E.md.head[i].code == code) h = (int)i;
+    if (h < 0) fail(NB_ERR_ARGUMENT, "the model has no probe head with code " + std::to_string(code));
+    NB_CUDA(cudaSetDevice(E.device));
+    E.settle();
+    const HeadDev& H = E.md.head[h];
+    std::vector<int32_t> rows{0};
+    for (int32_t l : session->active) rows.push_back(l + 1);
+    int32_t* hr = E.h_head.as<int32_t>();
+    std::copy(rows.begin(), rows.end(), hr);
+    NB_CUDA(cudaMemcpyAsync(E.d_head_rows, hr, rows.size() * 4, cudaMemcpyHostToDevice, E.stream));
+    nbk::head_output(E.md, h, (int)session->slot, E.d_head_rows, (int)rows.size(), E.d_head_readouts, E.d_head_weights, E.d_head_pooled,
+                     E.d_head_act, E.d_head_scale, 128, E.d_head_out, project_out, E.stream);
+    const size_t n = project_out ? H.outputs : (size_t)H.queries * E.md.d_model;
+    float* staged = E.h_head.as<float>();
+    NB_CUDA(cudaMemcpyAsync(staged, project_out ? E.d_head_out : E.d_head_pooled, n * 4, cudaMemcpyDeviceToHost, E.stream));
+    queue_error_read(E);
+    NB_CUDA(cudaStreamSynchronize(E.stream));
+    raise_device_error(E);
+    std::copy(staged, staged + std::min(n, capacity), out);
+    if (count) *count = n;
+  });
+}
+
+nb_status nb_session_head_output(nb_session* session, uint32_t code, float* out, size_t capacity, size_t* count) {
+  return head_values(session, code, out, capacity, count, true);
+}
+
+nb_status nb_session_pooled_readout(nb_session* session, uint32_t code, float* out, size_t capacity, size_t* count) {
+  return head_values(session, code, out, capacity, count, false);
 }
 
 static void run_tokens(nb_session* s, const uint32_t* ids, size_t count) {
@@ -1143,6 +1297,9 @@ static Work work_rows(const Engine& E, const Work& w, uint32_t b0) {
   s.act_scale = w.act_scale + b0 * E.act_groups;
   s.engram_kv = w.engram_kv ? w.engram_kv + b0 * 2 * d : nullptr;
   s.xin = w.xin ? w.xin + b0 * d : nullptr;
+  s.cells = w.cells ? w.cells + b0 * d : nullptr;
+  s.scores = w.scores ? w.scores + b0 * E.head_pairs : nullptr;
+  s.scan = w.scan ? w.scan + b0 * E.head_pairs * 2 : nullptr;
   s.proj = w.proj + b0 * (2 * H + 2 * KV) * HEAD_DIM;
   s.qcodes = w.qcodes + b0 * H * HEAD_DIM;
   s.qscale = w.qscale + b0 * H;
@@ -1172,10 +1329,12 @@ static void build_group(nb_batch* b, bool masked, bool stats, uint32_t b0, uint3
   Work w = work_rows(E, base, b0);
   KvDev kv = E.kv();
   nbk::launch_embed(E.md, w, n, st);
+  if (E.md.num_heads) nbk::launch_observe(E.md, w, w.stream, n, 0, st);
   for (size_t slot = 0; slot < b->active.size(); ++slot) {
     int layer = b->active[slot];
     nbk::launch_layer(E.md, E.layers[layer], w, kv, n, layer, (int)slot, E.t_cap, true, st);
     std::swap(w.stream, w.next_stream);
+    if (E.md.num_heads) nbk::launch_observe(E.md, w, w.stream, n, layer + 1, st);
   }
   nbk::launch_final(E.md, w, E.d_hidden, n, st);
   nbk::launch_advance(b->d_meta + b0, n, st);
@@ -1288,7 +1447,7 @@ static uint32_t stage_step(nb_batch* b) {
     // generator.rs:99: a step needs session.len() + 1 < max_seq_len
     bool ok = s->length + 1 < E.geo.max_seq_len;
     ha[i] = ok ? 1 : 0;
-    hm[i] = TokenMeta{ok ? (int32_t)s->slot : -1, (int32_t)s->length, 1, 0};
+    hm[i] = TokenMeta{ok ? (int32_t)s->slot : -1, (int32_t)s->length, 1, 1 << 16};
     if (ok) {
       E.prepare_append(s->slot, b->active, s->length);
       ++live;
@@ -1676,7 +1835,7 @@ extern "C" nb_status nb_debug_time_attention(nb_batch* batch, uint32_t reps, flo
     for (uint32_t i = 0; i < B; ++i) {
       nb_session* s = batch->sessions[i];
       uint32_t pos = s->length ? s->length - 1 : 0;
-      hm[i] = TokenMeta{(int32_t)s->slot, (int32_t)pos, 1, 0};
+      hm[i] = TokenMeta{(int32_t)s->slot, (int32_t)pos, 1, 1 << 16};
       bytes += (double)(pos + 1) * per_position;
     }
     NB_CUDA(cudaMemcpyAsync(batch->d_meta, hm, B * sizeof(TokenMeta), cudaMemcpyHostToDevice, E.stream));

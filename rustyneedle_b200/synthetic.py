@@ -9,7 +9,8 @@ tensors follow the canonical positional order of crates/cact/src/layout.rs:190-2
 embedding; per layer norm_in, q, k, v, [q, k, v conv taps], q_norm, k_norm, gate_proj, out_proj,
 post_norm, attn_gate, pre_hada and 13 Hadamard tensors; nine lane tensors; two
 Hadamard permutations; [per engram site: tables, key_proj, value_proj, taps];
-final_norm; the tokenizer blob.
+final_norm; [the probe-head manifest and each head's probes, gain, query,
+row_bias, proj, bias (and calibration for code 3)]; the tokenizer blob.
 
 Weights are codebook-quantised (kind 3): uniform indices, packed least
 significant bit first, and one fp16 norm per row drawn log-uniform in
@@ -76,6 +77,10 @@ class Geometry:
     engram_conv_taps: int = 3
     engram_dilation: int = 2
     engram_seed_heads: int = 0
+    probe_heads: tuple = ()   # head manifest codes (1, 2 or 3)
+    probes_per_layer: int = 2
+    head_queries: int = 2
+    head_outputs: int = 3
     extra: dict = field(default_factory=dict)
 
 
@@ -246,6 +251,18 @@ def write_archive(path: str, seed: int = 0, geometry: Geometry | None = None) ->
             taps[0] += 1.0
             w.single(taps)
     w.single(zeros(d))  # final_norm
+    if g.probe_heads:  # crates/cact/src/layout.rs:236-254: manifest, then per head 6 tensors (+ calibration for code 3)
+        w.add(KIND_HALF, (len(g.probe_heads),), np.array(g.probe_heads, dtype=np.float16).tobytes())
+        slots = (L + 1) * g.probes_per_layer
+        for code in g.probe_heads:
+            w.codebook_matrix(rng, slots, d, g.embedding_bits, g.group)  # probes
+            w.single(1.0 + 0.1 * rng.standard_normal(slots))  # gain
+            w.codebook_matrix(rng, g.head_queries, d, g.embedding_bits, g.group)  # query
+            w.single(0.5 * rng.standard_normal(g.head_queries * slots))  # row_bias
+            w.codebook_matrix(rng, g.head_outputs, g.head_queries * d, g.projection_bits, g.group)  # proj
+            w.single(0.1 * rng.standard_normal(g.head_outputs))  # bias
+            if code == 3:
+                w.single(rng.standard_normal(4))  # calibration
     w.add(KIND_RAW, (0,), tokenizer_blob(g.vocab))
 
     header = [FORMAT_TAG, len(w.records), codebook.size, 0, 8, g.vocab, g.out_vocab, d, H, KV, L, hd, hd,

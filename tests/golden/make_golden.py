@@ -64,6 +64,7 @@ def main() -> None:
 
     prefill = read("crates/model/tests/prefill.rs")
     pcos = float(re.search(r"cosine\(&a, &b\) > ([\d.]+)", prefill).group(1))
+    htol = float(re.search(r"\(ha - hb\)\.abs\(\) < ([\d.]+)", prefill).group(1))
     dcos = float(re.search(r"cosine\(&a\.logits\(\), &b\.logits\(\)\) > ([\d.]+)", depth).group(1))
 
     kats = {
@@ -82,6 +83,7 @@ def main() -> None:
                      "tolerance": ftol},
         "softmax": {"logits": logits, "tolerance": stol},
         "prefill_cosine": pcos,
+        "prefill_head_tolerance": htol,
         "full_depth_cosine": dcos,
     }
     with open(OUT, "w") as f:

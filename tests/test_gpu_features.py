@@ -1,10 +1,11 @@
 """Parity of the archive features the default synthetic geometry leaves out:
 QKV causal convolution taps (model/src/attention.rs:83-117, 243-276), the
-sliding window with global layers (attention.rs:171-177) and engram sites
-(model/src/engram.rs, session.rs:93-113, 180-190). The archives are 6-layer
+sliding window with global layers (attention.rs:171-177), engram sites
+(model/src/engram.rs, session.rs:93-113, 180-190) and probe heads
+(model/src/heads.rs, session.rs:144-160). The archives are 6-layer
 synthetic models with 3 taps, a 40-position window and layers 0 and 5
-global, plus engram sites for the second half; every case is bit-exact
-against the CPU restatement in INT mode."""
+global, with engram sites and probe heads added in the later groups; every
+case is bit-exact against the CPU restatement in INT mode."""
 
 import numpy as np
 import pytest
@@ -340,4 +341,139 @@ def test_engram_variants(native_built, oracle_lib, variant):
     for s, o in zip(sessions, oracles):
         assert _bits_equal(s.logits(), o.logits())
         s.close()
+    model.close()
+
+
+# -------------------------------------------------------------- probe heads
+def _heads_geometry(**kw):
+    base = dict(probe_heads=(2, 3), probes_per_layer=2, head_queries=2, head_outputs=3)
+    base.update(kw)
+    return _engram_geometry(**base)
+
+
+@pytest.fixture(scope="module")
+def heads_path():
+    from rustyneedle_b200 import synthetic
+
+    return synthetic.cached_archive(seed=16, geometry=_heads_geometry())
+
+
+@pytest.fixture(scope="module")
+def heads_model(native_built, heads_path):
+    import rustyneedle_b200 as nb
+
+    return nb.Model.open(heads_path, max_sessions=96)
+
+
+@pytest.fixture(scope="module")
+def heads_oracle(oracle_lib, heads_path):
+    return oracle_lib.Model.open(heads_path, oracle_lib.MODE_INT, 0)
+
+
+def _heads_equal(s, o):
+    for code in (2, 3):
+        got, want = s.head_output(code), o.head_output(code)
+        assert _bits_equal(got, want), (code, _mismatch(got, want))
+        got, want = s.pooled_readout(code), o.pooled_readout(code)
+        assert _bits_equal(got, want), (code, _mismatch(got, want))
+    assert s.head_output(1) is None and o.head_output(1) is None
+
+
+def test_heads_after_prefill_ragged_feeds_and_steps(heads_model, heads_oracle, oracle_lib):
+    """ProbeHead::observe over a 90-token pass (one run: the online softmax in
+    position order), ragged feeds and greedy steps; head_output and
+    pooled_readout of heads 2 and 3 (code 3 carries a calibration tensor)."""
+    import rustyneedle_b200 as nb
+
+    s = nb.Session(heads_model)
+    o = oracle_lib.Session(heads_oracle)
+    ids = prompt_ids(51, 90)
+    s.feed(ids)
+    o.feed(ids)
+    _heads_equal(s, o)
+    more = prompt_ids(52, 12)
+    at = 0
+    for n in (1, 3, 7, 1):
+        s.feed(more[at:at + n])
+        o.feed(more[at:at + n])
+        at += n
+    for _ in range(5):
+        token = oracle_lib.argmax(o.logits())
+        o.push(token)
+        assert s.step() == token
+    _heads_equal(s, o)
+    c, oc = s.clone(), o.clone()
+    c.push(21)
+    oc.push(21)
+    _heads_equal(c, oc)
+    _heads_equal(s, o)
+    s.close()
+    c.close()
+
+
+def test_heads_over_small_passes_and_a_shallow_depth(native_built, heads_path, heads_oracle, oracle_lib):
+    """max_batch_tokens 5 splits one prompt over many passes (each a run of its
+    own); depth 3 pools the embedding cell and its three layers only."""
+    import rustyneedle_b200 as nb
+
+    model = nb.Model.open(heads_path, max_sessions=4, max_batch_tokens=5)
+    ids = prompt_ids(53, 47)
+    for depth in (6, 3):
+        m = model if depth == 6 else model.with_depth(depth)
+        om = heads_oracle if depth == 6 else heads_oracle.with_depth(depth)
+        s = nb.Session(m)
+        s.feed(ids)
+        o = oracle_lib.Session(om)
+        o.feed(ids)
+        _heads_equal(s, o)
+        s.close()
+    model.close()
+
+
+@pytest.mark.parametrize("count", [6, 72])
+def test_heads_after_batched_decode(heads_model, heads_oracle, oracle_lib, count):
+    import rustyneedle_b200 as nb
+
+    base = [1, 4, 9, 30]
+    lengths = (base * (count // len(base) + 1))[:count]
+    sessions, oracles = [], []
+    for i, n in enumerate(lengths):
+        ids = prompt_ids(1000 + i, n)
+        s = nb.Session(heads_model)
+        s.feed(ids)
+        sessions.append(s)
+        o = oracle_lib.Session(heads_oracle)
+        o.feed(ids)
+        oracles.append(o)
+    batch = nb.Batch(heads_model, sessions)
+    for _ in range(3):
+        got = batch.step()
+        want = []
+        for o in oracles:
+            token = oracle_lib.argmax(o.logits())
+            o.push(token)
+            want.append(token)
+        assert list(got) == want
+    batch.close()
+    for s, o in list(zip(sessions, oracles))[:8]:
+        _heads_equal(s, o)
+    for s in sessions:
+        s.close()
+
+
+def test_one_query_head_projects_through_a_512_product(native_built, oracle_lib):
+    import rustyneedle_b200 as nb
+    from rustyneedle_b200 import synthetic
+
+    path = synthetic.cached_archive(seed=17, geometry=_heads_geometry(probe_heads=(2, 3, 1), head_queries=1, probes_per_layer=3,
+                                                                      engram_sites=()))
+    model = nb.Model.open(path, max_sessions=2)
+    omodel = oracle_lib.Model.open(path, oracle_lib.MODE_INT, 0)
+    s, o = nb.Session(model), oracle_lib.Session(omodel)
+    ids = prompt_ids(54, 33)
+    s.feed(ids)
+    o.feed(ids)
+    for code in (1, 2, 3):
+        assert _bits_equal(s.head_output(code), o.head_output(code)), code
+    s.close()
     model.close()

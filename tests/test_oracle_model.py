@@ -209,3 +209,32 @@ def test_engram_prefill_agrees_with_stepping(oracle_lib, kats):
     a, b = fed.logits(), pushed.logits()
     assert _cos(a, b) > kats["prefill_cosine"]
     assert oracle_lib.argmax(a) == oracle_lib.argmax(b)
+
+
+def test_probe_heads_follow_the_reference_tests(oracle_lib, kats):
+    """crates/model/tests/prefill.rs: batched vs stepped head_output(2)[0] within
+    0.1 (FLOAT mode); INT feeds equal pushes bit for bit; a head that is not in
+    the manifest reads None; a shallower depth pools fewer rows."""
+    from rustyneedle_b200 import synthetic
+
+    path = synthetic.cached_archive(seed=15, geometry=_features(probe_heads=(2, 3)))
+    ids = prompt_ids(9, 45)
+    mf = oracle_lib.Model.open(path, oracle_lib.MODE_FLOAT, 0)
+    fed, pushed = oracle_lib.Session(mf), oracle_lib.Session(mf)
+    fed.feed(ids)
+    for t in ids:
+        pushed.push(int(t))
+    assert abs(fed.head_output(2)[0] - pushed.head_output(2)[0]) < kats["prefill_head_tolerance"]
+    mi = oracle_lib.Model.open(path, oracle_lib.MODE_INT, 0)
+    fed, pushed = oracle_lib.Session(mi), oracle_lib.Session(mi)
+    fed.feed(ids)
+    for t in ids:
+        pushed.push(int(t))
+    for code in (2, 3):
+        assert np.array_equal(fed.head_output(code), pushed.head_output(code))
+        assert np.array_equal(fed.pooled_readout(code), pushed.pooled_readout(code))
+    assert fed.head_output(1) is None
+    shallow = oracle_lib.Session(mi.with_depth(2))
+    shallow.feed(ids)
+    assert shallow.head_output(2).shape == fed.head_output(2).shape
+    assert not np.array_equal(shallow.head_output(2), fed.head_output(2))
