@@ -120,16 +120,17 @@ __global__ void __launch_bounds__(128) k_engram_gather(ModelDev md, EngramDev E,
   if (t >= M) return;
   const TokenMeta meta = load_meta(w.meta, t);
   if (meta.slot < 0) return;
-  const int tables = (int)md.engram_tables, sub = (int)md.engram_sub_dim, K = tables * sub, gpt = sub / GROUP;
+  const EngramConfig& c = E.cfg;
+  const int tables = (int)c.tables, sub = (int)c.sub_dim, K = tables * sub, gpt = sub / GROUP;
   if (tid < tables) {
-    const int oi = tid / (int)md.engram_heads_per_order, head = tid % (int)md.engram_heads_per_order, order = (int)md.engram_order[oi];
-    uint32_t acc = 0x9E3779B9u * (uint32_t)(oi * (int)md.engram_stride + head + 1);
+    const int oi = tid / (int)c.heads_per_order, head = tid % (int)c.heads_per_order, order = (int)c.order[oi];
+    uint32_t acc = 0x9E3779B9u * (uint32_t)(oi * (int)c.stride + head + 1);
     for (int back = 0; back < order; ++back) {
       const uint32_t token = meta.position >= back ? token_at(md, w, t, meta, meta.position - back) : 0u;
       acc = (acc ^ token) * 0x01000193u;
     }
     acc ^= acc >> 15;
-    s_row[tid] = meta.position + 1 >= order ? (uint32_t)tid * md.engram_slots + acc % md.engram_slots : 0xffffffffu;
+    s_row[tid] = meta.position + 1 >= order ? (uint32_t)tid * c.slots + acc % c.slots : 0xffffffffu;
   }
   __syncthreads();
   float peak = 0.0f;
@@ -152,7 +153,7 @@ __global__ void __launch_bounds__(128) k_engram_gather(ModelDev md, EngramDev E,
   __syncthreads();
   const float scale = int8_scale_of(fmaxf(fmaxf(s_red[0], s_red[1]), fmaxf(s_red[2], s_red[3])));
   pdl_trigger();
-  const int groups = (int)md.engram_k / GROUP;
+  const int groups = (int)c.k / GROUP;
   for (int g = warp; g < groups; g += 4) {
     uint32_t packed = 0;
     float sc = 0.0f;
@@ -181,8 +182,8 @@ __device__ __forceinline__ void engram_add(const ModelDev& md, const EngramDev& 
   const TokenMeta meta = load_meta(w.meta, t);
   const float* kv = w.engram_kv + (size_t)t * 2 * d;
   for (int i = tid; i < d; i += nthreads) s_key[i] = __ldcg(kv + i);
-  if (tid < (int)md.engram_conv_taps) {  // each tap's raw value row (null: the position is too short)
-    const int back = tid * (int)md.engram_dilation, R = (int)md.engram_ring_rows;
+  if (tid < (int)E.cfg.conv_taps) {  // each tap's raw value row (null: the position is too short)
+    const int back = tid * (int)E.cfg.dilation, R = (int)E.cfg.ring_rows;
     const float* src = nullptr;
     if (meta.position >= back) {
       bool here = back == 0;
@@ -212,7 +213,7 @@ __device__ __forceinline__ void engram_add(const ModelDev& md, const EngramDev& 
   const float alpha = s_e[0];
   for (int i = tid; i < d; i += nthreads) {
     float value = 0.0f;
-    for (int tap = 0; tap < (int)md.engram_conv_taps; ++tap) {
+    for (int tap = 0; tap < (int)E.cfg.conv_taps; ++tap) {
       const float* src = s_src[tap];
       if (src) value = fadd(value, fmul(__ldg(E.taps + (size_t)tap * d + i), __ldcg(src + i)));
     }
@@ -467,7 +468,7 @@ __global__ void __launch_bounds__(256) k_route(ModelDev md, LayerDev L, Work w, 
   }
   named_barrier(1, nthreads);
   if (engram) {
-    engram_add(md, L.engram, w, t, nthreads, s_x, s_stream, s_stream + d, xg);  // the lanes are no longer needed
+    engram_add(md, *L.engram, w, t, nthreads, s_x, s_stream, s_stream + d, xg);  // the lanes are no longer needed
     named_barrier(1, nthreads);
   }
   if (warp == 0) {
@@ -1596,7 +1597,7 @@ __device__ __forceinline__ void conv_ring_store(const ModelDev& md, const LayerD
 // in this pass store their raw values in the site's ring (k_route, launches
 // earlier, has read it).
 __device__ __forceinline__ void engram_ring_store(const ModelDev& md, const EngramDev& E, const Work& w, int M, int t, int part, int parts) {
-  const int R = (int)md.engram_ring_rows, d = (int)md.d_model;
+  const int R = (int)E.cfg.ring_rows, d = (int)md.d_model;
   const TokenMeta meta = load_meta(w.meta, t);
   if (t + R < M) {
     const TokenMeta o = load_meta(w.meta, t + R);
@@ -1639,7 +1640,7 @@ __device__ __forceinline__ bool block_front(const ModelDev& md, const LayerDev& 
   }
   stage_async(s_a, w.outp + (size_t)t * d, d);
   if (md.conv_ring) conv_ring_store(md, L, w, M, t, part, parts);
-  if (L.engram_site >= 0 && L.engram.ring) engram_ring_store(md, L.engram, w, M, t, part, parts);
+  if (L.engram && L.engram->ring) engram_ring_store(md, *L.engram, w, M, t, part, parts);
   cp_async_wait_all();
   // the staged rows, the gate and the barrier's initialisation are visible to
   // every thread past this point; then each thread waits for the bulk copies
@@ -1942,12 +1943,12 @@ __global__ void __launch_bounds__(128) k_observe(ModelDev md, Work w, const floa
   }
   __syncthreads();
   int pairs = 0;
-  for (uint32_t h = 0; h < md.num_heads; ++h) pairs += (int)md.head[h].probes;
+  for (uint32_t h = 0; h < md.num_probe_heads; ++h) pairs += (int)md.probe_heads[h].probes;
   const float root = md.sqrt_d;
   for (int p = warp; p < pairs; p += blockDim.x >> 5) {
     int h = 0, k = p;
-    while (k >= (int)md.head[h].probes) k -= (int)md.head[h++].probes;
-    const HeadDev& H = md.head[h];
+    while (k >= (int)md.probe_heads[h].probes) k -= (int)md.probe_heads[h++].probes;
+    const HeadDev& H = md.probe_heads[h];
     const float dot = dot_product_warp(s_cell, H.directions + ((size_t)row * H.probes + k) * d, d);
     if (lane == 0) w.scores[(size_t)t * pairs + p] = fdiv(dot, root);
   }
@@ -1961,8 +1962,8 @@ __global__ void __launch_bounds__(128) k_observe(ModelDev md, Work w, const floa
   // the scalar recurrence per (head, probe), token by token
   for (int p = tid; p < pairs; p += blockDim.x) {
     int h = 0, k = p;
-    while (k >= (int)md.head[h].probes) k -= (int)md.head[h++].probes;
-    const HeadDev& H = md.head[h];
+    while (k >= (int)md.probe_heads[h].probes) k -= (int)md.probe_heads[h++].probes;
+    const HeadDev& H = md.probe_heads[h];
     const size_t slot = (size_t)meta.slot * (md.num_layers + 1) * H.probes + (size_t)row * H.probes + k;
     float peak = H.peak[slot], total = H.total[slot];
     for (int r = 0; r < len; ++r) {
@@ -1983,8 +1984,8 @@ __global__ void __launch_bounds__(128) k_observe(ModelDev md, Work w, const floa
   for (int e = tid; e < pairs * d; e += blockDim.x) {
     const int p = e / d, i = e % d;
     int h = 0, k = p;
-    while (k >= (int)md.head[h].probes) k -= (int)md.head[h++].probes;
-    const HeadDev& H = md.head[h];
+    while (k >= (int)md.probe_heads[h].probes) k -= (int)md.probe_heads[h++].probes;
+    const HeadDev& H = md.probe_heads[h];
     float* target = H.weighted + ((size_t)meta.slot * (md.num_layers + 1) * H.probes + (size_t)row * H.probes + k) * d + i;
     float v = *target;
     for (int r = 0; r < len; ++r) {
@@ -2003,7 +2004,7 @@ __global__ void __launch_bounds__(128) k_observe(ModelDev md, Work w, const floa
 // weighted sum of the readouts in slot order into `pooled`. One CTA of 256.
 __global__ void __launch_bounds__(256) k_head_pool(ModelDev md, int h, int slot, const int32_t* __restrict__ rows, int nrows,
                                                    float* __restrict__ readouts, float* __restrict__ weights, float* __restrict__ pooled) {
-  const HeadDev& H = md.head[h];
+  const HeadDev& H = md.probe_heads[h];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, d = (int)md.d_model, P = (int)H.probes, slots = nrows * P;
   const int all = (int)(md.num_layers + 1) * P;
   const size_t base = (size_t)slot * all;
@@ -2348,14 +2349,14 @@ static void launch_block(const ModelDev& md, const LayerDev& L, const Work& w, i
   }
 }
 
-void launch_layer(const ModelDev& md, const LayerDev& L, const Work& w, const KvDev& kv, int M, int layer, int slot, int t_cap,
-                  bool distinct, cudaStream_t st) {
+void launch_layer(const ModelDev& md, const LayerDev& L, const EngramDev* engram, const Work& w, const KvDev& kv, int M, int layer,
+                  int slot, int t_cap, bool distinct, cudaStream_t st) {
   t_pass_tokens = M;
   const int d = md.d_model, H = md.heads, KV = md.kv_heads;
   const int proj_stride = (2 * H + 2 * KV) * HEAD_DIM;
-  if (L.engram_site >= 0) {  // the site's key and raw value rows (engram.rs:84-90)
-    launch(k_engram_gather, M, 128, 0, st, md, L.engram, w, M);
-    project(L.engram.kv, w.act, w.act_scale, w.engram_kv, M, 2 * d, w.meta, st, md.error, (int)w.act_rows);
+  if (engram) {  // the site's key and raw value rows (engram.rs:84-90)
+    launch(k_engram_gather, M, 128, 0, st, md, *engram, w, M);
+    project(engram->kv, w.act, w.act_scale, w.engram_kv, M, 2 * d, w.meta, st, md.error, (int)w.act_rows);
   }
   launch(k_route, M, 256, route_smem(md), st, md, L, w, M, layer, slot, md.error);
   project(L.qkvg, w.act, w.act_scale, w.proj, M, proj_stride, w.meta, st, md.error);
@@ -2380,9 +2381,8 @@ void launch_observe(const ModelDev& md, const Work& w, const float* stream, int 
   launch(k_observe, M, 128, 0, st, md, w, stream, M, row);
 }
 
-void head_output(const ModelDev& md, int h, int slot, const int32_t* rows, int nrows, float* readouts, float* weights, float* pooled,
-                 int8_t* act, float* act_scale, int act_rows, float* out, bool project_out, cudaStream_t st) {
-  const HeadDev& H = md.head[h];
+void head_output(const ModelDev& md, const HeadDev& H, int h, int slot, const int32_t* rows, int nrows, float* readouts, float* weights,
+                 float* pooled, int8_t* act, float* act_scale, int act_rows, float* out, bool project_out, cudaStream_t st) {
   k_head_pool<<<1, 256, 0, st>>>(md, h, slot, rows, nrows, readouts, weights, pooled);
   if (!project_out) return;
   // ProbeHead::project (heads.rs:117-125): rotate and quantise per group (no

@@ -16,20 +16,23 @@ long launch_counter();
 
 void launch_embed(const nbl::ModelDev& md, const nbl::Work& w, int M, cudaStream_t st);
 // One decoder layer of M tokens. `distinct`: every token of the pass belongs
-// to a different sequence (a decode step, or a one-token feed).
-void launch_layer(const nbl::ModelDev& md, const nbl::LayerDev& L, const nbl::Work& w, const nbl::KvDev& kv, int M, int layer,
-                  int slot, int t_cap, bool distinct, cudaStream_t st);
+// to a different sequence (a decode step, or a one-token feed). `engram`: the
+// host copy of the layer's engram site, or null.
+void launch_layer(const nbl::ModelDev& md, const nbl::LayerDev& L, const nbl::EngramDev* engram, const nbl::Work& w,
+                  const nbl::KvDev& kv, int M, int layer, int slot, int t_cap, bool distinct, cudaStream_t st);
 void launch_final(const nbl::ModelDev& md, const nbl::Work& w, float* hidden, int M, cudaStream_t st);
 // ProbeHead::observe of cell row `row` (0: the embedding, layer + 1) of every
 // token of the pass; `stream` holds the lanes after that layer.
 void launch_observe(const nbl::ModelDev& md, const nbl::Work& w, const float* stream, int M, int row, cudaStream_t st);
 // ProbeHead::pooled (into `pooled`, queries · d) and, with project_out,
-// ProbeHead::project (into `out`) of head h of the session in `slot`; `rows`
+// ProbeHead::project (into `out`) of head h (`head`: its host copy) of the
+// session in `slot`; `rows`
 // (device) lists the model's nrows cell rows; readouts: nrows · probes · d
 // floats, weights: nrows · probes floats; act/act_scale: a zeroed one-token
 // activation buffer of K-chunk-major rows `act_rows`.
-void head_output(const nbl::ModelDev& md, int h, int slot, const int32_t* rows, int nrows, float* readouts, float* weights,
-                 float* pooled, int8_t* act, float* act_scale, int act_rows, float* out, bool project_out, cudaStream_t st);
+void head_output(const nbl::ModelDev& md, const nbl::HeadDev& head, int h, int slot, const int32_t* rows, int nrows, float* readouts,
+                 float* weights, float* pooled, int8_t* act, float* act_scale, int act_rows, float* out, bool project_out,
+                 cudaStream_t st);
 // Codebook rows dequantised to f32 (QuantisedMatrix::dequantise_row).
 void dense_rows(const uint8_t* packed, uint32_t row_bytes, uint32_t bits, const float* levels, const float* norms, int rows, int cols,
                 float inv_sqrt_group, float* out, cudaStream_t st);

@@ -113,7 +113,15 @@ struct HadamardDev {
   const float *cond_v, *cond_u;
 };
 
+// config.rs:4-14, the same for every site
+struct EngramConfig {
+  uint32_t slots, sub_dim, tables, orders, heads_per_order, stride;
+  uint32_t order[4];
+  uint32_t conv_taps, dilation, ring_rows, k;  // ring_rows = (conv_taps - 1) · dilation; k: the padded product K
+};
+
 struct EngramDev {
+  EngramConfig cfg;
   const uint8_t* packed;   // tables · slots rows of packed codes
   uint32_t row_bytes, bits;
   const float* levels;     // 2^bits levels
@@ -145,8 +153,8 @@ struct LayerDev {
   int global;  // 1 when the layer attends to the whole context
   int index;   // the layer's index in the archive
   const float* taps;  // [conv_taps][q | k | v] causal convolution gains; null without taps
-  int engram_site;    // the engram site on this layer (the first listed), -1 for none
-  EngramDev engram;   // that site's weights and ring
+  int engram_site;           // the engram site on this layer (the first listed), -1 for none
+  const EngramDev* engram;   // that site's weights and ring (device memory); null for none
 };
 
 struct ModelDev {
@@ -173,15 +181,10 @@ struct ModelDev {
   uint32_t conv_taps;         // QKV causal convolution taps (0 = none)
   uint32_t qkv_width;         // (heads + 2 kv_heads) * head_dim: the convolved part of a projection row
   float* conv_ring;           // [slots][layers][conv_taps - 1][qkv_width]; null when conv_taps < 2
-  // engram configuration (config.rs:4-14)
-  uint32_t engram_slots, engram_sub_dim, engram_tables, engram_orders, engram_heads_per_order, engram_stride;
-  uint32_t engram_order[4];
-  uint32_t engram_conv_taps, engram_dilation, engram_ring_rows, engram_k;  // engram_k: the padded product K
-  uint32_t* token_ring;       // [slots][token_rows]; null when token_rows == 0
+  uint32_t* token_ring;       // [slots][token_rows] (engram sites); null when token_rows == 0
   uint32_t token_rows;        // max order - 1
-  // probe heads
-  uint32_t num_heads;
-  HeadDev head[MAX_PROBE_HEADS];
+  uint32_t num_probe_heads;
+  const HeadDev* probe_heads;  // [num_probe_heads] (device memory)
 };
 
 // Per-token metadata of one forward pass.

@@ -189,7 +189,8 @@ struct Engine {
   std::vector<uint8_t> slot_dirty;
   float* d_hidden = nullptr;  // [slots][d]
   size_t conv_ring_floats = 0;  // per slot: md.conv_ring's [layers][taps - 1][q | k | v]
-  std::vector<EngramDev> engram_sites;
+  std::vector<EngramDev> engram_sites;  // host copies (the layers point at the device copies)
+  std::vector<HeadDev> heads;           // host copies of md.heads
   uint32_t act_groups = 0;  // act_scale floats per token: the widest product's groups
   // probe heads: (head, probe) pairs, the widest projection K, the most slots per session
   uint32_t head_pairs = 0, head_k = 0;
@@ -218,6 +219,10 @@ struct Engine {
   int t_cap = 0;
 
   KvDev kv() const { return KvDev{pool, d_page_table, max_pages, geo.num_layers}; }
+  const EngramDev* engram_of(int layer) const {
+    const int site = layers[layer].engram_site;
+    return site >= 0 ? &engram_sites[site] : nullptr;
+  }
 
   ~Engine() {
     if (device >= 0) cudaSetDevice(device);
@@ -448,18 +453,19 @@ std::shared_ptr<Engine> open_engine(const char* path, const nb_options* opt) {
   md.sliding_window = g.sliding_window;
   md.conv_taps = g.qkv_conv_taps;
   md.qkv_width = (H + 2 * KV) * HEAD_DIM;
+  EngramConfig ecfg{};
   if (!g.engram_sites.empty()) {
-    md.engram_slots = g.engram_slots;
-    md.engram_sub_dim = g.engram_sub_dim;
-    md.engram_tables = g.engram_tables;
-    md.engram_orders = (uint32_t)g.engram_orders.size();
-    md.engram_heads_per_order = g.engram_tables / md.engram_orders;
-    md.engram_stride = g.engram_seed_heads ? g.engram_seed_heads : md.engram_heads_per_order;
-    for (uint32_t i = 0; i < md.engram_orders; ++i) md.engram_order[i] = g.engram_orders[i];
-    md.engram_conv_taps = g.engram_conv_taps;
-    md.engram_dilation = g.engram_conv_dilation;
-    md.engram_ring_rows = (g.engram_conv_taps - 1) * g.engram_conv_dilation;
-    md.engram_k = g.engram_tables * g.engram_sub_dim <= 512 ? 512 : 2048;
+    ecfg.slots = g.engram_slots;
+    ecfg.sub_dim = g.engram_sub_dim;
+    ecfg.tables = g.engram_tables;
+    ecfg.orders = (uint32_t)g.engram_orders.size();
+    ecfg.heads_per_order = g.engram_tables / ecfg.orders;
+    ecfg.stride = g.engram_seed_heads ? g.engram_seed_heads : ecfg.heads_per_order;
+    for (uint32_t i = 0; i < ecfg.orders; ++i) ecfg.order[i] = g.engram_orders[i];
+    ecfg.conv_taps = g.engram_conv_taps;
+    ecfg.dilation = g.engram_conv_dilation;
+    ecfg.ring_rows = (g.engram_conv_taps - 1) * g.engram_conv_dilation;
+    ecfg.k = g.engram_tables * g.engram_sub_dim <= 512 ? 512 : 2048;
     md.token_rows = max_order - 1;
   }
   md.sqrt_d = std::sqrt((float)d);
@@ -615,6 +621,7 @@ std::shared_ptr<Engine> open_engine(const char* path, const nb_options* opt) {
   for (size_t si = 0; si < g.engram_sites.size(); ++si) {
     const std::array<uint32_t, 4>& e = lay.engrams.at(si);
     EngramDev S{};
+    S.cfg = ecfg;
     const nba::Record& tr = a.record(e[0]);
     if (tr.kind != nba::CODEBOOK || tr.rows() < (uint64_t)g.engram_tables * g.engram_slots || tr.columns() != g.engram_sub_dim ||
         tr.group() != GROUP)
@@ -636,7 +643,7 @@ std::shared_ptr<Engine> open_engine(const char* path, const nb_options* opt) {
       }
       S.norms = A.upload(norms, st);
     }
-    const uint32_t K = g.engram_tables * g.engram_sub_dim, KP = md.engram_k, kg = K / GROUP, pg = KP / GROUP;
+    const uint32_t K = g.engram_tables * g.engram_sub_dim, KP = ecfg.k, kg = K / GROUP, pg = KP / GROUP;
     check_matrix(a, e[1], d, K, "engram key_proj");
     check_matrix(a, e[2], d, K, "engram value_proj");
     Levels lk = levels_for(a.record(e[1]).bits, a.codebook(), GROUP);
@@ -659,10 +666,11 @@ std::shared_ptr<Engine> open_engine(const char* path, const nb_options* opt) {
   // probe heads (heads.rs:29-50): directions and queries dequantised to f32
   // on the device, gains and biases, the projection as a product
   if (lay.heads.size() > (size_t)MAX_PROBE_HEADS) fail(NB_ERR_UNSUPPORTED, "more than 4 probe heads are not implemented");
-  md.num_heads = (uint32_t)lay.heads.size();
+  md.num_probe_heads = (uint32_t)lay.heads.size();
+  E->heads.resize(lay.heads.size());
   for (size_t hi = 0; hi < lay.heads.size(); ++hi) {
     const nba::Layout::HeadIdx& t = lay.heads[hi];
-    HeadDev& H = md.head[hi];
+    HeadDev& H = E->heads[hi];
     H.code = (int)t.code;
     auto dense = [&](uint32_t index, const char* what) {
       const nba::Record& r = a.record(index);
@@ -733,8 +741,8 @@ std::shared_ptr<Engine> open_engine(const char* path, const nb_options* opt) {
   for (uint32_t s = E->max_sessions; s-- > 0;) E->free_slots.push_back(s);
   E->d_hidden = A.alloc<float>((size_t)E->max_sessions * d);
   NB_CUDA(cudaMemsetAsync(E->d_hidden, 0, (size_t)E->max_sessions * d * 4, st));
-  for (uint32_t hi = 0; hi < md.num_heads; ++hi) {  // ProbeAccumulator (heads.rs:151-156) per slot
-    HeadDev& H = md.head[hi];
+  for (uint32_t hi = 0; hi < md.num_probe_heads; ++hi) {  // ProbeAccumulator (heads.rs:151-156) per slot
+    HeadDev& H = E->heads[hi];
     const size_t all = (size_t)(L + 1) * H.probes;
     H.peak = A.alloc<float>(E->max_sessions * all);
     H.total = A.alloc<float>(E->max_sessions * all);
@@ -743,7 +751,8 @@ std::shared_ptr<Engine> open_engine(const char* path, const nb_options* opt) {
     E->head_k = std::max<uint32_t>(E->head_k, H.proj.cols);
     E->head_slots = std::max<size_t>(E->head_slots, all);
   }
-  if (md.num_heads) {
+  if (md.num_probe_heads) {
+    md.probe_heads = A.upload(E->heads, st);
     E->d_head_rows = A.alloc<int32_t>(L + 1);
     E->d_head_readouts = A.alloc<float>(E->head_slots * d);
     E->d_head_weights = A.alloc<float>(E->head_slots);
@@ -756,20 +765,22 @@ std::shared_ptr<Engine> open_engine(const char* path, const nb_options* opt) {
     E->h_head.ensure(std::max<size_t>(E->head_k, 4096) * 4);
   }
   for (EngramDev& S : sites)
-    if (md.engram_ring_rows) {
-      S.ring = A.alloc<float>((size_t)E->max_sessions * md.engram_ring_rows * d);
-      NB_CUDA(cudaMemsetAsync(S.ring, 0, (size_t)E->max_sessions * md.engram_ring_rows * d * 4, st));
+    if (ecfg.ring_rows) {
+      S.ring = A.alloc<float>((size_t)E->max_sessions * ecfg.ring_rows * d);
+      NB_CUDA(cudaMemsetAsync(S.ring, 0, (size_t)E->max_sessions * ecfg.ring_rows * d * 4, st));
     }
+  const EngramDev* d_sites = sites.empty() ? nullptr : A.upload(sites, st);
   if (md.token_rows) {
     md.token_ring = A.alloc<uint32_t>((size_t)E->max_sessions * md.token_rows);
     NB_CUDA(cudaMemsetAsync(md.token_ring, 0, (size_t)E->max_sessions * md.token_rows * 4, st));
   }
   for (uint32_t l = 0; l < L; ++l) {  // ModelConfig::engram_site_at: the first site listed on the layer
     E->layers[l].engram_site = -1;
+    E->layers[l].engram = nullptr;
     for (size_t si = 0; si < sites.size() && E->layers[l].engram_site < 0; ++si)
       if (g.engram_sites[si] == l) {
         E->layers[l].engram_site = (int)si;
-        E->layers[l].engram = sites[si];
+        E->layers[l].engram = d_sites + si;
       }
   }
   E->engram_sites = sites;
@@ -780,7 +791,7 @@ std::shared_ptr<Engine> open_engine(const char* path, const nb_options* opt) {
   }
 
   E->capacity = std::max<uint32_t>(opt && opt->max_batch_tokens ? opt->max_batch_tokens : 1024, E->max_sessions);
-  const uint32_t M = E->capacity, AW = H * HEAD_DIM, actw = std::max({d, AW, md.engram_k});
+  const uint32_t M = E->capacity, AW = H * HEAD_DIM, actw = std::max({d, AW, ecfg.k});
   E->act_groups = actw / GROUP;
   Work& w = E->work;
   w.capacity = M;
@@ -798,7 +809,7 @@ std::shared_ptr<Engine> open_engine(const char* path, const nb_options* opt) {
     w.engram_kv = A.alloc<float>((size_t)M * 2 * d);
     w.xin = A.alloc<float>((size_t)M * d);
   }
-  if (md.num_heads) {
+  if (md.num_probe_heads) {
     if (M > 0xffff) fail(NB_ERR_ARGUMENT, "passes of more than 65535 tokens are not supported with probe heads");
     w.cells = A.alloc<float>((size_t)M * d);
     w.scores = A.alloc<float>((size_t)M * E->head_pairs);
@@ -878,12 +889,12 @@ void forward(Engine& E, const std::vector<int32_t>& active, const TokenSpec* spe
     seen[specs[i].slot] = 1;
   }
   nbk::launch_embed(E.md, w, (int)count, E.stream);
-  if (E.md.num_heads) nbk::launch_observe(E.md, w, w.stream, (int)count, 0, E.stream);
+  if (E.md.num_probe_heads) nbk::launch_observe(E.md, w, w.stream, (int)count, 0, E.stream);
   for (size_t slot = 0; slot < active.size(); ++slot) {
     int layer = active[slot];
-    nbk::launch_layer(E.md, E.layers[layer], w, kv, (int)count, layer, (int)slot, E.t_cap, distinct, E.stream);
+    nbk::launch_layer(E.md, E.layers[layer], E.engram_of(layer), w, kv, (int)count, layer, (int)slot, E.t_cap, distinct, E.stream);
     std::swap(w.stream, w.next_stream);
-    if (E.md.num_heads) nbk::launch_observe(E.md, w, w.stream, (int)count, layer + 1, E.stream);
+    if (E.md.num_probe_heads) nbk::launch_observe(E.md, w, w.stream, (int)count, layer + 1, E.stream);
   }
   nbk::launch_final(E.md, w, E.d_hidden, (int)count, E.stream);
   NB_CUDA(cudaGetLastError());
@@ -1036,8 +1047,8 @@ nb_status nb_session_create(nb_model* model, nb_session** out) {
     s->slot = E.free_slots.back();
     E.free_slots.pop_back();
     NB_CUDA(cudaMemsetAsync(E.d_hidden + (size_t)s->slot * E.md.d_model, 0, E.md.d_model * 4, E.stream));
-    for (uint32_t h = 0; h < E.md.num_heads; ++h) {  // ProbeHead::accumulator (heads.rs:80-83)
-      const HeadDev& H = E.md.head[h];
+    for (uint32_t h = 0; h < E.md.num_probe_heads; ++h) {  // ProbeHead::accumulator (heads.rs:80-83)
+      const HeadDev& H = E.heads[h];
       const size_t all = (size_t)(E.md.num_layers + 1) * H.probes;
       nbk::fill(H.peak + s->slot * all, all, -INFINITY, E.stream);
       NB_CUDA(cudaMemsetAsync(H.total + s->slot * all, 0, all * 4, E.stream));
@@ -1069,8 +1080,8 @@ nb_status nb_session_clone(const nb_session* session, nb_session** out) {
     NB_CUDA(cudaMemcpyAsync(E.d_hidden + (size_t)s->slot * E.md.d_model, E.d_hidden + (size_t)session->slot * E.md.d_model,
                             E.md.d_model * 4, cudaMemcpyDeviceToDevice, E.stream));
     const size_t d = E.md.d_model;
-    for (uint32_t h = 0; h < E.md.num_heads; ++h) {  // the probe accumulators are part of the session (session.rs:26)
-      const HeadDev& H = E.md.head[h];
+    for (uint32_t h = 0; h < E.md.num_probe_heads; ++h) {  // the probe accumulators are part of the session (session.rs:26)
+      const HeadDev& H = E.heads[h];
       const size_t all = (size_t)(E.md.num_layers + 1) * H.probes;
       NB_CUDA(cudaMemcpyAsync(H.peak + s->slot * all, H.peak + session->slot * all, all * 4, cudaMemcpyDeviceToDevice, E.stream));
       NB_CUDA(cudaMemcpyAsync(H.total + s->slot * all, H.total + session->slot * all, all * 4, cudaMemcpyDeviceToDevice, E.stream));
@@ -1079,8 +1090,8 @@ nb_status nb_session_clone(const nb_session* session, nb_session** out) {
     }
     for (const EngramDev& S : E.engram_sites)  // EngramSiteState is part of the session (session.rs:22)
       if (S.ring)
-        NB_CUDA(cudaMemcpyAsync(S.ring + (size_t)s->slot * E.md.engram_ring_rows * d, S.ring + (size_t)session->slot * E.md.engram_ring_rows * d,
-                                (size_t)E.md.engram_ring_rows * d * 4, cudaMemcpyDeviceToDevice, E.stream));
+        NB_CUDA(cudaMemcpyAsync(S.ring + (size_t)s->slot * S.cfg.ring_rows * d, S.ring + (size_t)session->slot * S.cfg.ring_rows * d,
+                                (size_t)S.cfg.ring_rows * d * 4, cudaMemcpyDeviceToDevice, E.stream));
     if (E.md.token_ring)
       NB_CUDA(cudaMemcpyAsync(E.md.token_ring + (size_t)s->slot * E.md.token_rows, E.md.token_ring + (size_t)session->slot * E.md.token_rows,
                               E.md.token_rows * 4, cudaMemcpyDeviceToDevice, E.stream));
@@ -1140,18 +1151,18 @@ static nb_status head_values(nb_session* session, uint32_t code, float* out, siz
     Engine& E = *session->engine;
     std::lock_guard<std::mutex> lock(E.mutex);
     int h = -1;
-    for (uint32_t i = 0; i < E.md.num_heads && h < 0; ++i)
-      if ((uint32_t)E.md.head[i].code == code) h = (int)i;
+    for (uint32_t i = 0; i < E.md.num_probe_heads && h < 0; ++i)
+      if ((uint32_t)E.heads[i].code == code) h = (int)i;
     if (h < 0) fail(NB_ERR_ARGUMENT, "the model has no probe head with code " + std::to_string(code));
     NB_CUDA(cudaSetDevice(E.device));
     E.settle();
-    const HeadDev& H = E.md.head[h];
+    const HeadDev& H = E.heads[h];
     std::vector<int32_t> rows{0};
     for (int32_t l : session->active) rows.push_back(l + 1);
     int32_t* hr = E.h_head.as<int32_t>();
     std::copy(rows.begin(), rows.end(), hr);
     NB_CUDA(cudaMemcpyAsync(E.d_head_rows, hr, rows.size() * 4, cudaMemcpyHostToDevice, E.stream));
-    nbk::head_output(E.md, h, (int)session->slot, E.d_head_rows, (int)rows.size(), E.d_head_readouts, E.d_head_weights, E.d_head_pooled,
+    nbk::head_output(E.md, H, h, (int)session->slot, E.d_head_rows, (int)rows.size(), E.d_head_readouts, E.d_head_weights, E.d_head_pooled,
                      E.d_head_act, E.d_head_scale, 128, E.d_head_out, project_out, E.stream);
     const size_t n = project_out ? H.outputs : (size_t)H.queries * E.md.d_model;
     float* staged = E.h_head.as<float>();
@@ -1329,12 +1340,12 @@ static void build_group(nb_batch* b, bool masked, bool stats, uint32_t b0, uint3
   Work w = work_rows(E, base, b0);
   KvDev kv = E.kv();
   nbk::launch_embed(E.md, w, n, st);
-  if (E.md.num_heads) nbk::launch_observe(E.md, w, w.stream, n, 0, st);
+  if (E.md.num_probe_heads) nbk::launch_observe(E.md, w, w.stream, n, 0, st);
   for (size_t slot = 0; slot < b->active.size(); ++slot) {
     int layer = b->active[slot];
-    nbk::launch_layer(E.md, E.layers[layer], w, kv, n, layer, (int)slot, E.t_cap, true, st);
+    nbk::launch_layer(E.md, E.layers[layer], E.engram_of(layer), w, kv, n, layer, (int)slot, E.t_cap, true, st);
     std::swap(w.stream, w.next_stream);
-    if (E.md.num_heads) nbk::launch_observe(E.md, w, w.stream, n, layer + 1, st);
+    if (E.md.num_probe_heads) nbk::launch_observe(E.md, w, w.stream, n, layer + 1, st);
   }
   nbk::launch_final(E.md, w, E.d_hidden, n, st);
   nbk::launch_advance(b->d_meta + b0, n, st);
