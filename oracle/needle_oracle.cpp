@@ -222,6 +222,9 @@ struct Layout {
   struct HeadT { uint8_t code; size_t probes, gain, query, row_bias, proj, bias; };
   std::vector<HeadT> heads;
   bool audio = false;
+  std::vector<std::array<size_t, 10>> cross;  // per decoder layer: norm, q, k, v, gate, out, q_norm, k_norm, post_norm, gate scalar
+  size_t position_gate = 0;
+  size_t text_vocab = 0;
   size_t tokenizer;
 };
 
@@ -301,7 +304,13 @@ Layout resolve_layout(const Archive& a) {
     const float* v = reinterpret_cast<const float*>(a.data(manifest));
     if (r.byte_len / 4 != 13 || v[0] != 3246.0f) throw Failure(ERR_ARCHIVE, "unexpected tensor layout: audio manifest is malformed");
     size_t encoder_layers = (size_t)v[3], stem_stages = (size_t)v[7];
-    for (size_t l = 0; l < a.geo.num_layers * 10 + 1; ++l) take();
+    L.text_vocab = (size_t)v[2];
+    for (size_t l = 0; l < a.geo.num_layers; ++l) {
+      std::array<size_t, 10> c;
+      for (size_t& x : c) x = take();
+      L.cross.push_back(c);
+    }
+    L.position_gate = take();
     for (size_t l = 0; l < encoder_layers; ++l)
       for (int i = 0; i < 17 + 26; ++i) take();
     for (int i = 0; i < 9 + 1 + 1; ++i) take();
@@ -853,9 +862,19 @@ struct ProbeHeadW {
   QMatrix projection;
 };
 
+// whistle/src/cross.rs:8-19
+struct CrossLayerW {
+  std::vector<float> norm, q_norm, k_norm, post_norm;
+  QMatrix q, k, v, gate, out;
+  float gate_scalar = 0.0f;
+};
+
 struct Weights {
   QMatrix embedding;
   std::vector<LayerW> layers;
+  std::vector<CrossLayerW> cross;  // a Whistle archive's cross attention, per decoder layer
+  float position_gate = 0.0f;
+  size_t text_vocab = 0;
   LanesW lanes;
   std::vector<EngramW> engrams;  // one per engram site
   std::vector<ProbeHeadW> heads;
@@ -1062,6 +1081,24 @@ std::shared_ptr<Weights> load_weights(const Archive& a, const Layout& L) {
         hw.projection.columns != hw.queries * hw.width || hw.bias.size() < hw.projection.rows)
       throw Failure(ERR_ARCHIVE, "probe head tensors do not match one another");
     w->heads.push_back(std::move(hw));
+  }
+  for (const auto& c : L.cross) {  // CrossWeights::load (cross.rs:38-56)
+    CrossLayerW cw;
+    cw.norm = floats(a, c[0]);
+    cw.q = load_matrix(a, c[1]);
+    cw.k = load_matrix(a, c[2]);
+    cw.v = load_matrix(a, c[3]);
+    cw.gate = load_matrix(a, c[4]);
+    cw.out = load_matrix(a, c[5]);
+    cw.q_norm = floats(a, c[6]);
+    cw.k_norm = floats(a, c[7]);
+    cw.post_norm = floats(a, c[8]);
+    cw.gate_scalar = floats(a, c[9]).at(0);
+    w->cross.push_back(std::move(cw));
+  }
+  if (L.audio) {
+    w->position_gate = floats(a, L.position_gate).at(0);
+    w->text_vocab = L.text_vocab;
   }
   w->final_norm = floats(a, L.final_norm);
   return w;
@@ -1382,13 +1419,17 @@ std::vector<float> attend(const nbo_model* M, const LayerW& W, size_t layer, Cac
 
 // The post-attention half of a block (session.rs:121-137): post norm, gated
 // residual, Hadamard MLP, lane delta and lane combine.
+struct CrossMemory;
+void cross_apply(const nbo_model* M, const CrossMemory& mem, size_t layer, float* x);
+
 void finish_block(const nbo_model* M, const LayerW& W, const Routing& r, std::vector<float>& x, std::vector<float>& attended,
-                  const float* stream, float* next) {
+                  const float* stream, float* next, const CrossMemory* cross = nullptr, size_t layer = 0) {
   const Geometry& g = M->archive->geo;
   size_t d = g.d_model, lanes = g.mhc_lanes;
   zero_centred_norm_in_place(attended.data(), W.post_norm.data(), d);
   float gate = sigmoid(W.attention_gate);
   for (size_t i = 0; i < d; ++i) x[i] += gate * attended[i];
+  if (cross) cross_apply(M, *cross, layer, x.data());  // session.rs:126-128
   std::vector<float> pre(d);
   zero_centred_norm(x.data(), W.pre_hada.data(), pre.data(), d);
   std::vector<float> mlp = hadamard_apply(W.hada, pre.data(), d, M->mode);
@@ -1551,6 +1592,112 @@ std::vector<float> project_head(const nbo_model* M, const ProbeHeadW& h, const s
   return out;
 }
 
+// ---------------------------------------------------------- Whistle cross attention
+// whistle/src/cross.rs:29-35: per decoder layer the int8 keys [frame][head][qk]
+// with their scales [frame][head], and the values likewise.
+struct CrossMemory {
+  size_t frames = 0;
+  std::vector<std::vector<int8_t>> keys, values;
+  std::vector<std::vector<float>> key_scales, value_scales;
+};
+
+// CrossWeights::memory (cross.rs:58-99).
+CrossMemory cross_memory(const nbo_model* M, const float* encoded, size_t frames) {
+  const Geometry& g = M->archive->geo;
+  const Weights& W = *M->weights;
+  const size_t dim = g.d_model, half = dim / 2, qk = g.qk_head_dim, vd = g.v_head_dim, heads = dim / vd;
+  const float gate = sigmoid(W.position_gate);
+  const float rate = -std::log(10000.0f) / ((float)half - 1.0f);
+  std::vector<float> memory(frames * dim);
+  for (size_t t = 0; t < frames; ++t) {
+    const float* row = encoded + t * dim;
+    float* out = &memory[t * dim];
+    for (size_t j = 0; j < half; ++j) {
+      const float angle = (float)t * std::exp(rate * (float)j);
+      out[j] = row[j] + gate * std::sin(angle);
+      out[half + j] = row[half + j] + gate * std::cos(angle);
+    }
+    fake_quantise_int8(out, dim);
+  }
+  CrossMemory mem;
+  mem.frames = frames;
+  for (const CrossLayerW& layer : W.cross) {
+    const size_t kr = layer.k.rows, vr = layer.v.rows;
+    std::vector<float> k(frames * kr), v(frames * vr);
+    if (M->mode == NBO_MODE_INT) {  // the integer batched product computes each row as the single-row one does
+      for (size_t t = 0; t < frames; ++t) {
+        std::vector<float> rotated = layer.k.prepare(&memory[t * dim]);
+        std::vector<Job> jobs{{&layer.k, 0, &k[t * kr], kr}, {&layer.v, 0, &v[t * vr], vr}};
+        multiply_jobs(jobs, rotated.data(), M->mode, M->threads);
+      }
+    } else {
+      const size_t padded = layer.k.padded;
+      std::vector<float> rotated(frames * padded);
+      for (size_t t = 0; t < frames; ++t) {
+        std::vector<float> r = layer.k.prepare(&memory[t * dim]);
+        std::memcpy(&rotated[t * padded], r.data(), padded * sizeof(float));
+      }
+      multiply_batch_float(layer.k, rotated.data(), frames, k.data(), M->threads);
+      multiply_batch_float(layer.v, rotated.data(), frames, v.data(), M->threads);
+    }
+    std::vector<int8_t> kc(k.size()), vc(v.size());
+    std::vector<float> ks(frames * heads), vs(frames * heads);
+    for (size_t i = 0; i < frames * heads; ++i) {
+      zero_centred_norm_in_place(&k[i * qk], layer.k_norm.data(), qk);
+      ks[i] = quantise_int8(&k[i * qk], &kc[i * qk], qk);
+      vs[i] = quantise_int8(&v[i * vd], &vc[i * vd], vd);
+    }
+    mem.keys.push_back(std::move(kc));
+    mem.key_scales.push_back(std::move(ks));
+    mem.values.push_back(std::move(vc));
+    mem.value_scales.push_back(std::move(vs));
+  }
+  return mem;
+}
+
+// CrossState::apply (cross.rs:121-182) on x after the layer's attention residual.
+void cross_apply(const nbo_model* M, const CrossMemory& mem, size_t layer_index, float* x) {
+  const Geometry& g = M->archive->geo;
+  const CrossLayerW& layer = M->weights->cross.at(layer_index);
+  const size_t dim = g.d_model, qk = g.qk_head_dim, vd = g.v_head_dim, heads = dim / vd, frames = mem.frames;
+  std::vector<float> normed(dim);
+  zero_centred_norm(x, layer.norm.data(), normed.data(), dim);
+  fake_quantise_int8(normed.data(), dim);
+  std::vector<float> rotated = layer.q.prepare(normed.data());
+  std::vector<float> q(layer.q.rows), gate(layer.gate.rows);
+  multiply_jobs({{&layer.q, 0, q.data(), layer.q.rows}}, rotated.data(), M->mode, M->threads);
+  multiply_jobs({{&layer.gate, 0, gate.data(), layer.gate.rows}}, rotated.data(), M->mode, M->threads);
+  const float inverse_root = 1.0f / std::sqrt((float)qk);
+  std::vector<float> context(heads * vd, 0.0f), scores(frames);
+  for (size_t head = 0; head < heads; ++head) {
+    float* query = &q[head * qk];
+    zero_centred_norm_in_place(query, layer.q_norm.data(), qk);
+    std::vector<int8_t> codes(qk);
+    const float query_scale = quantise_int8(query, codes.data(), qk) * inverse_root;
+    for (size_t f = 0; f < frames; ++f) {
+      const int8_t* key = &mem.keys[layer_index][(f * heads + head) * qk];
+      int32_t dot = 0;
+      for (size_t i = 0; i < qk; ++i) dot += (int32_t)codes[i] * (int32_t)key[i];
+      scores[f] = (float)dot * mem.key_scales[layer_index][f * heads + head] * query_scale;
+    }
+    softmax_in_place(scores.data(), frames);
+    float* out = &context[head * vd];
+    for (size_t f = 0; f < frames; ++f) {
+      const float scale = mem.value_scales[layer_index][f * heads + head] * scores[f];
+      const int8_t* value = &mem.values[layer_index][(f * heads + head) * vd];
+      for (size_t i = 0; i < vd; ++i) out[i] += scale * (float)value[i];
+    }
+  }
+  for (size_t i = 0; i < context.size(); ++i) context[i] *= sigmoid(gate[i]);
+  fake_quantise_int8(context.data(), context.size());
+  std::vector<float> rotated_out = layer.out.prepare(context.data());
+  std::vector<float> attended(layer.out.rows);
+  multiply_jobs({{&layer.out, 0, attended.data(), layer.out.rows}}, rotated_out.data(), M->mode, M->threads);
+  zero_centred_norm_in_place(attended.data(), layer.post_norm.data(), dim);
+  const float gain = sigmoid(layer.gate_scalar);
+  for (size_t i = 0; i < dim; ++i) x[i] += gain * attended[i];
+}
+
 std::vector<float> embed(const nbo_model* M, uint32_t token) {
   const Geometry& g = M->archive->geo;
   if (token >= M->weights->embedding.rows) throw Failure(ERR_ARGUMENT, "token id outside the embedding");
@@ -1563,7 +1710,7 @@ std::vector<float> embed(const nbo_model* M, uint32_t token) {
 }
 
 // session.rs:76-148
-void push(nbo_session* s, uint32_t token, float* trace) {
+void push(nbo_session* s, uint32_t token, float* trace, const CrossMemory* cross = nullptr) {
   const nbo_model* M = s->model;
   const Geometry& g = M->archive->geo;
   size_t d = g.d_model, lanes = g.mhc_lanes;
@@ -1590,7 +1737,7 @@ void push(nbo_session* s, uint32_t token, float* trace) {
     if (site >= 0 && !ekey[site].empty()) add_engram(x.data(), ekey[site].data(), evalue[site].data(), d);
     zero_centred_norm(x.data(), W.norm_in.data(), normed.data(), d);
     std::vector<float> attended = attend(M, W, layer, s->caches[layer], s->frequencies.data(), position, normed.data());
-    finish_block(M, W, r, x, attended, stream.data(), next.data());
+    finish_block(M, W, r, x, attended, stream.data(), next.data(), cross, layer);
     std::swap(stream, next);
     if (trace) std::memcpy(trace + slot * lanes * d, stream.data(), lanes * d * sizeof(float));
     if (!M->weights->heads.empty()) cells.push_back(lane_mean(stream.data(), d, lanes));
@@ -1884,6 +2031,34 @@ long nbo_session_head_output(const nbo_session* s, int code, float* out, size_t 
 long nbo_session_pooled_readout(const nbo_session* s, int code, float* out, size_t cap) { return head_values(s, code, out, cap, false); }
 
 void nbo_session_push(nbo_session* s, uint32_t token) { guard([&] { push(s, token, nullptr); }); }
+
+// Whistle: CrossWeights::memory of an encoder output [frames][d_model], and
+// Session::push_with(token, CrossState) (session.rs:76-148 with the hook).
+struct nbo_cross_memory {
+  nbo::CrossMemory m;
+};
+int nbo_cross_memory_new(const nbo_model* model, const float* encoded, size_t frames, nbo_cross_memory** out) {
+  *out = nullptr;
+  return guard([&] {
+    if (model->weights->cross.empty()) throw nbo::Failure(nbo::ERR_ARGUMENT, "the archive carries no cross attention");
+    auto* m = new nbo_cross_memory();
+    m->m = nbo::cross_memory(model, encoded, frames);
+    *out = m;
+  });
+}
+void nbo_cross_memory_free(nbo_cross_memory* memory) { delete memory; }
+size_t nbo_cross_memory_read(const nbo_cross_memory* memory, int layer, int8_t* keys, float* key_scales, int8_t* values, float* value_scales) {
+  const nbo::CrossMemory& m = memory->m;
+  std::memcpy(keys, m.keys[layer].data(), m.keys[layer].size());
+  std::memcpy(key_scales, m.key_scales[layer].data(), m.key_scales[layer].size() * 4);
+  std::memcpy(values, m.values[layer].data(), m.values[layer].size());
+  std::memcpy(value_scales, m.value_scales[layer].data(), m.value_scales[layer].size() * 4);
+  return m.frames;
+}
+int nbo_session_push_cross(nbo_session* s, uint32_t token, const nbo_cross_memory* memory) {
+  return guard([&] { push(s, token, nullptr, &memory->m); });
+}
+size_t nbo_model_text_vocab(const nbo_model* model) { return model->weights->text_vocab; }
 void nbo_session_push_traced(nbo_session* s, uint32_t token, float* trace) { guard([&] { push(s, token, trace); }); }
 void nbo_session_feed(nbo_session* s, const uint32_t* tokens, size_t count) { guard([&] { feed(s, tokens, count); }); }
 void nbo_session_logits(const nbo_session* s, float* out) { guard([&] { logits(s, out); }); }

@@ -54,6 +54,17 @@ size_t nbo_session_len(const nbo_session* session);
 // Session::head_output / pooled_readout: values written (at most cap), -1 without a head `code`.
 long nbo_session_head_output(const nbo_session* session, int code, float* out, size_t cap);
 long nbo_session_pooled_readout(const nbo_session* session, int code, float* out, size_t cap);
+
+// Whistle (whistle/src/cross.rs): the cross-attention memory of an encoder
+// output [frames][d_model], its per-layer keys/values, and a push through the
+// cross-attention hook; the archive's text vocabulary size (0 without audio).
+typedef struct nbo_cross_memory nbo_cross_memory;
+int nbo_cross_memory_new(const nbo_model* model, const float* encoded, size_t frames, nbo_cross_memory** out);
+void nbo_cross_memory_free(nbo_cross_memory* memory);
+size_t nbo_cross_memory_read(const nbo_cross_memory* memory, int layer, int8_t* keys, float* key_scales, int8_t* values,
+                             float* value_scales);
+int nbo_session_push_cross(nbo_session* session, uint32_t token, const nbo_cross_memory* memory);
+size_t nbo_model_text_vocab(const nbo_model* model);
 void nbo_session_push(nbo_session* session, uint32_t token);
 /* push that also records the lane stream after every active layer:
  * trace holds depth × lanes × d_model floats. */

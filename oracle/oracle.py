@@ -54,6 +54,11 @@ def _declare(L: ctypes.CDLL) -> None:
         "nbo_session_free": (None, [P]),
         "nbo_session_len": (SZ, [P]),
         "nbo_session_head_output": (ctypes.c_long, [P, ctypes.c_int, P, SZ]),
+        "nbo_cross_memory_new": (I, [P, P, SZ, P]),
+        "nbo_cross_memory_free": (None, [P]),
+        "nbo_cross_memory_read": (SZ, [P, I, P, P, P, P]),
+        "nbo_session_push_cross": (I, [P, ctypes.c_uint32, P]),
+        "nbo_model_text_vocab": (SZ, [P]),
         "nbo_session_pooled_readout": (ctypes.c_long, [P, ctypes.c_int, P, SZ]),
         "nbo_session_push": (None, [P, U32]),
         "nbo_session_push_traced": (None, [P, U32, P]),
@@ -189,6 +194,12 @@ class Session:
         out = np.empty(1 << 14, dtype=np.float32)
         n = fn(self._h, int(code), _ptr(out), out.size)
         return None if n < 0 else out[:n].copy()
+
+    def push_cross(self, token: int, memory: "CrossMemory") -> None:
+        """Session::push_with(token, CrossState) (whistle lib.rs:255-293)."""
+        status = lib().nbo_session_push_cross(self._h, int(token), memory._h)
+        if status:
+            raise OracleError(status)
 
     def head_output(self, code: int):
         """Session::head_output (session.rs:150-154); None without that head."""
@@ -354,3 +365,34 @@ def ladder_select(layers: int, depth: int):
 
 def half_to_f32(bits: int) -> float:
     return float(lib().nbo_half_to_f32(bits))
+
+
+class CrossMemory:
+    """CrossWeights::memory (whistle/src/cross.rs:58-99) of an encoder output [frames][d_model]."""
+
+    def __init__(self, model: Model, encoded: np.ndarray):
+        enc = np.ascontiguousarray(encoded, dtype=np.float32)
+        self.frames = enc.shape[0]
+        self.model = model
+        h = ctypes.c_void_p()
+        status = lib().nbo_cross_memory_new(model._h, _ptr(enc), self.frames, ctypes.byref(h))
+        if status:
+            raise OracleError(status)
+        self._h = h
+
+    def read(self, layer: int, heads: int, head_dim: int = 64):
+        keys = np.empty((self.frames, heads, head_dim), dtype=np.int8)
+        values = np.empty_like(keys)
+        ks = np.empty((self.frames, heads), dtype=np.float32)
+        vs = np.empty_like(ks)
+        lib().nbo_cross_memory_read(self._h, layer, _ptr(keys), _ptr(ks), _ptr(values), _ptr(vs))
+        return keys, ks, values, vs
+
+    def __del__(self):
+        if getattr(self, "_h", None):
+            lib().nbo_cross_memory_free(self._h)
+            self._h = None
+
+
+def text_vocab(model: Model) -> int:
+    return int(lib().nbo_model_text_vocab(model._h))

@@ -10,7 +10,10 @@ embedding; per layer norm_in, q, k, v, [q, k, v conv taps], q_norm, k_norm, gate
 post_norm, attn_gate, pre_hada and 13 Hadamard tensors; nine lane tensors; two
 Hadamard permutations; [per engram site: tables, key_proj, value_proj, taps];
 final_norm; [the probe-head manifest and each head's probes, gain, query,
-row_bias, proj, bias (and calibration for code 3)]; the tokenizer blob.
+row_bias, proj, bias (and calibration for code 3)]; [a Whistle audio section:
+manifest, per decoder layer norm, q/k/v/gate/out projections, q_norm, k_norm,
+post_norm and gate, the position gate, and one-value placeholders for the
+encoder, which this build does not run]; the tokenizer blob.
 
 Weights are codebook-quantised (kind 3): uniform indices, packed least
 significant bit first, and one fp16 norm per row drawn log-uniform in
@@ -81,6 +84,7 @@ class Geometry:
     probes_per_layer: int = 2
     head_queries: int = 2
     head_outputs: int = 3
+    text_vocab: int = 0       # > 0: a Whistle archive (audio manifest, cross-attention tensors per decoder layer)
     extra: dict = field(default_factory=dict)
 
 
@@ -263,6 +267,23 @@ def write_archive(path: str, seed: int = 0, geometry: Geometry | None = None) ->
             w.single(0.1 * rng.standard_normal(g.head_outputs))  # bias
             if code == 3:
                 w.single(rng.standard_normal(4))  # calibration
+    if g.text_vocab:  # crates/cact/src/layout.rs:256-293: manifest, 10 cross tensors per decoder layer, position gate, encoder
+        # manifest: magic, version, text_vocab, encoder_layers, encoder_lanes, conv_kernel, stem_channels, stem_stages,
+        # mels, sample_rate, fft_size, window, hop. The encoder is not part of this build: no encoder layers, one stem
+        # stage, and one-value placeholders for its lanes, final norm, stem and mel tensors.
+        w.single(np.array([3246, 1, g.text_vocab, 0, lanes, 31, 64, 1, 80, 16000, 400, 400, 160], dtype=np.float32))
+        for _ in range(L):
+            w.single(zeros(d))  # norm
+            for _ in range(4):  # q, k, v, gate projections
+                w.codebook_matrix(rng, H * hd, d, g.projection_bits, g.group)
+            w.codebook_matrix(rng, d, H * hd, g.projection_bits, g.group)  # out_proj
+            w.single(zeros(hd))  # q_norm
+            w.single(zeros(hd))  # k_norm
+            w.single(zeros(d))  # post_norm
+            w.single(rng.standard_normal(1))  # gate
+        w.single(rng.standard_normal(1))  # position gate
+        for _ in range(9 + 1 + 1 + 1 + 1):  # encoder lanes, final norm, stem first and out, mel
+            w.single(zeros(1))
     w.add(KIND_RAW, (0,), tokenizer_blob(g.vocab))
 
     header = [FORMAT_TAG, len(w.records), codebook.size, 0, 8, g.vocab, g.out_vocab, d, H, KV, L, hd, hd,

@@ -238,3 +238,29 @@ def test_probe_heads_follow_the_reference_tests(oracle_lib, kats):
     shallow.feed(ids)
     assert shallow.head_output(2).shape == fed.head_output(2).shape
     assert not np.array_equal(shallow.head_output(2), fed.head_output(2))
+
+
+def test_whistle_cross_attention_restatement(oracle_lib):
+    """whistle/src/cross.rs: the memory of an encoder output is deterministic,
+    the cross hook changes the decoder's result, and without a cross memory
+    a Whistle archive decodes as its plain decoder."""
+    from rustyneedle_b200 import synthetic
+
+    path = synthetic.cached_archive(seed=18, geometry=_features(text_vocab=8000))
+    m = oracle_lib.Model.open(path, oracle_lib.MODE_INT, 0)
+    assert oracle_lib.text_vocab(m) == 8000
+    enc = np.random.default_rng(1).standard_normal((120, 512)).astype(np.float32)
+    a, b = oracle_lib.CrossMemory(m, enc), oracle_lib.CrossMemory(m, enc)
+    for layer in range(4):
+        for x, y in zip(a.read(layer, 8), b.read(layer, 8)):
+            assert np.array_equal(x, y)
+    plain, crossed = oracle_lib.Session(m), oracle_lib.Session(m)
+    for t in (1, 8003, 40, 41):
+        plain.push(t)
+        crossed.push_cross(t, a)
+    assert not np.array_equal(plain.logits(), crossed.logits())
+    decoder = oracle_lib.Model.open(synthetic.cached_archive(seed=18, geometry=_features()), oracle_lib.MODE_INT, 0)
+    twin = oracle_lib.Session(decoder)
+    for t in (1, 8003, 40, 41):
+        twin.push(t)
+    assert np.array_equal(plain.logits(), twin.logits())
