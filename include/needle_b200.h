@@ -121,6 +121,25 @@ nb_status nb_session_head_output(nb_session* session, uint32_t code, float* out,
  * queries x d_model floats (Engine::embed reads head 3's, engine.rs:113-123). */
 nb_status nb_session_pooled_readout(nb_session* session, uint32_t code, float* out, size_t capacity, size_t* count);
 
+/* Whistle (crates/whistle): a cross-attention memory of one encoder output.
+ * CrossWeights::memory (whistle/src/cross.rs:58-99): the gated positional
+ * signal added to `encoded` ([frames][d_model] f32, host memory), then every
+ * decoder layer's int8 keys and values. NB_ERR_UNSUPPORTED when the archive
+ * carries no audio section; frames in 1..4096. */
+typedef struct nb_cross_memory nb_cross_memory;
+nb_status nb_cross_memory_create(nb_model* model, const float* encoded, size_t frames, nb_cross_memory** out);
+void nb_cross_memory_release(nb_cross_memory* memory);
+
+/* Session::push_with(token, Some(CrossState)) for every later pass of the
+ * session (session.rs:126-128, whistle lib.rs:255-293): each layer's cross
+ * attention over `memory` runs after its self-attention residual. NULL
+ * detaches. The session keeps the memory alive; clones share it. */
+nb_status nb_session_set_cross(nb_session* session, nb_cross_memory* memory);
+
+/* AudioManifest::text_vocab (crates/cact/src/layout.rs:265-279): the ids below
+ * it are text, those from it on name languages; 0 without an audio section. */
+size_t nb_model_text_vocab(const nb_model* model);
+
 /* Session::len (session.rs:44-46). */
 size_t nb_session_len(const nb_session* session);
 

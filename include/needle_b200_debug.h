@@ -58,6 +58,11 @@ nb_status nb_debug_kv(nb_session* session, uint32_t layer, int8_t* keys, float* 
  * must read (keys, values and their scales of every attended position). */
 nb_status nb_debug_time_attention(nb_batch* batch, uint32_t reps, float* ms_per_launch, double* bytes_per_launch);
 
+/* A cross memory's keys, key scales, values and value scales of one decoder
+ * layer: [frames][heads][64] int8 and [frames][heads] f32 each. */
+nb_status nb_debug_cross_memory(const nb_cross_memory* memory, int layer, int8_t* keys, float* key_scales, int8_t* values,
+                                float* value_scales);
+
 /* Kernels in the batch's step graph (the last one recorded; 0 before the
  * first step). No reference counterpart: the bench's launch count. */
 nb_status nb_debug_step_kernels(nb_batch* batch, uint32_t* kernels);

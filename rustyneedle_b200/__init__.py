@@ -17,6 +17,7 @@ from __future__ import annotations
 from ._native import (  # noqa: F401
     Batch,
     ContextOverflow,
+    CrossMemory,
     DepthError,
     Model,
     ModelConfig,
@@ -28,4 +29,4 @@ from ._native import (  # noqa: F401
 )
 
 __all__ = ["Model", "Session", "Batch", "ModelConfig", "StepStats", "NeedleError", "DepthError", "ContextOverflow",
-           "feed_many", "library_path"]
+           "feed_many", "library_path", "CrossMemory"]

@@ -83,6 +83,10 @@ def lib() -> ctypes.CDLL:
             "nb_sessions_feed": (I, [P, P, P, SZ]),
             "nb_session_push": (I, [P, U32]),
             "nb_session_logits": (I, [P, P, SZ]),
+            "nb_cross_memory_create": (I, [P, P, SZ, P]),
+            "nb_cross_memory_release": (None, [P]),
+            "nb_session_set_cross": (I, [P, P]),
+            "nb_model_text_vocab": (SZ, [P]),
             "nb_session_head_output": (I, [P, U32, P, SZ, ctypes.POINTER(SZ)]),
             "nb_session_pooled_readout": (I, [P, U32, P, SZ, ctypes.POINTER(SZ)]),
             "nb_session_len": (SZ, [P]),
@@ -163,6 +167,10 @@ class Model:
     def active_layers(self) -> list:
         return list(self.config.active_layers)
 
+    def text_vocab(self) -> int:
+        """AudioManifest::text_vocab of a Whistle archive (0 without an audio section)."""
+        return int(lib().nb_model_text_vocab(self._h))
+
     def synchronize(self) -> None:
         _check(lib().nb_model_synchronize(self._h))
 
@@ -208,6 +216,12 @@ class Session:
         _check(lib().nb_session_logits(self._h, _ptr(out), out.size))
         return out
 
+    def set_cross(self, memory: "CrossMemory | None") -> None:
+        """Every later pass attends to `memory` after each layer's attention
+        (Session::push_with with a CrossState); None detaches."""
+        _check(lib().nb_session_set_cross(self._h, memory._h if memory is not None else None))
+        self.cross = memory
+
     def _head(self, fn, code: int):
         out = np.empty(1 << 14, dtype=np.float32)
         n = ctypes.c_size_t()
@@ -240,6 +254,29 @@ class Session:
     def close(self) -> None:
         if getattr(self, "_h", None):
             lib().nb_session_release(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class CrossMemory:
+    """CrossWeights::memory of an encoder output [frames][d_model] (Whistle)."""
+
+    def __init__(self, model: Model, encoded: np.ndarray):
+        enc = np.ascontiguousarray(encoded, dtype=np.float32)
+        self.model = model
+        self.frames = int(enc.shape[0])
+        h = ctypes.c_void_p()
+        _check(lib().nb_cross_memory_create(model._h, _ptr(enc), self.frames, ctypes.byref(h)))
+        self._h = h
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            lib().nb_cross_memory_release(self._h)
             self._h = None
 
     def __del__(self):

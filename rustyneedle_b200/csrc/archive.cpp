@@ -250,7 +250,13 @@ Layout Archive::resolve() const {
     std::memcpy(v, data(manifest), sizeof v);
     if (v[0] != 3246.0f) fail(NB_ERR_ARCHIVE, "unexpected tensor layout: audio manifest is malformed");
     uint32_t encoder_layers = (uint32_t)v[3], stem_stages = (uint32_t)v[7];
-    for (uint32_t i = 0; i < geo_.num_layers * 10 + 1; ++i) take();
+    L.text_vocab = (uint32_t)v[2];
+    for (uint32_t l = 0; l < geo_.num_layers; ++l) {
+      std::array<uint32_t, 10> c;
+      for (uint32_t& x : c) x = take();
+      L.cross.push_back(c);
+    }
+    L.position_gate = take();
     for (uint32_t l = 0; l < encoder_layers; ++l)
       for (int i = 0; i < 6 + 11 + 26; ++i) take();
     for (int i = 0; i < 9 + 1 + 1; ++i) take();

@@ -66,6 +66,9 @@ struct Layout {
   struct HeadIdx { uint32_t code, probes, gain, query, row_bias, proj, bias; };
   std::vector<HeadIdx> heads;  // crates/cact/src/layout.rs:236-254
   bool audio = false;
+  std::vector<std::array<uint32_t, 10>> cross;  // per decoder layer: norm, q, k, v, gate, out, q_norm, k_norm, post_norm, gate
+  uint32_t position_gate = 0;
+  uint32_t text_vocab = 0;
   uint32_t tokenizer = 0;
 };
 

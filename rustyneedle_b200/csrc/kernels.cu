@@ -1638,7 +1638,8 @@ __device__ __forceinline__ bool block_front(const ModelDev& md, const LayerDev& 
     if (tid == 0 && !mbar_wait(bar, 0)) atomicExch(error, 1);  // no copy outlives the CTA
     return false;
   }
-  stage_async(s_a, w.outp + (size_t)t * d, d);
+  // with Whistle cross attention, k_resid and the cross step have formed x after the residual
+  stage_async(s_a, (md.cross ? w.xr : w.outp) + (size_t)t * d, d);
   if (md.conv_ring) conv_ring_store(md, L, w, M, t, part, parts);
   if (L.engram && L.engram->ring) engram_ring_store(md, *L.engram, w, M, t, part, parts);
   cp_async_wait_all();
@@ -1646,16 +1647,18 @@ __device__ __forceinline__ bool block_front(const ModelDev& md, const LayerDev& 
   // every thread past this point; then each thread waits for the bulk copies
   __syncthreads();
   if (!mbar_wait(bar, 0) && tid == 0) atomicExch(error, 1);
-  if (warp == 0) {
-    float ss = sum_of_squares_warp(s_a, d);
-    if (lane == 0) s_inv = inverse_rms(ss, d);
+  if (!md.cross) {
+    if (warp == 0) {
+      float ss = sum_of_squares_warp(s_a, d);
+      if (lane == 0) s_inv = inverse_rms(ss, d);
+    }
+    __syncthreads();
+    for (int i = tid; i < d; i += BLOCK_THREADS) {
+      float a = fmul(fmul(fadd(1.0f, s_gpost[i]), s_a[i]), s_inv);
+      s_a[i] = fadd(s_x[i], fmul(s_gate, a));
+    }
+    __syncthreads();
   }
-  __syncthreads();
-  for (int i = tid; i < d; i += BLOCK_THREADS) {
-    float a = fmul(fmul(fadd(1.0f, s_gpost[i]), s_a[i]), s_inv);
-    s_a[i] = fadd(s_x[i], fmul(s_gate, a));
-  }
-  __syncthreads();
   if (warp == 0) {
     float ss = sum_of_squares_warp(s_a, d);
     if (lane == 0) s_inv = inverse_rms(ss, d);
@@ -2073,6 +2076,241 @@ __global__ void k_fill(float* __restrict__ p, size_t n, float value) {
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) p[i] = value;
 }
 
+// ------------------------------------------------- Whistle cross attention
+// A 64-value head held by a warp (lane: elements lane, lane + 32):
+// zero_centred_norm_in_place (ops.rs:52-58; the square sum in the reference's
+// eight-lane order), then quantise_int8 (ops.rs:112-118) into c0, c1; returns
+// the scale.
+__device__ __forceinline__ float norm_quant_head64(float e0, float e1, const float* gain, bool norm, int8_t& c0, int8_t& c1) {
+  const int lane = threadIdx.x & 31;
+  if (norm) {
+    float acc = 0.0f;
+    const int chain = lane & 7;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      const float v = __shfl_sync(FULL, e0, chain + 8 * c);
+      acc = fadd(acc, fmul(v, v));
+    }
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      const float v = __shfl_sync(FULL, e1, chain + 8 * c);
+      acc = fadd(acc, fmul(v, v));
+    }
+    float s = SUM_START;
+#pragma unroll
+    for (int l = 0; l < 8; ++l) s = fadd(s, __shfl_sync(FULL, acc, l));
+    const float inv = inverse_rms(s, HEAD_DIM);
+    e0 = fmul(fmul(fadd(1.0f, gain[lane]), e0), inv);
+    e1 = fmul(fmul(fadd(1.0f, gain[lane + 32]), e1), inv);
+  }
+  const float peak = warp_max(fmaxf(fabsf(e0), fabsf(e1)));
+  const float scale = int8_scale_of(peak);
+  c0 = (int8_t)clampf(rintf(fdiv(e0, scale)), -128.0f, 127.0f);
+  c1 = (int8_t)clampf(rintf(fdiv(e1, scale)), -128.0f, 127.0f);
+  return scale;
+}
+
+// CrossWeights::memory, first step (cross.rs:64-74): row t of the encoder
+// output plus the gated positional signal (sin in the first half, cos in the
+// second; the angles' sin and cos come as tables). grid frames, block 128.
+__global__ void __launch_bounds__(128) k_cross_memory_in(const float* __restrict__ encoded, const float* __restrict__ sin_tab,
+                                                         const float* __restrict__ cos_tab, float gate, int d, float* __restrict__ out) {
+  const int t = blockIdx.x, half = d / 2;
+  for (int j = threadIdx.x; j < half; j += blockDim.x) {
+    out[(size_t)t * d + j] = fadd(encoded[(size_t)t * d + j], fmul(gate, sin_tab[(size_t)t * half + j]));
+    out[(size_t)t * d + half + j] = fadd(encoded[(size_t)t * d + half + j], fmul(gate, cos_tab[(size_t)t * half + j]));
+  }
+}
+
+// CrossWeights::memory, last step (cross.rs:83-96): per (frame, head) the key
+// normed with k_norm and quantised, the value quantised. kv: [frames][2d]
+// (keys, then values). grid frames, block 64 · heads (a warp per head and side).
+__global__ void k_cross_memory_heads(const float* __restrict__ kv, int d, const float* __restrict__ k_norm, int8_t* __restrict__ keys,
+                                     float* __restrict__ kscale, int8_t* __restrict__ values, float* __restrict__ vscale) {
+  const int t = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31, heads = d / HEAD_DIM;
+  const bool key = warp < heads;
+  const int h = key ? warp : warp - heads;
+  const float* src = kv + (size_t)t * 2 * d + (key ? 0 : d) + h * HEAD_DIM;
+  int8_t c0, c1;
+  const float scale = norm_quant_head64(src[lane], src[lane + 32], k_norm, key, c0, c1);
+  int8_t* codes = (key ? keys : values) + ((size_t)t * heads + h) * HEAD_DIM;
+  codes[lane] = c0;
+  codes[lane + 32] = c1;
+  if (lane == 0) (key ? kscale : vscale)[(size_t)t * heads + h] = scale;
+}
+
+// x after the layer's attention residual (session.rs:121-125, as the block
+// finish forms it) into w.xr, the input of the cross attention. grid M, block 128.
+__global__ void __launch_bounds__(128) k_resid(ModelDev md, LayerDev L, Work w, int M) {
+  __shared__ __align__(16) float s_a[MAX_D];
+  __shared__ float s_inv;
+  pdl_wait();
+  const int t = blockIdx.x, d = (int)md.d_model;
+  if (t >= M || load_meta(w.meta, t).slot < 0) return;
+  for (int i = threadIdx.x; i < d; i += blockDim.x) s_a[i] = __ldcg(w.outp + (size_t)t * d + i);
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    const float ss = sum_of_squares_warp(s_a, d);
+    if (threadIdx.x == 0) s_inv = inverse_rms(ss, d);
+  }
+  __syncthreads();
+  const float gate = sigmoid(L.attn_gate);
+  for (int i = threadIdx.x; i < d; i += blockDim.x) {
+    const float a = fmul(fmul(fadd(1.0f, L.post_norm[i]), s_a[i]), s_inv);
+    w.xr[(size_t)t * d + i] = fadd(__ldcg(w.x + (size_t)t * d + i), fmul(gate, a));
+  }
+}
+
+// CrossState::apply (cross.rs:121-130), first step: zero_centred_norm of x
+// with the layer's cross norm, then fake_quantise_int8 and the per-group
+// rotation and codes of the q|gate product's input. grid M, block 128.
+__global__ void __launch_bounds__(128) k_cross_q(ModelDev md, int layer, Work w, int M) {
+  __shared__ __align__(16) float s_v[PREP_MAX_K];
+  __shared__ float s_red[4];
+  __shared__ float s_inv;
+  pdl_wait();
+  const int t = blockIdx.x, d = (int)md.d_model;
+  if (t >= M) return;
+  const TokenMeta meta = load_meta(w.meta, t);
+  if (meta.slot < 0 || !md.slot_cross[meta.slot]) return;
+  const CrossLayerDev& C = md.cross[layer];
+  for (int i = threadIdx.x; i < d; i += blockDim.x) s_v[i] = __ldcg(w.xr + (size_t)t * d + i);
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    const float ss = sum_of_squares_warp(s_v, d);
+    if (threadIdx.x == 0) s_inv = inverse_rms(ss, d);
+  }
+  __syncthreads();
+  float* normed = w.attn + (size_t)t * md.heads * HEAD_DIM;  // free here: the attention rows are consumed
+  for (int i = threadIdx.x; i < d; i += blockDim.x) normed[i] = fmul(fmul(fadd(1.0f, C.norm[i]), s_v[i]), s_inv);
+  __syncthreads();
+  prep_token(normed, nullptr, d, w.act, w.act_scale, t, md.inv_sqrt_group, 1, 0, s_v, s_red);
+}
+
+// CrossState::apply, per head (cross.rs:131-163): the query normed with q_norm
+// and quantised; int8 scores over the memory's frames, dot · key_scale ·
+// query_scale; softmax_in_place (peak, fast_exp, one ordered total from +0.0,
+// times 1 / total); the context Σ_frame (value_scale · weight) · code in frame
+// order per dimension; times sigmoid(gate) (cross.rs:164-166) into the rows of
+// w.attn. grid (M, heads), block 256.
+constexpr int CROSS_THREADS = 256;
+__global__ void __launch_bounds__(CROSS_THREADS) k_cross_attend(ModelDev md, int layer, Work w, int M) {
+  extern __shared__ float s_sc[];  // [MAX_CROSS_FRAMES] scores, then weights; [MAX_CROSS_FRAMES] value scale · weight
+  float* s_vw = s_sc + MAX_CROSS_FRAMES;
+  __shared__ __align__(16) int8_t s_q[HEAD_DIM];
+  __shared__ float s_qs, s_red[CROSS_THREADS / 32], s_peak, s_inverse;
+  pdl_wait();
+  const int t = blockIdx.x, h = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  if (t >= M) return;
+  const TokenMeta meta = load_meta(w.meta, t);
+  if (meta.slot < 0) return;
+  const CrossMemDev* mem = md.slot_cross[meta.slot];
+  if (!mem) return;
+  const CrossLayerDev& C = md.cross[layer];
+  const int d = (int)md.d_model, heads = (int)md.heads, frames = mem->frames;
+  const int8_t* keys = mem->keys + (size_t)layer * frames * heads * HEAD_DIM;
+  const float* kscale = mem->kscale + (size_t)layer * frames * heads;
+  const int8_t* values = mem->values + (size_t)layer * frames * heads * HEAD_DIM;
+  const float* vscale = mem->vscale + (size_t)layer * frames * heads;
+  if (warp == 0) {
+    const float* q = w.cq + (size_t)t * 2 * d + h * HEAD_DIM;
+    int8_t c0, c1;
+    const float scale = norm_quant_head64(__ldcg(q + lane), __ldcg(q + lane + 32), C.q_norm, true, c0, c1);
+    s_q[lane] = c0;
+    s_q[lane + 32] = c1;
+    if (lane == 0) s_qs = fmul(scale, md.inv_root_qk);
+  }
+  __syncthreads();
+  float peak = -INFINITY;
+  const uint4* qv = reinterpret_cast<const uint4*>(s_q);
+  for (int f = tid; f < frames; f += CROSS_THREADS) {
+    const uint4* kp = reinterpret_cast<const uint4*>(keys + ((size_t)f * heads + h) * HEAD_DIM);
+    int part[4] = {0, 0, 0, 0};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const uint4 kk = kp[k], qq = qv[k];
+      part[0] = dp4a(kk.x, qq.x, part[0]);
+      part[1] = dp4a(kk.y, qq.y, part[1]);
+      part[2] = dp4a(kk.z, qq.z, part[2]);
+      part[3] = dp4a(kk.w, qq.w, part[3]);
+    }
+    const int dot = (part[0] + part[1]) + (part[2] + part[3]);
+    const float sc = fmul(fmul((float)dot, kscale[(size_t)f * heads + h]), s_qs);
+    s_sc[f] = sc;
+    peak = fmaxf(peak, sc);
+  }
+  peak = warp_max(peak);
+  if (lane == 0) s_red[warp] = peak;
+  __syncthreads();
+  if (tid == 0) {
+    float m = s_red[0];
+    for (int k = 1; k < CROSS_THREADS / 32; ++k) m = fmaxf(m, s_red[k]);
+    s_peak = m;
+  }
+  __syncthreads();
+  for (int f = tid; f < frames; f += CROSS_THREADS) s_sc[f] = fast_exp(fsub(s_sc[f], s_peak));
+  __syncthreads();
+  if (warp == 0) {  // the total, one chain in frame order from +0.0 (ops.rs:92-101)
+    float total = 0.0f;
+    if (lane == 0) {
+      int f = 0;
+      for (; f + 16 <= frames; f += 16) {
+        float v[16];
+#pragma unroll
+        for (int k = 0; k < 16; ++k) v[k] = s_sc[f + k];
+#pragma unroll
+        for (int k = 0; k < 16; ++k) total = fadd(total, v[k]);
+      }
+      for (; f < frames; ++f) total = fadd(total, s_sc[f]);
+      s_inverse = fdiv(1.0f, total);
+    }
+  }
+  __syncthreads();
+  for (int f = tid; f < frames; f += CROSS_THREADS) s_vw[f] = fmul(vscale[(size_t)f * heads + h], fmul(s_sc[f], s_inverse));
+  __syncthreads();
+  pdl_trigger();
+  if (tid < HEAD_DIM) {
+    const int8_t* vcol = values + (size_t)h * HEAD_DIM + tid;
+    const size_t stride = (size_t)heads * HEAD_DIM;
+    float acc = 0.0f;
+    int f = 0;
+    for (; f + 8 <= frames; f += 8) {
+      float c[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) c[k] = (float)vcol[(size_t)(f + k) * stride];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) acc = fadd(acc, fmul(s_vw[f + k], c[k]));
+    }
+    for (; f < frames; ++f) acc = fadd(acc, fmul(s_vw[f], (float)vcol[(size_t)f * stride]));
+    const float g = __ldcg(w.cq + (size_t)t * 2 * d + d + h * HEAD_DIM + tid);
+    w.attn[(size_t)t * heads * HEAD_DIM + h * HEAD_DIM + tid] = fmul(acc, sigmoid(g));
+  }
+}
+
+// CrossState::apply, last step (cross.rs:170-181): the out product's row
+// normed with post_norm, then x += sigmoid(gate) · attended. grid M, block 128.
+__global__ void __launch_bounds__(128) k_cross_finish(ModelDev md, int layer, Work w, int M) {
+  __shared__ __align__(16) float s_a[MAX_D];
+  __shared__ float s_inv;
+  pdl_wait();
+  const int t = blockIdx.x, d = (int)md.d_model;
+  if (t >= M) return;
+  const TokenMeta meta = load_meta(w.meta, t);
+  if (meta.slot < 0 || !md.slot_cross[meta.slot]) return;
+  const CrossLayerDev& C = md.cross[layer];
+  for (int i = threadIdx.x; i < d; i += blockDim.x) s_a[i] = __ldcg(w.outp + (size_t)t * d + i);
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    const float ss = sum_of_squares_warp(s_a, d);
+    if (threadIdx.x == 0) s_inv = inverse_rms(ss, d);
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < d; i += blockDim.x) {
+    const float a = fmul(fmul(fadd(1.0f, C.post_norm[i]), s_a[i]), s_inv);
+    w.xr[(size_t)t * d + i] = fadd(__ldcg(w.xr + (size_t)t * d + i), fmul(C.gain, a));
+  }
+}
+
 // ------------------------------------------------------------------ select
 // argmax / argmax_allowed (generator.rs:147-165): the first index holding the
 // maximum over the allowed ids, or over all ids when none is allowed.
@@ -2235,6 +2473,7 @@ cudaError_t configure(const ModelDev& md, int t_cap) {
   if ((e = cudaFuncSetAttribute(k_block_split<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)block_split_smem(md)))) return e;
   if ((e = cudaFuncSetAttribute(k_block_split<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)block_split_smem(md)))) return e;
   if ((e = cudaFuncSetAttribute(k_stats, cudaFuncAttributeMaxDynamicSharedMemorySize, 2 * 8192 * 4))) return e;
+  if ((e = cudaFuncSetAttribute(k_cross_attend, cudaFuncAttributeMaxDynamicSharedMemorySize, 2 * MAX_CROSS_FRAMES * 4))) return e;
   if ((e = cudaFuncSetAttribute(k_gemm<16, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gemm_smem<16>()))) return e;
   if ((e = cudaFuncSetAttribute(k_gemm<32, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gemm_smem<32>()))) return e;
   if ((e = cudaFuncSetAttribute(k_gemm<16, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gemm_smem<16>()))) return e;
@@ -2349,8 +2588,8 @@ static void launch_block(const ModelDev& md, const LayerDev& L, const Work& w, i
   }
 }
 
-void launch_layer(const ModelDev& md, const LayerDev& L, const EngramDev* engram, const Work& w, const KvDev& kv, int M, int layer,
-                  int slot, int t_cap, bool distinct, cudaStream_t st) {
+void launch_layer(const ModelDev& md, const LayerDev& L, const EngramDev* engram, const CrossLayerDev* cross, const Work& w,
+                  const KvDev& kv, int M, int layer, int slot, int t_cap, bool distinct, cudaStream_t st) {
   t_pass_tokens = M;
   const int d = md.d_model, H = md.heads, KV = md.kv_heads;
   const int proj_stride = (2 * H + 2 * KV) * HEAD_DIM;
@@ -2373,7 +2612,33 @@ void launch_layer(const ModelDev& md, const LayerDev& L, const EngramDev* engram
            (const float*)(w.proj + (H + 2 * KV) * HEAD_DIM), proj_stride, H * HEAD_DIM, w.act, w.act_scale, M, w.meta,
            md.inv_sqrt_group, 1, 0);
   project(L.out, w.act, w.act_scale, w.outp, M, d, w.meta, st, md.error);
+  if (cross) {  // Whistle: CrossState::apply after the attention residual (session.rs:126-128)
+    launch(k_resid, M, 128, 0, st, md, L, w, M);
+    launch(k_cross_q, M, 128, 0, st, md, layer, w, M);
+    project(cross->qg, w.act, w.act_scale, w.cq, M, 2 * d, w.meta, st, md.error);
+    launch(k_cross_attend, dim3(M, md.heads), CROSS_THREADS, 2 * MAX_CROSS_FRAMES * sizeof(float), st, md, layer, w, M);
+    launch(k_prep, M, 128, 0, st, (const float*)w.attn, H * HEAD_DIM, (const int32_t*)nullptr, (const float*)nullptr, 0, H * HEAD_DIM,
+           w.act, w.act_scale, M, w.meta, md.inv_sqrt_group, 1, 0);
+    project(cross->out, w.act, w.act_scale, w.outp, M, d, w.meta, st, md.error);
+    launch(k_cross_finish, M, 128, 0, st, md, layer, w, M);
+  }
   launch_block(md, L, w, M, st);
+}
+
+cudaError_t cross_memory(const ModelDev& md, const std::vector<CrossLayerDev>& layers, const float* encoded, int frames,
+                         const float* sin_tab, const float* cos_tab, float gate, float* rows, int8_t* act, float* act_scale, int act_rows,
+                         float* kv, int8_t* keys, float* kscale, int8_t* values, float* vscale, cudaStream_t st) {
+  const int d = (int)md.d_model, heads = (int)md.heads;
+  k_cross_memory_in<<<frames, 128, 0, st>>>(encoded, sin_tab, cos_tab, gate, d, rows);
+  k_prep<<<frames, 128, 0, st>>>(rows, d, (const int32_t*)nullptr, (const float*)nullptr, 0, d, act, act_scale, frames,
+                                 (const TokenMeta*)nullptr, md.inv_sqrt_group, 1, act_rows);
+  for (size_t l = 0; l < layers.size(); ++l) {
+    project(layers[l].kv, act, act_scale, kv, frames, 2 * d, nullptr, st, md.error, act_rows);
+    const size_t at = l * (size_t)frames * heads;
+    k_cross_memory_heads<<<frames, 64 * heads, 0, st>>>(kv, d, layers[l].k_norm, keys + at * HEAD_DIM, kscale + at,
+                                                       values + at * HEAD_DIM, vscale + at);
+  }
+  return cudaGetLastError();
 }
 
 void launch_observe(const ModelDev& md, const Work& w, const float* stream, int M, int row, cudaStream_t st) {

@@ -3,6 +3,8 @@
 
 #include <cuda_runtime.h>
 
+#include <vector>
+
 #include "exactmath.h"
 #include "layout.h"
 
@@ -18,8 +20,15 @@ void launch_embed(const nbl::ModelDev& md, const nbl::Work& w, int M, cudaStream
 // One decoder layer of M tokens. `distinct`: every token of the pass belongs
 // to a different sequence (a decode step, or a one-token feed). `engram`: the
 // host copy of the layer's engram site, or null.
-void launch_layer(const nbl::ModelDev& md, const nbl::LayerDev& L, const nbl::EngramDev* engram, const nbl::Work& w,
-                  const nbl::KvDev& kv, int M, int layer, int slot, int t_cap, bool distinct, cudaStream_t st);
+void launch_layer(const nbl::ModelDev& md, const nbl::LayerDev& L, const nbl::EngramDev* engram, const nbl::CrossLayerDev* cross,
+                  const nbl::Work& w, const nbl::KvDev& kv, int M, int layer, int slot, int t_cap, bool distinct, cudaStream_t st);
+// CrossWeights::memory of `frames` encoder rows (device): `rows` (frames · d
+// floats), `act`/`act_scale` (a K = d activation buffer of `act_rows` rows)
+// and `kv` (frames · 2d floats) are scratch; keys/values [layers][frames]
+// [heads][64] and their scales [layers][frames][heads] are written.
+cudaError_t cross_memory(const nbl::ModelDev& md, const std::vector<nbl::CrossLayerDev>& layers, const float* encoded, int frames,
+                         const float* sin_tab, const float* cos_tab, float gate, float* rows, int8_t* act, float* act_scale,
+                         int act_rows, float* kv, int8_t* keys, float* kscale, int8_t* values, float* vscale, cudaStream_t st);
 void launch_final(const nbl::ModelDev& md, const nbl::Work& w, float* hidden, int M, cudaStream_t st);
 // ProbeHead::observe of cell row `row` (0: the embedding, layer + 1) of every
 // token of the pass; `stream` holds the lanes after that layer.

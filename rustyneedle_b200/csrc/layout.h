@@ -39,6 +39,12 @@
 // accumulators peak, total [rows][probes] and weighted [rows][probes][d], all
 // indexed by the archive row (0 = the embedding cell, layer + 1), so every
 // depth uses its subset.
+//
+// Whistle cross attention (whistle/src/cross.rs): per decoder layer the q|gate
+// and k|v products (k|v builds the memory) and the out product; a memory holds
+// for every layer the int8 keys and values [frame][head][64] of one encoder
+// output with their scales [frame][head]; slot_cross[slot] points at the
+// memory a session attends to (null: none).
 #pragma once
 
 #include <stddef.h>
@@ -144,6 +150,23 @@ struct HeadDev {
 };
 constexpr int MAX_PROBE_HEADS = 4;
 
+struct CrossLayerDev {
+  QMat qg;   // q_proj rows, then gate_proj rows
+  QMat kv;   // k_proj rows, then v_proj rows (the memory)
+  QMat out;
+  const float *norm, *q_norm, *k_norm, *post_norm;
+  float gain;  // sigmoid(gate)
+};
+
+struct CrossMemDev {
+  int frames;
+  const int8_t* keys;    // [layers][frames][heads][64]
+  const float* kscale;   // [layers][frames][heads]
+  const int8_t* values;  // [layers][frames][heads][64]
+  const float* vscale;   // [layers][frames][heads]
+};
+constexpr int MAX_CROSS_FRAMES = 4096;
+
 struct LayerDev {
   QMat qkvg;  // q, k, v and gate_proj stacked row-wise (one fused product, matrix.rs:167-193)
   QMat out;
@@ -185,6 +208,8 @@ struct ModelDev {
   uint32_t token_rows;        // max order - 1
   uint32_t num_probe_heads;
   const HeadDev* probe_heads;  // [num_probe_heads] (device memory)
+  const CrossLayerDev* cross;              // [num_layers] (device memory); null without a Whistle section
+  const CrossMemDev* const* slot_cross;    // [slots] the memory each session attends to (null: none)
 };
 
 // Per-token metadata of one forward pass.
@@ -218,6 +243,8 @@ struct Work {
   float* cells;             // [M][d] a layer's lane means (probe heads)
   float* scores;            // [M][heads · probes] their probe scores / sqrt(d)
   float* scan;              // [M][heads · probes][2] the run's rescale and weight per token
+  float* xr;                // [M][d] x after the attention residual and the cross attention (Whistle)
+  float* cq;                // [M][2d] the cross attention's q and gate rows (Whistle)
   uint32_t act_rows;        // rows of the activation buffer's K-chunk-major layout
 };
 

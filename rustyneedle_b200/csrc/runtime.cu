@@ -191,6 +191,11 @@ struct Engine {
   size_t conv_ring_floats = 0;  // per slot: md.conv_ring's [layers][taps - 1][q | k | v]
   std::vector<EngramDev> engram_sites;  // host copies (the layers point at the device copies)
   std::vector<HeadDev> heads;           // host copies of md.heads
+  std::vector<CrossLayerDev> cross_layers;  // Whistle: host copies of md.cross
+  float position_gate = 0.0f;               // sigmoid of the archive's position gate
+  uint32_t text_vocab = 0;
+  const CrossMemDev** d_slot_cross = nullptr;  // md.slot_cross
+  const CrossLayerDev* cross_of(int layer) const { return cross_layers.empty() ? nullptr : &cross_layers[layer]; }
   uint32_t act_groups = 0;  // act_scale floats per token: the widest product's groups
   // probe heads: (head, probe) pairs, the widest projection K, the most slots per session
   uint32_t head_pairs = 0, head_k = 0;
@@ -720,6 +725,44 @@ std::shared_ptr<Engine> open_engine(const char* path, const nb_options* opt) {
     H.bias = A.upload(floats_of(a, t.bias, H.outputs, "probe head bias"), st);
   }
 
+  // Whistle cross attention (CrossWeights::load, whistle/src/cross.rs:38-56)
+  if (lay.audio) {
+    if (lay.cross.size() != L) fail(NB_ERR_ARCHIVE, "the audio section does not carry cross attention for every decoder layer");
+    auto stacked = [&](uint32_t first_idx, uint32_t second_idx, const char* what) {
+      check_matrix(a, first_idx, H * HEAD_DIM, d, what);
+      check_matrix(a, second_idx, H * HEAD_DIM, d, what);
+      Levels l1 = levels_for(a.record(first_idx).bits, a.codebook(), GROUP), l2 = levels_for(a.record(second_idx).bits, a.codebook(), GROUP);
+      if (l1.fused != l2.fused) fail(NB_ERR_UNSUPPORTED, std::string(what) + ": both products must share one code width");
+      std::vector<int8_t> codes;
+      std::vector<float> scales;
+      expand_matrix(a, first_idx, l1, true, codes, scales, 0, 2 * H * HEAD_DIM);
+      expand_matrix(a, second_idx, l2, true, codes, scales, H * HEAD_DIM, 2 * H * HEAD_DIM);
+      return QMat{A.upload(codes, st), A.upload(scales, st), l1.int_scale, 2 * H * HEAD_DIM, d, d / GROUP, l1.fused ? 1 : 0};
+    };
+    auto sig = [](float v) { return 1.0f / (1.0f + std::exp(-v)); };  // ops.rs:69-71 in f32
+    for (uint32_t l = 0; l < L; ++l) {
+      const std::array<uint32_t, 10>& c = lay.cross[l];
+      CrossLayerDev C{};
+      C.norm = A.upload(floats_of(a, c[0], d, "cross norm"), st);
+      C.qg = stacked(c[1], c[4], "cross q/gate");
+      C.kv = stacked(c[2], c[3], "cross k/v");
+      check_matrix(a, c[5], d, H * HEAD_DIM, "cross out_proj");
+      Levels lo = levels_for(a.record(c[5]).bits, a.codebook(), GROUP);
+      std::vector<int8_t> codes;
+      std::vector<float> scales;
+      expand_matrix(a, c[5], lo, true, codes, scales, 0, d);
+      C.out = QMat{A.upload(codes, st), A.upload(scales, st), lo.int_scale, d, H * HEAD_DIM, (H * HEAD_DIM) / GROUP, lo.fused ? 1 : 0};
+      C.q_norm = A.upload(floats_of(a, c[6], HEAD_DIM, "cross q_norm"), st);
+      C.k_norm = A.upload(floats_of(a, c[7], HEAD_DIM, "cross k_norm"), st);
+      C.post_norm = A.upload(floats_of(a, c[8], d, "cross post_norm"), st);
+      C.gain = sig(floats_of(a, c[9], 1, "cross gate")[0]);
+      E->cross_layers.push_back(C);
+    }
+    md.cross = A.upload(E->cross_layers, st);
+    E->position_gate = sig(floats_of(a, lay.position_gate, 1, "position gate")[0]);
+    E->text_vocab = lay.text_vocab;
+  }
+
   // sessions, KV pool, workspace
   E->max_sessions = opt && opt->max_sessions ? opt->max_sessions : 256;
   E->max_pages = (g.max_seq_len + PAGE_POSITIONS - 1) / PAGE_POSITIONS;
@@ -763,6 +806,11 @@ std::shared_ptr<Engine> open_engine(const char* path, const nb_options* opt) {
     NB_CUDA(cudaMemsetAsync(E->d_head_scale, 0, (E->head_k / GROUP) * 4, st));
     E->d_head_out = A.alloc<float>(std::max<size_t>(E->head_k, 4096));
     E->h_head.ensure(std::max<size_t>(E->head_k, 4096) * 4);
+  }
+  if (md.cross) {
+    E->d_slot_cross = A.alloc<const CrossMemDev*>(E->max_sessions);
+    NB_CUDA(cudaMemsetAsync(E->d_slot_cross, 0, E->max_sessions * sizeof(void*), st));
+    md.slot_cross = E->d_slot_cross;
   }
   for (EngramDev& S : sites)
     if (ecfg.ring_rows) {
@@ -808,6 +856,10 @@ std::shared_ptr<Engine> open_engine(const char* path, const nb_options* opt) {
   if (!sites.empty()) {
     w.engram_kv = A.alloc<float>((size_t)M * 2 * d);
     w.xin = A.alloc<float>((size_t)M * d);
+  }
+  if (md.cross) {
+    w.xr = A.alloc<float>((size_t)M * d);
+    w.cq = A.alloc<float>((size_t)M * 2 * d);
   }
   if (md.num_probe_heads) {
     if (M > 0xffff) fail(NB_ERR_ARGUMENT, "passes of more than 65535 tokens are not supported with probe heads");
@@ -892,7 +944,7 @@ void forward(Engine& E, const std::vector<int32_t>& active, const TokenSpec* spe
   if (E.md.num_probe_heads) nbk::launch_observe(E.md, w, w.stream, (int)count, 0, E.stream);
   for (size_t slot = 0; slot < active.size(); ++slot) {
     int layer = active[slot];
-    nbk::launch_layer(E.md, E.layers[layer], E.engram_of(layer), w, kv, (int)count, layer, (int)slot, E.t_cap, distinct, E.stream);
+    nbk::launch_layer(E.md, E.layers[layer], E.engram_of(layer), E.cross_of(layer), w, kv, (int)count, layer, (int)slot, E.t_cap, distinct, E.stream);
     std::swap(w.stream, w.next_stream);
     if (E.md.num_probe_heads) nbk::launch_observe(E.md, w, w.stream, (int)count, layer + 1, E.stream);
   }
@@ -907,10 +959,43 @@ void forward(Engine& E, const std::vector<int32_t>& active, const TokenSpec* spe
 
 using namespace nbr;
 
+// A device buffer freed on scope exit.
+struct DevTemp {
+  void* p = nullptr;
+  explicit DevTemp(size_t bytes) { NB_CUDA(cudaMalloc(&p, bytes)); }
+  ~DevTemp() { cudaFree(p); }
+  template <typename T>
+  T* as() { return static_cast<T*>(p); }
+};
+
 // ------------------------------------------------------------------- C ABI
 struct nb_model {
   std::shared_ptr<Engine> engine;
   std::vector<int32_t> active;
+};
+
+// Whistle: the cross-attention memory of one encoder output (CrossMemory,
+// whistle/src/cross.rs:29-35), in device memory of its own.
+struct CrossMem {
+  std::shared_ptr<Engine> engine;
+  int frames = 0;
+  int8_t *keys = nullptr, *values = nullptr;
+  float *kscale = nullptr, *vscale = nullptr;
+  CrossMemDev* dev = nullptr;
+  ~CrossMem() {
+    if (!engine) return;
+    cudaSetDevice(engine->device);
+    cudaStreamSynchronize(engine->stream);  // no queued pass still reads it
+    cudaFree(keys);
+    cudaFree(values);
+    cudaFree(kscale);
+    cudaFree(vscale);
+    cudaFree(dev);
+  }
+};
+
+struct nb_cross_memory {
+  std::shared_ptr<CrossMem> mem;
 };
 
 struct nb_session {
@@ -918,6 +1003,7 @@ struct nb_session {
   std::vector<int32_t> active;
   uint32_t slot = 0;
   uint32_t length = 0;
+  std::shared_ptr<CrossMem> cross;  // Whistle: the memory every pass of this session attends to
 };
 
 struct nb_batch {
@@ -1033,6 +1119,8 @@ nb_status nb_model_synchronize(nb_model* model) {
   });
 }
 
+static void set_slot_cross(Engine& E, uint32_t slot, const CrossMemDev* p);
+
 nb_status nb_session_create(nb_model* model, nb_session** out) {
   if (!model || !out) return NB_ERR_ARGUMENT;
   *out = nullptr;
@@ -1080,6 +1168,7 @@ nb_status nb_session_clone(const nb_session* session, nb_session** out) {
     NB_CUDA(cudaMemcpyAsync(E.d_hidden + (size_t)s->slot * E.md.d_model, E.d_hidden + (size_t)session->slot * E.md.d_model,
                             E.md.d_model * 4, cudaMemcpyDeviceToDevice, E.stream));
     const size_t d = E.md.d_model;
+    set_slot_cross(E, s->slot, s->cross ? s->cross->dev : nullptr);  // the clone attends to the same memory
     for (uint32_t h = 0; h < E.md.num_probe_heads; ++h) {  // the probe accumulators are part of the session (session.rs:26)
       const HeadDev& H = E.heads[h];
       const size_t all = (size_t)(E.md.num_layers + 1) * H.probes;
@@ -1119,6 +1208,10 @@ void nb_session_release(nb_session* session) {
         p = -1;
       }
     E.slot_dirty[session->slot] = 1;
+    try {
+      set_slot_cross(E, session->slot, nullptr);
+    } catch (...) {
+    }
     E.free_slots.push_back(session->slot);
   }
   delete session;
@@ -1142,6 +1235,93 @@ static void raise_device_error(Engine& E) {
     NB_CUDA(cudaMemsetAsync(E.d_error, 0, sizeof(int), E.stream));
     fail(NB_ERR_TIMEOUT, "a bounded device wait gave up");
   }
+}
+
+// Writes the session's entry of the slot-to-memory table.
+static void set_slot_cross(Engine& E, uint32_t slot, const CrossMemDev* p) {
+  if (E.d_slot_cross) NB_CUDA(cudaMemcpyAsync(E.d_slot_cross + slot, &p, sizeof p, cudaMemcpyHostToDevice, E.stream));
+}
+
+nb_status nb_cross_memory_create(nb_model* model, const float* encoded, size_t frames, nb_cross_memory** out) {
+  if (!model || !out || !encoded) return NB_ERR_ARGUMENT;
+  *out = nullptr;
+  return guard([&] {
+    Engine& E = *model->engine;
+    std::lock_guard<std::mutex> lock(E.mutex);
+    if (E.cross_layers.empty()) fail(NB_ERR_UNSUPPORTED, "the archive carries no audio section (cross attention)");
+    if (frames == 0 || frames > (size_t)MAX_CROSS_FRAMES) fail(NB_ERR_ARGUMENT, "frames must be in 1.." + std::to_string(MAX_CROSS_FRAMES));
+    NB_CUDA(cudaSetDevice(E.device));
+    E.settle();
+    const int d = (int)E.md.d_model, H = (int)E.md.heads, L = (int)E.geo.num_layers, half = d / 2, F = (int)frames;
+    // the positional angles' sine and cosine (cross.rs:62-73), the platform
+    // libm's as in the reference, like the rotary table
+    std::vector<float> sin_t((size_t)F * half), cos_t((size_t)F * half);
+    const float rate = -std::log(10000.0f) / ((float)half - 1.0f);
+    for (int t = 0; t < F; ++t)
+      for (int j = 0; j < half; ++j) {
+        const float angle = (float)t * std::exp(rate * (float)j);
+        sin_t[(size_t)t * half + j] = std::sin(angle);
+        cos_t[(size_t)t * half + j] = std::cos(angle);
+      }
+    auto m = std::make_shared<CrossMem>();
+    const size_t codes = (size_t)L * F * H * HEAD_DIM, scales = (size_t)L * F * H;
+    NB_CUDA(cudaMalloc(&m->keys, codes));
+    NB_CUDA(cudaMalloc(&m->values, codes));
+    NB_CUDA(cudaMalloc(&m->kscale, scales * 4));
+    NB_CUDA(cudaMalloc(&m->vscale, scales * 4));
+    NB_CUDA(cudaMalloc(&m->dev, sizeof(CrossMemDev)));
+    m->engine = model->engine;
+    m->frames = F;
+    const int act_rows = (F + 127) / 128 * 128;
+    DevTemp enc((size_t)F * d * 4), sn(sin_t.size() * 4), cs(cos_t.size() * 4), rows((size_t)F * d * 4), act((size_t)act_rows * d),
+        act_scale((size_t)F * (d / GROUP) * 4), kv((size_t)F * 2 * d * 4);
+    NB_CUDA(cudaMemcpyAsync(enc.p, encoded, (size_t)F * d * 4, cudaMemcpyHostToDevice, E.stream));
+    NB_CUDA(cudaMemcpyAsync(sn.p, sin_t.data(), sin_t.size() * 4, cudaMemcpyHostToDevice, E.stream));
+    NB_CUDA(cudaMemcpyAsync(cs.p, cos_t.data(), cos_t.size() * 4, cudaMemcpyHostToDevice, E.stream));
+    NB_CUDA(nbk::cross_memory(E.md, E.cross_layers, enc.as<float>(), F, sn.as<float>(), cs.as<float>(), E.position_gate, rows.as<float>(),
+                              act.as<int8_t>(), act_scale.as<float>(), act_rows, kv.as<float>(), m->keys, m->kscale, m->values, m->vscale,
+                              E.stream));
+    const CrossMemDev h{F, m->keys, m->kscale, m->values, m->vscale};
+    NB_CUDA(cudaMemcpyAsync(m->dev, &h, sizeof h, cudaMemcpyHostToDevice, E.stream));
+    queue_error_read(E);
+    NB_CUDA(cudaStreamSynchronize(E.stream));
+    raise_device_error(E);
+    *out = new nb_cross_memory{m};
+  });
+}
+
+void nb_cross_memory_release(nb_cross_memory* memory) { delete memory; }
+
+nb_status nb_session_set_cross(nb_session* session, nb_cross_memory* memory) {
+  if (!session) return NB_ERR_ARGUMENT;
+  return guard([&] {
+    Engine& E = *session->engine;
+    std::lock_guard<std::mutex> lock(E.mutex);
+    if (memory && memory->mem->engine != session->engine) fail(NB_ERR_ARGUMENT, "the memory belongs to another model");
+    NB_CUDA(cudaSetDevice(E.device));
+    session->cross = memory ? memory->mem : nullptr;
+    set_slot_cross(E, session->slot, session->cross ? session->cross->dev : nullptr);
+  });
+}
+
+size_t nb_model_text_vocab(const nb_model* model) { return model ? model->engine->text_vocab : 0; }
+
+nb_status nb_debug_cross_memory(const nb_cross_memory* memory, int layer, int8_t* keys, float* key_scales, int8_t* values,
+                                float* value_scales) {
+  if (!memory || !keys || !key_scales || !values || !value_scales) return NB_ERR_ARGUMENT;
+  return guard([&] {
+    const CrossMem& m = *memory->mem;
+    Engine& E = *m.engine;
+    std::lock_guard<std::mutex> lock(E.mutex);
+    if (layer < 0 || layer >= (int)E.geo.num_layers) fail(NB_ERR_ARGUMENT, "layer out of range");
+    NB_CUDA(cudaSetDevice(E.device));
+    NB_CUDA(cudaStreamSynchronize(E.stream));
+    const size_t n = (size_t)m.frames * E.md.heads, at = (size_t)layer * n;
+    NB_CUDA(cudaMemcpy(keys, m.keys + at * HEAD_DIM, n * HEAD_DIM, cudaMemcpyDeviceToHost));
+    NB_CUDA(cudaMemcpy(values, m.values + at * HEAD_DIM, n * HEAD_DIM, cudaMemcpyDeviceToHost));
+    NB_CUDA(cudaMemcpy(key_scales, m.kscale + at, n * 4, cudaMemcpyDeviceToHost));
+    NB_CUDA(cudaMemcpy(value_scales, m.vscale + at, n * 4, cudaMemcpyDeviceToHost));
+  });
 }
 
 // Session::head_output / pooled_readout (session.rs:150-160).
@@ -1311,6 +1491,8 @@ static Work work_rows(const Engine& E, const Work& w, uint32_t b0) {
   s.cells = w.cells ? w.cells + b0 * d : nullptr;
   s.scores = w.scores ? w.scores + b0 * E.head_pairs : nullptr;
   s.scan = w.scan ? w.scan + b0 * E.head_pairs * 2 : nullptr;
+  s.xr = w.xr ? w.xr + b0 * d : nullptr;
+  s.cq = w.cq ? w.cq + b0 * 2 * d : nullptr;
   s.proj = w.proj + b0 * (2 * H + 2 * KV) * HEAD_DIM;
   s.qcodes = w.qcodes + b0 * H * HEAD_DIM;
   s.qscale = w.qscale + b0 * H;
@@ -1343,7 +1525,7 @@ static void build_group(nb_batch* b, bool masked, bool stats, uint32_t b0, uint3
   if (E.md.num_probe_heads) nbk::launch_observe(E.md, w, w.stream, n, 0, st);
   for (size_t slot = 0; slot < b->active.size(); ++slot) {
     int layer = b->active[slot];
-    nbk::launch_layer(E.md, E.layers[layer], E.engram_of(layer), w, kv, n, layer, (int)slot, E.t_cap, true, st);
+    nbk::launch_layer(E.md, E.layers[layer], E.engram_of(layer), E.cross_of(layer), w, kv, n, layer, (int)slot, E.t_cap, true, st);
     std::swap(w.stream, w.next_stream);
     if (E.md.num_probe_heads) nbk::launch_observe(E.md, w, w.stream, n, layer + 1, st);
   }

@@ -28,6 +28,7 @@ def _declare() -> None:
         "nb_debug_hadamard": [P, U32, P, SZ, P],
         "nb_debug_kv": [P, U32, P, P, P, P],
         "nb_debug_time_attention": [P, U32, ctypes.POINTER(ctypes.c_float), ctypes.POINTER(ctypes.c_double)],
+        "nb_debug_cross_memory": [P, ctypes.c_int, P, P, P, P],
         "nb_debug_step_kernels": [P, ctypes.POINTER(ctypes.c_uint32)],
         "nb_debug_product": [I, U32, P, P, P, U32, U32, P, U32, P, U32, ctypes.POINTER(ctypes.c_float)],
     }.items():
@@ -77,6 +78,17 @@ def kv(session: Session, layer: int):
     ks = np.zeros((c.num_kv_heads, n), dtype=np.float32)
     vs = np.zeros_like(ks)
     _check(lib().nb_debug_kv(session._h, layer, _ptr(keys), _ptr(ks), _ptr(values), _ptr(vs)))
+    return keys, ks, values, vs
+
+
+def cross_memory(memory, layer: int, heads: int, head_dim: int = 64):
+    """A cross memory's keys, key scales, values and value scales of one layer."""
+    _declare()
+    keys = np.empty((memory.frames, heads, head_dim), dtype=np.int8)
+    values = np.empty_like(keys)
+    ks = np.empty((memory.frames, heads), dtype=np.float32)
+    vs = np.empty_like(ks)
+    _check(lib().nb_debug_cross_memory(memory._h, layer, keys.ctypes.data, ks.ctypes.data, values.ctypes.data, vs.ctypes.data))
     return keys, ks, values, vs
 
 
