@@ -58,6 +58,7 @@ def parse():
     p.add_argument("--no-cpu", action="store_true")
     p.add_argument("--profile", action="store_true", help="64 sequences, no extras: the small case for ncu captures")
     p.add_argument("--batch1-only", action="store_true", help="only the batch-1 configuration (ncu launch lists)")
+    p.add_argument("--no-whistle", action="store_true", help="skip the Whistle decoder section (config 4)")
     p.add_argument("--ncu-range", action="store_true",
                    help="bracket the timed steps with cudaProfilerStart/Stop (ncu --profile-from-start off)")
     p.add_argument("--products", action="store_true",
@@ -308,6 +309,8 @@ def main():
         batch.close()
         line["batch1"] = batch1(nb, model, local)
         line["config0"] = config0(nb, model)
+        if not args.no_whistle:
+            line["config4"] = whistle(nb, local)
     if rank == 0 and world == 1 and not args.no_cpu and not args.profile:
         from oracle import oracle
 
@@ -315,6 +318,8 @@ def main():
         line["cpu_baseline"] = cpu_baseline(archive, rank_prompts, os.cpu_count() or 1)
         if "config0" in line:
             line["config0"]["cpu"] = config0_cpu(archive)
+        if "config4" in line:
+            line["config4"]["cpu"] = whistle_cpu()
     if rank == 0:
         print(json.dumps(line), flush=True)
     batch.close()
@@ -358,6 +363,82 @@ def config0_cpu(archive: str):
     p50 = float(np.percentile(times[4:], 50))
     return {"p50_ms_per_token": round(p50, 4), "tokens_per_s": round(1000.0 / p50, 1), "cores": 1,
             "kind": "port", "sample": "60 timed greedy tokens after 4 untimed"}
+
+
+WHISTLE = dict(layers=8, text_vocab=8000, frames=1500, batch=64, tokens=224)
+
+
+def whistle_archive():
+    from rustyneedle_b200 import synthetic
+
+    return synthetic.cached_archive(seed=0, geometry=synthetic.Geometry(num_layers=WHISTLE["layers"], text_vocab=WHISTLE["text_vocab"]))
+
+
+def whistle(nb, device: int = 0):
+    """Config 4: a Whistle decoder (depth 8), 64 utterances each cross-attending
+    to its own 1500 x 512 N(0, 1) encoder output, bos and a language token,
+    then 224 greedy text tokens (ids below text_vocab) on the device."""
+    import torch
+
+    model = nb.Model.open(whistle_archive(), device=device, max_sessions=WHISTLE["batch"])
+    B, V, T = WHISTLE["batch"], model.config.output_vocab, WHISTLE["tokens"]
+    rng = np.random.default_rng(11)
+    sessions, memories, mem_ms = [], [], []
+    for i in range(B):
+        enc = rng.standard_normal((WHISTLE["frames"], model.config.d_model)).astype(np.float32)
+        t = time.perf_counter()
+        mem = nb.CrossMemory(model, enc)
+        mem_ms.append(1000 * (time.perf_counter() - t))
+        s = nb.Session(model)
+        s.set_cross(mem)
+        s.push(1)
+        s.push(WHISTLE["text_vocab"] + i % (V - WHISTLE["text_vocab"]))
+        sessions.append(s)
+        memories.append(mem)
+    allowed = np.zeros(V, dtype=bool)
+    allowed[:WHISTLE["text_vocab"]] = True
+    words = np.packbits(allowed, bitorder="little").view(np.uint32)
+    masks = torch.from_numpy(np.tile(words, (T + 4) * B).astype(np.int32)).to(f"cuda:{device}")
+    batch = nb.Batch(model, sessions)
+    warm = 4
+    batch.run(warm, masks.data_ptr())
+    with Clocks(device) as clocks:
+        ms = batch.run(T, masks.data_ptr() + warm * B * (V // 32) * 4)
+    out = {"workload": "config4: synthetic Whistle decoder (depth 8, d 512, 8 heads, seed 0), 64 utterances per GPU, each "
+                       "cross-attending to its own 1500 x 512 N(0,1) encoder output; bos and a language token, then 224 greedy "
+                       "text tokens (ids < 8000 of 8192) per utterance, device-resident steps",
+           "tokens_per_s": round(B * T / (ms / 1000.0), 1), "ms_per_step": round(ms / T, 4),
+           "memory_ms_per_utterance": round(float(np.median(mem_ms)), 3), "clocks": clocks.summary()}
+    batch.close()
+    for s in sessions:
+        s.close()
+    for m in memories:
+        m.close()
+    model.close()
+    return out
+
+
+def whistle_cpu(sample_tokens: int = 4):
+    """Config 4 on the CPU oracle (FLOAT mode, all host cores): one utterance's
+    memory, bos and a language token, then a few greedy text tokens."""
+    from oracle import oracle
+
+    model = oracle.Model.open(whistle_archive(), oracle.MODE_FLOAT, os.cpu_count() or 1)
+    enc = np.random.default_rng(11).standard_normal((WHISTLE["frames"], 512)).astype(np.float32)
+    t = time.perf_counter()
+    mem = oracle.CrossMemory(model, enc)
+    mem_ms = 1000 * (time.perf_counter() - t)
+    s = oracle.Session(model)
+    s.push_cross(1, mem)
+    s.push_cross(WHISTLE["text_vocab"], mem)
+    allowed = np.zeros(8192, dtype=np.uint8)
+    allowed[:WHISTLE["text_vocab"]] = 1
+    t = time.perf_counter()
+    for _ in range(sample_tokens):
+        s.push_cross(oracle.argmax_allowed(s.logits(), allowed), mem)
+    ms = 1000 * (time.perf_counter() - t) / sample_tokens
+    return {"tokens_per_s": round(1000.0 / ms, 2), "ms_per_token": round(ms, 2), "memory_ms": round(mem_ms, 1),
+            "cores": os.cpu_count() or 1, "kind": "port", "sample": f"one utterance, {sample_tokens} greedy tokens after bos and a language token"}
 
 
 def batch1(nb, model, device: int = 0, ncu_range: bool = False):

@@ -2194,6 +2194,7 @@ __global__ void __launch_bounds__(128) k_cross_q(ModelDev md, int layer, Work w,
 // order per dimension; times sigmoid(gate) (cross.rs:164-166) into the rows of
 // w.attn. grid (M, heads), block 256.
 constexpr int CROSS_THREADS = 256;
+constexpr int CROSS_CHUNK = 128;  // frames per staged value tile (8 KB)
 __global__ void __launch_bounds__(CROSS_THREADS) k_cross_attend(ModelDev md, int layer, Work w, int M) {
   extern __shared__ float s_sc[];  // [MAX_CROSS_FRAMES] scores, then weights; [MAX_CROSS_FRAMES] value scale · weight
   float* s_vw = s_sc + MAX_CROSS_FRAMES;
@@ -2267,21 +2268,41 @@ __global__ void __launch_bounds__(CROSS_THREADS) k_cross_attend(ModelDev md, int
   }
   __syncthreads();
   for (int f = tid; f < frames; f += CROSS_THREADS) s_vw[f] = fmul(vscale[(size_t)f * heads + h], fmul(s_sc[f], s_inverse));
-  __syncthreads();
   pdl_trigger();
-  if (tid < HEAD_DIM) {
-    const int8_t* vcol = values + (size_t)h * HEAD_DIM + tid;
-    const size_t stride = (size_t)heads * HEAD_DIM;
-    float acc = 0.0f;
-    int f = 0;
-    for (; f + 8 <= frames; f += 8) {
-      float c[8];
-#pragma unroll
-      for (int k = 0; k < 8; ++k) c[k] = (float)vcol[(size_t)(f + k) * stride];
-#pragma unroll
-      for (int k = 0; k < 8; ++k) acc = fadd(acc, fmul(s_vw[f + k], c[k]));
+  // the value rows of this head pass through a double-buffered shared tile of
+  // CROSS_CHUNK frames (16-byte copies by every thread); thread d < 64 runs
+  // dimension d's ordered sum over the frames
+  __shared__ __align__(16) int8_t s_val[2][CROSS_CHUNK * HEAD_DIM];
+  const int8_t* vbase = values + (size_t)h * HEAD_DIM;
+  const size_t stride = (size_t)heads * HEAD_DIM;
+  auto stage = [&](int chunk) {
+    const int f0 = chunk * CROSS_CHUNK, n = min(CROSS_CHUNK, frames - f0);
+    for (int i = tid; i < n * (HEAD_DIM / 16); i += CROSS_THREADS) {
+      const int f = i / (HEAD_DIM / 16), part = i % (HEAD_DIM / 16);
+      cp_async16(&s_val[chunk & 1][f * HEAD_DIM + part * 16], vbase + (size_t)(f0 + f) * stride + part * 16);
     }
-    for (; f < frames; ++f) acc = fadd(acc, fmul(s_vw[f], (float)vcol[(size_t)f * stride]));
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+  const int chunks = (frames + CROSS_CHUNK - 1) / CROSS_CHUNK;
+  stage(0);
+  float acc = 0.0f;
+  for (int c = 0; c < chunks; ++c) {
+    if (c + 1 < chunks) {
+      stage(c + 1);
+      asm volatile("cp.async.wait_group 1;" ::: "memory");
+    } else {
+      asm volatile("cp.async.wait_group 0;" ::: "memory");
+    }
+    __syncthreads();  // chunk c is in place (and, at c = 0, every s_vw entry)
+    if (tid < HEAD_DIM) {
+      const int f0 = c * CROSS_CHUNK, n = min(CROSS_CHUNK, frames - f0);
+      const int8_t* col = &s_val[c & 1][tid];
+#pragma unroll 8
+      for (int f = 0; f < n; ++f) acc = fadd(acc, fmul(s_vw[f0 + f], (float)col[f * HEAD_DIM]));
+    }
+    __syncthreads();  // buffer c & 1 is free for chunk c + 2
+  }
+  if (tid < HEAD_DIM) {
     const float g = __ldcg(w.cq + (size_t)t * 2 * d + d + h * HEAD_DIM + tid);
     w.attn[(size_t)t * heads * HEAD_DIM + h * HEAD_DIM + tid] = fmul(acc, sigmoid(g));
   }
