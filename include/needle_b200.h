@@ -125,7 +125,7 @@ nb_status nb_session_pooled_readout(nb_session* session, uint32_t code, float* o
  * CrossWeights::memory (whistle/src/cross.rs:58-99): the gated positional
  * signal added to `encoded` ([frames][d_model] f32, host memory), then every
  * decoder layer's int8 keys and values. NB_ERR_UNSUPPORTED when the archive
- * carries no audio section; frames in 1..4096. */
+ * carries no audio section; frames in 1..2048 (a 30-second window is 1500). */
 typedef struct nb_cross_memory nb_cross_memory;
 nb_status nb_cross_memory_create(nb_model* model, const float* encoded, size_t frames, nb_cross_memory** out);
 void nb_cross_memory_release(nb_cross_memory* memory);

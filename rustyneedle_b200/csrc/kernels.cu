@@ -2110,6 +2110,12 @@ __device__ __forceinline__ float norm_quant_head64(float e0, float e1, const flo
   return scale;
 }
 
+// An int8 as f32, exactly, on the FP32 pipe: 2^23 + (v + 128) is an f32 whose
+// low mantissa bits hold v + 128, and subtracting 2^23 + 128 is exact.
+__device__ __forceinline__ float int8_to_float(int8_t v) {
+  return fsub(__int_as_float(0x4B000000 | (int)(v + 128)), 8388736.0f);
+}
+
 // CrossWeights::memory, first step (cross.rs:64-74): row t of the encoder
 // output plus the gated positional signal (sin in the first half, cos in the
 // second; the angles' sin and cos come as tables). grid frames, block 128.
@@ -2194,7 +2200,8 @@ __global__ void __launch_bounds__(128) k_cross_q(ModelDev md, int layer, Work w,
 // order per dimension; times sigmoid(gate) (cross.rs:164-166) into the rows of
 // w.attn. grid (M, heads), block 256.
 constexpr int CROSS_THREADS = 256;
-constexpr int CROSS_CHUNK = 128;  // frames per staged value tile (8 KB)
+constexpr int CROSS_CHUNK = 128;   // frames per staged value tile (8 KB)
+constexpr int CROSS_BUFFERS = 4;   // value tiles in shared memory (three in flight)
 __global__ void __launch_bounds__(CROSS_THREADS) k_cross_attend(ModelDev md, int layer, Work w, int M) {
   extern __shared__ float s_sc[];  // [MAX_CROSS_FRAMES] scores, then weights; [MAX_CROSS_FRAMES] value scale · weight
   float* s_vw = s_sc + MAX_CROSS_FRAMES;
@@ -2213,6 +2220,22 @@ __global__ void __launch_bounds__(CROSS_THREADS) k_cross_attend(ModelDev md, int
   const float* kscale = mem->kscale + (size_t)layer * frames * heads;
   const int8_t* values = mem->values + (size_t)layer * frames * heads * HEAD_DIM;
   const float* vscale = mem->vscale + (size_t)layer * frames * heads;
+  // the value rows of this head pass through CROSS_BUFFERS shared tiles of
+  // CROSS_CHUNK frames (16-byte copies by every thread), CROSS_BUFFERS - 1
+  // ahead: they do not depend on the softmax, so the first ones load now
+  __shared__ __align__(16) int8_t s_val[CROSS_BUFFERS][CROSS_CHUNK * HEAD_DIM];
+  const int8_t* vbase = values + (size_t)h * HEAD_DIM;
+  const size_t vstride = (size_t)heads * HEAD_DIM;
+  auto stage = [&](int chunk) {  // commits one group, empty past the last chunk
+    const int f0 = chunk * CROSS_CHUNK, n = min(CROSS_CHUNK, frames - f0);
+    for (int i = tid; i < n * (HEAD_DIM / 16); i += CROSS_THREADS) {
+      const int f = i / (HEAD_DIM / 16), part = i % (HEAD_DIM / 16);
+      cp_async16(&s_val[chunk % CROSS_BUFFERS][f * HEAD_DIM + part * 16], vbase + (size_t)(f0 + f) * vstride + part * 16);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+#pragma unroll
+  for (int c = 0; c < CROSS_BUFFERS - 1; ++c) stage(c);
   if (warp == 0) {
     const float* q = w.cq + (size_t)t * 2 * d + h * HEAD_DIM;
     int8_t c0, c1;
@@ -2224,21 +2247,34 @@ __global__ void __launch_bounds__(CROSS_THREADS) k_cross_attend(ModelDev md, int
   __syncthreads();
   float peak = -INFINITY;
   const uint4* qv = reinterpret_cast<const uint4*>(s_q);
-  for (int f = tid; f < frames; f += CROSS_THREADS) {
-    const uint4* kp = reinterpret_cast<const uint4*>(keys + ((size_t)f * heads + h) * HEAD_DIM);
-    int part[4] = {0, 0, 0, 0};
+  for (int f0 = tid; f0 < frames; f0 += 2 * CROSS_THREADS) {  // two frames' keys in flight
+    uint4 kk[2][4];
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const uint4 kk = kp[k], qq = qv[k];
-      part[0] = dp4a(kk.x, qq.x, part[0]);
-      part[1] = dp4a(kk.y, qq.y, part[1]);
-      part[2] = dp4a(kk.z, qq.z, part[2]);
-      part[3] = dp4a(kk.w, qq.w, part[3]);
+    for (int u = 0; u < 2; ++u) {
+      const int f = min(f0 + u * CROSS_THREADS, frames - 1);
+      const uint4* kp = reinterpret_cast<const uint4*>(keys + ((size_t)f * heads + h) * HEAD_DIM);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) kk[u][k] = kp[k];
     }
-    const int dot = (part[0] + part[1]) + (part[2] + part[3]);
-    const float sc = fmul(fmul((float)dot, kscale[(size_t)f * heads + h]), s_qs);
-    s_sc[f] = sc;
-    peak = fmaxf(peak, sc);
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const int f = f0 + u * CROSS_THREADS;
+      if (f < frames) {
+        int part[4] = {0, 0, 0, 0};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const uint4 qq = qv[k];
+          part[0] = dp4a(kk[u][k].x, qq.x, part[0]);
+          part[1] = dp4a(kk[u][k].y, qq.y, part[1]);
+          part[2] = dp4a(kk[u][k].z, qq.z, part[2]);
+          part[3] = dp4a(kk[u][k].w, qq.w, part[3]);
+        }
+        const int dot = (part[0] + part[1]) + (part[2] + part[3]);
+        const float sc = fmul(fmul((float)dot, kscale[(size_t)f * heads + h]), s_qs);
+        s_sc[f] = sc;
+        peak = fmaxf(peak, sc);
+      }
+    }
   }
   peak = warp_max(peak);
   if (lane == 0) s_red[warp] = peak;
@@ -2269,38 +2305,20 @@ __global__ void __launch_bounds__(CROSS_THREADS) k_cross_attend(ModelDev md, int
   __syncthreads();
   for (int f = tid; f < frames; f += CROSS_THREADS) s_vw[f] = fmul(vscale[(size_t)f * heads + h], fmul(s_sc[f], s_inverse));
   pdl_trigger();
-  // the value rows of this head pass through a double-buffered shared tile of
-  // CROSS_CHUNK frames (16-byte copies by every thread); thread d < 64 runs
-  // dimension d's ordered sum over the frames
-  __shared__ __align__(16) int8_t s_val[2][CROSS_CHUNK * HEAD_DIM];
-  const int8_t* vbase = values + (size_t)h * HEAD_DIM;
-  const size_t stride = (size_t)heads * HEAD_DIM;
-  auto stage = [&](int chunk) {
-    const int f0 = chunk * CROSS_CHUNK, n = min(CROSS_CHUNK, frames - f0);
-    for (int i = tid; i < n * (HEAD_DIM / 16); i += CROSS_THREADS) {
-      const int f = i / (HEAD_DIM / 16), part = i % (HEAD_DIM / 16);
-      cp_async16(&s_val[chunk & 1][f * HEAD_DIM + part * 16], vbase + (size_t)(f0 + f) * stride + part * 16);
-    }
-    asm volatile("cp.async.commit_group;" ::: "memory");
-  };
+  // thread d < 64 runs dimension d's ordered sum over the frames
   const int chunks = (frames + CROSS_CHUNK - 1) / CROSS_CHUNK;
-  stage(0);
   float acc = 0.0f;
   for (int c = 0; c < chunks; ++c) {
-    if (c + 1 < chunks) {
-      stage(c + 1);
-      asm volatile("cp.async.wait_group 1;" ::: "memory");
-    } else {
-      asm volatile("cp.async.wait_group 0;" ::: "memory");
-    }
+    stage(c + CROSS_BUFFERS - 1);  // into the buffer chunk c - 1 has freed
+    asm volatile("cp.async.wait_group %0;" ::"n"(CROSS_BUFFERS - 1) : "memory");
     __syncthreads();  // chunk c is in place (and, at c = 0, every s_vw entry)
     if (tid < HEAD_DIM) {
       const int f0 = c * CROSS_CHUNK, n = min(CROSS_CHUNK, frames - f0);
-      const int8_t* col = &s_val[c & 1][tid];
+      const int8_t* col = &s_val[c % CROSS_BUFFERS][tid];
 #pragma unroll 8
-      for (int f = 0; f < n; ++f) acc = fadd(acc, fmul(s_vw[f0 + f], (float)col[f * HEAD_DIM]));
+      for (int f = 0; f < n; ++f) acc = fadd(acc, fmul(s_vw[f0 + f], int8_to_float(col[f * HEAD_DIM])));
     }
-    __syncthreads();  // buffer c & 1 is free for chunk c + 2
+    __syncthreads();  // buffer c % CROSS_BUFFERS is free for chunk c + CROSS_BUFFERS
   }
   if (tid < HEAD_DIM) {
     const float g = __ldcg(w.cq + (size_t)t * 2 * d + d + h * HEAD_DIM + tid);

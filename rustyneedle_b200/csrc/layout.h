@@ -165,7 +165,7 @@ struct CrossMemDev {
   const int8_t* values;  // [layers][frames][heads][64]
   const float* vscale;   // [layers][frames][heads]
 };
-constexpr int MAX_CROSS_FRAMES = 4096;
+constexpr int MAX_CROSS_FRAMES = 2048;  // a 30-second window is 1500 frames
 
 struct LayerDev {
   QMat qkvg;  // q, k, v and gate_proj stacked row-wise (one fused product, matrix.rs:167-193)
