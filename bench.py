@@ -59,6 +59,7 @@ def parse():
     p.add_argument("--profile", action="store_true", help="64 sequences, no extras: the small case for ncu captures")
     p.add_argument("--batch1-only", action="store_true", help="only the batch-1 configuration (ncu launch lists)")
     p.add_argument("--no-whistle", action="store_true", help="skip the Whistle decoder section (config 4)")
+    p.add_argument("--whistle-only", action="store_true", help="only the Whistle decoder section (config 4; ncu launch lists)")
     p.add_argument("--ncu-range", action="store_true",
                    help="bracket the timed steps with cudaProfilerStart/Stop (ncu --profile-from-start off)")
     p.add_argument("--products", action="store_true",
@@ -239,6 +240,9 @@ def main():
     if args.batch1_only:
         print(json.dumps({"batch1": batch1(nb, model, local, args.ncu_range)}), flush=True)
         return
+    if args.whistle_only:
+        print(json.dumps({"config4": whistle(nb, local, args.ncu_range)}), flush=True)
+        return
     t0 = time.perf_counter()
     sessions = [nb.Session(model) for _ in rank_prompts]
     nb.feed_many(sessions, rank_prompts)  # the prompts packed into shared prefill passes
@@ -374,10 +378,11 @@ def whistle_archive():
     return synthetic.cached_archive(seed=0, geometry=synthetic.Geometry(num_layers=WHISTLE["layers"], text_vocab=WHISTLE["text_vocab"]))
 
 
-def whistle(nb, device: int = 0):
+def whistle(nb, device: int = 0, ncu_range: bool = False):
     """Config 4: a Whistle decoder (depth 8), 64 utterances each cross-attending
     to its own 1500 x 512 N(0, 1) encoder output, bos and a language token,
-    then 224 greedy text tokens (ids below text_vocab) on the device."""
+    then 224 greedy text tokens (ids below text_vocab) on the device (with
+    ncu_range, two more steps bracketed by cudaProfilerStart/Stop)."""
     import torch
 
     model = nb.Model.open(whistle_archive(), device=device, max_sessions=WHISTLE["batch"])
@@ -398,12 +403,17 @@ def whistle(nb, device: int = 0):
     allowed = np.zeros(V, dtype=bool)
     allowed[:WHISTLE["text_vocab"]] = True
     words = np.packbits(allowed, bitorder="little").view(np.uint32)
-    masks = torch.from_numpy(np.tile(words, (T + 4) * B).astype(np.int32)).to(f"cuda:{device}")
+    masks = torch.from_numpy(np.tile(words, (T + 6) * B).astype(np.int32)).to(f"cuda:{device}")
     batch = nb.Batch(model, sessions)
     warm = 4
     batch.run(warm, masks.data_ptr())
     with Clocks(device) as clocks:
         ms = batch.run(T, masks.data_ptr() + warm * B * (V // 32) * 4)
+    if ncu_range:
+        torch.cuda.synchronize(device)
+        torch.cuda.cudart().cudaProfilerStart()
+        batch.run(2, masks.data_ptr() + (warm + T) * B * (V // 32) * 4)
+        torch.cuda.cudart().cudaProfilerStop()
     out = {"workload": "config4: synthetic Whistle decoder (depth 8, d 512, 8 heads, seed 0), 64 utterances per GPU, each "
                        "cross-attending to its own 1500 x 512 N(0,1) encoder output; bos and a language token, then 224 greedy "
                        "text tokens (ids < 8000 of 8192) per utterance, device-resident steps",
