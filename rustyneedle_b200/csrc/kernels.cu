@@ -1638,8 +1638,11 @@ __device__ __forceinline__ bool block_front(const ModelDev& md, const LayerDev& 
     if (tid == 0 && !mbar_wait(bar, 0)) atomicExch(error, 1);  // no copy outlives the CTA
     return false;
   }
-  // with Whistle cross attention, k_resid and the cross step have formed x after the residual
+  // with Whistle cross attention, k_cross_q has formed x after the residual (w.xr)
+  // and, for sessions with a memory, the cross out product sits in w.outp
   stage_async(s_a, (md.cross ? w.xr : w.outp) + (size_t)t * d, d);
+  const bool cross_live = md.cross && md.slot_cross[load_meta(w.meta, t).slot];
+  if (cross_live) stage_async(s_pre, w.outp + (size_t)t * d, d);
   if (md.conv_ring) conv_ring_store(md, L, w, M, t, part, parts);
   if (L.engram && L.engram->ring) engram_ring_store(md, *L.engram, w, M, t, part, parts);
   cp_async_wait_all();
@@ -1656,6 +1659,20 @@ __device__ __forceinline__ bool block_front(const ModelDev& md, const LayerDev& 
     for (int i = tid; i < d; i += BLOCK_THREADS) {
       float a = fmul(fmul(fadd(1.0f, s_gpost[i]), s_a[i]), s_inv);
       s_a[i] = fadd(s_x[i], fmul(s_gate, a));
+    }
+    __syncthreads();
+  } else if (cross_live) {
+    // CrossState::apply's last step (cross.rs:176-181): the out product normed
+    // with the cross post norm, then x += sigmoid(gate) · attended
+    const CrossLayerDev& C = md.cross[L.index];
+    if (warp == 0) {
+      float ss = sum_of_squares_warp(s_pre, d);
+      if (lane == 0) s_inv = inverse_rms(ss, d);
+    }
+    __syncthreads();
+    for (int i = tid; i < d; i += BLOCK_THREADS) {
+      const float a = fmul(fmul(fadd(1.0f, C.post_norm[i]), s_pre[i]), s_inv);
+      s_a[i] = fadd(s_a[i], fmul(C.gain, a));
     }
     __syncthreads();
   }
@@ -2146,31 +2163,11 @@ __global__ void k_cross_memory_heads(const float* __restrict__ kv, int d, const 
 }
 
 // x after the layer's attention residual (session.rs:121-125, as the block
-// finish forms it) into w.xr, the input of the cross attention. grid M, block 128.
-__global__ void __launch_bounds__(128) k_resid(ModelDev md, LayerDev L, Work w, int M) {
-  __shared__ __align__(16) float s_a[MAX_D];
-  __shared__ float s_inv;
-  pdl_wait();
-  const int t = blockIdx.x, d = (int)md.d_model;
-  if (t >= M || load_meta(w.meta, t).slot < 0) return;
-  for (int i = threadIdx.x; i < d; i += blockDim.x) s_a[i] = __ldcg(w.outp + (size_t)t * d + i);
-  __syncthreads();
-  if (threadIdx.x < 32) {
-    const float ss = sum_of_squares_warp(s_a, d);
-    if (threadIdx.x == 0) s_inv = inverse_rms(ss, d);
-  }
-  __syncthreads();
-  const float gate = sigmoid(L.attn_gate);
-  for (int i = threadIdx.x; i < d; i += blockDim.x) {
-    const float a = fmul(fmul(fadd(1.0f, L.post_norm[i]), s_a[i]), s_inv);
-    w.xr[(size_t)t * d + i] = fadd(__ldcg(w.x + (size_t)t * d + i), fmul(gate, a));
-  }
-}
-
-// CrossState::apply (cross.rs:121-130), first step: zero_centred_norm of x
-// with the layer's cross norm, then fake_quantise_int8 and the per-group
-// rotation and codes of the q|gate product's input. grid M, block 128.
-__global__ void __launch_bounds__(128) k_cross_q(ModelDev md, int layer, Work w, int M) {
+// finish forms it) into w.xr for every token, then for the tokens of sessions
+// with a cross memory CrossState::apply's first step (cross.rs:121-130):
+// zero_centred_norm with the layer's cross norm, fake_quantise_int8 and the
+// q|gate product's activation step. grid M, block 128.
+__global__ void __launch_bounds__(128) k_cross_q(ModelDev md, LayerDev L, int layer, Work w, int M) {
   __shared__ __align__(16) float s_v[PREP_MAX_K];
   __shared__ float s_red[4];
   __shared__ float s_inv;
@@ -2178,9 +2175,24 @@ __global__ void __launch_bounds__(128) k_cross_q(ModelDev md, int layer, Work w,
   const int t = blockIdx.x, d = (int)md.d_model;
   if (t >= M) return;
   const TokenMeta meta = load_meta(w.meta, t);
-  if (meta.slot < 0 || !md.slot_cross[meta.slot]) return;
+  if (meta.slot < 0) return;
+  for (int i = threadIdx.x; i < d; i += blockDim.x) s_v[i] = __ldcg(w.outp + (size_t)t * d + i);
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    const float ss = sum_of_squares_warp(s_v, d);
+    if (threadIdx.x == 0) s_inv = inverse_rms(ss, d);
+  }
+  __syncthreads();
+  const float gate = sigmoid(L.attn_gate), inv_a = s_inv;
+  __syncthreads();
+  for (int i = threadIdx.x; i < d; i += blockDim.x) {
+    const float a = fmul(fmul(fadd(1.0f, L.post_norm[i]), s_v[i]), inv_a);
+    const float x = fadd(__ldcg(w.x + (size_t)t * d + i), fmul(gate, a));
+    s_v[i] = x;
+    w.xr[(size_t)t * d + i] = x;
+  }
+  if (!md.slot_cross[meta.slot]) return;  // no cross attention for this session (the whole block agrees)
   const CrossLayerDev& C = md.cross[layer];
-  for (int i = threadIdx.x; i < d; i += blockDim.x) s_v[i] = __ldcg(w.xr + (size_t)t * d + i);
   __syncthreads();
   if (threadIdx.x < 32) {
     const float ss = sum_of_squares_warp(s_v, d);
@@ -2323,30 +2335,6 @@ __global__ void __launch_bounds__(CROSS_THREADS) k_cross_attend(ModelDev md, int
   if (tid < HEAD_DIM) {
     const float g = __ldcg(w.cq + (size_t)t * 2 * d + d + h * HEAD_DIM + tid);
     w.attn[(size_t)t * heads * HEAD_DIM + h * HEAD_DIM + tid] = fmul(acc, sigmoid(g));
-  }
-}
-
-// CrossState::apply, last step (cross.rs:170-181): the out product's row
-// normed with post_norm, then x += sigmoid(gate) · attended. grid M, block 128.
-__global__ void __launch_bounds__(128) k_cross_finish(ModelDev md, int layer, Work w, int M) {
-  __shared__ __align__(16) float s_a[MAX_D];
-  __shared__ float s_inv;
-  pdl_wait();
-  const int t = blockIdx.x, d = (int)md.d_model;
-  if (t >= M) return;
-  const TokenMeta meta = load_meta(w.meta, t);
-  if (meta.slot < 0 || !md.slot_cross[meta.slot]) return;
-  const CrossLayerDev& C = md.cross[layer];
-  for (int i = threadIdx.x; i < d; i += blockDim.x) s_a[i] = __ldcg(w.outp + (size_t)t * d + i);
-  __syncthreads();
-  if (threadIdx.x < 32) {
-    const float ss = sum_of_squares_warp(s_a, d);
-    if (threadIdx.x == 0) s_inv = inverse_rms(ss, d);
-  }
-  __syncthreads();
-  for (int i = threadIdx.x; i < d; i += blockDim.x) {
-    const float a = fmul(fmul(fadd(1.0f, C.post_norm[i]), s_a[i]), s_inv);
-    w.xr[(size_t)t * d + i] = fadd(__ldcg(w.xr + (size_t)t * d + i), fmul(C.gain, a));
   }
 }
 
@@ -2652,14 +2640,12 @@ void launch_layer(const ModelDev& md, const LayerDev& L, const EngramDev* engram
            md.inv_sqrt_group, 1, 0);
   project(L.out, w.act, w.act_scale, w.outp, M, d, w.meta, st, md.error);
   if (cross) {  // Whistle: CrossState::apply after the attention residual (session.rs:126-128)
-    launch(k_resid, M, 128, 0, st, md, L, w, M);
-    launch(k_cross_q, M, 128, 0, st, md, layer, w, M);
+    launch(k_cross_q, M, 128, 0, st, md, L, layer, w, M);
     project(cross->qg, w.act, w.act_scale, w.cq, M, 2 * d, w.meta, st, md.error);
     launch(k_cross_attend, dim3(M, md.heads), CROSS_THREADS, 2 * MAX_CROSS_FRAMES * sizeof(float), st, md, layer, w, M);
     launch(k_prep, M, 128, 0, st, (const float*)w.attn, H * HEAD_DIM, (const int32_t*)nullptr, (const float*)nullptr, 0, H * HEAD_DIM,
            w.act, w.act_scale, M, w.meta, md.inv_sqrt_group, 1, 0);
-    project(cross->out, w.act, w.act_scale, w.outp, M, d, w.meta, st, md.error);
-    launch(k_cross_finish, M, 128, 0, st, md, layer, w, M);
+    project(cross->out, w.act, w.act_scale, w.outp, M, d, w.meta, st, md.error);  // the block finish adds it
   }
   launch_block(md, L, w, M, st);
 }
