@@ -229,6 +229,9 @@ def main():
     rank, world, local = ranks.rank, ranks.world, ranks.local
     dist = dp.init_group(ranks, "nccl")
 
+    if args.whistle_only:  # before the config-2 model and its KV pool
+        print(json.dumps({"config4": whistle(nb, local, args.ncu_range)}), flush=True)
+        return
     archive = synthetic.cached_archive(seed=0)
     seqs = 64 if args.profile else args.seqs
     rank_prompts = prompts(rank, seqs)
@@ -239,9 +242,6 @@ def main():
         model = model.with_depth(DEPTH)
     if args.batch1_only:
         print(json.dumps({"batch1": batch1(nb, model, local, args.ncu_range)}), flush=True)
-        return
-    if args.whistle_only:
-        print(json.dumps({"config4": whistle(nb, local, args.ncu_range)}), flush=True)
         return
     t0 = time.perf_counter()
     sessions = [nb.Session(model) for _ in rank_prompts]
