@@ -312,9 +312,10 @@ def main():
     if not args.no_batch1 and rank == 0 and not args.profile:
         batch.close()
         line["batch1"] = batch1(nb, model, local)
-        line["config0"] = config0(nb, model)
-        if not args.no_whistle:
-            line["config4"] = whistle(nb, local)
+        if world == 1:  # single-GPU configurations: a scaling run only repeats them
+            line["config0"] = config0(nb, model)
+            if not args.no_whistle:
+                line["config4"] = whistle(nb, local)
     if rank == 0 and world == 1 and not args.no_cpu and not args.profile:
         from oracle import oracle
 
