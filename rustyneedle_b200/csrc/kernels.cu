@@ -2257,31 +2257,30 @@ __global__ void __launch_bounds__(CROSS_THREADS) k_cross_attend(ModelDev md, int
     if (lane == 0) s_qs = fmul(scale, md.inv_root_qk);
   }
   __syncthreads();
+  // the scores: four lanes per frame, each with 16 bytes of the key row (a
+  // warp reads eight whole rows per load), the exact int32 dot summed over
+  // the quad; each warp takes 8 frames per round, eight rounds in flight
   float peak = -INFINITY;
-  const uint4* qv = reinterpret_cast<const uint4*>(s_q);
-  for (int f0 = tid; f0 < frames; f0 += 2 * CROSS_THREADS) {  // two frames' keys in flight
-    uint4 kk[2][4];
+  const int quarter = lane & 3;
+  const uint4 qq = reinterpret_cast<const uint4*>(s_q)[quarter];
+  constexpr int ROUND = CROSS_THREADS / 4, DEPTH = 8;
+  for (int base = warp * 8; base < frames; base += ROUND * DEPTH) {  // uniform per warp
+    uint4 kk[DEPTH];
 #pragma unroll
-    for (int u = 0; u < 2; ++u) {
-      const int f = min(f0 + u * CROSS_THREADS, frames - 1);
-      const uint4* kp = reinterpret_cast<const uint4*>(keys + ((size_t)f * heads + h) * HEAD_DIM);
-#pragma unroll
-      for (int k = 0; k < 4; ++k) kk[u][k] = kp[k];
+    for (int u = 0; u < DEPTH; ++u) {
+      const int f = min(base + u * ROUND + (lane >> 2), frames - 1);
+      kk[u] = reinterpret_cast<const uint4*>(keys + ((size_t)f * heads + h) * HEAD_DIM)[quarter];
     }
 #pragma unroll
-    for (int u = 0; u < 2; ++u) {
-      const int f = f0 + u * CROSS_THREADS;
-      if (f < frames) {
-        int part[4] = {0, 0, 0, 0};
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const uint4 qq = qv[k];
-          part[0] = dp4a(kk[u][k].x, qq.x, part[0]);
-          part[1] = dp4a(kk[u][k].y, qq.y, part[1]);
-          part[2] = dp4a(kk[u][k].z, qq.z, part[2]);
-          part[3] = dp4a(kk[u][k].w, qq.w, part[3]);
-        }
-        const int dot = (part[0] + part[1]) + (part[2] + part[3]);
+    for (int u = 0; u < DEPTH; ++u) {
+      int dot = dp4a(kk[u].x, qq.x, 0);
+      dot = dp4a(kk[u].y, qq.y, dot);
+      dot = dp4a(kk[u].z, qq.z, dot);
+      dot = dp4a(kk[u].w, qq.w, dot);
+      dot += __shfl_xor_sync(FULL, dot, 1);
+      dot += __shfl_xor_sync(FULL, dot, 2);
+      const int f = base + u * ROUND + (lane >> 2);
+      if (quarter == 0 && f < frames) {
         const float sc = fmul(fmul((float)dot, kscale[(size_t)f * heads + h]), s_qs);
         s_sc[f] = sc;
         peak = fmaxf(peak, sc);
