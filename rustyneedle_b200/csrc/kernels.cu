@@ -2147,19 +2147,22 @@ __global__ void __launch_bounds__(128) k_cross_memory_in(const float* __restrict
 
 // CrossWeights::memory, last step (cross.rs:83-96): per (frame, head) the key
 // normed with k_norm and quantised, the value quantised. kv: [frames][2d]
-// (keys, then values). grid frames, block 64 · heads (a warp per head and side).
-__global__ void k_cross_memory_heads(const float* __restrict__ kv, int d, const float* __restrict__ k_norm, int8_t* __restrict__ keys,
-                                     float* __restrict__ kscale, int8_t* __restrict__ values, float* __restrict__ vscale) {
+// (keys, then values). Stored head-major, [head][frame][64] and [head][frame],
+// so that one head's rows are one contiguous block. grid frames, block
+// 64 · heads (a warp per head and side).
+__global__ void k_cross_memory_heads(const float* __restrict__ kv, int d, int frames, const float* __restrict__ k_norm,
+                                     int8_t* __restrict__ keys, float* __restrict__ kscale, int8_t* __restrict__ values,
+                                     float* __restrict__ vscale) {
   const int t = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31, heads = d / HEAD_DIM;
   const bool key = warp < heads;
   const int h = key ? warp : warp - heads;
   const float* src = kv + (size_t)t * 2 * d + (key ? 0 : d) + h * HEAD_DIM;
   int8_t c0, c1;
   const float scale = norm_quant_head64(src[lane], src[lane + 32], k_norm, key, c0, c1);
-  int8_t* codes = (key ? keys : values) + ((size_t)t * heads + h) * HEAD_DIM;
+  int8_t* codes = (key ? keys : values) + ((size_t)h * frames + t) * HEAD_DIM;
   codes[lane] = c0;
   codes[lane + 32] = c1;
-  if (lane == 0) (key ? kscale : vscale)[(size_t)t * heads + h] = scale;
+  if (lane == 0) (key ? kscale : vscale)[(size_t)h * frames + t] = scale;
 }
 
 // x after the layer's attention residual (session.rs:121-125, as the block
@@ -2236,8 +2239,8 @@ __global__ void __launch_bounds__(CROSS_THREADS) k_cross_attend(ModelDev md, int
   // CROSS_CHUNK frames (16-byte copies by every thread), CROSS_BUFFERS - 1
   // ahead: they do not depend on the softmax, so the first ones load now
   __shared__ __align__(16) int8_t s_val[CROSS_BUFFERS][CROSS_CHUNK * HEAD_DIM];
-  const int8_t* vbase = values + (size_t)h * HEAD_DIM;
-  const size_t vstride = (size_t)heads * HEAD_DIM;
+  const int8_t* vbase = values + (size_t)h * frames * HEAD_DIM;  // this head's rows, contiguous
+  const size_t vstride = HEAD_DIM;
   auto stage = [&](int chunk) {  // commits one group, empty past the last chunk
     const int f0 = chunk * CROSS_CHUNK, n = min(CROSS_CHUNK, frames - f0);
     for (int i = tid; i < n * (HEAD_DIM / 16); i += CROSS_THREADS) {
@@ -2269,7 +2272,7 @@ __global__ void __launch_bounds__(CROSS_THREADS) k_cross_attend(ModelDev md, int
 #pragma unroll
     for (int u = 0; u < DEPTH; ++u) {
       const int f = min(base + u * ROUND + (lane >> 2), frames - 1);
-      kk[u] = reinterpret_cast<const uint4*>(keys + ((size_t)f * heads + h) * HEAD_DIM)[quarter];
+      kk[u] = reinterpret_cast<const uint4*>(keys + ((size_t)h * frames + f) * HEAD_DIM)[quarter];
     }
 #pragma unroll
     for (int u = 0; u < DEPTH; ++u) {
@@ -2281,7 +2284,7 @@ __global__ void __launch_bounds__(CROSS_THREADS) k_cross_attend(ModelDev md, int
       dot += __shfl_xor_sync(FULL, dot, 2);
       const int f = base + u * ROUND + (lane >> 2);
       if (quarter == 0 && f < frames) {
-        const float sc = fmul(fmul((float)dot, kscale[(size_t)f * heads + h]), s_qs);
+        const float sc = fmul(fmul((float)dot, kscale[(size_t)h * frames + f]), s_qs);
         s_sc[f] = sc;
         peak = fmaxf(peak, sc);
       }
@@ -2314,7 +2317,7 @@ __global__ void __launch_bounds__(CROSS_THREADS) k_cross_attend(ModelDev md, int
     }
   }
   __syncthreads();
-  for (int f = tid; f < frames; f += CROSS_THREADS) s_vw[f] = fmul(vscale[(size_t)f * heads + h], fmul(s_sc[f], s_inverse));
+  for (int f = tid; f < frames; f += CROSS_THREADS) s_vw[f] = fmul(vscale[(size_t)h * frames + f], fmul(s_sc[f], s_inverse));
   pdl_trigger();
   // thread d < 64 runs dimension d's ordered sum over the frames
   const int chunks = (frames + CROSS_CHUNK - 1) / CROSS_CHUNK;
@@ -2659,7 +2662,7 @@ cudaError_t cross_memory(const ModelDev& md, const std::vector<CrossLayerDev>& l
   for (size_t l = 0; l < layers.size(); ++l) {
     project(layers[l].kv, act, act_scale, kv, frames, 2 * d, nullptr, st, md.error, act_rows);
     const size_t at = l * (size_t)frames * heads;
-    k_cross_memory_heads<<<frames, 64 * heads, 0, st>>>(kv, d, layers[l].k_norm, keys + at * HEAD_DIM, kscale + at,
+    k_cross_memory_heads<<<frames, 64 * heads, 0, st>>>(kv, d, frames, layers[l].k_norm, keys + at * HEAD_DIM, kscale + at,
                                                        values + at * HEAD_DIM, vscale + at);
   }
   return cudaGetLastError();

@@ -42,8 +42,8 @@
 //
 // Whistle cross attention (whistle/src/cross.rs): per decoder layer the q|gate
 // and k|v products (k|v builds the memory) and the out product; a memory holds
-// for every layer the int8 keys and values [frame][head][64] of one encoder
-// output with their scales [frame][head]; slot_cross[slot] points at the
+// for every layer the int8 keys and values [head][frame][64] of one encoder
+// output with their scales [head][frame]; slot_cross[slot] points at the
 // memory a session attends to (null: none).
 #pragma once
 
@@ -160,10 +160,10 @@ struct CrossLayerDev {
 
 struct CrossMemDev {
   int frames;
-  const int8_t* keys;    // [layers][frames][heads][64]
-  const float* kscale;   // [layers][frames][heads]
-  const int8_t* values;  // [layers][frames][heads][64]
-  const float* vscale;   // [layers][frames][heads]
+  const int8_t* keys;    // [layers][heads][frames][64] (head-major: one head's rows are contiguous)
+  const float* kscale;   // [layers][heads][frames]
+  const int8_t* values;  // [layers][heads][frames][64]
+  const float* vscale;   // [layers][heads][frames]
 };
 constexpr int MAX_CROSS_FRAMES = 2048;  // a 30-second window is 1500 frames
 

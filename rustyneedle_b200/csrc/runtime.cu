@@ -1316,11 +1316,21 @@ nb_status nb_debug_cross_memory(const nb_cross_memory* memory, int layer, int8_t
     if (layer < 0 || layer >= (int)E.geo.num_layers) fail(NB_ERR_ARGUMENT, "layer out of range");
     NB_CUDA(cudaSetDevice(E.device));
     NB_CUDA(cudaStreamSynchronize(E.stream));
-    const size_t n = (size_t)m.frames * E.md.heads, at = (size_t)layer * n;
-    NB_CUDA(cudaMemcpy(keys, m.keys + at * HEAD_DIM, n * HEAD_DIM, cudaMemcpyDeviceToHost));
-    NB_CUDA(cudaMemcpy(values, m.values + at * HEAD_DIM, n * HEAD_DIM, cudaMemcpyDeviceToHost));
-    NB_CUDA(cudaMemcpy(key_scales, m.kscale + at, n * 4, cudaMemcpyDeviceToHost));
-    NB_CUDA(cudaMemcpy(value_scales, m.vscale + at, n * 4, cudaMemcpyDeviceToHost));
+    // the device keeps [head][frame]; the caller gets the reference's [frame][head]
+    const size_t F = (size_t)m.frames, H = E.md.heads, n = F * H, at = (size_t)layer * n;
+    std::vector<int8_t> k(n * HEAD_DIM), v(n * HEAD_DIM);
+    std::vector<float> ks(n), vs(n);
+    NB_CUDA(cudaMemcpy(k.data(), m.keys + at * HEAD_DIM, n * HEAD_DIM, cudaMemcpyDeviceToHost));
+    NB_CUDA(cudaMemcpy(v.data(), m.values + at * HEAD_DIM, n * HEAD_DIM, cudaMemcpyDeviceToHost));
+    NB_CUDA(cudaMemcpy(ks.data(), m.kscale + at, n * 4, cudaMemcpyDeviceToHost));
+    NB_CUDA(cudaMemcpy(vs.data(), m.vscale + at, n * 4, cudaMemcpyDeviceToHost));
+    for (size_t h = 0; h < H; ++h)
+      for (size_t f = 0; f < F; ++f) {
+        std::memcpy(keys + (f * H + h) * HEAD_DIM, &k[(h * F + f) * HEAD_DIM], HEAD_DIM);
+        std::memcpy(values + (f * H + h) * HEAD_DIM, &v[(h * F + f) * HEAD_DIM], HEAD_DIM);
+        key_scales[f * H + h] = ks[h * F + f];
+        value_scales[f * H + h] = vs[h * F + f];
+      }
   });
 }
 
