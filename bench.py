@@ -314,6 +314,7 @@ def main():
         line["batch1"] = batch1(nb, model, local)
         if world == 1:  # single-GPU configurations: a scaling run only repeats them
             line["config0"] = config0(nb, model)
+            line["grammar"] = grammar_masks(nb, model)
             if not args.no_whistle:
                 line["config4"] = whistle(nb, local)
     if rank == 0 and world == 1 and not args.no_cpu and not args.profile:
@@ -325,6 +326,8 @@ def main():
             line["config0"]["cpu"] = config0_cpu(archive)
         if "config4" in line:
             line["config4"]["cpu"] = whistle_cpu()
+        if "grammar" in line:
+            line["grammar"]["cpu"] = grammar_masks_cpu()
     if rank == 0:
         print(json.dumps(line), flush=True)
     batch.close()
@@ -368,6 +371,81 @@ def config0_cpu(archive: str):
     p50 = float(np.percentile(times[4:], 50))
     return {"p50_ms_per_token": round(p50, 4), "tokens_per_s": round(1000.0 / p50, 1), "cores": 1,
             "kind": "port", "sample": "60 timed greedy tokens after 4 untimed"}
+
+
+GRAMMAR = dict(sequences=256, tools=64, seed=5)
+
+
+def grammar_workload(vocab: int):
+    """A tool-name choice over 64 names and a vocabulary of short pieces (the shapes of a call's name literal)."""
+    rng = np.random.default_rng(GRAMMAR["seed"])
+    letters = np.frombuffer(b"abcdefghijklmnopqrstuvwxyz_", dtype=np.uint8)
+    names = [bytes(rng.choice(letters, size=int(rng.integers(6, 20))).tolist()) for _ in range(GRAMMAR["tools"])]
+    joined = b"|".join(names)
+    pieces = [None, None, None]
+    while len(pieces) < vocab:
+        a = int(rng.integers(0, len(joined)))
+        pieces.append(joined[a:a + int(rng.integers(1, 7))] if rng.random() < 0.8
+                      else bytes(rng.integers(32, 127, size=int(rng.integers(1, 8))).tolist()))
+    return names, pieces
+
+
+def grammar_masks(nb, model):
+    """Device grammar masks for 256 sequences inside a tool-name literal: µs per batch mask and per advance."""
+    import torch
+
+    V = model.config.output_vocab
+    B = GRAMMAR["sequences"]
+    names, pieces = grammar_workload(V)
+    trans, complete, start = nb.literal_automaton(names)
+    aut = nb.TokenAutomaton(model, trans, complete, start, pieces, 1, 2)
+    rng = np.random.default_rng(6)
+    # every sequence inside the literal, part-way along one of the names
+    states = np.full(B, start, dtype=np.uint32)
+    for b in range(B):
+        for byte in names[int(rng.integers(0, len(names)))][: int(rng.integers(0, 4))]:
+            states[b] = trans[states[b], byte]
+    d_states = torch.from_numpy(states.view(np.int32).copy()).cuda()
+    d_mask = torch.zeros(B * V // 32, dtype=torch.int32, device="cuda")
+    d_next = torch.full((B,), 0xFFFF, dtype=torch.int32, device="cuda")
+    torch.cuda.synchronize()
+    reps = 200
+    for _ in range(10):
+        aut.mask(d_states, d_mask)
+    model.synchronize()
+    t = time.perf_counter()
+    for _ in range(reps):
+        aut.mask(d_states, d_mask)
+    model.synchronize()
+    mask_us = 1e6 * (time.perf_counter() - t) / reps
+    t = time.perf_counter()
+    for _ in range(reps):
+        aut.advance(d_next, d_states)  # id 0xFFFF is beyond the vocabulary: the walk is skipped, the states stay
+    model.synchronize()
+    advance_us = 1e6 * (time.perf_counter() - t) / reps
+    aut.check()
+    aut.close()
+    return {"workload": f"{B} sequences inside a {len(names)}-name tool literal ({trans.shape[0]} automaton states), "
+            f"vocabulary {V} pieces of 1-7 bytes", "mask_us": round(mask_us, 2), "advance_us": round(advance_us, 2),
+            "masks_per_s": round(B * 1e6 / mask_us, 1),
+            "note": "host wall time per call (launch included) over 200 back-to-back calls, then a synchronise"}
+
+
+def grammar_masks_cpu():
+    """TokenBytes::allowed restated in Python (oracle/grammar.py) for 4 sequences of the same workload."""
+    from oracle import grammar as og
+
+    names, pieces = grammar_workload(8192)
+    rng = np.random.default_rng(6)
+    t = time.perf_counter()
+    for _ in range(4):
+        m = og.LiteralMachine(names)
+        for byte in names[int(rng.integers(0, len(names)))][: int(rng.integers(0, 4))]:
+            m.step(byte)
+        og.allowed(pieces, m)
+    per = (time.perf_counter() - t) / 4
+    return {"masks_per_s": round(1.0 / per, 1), "cores": 1, "kind": "port",
+            "sample": "4 masks, pure-Python restatement of TokenBytes::allowed (the reference's is Rust)"}
 
 
 WHISTLE = dict(layers=8, text_vocab=8000, frames=1500, batch=64, tokens=224)

@@ -127,6 +127,7 @@ nb_status nb_session_pooled_readout(nb_session* session, uint32_t code, float* o
  * decoder layer's int8 keys and values. NB_ERR_UNSUPPORTED when the archive
  * carries no audio section; frames in 1..2048 (a 30-second window is 1500). */
 typedef struct nb_cross_memory nb_cross_memory;
+typedef struct nb_token_automaton nb_token_automaton;
 nb_status nb_cross_memory_create(nb_model* model, const float* encoded, size_t frames, nb_cross_memory** out);
 void nb_cross_memory_release(nb_cross_memory* memory);
 
@@ -179,6 +180,51 @@ nb_status nb_batch_step_device(nb_batch* batch, const uint32_t* mask_bits_device
  * take `steps` more tokens. */
 nb_status nb_batch_run(nb_batch* batch, uint32_t steps, const uint32_t* mask_bits_device, uint32_t* tokens_device,
                        float* elapsed_ms);
+
+/* Device grammar masks. The reference builds each constrained step's mask on
+ * the host: TokenBytes::allowed (crates/grammar/src/mask.rs:28-42) steps a
+ * clone of the call machine through every vocabulary piece, and
+ * TokenBytes::advance (mask.rs:44-49) steps the live machine with the chosen
+ * piece, inside run_turn (crates/generate/src/generator.rs:102-124). Here the
+ * caller compiles the machine into a byte automaton and both operations run on
+ * the device for a whole batch.
+ *
+ * transitions: num_states × 256 next states (0 = the byte is rejected); state 0
+ * means "no call machine" and must not be complete. complete[s] != 0: the
+ * machine is done (CallMachine::is_complete, call.rs:83-85), so only call_end is
+ * allowed. start_state: the state grammar.start() enters after call_start.
+ * token_bytes / token_offsets (vocab + 1 entries): each output id's piece as
+ * TokenBytes::bytes gives it (mask.rs:24-26; an empty range = no bytes, never
+ * allowed). vocab must equal the model's output vocabulary. The arrays are
+ * copied; they may be freed on return. */
+#define NB_AUTOMATON_MAX_STATES (1u << 20)
+#define NB_AUTOMATON_MAX_PIECE 255u
+nb_status nb_token_automaton_create(nb_model* model, const uint32_t* transitions, uint32_t num_states,
+                                    const uint8_t* complete, uint32_t start_state, const uint8_t* token_bytes,
+                                    const uint32_t* token_offsets, uint32_t vocab, uint32_t call_start,
+                                    uint32_t call_end, nb_token_automaton** out);
+void nb_token_automaton_release(nb_token_automaton* automaton);
+
+/* Mask words (count × vocab/32, the layout nb_batch_step_device takes) for
+ * `count` sequences whose automaton states are states_device[0..count): all ids
+ * for state 0, call_end alone for a complete state, else the ids whose bytes the
+ * automaton accepts from that state (TokenBytes::allowed). Device pointers;
+ * queued on the model's stream, no synchronisation. */
+nb_status nb_token_automaton_mask(nb_token_automaton* automaton, const uint32_t* states_device, uint32_t count,
+                                  uint32_t* mask_bits_device);
+
+/* Advances states_device with the chosen ids next_device (generator.rs:118-124):
+ * call_start with state 0 enters start_state, call_end returns to 0, any other
+ * id steps the automaton through its bytes and keeps the last accepted state;
+ * UINT32_MAX (a sequence not stepped) leaves the state. Queued on the model's
+ * stream, no synchronisation. */
+nb_status nb_token_automaton_advance(nb_token_automaton* automaton, const uint32_t* next_device, uint32_t count,
+                                     uint32_t* states_device);
+
+/* Waits for the model's stream and reports NB_ERR_ARGUMENT if a mask or an
+ * advance since the last check met a state >= num_states (such a sequence was
+ * masked as unconstrained and not advanced); clears the report. */
+nb_status nb_token_automaton_check(nb_token_automaton* automaton);
 
 /* Waits for the model's stream. */
 nb_status nb_model_synchronize(nb_model* model);

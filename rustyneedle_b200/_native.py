@@ -97,6 +97,11 @@ def lib() -> ctypes.CDLL:
             "nb_batch_step_device": (I, [P, P, P, P]),
             "nb_batch_run": (I, [P, U32, P, P, ctypes.POINTER(ctypes.c_float)]),
             "nb_build_expf_table": (I, [ctypes.c_char_p]),
+            "nb_token_automaton_create": (I, [P, P, U32, P, U32, P, P, U32, U32, U32, ctypes.POINTER(P)]),
+            "nb_token_automaton_release": (None, [P]),
+            "nb_token_automaton_mask": (I, [P, P, U32, P]),
+            "nb_token_automaton_advance": (I, [P, P, U32, P]),
+            "nb_token_automaton_check": (I, [P]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -326,6 +331,10 @@ class Batch:
         if stats:
             return self._next.copy(), [StepStats(s.probability, s.mass, s.status) for s in self._stats]
         return self._next.copy()
+
+    def step_device(self, mask_bits_device: int | None, next_device: int) -> None:
+        """One step with device mask words (or None) and device output ids (nb_batch_step_device)."""
+        _check(lib().nb_batch_step_device(self._h, mask_bits_device, next_device, None))
 
     def run(self, steps: int, mask_bits_device: int | None = None, tokens_device: int | None = None) -> float:
         """`steps` device-resident greedy steps; returns their device time in ms."""

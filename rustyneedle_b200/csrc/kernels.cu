@@ -2535,6 +2535,7 @@ static bool pdl_enabled() {
 
 static thread_local long t_launches = 0;  // kernels this thread has launched (or recorded into a graph)
 long launch_counter() { return t_launches; }
+void note_launch() { ++t_launches; }
 
 template <typename... P, typename... A>
 static void launch_clustered(void (*kernel)(P...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, dim3 cluster, A&&... args) {

@@ -15,6 +15,7 @@ cudaError_t configure(const nbl::ModelDev& md, int t_cap);
 // Kernels the calling thread has launched or recorded into a graph so far
 // (the token loop's launchers; the test hooks are not counted).
 long launch_counter();
+void note_launch();
 
 void launch_embed(const nbl::ModelDev& md, const nbl::Work& w, int M, cudaStream_t st);
 // One decoder layer of M tokens. `distinct`: every token of the pass belongs
@@ -77,5 +78,25 @@ cudaError_t static_scratch_setup(int device);
 // *wait_failed whether a bounded wait of the product gave up.
 cudaError_t launch_static_project(int device, const nbl::ModelDev& md, const nbl::QMat& W, const float* in, int M, float* out,
                                   cudaStream_t st, int* wait_failed);
+
+// A byte automaton for device grammar masks (grammar.cu): transitions
+// [num_states][256] (0 = byte rejected; state 0 = no call machine), complete
+// [num_states], the vocabulary's pieces as bytes + offsets [vocab + 1], the
+// call's start state and marker ids, and an error word (bit 0: a state out of
+// range was met).
+struct AutomatonDev {
+  const uint32_t* transitions = nullptr;
+  const uint8_t* complete = nullptr;
+  const uint8_t* bytes = nullptr;
+  const uint32_t* offsets = nullptr;
+  uint32_t* error = nullptr;
+  uint32_t num_states = 0, start = 0, call_start = 0, call_end = 0;
+  int vocab = 0;
+};
+// TokenBytes::allowed for `count` sequences: mask [count][vocab / 32] words.
+cudaError_t automaton_mask(const AutomatonDev& a, const uint32_t* states, int count, uint32_t* mask, cudaStream_t st);
+// TokenBytes::advance plus the call markers of run_turn for `count` sequences.
+cudaError_t automaton_advance(const AutomatonDev& a, const uint32_t* next, int count, uint32_t* states,
+                              cudaStream_t st);
 
 }  // namespace nbk

@@ -998,6 +998,22 @@ struct nb_cross_memory {
   std::shared_ptr<CrossMem> mem;
 };
 
+struct nb_token_automaton {
+  std::shared_ptr<Engine> engine;
+  nbk::AutomatonDev dev;
+  void *transitions = nullptr, *complete = nullptr, *bytes = nullptr, *offsets = nullptr, *error = nullptr;
+  ~nb_token_automaton() {
+    if (!engine) return;
+    cudaSetDevice(engine->device);
+    cudaStreamSynchronize(engine->stream);  // no queued mask or advance still reads it
+    cudaFree(transitions);
+    cudaFree(complete);
+    cudaFree(bytes);
+    cudaFree(offsets);
+    cudaFree(error);
+  }
+};
+
 struct nb_session {
   std::shared_ptr<Engine> engine;
   std::vector<int32_t> active;
@@ -1291,6 +1307,100 @@ nb_status nb_cross_memory_create(nb_model* model, const float* encoded, size_t f
 }
 
 void nb_cross_memory_release(nb_cross_memory* memory) { delete memory; }
+
+nb_status nb_token_automaton_create(nb_model* model, const uint32_t* transitions, uint32_t num_states,
+                                    const uint8_t* complete, uint32_t start_state, const uint8_t* token_bytes,
+                                    const uint32_t* token_offsets, uint32_t vocab, uint32_t call_start,
+                                    uint32_t call_end, nb_token_automaton** out) {
+  if (!model || !out || !transitions || !complete || !token_offsets) return NB_ERR_ARGUMENT;
+  *out = nullptr;
+  return guard([&] {
+    Engine& E = *model->engine;
+    std::lock_guard<std::mutex> lock(E.mutex);
+    if (vocab != E.md.output_vocab)
+      fail(NB_ERR_ARGUMENT, "the automaton's vocabulary must cover the model's " + std::to_string(E.md.output_vocab) + " output ids");
+    if (num_states < 2 || num_states > NB_AUTOMATON_MAX_STATES)
+      fail(NB_ERR_ARGUMENT, "num_states must be in 2.." + std::to_string(NB_AUTOMATON_MAX_STATES));
+    if (start_state == 0 || start_state >= num_states) fail(NB_ERR_ARGUMENT, "start_state must be in 1..num_states-1");
+    if (call_start >= vocab || call_end >= vocab) fail(NB_ERR_ARGUMENT, "call_start and call_end must be output ids");
+    if (complete[0]) fail(NB_ERR_ARGUMENT, "state 0 (no call machine) cannot be complete");
+    const size_t cells = (size_t)num_states * 256;
+    for (size_t i = 0; i < cells; ++i)
+      if (transitions[i] >= num_states) fail(NB_ERR_ARGUMENT, "a transition leads outside the automaton");
+    if (token_offsets[0] != 0) fail(NB_ERR_ARGUMENT, "token_offsets[0] must be 0");
+    for (uint32_t t = 0; t < vocab; ++t) {
+      if (token_offsets[t + 1] < token_offsets[t]) fail(NB_ERR_ARGUMENT, "token_offsets must not decrease");
+      if (token_offsets[t + 1] - token_offsets[t] > NB_AUTOMATON_MAX_PIECE)
+        fail(NB_ERR_ARGUMENT, "a piece is longer than " + std::to_string(NB_AUTOMATON_MAX_PIECE) + " bytes");
+    }
+    const size_t nbytes = token_offsets[vocab];
+    if (nbytes && !token_bytes) fail(NB_ERR_ARGUMENT, "token_bytes is null");
+    NB_CUDA(cudaSetDevice(E.device));
+    auto a = std::make_unique<nb_token_automaton>();
+    a->engine = model->engine;
+    NB_CUDA(cudaMalloc(&a->transitions, cells * 4));
+    NB_CUDA(cudaMalloc(&a->complete, num_states));
+    NB_CUDA(cudaMalloc(&a->bytes, nbytes ? nbytes : 1));
+    NB_CUDA(cudaMalloc(&a->offsets, ((size_t)vocab + 1) * 4));
+    NB_CUDA(cudaMalloc(&a->error, 4));
+    NB_CUDA(cudaMemcpyAsync(a->transitions, transitions, cells * 4, cudaMemcpyHostToDevice, E.stream));
+    NB_CUDA(cudaMemcpyAsync(a->complete, complete, num_states, cudaMemcpyHostToDevice, E.stream));
+    if (nbytes) NB_CUDA(cudaMemcpyAsync(a->bytes, token_bytes, nbytes, cudaMemcpyHostToDevice, E.stream));
+    NB_CUDA(cudaMemcpyAsync(a->offsets, token_offsets, ((size_t)vocab + 1) * 4, cudaMemcpyHostToDevice, E.stream));
+    NB_CUDA(cudaMemsetAsync(a->error, 0, 4, E.stream));
+    NB_CUDA(cudaStreamSynchronize(E.stream));  // the host arrays may go once this returns
+    nbk::AutomatonDev& d = a->dev;
+    d.transitions = static_cast<const uint32_t*>(a->transitions);
+    d.complete = static_cast<const uint8_t*>(a->complete);
+    d.bytes = static_cast<const uint8_t*>(a->bytes);
+    d.offsets = static_cast<const uint32_t*>(a->offsets);
+    d.error = static_cast<uint32_t*>(a->error);
+    d.num_states = num_states;
+    d.start = start_state;
+    d.call_start = call_start;
+    d.call_end = call_end;
+    d.vocab = (int)vocab;
+    *out = a.release();
+  });
+}
+
+void nb_token_automaton_release(nb_token_automaton* automaton) { delete automaton; }
+
+nb_status nb_token_automaton_mask(nb_token_automaton* automaton, const uint32_t* states_device, uint32_t count,
+                                  uint32_t* mask_bits_device) {
+  if (!automaton || (count && (!states_device || !mask_bits_device))) return NB_ERR_ARGUMENT;
+  return guard([&] {
+    Engine& E = *automaton->engine;
+    std::lock_guard<std::mutex> lock(E.mutex);
+    NB_CUDA(cudaSetDevice(E.device));
+    NB_CUDA(nbk::automaton_mask(automaton->dev, states_device, (int)count, mask_bits_device, E.stream));
+  });
+}
+
+nb_status nb_token_automaton_advance(nb_token_automaton* automaton, const uint32_t* next_device, uint32_t count,
+                                     uint32_t* states_device) {
+  if (!automaton || (count && (!states_device || !next_device))) return NB_ERR_ARGUMENT;
+  return guard([&] {
+    Engine& E = *automaton->engine;
+    std::lock_guard<std::mutex> lock(E.mutex);
+    NB_CUDA(cudaSetDevice(E.device));
+    NB_CUDA(nbk::automaton_advance(automaton->dev, next_device, (int)count, states_device, E.stream));
+  });
+}
+
+nb_status nb_token_automaton_check(nb_token_automaton* automaton) {
+  if (!automaton) return NB_ERR_ARGUMENT;
+  return guard([&] {
+    Engine& E = *automaton->engine;
+    std::lock_guard<std::mutex> lock(E.mutex);
+    NB_CUDA(cudaSetDevice(E.device));
+    uint32_t word = 0;
+    NB_CUDA(cudaMemcpyAsync(&word, automaton->dev.error, 4, cudaMemcpyDeviceToHost, E.stream));
+    NB_CUDA(cudaMemsetAsync(automaton->dev.error, 0, 4, E.stream));
+    NB_CUDA(cudaStreamSynchronize(E.stream));
+    if (word) fail(NB_ERR_ARGUMENT, "a sequence state was outside the automaton (masked as unconstrained, not advanced)");
+  });
+}
 
 nb_status nb_session_set_cross(nb_session* session, nb_cross_memory* memory) {
   if (!session) return NB_ERR_ARGUMENT;
