@@ -234,12 +234,12 @@ nb_status nb_model_synchronize(nb_model* model);
  * f32::exp exactly) and writes it to `path`. Runs on the host CPU. */
 nb_status nb_build_expf_table(const char* path);
 
-/* Allocation-free codebook product. It has no counterpart in the reference:
- * it serves callers that may not allocate device memory — a host that has
+/* Allocation-free codebook product. It has no counterpart in the reference.
+ * It serves callers that may not allocate device memory — a host that has
  * given all of the GPU's memory to its own pool, or a thread that must not
  * take the device-wide synchronisation cudaMalloc/cudaFree imply — with the
- * same result as QuantisedMatrix::prepare + multiply_vector
- * (crates/kernels/src/matrix.rs:123-165) through one device matrix: which = 0
+ * product of one device matrix, the same result the model's own passes
+ * compute with it: which = 0
  * the fused q/k/v/gate rows of `layer`, 1 its out_proj, 2 the tied embedding.
  * in_device: count × 512 floats (16-byte aligned), out_device: count × rows
  * floats, both device memory of the model's GPU; stream: a cudaStream_t of that

@@ -85,3 +85,68 @@ def close_group(dist) -> None:
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
+
+
+@dataclass
+class ShardResult:
+    device: int
+    tokens: np.ndarray      # [steps][sequences] chosen ids
+    logits: np.ndarray      # [sequences][output_vocab] after the last step
+    device_ms: float        # device time of the decode steps (CUDA events on the model's stream)
+
+
+def decode_on_devices(archive: str, shards: list[list[np.ndarray]], devices: list[int], steps: int,
+                      depth: int) -> list[ShardResult]:
+    """Greedy-decodes shards[i] on devices[i], all GPUs driven from this one
+    process with one host thread per GPU (the threading a single Rust host
+    serving several GPUs uses: one model, one CUDA stream and one host thread
+    per device, no lock shared between them; the reference's process-wide
+    spin pool, crates/kernels/src/pool.rs:42-161, has no counterpart).
+
+    Each thread opens its own model on its device, feeds its shard's prompts
+    in shared prefill passes and steps them as one batch; the library
+    releases the GIL inside every call, so the devices run concurrently. A
+    thread's failure is raised here after every thread has finished."""
+    import threading
+
+    if len(shards) != len(devices):
+        raise ValueError("one shard per device")
+    results: list = [None] * len(devices)
+    errors: list = []
+
+    def work(i: int) -> None:
+        import rustyneedle_b200 as nb
+
+        try:
+            shard = shards[i]
+            pages = kv_pages_for(shard, steps + 2, depth)
+            model = nb.Model.open(archive, device=devices[i], max_sessions=len(shard) + 1, kv_pages=pages)
+            if depth != model.config.num_layers:
+                model = model.with_depth(depth)
+            sessions = [nb.Session(model) for _ in shard]
+            nb.feed_many(sessions, shard)
+            batch = nb.Batch(model, sessions)
+            import torch
+
+            tokens = torch.zeros(steps * len(shard), dtype=torch.int32, device=f"cuda:{devices[i]}")
+            torch.cuda.synchronize(devices[i])  # the fill (torch's stream) before the model's stream writes
+            ms = batch.run(steps, None, tokens.data_ptr())  # returns after the run's end event
+            logits = np.stack([s.logits() for s in sessions])
+            results[i] = ShardResult(devices[i], tokens.cpu().numpy().view(np.uint32).reshape(steps, len(shard)),
+                                     logits, ms)
+            batch.close()
+            for s in sessions:
+                s.close()
+            model.close()
+        except BaseException as e:  # reported by the caller's thread
+            errors.append((devices[i], e))
+
+    threads = [threading.Thread(target=work, args=(i,), name=f"needle-gpu{d}") for i, d in enumerate(devices)]
+    for t in threads:
+        t.start()
+    for t in threads:
+        t.join()
+    if errors:
+        device, e = errors[0]
+        raise RuntimeError(f"decoding on device {device} failed: {e}") from e
+    return results

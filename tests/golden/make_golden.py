@@ -1,6 +1,9 @@
 """Extracts the known-answer vectors of the reference's own unit tests into
-reference_kats.json. Run in the build container, where the reference tree is
-mounted; the JSON is committed so the tests never read the reference at run time.
+reference_kats.json. Run it where a rustyneedle checkout is at hand, giving the
+checkout's root as the first argument or in $RUSTYNEEDLE_REFERENCE; the JSON is
+committed so the tests never read the reference at run time.
+
+    python tests/golden/make_golden.py <rustyneedle checkout>
 
 Sources (paths inside the rustyneedle workspace):
   crates/model/tests/ladder.rs      bisection order and depth selections
@@ -18,7 +21,7 @@ import os
 import re
 import sys
 
-ROOT = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("RUSTYNEEDLE_REFERENCE", "/root/reference")
+ROOT = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("RUSTYNEEDLE_REFERENCE")
 OUT = os.path.join(os.path.dirname(os.path.abspath(__file__)), "reference_kats.json")
 
 
@@ -32,6 +35,8 @@ def ints(text: str) -> list[int]:
 
 
 def main() -> None:
+    if not ROOT:
+        sys.exit("usage: make_golden.py <rustyneedle checkout> (or set RUSTYNEEDLE_REFERENCE)")
     ladder = read("crates/model/tests/ladder.rs")
     order = ints(re.search(r"ladder::order\(20\),\s*vec!\[([^\]]*)\]", ladder).group(1))
     selects = {}
