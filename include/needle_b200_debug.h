@@ -44,11 +44,12 @@ nb_status nb_debug_product(int device, uint32_t bits, const uint8_t* packed, con
 
 /* A plain streaming read of a `bytes`-long device buffer (a multiple of 16)
  * on device `device`, through L2 with 16-byte loads, four 512-thread CTAs per
- * SM: *ms_per_read receives the mean device time of one read over `reps`
- * reads after three untimed ones (CUDA events). Below the L2 size it measures
- * the L2 read bandwidth, well above it the HBM read bandwidth. No reference
- * counterpart: the denominator of the batch-1 roofline. */
-nb_status nb_debug_read_bandwidth(int device, size_t bytes, uint32_t reps, float* ms_per_read);
+ * SM, `passes` (1-4096) reads of the whole buffer per launch: *ms_per_read
+ * receives the mean device time of one read of the buffer over `reps`
+ * launches after three untimed ones (CUDA events). Below the L2 size it
+ * measures the L2 read bandwidth, well above it the HBM read bandwidth. No
+ * reference counterpart: the denominator of the batch-1 roofline. */
+nb_status nb_debug_read_bandwidth(int device, size_t bytes, uint32_t passes, uint32_t reps, float* ms_per_read);
 
 /* The session's final hidden state (session.rs:140-143): d_model floats. */
 nb_status nb_debug_hidden(nb_session* session, float* out);

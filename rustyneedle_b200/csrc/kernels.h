@@ -67,9 +67,10 @@ void launch_debug_project(const nbl::ModelDev& md, const nbl::QMat& W, const flo
 cudaError_t launch_product_bench(const nbl::QMat& W, const float* in, int M, int8_t* act, float* act_scale, int act_rows, float* out,
                                  int* error, int reps, float* ms, cudaStream_t st);
 
-// A streaming read of `bytes` (a multiple of 16) from `data` through L2, three
-// untimed launches then `reps` timed ones; *ms = the mean device time of one.
-cudaError_t launch_read_bench(const void* data, size_t bytes, uint32_t* sink, int reps, float* ms, cudaStream_t st);
+// A streaming read of `bytes` (a multiple of 16) from `data` through L2,
+// `passes` times per launch; three untimed launches then `reps` timed ones;
+// *ms = the mean device time of one launch.
+cudaError_t launch_read_bench(const void* data, size_t bytes, int passes, uint32_t* sink, int reps, float* ms, cudaStream_t st);
 
 // The allocation-free product: tokens per call the file-scope scratch holds.
 constexpr int STATIC_MAX_TOKENS = 256;

@@ -2078,8 +2078,8 @@ nb_status nb_debug_product(int device, uint32_t bits, const uint8_t* packed, con
   });
 }
 
-nb_status nb_debug_read_bandwidth(int device, size_t bytes, uint32_t reps, float* ms_per_read) {
-  if (!ms_per_read || bytes < 16 || bytes % 16 != 0 || reps == 0) return NB_ERR_ARGUMENT;
+nb_status nb_debug_read_bandwidth(int device, size_t bytes, uint32_t passes, uint32_t reps, float* ms_per_read) {
+  if (!ms_per_read || bytes < 16 || bytes % 16 != 0 || reps == 0 || passes == 0 || passes > 4096) return NB_ERR_ARGUMENT;
   return guard([&] {
     int devices = 0;
     if (cudaGetDeviceCount(&devices) != cudaSuccess || devices == 0) fail(NB_ERR_NO_DEVICE, "no CUDA device");
@@ -2091,11 +2091,11 @@ nb_status nb_debug_read_bandwidth(int device, size_t bytes, uint32_t reps, float
     cudaError_t e = cudaMemsetAsync(buffer.p, 0x5A, bytes, st);
     if (e == cudaSuccess) e = cudaMemsetAsync(sink.p, 0, 16, st);
     float ms = 0.0f;
-    if (e == cudaSuccess) e = nbk::launch_read_bench(buffer.p, bytes, sink.p, (int)reps, &ms, st);
+    if (e == cudaSuccess) e = nbk::launch_read_bench(buffer.p, bytes, (int)passes, sink.p, (int)reps, &ms, st);
     if (e == cudaSuccess) e = cudaStreamSynchronize(st);
     cudaStreamDestroy(st);
     NB_CUDA(e);
-    *ms_per_read = ms;
+    *ms_per_read = ms / (float)passes;
   });
 }
 

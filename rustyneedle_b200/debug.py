@@ -31,7 +31,7 @@ def _declare() -> None:
         "nb_debug_cross_memory": [P, ctypes.c_int, P, P, P, P],
         "nb_debug_step_kernels": [P, ctypes.POINTER(ctypes.c_uint32)],
         "nb_debug_product": [I, U32, P, P, P, U32, U32, P, U32, P, U32, ctypes.POINTER(ctypes.c_float)],
-        "nb_debug_read_bandwidth": [I, SZ, U32, ctypes.POINTER(ctypes.c_float)],
+        "nb_debug_read_bandwidth": [I, SZ, U32, U32, ctypes.POINTER(ctypes.c_float)],
     }.items():
         fn = getattr(L, name)
         fn.restype = I
@@ -126,10 +126,11 @@ def product(bits: int, packed: np.ndarray, levels: np.ndarray, norms: np.ndarray
     return out, float(ms.value)
 
 
-def read_bandwidth(nbytes: int, reps: int = 20, device: int = 0) -> float:
-    """GB/s of a plain streaming read of an `nbytes` device buffer (the mean of
-    `reps` timed reads): the L2 read peak below the L2 size, HBM above it."""
+def read_bandwidth(nbytes: int, passes: int = 1, reps: int = 20, device: int = 0) -> float:
+    """GB/s of a plain streaming read of an `nbytes` device buffer, read
+    `passes` times per launch (the mean over `reps` launches): the L2 read
+    peak below the L2 size, HBM above it."""
     _declare()
     ms = ctypes.c_float()
-    _check(lib().nb_debug_read_bandwidth(device, nbytes, reps, ctypes.byref(ms)))
+    _check(lib().nb_debug_read_bandwidth(device, nbytes, passes, reps, ctypes.byref(ms)))
     return nbytes / (ms.value / 1000.0) / 1e9

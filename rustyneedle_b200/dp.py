@@ -81,6 +81,18 @@ def max_over_ranks(dist, value: float, device: str = "cpu") -> float:
     return float(t.item())
 
 
+def gather_over_ranks(dist, values: list[float], device: str = "cpu") -> list[list[float]]:
+    """Every rank's `values` (the same count on each rank), in rank order."""
+    if dist is None:
+        return [list(values)]
+    import torch
+
+    mine = torch.tensor(values, dtype=torch.float64, device=device)
+    parts = [torch.zeros_like(mine) for _ in range(dist.get_world_size())]
+    dist.all_gather(parts, mine)
+    return [[float(x) for x in p.cpu()] for p in parts]
+
+
 def close_group(dist) -> None:
     if dist is not None:
         dist.barrier()

@@ -83,3 +83,38 @@ def text_allowed(vocab: int) -> np.ndarray:
 
 def text_words(vocab: int) -> np.ndarray:
     return np.packbits(text_allowed(vocab), bitorder="little").view(np.uint32)
+
+
+def token_weight_bytes(depth: int, d: int = 512, heads: int = 8, kv_heads: int = 4, head_dim: int = 64,
+                       hada_n: int = 2048, left: int = 64, right: int = 32, rank: int = 8, lanes: int = 4,
+                       vocab: int = 8192, group: int = 128, projection_bits: int = 2, embedding_bits: int = 4,
+                       phi_bits: int = 4) -> int:
+    """Bytes of weights one decode token touches at `depth` layers, in the
+    archive's representation (packed codes and fp16 group norms, f32 vectors):
+    per layer the q/k/v/gate/out projections, the lane phi rows (4 + 4 + 16 of
+    lanes * d columns) and routing scalars, the norms and gates, and the
+    Hadamard MLP's diagonals, bias, three Kronecker factor pairs and rank-r
+    condition; once per token the two permutations, the final norm, the tied
+    logits matrix and one embedding row."""
+
+    def codebook(rows: int, cols: int, bits: int) -> int:
+        return rows * cols * bits // 8 + rows * (-(-cols // group)) * 2
+
+    projections = (codebook(heads * head_dim, d, projection_bits) + 2 * codebook(kv_heads * head_dim, d, projection_bits)
+                   + codebook(heads * head_dim, d, projection_bits) + codebook(d, heads * head_dim, projection_bits))
+    phi = codebook((2 + lanes) * lanes, lanes * d, phi_bits)
+    routing = 4 * (3 + 2 * lanes + lanes * lanes)
+    vectors = 4 * (d + 2 * head_dim + d + 1 + d)  # norm_in, q_norm, k_norm, post_norm, attn_gate, pre_hada
+    hadamard = 4 * (5 * hada_n + 3 * (left * left + right * right) + d * rank + rank * hada_n)
+    per_layer = projections + phi + routing + vectors + hadamard
+    once = 4 * 2 * hada_n + 4 * d + codebook(vocab, d, embedding_bits) + codebook(1, d, embedding_bits)
+    return depth * per_layer + once
+
+
+def prefill_product_macs(tokens: int, depth: int, d: int = 512, lanes: int = 4, vocab: int = 8192) -> int:
+    """int8 multiply-accumulates of the codebook products of a `tokens`-long
+    prefill: per token and layer the fused q/k/v/gate (1536 rows), out_proj
+    (512 rows) and lane phi rows (24 of lanes * d columns); the logits of the
+    last token only."""
+    per_token_layer = (1536 + 512) * d + (2 + lanes) * lanes * lanes * d
+    return tokens * depth * per_token_layer + vocab * d

@@ -78,3 +78,17 @@ def test_one_rank_needs_no_group():
     assert dp.max_over_ranks(None, 3.5) == 3.5
     dp.barrier(None)
     dp.close_group(None)
+
+
+def test_decode_on_devices_reports_a_thread_failure(native_built, archive_path):
+    """A device thread that fails (here: no GPU, or a device ordinal that does
+    not exist) is reported to the caller after every thread has finished."""
+    shards = [dp.shard_prompts(0, 1, 8, 12), dp.shard_prompts(1, 1, 8, 12)]
+    with pytest.raises(RuntimeError, match="decoding on device"):
+        dp.decode_on_devices(archive_path, shards, [999, 998], 1, depth=2)
+    with pytest.raises(ValueError):
+        dp.decode_on_devices(archive_path, shards, [0], 1, depth=2)
+
+
+def test_gather_over_one_rank():
+    assert dp.gather_over_ranks(None, [1.5, 2.0]) == [[1.5, 2.0]]
