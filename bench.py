@@ -500,79 +500,106 @@ def config0_cpu(archive: str):
             "kind": "port", "sample": "60 timed greedy tokens after 4 untimed"}
 
 
-GRAMMAR = dict(sequences=256, tools=64, seed=5)
+GRAMMAR = dict(sequences=256, seed=5, tools="home_assistant.json")
 
 
 def grammar_workload(vocab: int):
-    """A tool-name choice over 64 names and a vocabulary of short pieces (the shapes of a call's name literal)."""
+    """Whole tool calls over the reference's home-assistant tools (object
+    arguments, enums, bounded integers, a choice; tests/golden/tool_schemas.json)
+    and a vocabulary of the 256 byte pieces plus pieces cut from the tools'
+    JSON. Each of the 256 sequences stands part-way into a call: a seeded walk
+    of 0-80 accepted bytes through the call machine. Returns (tools, pieces,
+    the sequences' byte prefixes)."""
+    from rustyneedle_b200.grammar import call_automaton
+
+    with open(os.path.join(ROOT, "tests", "golden", "tool_schemas.json")) as f:
+        tools = json.load(f)[GRAMMAR["tools"]]
     rng = np.random.default_rng(GRAMMAR["seed"])
-    letters = np.frombuffer(b"abcdefghijklmnopqrstuvwxyz_", dtype=np.uint8)
-    names = [bytes(rng.choice(letters, size=int(rng.integers(6, 20))).tolist()) for _ in range(GRAMMAR["tools"])]
-    joined = b"|".join(names)
-    pieces = [None, None, None]
+    text = json.dumps(tools).encode() + b'[{"name":"' + b',"arguments":{' + b'0123456789}],'
+    pieces = [None, None, None] + [bytes([b]) for b in range(256)]
     while len(pieces) < vocab:
-        a = int(rng.integers(0, len(joined)))
-        pieces.append(joined[a:a + int(rng.integers(1, 7))] if rng.random() < 0.8
-                      else bytes(rng.integers(32, 127, size=int(rng.integers(1, 8))).tolist()))
-    return names, pieces
+        a = int(rng.integers(0, len(text)))
+        pieces.append(text[a:a + int(rng.integers(1, 8))])
+    trans, complete, start = call_automaton(tools)
+    structural = list(b'"}]:,{[0123456789')
+    prefixes = []
+    for _ in range(GRAMMAR["sequences"]):
+        s, prefix = start, b""
+        for _ in range(int(rng.integers(0, 81))):
+            ok = [b for b in range(256) if trans[s, b] and not trans[s, b] & 0x80000000]
+            if not ok or complete[s]:
+                break
+            pick = int(rng.choice(structural))
+            b = pick if pick in ok and rng.random() < 0.5 else int(rng.choice(ok))
+            s, prefix = int(trans[s, b]), prefix + bytes([b])
+        prefixes.append(prefix)
+    return tools, pieces, prefixes
 
 
 def grammar_masks(nb, model):
-    """Device grammar masks for 256 sequences inside a tool-name literal: µs per batch mask and per advance."""
+    """Device grammar masks for 256 sequences inside whole tool calls: µs per batch mask and per advance."""
     import torch
 
     V = model.config.output_vocab
     B = GRAMMAR["sequences"]
-    names, pieces = grammar_workload(V)
-    trans, complete, start = nb.literal_automaton(names)
+    tools, pieces, prefixes = grammar_workload(V)
+    t = time.perf_counter()
+    trans, complete, start = nb.call_automaton(tools)
+    compile_ms = 1000 * (time.perf_counter() - t)
     aut = nb.TokenAutomaton(model, trans, complete, start, pieces, 1, 2)
-    rng = np.random.default_rng(6)
-    # every sequence inside the literal, part-way along one of the names
-    states = np.full(B, start, dtype=np.uint32)
-    for b in range(B):
-        for byte in names[int(rng.integers(0, len(names)))][: int(rng.integers(0, 4))]:
-            states[b] = trans[states[b], byte]
+    states = np.zeros(B, dtype=np.uint32)
+    for b, prefix in enumerate(prefixes):
+        s = start
+        for byte in prefix:
+            s = int(trans[s, byte])
+        states[b] = s
     d_states = torch.from_numpy(states.view(np.int32).copy()).cuda()
     d_mask = torch.zeros(B * V // 32, dtype=torch.int32, device="cuda")
     d_next = torch.full((B,), 0xFFFF, dtype=torch.int32, device="cuda")
     torch.cuda.synchronize()
     reps = 200
     for _ in range(10):
-        aut.mask(d_states, d_mask)
+        aut.mask(d_states, d_mask, sync=False)
     model.synchronize()
     t = time.perf_counter()
     for _ in range(reps):
-        aut.mask(d_states, d_mask)
+        aut.mask(d_states, d_mask, sync=False)
     model.synchronize()
     mask_us = 1e6 * (time.perf_counter() - t) / reps
     t = time.perf_counter()
     for _ in range(reps):
-        aut.advance(d_next, d_states)  # id 0xFFFF is beyond the vocabulary: the walk is skipped, the states stay
+        aut.advance(d_next, d_states, sync=False)  # id 0xFFFF is beyond the vocabulary: the walk is skipped, the states stay
     model.synchronize()
     advance_us = 1e6 * (time.perf_counter() - t) / reps
     aut.check()
     aut.close()
-    return {"workload": f"{B} sequences inside a {len(names)}-name tool literal ({trans.shape[0]} automaton states), "
-            f"vocabulary {V} pieces of 1-7 bytes", "mask_us": round(mask_us, 2), "advance_us": round(advance_us, 2),
+    return {"workload": f"{B} sequences part-way into whole tool calls over the reference's {len(tools)} home-assistant "
+                        f"tools ({trans.shape[0]} automaton states, compiled in {compile_ms:.1f} ms), vocabulary {V} "
+                        f"pieces (256 bytes and cuts of the tools JSON)",
+            "mask_us": round(mask_us, 2), "advance_us": round(advance_us, 2),
             "masks_per_s": round(B * 1e6 / mask_us, 1),
             "note": "host wall time per call (launch included) over 200 back-to-back calls, then a synchronise"}
 
 
 def grammar_masks_cpu():
-    """TokenBytes::allowed restated in Python (oracle/grammar.py) for 4 sequences of the same workload."""
+    """TokenBytes::allowed over the restated CallMachine (oracle/grammar.py,
+    pure Python) for 4 sequences of the same workload."""
     from oracle import grammar as og
 
-    names, pieces = grammar_workload(8192)
-    rng = np.random.default_rng(6)
-    t = time.perf_counter()
-    for _ in range(4):
-        m = og.LiteralMachine(names)
-        for byte in names[int(rng.integers(0, len(names)))][: int(rng.integers(0, 4))]:
+    tools, pieces, prefixes = grammar_workload(8192)
+    grammar = og.CallGrammar(tools)
+    machines = []
+    for prefix in prefixes[:4]:
+        m = grammar.start()
+        for byte in prefix:
             m.step(byte)
+        machines.append(m)
+    t = time.perf_counter()
+    for m in machines:
         og.allowed(pieces, m)
-    per = (time.perf_counter() - t) / 4
+    per = (time.perf_counter() - t) / len(machines)
     return {"masks_per_s": round(1.0 / per, 1), "cores": 1, "kind": "port",
-            "sample": "4 masks, pure-Python restatement of TokenBytes::allowed (the reference's is Rust)"}
+            "sample": "4 masks, pure-Python restatement of TokenBytes::allowed over CallMachine (the reference's is Rust)"}
 
 
 from rustyneedle_b200.workloads import WHISTLE, whistle_archive  # noqa: E402

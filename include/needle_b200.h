@@ -118,7 +118,7 @@ nb_status nb_session_logits(nb_session* session, float* out, size_t capacity);
 nb_status nb_session_head_output(nb_session* session, uint32_t code, float* out, size_t capacity, size_t* count);
 
 /* Session::pooled_readout (session.rs:156-160): the pooled readout itself,
- * queries x d_model floats (Engine::embed reads head 3's, engine.rs:113-123). */
+ * queries x d_model floats (Engine::embed reads head 2's, CONFIDENCE_HEAD, engine.rs:110-120). */
 nb_status nb_session_pooled_readout(nb_session* session, uint32_t code, float* out, size_t capacity, size_t* count);
 
 /* Whistle (crates/whistle): a cross-attention memory of one encoder output.
@@ -189,7 +189,10 @@ nb_status nb_batch_run(nb_batch* batch, uint32_t steps, const uint32_t* mask_bit
  * caller compiles the machine into a byte automaton and both operations run on
  * the device for a whole batch.
  *
- * transitions: num_states × 256 next states (0 = the byte is rejected); state 0
+ * transitions: num_states × 256 next states (0 = the byte is rejected; a value
+ * with the top bit set also rejects the byte and leaves the machine in the state
+ * of the low 31 bits, as the reference's array and object stages change state on
+ * some bytes they reject, machine.rs:357-364, 444-451, 495-505); state 0
  * means "no call machine" and must not be complete. complete[s] != 0: the
  * machine is done (CallMachine::is_complete, call.rs:83-85), so only call_end is
  * allowed. start_state: the state grammar.start() enters after call_start.
@@ -225,6 +228,30 @@ nb_status nb_token_automaton_advance(nb_token_automaton* automaton, const uint32
  * advance since the last check met a state >= num_states (such a sequence was
  * masked as unconstrained and not advanced); clears the report. */
 nb_status nb_token_automaton_check(nb_token_automaton* automaton);
+
+/* A compiled tool-call grammar: the byte automaton of CallGrammar's
+ * CallMachine (crates/grammar/src/call.rs:33-174) for the tools JSON that
+ * CallGrammar::from_tools_json takes (call.rs:16-31, 47-49; the schemas as
+ * schema::compile reads them, schema.rs:29-141), ready for
+ * nb_token_automaton_create. Host only: no GPU is needed.
+ *
+ * require_call != 0 is CallGrammar::require_call (call.rs:51-55): no empty
+ * call list, and with permitted (permitted_count indices into the tool list)
+ * only those tools; permitted must be NULL without require_call. The
+ * automaton's states are the call machine's reachable states (state 0 = no
+ * machine); exploring more than max_states (0 = NB_AUTOMATON_MAX_STATES)
+ * fails with NB_ERR_UNSUPPORTED, the caller then keeps building masks on the
+ * host. Malformed JSON fails with NB_ERR_ARGUMENT. */
+typedef struct nb_call_grammar nb_call_grammar;
+nb_status nb_call_grammar_compile(const char* tools_json, int require_call, const uint32_t* permitted, size_t permitted_count,
+                                  uint32_t max_states, nb_call_grammar** out);
+/* Its number of states S (state 0 included). */
+uint32_t nb_call_grammar_states(const nb_call_grammar* grammar);
+/* Copies its tables: transitions (S × 256), complete (S) and the start state
+ * (CallMachine::start, call.rs:57-59), in nb_token_automaton_create's form. */
+nb_status nb_call_grammar_tables(const nb_call_grammar* grammar, uint32_t* transitions, uint8_t* complete,
+                                 uint32_t* start_state);
+void nb_call_grammar_release(nb_call_grammar* grammar);
 
 /* Waits for the model's stream. */
 nb_status nb_model_synchronize(nb_model* model);

@@ -27,8 +27,8 @@ from ._native import (  # noqa: F401
     feed_many,
     library_path,
 )
-from .grammar import TokenAutomaton, literal_automaton, token_table  # noqa: F401
+from .grammar import TokenAutomaton, call_automaton, literal_automaton, token_table  # noqa: F401
 
 __all__ = ["Model", "Session", "Batch", "ModelConfig", "StepStats", "NeedleError", "DepthError", "ContextOverflow",
            "feed_many", "library_path", "CrossMemory",
-           "TokenAutomaton", "literal_automaton", "token_table"]
+           "TokenAutomaton", "call_automaton", "literal_automaton", "token_table"]

@@ -22,7 +22,7 @@ LIBRARY = os.path.join(OUT, "libneedle_b200.so")
 EXPF_TABLE = os.path.join(OUT, "glibc_expf_exceptions.bin")
 INCLUDE = os.path.join(os.path.dirname(HERE), "include")
 
-SOURCES = ["kernels.cu", "grammar.cu", "runtime.cu", "archive.cpp", "expf_table.cpp"]
+SOURCES = ["kernels.cu", "grammar.cu", "runtime.cu", "archive.cpp", "expf_table.cpp", "call_grammar.cpp"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ARCH + ["-O3", "-lineinfo", "-std=c++17", "-fmad=false", "--expt-relaxed-constexpr",
                      "-Xcompiler", "-fPIC,-ffp-contract=off,-O3", f"-I{INCLUDE}"]

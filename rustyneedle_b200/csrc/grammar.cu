@@ -5,8 +5,11 @@
 // machine once per vocabulary piece and steps it byte by byte, and
 // TokenBytes::advance (mask.rs:44-49) steps the live machine with the chosen
 // piece. Here the machine is given as a byte automaton — transitions
-// [state][256], 0 = the byte is rejected — compiled by the caller, and both
-// operations run on the device for a whole batch:
+// [state][256]: the next state; 0 = the byte is rejected; the top bit set =
+// the byte is rejected and the machine moves to the state in the low 31 bits
+// (the reference's array and object stages change state on some bytes they
+// reject) — compiled by the caller (nb_call_grammar_compile builds it from the
+// tools JSON), and both operations run on the device for a whole batch:
 //
 //   states[b] == 0      no call machine (generator.rs:110, argmax over all ids)
 //   complete[states[b]] the machine is done; only call_end is allowed
@@ -16,8 +19,8 @@
 //
 // and the advance follows generator.rs:118-124: call_start with no machine
 // enters `start`, call_end leaves it, any other token steps the machine
-// through its bytes and keeps the last accepted state (a rejected byte leaves
-// LiteralState and Choice unchanged, machine.rs:39-52, 294-303).
+// through its bytes until the first rejected one (TokenBytes::advance's
+// `all`), which leaves the state or moves it where the top bit says.
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -29,6 +32,7 @@ namespace nbk {
 constexpr int AUTOMATON_THREADS = 256;
 constexpr int AUTOMATON_ROUNDS = 4;  // tokens per thread: a CTA covers 1024 ids
 constexpr uint32_t AUTOMATON_BAD_STATE = 1u;
+constexpr uint32_t REJECT_MOVES = 0x80000000u;  // a rejected byte that still changes the state
 
 // grid (ceil(V / 1024), count), block 256. Each warp's 32 consecutive ids form
 // one mask word (ballot). The first byte of every piece is looked up in the
@@ -63,9 +67,11 @@ __global__ void __launch_bounds__(AUTOMATON_THREADS)
       } else {
         const uint32_t o = offsets[t], e = offsets[t + 1];
         if (e > o) {
-          uint32_t q = s_row[bytes[o]];
-          for (uint32_t k = o + 1; q != 0 && k < e; ++k) q = transitions[(size_t)q * 256 + bytes[k]];
-          ok = q != 0;
+          // a rejection, with or without a state change, ends the walk: the
+          // entry is then 0 or has the top bit set, both not positive as int32
+          int32_t q = (int32_t)s_row[bytes[o]];
+          for (uint32_t k = o + 1; q > 0 && k < e; ++k) q = (int32_t)transitions[(size_t)q * 256 + bytes[k]];
+          ok = q > 0;
         }
       }
     }
@@ -99,6 +105,10 @@ __global__ void k_automaton_advance(const uint32_t* __restrict__ transitions, ui
     for (uint32_t k = offsets[t], e = offsets[t + 1]; k < e; ++k) {
       const uint32_t q = transitions[(size_t)s * 256 + bytes[k]];
       if (q == 0) break;
+      if (q & REJECT_MOVES) {
+        s = q & ~REJECT_MOVES;
+        break;
+      }
       s = q;
     }
   }

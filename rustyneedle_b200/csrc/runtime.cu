@@ -1326,7 +1326,7 @@ nb_status nb_token_automaton_create(nb_model* model, const uint32_t* transitions
     if (complete[0]) fail(NB_ERR_ARGUMENT, "state 0 (no call machine) cannot be complete");
     const size_t cells = (size_t)num_states * 256;
     for (size_t i = 0; i < cells; ++i)
-      if (transitions[i] >= num_states) fail(NB_ERR_ARGUMENT, "a transition leads outside the automaton");
+      if ((transitions[i] & 0x7FFFFFFFu) >= num_states) fail(NB_ERR_ARGUMENT, "a transition leads outside the automaton");
     if (token_offsets[0] != 0) fail(NB_ERR_ARGUMENT, "token_offsets[0] must be 0");
     for (uint32_t t = 0; t < vocab; ++t) {
       if (token_offsets[t + 1] < token_offsets[t]) fail(NB_ERR_ARGUMENT, "token_offsets must not decrease");

@@ -8,13 +8,17 @@ compiled into a byte automaton once, and the masks and the advance run on the
 device for a whole batch (`TokenAutomaton`).
 
 `token_table` lays out the vocabulary as TokenBytes::new does (mask.rs:12-22:
-a piece per id, None for ids without bytes). `literal_automaton` compiles a
-Literals machine (LiteralState, crates/grammar/src/machine.rs:278-312), the
-form a call's tool-name choice takes (call.rs:87-90), into a trie automaton.
+a piece per id, None for ids without bytes). `call_automaton` compiles a whole
+tool-call grammar — CallGrammar::from_tools_json and its CallMachine
+(crates/grammar/src/call.rs:16-174, every schema form of schema.rs and
+machine.rs) — in the library (nb_call_grammar_compile, host only).
+`literal_automaton` compiles a tool-name choice alone (the Name stage of
+CallMachine::step, call.rs:123-130) into a trie automaton.
 """
 from __future__ import annotations
 
 import ctypes
+import json
 
 import numpy as np
 
@@ -36,15 +40,17 @@ def token_table(pieces: list) -> tuple[np.ndarray, np.ndarray]:
 
 
 def literal_automaton(options: list, permitted: list | None = None) -> tuple[np.ndarray, np.ndarray, int]:
-    """Trie automaton of LiteralState::restricted(options, permitted) (machine.rs:290-303).
+    """Trie automaton of the Name stage of CallMachine::step (call.rs:123-130)
+    over LiteralState::restricted(options, permitted) (machine.rs:290-312).
 
     A LiteralState is its alive options and its position; the states reachable
-    from the start are exactly the prefixes shared by the alive options, so the
-    trie over the permitted options' bytes is the machine. Returns
-    (transitions [S][256] uint32, complete [S] uint8, start = 1); state 0 is the
-    "no machine" state and every rejected byte maps to 0. complete marks a node
-    that ends an option (can_finish, machine.rs:305-307) and has no longer
-    option beneath it: the machine accepts no further byte.
+    from the start are the prefixes the alive options share, so the trie of the
+    permitted options is the machine. The stage ends as soon as chosen() finds
+    an alive option that has ended, so a node that ends an option is complete
+    and nothing beneath it is reachable (with 'get' and 'get_user' permitted,
+    'get' is chosen after its third byte). Returns (transitions [S][256]
+    uint32, complete [S] uint8, start = 1); state 0 is the "no machine" state
+    and every rejected byte maps to 0.
     """
     chosen = range(len(options)) if permitted is None else permitted
     edges: list[dict] = [{}, {}]
@@ -60,13 +66,61 @@ def literal_automaton(options: list, permitted: list | None = None) -> tuple[np.
                 ends.append(False)
             node = nxt
         ends[node] = True
-    transitions = np.zeros((len(edges), 256), dtype=np.uint32)
-    complete = np.zeros(len(edges), dtype=np.uint8)
-    for node, out in enumerate(edges):
-        for byte, nxt in out.items():
-            transitions[node, byte] = nxt
-        complete[node] = 1 if (node != 0 and ends[node] and not out) else 0
+    # keep what the stage can reach: nothing below a node that ends an option
+    number = {1: 1}
+    order = [1]
+    for node in order:
+        if ends[node]:
+            continue
+        for byte, nxt in sorted(edges[node].items()):
+            number[nxt] = len(order) + 1
+            order.append(nxt)
+    transitions = np.zeros((len(order) + 1, 256), dtype=np.uint32)
+    complete = np.zeros(len(order) + 1, dtype=np.uint8)
+    for node in order:
+        s = number[node]
+        complete[s] = 1 if ends[node] else 0
+        if not ends[node]:
+            for byte, nxt in edges[node].items():
+                transitions[s, byte] = number[nxt]
     return transitions, complete, 1
+
+
+def call_automaton(tools, require_call: bool = False, permitted: list | None = None,
+                   max_states: int = 0) -> tuple[np.ndarray, np.ndarray, int]:
+    """The byte automaton of CallGrammar::from_tools_json(tools) (call.rs:47-49),
+    with require_call(permitted) when require_call (call.rs:51-55), compiled by
+    the library on the host (nb_call_grammar_compile). `tools` is the JSON text
+    or the decoded list. Returns (transitions [S][256] uint32, complete [S]
+    uint8, start), the tables TokenAutomaton takes. Raises NeedleError with
+    NB_ERR_UNSUPPORTED when the machine has more than max_states states."""
+    text = tools if isinstance(tools, str) else json.dumps(tools)
+    L = lib()
+    if not getattr(L, "_call_grammar_declared", False):
+        P, U32 = ctypes.c_void_p, ctypes.c_uint32
+        L.nb_call_grammar_compile.argtypes = [ctypes.c_char_p, ctypes.c_int, P, ctypes.c_size_t, U32, ctypes.POINTER(P)]
+        L.nb_call_grammar_compile.restype = ctypes.c_int
+        L.nb_call_grammar_states.argtypes = [P]
+        L.nb_call_grammar_states.restype = U32
+        L.nb_call_grammar_tables.argtypes = [P, P, P, ctypes.POINTER(U32)]
+        L.nb_call_grammar_tables.restype = ctypes.c_int
+        L.nb_call_grammar_release.argtypes = [P]
+        L.nb_call_grammar_release.restype = None
+        L._call_grammar_declared = True
+    allowed = None if permitted is None else np.ascontiguousarray(permitted, dtype=np.uint32)
+    h = ctypes.c_void_p()
+    _check(L.nb_call_grammar_compile(text.encode(), 1 if require_call else 0,
+                                     _ptr(allowed) if allowed is not None and allowed.size else None,
+                                     0 if allowed is None else allowed.size, max_states, ctypes.byref(h)))
+    try:
+        n = int(L.nb_call_grammar_states(h))
+        transitions = np.zeros((n, 256), dtype=np.uint32)
+        complete = np.zeros(n, dtype=np.uint8)
+        start = ctypes.c_uint32()
+        _check(L.nb_call_grammar_tables(h, _ptr(transitions), _ptr(complete), ctypes.byref(start)))
+    finally:
+        L.nb_call_grammar_release(h)
+    return transitions, complete, int(start.value)
 
 
 def _address(buffer) -> int | None:
@@ -94,14 +148,36 @@ class TokenAutomaton:
                                                int(call_start), int(call_end), ctypes.byref(h)))
         self._h = h
 
-    def mask(self, states, mask_bits, count: int | None = None) -> None:
+    # The kernels run on the model's CUDA stream. Buffers that torch has just
+    # written on its own stream must be complete before they are read there,
+    # and torch must not read the results before the model's stream is done:
+    # with sync (the default) the wrapper waits for torch's current stream
+    # before queuing and for the model's stream after it.
+    def _torch_ready(self, *buffers) -> None:
+        for b in buffers:
+            if hasattr(b, "data_ptr") and getattr(b, "is_cuda", False):
+                import torch
+
+                torch.cuda.current_stream(b.device).synchronize()
+                return
+
+    def mask(self, states, mask_bits, count: int | None = None, sync: bool = True) -> None:
         """Device mask words [count][vocab/32] for device states (uint32/int32 tensors)."""
         n = int(states.numel()) if count is None else count
+        if sync:
+            self._torch_ready(states, mask_bits)
         _check(lib().nb_token_automaton_mask(self._h, _address(states), n, _address(mask_bits)))
+        if sync:
+            self.model.synchronize()
 
-    def advance(self, next_ids, states, count: int | None = None) -> None:
+    def advance(self, next_ids, states, count: int | None = None, sync: bool = True) -> None:
+        """Advances the device states with the chosen ids (run_turn's markers included)."""
         n = int(states.numel()) if count is None else count
+        if sync:
+            self._torch_ready(next_ids, states)
         _check(lib().nb_token_automaton_advance(self._h, _address(next_ids), n, _address(states)))
+        if sync:
+            self.model.synchronize()
 
     def check(self) -> None:
         _check(lib().nb_token_automaton_check(self._h))

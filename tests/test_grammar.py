@@ -1,8 +1,10 @@
 """Device grammar masks, host side: the trie automaton that literal_automaton
-compiles reproduces LiteralState (crates/grammar/src/machine.rs:278-312) under
-TokenBytes::allowed / advance (crates/grammar/src/mask.rs:28-49) along random
-constrained walks, and the automaton's marker rules follow run_turn
-(crates/generate/src/generator.rs:102-124). CPU only."""
+compiles reproduces a call's tool-name choice (the Name stage of
+CallMachine::step over LiteralState, crates/grammar/src/call.rs:123-130,
+machine.rs:278-312) under TokenBytes::allowed / advance
+(crates/grammar/src/mask.rs:28-49) along random constrained walks, and the
+automaton's marker rules follow run_turn (crates/generate/src/generator.rs:102-124).
+CPU only."""
 
 import numpy as np
 
@@ -29,10 +31,6 @@ def _pieces(rng, count):
     return pieces
 
 
-def _complete(machine):
-    return machine.can_finish() and not machine.accepts_more()
-
-
 def test_token_table_layout():
     data, offsets = token_table([b"ab", None, b"", b"c"])
     assert data.tobytes() == b"abc"
@@ -51,9 +49,9 @@ def test_literal_automaton_matches_literal_state():
     for permitted in (None, [0, 1, 3], [4, 2]):
         trans, complete, start = literal_automaton(OPTIONS, permitted)
         for _ in range(25):
-            machine, state = og.LiteralMachine(OPTIONS, permitted), start
+            machine, state = og.NameChoice(OPTIONS, permitted), start
             for _ in range(12):
-                if _complete(machine):
+                if machine.is_complete():
                     assert complete[state]
                     break
                 assert not complete[state]
@@ -92,7 +90,7 @@ def test_automaton_markers_follow_run_turn():
     else:
         pieces.append(b"gex")
         t = len(pieces) - 1
-    m = og.LiteralMachine(OPTIONS)
-    assert not og.advance(pieces, m, t) and m.position == 2
+    m = og.NameChoice(OPTIONS)
+    assert not og.advance(pieces, m, t) and m.literal.position == 2
     s = adv(s, t)
     assert og.automaton_mask(trans, complete, pieces, s, CALL_END) == og.allowed(pieces, m)
