@@ -42,6 +42,14 @@ nb_status nb_debug_hadamard(nb_model* model, uint32_t layer, const float* in, si
 nb_status nb_debug_product(int device, uint32_t bits, const uint8_t* packed, const float* levels, const uint16_t* norms, uint32_t rows,
                            uint32_t cols, const float* in, uint32_t count, float* out, uint32_t reps, float* ms_per_product);
 
+/* Failure detection test: the next `count` routing CTAs (k_route) on the
+ * model's GPU each give up a short bounded wait on a barrier no copy will
+ * complete, before issuing any copy, and set the engine's error flag; the next
+ * synchronising call that ran them returns NB_ERR_TIMEOUT, as for any device
+ * wait that gave up. The session that ran them is left inconsistent; other
+ * sessions and models are not affected. No reference counterpart. */
+nb_status nb_debug_expire_waits(nb_model* model, uint32_t count);
+
 /* A plain streaming read of a `bytes`-long device buffer (a multiple of 16)
  * on device `device`, through L2 with 16-byte loads, four 512-thread CTAs per
  * SM, `passes` (1-4096) reads of the whole buffer per launch: *ms_per_read

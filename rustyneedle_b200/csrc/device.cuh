@@ -45,6 +45,20 @@ constexpr uint32_t MBAR_WAIT_LIMIT = 1u << 24;
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
+__device__ __forceinline__ bool mbar_wait_polls(uint32_t bar, uint32_t phase, uint32_t polls) {
+  for (uint32_t i = 0; i < polls; ++i) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.b32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(bar), "r"(phase)
+        : "memory");
+    if (done) return true;
+  }
+  return false;
+}
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t phase) {
   for (uint32_t i = 0; i < MBAR_WAIT_LIMIT; ++i) {
     uint32_t done;

@@ -237,6 +237,25 @@ __host__ __device__ inline size_t route_floats(int d) {
   return PHI_ROWS * n / 4 + 2 * n + 8 * (n / 8 + 4) + n / 4 + PHI_ROWS * ng + d;
 }
 
+// Failure detection test hook: while g_expire_route > 0, each k_route CTA
+// that takes one of its counts gives up a bounded wait on a barrier that no
+// copy will complete (short poll limit), records the engine's error flag and
+// returns — before it issues any copy, so nothing asynchronous outlives it.
+// The host then reports NB_ERR_TIMEOUT like any expired wait. Set only by
+// nb_debug_expire_waits; 0 otherwise.
+__device__ int g_expire_route = 0;
+constexpr uint32_t EXPIRE_POLLS = 1u << 12;
+
+__device__ __forceinline__ bool take_expiry() {
+  int v = *reinterpret_cast<volatile int*>(&g_expire_route);
+  while (v > 0) {
+    const int prev = atomicCAS(&g_expire_route, v, v - 1);
+    if (prev == v) return true;
+    v = prev;
+  }
+  return false;
+}
+
 __global__ void __launch_bounds__(256) k_route(ModelDev md, LayerDev L, Work w, int M, int layer, int slot, int* error) {
   extern __shared__ __align__(16) float sm[];
   const int t = blockIdx.x;
@@ -257,6 +276,18 @@ __global__ void __launch_bounds__(256) k_route(ModelDev md, LayerDev L, Work w, 
   __shared__ __align__(8) uint64_t s_bar;
   const uint32_t bar = smem_u32(&s_bar);
 
+  {
+    __shared__ int s_expire;
+    if (tid == 0) s_expire = take_expiry();
+    __syncthreads();
+    if (s_expire) {
+      if (tid == 0) {
+        bulk_start(bar, 16);  // 16 bytes announced, no copy issued: the wait cannot complete
+        if (!mbar_wait_polls(bar, 0, EXPIRE_POLLS)) atomicExch(error, 1);
+      }
+      return;
+    }
+  }
   // the layer's constant weights first, then (once the previous kernel is
   // done) the token's stream. One thread arms the barrier and issues the bulk
   // copies: the pre, post and residual rows of this layer are contiguous in
@@ -2872,6 +2903,10 @@ cudaError_t launch_product_bench(const QMat& W, const float* in, int M, int8_t* 
   cudaEventDestroy(stop);
   *ms = total / (float)reps;
   return e;
+}
+
+cudaError_t set_expire_route(int count, cudaStream_t st) {
+  return cudaMemcpyToSymbolAsync(g_expire_route, &count, sizeof(int), 0, cudaMemcpyHostToDevice, st);
 }
 
 // ------------------------------------------------------- read bandwidth

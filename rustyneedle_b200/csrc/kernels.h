@@ -67,6 +67,10 @@ void launch_debug_project(const nbl::ModelDev& md, const nbl::QMat& W, const flo
 cudaError_t launch_product_bench(const nbl::QMat& W, const float* in, int M, int8_t* act, float* act_scale, int act_rows, float* out,
                                  int* error, int reps, float* ms, cudaStream_t st);
 
+// Failure detection test hook: the next `count` k_route CTAs each give up a
+// short bounded wait before issuing any copy and set the engine's error flag.
+cudaError_t set_expire_route(int count, cudaStream_t st);
+
 // A streaming read of `bytes` (a multiple of 16) from `data` through L2,
 // `passes` times per launch; three untimed launches then `reps` timed ones;
 // *ms = the mean device time of one launch.

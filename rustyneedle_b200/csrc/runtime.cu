@@ -2078,6 +2078,17 @@ nb_status nb_debug_product(int device, uint32_t bits, const uint8_t* packed, con
   });
 }
 
+nb_status nb_debug_expire_waits(nb_model* model, uint32_t count) {
+  if (!model) return NB_ERR_ARGUMENT;
+  return guard([&] {
+    Engine& E = *model->engine;
+    std::lock_guard<std::mutex> lock(E.mutex);
+    NB_CUDA(cudaSetDevice(E.device));
+    NB_CUDA(nbk::set_expire_route((int)count, E.stream));
+    NB_CUDA(cudaStreamSynchronize(E.stream));
+  });
+}
+
 nb_status nb_debug_read_bandwidth(int device, size_t bytes, uint32_t passes, uint32_t reps, float* ms_per_read) {
   if (!ms_per_read || bytes < 16 || bytes % 16 != 0 || reps == 0 || passes == 0 || passes > 4096) return NB_ERR_ARGUMENT;
   return guard([&] {

@@ -32,6 +32,7 @@ def _declare() -> None:
         "nb_debug_step_kernels": [P, ctypes.POINTER(ctypes.c_uint32)],
         "nb_debug_product": [I, U32, P, P, P, U32, U32, P, U32, P, U32, ctypes.POINTER(ctypes.c_float)],
         "nb_debug_read_bandwidth": [I, SZ, U32, U32, ctypes.POINTER(ctypes.c_float)],
+        "nb_debug_expire_waits": [P, U32],
     }.items():
         fn = getattr(L, name)
         fn.restype = I
@@ -134,3 +135,9 @@ def read_bandwidth(nbytes: int, passes: int = 1, reps: int = 20, device: int = 0
     ms = ctypes.c_float()
     _check(lib().nb_debug_read_bandwidth(device, nbytes, passes, reps, ctypes.byref(ms)))
     return nbytes / (ms.value / 1000.0) / 1e9
+
+
+def expire_waits(model: Model, count: int = 1) -> None:
+    """The next `count` routing CTAs give up a bounded wait (nb_debug_expire_waits)."""
+    _declare()
+    _check(lib().nb_debug_expire_waits(model._h, count))
