@@ -285,6 +285,7 @@ __global__ void __launch_bounds__(256) k_route(ModelDev md, LayerDev L, Work w, 
         bulk_start(bar, 16);  // 16 bytes announced, no copy issued: the wait cannot complete
         if (!mbar_wait_polls(bar, 0, EXPIRE_POLLS)) atomicExch(error, 1);
       }
+      pdl_wait();  // every kernel of a pass waits for its predecessor before it exits
       return;
     }
   }
