@@ -714,6 +714,229 @@ __global__ void __launch_bounds__(GEMM_THREADS_PER_TOKEN * NT) k_gemm(QMat W, co
   if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(COLS) : "memory");
 }
 
+// ------------------------------------------- tensor-core product, large passes
+// For passes of at least WIDE_MIN_TOKENS tokens through a K = 512 matrix: a
+// persistent CTA per SM keeps one 128-row weight tile resident in shared
+// memory and walks 64-token tiles (CTA (r, p) takes token tiles p, p + P, ...
+// of row tile r), warp-specialised:
+//   warp 0 (one lane)   streams the token tiles through a WIDE_STAGES-deep
+//                       ring of 32 KB stages (bulk copies onto mbarriers)
+//   warp 1 (one lane)   issues each tile's 16 tcgen05.mma kind::i8 (four
+//                       K = 32 steps per 128-column group) into one of two
+//                       TMEM accumulator sets [4 groups][64 tokens], then
+//                       commits the stage back to warp 0 and the set to the
+//                       epilogue
+//   warps 4..19         drain a set while the MMAs fill the other: warp w
+//                       reads TMEM lane quadrant w % 4 (thread = weight row)
+//                       for tokens 16·((w - 4) / 4) .. +15 and combines the
+//                       groups in order exactly as k_gemm does (fma for 2-bit
+//                       panels, the product chain for 4-bit rows)
+// so the tensor cores of a tile overlap the combine and stores of the one
+// before. Every wait is bounded; a wait that gives up sets the error flag, the
+// other roles stop at their next wait, and warp 0 waits (bounded) for the
+// copies it issued before the CTA frees its TMEM and exits.
+constexpr int WIDE_NT = 64;
+constexpr int WIDE_STAGES = 3;
+constexpr int WIDE_MIN_TOKENS = 256;
+constexpr int WIDE_EPI_WARPS = 16;
+constexpr int WIDE_THREADS = (4 + WIDE_EPI_WARPS) * 32;
+constexpr uint32_t WIDE_A_BYTES = GEMM_ROWS * GEMM_K, WIDE_B_BYTES = WIDE_NT * GEMM_K;
+constexpr uint32_t WIDE_S_BYTES = WIDE_NT * (GEMM_K / GROUP) * 4;  // a token tile's act scales
+constexpr size_t wide_smem() { return (size_t)WIDE_A_BYTES + (size_t)WIDE_STAGES * (WIDE_B_BYTES + WIDE_S_BYTES); }
+
+__global__ void __launch_bounds__(WIDE_THREADS, 1) k_gemm_wide(QMat W, const int8_t* __restrict__ act, const float* __restrict__ act_scale,
+                                                              float* __restrict__ out, int M, int out_stride,
+                                                              const TokenMeta* __restrict__ meta, int* __restrict__ error) {
+  constexpr int GK = GEMM_K / GROUP;        // 4 groups
+  constexpr uint32_t SET = GK * WIDE_NT;    // TMEM columns of one accumulator set
+  constexpr uint32_t COLS = 2 * SET;        // 512
+  constexpr uint32_t IDESC = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(WIDE_NT >> 3) << 17) | ((uint32_t)(GEMM_ROWS >> 4) << 24);
+  constexpr uint32_t PIECE = 16384;
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + WIDE_A_BYTES;
+  float* sS = reinterpret_cast<float*>(sB + (size_t)WIDE_STAGES * WIDE_B_BYTES);  // [stage][64 tokens][4 groups]
+  __shared__ __align__(8) uint64_t bars[1 + 2 * WIDE_STAGES + 4];
+  __shared__ uint32_t s_tmem;
+  __shared__ volatile int s_fail;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int tile = blockIdx.x, P = gridDim.y, p = blockIdx.y;
+  const int token_tiles = (M + WIDE_NT - 1) / WIDE_NT;
+  const int my_tiles = p < token_tiles ? (token_tiles - p + P - 1) / P : 0;
+  const uint32_t bar_a = smem_u32(&bars[0]);
+  auto full = [&](int s) { return smem_u32(&bars[1 + s]); };
+  auto empty = [&](int s) { return smem_u32(&bars[1 + WIDE_STAGES + s]); };
+  auto tfull = [&](int b) { return smem_u32(&bars[1 + 2 * WIDE_STAGES + b]); };
+  auto tempty = [&](int b) { return smem_u32(&bars[3 + 2 * WIDE_STAGES + b]); };
+  auto copy = [&](uint8_t* dst, const uint8_t* src, uint32_t bytes, uint32_t bar) {
+    for (uint32_t off = 0; off < bytes; off += PIECE)
+      asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(dst + off)),
+                   "l"(src + off), "r"(min(PIECE, bytes - off)), "r"(bar)
+                   : "memory");
+  };
+  auto expect = [&](uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+  };
+
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s_tmem)), "r"(COLS) : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  if (tid == 0) {
+    s_fail = 0;
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar_a), "r"(1) : "memory");
+    for (int s = 0; s < WIDE_STAGES; ++s) {
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(full(s)), "r"(1) : "memory");
+      // a stage is free once its MMAs have completed (one commit) and every epilogue warp has read its scales
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(empty(s)), "r"(1 + WIDE_EPI_WARPS) : "memory");
+    }
+    for (int b = 0; b < 2; ++b) {
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(tfull(b)), "r"(1) : "memory");
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(tempty(b)), "r"(WIDE_EPI_WARPS) : "memory");
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    // the weight tile is constant: its copy starts before the previous kernel has finished
+    if (my_tiles > 0) {
+      expect(bar_a, WIDE_A_BYTES);
+      copy(sA, reinterpret_cast<const uint8_t*>(W.codes) + (size_t)tile * WIDE_A_BYTES, WIDE_A_BYTES, bar_a);
+    }
+  }
+  // an epilogue thread's weight row and its per-group scales (constant)
+  const int ew = warp - 4, quad = warp & 3, half = ew >> 2;
+  const int row = tile * GEMM_ROWS + quad * 32 + lane;
+  const bool valid = ew >= 0 && row < (int)W.rows;
+  float ws[GK];
+#pragma unroll
+  for (int g = 0; g < GK; ++g) ws[g] = valid ? W.scales[(size_t)row * GK + g] : 0.0f;
+  pdl_wait();
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();  // barriers initialised, TMEM allocated
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = s_tmem;
+  int issued = 0;    // token tiles whose copies warp 0 has issued
+  int committed = 0;  // token tiles whose MMAs warp 1 has issued
+
+  if (warp == 0 && lane == 0) {
+    for (int i = 0; i < my_tiles && !s_fail; ++i) {
+      const int s = i % WIDE_STAGES;
+      if (i >= WIDE_STAGES && !mbar_wait(empty(s), ((i / WIDE_STAGES) - 1) & 1)) {
+        s_fail = 1;
+        break;
+      }
+      const int m0 = (p + i * P) * WIDE_NT;
+      // the token tile and its act scales (only the pass's tokens: the scale rows end at M)
+      const uint32_t sbytes = (uint32_t)min(WIDE_NT, M - m0) * GK * 4;
+      expect(full(s), WIDE_B_BYTES + sbytes);
+      copy(sB + (size_t)s * WIDE_B_BYTES, reinterpret_cast<const uint8_t*>(act) + (size_t)(m0 / 8) * (8 * GEMM_K), WIDE_B_BYTES, full(s));
+      copy(reinterpret_cast<uint8_t*>(sS + (size_t)s * WIDE_NT * GK), reinterpret_cast<const uint8_t*>(act_scale + (size_t)m0 * GK), sbytes,
+           full(s));
+      ++issued;
+    }
+  } else if (warp == 1 && lane == 0) {
+    if (my_tiles > 0 && !mbar_wait(bar_a, 0)) s_fail = 1;
+    for (int i = 0; i < my_tiles && !s_fail; ++i) {
+      const int s = i % WIDE_STAGES, b = i & 1;
+      if (!mbar_wait(full(s), (i / WIDE_STAGES) & 1) || (i >= 2 && !mbar_wait(tempty(b), ((i >> 1) - 1) & 1))) {
+        s_fail = 1;
+        break;
+      }
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      const uint32_t a0 = smem_u32(sA), b0 = smem_u32(sB + (size_t)s * WIDE_B_BYTES);
+#pragma unroll
+      for (int g = 0; g < GK; ++g)
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const int step = g * 4 + k;  // K bytes 32·step .. 32·step+31
+          const uint64_t da = umma_desc(a0 + step * 256, 128, GEMM_KC * 128);
+          const uint64_t db = umma_desc(b0 + step * 256, 128, GEMM_KC * 128);
+          const uint32_t d_tmem = tmem + b * SET + g * WIDE_NT, accumulate = k > 0 ? 1u : 0u;
+          asm volatile(
+              "{\n\t.reg .pred p;\n\t"
+              "setp.ne.b32 p, %4, 0;\n\t"
+              "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}" ::"r"(d_tmem),
+              "l"(da), "l"(db), "r"(IDESC), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
+              : "memory");
+        }
+      asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(empty(s)) : "memory");
+      asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(tfull(b)) : "memory");
+      ++committed;
+    }
+  } else if (ew >= 0) {
+    const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16);
+    const int c0 = half * 16;
+    for (int i = 0; i < my_tiles; ++i) {
+      const int b = i & 1;
+      const float* tscale = sS + (size_t)(i % WIDE_STAGES) * WIDE_NT * GK;  // filled before the MMAs of this tile started
+      bool ok = !s_fail;
+      if (ok && lane == 0) ok = mbar_wait(tfull(b), (i >> 1) & 1);
+      ok = __shfl_sync(FULL, ok ? 1 : 0, 0) != 0;
+      if (!ok) {
+        s_fail = 1;
+        break;
+      }
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      const int m0 = (p + i * P) * WIDE_NT;
+      float total[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) total[j] = 0.0f;
+#pragma unroll
+      for (int g = 0; g < GK; ++g) {
+        uint32_t a[2][8];
+#pragma unroll
+        for (int q = 0; q < 2; ++q)
+          asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+                       : "=r"(a[q][0]), "=r"(a[q][1]), "=r"(a[q][2]), "=r"(a[q][3]), "=r"(a[q][4]), "=r"(a[q][5]), "=r"(a[q][6]),
+                         "=r"(a[q][7])
+                       : "r"(lane_base + b * SET + g * WIDE_NT + c0 + q * 8));
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+        for (int q = 0; q < 2; ++q)
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const int m = m0 + c0 + q * 8 + j;
+            const float accv = (float)(int)a[q][j];
+            const float as = m < M ? tscale[(c0 + q * 8 + j) * GK + g] : 0.0f;
+            float& t = total[q * 8 + j];
+            t = W.fused ? __fmaf_rn(accv, fmul(ws[g], as), t) : fadd(t, fmul(fmul(fmul(accv, ws[g]), W.level_scale), as));
+          }
+      }
+      // this set's accumulators are read (the MMAs of tile i + 2 may overwrite
+      // it) and so are the stage's scales (the copy of tile i + WIDE_STAGES may refill it)
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) {
+        asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(tempty(b)) : "memory");
+        asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(empty(i % WIDE_STAGES)) : "memory");
+      }
+      if (valid) {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const int m = m0 + c0 + j;
+          if (m < M && !(meta && __ldcg(&meta[m].slot) < 0)) out[(size_t)m * out_stride + row] = total[j];
+        }
+      }
+    }
+  }
+  pdl_trigger();
+  // nothing asynchronous outlives the CTA: warp 0 waits (bounded) for every
+  // copy it issued, warp 1 for every MMA it issued (the epilogue has already
+  // seen them complete unless a wait gave up)
+  if (warp == 0 && lane == 0) {
+    for (int i = max(0, issued - WIDE_STAGES); i < issued; ++i) mbar_wait(full(i % WIDE_STAGES), (i / WIDE_STAGES) & 1);
+    if (my_tiles > 0) mbar_wait(bar_a, 0);
+  } else if (warp == 1 && lane == 0) {
+    for (int i = max(0, committed - 2); i < committed; ++i) mbar_wait(tfull(i & 1), (i >> 1) & 1);
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (s_fail && tid == 0) atomicExch(error, 1);
+  if (warp == 0) {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(COLS) : "memory");
+  }
+}
+
 // -------------------------------------------------------------------- gemv
 // The same product for a few tokens (decode at small batch) as a memory-bound
 // int8 GEMV on the CUDA cores. A warp owns one 8-row block of the
@@ -2539,6 +2762,7 @@ cudaError_t configure(const ModelDev& md, int t_cap) {
   if ((e = cudaFuncSetAttribute(k_gemm<32, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gemm_smem<32>()))) return e;
   if ((e = cudaFuncSetAttribute(k_gemm<16, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gemm_smem<16>()))) return e;
   if ((e = cudaFuncSetAttribute(k_gemm<32, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gemm_smem<32>()))) return e;
+  if ((e = cudaFuncSetAttribute(k_gemm_wide, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)wide_smem()))) return e;
 
   return cudaSuccess;
 }
@@ -2611,6 +2835,17 @@ static void project(const QMat& W, const int8_t* act, const float* act_scale, fl
       launch(k_gemv<4>, ctas, GEMV_WARPS * 32, 0, st, W, act, act_scale, out, M, out_stride, meta, act_rows);
     else
       launch(k_gemv<1>, ctas, GEMV_WARPS * 32, 0, st, W, act, act_scale, out, M, out_stride, meta, act_rows);
+  } else if (!wide && M >= WIDE_MIN_TOKENS) {
+    // persistent CTAs, one per SM: P of them share each row tile's token tiles
+    static const int sms = [] {
+      int device = 0, n = 0;
+      cudaGetDevice(&device);
+      cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device);
+      return n > 0 ? n : 148;
+    }();
+    const int token_tiles = (M + WIDE_NT - 1) / WIDE_NT;
+    const int P = std::max(1, std::min(token_tiles, sms / tiles));
+    launch(k_gemm_wide, dim3(tiles, P), WIDE_THREADS, wide_smem(), st, W, act, act_scale, out, M, out_stride, meta, error);
   } else if (M <= 16) {
     auto k = wide ? k_gemm<16, 4> : k_gemm<16, 1>;
     launch(k, dim3(tiles, 1), GEMM_THREADS_PER_TOKEN * 16, gemm_smem<16>(), st, W, act, act_scale, out, M, out_stride, meta, error, act_rows);
@@ -2884,6 +3119,7 @@ cudaError_t launch_product_bench(const QMat& W, const float* in, int M, int8_t* 
   if ((e = cudaFuncSetAttribute(k_gemm<32, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gemm_smem<32>()))) return e;
   if ((e = cudaFuncSetAttribute(k_gemm<16, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gemm_smem<16>()))) return e;
   if ((e = cudaFuncSetAttribute(k_gemm<32, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gemm_smem<32>()))) return e;
+  if ((e = cudaFuncSetAttribute(k_gemm_wide, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)wide_smem()))) return e;
   t_pass_tokens = M;
   const int K = (int)W.cols;
   k_prep<<<M, 128, 0, st>>>(in, K, nullptr, nullptr, 0, K, act, act_scale, M, nullptr, 1.0f / std::sqrt((float)GROUP), 0, act_rows);

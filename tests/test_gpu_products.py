@@ -37,3 +37,22 @@ def test_product_timing_is_reported(native_built):
     x = np.random.default_rng(0).standard_normal((64, 512)).astype(np.float32)
     _, ms = debug.product(2, packed, levels, norms, 2048, 512, x, reps=5)
     assert 0.0 < ms < 50.0
+
+
+@pytest.mark.parametrize("cols,rows,bits", [(512, 2048, 2), (512, 8192, 4), (512, 512, 2)])
+@pytest.mark.parametrize("tokens", [256, 300, 1000])
+def test_large_pass_product_every_token(native_built, oracle_lib, cols, rows, bits, tokens):
+    """Passes of at least 256 tokens through a K = 512 matrix run the
+    persistent, pipelined tensor-core product (64-token tiles, two TMEM
+    accumulator sets): every token's row of outputs, a ragged last tile and
+    CTAs that walk several tiles included, bit-exact against the restatement."""
+    from rustyneedle_b200 import debug, synthetic
+
+    packed, levels, norms = synthetic.product_matrix(seed=3 * cols + rows + bits, rows=rows, columns=cols, bits=bits)
+    rng = np.random.default_rng(tokens + rows)
+    x = (rng.standard_normal((tokens, cols)) * rng.uniform(0.01, 3.0, (tokens, 1))).astype(np.float32)
+    x[tokens // 3] = 0.0
+    got, _ = debug.product(bits, packed, levels, norms, rows, cols, x)
+    for t in range(tokens):
+        want = oracle_lib.product_raw(oracle_lib.MODE_INT, bits, packed, levels, norms, rows, cols, x[t])
+        assert np.array_equal(got[t].view(np.uint32), want.view(np.uint32)), (t, np.flatnonzero(got[t] != want)[:5])
