@@ -60,6 +60,8 @@ def parse():
     p.add_argument("--warmup", type=int, default=4)
     p.add_argument("--impl", default="b200", choices=["b200", "reference"])
     p.add_argument("--seqs", type=int, default=SEQS_PER_GPU)
+    p.add_argument("--shard", type=int, default=None,
+                   help="one GPU decoding the sequences rank SHARD gets at N > 1 (its shard timed alone)")
     p.add_argument("--no-batch1", action="store_true")
     p.add_argument("--no-cpu", action="store_true")
     p.add_argument("--profile", action="store_true", help="64 sequences, no extras: the small case for ncu captures")
@@ -341,7 +343,8 @@ def main():
         return
     archive = synthetic.cached_archive(seed=0)
     seqs = 64 if args.profile else args.seqs
-    rank_prompts = prompts(rank, seqs)
+    shard = rank if args.shard is None or world > 1 else args.shard
+    rank_prompts = prompts(shard, seqs)
     # KV pool sized to the run: every sequence's prompt plus the decode steps, plus the batch-1 session
     pages = dp.kv_pages_for(rank_prompts, 2 * args.steps + 2 * args.warmup + 8, DEPTH)
     model = nb.Model.open(archive, device=local, max_sessions=seqs + 4, kv_pages=pages)
@@ -424,7 +427,8 @@ def main():
             "config": {"workload": "config2: depth-20 synthetic Needle-3 (seed 0), 256 sequences per GPU, prompts "
                                    "uniform in [128, 1024], greedy decode, paged int8 KV (64-token pages)",
                        "sequences_per_gpu": seqs, "depth": DEPTH, "parallelism": f"dp{world} (sequences sharded)",
-                       "l2": "inputs larger than L2 (KV cache ~2 GB per GPU)", "setup_s": round(setup_s, 1)},
+                       "l2": "inputs larger than L2 (KV cache ~2 GB per GPU)", "setup_s": round(setup_s, 1),
+                       **({"shard": shard} if shard != rank else {})},
             "e2e": e2e, "roofline": roofline, "step_roofline": step_roofline,
             "gpu_launches": debug.step_kernels(batch) * args.steps, "clocks": clocks.summary(), "per_rank": per_rank}
 

@@ -44,7 +44,8 @@ nb_status nb_debug_product(int device, uint32_t bits, const uint8_t* packed, con
 
 /* Failure detection test: the next `count` routing CTAs (k_route) on the
  * model's GPU each give up a short bounded wait on a barrier no copy will
- * complete, before issuing any copy, and set the engine's error flag; the next
+ * complete, set the engine's error flag and return once their own copies have
+ * landed (nothing asynchronous outlives them); the next
  * synchronising call that ran them returns NB_ERR_TIMEOUT, as for any device
  * wait that gave up. The session that ran them is left inconsistent; other
  * sessions and models are not affected. No reference counterpart. */

@@ -25,6 +25,15 @@ __device__ __forceinline__ float fdiv(float a, float b) { return __fdiv_rn(a, b)
 __device__ __forceinline__ float frcp(float a) { return __frcp_rn(a); }
 __device__ __forceinline__ float fsqrt(float a) { return __fsqrt_rn(a); }
 
+// Exact int32 → f32 of a 128-column group sum of int8 × int8 products
+// (|x| ≤ 128·128·128 = 2^21 < 2^22), by the magic-number method: the bits
+// 0x4B400000 + x are the float 1.5·2^23 + x (unit spacing in [2^23, 2^24), the
+// exponent unchanged for |x| < 2^22), and subtracting 1.5·2^23 is exact. Two
+// full-rate instructions in place of a conversion-unit I2F.
+__device__ __forceinline__ float group_sum_to_float(uint32_t x) {
+  return fsub(__int_as_float((int)(0x4B400000u + x)), 12582912.0f);
+}
+
 // Programmatic dependent launch. Every kernel of the token loop is launched
 // with programmatic stream serialisation: it may start while its predecessor
 // on the stream still runs. pdl_wait() blocks until the predecessor grid has

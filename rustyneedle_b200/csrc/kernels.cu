@@ -22,6 +22,7 @@
 #include <cmath>
 #include <cstdlib>
 #include <mutex>
+#include <type_traits>
 #include <utility>
 
 #include "device.cuh"
@@ -239,12 +240,20 @@ __host__ __device__ inline size_t route_floats(int d) {
 
 // Failure detection test hook: while g_expire_route > 0, each k_route CTA
 // that takes one of its counts gives up a bounded wait on a barrier that no
-// copy will complete (short poll limit), records the engine's error flag and
-// returns — before it issues any copy, so nothing asynchronous outlives it.
-// The host then reports NB_ERR_TIMEOUT like any expired wait. Set only by
-// nb_debug_expire_waits; 0 otherwise.
+// copy will complete (short poll limit), records the engine's error flag,
+// waits for its own bulk copies (which do complete, so nothing asynchronous
+// outlives it) and returns without touching the token. The host then reports
+// NB_ERR_TIMEOUT like any expired wait. Set only by nb_debug_expire_waits; 0
+// otherwise.
 __device__ int g_expire_route = 0;
 constexpr uint32_t EXPIRE_POLLS = 1u << 12;
+
+__device__ __forceinline__ void expire_wait(int* error) {
+  __shared__ __align__(8) uint64_t s_never;
+  const uint32_t never = smem_u32(&s_never);
+  bulk_start(never, 16);  // 16 bytes announced, no copy issued: the wait cannot complete
+  if (!mbar_wait_polls(never, 0, EXPIRE_POLLS)) atomicExch(error, 1);
+}
 
 __device__ __forceinline__ bool take_expiry() {
   int v = *reinterpret_cast<volatile int*>(&g_expire_route);
@@ -276,23 +285,13 @@ __global__ void __launch_bounds__(256) k_route(ModelDev md, LayerDev L, Work w, 
   __shared__ __align__(8) uint64_t s_bar;
   const uint32_t bar = smem_u32(&s_bar);
 
-  {
-    __shared__ int s_expire;
-    if (tid == 0) s_expire = take_expiry();
-    __syncthreads();
-    if (s_expire) {
-      if (tid == 0) {
-        bulk_start(bar, 16);  // 16 bytes announced, no copy issued: the wait cannot complete
-        if (!mbar_wait_polls(bar, 0, EXPIRE_POLLS)) atomicExch(error, 1);
-      }
-      pdl_wait();  // every kernel of a pass waits for its predecessor before it exits
-      return;
-    }
-  }
   // the layer's constant weights first, then (once the previous kernel is
   // done) the token's stream. One thread arms the barrier and issues the bulk
   // copies: the pre, post and residual rows of this layer are contiguous in
-  // their matrices (rows 4l.., 4l.., 16l..), so seven copies in all.
+  // their matrices (rows 4l.., 4l.., 16l..), so seven copies in all. The test
+  // hook's count is read after the copies are issued, so its load overlaps
+  // them instead of delaying them.
+  __shared__ int s_expire;
   if (tid == 0) {
     bulk_start(bar, PHI_ROWS * n + (PHI_ROWS * ng + d) * 4);
     bulk_copy(s_phiw, md.phi_pre.codes + (size_t)layer * LANES * n, LANES * n, bar);
@@ -302,6 +301,7 @@ __global__ void __launch_bounds__(256) k_route(ModelDev md, LayerDev L, Work w, 
     bulk_copy(s_norms + LANES * ng, md.phi_post.scales + (size_t)layer * LANES * ng, LANES * ng * 4, bar);
     bulk_copy(s_norms + 2 * LANES * ng, md.phi_res.scales + (size_t)layer * LANES * LANES * ng, LANES * LANES * ng * 4, bar);
     bulk_copy(s_gain, L.norm_in, d * 4, bar);
+    s_expire = take_expiry();
   }
   // the routing parameters of this layer (constant): the pre/post gate
   // threads' scale and bias, and warp 7's residual-mixing ones
@@ -317,12 +317,22 @@ __global__ void __launch_bounds__(256) k_route(ModelDev md, LayerDev L, Work w, 
   }
   pdl_wait();
   if (t >= M || w.meta[t].slot < 0) {
-    if (tid == 0 && !mbar_wait(bar, 0)) atomicExch(error, 1);  // no copy outlives the CTA
+    if (tid == 0) {
+      if (s_expire) expire_wait(error);
+      if (!mbar_wait(bar, 0)) atomicExch(error, 1);  // no copy outlives the CTA
+    }
     return;
   }
   stage_async(s_stream, w.stream + (size_t)t * n, n);
   cp_async_wait_all();
   __syncthreads();
+  if (s_expire) {
+    if (tid == 0) {
+      expire_wait(error);
+      if (!mbar_wait(bar, 0)) atomicExch(error, 1);
+    }
+    return;
+  }
   // unit_rms over all lanes (ops.rs:60-66): the squares, placed chain-major
   // (value v joins chain v % 8 at place v / 8), and the peak |x|, which the
   // positive scale keeps: max |x·inv| = max|x| · inv
@@ -694,7 +704,7 @@ __global__ void __launch_bounds__(GEMM_THREADS_PER_TOKEN * NT) k_gemm(QMat W, co
         const int g = g0 + gi;
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-          const float acc = (float)(int)a[gi][j];
+          const float acc = group_sum_to_float(a[gi][j]);
           const float as = s_as[(c0 + j) * GK + g];
           total[j] =
               W.fused ? __fmaf_rn(acc, fmul(ws[g], as), total[j]) : fadd(total[j], fmul(fmul(fmul(acc, ws[g]), W.level_scale), as));
@@ -865,58 +875,75 @@ __global__ void __launch_bounds__(WIDE_THREADS, 1) k_gemm_wide(QMat W, const int
   } else if (ew >= 0) {
     const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16);
     const int c0 = half * 16;
-    for (int i = 0; i < my_tiles; ++i) {
-      const int b = i & 1;
-      const float* tscale = sS + (size_t)(i % WIDE_STAGES) * WIDE_NT * GK;  // filled before the MMAs of this tile started
-      bool ok = !s_fail;
-      if (ok && lane == 0) ok = mbar_wait(tfull(b), (i >> 1) & 1);
-      ok = __shfl_sync(FULL, ok ? 1 : 0, 0) != 0;
-      if (!ok) {
-        s_fail = 1;
-        break;
-      }
-      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-      const int m0 = (p + i * P) * WIDE_NT;
-      float total[16];
+    // the combine per tile, with the product form (fused panels or the 4-bit
+    // chain) fixed outside the loops
+    auto drain = [&](auto fused_tag) {
+      constexpr bool FUSED = decltype(fused_tag)::value;
+      const float level = W.level_scale;
+      for (int i = 0; i < my_tiles; ++i) {
+        const int b = i & 1;
+        bool ok = !s_fail;
+        if (ok && lane == 0) ok = mbar_wait(tfull(b), (i >> 1) & 1);
+        ok = __shfl_sync(FULL, ok ? 1 : 0, 0) != 0;
+        if (!ok) {
+          s_fail = 1;
+          break;
+        }
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const int m0 = (p + i * P) * WIDE_NT;
+        // which of this warp's 16 tokens are stored: bit j for token m0 + c0 + j
+        bool live = false;
+        if (lane < 16) {
+          const int m = m0 + c0 + lane;
+          live = m < M && !(meta && __ldcg(&meta[m].slot) < 0);
+        }
+        const uint32_t store = __ballot_sync(FULL, live);
+        // the tile's act scales, [token][group] (a token past M reads a stale
+        // stage entry; its output is not stored)
+        const float4* tscale = reinterpret_cast<const float4*>(sS + (size_t)(i % WIDE_STAGES) * WIDE_NT * GK) + c0;
+        float total[16];
 #pragma unroll
-      for (int j = 0; j < 16; ++j) total[j] = 0.0f;
+        for (int q = 0; q < 2; ++q) {
+          uint32_t a[GK][8];
 #pragma unroll
-      for (int g = 0; g < GK; ++g) {
-        uint32_t a[2][8];
-#pragma unroll
-        for (int q = 0; q < 2; ++q)
-          asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
-                       : "=r"(a[q][0]), "=r"(a[q][1]), "=r"(a[q][2]), "=r"(a[q][3]), "=r"(a[q][4]), "=r"(a[q][5]), "=r"(a[q][6]),
-                         "=r"(a[q][7])
-                       : "r"(lane_base + b * SET + g * WIDE_NT + c0 + q * 8));
-        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-        for (int q = 0; q < 2; ++q)
+          for (int g = 0; g < GK; ++g)
+            asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+                         : "=r"(a[g][0]), "=r"(a[g][1]), "=r"(a[g][2]), "=r"(a[g][3]), "=r"(a[g][4]), "=r"(a[g][5]), "=r"(a[g][6]),
+                           "=r"(a[g][7])
+                         : "r"(lane_base + b * SET + g * WIDE_NT + c0 + q * 8));
+          asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
-            const int m = m0 + c0 + q * 8 + j;
-            const float accv = (float)(int)a[q][j];
-            const float as = m < M ? tscale[(c0 + q * 8 + j) * GK + g] : 0.0f;
-            float& t = total[q * 8 + j];
-            t = W.fused ? __fmaf_rn(accv, fmul(ws[g], as), t) : fadd(t, fmul(fmul(fmul(accv, ws[g]), W.level_scale), as));
-          }
-      }
-      // this set's accumulators are read (the MMAs of tile i + 2 may overwrite
-      // it) and so are the stage's scales (the copy of tile i + WIDE_STAGES may refill it)
-      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-      __syncwarp();
-      if (lane == 0) {
-        asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(tempty(b)) : "memory");
-        asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(empty(i % WIDE_STAGES)) : "memory");
-      }
-      if (valid) {
+            const float4 s4 = tscale[q * 8 + j];
+            const float as[GK] = {s4.x, s4.y, s4.z, s4.w};
+            float t = 0.0f;
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const int m = m0 + c0 + j;
-          if (m < M && !(meta && __ldcg(&meta[m].slot) < 0)) out[(size_t)m * out_stride + row] = total[j];
+            for (int g = 0; g < GK; ++g) {
+              const float accv = group_sum_to_float(a[g][j]);
+              t = FUSED ? __fmaf_rn(accv, fmul(ws[g], as[g]), t) : fadd(t, fmul(fmul(fmul(accv, ws[g]), level), as[g]));
+            }
+            total[q * 8 + j] = t;
+          }
+        }
+        // this set's accumulators are read (the MMAs of tile i + 2 may overwrite
+        // it) and so are the stage's scales (the copy of tile i + WIDE_STAGES may refill it)
+        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+        __syncwarp();
+        if (lane == 0) {
+          asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(tempty(b)) : "memory");
+          asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(empty(i % WIDE_STAGES)) : "memory");
+        }
+        if (valid) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j)
+            if ((store >> j) & 1) out[(size_t)(m0 + c0 + j) * out_stride + row] = total[j];
         }
       }
-    }
+    };
+    if (W.fused)
+      drain(std::true_type{});
+    else
+      drain(std::false_type{});
   }
   pdl_trigger();
   // nothing asynchronous outlives the CTA: warp 0 waits (bounded) for every
@@ -1010,7 +1037,7 @@ __global__ void __launch_bounds__(GEMV_WARPS * 32) k_gemv(QMat W, const int8_t* 
         float total = KCH > 1 && c > 0 ? s_tot[KCH > 1 ? t : 0][warp * 8 + lane] : 0.0f;
 #pragma unroll
         for (int g = 0; g < GC; ++g) {
-          const float a = (float)acc[g], as = s_as[t][c * GC + g], w = ws[c * GC + g];
+          const float a = group_sum_to_float((uint32_t)acc[g]), as = s_as[t][c * GC + g], w = ws[c * GC + g];
           total = W.fused ? __fmaf_rn(a, fmul(w, as), total) : fadd(total, fmul(fmul(fmul(a, w), W.level_scale), as));
         }
         if (c + 1 < KCH)
@@ -2822,9 +2849,10 @@ static void launch(void (*kernel)(P...), dim3 grid, dim3 block, size_t smem, cud
 }
 
 // One codebook product of M tokens through W (K = W.cols: 512, or 2048 in the
-// product benchmark): the CUDA-core GEMV for a few tokens, else tcgen05 tiles
-// of 16 or 32 tokens. act_rows is the row capacity of the activation buffer
-// (it places the chunks of K > 512).
+// product benchmark): the CUDA-core GEMV for a few tokens, the pipelined
+// persistent tcgen05 kernel for passes of at least WIDE_MIN_TOKENS tokens at
+// K = 512, else tcgen05 tiles of 16 or 32 tokens. act_rows is the row
+// capacity of the activation buffer (it places the chunks of K > 512).
 static void project(const QMat& W, const int8_t* act, const float* act_scale, float* out, int M, int out_stride,
                     const TokenMeta* meta, cudaStream_t st, int* error, int act_rows = 0) {
   const int tiles = (W.rows + GEMM_ROWS - 1) / GEMM_ROWS;

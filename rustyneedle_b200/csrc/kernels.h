@@ -68,7 +68,8 @@ cudaError_t launch_product_bench(const nbl::QMat& W, const float* in, int M, int
                                  int* error, int reps, float* ms, cudaStream_t st);
 
 // Failure detection test hook: the next `count` k_route CTAs each give up a
-// short bounded wait before issuing any copy and set the engine's error flag.
+// short bounded wait on a barrier no copy completes, set the engine's error
+// flag, wait for their own copies and return.
 cudaError_t set_expire_route(int count, cudaStream_t st);
 
 // A streaming read of `bytes` (a multiple of 16) from `data` through L2,

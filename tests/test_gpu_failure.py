@@ -2,8 +2,8 @@
 runs out is reported as NB_ERR_TIMEOUT and leaves the device usable.
 
 nb_debug_expire_waits makes the next routing CTAs give up a short bounded
-wait on a barrier that no copy will complete, before they issue any copy (so
-nothing asynchronous outlives them), exactly the path an expired wait of the
+wait on a barrier that no copy will complete and wait for their own bulk
+copies before they leave (so nothing asynchronous outlives them), exactly the path an expired wait of the
 token loop takes: the engine's error flag is set, and the next synchronising
 call reports the status. Afterwards a fresh session on the same model, and a
 fresh model on the same device, decode bit-identically to the CPU
