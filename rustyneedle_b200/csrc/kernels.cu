@@ -727,46 +727,53 @@ __global__ void __launch_bounds__(GEMM_THREADS_PER_TOKEN * NT) k_gemm(QMat W, co
 // ------------------------------------------- tensor-core product, large passes
 // For passes of at least WIDE_MIN_TOKENS tokens through a K = 512 matrix: a
 // persistent CTA per SM keeps one 128-row weight tile resident in shared
-// memory and walks 64-token tiles (CTA (r, p) takes token tiles p, p + P, ...
+// memory and walks 128-token tiles (CTA (r, p) takes token tiles p, p + P, ...
 // of row tile r), warp-specialised:
-//   warp 0 (one lane)   streams the token tiles through a WIDE_STAGES-deep
-//                       ring of 32 KB stages (bulk copies onto mbarriers)
-//   warp 1 (one lane)   issues each tile's 16 tcgen05.mma kind::i8 (four
-//                       K = 32 steps per 128-column group) into one of two
-//                       TMEM accumulator sets [4 groups][64 tokens], then
-//                       commits the stage back to warp 0 and the set to the
-//                       epilogue
-//   warps 4..19         drain a set while the MMAs fill the other: warp w
-//                       reads TMEM lane quadrant w % 4 (thread = weight row)
-//                       for tokens 16·((w - 4) / 4) .. +15 and combines the
-//                       groups in order exactly as k_gemm does (fma for 2-bit
-//                       panels, the product chain for 4-bit rows)
-// so the tensor cores of a tile overlap the combine and stores of the one
-// before. Every wait is bounded; a wait that gives up sets the error flag, the
-// other roles stop at their next wait, and warp 0 waits (bounded) for the
-// copies it issued before the CTA frees its TMEM and exits.
-constexpr int WIDE_NT = 64;
-constexpr int WIDE_STAGES = 3;
+//   warp 0 (one lane)   streams each tile's token codes through a 2-stage ring
+//                       (64 KB stages, freed when the tile's MMAs complete) and
+//                       its act scales through a 4-stage ring (freed by the
+//                       epilogue), bulk copies onto mbarriers
+//   warp 1 (one lane)   issues the tile's tcgen05.mma kind::i8 (M = 128,
+//                       N = 128: twice the work of N = 64 for a little more
+//                       time per instruction) in two halves, groups 0-1 into
+//                       TMEM columns 0..255 and groups 2-3 into 256..511,
+//                       committing each half to the epilogue
+//   warps 4..19         thread = weight row (warp w reads TMEM lane quadrant
+//                       w % 4) for tokens 32·((w - 4) / 4) .. +31: drain the
+//                       first half into running totals (groups 0, 1 in order),
+//                       hand its columns back, then the second (groups 2, 3),
+//                       exactly k_gemm's combine
+// so the MMAs of one half overlap the combine of the other, and the next
+// tile's first half starts while the epilogue drains this tile's second.
+// Every wait is bounded; a wait that gives up sets the error flag, the other
+// roles stop at their next wait, and the copy and MMA threads wait (bounded)
+// for what they issued before the CTA frees its TMEM and exits.
+constexpr int WIDE_NT = 128;
+constexpr int WIDE_CODE_STAGES = 2;
+constexpr int WIDE_SCALE_STAGES = 4;
 constexpr int WIDE_MIN_TOKENS = 256;
 constexpr int WIDE_EPI_WARPS = 16;
+constexpr int WIDE_EPI_TOKENS = WIDE_NT / (WIDE_EPI_WARPS / 4);  // 32 tokens per epilogue warp
 constexpr int WIDE_THREADS = (4 + WIDE_EPI_WARPS) * 32;
 constexpr uint32_t WIDE_A_BYTES = GEMM_ROWS * GEMM_K, WIDE_B_BYTES = WIDE_NT * GEMM_K;
 constexpr uint32_t WIDE_S_BYTES = WIDE_NT * (GEMM_K / GROUP) * 4;  // a token tile's act scales
-constexpr size_t wide_smem() { return (size_t)WIDE_A_BYTES + (size_t)WIDE_STAGES * (WIDE_B_BYTES + WIDE_S_BYTES); }
+constexpr size_t wide_smem() {
+  return (size_t)WIDE_A_BYTES + (size_t)WIDE_CODE_STAGES * WIDE_B_BYTES + (size_t)WIDE_SCALE_STAGES * WIDE_S_BYTES;
+}
 
 __global__ void __launch_bounds__(WIDE_THREADS, 1) k_gemm_wide(QMat W, const int8_t* __restrict__ act, const float* __restrict__ act_scale,
                                                               float* __restrict__ out, int M, int out_stride,
                                                               const TokenMeta* __restrict__ meta, int* __restrict__ error) {
-  constexpr int GK = GEMM_K / GROUP;        // 4 groups
-  constexpr uint32_t SET = GK * WIDE_NT;    // TMEM columns of one accumulator set
-  constexpr uint32_t COLS = 2 * SET;        // 512
+  constexpr int GK = GEMM_K / GROUP;  // 4 groups: columns g·128 .. g·128+127 of TMEM
+  constexpr uint32_t COLS = GK * WIDE_NT;  // 512
   constexpr uint32_t IDESC = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(WIDE_NT >> 3) << 17) | ((uint32_t)(GEMM_ROWS >> 4) << 24);
   constexpr uint32_t PIECE = 16384;
+  constexpr int CS = WIDE_CODE_STAGES, SS = WIDE_SCALE_STAGES;
   extern __shared__ __align__(128) uint8_t smem[];
   uint8_t* sA = smem;
   uint8_t* sB = smem + WIDE_A_BYTES;
-  float* sS = reinterpret_cast<float*>(sB + (size_t)WIDE_STAGES * WIDE_B_BYTES);  // [stage][64 tokens][4 groups]
-  __shared__ __align__(8) uint64_t bars[1 + 2 * WIDE_STAGES + 4];
+  float* sS = reinterpret_cast<float*>(sB + (size_t)CS * WIDE_B_BYTES);  // [stage][128 tokens][4 groups]
+  __shared__ __align__(8) uint64_t bars[1 + 2 * CS + 2 * SS + 4];
   __shared__ uint32_t s_tmem;
   __shared__ volatile int s_fail;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -774,10 +781,12 @@ __global__ void __launch_bounds__(WIDE_THREADS, 1) k_gemm_wide(QMat W, const int
   const int token_tiles = (M + WIDE_NT - 1) / WIDE_NT;
   const int my_tiles = p < token_tiles ? (token_tiles - p + P - 1) / P : 0;
   const uint32_t bar_a = smem_u32(&bars[0]);
-  auto full = [&](int s) { return smem_u32(&bars[1 + s]); };
-  auto empty = [&](int s) { return smem_u32(&bars[1 + WIDE_STAGES + s]); };
-  auto tfull = [&](int b) { return smem_u32(&bars[1 + 2 * WIDE_STAGES + b]); };
-  auto tempty = [&](int b) { return smem_u32(&bars[3 + 2 * WIDE_STAGES + b]); };
+  auto cfull = [&](int s) { return smem_u32(&bars[1 + s]); };
+  auto cempty = [&](int s) { return smem_u32(&bars[1 + CS + s]); };
+  auto sfull = [&](int s) { return smem_u32(&bars[1 + 2 * CS + s]); };
+  auto sempty = [&](int s) { return smem_u32(&bars[1 + 2 * CS + SS + s]); };
+  auto hfull = [&](int h) { return smem_u32(&bars[1 + 2 * CS + 2 * SS + h]); };
+  auto hempty = [&](int h) { return smem_u32(&bars[3 + 2 * CS + 2 * SS + h]); };
   auto copy = [&](uint8_t* dst, const uint8_t* src, uint32_t bytes, uint32_t bar) {
     for (uint32_t off = 0; off < bytes; off += PIECE)
       asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(dst + off)),
@@ -787,6 +796,9 @@ __global__ void __launch_bounds__(WIDE_THREADS, 1) k_gemm_wide(QMat W, const int
   auto expect = [&](uint32_t bar, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
   };
+  auto init = [&](uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+  };
 
   if (warp == 0) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s_tmem)), "r"(COLS) : "memory");
@@ -794,15 +806,18 @@ __global__ void __launch_bounds__(WIDE_THREADS, 1) k_gemm_wide(QMat W, const int
   }
   if (tid == 0) {
     s_fail = 0;
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar_a), "r"(1) : "memory");
-    for (int s = 0; s < WIDE_STAGES; ++s) {
-      asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(full(s)), "r"(1) : "memory");
-      // a stage is free once its MMAs have completed (one commit) and every epilogue warp has read its scales
-      asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(empty(s)), "r"(1 + WIDE_EPI_WARPS) : "memory");
+    init(bar_a, 1);
+    for (int s = 0; s < CS; ++s) {
+      init(cfull(s), 1);
+      init(cempty(s), 1);  // the tile's last commit
     }
-    for (int b = 0; b < 2; ++b) {
-      asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(tfull(b)), "r"(1) : "memory");
-      asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(tempty(b)), "r"(WIDE_EPI_WARPS) : "memory");
+    for (int s = 0; s < SS; ++s) {
+      init(sfull(s), 1);
+      init(sempty(s), WIDE_EPI_WARPS);  // every epilogue warp has combined the tile
+    }
+    for (int h = 0; h < 2; ++h) {
+      init(hfull(h), 1);
+      init(hempty(h), WIDE_EPI_WARPS);
     }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -813,7 +828,7 @@ __global__ void __launch_bounds__(WIDE_THREADS, 1) k_gemm_wide(QMat W, const int
     }
   }
   // an epilogue thread's weight row and its per-group scales (constant)
-  const int ew = warp - 4, quad = warp & 3, half = ew >> 2;
+  const int ew = warp - 4, quad = warp & 3;
   const int row = tile * GEMM_ROWS + quad * 32 + lane;
   const bool valid = ew >= 0 && row < (int)W.rows;
   float ws[GK];
@@ -824,118 +839,145 @@ __global__ void __launch_bounds__(WIDE_THREADS, 1) k_gemm_wide(QMat W, const int
   __syncthreads();  // barriers initialised, TMEM allocated
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem = s_tmem;
-  int issued = 0;    // token tiles whose copies warp 0 has issued
+  int issued = 0;     // token tiles whose copies warp 0 has issued
   int committed = 0;  // token tiles whose MMAs warp 1 has issued
 
   if (warp == 0 && lane == 0) {
     for (int i = 0; i < my_tiles && !s_fail; ++i) {
-      const int s = i % WIDE_STAGES;
-      if (i >= WIDE_STAGES && !mbar_wait(empty(s), ((i / WIDE_STAGES) - 1) & 1)) {
+      const int c = i % CS, sc = i % SS;
+      if ((i >= CS && !mbar_wait(cempty(c), ((i / CS) - 1) & 1)) || (i >= SS && !mbar_wait(sempty(sc), ((i / SS) - 1) & 1))) {
         s_fail = 1;
         break;
       }
       const int m0 = (p + i * P) * WIDE_NT;
-      // the token tile and its act scales (only the pass's tokens: the scale rows end at M)
+      // the token tile (the activation rows are allocated in whole 128-token
+      // tiles) and its act scales (only the pass's tokens: the scale rows end at M)
       const uint32_t sbytes = (uint32_t)min(WIDE_NT, M - m0) * GK * 4;
-      expect(full(s), WIDE_B_BYTES + sbytes);
-      copy(sB + (size_t)s * WIDE_B_BYTES, reinterpret_cast<const uint8_t*>(act) + (size_t)(m0 / 8) * (8 * GEMM_K), WIDE_B_BYTES, full(s));
-      copy(reinterpret_cast<uint8_t*>(sS + (size_t)s * WIDE_NT * GK), reinterpret_cast<const uint8_t*>(act_scale + (size_t)m0 * GK), sbytes,
-           full(s));
+      expect(cfull(c), WIDE_B_BYTES);
+      copy(sB + (size_t)c * WIDE_B_BYTES, reinterpret_cast<const uint8_t*>(act) + (size_t)(m0 / 8) * (8 * GEMM_K), WIDE_B_BYTES, cfull(c));
+      expect(sfull(sc), sbytes);
+      copy(reinterpret_cast<uint8_t*>(sS + (size_t)sc * WIDE_NT * GK), reinterpret_cast<const uint8_t*>(act_scale + (size_t)m0 * GK), sbytes,
+           sfull(sc));
       ++issued;
     }
   } else if (warp == 1 && lane == 0) {
     if (my_tiles > 0 && !mbar_wait(bar_a, 0)) s_fail = 1;
     for (int i = 0; i < my_tiles && !s_fail; ++i) {
-      const int s = i % WIDE_STAGES, b = i & 1;
-      if (!mbar_wait(full(s), (i / WIDE_STAGES) & 1) || (i >= 2 && !mbar_wait(tempty(b), ((i >> 1) - 1) & 1))) {
+      const int c = i % CS;
+      if (!mbar_wait(cfull(c), (i / CS) & 1)) {
         s_fail = 1;
         break;
       }
-      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-      const uint32_t a0 = smem_u32(sA), b0 = smem_u32(sB + (size_t)s * WIDE_B_BYTES);
+      const uint32_t a0 = smem_u32(sA), b0 = smem_u32(sB + (size_t)c * WIDE_B_BYTES);
+      bool ok = true;
+      int halves = 0;
 #pragma unroll
-      for (int g = 0; g < GK; ++g)
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const int step = g * 4 + k;  // K bytes 32·step .. 32·step+31
-          const uint64_t da = umma_desc(a0 + step * 256, 128, GEMM_KC * 128);
-          const uint64_t db = umma_desc(b0 + step * 256, 128, GEMM_KC * 128);
-          const uint32_t d_tmem = tmem + b * SET + g * WIDE_NT, accumulate = k > 0 ? 1u : 0u;
-          asm volatile(
-              "{\n\t.reg .pred p;\n\t"
-              "setp.ne.b32 p, %4, 0;\n\t"
-              "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}" ::"r"(d_tmem),
-              "l"(da), "l"(db), "r"(IDESC), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
-              : "memory");
+      for (int h = 0; h < 2; ++h) {
+        // the epilogue has drained this half of the previous tile
+        if (i >= 1 && !mbar_wait(hempty(h), (i - 1) & 1)) {
+          ok = false;
+          break;
         }
-      asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(empty(s)) : "memory");
-      asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(tfull(b)) : "memory");
-      ++committed;
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+#pragma unroll
+        for (int gi = 0; gi < 2; ++gi)
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const int g = 2 * h + gi, step = g * 4 + k;  // K bytes 32·step .. 32·step+31
+            const uint64_t da = umma_desc(a0 + step * 256, 128, GEMM_KC * 128);
+            const uint64_t db = umma_desc(b0 + step * 256, 128, GEMM_KC * 128);
+            const uint32_t d_tmem = tmem + g * WIDE_NT, accumulate = k > 0 ? 1u : 0u;
+            asm volatile(
+                "{\n\t.reg .pred p;\n\t"
+                "setp.ne.b32 p, %4, 0;\n\t"
+                "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}" ::"r"(d_tmem),
+                "l"(da), "l"(db), "r"(IDESC), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
+                : "memory");
+          }
+        asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(hfull(h)) : "memory");
+        ++halves;
+      }
+      if (halves > 0) {
+        // every MMA issued for the tile has read the code stage once this
+        // completes (also after a wait gave up: the exit waits for it)
+        asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(cempty(c)) : "memory");
+        ++committed;
+      }
+      if (!ok) {
+        s_fail = 1;
+        break;
+      }
     }
   } else if (ew >= 0) {
     const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16);
-    const int c0 = half * 16;
+    const int c0 = (ew >> 2) * WIDE_EPI_TOKENS;
     // the combine per tile, with the product form (fused panels or the 4-bit
     // chain) fixed outside the loops
     auto drain = [&](auto fused_tag) {
       constexpr bool FUSED = decltype(fused_tag)::value;
       const float level = W.level_scale;
       for (int i = 0; i < my_tiles; ++i) {
-        const int b = i & 1;
+        const int sc = i % SS;
         bool ok = !s_fail;
-        if (ok && lane == 0) ok = mbar_wait(tfull(b), (i >> 1) & 1);
+        if (ok && lane == 0) ok = mbar_wait(sfull(sc), (i / SS) & 1);
         ok = __shfl_sync(FULL, ok ? 1 : 0, 0) != 0;
         if (!ok) {
           s_fail = 1;
           break;
         }
-        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         const int m0 = (p + i * P) * WIDE_NT;
-        // which of this warp's 16 tokens are stored: bit j for token m0 + c0 + j
-        bool live = false;
-        if (lane < 16) {
-          const int m = m0 + c0 + lane;
-          live = m < M && !(meta && __ldcg(&meta[m].slot) < 0);
-        }
-        const uint32_t store = __ballot_sync(FULL, live);
+        // which of this warp's 32 tokens are stored: bit j for token m0 + c0 + j
+        const int m = m0 + c0 + lane;
+        const uint32_t store = __ballot_sync(FULL, m < M && !(meta && __ldcg(&meta[m].slot) < 0));
         // the tile's act scales, [token][group] (a token past M reads a stale
         // stage entry; its output is not stored)
-        const float4* tscale = reinterpret_cast<const float4*>(sS + (size_t)(i % WIDE_STAGES) * WIDE_NT * GK) + c0;
-        float total[16];
+        const float2* tscale = reinterpret_cast<const float2*>(sS + (size_t)sc * WIDE_NT * GK) + 2 * c0;
+        float total[WIDE_EPI_TOKENS];
 #pragma unroll
-        for (int q = 0; q < 2; ++q) {
-          uint32_t a[GK][8];
+        for (int h = 0; h < 2; ++h) {
+          if (ok && lane == 0) ok = mbar_wait(hfull(h), i & 1);
+          ok = __shfl_sync(FULL, ok ? 1 : 0, 0) != 0;
+          if (!ok) break;
+          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 #pragma unroll
-          for (int g = 0; g < GK; ++g)
-            asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
-                         : "=r"(a[g][0]), "=r"(a[g][1]), "=r"(a[g][2]), "=r"(a[g][3]), "=r"(a[g][4]), "=r"(a[g][5]), "=r"(a[g][6]),
-                           "=r"(a[g][7])
-                         : "r"(lane_base + b * SET + g * WIDE_NT + c0 + q * 8));
-          asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+          for (int q = 0; q < WIDE_EPI_TOKENS / 8; ++q) {
+            uint32_t a[2][8];
 #pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            const float4 s4 = tscale[q * 8 + j];
-            const float as[GK] = {s4.x, s4.y, s4.z, s4.w};
-            float t = 0.0f;
+            for (int gi = 0; gi < 2; ++gi)
+              asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+                           : "=r"(a[gi][0]), "=r"(a[gi][1]), "=r"(a[gi][2]), "=r"(a[gi][3]), "=r"(a[gi][4]), "=r"(a[gi][5]),
+                             "=r"(a[gi][6]), "=r"(a[gi][7])
+                           : "r"(lane_base + (2 * h + gi) * WIDE_NT + c0 + q * 8));
+            asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
-            for (int g = 0; g < GK; ++g) {
-              const float accv = group_sum_to_float(a[g][j]);
-              t = FUSED ? __fmaf_rn(accv, fmul(ws[g], as[g]), t) : fadd(t, fmul(fmul(fmul(accv, ws[g]), level), as[g]));
+            for (int j = 0; j < 8; ++j) {
+              const int n = q * 8 + j;
+              const float2 s2 = tscale[2 * n + h];  // groups 2h, 2h + 1 of token n
+              float t = h == 0 ? 0.0f : total[n];
+              const float as[2] = {s2.x, s2.y};
+#pragma unroll
+              for (int gi = 0; gi < 2; ++gi) {
+                const int g = 2 * h + gi;
+                const float accv = group_sum_to_float(a[gi][j]);
+                t = FUSED ? __fmaf_rn(accv, fmul(ws[g], as[gi]), t) : fadd(t, fmul(fmul(fmul(accv, ws[g]), level), as[gi]));
+              }
+              total[n] = t;
             }
-            total[q * 8 + j] = t;
           }
+          // this half's columns are read: the next tile's MMAs may overwrite them
+          asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+          __syncwarp();
+          if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(hempty(h)) : "memory");
         }
-        // this set's accumulators are read (the MMAs of tile i + 2 may overwrite
-        // it) and so are the stage's scales (the copy of tile i + WIDE_STAGES may refill it)
-        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-        __syncwarp();
-        if (lane == 0) {
-          asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(tempty(b)) : "memory");
-          asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(empty(i % WIDE_STAGES)) : "memory");
+        if (!ok) {
+          s_fail = 1;
+          break;
         }
+        // the stage's scales are read: the copy of tile i + WIDE_SCALE_STAGES may refill it
+        if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(sempty(sc)) : "memory");
         if (valid) {
 #pragma unroll
-          for (int j = 0; j < 16; ++j)
+          for (int j = 0; j < WIDE_EPI_TOKENS; ++j)
             if ((store >> j) & 1) out[(size_t)(m0 + c0 + j) * out_stride + row] = total[j];
         }
       }
@@ -950,10 +992,11 @@ __global__ void __launch_bounds__(WIDE_THREADS, 1) k_gemm_wide(QMat W, const int
   // copy it issued, warp 1 for every MMA it issued (the epilogue has already
   // seen them complete unless a wait gave up)
   if (warp == 0 && lane == 0) {
-    for (int i = max(0, issued - WIDE_STAGES); i < issued; ++i) mbar_wait(full(i % WIDE_STAGES), (i / WIDE_STAGES) & 1);
+    for (int i = max(0, issued - CS); i < issued; ++i) mbar_wait(cfull(i % CS), (i / CS) & 1);
+    for (int i = max(0, issued - SS); i < issued; ++i) mbar_wait(sfull(i % SS), (i / SS) & 1);
     if (my_tiles > 0) mbar_wait(bar_a, 0);
   } else if (warp == 1 && lane == 0) {
-    for (int i = max(0, committed - 2); i < committed; ++i) mbar_wait(tfull(i & 1), (i >> 1) & 1);
+    if (committed > 0) mbar_wait(cempty((committed - 1) % CS), ((committed - 1) / CS) & 1);
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
