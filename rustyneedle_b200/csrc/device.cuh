@@ -34,6 +34,29 @@ __device__ __forceinline__ float group_sum_to_float(uint32_t x) {
   return fsub(__int_as_float((int)(0x4B400000u + x)), 12582912.0f);
 }
 
+// Packed two-lane f32 arithmetic (PTX add/fma .rn.f32x2): each component
+// rounded to nearest exactly as the scalar .rn instruction.
+__device__ __forceinline__ float2 add2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return d;
+}
+
+// -0.0 in both lanes, read from memory so the compiler cannot see the value:
+// fma(a, b, -0.0) is a·b rounded once, exactly mul.rn, and a packed fma is
+// never merged with the packed add that follows it (a visible packed multiply
+// would be, into one fused multiply-add the reference never performs).
+__device__ float2 g_negzero = {-0.0f, -0.0f};
+
 // Programmatic dependent launch. Every kernel of the token loop is launched
 // with programmatic stream serialisation: it may start while its predecessor
 // on the stream still runs. pdl_wait() blocks until the predecessor grid has

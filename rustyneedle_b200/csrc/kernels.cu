@@ -17,10 +17,13 @@
 // then k_final (lane mean and final norm) and, per generated token, the tied
 // logits product and k_select (generator.rs:147-194).
 #include <cooperative_groups.h>
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 
 #include <cmath>
 #include <cstdlib>
+#include <cstring>
 #include <mutex>
 #include <type_traits>
 #include <utility>
@@ -738,13 +741,21 @@ __global__ void __launch_bounds__(GEMM_THREADS_PER_TOKEN * NT) k_gemm(QMat W, co
 //                       time per instruction) in two halves, groups 0-1 into
 //                       TMEM columns 0..255 and groups 2-3 into 256..511,
 //                       committing each half to the epilogue
+//   warp 2              transposes each tile's act scales to [group][token],
+//                       so a pair of tokens' scales of one group is one 8-byte
+//                       shared-memory load
 //   warps 4..19         thread = weight row (warp w reads TMEM lane quadrant
 //                       w % 4) for tokens 32·((w - 4) / 4) .. +31: drain the
 //                       first half into running totals (groups 0, 1 in order),
 //                       hand its columns back, then the second (groups 2, 3),
-//                       exactly k_gemm's combine
+//                       exactly k_gemm's combine, two tokens per packed f32x2
+//                       instruction; finished totals leave by TMA tensor stores
 // so the MMAs of one half overlap the combine of the other, and the next
 // tile's first half starts while the epilogue drains this tile's second.
+// The accumulators start from the bias 0x4B400000 (written into TMEM by the
+// epilogue when it hands columns back, and once before the first tile), so an
+// int32 group sum s arrives as the bits of the float 1.5·2^23 + s and its
+// exact f32 value is one subtraction (|s| ≤ 2^21; group_sum_to_float).
 // Every wait is bounded; a wait that gives up sets the error flag, the other
 // roles stop at their next wait, and the copy and MMA threads wait (bounded)
 // for what they issued before the CTA frees its TMEM and exits.
@@ -757,13 +768,17 @@ constexpr int WIDE_EPI_TOKENS = WIDE_NT / (WIDE_EPI_WARPS / 4);  // 32 tokens pe
 constexpr int WIDE_THREADS = (4 + WIDE_EPI_WARPS) * 32;
 constexpr uint32_t WIDE_A_BYTES = GEMM_ROWS * GEMM_K, WIDE_B_BYTES = WIDE_NT * GEMM_K;
 constexpr uint32_t WIDE_S_BYTES = WIDE_NT * (GEMM_K / GROUP) * 4;  // a token tile's act scales
+constexpr uint32_t WIDE_O_BYTES = 8 * 32 * 4;  // an epilogue warp's output staging: [8 tokens][32 rows] f32
+constexpr uint32_t WIDE_BIAS = 0x4B400000u;    // the float 1.5·2^23 as an int32
 constexpr size_t wide_smem() {
-  return (size_t)WIDE_A_BYTES + (size_t)WIDE_CODE_STAGES * WIDE_B_BYTES + (size_t)WIDE_SCALE_STAGES * WIDE_S_BYTES;
+  return (size_t)WIDE_A_BYTES + (size_t)WIDE_CODE_STAGES * WIDE_B_BYTES + 2 * (size_t)WIDE_SCALE_STAGES * WIDE_S_BYTES +
+         (size_t)WIDE_EPI_WARPS * WIDE_O_BYTES;
 }
 
 __global__ void __launch_bounds__(WIDE_THREADS, 1) k_gemm_wide(QMat W, const int8_t* __restrict__ act, const float* __restrict__ act_scale,
                                                               float* __restrict__ out, int M, int out_stride,
-                                                              const TokenMeta* __restrict__ meta, int* __restrict__ error) {
+                                                              const TokenMeta* __restrict__ meta, int* __restrict__ error,
+                                                              const __grid_constant__ CUtensorMap out_map, int tma_out) {
   constexpr int GK = GEMM_K / GROUP;  // 4 groups: columns g·128 .. g·128+127 of TMEM
   constexpr uint32_t COLS = GK * WIDE_NT;  // 512
   constexpr uint32_t IDESC = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(WIDE_NT >> 3) << 17) | ((uint32_t)(GEMM_ROWS >> 4) << 24);
@@ -772,8 +787,10 @@ __global__ void __launch_bounds__(WIDE_THREADS, 1) k_gemm_wide(QMat W, const int
   extern __shared__ __align__(128) uint8_t smem[];
   uint8_t* sA = smem;
   uint8_t* sB = smem + WIDE_A_BYTES;
-  float* sS = reinterpret_cast<float*>(sB + (size_t)CS * WIDE_B_BYTES);  // [stage][128 tokens][4 groups]
-  __shared__ __align__(8) uint64_t bars[1 + 2 * CS + 2 * SS + 4];
+  float* sS = reinterpret_cast<float*>(sB + (size_t)CS * WIDE_B_BYTES);  // [stage][128 tokens][4 groups], as copied
+  float* sT = sS + (size_t)SS * WIDE_NT * GK;                             // [stage][4 groups][128 tokens]
+  float* sO = sT + (size_t)SS * WIDE_NT * GK;                             // [epilogue warp][8 tokens][32 rows]
+  __shared__ __align__(8) uint64_t bars[1 + 2 * CS + 3 * SS + 4];
   __shared__ uint32_t s_tmem;
   __shared__ volatile int s_fail;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -785,8 +802,9 @@ __global__ void __launch_bounds__(WIDE_THREADS, 1) k_gemm_wide(QMat W, const int
   auto cempty = [&](int s) { return smem_u32(&bars[1 + CS + s]); };
   auto sfull = [&](int s) { return smem_u32(&bars[1 + 2 * CS + s]); };
   auto sempty = [&](int s) { return smem_u32(&bars[1 + 2 * CS + SS + s]); };
-  auto hfull = [&](int h) { return smem_u32(&bars[1 + 2 * CS + 2 * SS + h]); };
-  auto hempty = [&](int h) { return smem_u32(&bars[3 + 2 * CS + 2 * SS + h]); };
+  auto tfull = [&](int s) { return smem_u32(&bars[1 + 2 * CS + 2 * SS + s]); };
+  auto hfull = [&](int h) { return smem_u32(&bars[1 + 2 * CS + 3 * SS + h]); };
+  auto hempty = [&](int h) { return smem_u32(&bars[3 + 2 * CS + 3 * SS + h]); };
   auto copy = [&](uint8_t* dst, const uint8_t* src, uint32_t bytes, uint32_t bar) {
     for (uint32_t off = 0; off < bytes; off += PIECE)
       asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(dst + off)),
@@ -798,6 +816,11 @@ __global__ void __launch_bounds__(WIDE_THREADS, 1) k_gemm_wide(QMat W, const int
   };
   auto init = [&](uint32_t bar, uint32_t count) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+  };
+  auto arrive = [&](uint32_t bar) { asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory"); };
+  // the bias into 8 TMEM columns of this thread's lane
+  auto bias8 = [&](uint32_t taddr) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %1, %1, %1, %1, %1, %1, %1};" ::"r"(taddr), "r"(WIDE_BIAS) : "memory");
   };
 
   if (warp == 0) {
@@ -814,10 +837,11 @@ __global__ void __launch_bounds__(WIDE_THREADS, 1) k_gemm_wide(QMat W, const int
     for (int s = 0; s < SS; ++s) {
       init(sfull(s), 1);
       init(sempty(s), WIDE_EPI_WARPS);  // every epilogue warp has combined the tile
+      init(tfull(s), 1);
     }
     for (int h = 0; h < 2; ++h) {
       init(hfull(h), 1);
-      init(hempty(h), WIDE_EPI_WARPS);
+      init(hempty(h), WIDE_EPI_WARPS);  // completes once with the initial bias, then once per tile
     }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -839,6 +863,8 @@ __global__ void __launch_bounds__(WIDE_THREADS, 1) k_gemm_wide(QMat W, const int
   __syncthreads();  // barriers initialised, TMEM allocated
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem = s_tmem;
+  const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16);
+  const int c0 = (ew >> 2) * WIDE_EPI_TOKENS;
   int issued = 0;     // token tiles whose copies warp 0 has issued
   int committed = 0;  // token tiles whose MMAs warp 1 has issued
 
@@ -873,8 +899,8 @@ __global__ void __launch_bounds__(WIDE_THREADS, 1) k_gemm_wide(QMat W, const int
       int halves = 0;
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
-        // the epilogue has drained this half of the previous tile
-        if (i >= 1 && !mbar_wait(hempty(h), (i - 1) & 1)) {
+        // the epilogue has drained this half of the previous tile and reset it to the bias
+        if (!mbar_wait(hempty(h), i & 1)) {
           ok = false;
           break;
         }
@@ -886,13 +912,9 @@ __global__ void __launch_bounds__(WIDE_THREADS, 1) k_gemm_wide(QMat W, const int
             const int g = 2 * h + gi, step = g * 4 + k;  // K bytes 32·step .. 32·step+31
             const uint64_t da = umma_desc(a0 + step * 256, 128, GEMM_KC * 128);
             const uint64_t db = umma_desc(b0 + step * 256, 128, GEMM_KC * 128);
-            const uint32_t d_tmem = tmem + g * WIDE_NT, accumulate = k > 0 ? 1u : 0u;
-            asm volatile(
-                "{\n\t.reg .pred p;\n\t"
-                "setp.ne.b32 p, %4, 0;\n\t"
-                "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}" ::"r"(d_tmem),
-                "l"(da), "l"(db), "r"(IDESC), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
-                : "memory");
+            asm volatile("tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, 1;" ::"r"(tmem + g * WIDE_NT), "l"(da), "l"(db),
+                         "r"(IDESC)
+                         : "memory");
           }
         asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(hfull(h)) : "memory");
         ++halves;
@@ -908,9 +930,37 @@ __global__ void __launch_bounds__(WIDE_THREADS, 1) k_gemm_wide(QMat W, const int
         break;
       }
     }
+  } else if (warp == 2) {
+    for (int i = 0; i < my_tiles; ++i) {
+      const int sc = i % SS;
+      bool ok = !s_fail;
+      if (ok && lane == 0) ok = mbar_wait(sfull(sc), (i / SS) & 1);
+      if (!__shfl_sync(FULL, ok ? 1 : 0, 0)) {
+        s_fail = 1;
+        break;
+      }
+      // (a token past M transposes a stale entry; its output is not stored)
+      const float* src = sS + (size_t)sc * WIDE_NT * GK;
+      float* dst = sT + (size_t)sc * WIDE_NT * GK;
+#pragma unroll 4
+      for (int e = lane; e < WIDE_NT * GK; e += 32) dst[e] = src[(e % WIDE_NT) * GK + e / WIDE_NT];
+      __syncwarp();
+      if (lane == 0) arrive(tfull(sc));
+    }
   } else if (ew >= 0) {
-    const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16);
-    const int c0 = (ew >> 2) * WIDE_EPI_TOKENS;
+    // the bias into this warp's columns before the first tile's MMAs
+#pragma unroll
+    for (int g = 0; g < GK; ++g)
+#pragma unroll
+      for (int q = 0; q < WIDE_EPI_TOKENS / 8; ++q) bias8(lane_base + g * WIDE_NT + c0 + q * 8);
+    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncwarp();
+    if (lane == 0) {
+      arrive(hempty(0));
+      arrive(hempty(1));
+    }
+    const float2 nz = g_negzero;
     // the combine per tile, with the product form (fused panels or the 4-bit
     // chain) fixed outside the loops
     auto drain = [&](auto fused_tag) {
@@ -919,7 +969,7 @@ __global__ void __launch_bounds__(WIDE_THREADS, 1) k_gemm_wide(QMat W, const int
       for (int i = 0; i < my_tiles; ++i) {
         const int sc = i % SS;
         bool ok = !s_fail;
-        if (ok && lane == 0) ok = mbar_wait(sfull(sc), (i / SS) & 1);
+        if (ok && lane == 0) ok = mbar_wait(tfull(sc), (i / SS) & 1);
         ok = __shfl_sync(FULL, ok ? 1 : 0, 0) != 0;
         if (!ok) {
           s_fail = 1;
@@ -929,10 +979,12 @@ __global__ void __launch_bounds__(WIDE_THREADS, 1) k_gemm_wide(QMat W, const int
         // which of this warp's 32 tokens are stored: bit j for token m0 + c0 + j
         const int m = m0 + c0 + lane;
         const uint32_t store = __ballot_sync(FULL, m < M && !(meta && __ldcg(&meta[m].slot) < 0));
-        // the tile's act scales, [token][group] (a token past M reads a stale
-        // stage entry; its output is not stored)
-        const float2* tscale = reinterpret_cast<const float2*>(sS + (size_t)sc * WIDE_NT * GK) + 2 * c0;
-        float total[WIDE_EPI_TOKENS];
+        // every token of this warp's 32 is stored: the finished totals leave
+        // through the warp's staging buffer as TMA tensor stores of 8 tokens,
+        // so the warp goes on to the next tile while they drain to memory
+        const bool tma = tma_out && store == FULL;
+        const float* tscale = sT + (size_t)sc * WIDE_NT * GK + c0;  // [group][token]
+        float2 total[WIDE_EPI_TOKENS / 2];  // token pairs (2n, 2n + 1)
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
           if (ok && lane == 0) ok = mbar_wait(hfull(h), i & 1);
@@ -949,38 +1001,71 @@ __global__ void __launch_bounds__(WIDE_THREADS, 1) k_gemm_wide(QMat W, const int
                              "=r"(a[gi][6]), "=r"(a[gi][7])
                            : "r"(lane_base + (2 * h + gi) * WIDE_NT + c0 + q * 8));
             asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+            // the columns are read: back to the bias for the next tile's MMAs
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              const int n = q * 8 + j;
-              const float2 s2 = tscale[2 * n + h];  // groups 2h, 2h + 1 of token n
-              float t = h == 0 ? 0.0f : total[n];
-              const float as[2] = {s2.x, s2.y};
+            for (int gi = 0; gi < 2; ++gi) bias8(lane_base + (2 * h + gi) * WIDE_NT + c0 + q * 8);
+#pragma unroll
+            for (int pp = 0; pp < 4; ++pp) {
+              const int n2 = q * 4 + pp;  // the token pair (2·n2, 2·n2 + 1) of this warp's 32
+              float2 t = h == 0 ? make_float2(0.0f, 0.0f) : total[n2];
 #pragma unroll
               for (int gi = 0; gi < 2; ++gi) {
                 const int g = 2 * h + gi;
-                const float accv = group_sum_to_float(a[gi][j]);
-                t = FUSED ? __fmaf_rn(accv, fmul(ws[g], as[gi]), t) : fadd(t, fmul(fmul(fmul(accv, ws[g]), level), as[gi]));
+                const float2 acc = add2(make_float2(__int_as_float((int)a[gi][2 * pp]), __int_as_float((int)a[gi][2 * pp + 1])),
+                                        make_float2(-12582912.0f, -12582912.0f));
+                const float2 as = *reinterpret_cast<const float2*>(tscale + g * WIDE_NT + 2 * n2);
+                const float2 w = make_float2(ws[g], ws[g]);
+                if (FUSED)
+                  t = fma2(acc, fma2(w, as, nz), t);
+                else
+                  t = add2(t, fma2(fma2(fma2(acc, w, nz), make_float2(level, level), nz), as, nz));
               }
-              total[n] = t;
+              total[n2] = t;
+            }
+            if (h == 1) {
+              // the finished chunk of 8 tokens through the warp's staging
+              // buffer: a TMA tensor store, or (a warp with a token not to
+              // store) plain stores of the live tokens
+              float* stage = sO + (size_t)ew * (WIDE_O_BYTES / 4);
+              if (tma && lane == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");  // the previous store has read it
+              __syncwarp();
+#pragma unroll
+              for (int pp = 0; pp < 4; ++pp) {
+                stage[(2 * pp) * 32 + lane] = total[q * 4 + pp].x;
+                stage[(2 * pp + 1) * 32 + lane] = total[q * 4 + pp].y;
+              }
+              if (tma) {
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                __syncwarp();
+                if (lane == 0) {
+                  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+                                   reinterpret_cast<uint64_t>(&out_map)),
+                               "r"(tile * GEMM_ROWS + quad * 32), "r"(m0 + c0 + q * 8), "r"(smem_u32(stage))
+                               : "memory");
+                  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+                }
+              } else if (valid) {
+#pragma unroll 1
+                for (int j = 0; j < 8; ++j)
+                  if ((store >> (q * 8 + j)) & 1) out[(size_t)(m0 + c0 + q * 8 + j) * out_stride + row] = stage[j * 32 + lane];
+              }
             }
           }
-          // this half's columns are read: the next tile's MMAs may overwrite them
+          // this half's columns are read and reset to the bias: the next tile's MMAs may use them
+          asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
           asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
           __syncwarp();
-          if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(hempty(h)) : "memory");
+          if (lane == 0) arrive(hempty(h));
         }
         if (!ok) {
           s_fail = 1;
           break;
         }
         // the stage's scales are read: the copy of tile i + WIDE_SCALE_STAGES may refill it
-        if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(sempty(sc)) : "memory");
-        if (valid) {
-#pragma unroll
-          for (int j = 0; j < WIDE_EPI_TOKENS; ++j)
-            if ((store >> j) & 1) out[(size_t)(m0 + c0 + j) * out_stride + row] = total[j];
-        }
+        if (lane == 0) arrive(sempty(sc));
       }
+      // the tensor stores have completed before the CTA leaves
+      if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
     };
     if (W.fused)
       drain(std::true_type{});
@@ -1648,28 +1733,6 @@ __global__ void __launch_bounds__(128) k_prep(const float* __restrict__ in, int 
 // multiply-adds, two columns per packed instruction. The stage-A operand X
 // enters transposed (XT[j][i]). Operands arrive by cp.async, the next factor
 // pair while the current stage's elementwise pass runs.
-// Packed two-lane f32 arithmetic (PTX add/fma .rn.f32x2): each component
-// rounded to nearest exactly as the scalar .rn instruction.
-__device__ __forceinline__ float2 add2(float2 a, float2 b) {
-  float2 d;
-  asm("{\n\t.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
-      "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
-      : "=f"(d.x), "=f"(d.y) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
-  return d;
-}
-__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
-  float2 d;
-  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
-      "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
-      : "=f"(d.x), "=f"(d.y) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
-  return d;
-}
-
-// -0.0 in both lanes, read from memory so the compiler cannot see the value:
-// fma(a, b, -0.0) is a·b rounded once, exactly mul.rn, and a packed fma is
-// never merged with the packed add that follows it (a visible packed multiply
-// would be, into one fused multiply-add the reference never performs).
-__device__ float2 g_negzero = {-0.0f, -0.0f};
 
 template <int S, int R, bool FUSED32>
 __device__ __forceinline__ void tn_stage(const float* __restrict__ A, const float* __restrict__ B, float* __restrict__ C, float2 nz,
@@ -2891,6 +2954,29 @@ static void launch(void (*kernel)(P...), dim3 grid, dim3 block, size_t smem, cud
   launch_clustered(kernel, grid, block, smem, st, dim3(1, 1, 1), std::forward<A>(args)...);
 }
 
+// The output of a wide product as a 2-D tensor map (rows innermost, one
+// token per outer index) for TMA stores of [8 tokens][32 rows] boxes; rows
+// past `rows` and tokens past M are clipped by the copy. False (plain stores
+// then) when the driver entry point is missing or the base or the token
+// stride is not 16-byte aligned.
+static bool wide_out_map(CUtensorMap* map, const float* out, int rows, int M, int out_stride) {
+  static const PFN_cuTensorMapEncodeTiled encode = [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult found = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &found) != cudaSuccess ||
+        found != cudaDriverEntryPointSuccess)
+      return (PFN_cuTensorMapEncodeTiled) nullptr;
+    return reinterpret_cast<PFN_cuTensorMapEncodeTiled>(fn);
+  }();
+  std::memset(map, 0, sizeof *map);
+  if (!encode || (reinterpret_cast<uintptr_t>(out) & 15) || ((size_t)out_stride * 4) % 16) return false;
+  const cuuint64_t dims[2] = {(cuuint64_t)rows, (cuuint64_t)M};
+  const cuuint64_t strides[1] = {(cuuint64_t)out_stride * 4};
+  const cuuint32_t box[2] = {32, 8}, elements[2] = {1, 1};
+  return encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(out), dims, strides, box, elements, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 // One codebook product of M tokens through W (K = W.cols: 512, or 2048 in the
 // product benchmark): the CUDA-core GEMV for a few tokens, the pipelined
 // persistent tcgen05 kernel for passes of at least WIDE_MIN_TOKENS tokens at
@@ -2916,7 +3002,9 @@ static void project(const QMat& W, const int8_t* act, const float* act_scale, fl
     }();
     const int token_tiles = (M + WIDE_NT - 1) / WIDE_NT;
     const int P = std::max(1, std::min(token_tiles, sms / tiles));
-    launch(k_gemm_wide, dim3(tiles, P), WIDE_THREADS, wide_smem(), st, W, act, act_scale, out, M, out_stride, meta, error);
+    CUtensorMap map;
+    const int tma = wide_out_map(&map, out, (int)W.rows, M, out_stride) ? 1 : 0;
+    launch(k_gemm_wide, dim3(tiles, P), WIDE_THREADS, wide_smem(), st, W, act, act_scale, out, M, out_stride, meta, error, map, tma);
   } else if (M <= 16) {
     auto k = wide ? k_gemm<16, 4> : k_gemm<16, 1>;
     launch(k, dim3(tiles, 1), GEMM_THREADS_PER_TOKEN * 16, gemm_smem<16>(), st, W, act, act_scale, out, M, out_stride, meta, error, act_rows);
