@@ -1997,10 +1997,16 @@ __device__ __forceinline__ void engram_ring_store(const ModelDev& md, const Engr
   for (int i = part * share + (int)threadIdx.x; i < (part + 1) * share; i += blockDim.x) dst[i] = __ldcg(src + i);
 }
 
-template <int LEFT, int FACTORS>
+// No fused out product: the block finish stages the attention's out product row.
+struct StagedOut {
+  __device__ bool fused() const { return false; }
+  __device__ void operator()() const {}
+};
+
+template <int LEFT, int FACTORS, typename OutProduct = StagedOut>
 __device__ __forceinline__ bool block_front(const ModelDev& md, const LayerDev& L, const Work& w, int M, int t, int d, int* error,
                                             float* s_a, float* s_x, float* s_pre, float* s_condv, float* s_left, float* s_right,
-                                            float* s_gpost, float* s_gpre, int part, int parts) {
+                                            float* s_gpost, float* s_gpre, int part, int parts, const OutProduct& out_product = {}) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   __shared__ float s_inv, s_gate;
   __shared__ __align__(8) uint64_t s_bar;
@@ -2028,7 +2034,7 @@ __device__ __forceinline__ bool block_front(const ModelDev& md, const LayerDev& 
   }
   // with Whistle cross attention, k_cross_q has formed x after the residual (w.xr)
   // and, for sessions with a memory, the cross out product sits in w.outp
-  stage_async(s_a, (md.cross ? w.xr : w.outp) + (size_t)t * d, d);
+  if (!out_product.fused()) stage_async(s_a, (md.cross ? w.xr : w.outp) + (size_t)t * d, d);
   const bool cross_live = md.cross && md.slot_cross[load_meta(w.meta, t).slot];
   if (cross_live) stage_async(s_pre, w.outp + (size_t)t * d, d);
   if (md.conv_ring) conv_ring_store(md, L, w, M, t, part, parts);
@@ -2038,6 +2044,7 @@ __device__ __forceinline__ bool block_front(const ModelDev& md, const LayerDev& 
   // every thread past this point; then each thread waits for the bulk copies
   __syncthreads();
   if (!mbar_wait(bar, 0) && tid == 0) atomicExch(error, 1);
+  out_product();  // with the out product fused: s_a formed here, in every CTA of the cluster
   if (!md.cross) {
     if (warp == 0) {
       float ss = sum_of_squares_warp(s_a, d);
@@ -2179,8 +2186,29 @@ __device__ __forceinline__ float2 col_pair(const float* __restrict__ A, const fl
   return acc;
 }
 
+// The out product fused into the split block finish (a pass of at most
+// GEMV_MAX_TOKENS tokens, d = 512, four CTAs per token): CTA q forms rows
+// q·128 .. q·128+127 of the token's out product from the attention's int8
+// activations, with k_gemv's lane layout and ordered per-group combine, and
+// stores them into every CTA's s_a through distributed shared memory. Its
+// weight slice (64 KB of codes, 2 KB of scales) is bulk-copied before the
+// predecessor finishes.
+constexpr int FUSED_OUT_ROWS = 128;
+constexpr uint32_t FUSED_OUT_CODES = FUSED_OUT_ROWS * GEMM_K, FUSED_OUT_SCALES = FUSED_OUT_ROWS * (GEMM_K / GROUP) * 4;
+template <typename F>
+struct FusedOut {
+  bool on;
+  F f;
+  __device__ bool fused() const { return on; }
+  __device__ void operator()() const {
+    if (on) f();
+  }
+};
+__host__ __device__ constexpr size_t block_split_out_offset(size_t split_floats) { return (split_floats * 4 + 127) / 128 * 128; }
+
 template <int LEFT>
-__global__ void __launch_bounds__(BLOCK_THREADS) k_block_split(ModelDev md, LayerDev L, Work w, int M, int* error) {
+__global__ void __launch_bounds__(BLOCK_THREADS) k_block_split(ModelDev md, LayerDev L, Work w, int M, int* error, int fuse_out,
+                                                               int split_floats) {
   namespace cg = cooperative_groups;
   extern __shared__ float sm[];
   constexpr int N = LEFT * HADA_RIGHT, W = BlockSplit<LEFT>::W, CL = BlockSplit<LEFT>::CL;
@@ -2223,7 +2251,64 @@ __global__ void __launch_bounds__(BLOCK_THREADS) k_block_split(ModelDev md, Laye
 #pragma unroll
     for (int s = 0; s < LANES; ++s) sv[s] = __ldcg(w.stream + ((size_t)t * LANES + s) * d + ei);
   }
-  if (!block_front<LEFT, 1>(md, L, w, M, t, d, error, s_a, s_x, s_pre, s_condv, s_left, s_right, s_gpost, s_gpre, q, CL)) return;
+  // the fused out product: this CTA's weight slice, copied while the predecessor runs
+  uint8_t* s_wout = reinterpret_cast<uint8_t*>(sm) + block_split_out_offset((size_t)split_floats);
+  const float* s_wsc = reinterpret_cast<const float*>(s_wout + FUSED_OUT_CODES);
+  __shared__ __align__(8) uint64_t s_obar;
+  __shared__ __align__(16) uint4 s_act4[GEMM_KC];
+  __shared__ float s_as4[GEMM_K / GROUP];
+  const uint32_t obar = smem_u32(&s_obar);
+  const QMat& Wout = L.out;
+  if (fuse_out && tid == 0) {
+    bulk_start(obar, FUSED_OUT_CODES + FUSED_OUT_SCALES);
+    const uint8_t* codes = reinterpret_cast<const uint8_t*>(Wout.codes) + (size_t)q * FUSED_OUT_CODES;
+    for (uint32_t off = 0; off < FUSED_OUT_CODES; off += 16384) bulk_copy(s_wout + off, codes + off, 16384, obar);
+    bulk_copy(s_wout + FUSED_OUT_CODES, Wout.scales + (size_t)q * FUSED_OUT_ROWS * (GEMM_K / GROUP), FUSED_OUT_SCALES, obar);
+  }
+  auto out_product = [&] {
+    if (!mbar_wait(obar, 0) && tid == 0) atomicExch(error, 1);
+    // the token's activations (the attention, this kernel's predecessor, wrote them)
+    if (tid < GEMM_KC) s_act4[tid] = __ldcg(reinterpret_cast<const uint4*>(w.act + core_offset(t, tid * 16, GEMM_KC)));
+    if (tid < GEMM_K / GROUP) s_as4[tid] = __ldcg(w.act_scale + (size_t)t * (GEMM_K / GROUP) + tid);
+    cluster.sync();  // every CTA of the cluster runs (remote stores below); the row is visible to the block
+    const int lane = tid & 31, warp = tid >> 5, r8 = lane & 7, qd = lane >> 3;
+    for (int rb = warp; rb < FUSED_OUT_ROWS / 8; rb += BLOCK_THREADS / 32) {
+      // lane: row r8 of the 8-row block, 16-byte chunks 4j + qd (k_gemv's layout)
+      const uint4* blk = reinterpret_cast<const uint4*>(s_wout + (size_t)rb * 8 * GEMM_K);
+      int acc[GEMM_K / GROUP] = {0, 0, 0, 0};
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const uint4 wv = blk[j * 32 + lane], av = s_act4[4 * j + qd];
+        const int g = j >> 1;
+        acc[g] = dp4a(wv.x, av.x, acc[g]);
+        acc[g] = dp4a(wv.y, av.y, acc[g]);
+        acc[g] = dp4a(wv.z, av.z, acc[g]);
+        acc[g] = dp4a(wv.w, av.w, acc[g]);
+      }
+#pragma unroll
+      for (int g = 0; g < GEMM_K / GROUP; ++g) {
+        acc[g] += __shfl_xor_sync(FULL, acc[g], 8);
+        acc[g] += __shfl_xor_sync(FULL, acc[g], 16);
+      }
+      if (qd == 0) {
+        const int row = rb * 8 + r8;
+        float total = 0.0f;
+#pragma unroll
+        for (int g = 0; g < GEMM_K / GROUP; ++g) {
+          const float a = group_sum_to_float((uint32_t)acc[g]), as = s_as4[g], wsc = s_wsc[row * (GEMM_K / GROUP) + g];
+          total = Wout.fused ? __fmaf_rn(a, fmul(wsc, as), total) : fadd(total, fmul(fmul(fmul(a, wsc), Wout.level_scale), as));
+        }
+#pragma unroll
+        for (int p = 0; p < CL; ++p) *cluster.map_shared_rank(s_a + q * FUSED_OUT_ROWS + row, p) = total;
+      }
+    }
+    cluster.sync();  // s_a is whole in every CTA
+  };
+  const FusedOut<decltype(out_product)> fused{fuse_out != 0, out_product};
+  if (!block_front<LEFT, 1>(md, L, w, M, t, d, error, s_a, s_x, s_pre, s_condv, s_left, s_right, s_gpost, s_gpre, q, CL, fused)) {
+    if (fuse_out && tid == 0 && !mbar_wait(obar, 0)) atomicExch(error, 1);  // no copy outlives the CTA
+    return;
+  }
   cluster_arrive_relaxed();  // paired with the wait before the first remote store
   __syncthreads();
   hada_prepare<LEFT>(Hd, d, s_pre, xa, s_mod, s_condv);
@@ -2887,8 +2972,9 @@ cudaError_t configure(const ModelDev& md, int t_cap) {
     return e;
   if ((e = cudaFuncSetAttribute(k_block<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)block_smem(md)))) return e;
   if ((e = cudaFuncSetAttribute(k_block<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)block_smem(md)))) return e;
-  if ((e = cudaFuncSetAttribute(k_block_split<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)block_split_smem(md)))) return e;
-  if ((e = cudaFuncSetAttribute(k_block_split<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)block_split_smem(md)))) return e;
+  const int split_max = (int)(block_split_out_offset(block_split_smem(md) / 4) + FUSED_OUT_CODES + FUSED_OUT_SCALES);
+  if ((e = cudaFuncSetAttribute(k_block_split<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, split_max))) return e;
+  if ((e = cudaFuncSetAttribute(k_block_split<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, split_max))) return e;
   if ((e = cudaFuncSetAttribute(k_stats, cudaFuncAttributeMaxDynamicSharedMemorySize, 2 * 8192 * 4))) return e;
   if ((e = cudaFuncSetAttribute(k_cross_attend, cudaFuncAttributeMaxDynamicSharedMemorySize, 2 * MAX_CROSS_FRAMES * 4))) return e;
   if ((e = cudaFuncSetAttribute(k_gemm<16, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gemm_smem<16>()))) return e;
@@ -2977,6 +3063,16 @@ static bool wide_out_map(CUtensorMap* map, const float* out, int rows, int M, in
                 CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// Passes of at least this many tokens take the persistent product
+// ($NEEDLE_B200_WIDE_TOKENS overrides WIDE_MIN_TOKENS).
+static int wide_min_tokens() {
+  static const int n = [] {
+    const char* e = std::getenv("NEEDLE_B200_WIDE_TOKENS");
+    return e ? std::max(1, std::atoi(e)) : WIDE_MIN_TOKENS;
+  }();
+  return n;
+}
+
 // One codebook product of M tokens through W (K = W.cols: 512, or 2048 in the
 // product benchmark): the CUDA-core GEMV for a few tokens, the pipelined
 // persistent tcgen05 kernel for passes of at least WIDE_MIN_TOKENS tokens at
@@ -2992,7 +3088,7 @@ static void project(const QMat& W, const int8_t* act, const float* act_scale, fl
       launch(k_gemv<4>, ctas, GEMV_WARPS * 32, 0, st, W, act, act_scale, out, M, out_stride, meta, act_rows);
     else
       launch(k_gemv<1>, ctas, GEMV_WARPS * 32, 0, st, W, act, act_scale, out, M, out_stride, meta, act_rows);
-  } else if (!wide && M >= WIDE_MIN_TOKENS) {
+  } else if (!wide && M >= wide_min_tokens()) {
     // persistent CTAs, one per SM: P of them share each row tile's token tiles
     static const int sms = [] {
       int device = 0, n = 0;
@@ -3027,17 +3123,37 @@ void launch_embed(const ModelDev& md, const Work& w, int M, cudaStream_t st) {
 // (norms, softmax, elementwise passes in every CTA of a cluster) would cost
 // throughput. $NEEDLE_B200_BLOCK_SPLIT=N sets the threshold (0: never).
 constexpr int BLOCK_SPLIT_MAX_TOKENS = 64;
-static void launch_block(const ModelDev& md, const LayerDev& L, const Work& w, int M, cudaStream_t st) {
+static bool block_split_path(const ModelDev& md, int M) {
   static const int max_tokens = [] {
     const char* e = std::getenv("NEEDLE_B200_BLOCK_SPLIT");
     return e ? std::atoi(e) : BLOCK_SPLIT_MAX_TOKENS;
   }();
-  const int left = md.hada_left, W = 2 * BLOCK_THREADS / left, CL = HADA_RIGHT / W;
+  const int W = 2 * BLOCK_THREADS / (int)md.hada_left;
   // every thread of a CTA takes at most one element of the lane combine
-  const bool split = M <= max_tokens && ((int)md.d_model / HADA_RIGHT) * W <= BLOCK_THREADS;
-  if (split) {
+  return M <= max_tokens && ((int)md.d_model / HADA_RIGHT) * W <= BLOCK_THREADS;
+}
+
+// Whether the pass's out product runs inside the split block finish: a few
+// tokens (the product would be k_gemv's), d = 512 on four CTAs per token, no
+// cross attention (whose step reads the out product itself).
+// $NEEDLE_B200_FUSE_OUT=0 keeps the separate product.
+static bool fuse_out_product(const ModelDev& md, const LayerDev& L, int M, bool cross) {
+  static const bool off = [] {
+    const char* e = std::getenv("NEEDLE_B200_FUSE_OUT");
+    return e && e[0] == '0';
+  }();
+  const int CL = HADA_RIGHT / (2 * BLOCK_THREADS / (int)md.hada_left);
+  return !off && !cross && M <= GEMV_MAX_TOKENS && block_split_path(md, M) && CL * FUSED_OUT_ROWS == (int)md.d_model &&
+         L.out.rows == md.d_model && L.out.cols == (uint32_t)GEMM_K;
+}
+
+static void launch_block(const ModelDev& md, const LayerDev& L, const Work& w, int M, cudaStream_t st, bool fuse_out = false) {
+  const int left = md.hada_left, W = 2 * BLOCK_THREADS / left, CL = HADA_RIGHT / W;
+  if (block_split_path(md, M)) {
     auto k = left == 64 ? k_block_split<64> : k_block_split<32>;
-    launch_clustered(k, dim3(M * CL), BLOCK_THREADS, block_split_smem(md), st, dim3(CL, 1, 1), md, L, w, M, md.error);
+    const int split_floats = (int)(block_split_smem(md) / 4);
+    const size_t smem = fuse_out ? block_split_out_offset(split_floats) + FUSED_OUT_CODES + FUSED_OUT_SCALES : block_split_smem(md);
+    launch_clustered(k, dim3(M * CL), BLOCK_THREADS, smem, st, dim3(CL, 1, 1), md, L, w, M, md.error, fuse_out ? 1 : 0, split_floats);
   } else {
     auto k = left == 64 ? k_block<64> : k_block<32>;
     launch(k, M, BLOCK_THREADS, block_smem(md), st, md, L, w, M, md.error);
@@ -3067,7 +3183,8 @@ void launch_layer(const ModelDev& md, const LayerDev& L, const EngramDev* engram
     launch(k_prep, M, 128, 0, st, (const float*)w.attn, H * HEAD_DIM, (const int32_t*)nullptr,
            (const float*)(w.proj + (H + 2 * KV) * HEAD_DIM), proj_stride, H * HEAD_DIM, w.act, w.act_scale, M, w.meta,
            md.inv_sqrt_group, 1, 0);
-  project(L.out, w.act, w.act_scale, w.outp, M, d, w.meta, st, md.error);
+  const bool fuse_out = fuse_out_product(md, L, M, cross != nullptr);
+  if (!fuse_out) project(L.out, w.act, w.act_scale, w.outp, M, d, w.meta, st, md.error);
   if (cross) {  // Whistle: CrossState::apply after the attention residual (session.rs:126-128)
     launch(k_cross_q, M, 128, 0, st, md, L, layer, w, M);
     project(cross->qg, w.act, w.act_scale, w.cq, M, 2 * d, w.meta, st, md.error);
@@ -3076,7 +3193,7 @@ void launch_layer(const ModelDev& md, const LayerDev& L, const EngramDev* engram
            w.act, w.act_scale, M, w.meta, md.inv_sqrt_group, 1, 0);
     project(cross->out, w.act, w.act_scale, w.outp, M, d, w.meta, st, md.error);  // the block finish adds it
   }
-  launch_block(md, L, w, M, st);
+  launch_block(md, L, w, M, st, fuse_out);
 }
 
 cudaError_t cross_memory(const ModelDev& md, const std::vector<CrossLayerDev>& layers, const float* encoded, int frames,
