@@ -730,41 +730,39 @@ __global__ void __launch_bounds__(GEMM_THREADS_PER_TOKEN * NT) k_gemm(QMat W, co
 // ------------------------------------------- tensor-core product, large passes
 // For passes of at least WIDE_MIN_TOKENS tokens through a K = 512 matrix: a
 // persistent CTA per SM keeps one 128-row weight tile resident in shared
-// memory and walks 128-token tiles (CTA (r, p) takes token tiles p, p + P, ...
+// memory and walks 64-token tiles (CTA (r, p) takes token tiles p, p + P, ...
 // of row tile r), warp-specialised:
-//   warp 0 (one lane)   streams each tile's token codes through a 2-stage ring
-//                       (64 KB stages, freed when the tile's MMAs complete) and
-//                       its act scales through a 4-stage ring (freed by the
-//                       epilogue), bulk copies onto mbarriers
-//   warp 1 (one lane)   issues the tile's tcgen05.mma kind::i8 (M = 128,
-//                       N = 128: twice the work of N = 64 for a little more
-//                       time per instruction) in two halves, groups 0-1 into
-//                       TMEM columns 0..255 and groups 2-3 into 256..511,
-//                       committing each half to the epilogue
+//   warp 0 (one lane)   streams each tile's token codes through a ring of
+//                       32 KB stages (freed when the tile's MMAs complete) and
+//                       its act scales through a ring freed by the epilogue,
+//                       bulk copies onto mbarriers
+//   warp 1 (one lane)   issues the tile's 16 tcgen05.mma kind::i8 (M = 128,
+//                       N = 64, K = 32) into one of two TMEM accumulator sets
+//                       (columns 0..255 and 256..511, [4 groups][64 tokens]),
+//                       so the MMAs of one tile run while the epilogue drains
+//                       the previous one
 //   warp 2              transposes each tile's act scales to [group][token],
 //                       so a pair of tokens' scales of one group is one 8-byte
 //                       shared-memory load
 //   warps 4..19         thread = weight row (warp w reads TMEM lane quadrant
-//                       w % 4) for tokens 32·((w - 4) / 4) .. +31: drain the
-//                       first half into running totals (groups 0, 1 in order),
-//                       hand its columns back, then the second (groups 2, 3),
+//                       w % 4) for tokens 16·((w - 4) / 4) .. +15, in chunks
+//                       of 8 tokens: the four groups' accumulators in order,
 //                       exactly k_gemm's combine, two tokens per packed f32x2
-//                       instruction; finished totals leave by TMA tensor stores
-// so the MMAs of one half overlap the combine of the other, and the next
-// tile's first half starts while the epilogue drains this tile's second.
+//                       instruction; each finished chunk leaves by a TMA
+//                       tensor store
 // The accumulators start from the bias 0x4B400000 (written into TMEM by the
-// epilogue when it hands columns back, and once before the first tile), so an
+// epilogue when it hands a set back, and once before the first tile), so an
 // int32 group sum s arrives as the bits of the float 1.5·2^23 + s and its
 // exact f32 value is one subtraction (|s| ≤ 2^21; group_sum_to_float).
 // Every wait is bounded; a wait that gives up sets the error flag, the other
 // roles stop at their next wait, and the copy and MMA threads wait (bounded)
 // for what they issued before the CTA frees its TMEM and exits.
-constexpr int WIDE_NT = 128;
-constexpr int WIDE_CODE_STAGES = 2;
+constexpr int WIDE_NT = 64;
+constexpr int WIDE_CODE_STAGES = 3;
 constexpr int WIDE_SCALE_STAGES = 4;
 constexpr int WIDE_MIN_TOKENS = 256;
 constexpr int WIDE_EPI_WARPS = 16;
-constexpr int WIDE_EPI_TOKENS = WIDE_NT / (WIDE_EPI_WARPS / 4);  // 32 tokens per epilogue warp
+constexpr int WIDE_EPI_TOKENS = WIDE_NT / (WIDE_EPI_WARPS / 4);  // 16 tokens per epilogue warp
 constexpr int WIDE_THREADS = (4 + WIDE_EPI_WARPS) * 32;
 constexpr uint32_t WIDE_A_BYTES = GEMM_ROWS * GEMM_K, WIDE_B_BYTES = WIDE_NT * GEMM_K;
 constexpr uint32_t WIDE_S_BYTES = WIDE_NT * (GEMM_K / GROUP) * 4;  // a token tile's act scales
@@ -779,16 +777,17 @@ __global__ void __launch_bounds__(WIDE_THREADS, 1) k_gemm_wide(QMat W, const int
                                                               float* __restrict__ out, int M, int out_stride,
                                                               const TokenMeta* __restrict__ meta, int* __restrict__ error,
                                                               const __grid_constant__ CUtensorMap out_map, int tma_out) {
-  constexpr int GK = GEMM_K / GROUP;  // 4 groups: columns g·128 .. g·128+127 of TMEM
-  constexpr uint32_t COLS = GK * WIDE_NT;  // 512
+  constexpr int GK = GEMM_K / GROUP;            // 4 groups
+  constexpr uint32_t SET = GK * WIDE_NT;        // TMEM columns of one accumulator set: group g at g·64
+  constexpr uint32_t COLS = 2 * SET;            // 512
   constexpr uint32_t IDESC = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(WIDE_NT >> 3) << 17) | ((uint32_t)(GEMM_ROWS >> 4) << 24);
   constexpr uint32_t PIECE = 16384;
   constexpr int CS = WIDE_CODE_STAGES, SS = WIDE_SCALE_STAGES;
   extern __shared__ __align__(128) uint8_t smem[];
   uint8_t* sA = smem;
   uint8_t* sB = smem + WIDE_A_BYTES;
-  float* sS = reinterpret_cast<float*>(sB + (size_t)CS * WIDE_B_BYTES);  // [stage][128 tokens][4 groups], as copied
-  float* sT = sS + (size_t)SS * WIDE_NT * GK;                             // [stage][4 groups][128 tokens]
+  float* sS = reinterpret_cast<float*>(sB + (size_t)CS * WIDE_B_BYTES);  // [stage][64 tokens][4 groups], as copied
+  float* sT = sS + (size_t)SS * WIDE_NT * GK;                             // [stage][4 groups][64 tokens]
   float* sO = sT + (size_t)SS * WIDE_NT * GK;                             // [epilogue warp][8 tokens][32 rows]
   __shared__ __align__(8) uint64_t bars[1 + 2 * CS + 3 * SS + 4];
   __shared__ uint32_t s_tmem;
@@ -803,8 +802,8 @@ __global__ void __launch_bounds__(WIDE_THREADS, 1) k_gemm_wide(QMat W, const int
   auto sfull = [&](int s) { return smem_u32(&bars[1 + 2 * CS + s]); };
   auto sempty = [&](int s) { return smem_u32(&bars[1 + 2 * CS + SS + s]); };
   auto tfull = [&](int s) { return smem_u32(&bars[1 + 2 * CS + 2 * SS + s]); };
-  auto hfull = [&](int h) { return smem_u32(&bars[1 + 2 * CS + 3 * SS + h]); };
-  auto hempty = [&](int h) { return smem_u32(&bars[3 + 2 * CS + 3 * SS + h]); };
+  auto afull = [&](int b) { return smem_u32(&bars[1 + 2 * CS + 3 * SS + b]); };
+  auto aempty = [&](int b) { return smem_u32(&bars[3 + 2 * CS + 3 * SS + b]); };
   auto copy = [&](uint8_t* dst, const uint8_t* src, uint32_t bytes, uint32_t bar) {
     for (uint32_t off = 0; off < bytes; off += PIECE)
       asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(dst + off)),
@@ -832,16 +831,16 @@ __global__ void __launch_bounds__(WIDE_THREADS, 1) k_gemm_wide(QMat W, const int
     init(bar_a, 1);
     for (int s = 0; s < CS; ++s) {
       init(cfull(s), 1);
-      init(cempty(s), 1);  // the tile's last commit
+      init(cempty(s), 1);  // the tile's commit
     }
     for (int s = 0; s < SS; ++s) {
       init(sfull(s), 1);
       init(sempty(s), WIDE_EPI_WARPS);  // every epilogue warp has combined the tile
       init(tfull(s), 1);
     }
-    for (int h = 0; h < 2; ++h) {
-      init(hfull(h), 1);
-      init(hempty(h), WIDE_EPI_WARPS);  // completes once with the initial bias, then once per tile
+    for (int b = 0; b < 2; ++b) {
+      init(afull(b), 1);
+      init(aempty(b), WIDE_EPI_WARPS);  // completes once with the initial bias, then once per tile drained
     }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -889,46 +888,28 @@ __global__ void __launch_bounds__(WIDE_THREADS, 1) k_gemm_wide(QMat W, const int
   } else if (warp == 1 && lane == 0) {
     if (my_tiles > 0 && !mbar_wait(bar_a, 0)) s_fail = 1;
     for (int i = 0; i < my_tiles && !s_fail; ++i) {
-      const int c = i % CS;
-      if (!mbar_wait(cfull(c), (i / CS) & 1)) {
+      const int c = i % CS, b = i & 1;
+      // the code stage has landed; the epilogue has drained this set and reset it to the bias
+      if (!mbar_wait(cfull(c), (i / CS) & 1) || !mbar_wait(aempty(b), (i >> 1) & 1)) {
         s_fail = 1;
         break;
       }
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
       const uint32_t a0 = smem_u32(sA), b0 = smem_u32(sB + (size_t)c * WIDE_B_BYTES);
-      bool ok = true;
-      int halves = 0;
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        // the epilogue has drained this half of the previous tile and reset it to the bias
-        if (!mbar_wait(hempty(h), i & 1)) {
-          ok = false;
-          break;
+      for (int g = 0; g < GK; ++g)
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const int step = g * 4 + k;  // K bytes 32·step .. 32·step+31
+          const uint64_t da = umma_desc(a0 + step * 256, 128, GEMM_KC * 128);
+          const uint64_t db = umma_desc(b0 + step * 256, 128, GEMM_KC * 128);
+          asm volatile("tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, 1;" ::"r"(tmem + b * SET + g * WIDE_NT), "l"(da), "l"(db),
+                       "r"(IDESC)
+                       : "memory");
         }
-        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-#pragma unroll
-        for (int gi = 0; gi < 2; ++gi)
-#pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            const int g = 2 * h + gi, step = g * 4 + k;  // K bytes 32·step .. 32·step+31
-            const uint64_t da = umma_desc(a0 + step * 256, 128, GEMM_KC * 128);
-            const uint64_t db = umma_desc(b0 + step * 256, 128, GEMM_KC * 128);
-            asm volatile("tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, 1;" ::"r"(tmem + g * WIDE_NT), "l"(da), "l"(db),
-                         "r"(IDESC)
-                         : "memory");
-          }
-        asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(hfull(h)) : "memory");
-        ++halves;
-      }
-      if (halves > 0) {
-        // every MMA issued for the tile has read the code stage once this
-        // completes (also after a wait gave up: the exit waits for it)
-        asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(cempty(c)) : "memory");
-        ++committed;
-      }
-      if (!ok) {
-        s_fail = 1;
-        break;
-      }
+      asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(afull(b)) : "memory");
+      asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(cempty(c)) : "memory");
+      ++committed;
     }
   } else if (warp == 2) {
     for (int i = 0; i < my_tiles; ++i) {
@@ -948,121 +929,110 @@ __global__ void __launch_bounds__(WIDE_THREADS, 1) k_gemm_wide(QMat W, const int
       if (lane == 0) arrive(tfull(sc));
     }
   } else if (ew >= 0) {
-    // the bias into this warp's columns before the first tile's MMAs
+    // the bias into this warp's columns of both sets before the first tiles' MMAs
 #pragma unroll
-    for (int g = 0; g < GK; ++g)
+    for (int b = 0; b < 2; ++b)
 #pragma unroll
-      for (int q = 0; q < WIDE_EPI_TOKENS / 8; ++q) bias8(lane_base + g * WIDE_NT + c0 + q * 8);
+      for (int g = 0; g < GK; ++g)
+#pragma unroll
+        for (int q = 0; q < WIDE_EPI_TOKENS / 8; ++q) bias8(lane_base + b * SET + g * WIDE_NT + c0 + q * 8);
     asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncwarp();
     if (lane == 0) {
-      arrive(hempty(0));
-      arrive(hempty(1));
+      arrive(aempty(0));
+      arrive(aempty(1));
     }
     const float2 nz = g_negzero;
+    float* stage = sO + (size_t)ew * (WIDE_O_BYTES / 4);
     // the combine per tile, with the product form (fused panels or the 4-bit
     // chain) fixed outside the loops
     auto drain = [&](auto fused_tag) {
       constexpr bool FUSED = decltype(fused_tag)::value;
       const float level = W.level_scale;
       for (int i = 0; i < my_tiles; ++i) {
-        const int sc = i % SS;
+        const int sc = i % SS, b = i & 1;
         bool ok = !s_fail;
-        if (ok && lane == 0) ok = mbar_wait(tfull(sc), (i / SS) & 1);
+        if (ok && lane == 0) ok = mbar_wait(tfull(sc), (i / SS) & 1) && mbar_wait(afull(b), (i >> 1) & 1);
         ok = __shfl_sync(FULL, ok ? 1 : 0, 0) != 0;
         if (!ok) {
           s_fail = 1;
           break;
         }
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         const int m0 = (p + i * P) * WIDE_NT;
-        // which of this warp's 32 tokens are stored: bit j for token m0 + c0 + j
+        // which of this warp's 16 tokens are stored: bit j for token m0 + c0 + j
         const int m = m0 + c0 + lane;
-        const uint32_t store = __ballot_sync(FULL, m < M && !(meta && __ldcg(&meta[m].slot) < 0));
-        // every token of this warp's 32 is stored: the finished totals leave
-        // through the warp's staging buffer as TMA tensor stores of 8 tokens,
-        // so the warp goes on to the next tile while they drain to memory
-        const bool tma = tma_out && store == FULL;
+        const uint32_t store = __ballot_sync(FULL, lane < WIDE_EPI_TOKENS && m < M && !(meta && __ldcg(&meta[m].slot) < 0));
+        // every token of this warp's 16 is stored: each finished chunk of 8
+        // leaves through the warp's staging buffer as a TMA tensor store
+        const bool tma = tma_out && store == (1u << WIDE_EPI_TOKENS) - 1;
         const float* tscale = sT + (size_t)sc * WIDE_NT * GK + c0;  // [group][token]
-        float2 total[WIDE_EPI_TOKENS / 2];  // token pairs (2n, 2n + 1)
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          if (ok && lane == 0) ok = mbar_wait(hfull(h), i & 1);
-          ok = __shfl_sync(FULL, ok ? 1 : 0, 0) != 0;
-          if (!ok) break;
-          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        for (int q = 0; q < WIDE_EPI_TOKENS / 8; ++q) {
+          uint32_t a[GK][8];
 #pragma unroll
-          for (int q = 0; q < WIDE_EPI_TOKENS / 8; ++q) {
-            uint32_t a[2][8];
+          for (int g = 0; g < GK; ++g)
+            asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+                         : "=r"(a[g][0]), "=r"(a[g][1]), "=r"(a[g][2]), "=r"(a[g][3]), "=r"(a[g][4]), "=r"(a[g][5]), "=r"(a[g][6]),
+                           "=r"(a[g][7])
+                         : "r"(lane_base + b * SET + g * WIDE_NT + c0 + q * 8));
+          asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+          // the columns are read: back to the bias for the MMAs two tiles on
 #pragma unroll
-            for (int gi = 0; gi < 2; ++gi)
-              asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
-                           : "=r"(a[gi][0]), "=r"(a[gi][1]), "=r"(a[gi][2]), "=r"(a[gi][3]), "=r"(a[gi][4]), "=r"(a[gi][5]),
-                             "=r"(a[gi][6]), "=r"(a[gi][7])
-                           : "r"(lane_base + (2 * h + gi) * WIDE_NT + c0 + q * 8));
-            asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-            // the columns are read: back to the bias for the next tile's MMAs
+          for (int g = 0; g < GK; ++g) bias8(lane_base + b * SET + g * WIDE_NT + c0 + q * 8);
+          float2 total[4];  // the chunk's token pairs
 #pragma unroll
-            for (int gi = 0; gi < 2; ++gi) bias8(lane_base + (2 * h + gi) * WIDE_NT + c0 + q * 8);
+          for (int pp = 0; pp < 4; ++pp) {
+            float2 t = make_float2(0.0f, 0.0f);
 #pragma unroll
-            for (int pp = 0; pp < 4; ++pp) {
-              const int n2 = q * 4 + pp;  // the token pair (2·n2, 2·n2 + 1) of this warp's 32
-              float2 t = h == 0 ? make_float2(0.0f, 0.0f) : total[n2];
-#pragma unroll
-              for (int gi = 0; gi < 2; ++gi) {
-                const int g = 2 * h + gi;
-                const float2 acc = add2(make_float2(__int_as_float((int)a[gi][2 * pp]), __int_as_float((int)a[gi][2 * pp + 1])),
-                                        make_float2(-12582912.0f, -12582912.0f));
-                const float2 as = *reinterpret_cast<const float2*>(tscale + g * WIDE_NT + 2 * n2);
-                const float2 w = make_float2(ws[g], ws[g]);
-                if (FUSED)
-                  t = fma2(acc, fma2(w, as, nz), t);
-                else
-                  t = add2(t, fma2(fma2(fma2(acc, w, nz), make_float2(level, level), nz), as, nz));
-              }
-              total[n2] = t;
+            for (int g = 0; g < GK; ++g) {
+              const float2 acc = add2(make_float2(__int_as_float((int)a[g][2 * pp]), __int_as_float((int)a[g][2 * pp + 1])),
+                                      make_float2(-12582912.0f, -12582912.0f));
+              const float2 as = *reinterpret_cast<const float2*>(tscale + g * WIDE_NT + q * 8 + 2 * pp);
+              const float2 w = make_float2(ws[g], ws[g]);
+              if (FUSED)
+                t = fma2(acc, fma2(w, as, nz), t);
+              else
+                t = add2(t, fma2(fma2(fma2(acc, w, nz), make_float2(level, level), nz), as, nz));
             }
-            if (h == 1) {
-              // the finished chunk of 8 tokens through the warp's staging
-              // buffer: a TMA tensor store, or (a warp with a token not to
-              // store) plain stores of the live tokens
-              float* stage = sO + (size_t)ew * (WIDE_O_BYTES / 4);
-              if (tma && lane == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");  // the previous store has read it
-              __syncwarp();
-#pragma unroll
-              for (int pp = 0; pp < 4; ++pp) {
-                stage[(2 * pp) * 32 + lane] = total[q * 4 + pp].x;
-                stage[(2 * pp + 1) * 32 + lane] = total[q * 4 + pp].y;
-              }
-              if (tma) {
-                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                __syncwarp();
-                if (lane == 0) {
-                  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
-                                   reinterpret_cast<uint64_t>(&out_map)),
-                               "r"(tile * GEMM_ROWS + quad * 32), "r"(m0 + c0 + q * 8), "r"(smem_u32(stage))
-                               : "memory");
-                  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
-                }
-              } else if (valid) {
-#pragma unroll 1
-                for (int j = 0; j < 8; ++j)
-                  if ((store >> (q * 8 + j)) & 1) out[(size_t)(m0 + c0 + q * 8 + j) * out_stride + row] = stage[j * 32 + lane];
-              }
-            }
+            total[pp] = t;
           }
-          // this half's columns are read and reset to the bias: the next tile's MMAs may use them
-          asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
-          asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+          // the finished chunk through the warp's staging buffer: a TMA
+          // tensor store, or (a warp with a token not to store) plain stores
+          // of the live tokens
+          // (an earlier tile's tensor store may still be reading the buffer)
+          if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
           __syncwarp();
-          if (lane == 0) arrive(hempty(h));
+#pragma unroll
+          for (int pp = 0; pp < 4; ++pp) {
+            stage[(2 * pp) * 32 + lane] = total[pp].x;
+            stage[(2 * pp + 1) * 32 + lane] = total[pp].y;
+          }
+          if (tma) {
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            __syncwarp();
+            if (lane == 0) {
+              asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+                               reinterpret_cast<uint64_t>(&out_map)),
+                           "r"(tile * GEMM_ROWS + quad * 32), "r"(m0 + c0 + q * 8), "r"(smem_u32(stage))
+                           : "memory");
+              asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+            }
+          } else if (valid) {
+#pragma unroll 1
+            for (int j = 0; j < 8; ++j)
+              if ((store >> (q * 8 + j)) & 1) out[(size_t)(m0 + c0 + q * 8 + j) * out_stride + row] = stage[j * 32 + lane];
+          }
         }
-        if (!ok) {
-          s_fail = 1;
-          break;
+        // the set's columns are read and reset to the bias; the stage's scales are read
+        asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+        __syncwarp();
+        if (lane == 0) {
+          arrive(aempty(b));
+          arrive(sempty(sc));
         }
-        // the stage's scales are read: the copy of tile i + WIDE_SCALE_STAGES may refill it
-        if (lane == 0) arrive(sempty(sc));
       }
       // the tensor stores have completed before the CTA leaves
       if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
