@@ -40,12 +40,14 @@ def test_product_timing_is_reported(native_built):
 
 
 @pytest.mark.parametrize("cols,rows,bits", [(512, 2048, 2), (512, 8192, 4), (512, 512, 2)])
-@pytest.mark.parametrize("tokens", [256, 300, 1000])
+@pytest.mark.parametrize("tokens", [256, 300, 449, 1000])
 def test_large_pass_product_every_token(native_built, oracle_lib, cols, rows, bits, tokens):
     """Passes of at least 256 tokens through a K = 512 matrix run the
     persistent, pipelined tensor-core product (64-token tiles, two TMEM
-    accumulator sets): every token's row of outputs, a ragged last tile and
-    CTAs that walk several tiles included, bit-exact against the restatement."""
+    accumulator sets, TMA tensor stores of whole 8-token chunks and plain
+    stores where a warp's tokens run past the pass): every token's row of
+    outputs, ragged last tiles (300 = 4·64 + 44, 449 = 7·64 + 1) and CTAs that
+    walk several tiles included, bit-exact against the restatement."""
     from rustyneedle_b200 import debug, synthetic
 
     packed, levels, norms = synthetic.product_matrix(seed=3 * cols + rows + bits, rows=rows, columns=cols, bits=bits)
