@@ -187,6 +187,10 @@ struct Engine {
   std::vector<uint32_t> free_pages;
   std::vector<uint32_t> free_slots;
   std::vector<uint8_t> slot_dirty;
+  // per slot: the page index whose page is private to the slot at every layer
+  // of its session (-1: not known); sharing a page (a clone) or releasing the
+  // slot forgets it
+  std::vector<int32_t> slot_private;
   float* d_hidden = nullptr;  // [slots][d]
   size_t conv_ring_floats = 0;  // per slot: md.conv_ring's [layers][taps - 1][q | k | v]
   std::vector<EngramDev> engram_sites;  // host copies (the layers point at the device copies)
@@ -266,8 +270,9 @@ struct Engine {
 
   // Makes the page that receives `position` of every active layer private to `slot`.
   void prepare_append(uint32_t slot, const std::vector<int32_t>& active, uint32_t position) {
+    const uint32_t index = position / PAGE_POSITIONS;
+    if (slot_private[slot] == (int32_t)index) return;  // most steps: nothing to allocate or copy
     settle();
-    uint32_t index = position / PAGE_POSITIONS;
     for (int32_t layer : active) {
       int32_t& e = page_entry(slot, (uint32_t)layer, index);
       if (e < 0) {
@@ -282,6 +287,7 @@ struct Engine {
         slot_dirty[slot] = 1;
       }
     }
+    slot_private[slot] = (int32_t)index;
   }
 
   void flush_page_tables() {
@@ -781,6 +787,7 @@ std::shared_ptr<Engine> open_engine(const char* path, const nb_options* opt) {
   E->d_page_table = A.alloc<int32_t>(table_entries);
   NB_CUDA(cudaMemcpyAsync(E->d_page_table, E->h_table.p, table_entries * 4, cudaMemcpyHostToDevice, st));
   E->slot_dirty.assign(E->max_sessions, 0);
+  E->slot_private.assign(E->max_sessions, -1);
   for (uint32_t s = E->max_sessions; s-- > 0;) E->free_slots.push_back(s);
   E->d_hidden = A.alloc<float>((size_t)E->max_sessions * d);
   NB_CUDA(cudaMemsetAsync(E->d_hidden, 0, (size_t)E->max_sessions * d * 4, st));
@@ -887,12 +894,12 @@ std::shared_ptr<Engine> open_engine(const char* path, const nb_options* opt) {
   E->h_error.ensure(sizeof(int));
   E->d_logit_scale = A.alloc<float>((size_t)B * (d / GROUP));
   E->d_logits = A.alloc<float>((size_t)B * V);
-  E->d_slots = A.alloc<int32_t>(B);
+  E->d_slots = A.alloc<int32_t>(2 * (size_t)B);  // [slots][active flags]: one upload per step
+  E->d_active = E->d_slots + B;
   E->d_next = A.alloc<uint32_t>(B);
   E->d_peaks = A.alloc<float>((size_t)2 * B);
   E->d_stats = A.alloc<float>((size_t)2 * B);
   E->d_mask = A.alloc<uint32_t>((size_t)B * (V / 32));
-  E->d_active = A.alloc<int32_t>(B);
   E->h_tokens.ensure((size_t)M * 4);
   E->h_meta.ensure((size_t)M * sizeof(TokenMeta));
   E->t_cap = (int)((g.max_seq_len + 3) / 4 * 4);
@@ -1181,6 +1188,7 @@ nb_status nb_session_clone(const nb_session* session, nb_session** out) {
         if (p >= 0) ++E.refcount[p];
       }
     E.slot_dirty[s->slot] = 1;
+    E.slot_private[session->slot] = E.slot_private[s->slot] = -1;  // every page is shared now
     NB_CUDA(cudaMemcpyAsync(E.d_hidden + (size_t)s->slot * E.md.d_model, E.d_hidden + (size_t)session->slot * E.md.d_model,
                             E.md.d_model * 4, cudaMemcpyDeviceToDevice, E.stream));
     const size_t d = E.md.d_model;
@@ -1224,6 +1232,7 @@ void nb_session_release(nb_session* session) {
         p = -1;
       }
     E.slot_dirty[session->slot] = 1;
+    E.slot_private[session->slot] = -1;
     try {
       set_slot_cross(E, session->slot, nullptr);
     } catch (...) {
@@ -1301,6 +1310,7 @@ nb_status nb_cross_memory_create(nb_model* model, const float* encoded, size_t f
     NB_CUDA(cudaMemcpyAsync(m->dev, &h, sizeof h, cudaMemcpyHostToDevice, E.stream));
     queue_error_read(E);
     NB_CUDA(cudaStreamSynchronize(E.stream));
+    E.copies_in_flight = false;  // the staging copies have completed
     raise_device_error(E);
     *out = new nb_cross_memory{m};
   });
@@ -1469,6 +1479,7 @@ static nb_status head_values(nb_session* session, uint32_t code, float* out, siz
     NB_CUDA(cudaMemcpyAsync(staged, project_out ? E.d_head_out : E.d_head_pooled, n * 4, cudaMemcpyDeviceToHost, E.stream));
     queue_error_read(E);
     NB_CUDA(cudaStreamSynchronize(E.stream));
+    E.copies_in_flight = false;  // the staging copies have completed
     raise_device_error(E);
     std::copy(staged, staged + std::min(n, capacity), out);
     if (count) *count = n;
@@ -1554,6 +1565,7 @@ nb_status nb_sessions_feed(nb_session* const* sessions, const uint32_t* const* i
     }
     queue_error_read(E);
     NB_CUDA(cudaStreamSynchronize(E.stream));
+    E.copies_in_flight = false;  // the staging copies have completed
     raise_device_error(E);
     for (size_t i = 0; i < n; ++i) sessions[i]->length += (uint32_t)counts[i];
   });
@@ -1584,6 +1596,7 @@ nb_status nb_session_logits(nb_session* session, float* out, size_t capacity) {
     NB_CUDA(cudaMemcpyAsync(out, E.d_logits, (size_t)V * 4, cudaMemcpyDeviceToHost, E.stream));
     queue_error_read(E);
     NB_CUDA(cudaStreamSynchronize(E.stream));
+    E.copies_in_flight = false;  // the staging copies have completed
     raise_device_error(E);
   });
 }
@@ -1752,7 +1765,11 @@ static uint32_t stage_step(nb_batch* b) {
   const uint32_t B = (uint32_t)b->sessions.size();
   TokenMeta* hm = b->h_meta.as<TokenMeta>();
   int32_t* ha = b->h_active.as<int32_t>();
-  std::vector<int32_t> slots(B);
+  // the slots at [0, B), the active flags at [max_sessions, max_sessions + B):
+  // d_slots and d_active are one device array
+  const size_t flags = E.max_sessions;
+  E.h_misc.ensure((flags + B) * 4);
+  int32_t* slots = E.h_misc.as<int32_t>();
   uint32_t live = 0;
   for (uint32_t i = 0; i < B; ++i) {
     nb_session* s = b->sessions[i];
@@ -1767,11 +1784,9 @@ static uint32_t stage_step(nb_batch* b) {
     }
   }
   E.flush_page_tables();
-  E.h_misc.ensure(B * 4);
-  std::memcpy(E.h_misc.p, slots.data(), B * 4);
-  NB_CUDA(cudaMemcpyAsync(E.d_slots, E.h_misc.p, B * 4, cudaMemcpyHostToDevice, E.stream));
+  std::memcpy(slots + flags, ha, B * 4);
+  NB_CUDA(cudaMemcpyAsync(E.d_slots, slots, (flags + B) * 4, cudaMemcpyHostToDevice, E.stream));
   NB_CUDA(cudaMemcpyAsync(b->d_meta, hm, B * sizeof(TokenMeta), cudaMemcpyHostToDevice, E.stream));
-  NB_CUDA(cudaMemcpyAsync(E.d_active, ha, B * 4, cudaMemcpyHostToDevice, E.stream));
   E.copies_in_flight = true;
   return live;
 }
@@ -1828,6 +1843,7 @@ nb_status nb_batch_step(nb_batch* batch, const uint32_t* mask_bits, uint32_t* ne
     if (stats) NB_CUDA(cudaMemcpyAsync(batch->h_stats.p, E.d_stats, (size_t)B * 8, cudaMemcpyDeviceToHost, E.stream));
     queue_error_read(E);
     NB_CUDA(cudaStreamSynchronize(E.stream));
+    E.copies_in_flight = false;  // the staging copies have completed
     raise_device_error(E);
     const int32_t* ha = batch->h_active.as<int32_t>();
     for (uint32_t i = 0; i < B; ++i) {
@@ -1859,6 +1875,7 @@ nb_status nb_batch_step_device(nb_batch* batch, const uint32_t* mask_bits_device
     NB_CUDA(cudaMemcpyAsync(next_device, batch->d_tokens, B * 4, cudaMemcpyDeviceToDevice, E.stream));
     queue_error_read(E);
     NB_CUDA(cudaStreamSynchronize(E.stream));
+    E.copies_in_flight = false;  // the staging copies have completed
     raise_device_error(E);
     finish_step(batch);
   });
@@ -1900,6 +1917,7 @@ nb_status nb_batch_run(nb_batch* batch, uint32_t steps, const uint32_t* mask_bit
     cudaEventDestroy(start);
     cudaEventDestroy(stop);
     NB_CUDA(cudaStreamSynchronize(E.stream));
+    E.copies_in_flight = false;
     raise_device_error(E);
     if (elapsed_ms) *elapsed_ms = ms;
     for (nb_session* s : batch->sessions) s->length += steps;
