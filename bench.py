@@ -2,7 +2,9 @@
 
 Workload (the reference's batched-decoding configuration): the synthetic
 depth-20 Needle-3 archive (seed 0), 256 independent sequences per GPU with
-prompt lengths uniform in [128, 1024] (seeded per rank), greedy decoding. A
+prompt lengths uniform in [128, 1024] (one stratified draw, the same lengths
+on every rank in a per-rank seeded order, with per-rank seeded ids), greedy
+decoding. A
 step is one batched decode step of every sequence on the GPU: tied logits,
 argmax, and the forward pass of the chosen tokens through all 20 layers with
 the paged int8 KV cache. Sequences are sharded across ranks with no
@@ -425,7 +427,8 @@ def main():
             "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "int8+f32", "data": "synthetic",
             "config": {"workload": "config2: depth-20 synthetic Needle-3 (seed 0), 256 sequences per GPU, prompts "
-                                   "uniform in [128, 1024], greedy decode, paged int8 KV (64-token pages)",
+                                   "uniform in [128, 1024] (stratified: the same lengths on every rank), greedy decode, "
+                                   "paged int8 KV (64-token pages)",
                        "sequences_per_gpu": seqs, "depth": DEPTH, "parallelism": f"dp{world} (sequences sharded)",
                        "l2": "inputs larger than L2 (KV cache ~2 GB per GPU)", "setup_s": round(setup_s, 1),
                        **({"shard": shard} if shard != rank else {})},

@@ -34,12 +34,21 @@ def ranks_from_env() -> Ranks:
 
 def shard_prompts(rank: int, count: int, low: int = 128, high: int = 1024, seed_base: int = 1000,
                   id_low: int = 10, id_high: int = 8000) -> list[np.ndarray]:
-    """The `count` prompts of `rank`'s shard: lengths uniform in [low, high],
-    ids uniform in [id_low, id_high); seeded per rank, so a rank's shard does
-    not depend on the number of ranks (weak scaling)."""
-    rng = np.random.default_rng(seed_base + rank)
-    lengths = rng.integers(low, high + 1, count)
-    return [rng.integers(id_low, id_high, n).astype(np.uint32) for n in lengths]
+    """The `count` prompts of `rank`'s shard.
+
+    Lengths are uniform in [low, high] as a stratified draw: one length from
+    each of `count` equal strata of the range, drawn once from `seed_base`,
+    so every rank holds the same multiset of lengths and caches the same
+    number of positions (weak scaling with equal work per GPU; independent
+    draws per rank left up to 7 % more KV on one rank than another). Their
+    order and the ids (uniform in [id_low, id_high)) are seeded per rank, so
+    a rank's shard does not depend on the number of ranks."""
+    span = high - low + 1
+    offsets = np.random.default_rng(seed_base).random(count)
+    lengths = low + np.floor((np.arange(count) + offsets) * span / count).astype(np.int64)
+    rng = np.random.default_rng([seed_base, rank])
+    lengths = rng.permutation(lengths)
+    return [rng.integers(id_low, id_high, int(n)).astype(np.uint32) for n in lengths]
 
 
 def kv_pages_for(prompts: list[np.ndarray], extra_tokens: int, layers: int, spare_per_layer: int = 40) -> int:

@@ -10,7 +10,8 @@ against the CPU restatement.
   config 1  depth 20, batch 1, a 512-token prompt, 256 greedy steps each under
             a seeded bitset allowing ~5 % of the 8192 ids
   config 2  depth 20, 256 sequences per GPU, prompts uniform in [128, 1024]
-            (seeded per rank: `dp.shard_prompts`), greedy
+            (a stratified draw of lengths shared by every rank, order and
+            ids seeded per rank: `dp.shard_prompts`), greedy
   config 4  a depth-8 Whistle decoder, 64 utterances, each cross-attending to
             its own 1500 x 512 N(0, 1) encoder output; bos and a language
             token, then 224 greedy text tokens
