@@ -352,6 +352,22 @@ def test_clone_shares_the_prefix_copy_on_write(device_model, oracle_model, oracl
     ob.push(12)
     assert _bits_equal(a.logits(), oa.logits()) and _bits_equal(b.logits(), ob.logits())
     assert _bits_equal(base.logits(), o.logits())
+    # the original steps after the clones, through batch steps: it was the
+    # private owner of its last page before the clones shared it, so its next
+    # write must copy that page first and leave the clones' positions alone
+    batch = nb.Batch(model, [base])
+    for _ in range(3):
+        got = int(batch.step()[0])
+        want = oracle_lib.argmax(o.logits())
+        o.push(want)
+        assert got == want
+    batch.close()
+    assert _bits_equal(base.logits(), o.logits())
+    a.push(13)
+    oa.push(13)
+    b.push(14)
+    ob.push(14)
+    assert _bits_equal(a.logits(), oa.logits()) and _bits_equal(b.logits(), ob.logits())
 
 
 def test_chunked_prefill_is_exact(archive_path, oracle_model, oracle_lib):
