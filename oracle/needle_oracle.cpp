@@ -2196,6 +2196,22 @@ int nbo_product_raw(int mode, uint32_t bits, const uint8_t* packed, const float*
   });
 }
 
+// One head's attention (attend_head) over `count` cached positions given
+// directly: keys and values [count][dim] int8, their scales [count].
+int nbo_attend_head_raw(int mode, const int8_t* query, float query_scale, const int8_t* keys, const float* key_scales,
+                        const int8_t* values, const float* value_scales, size_t count, size_t dim, float* out) {
+  return guard([&] {
+    if (!query || !keys || !key_scales || !values || !value_scales || !out || count == 0 || dim == 0)
+      throw Failure(ERR_ARGUMENT, "a raw attention takes a query, at least one position and a head width");
+    Cache cache;
+    cache.keys.assign(keys, keys + count * dim);
+    cache.values.assign(values, values + count * dim);
+    cache.key_scales.assign(1, std::vector<float>(key_scales, key_scales + count));
+    cache.value_scales.assign(1, std::vector<float>(value_scales, value_scales + count));
+    attend_head(query, query_scale, cache, 0, 1, dim, dim, 0, count, mode, out);
+  });
+}
+
 int nbo_matrix_dequantise_row(const nbo_model* model, int tensor, size_t row, float* out) {
   return guard([&] {
     QMatrix m = load_matrix(*model->archive, (size_t)tensor);

@@ -120,6 +120,10 @@ int nbo_tensor_info(const nbo_model* model, int tensor, int64_t* out5);
  * sums (may be NULL) receives the INT path's per-group int32 sums. */
 int nbo_product_raw(int mode, uint32_t bits, const uint8_t* packed, const float* levels, const uint16_t* norms, size_t rows,
                     size_t cols, const float* input, float* out, int32_t* sums);
+/* attend_head (crates/kernels/src/attention.rs:53-77) of one head over count
+   positions given directly: keys, values [count][dim] int8; scales [count]. */
+int nbo_attend_head_raw(int mode, const int8_t* query, float query_scale, const int8_t* keys, const float* key_scales,
+                        const int8_t* values, const float* value_scales, size_t count, size_t dim, float* out);
 /* HadamardWeights::apply of one layer (crates/model/src/hadamard.rs:260-304). */
 int nbo_hadamard_apply(const nbo_model* model, int layer, const float* input, float* out);
 

@@ -88,6 +88,7 @@ def _declare(L: ctypes.CDLL) -> None:
         "nbo_product_raw": (I, [I, U32, P, P, P, SZ, SZ, P, P, P]),
         "nbo_tensor_info": (I, [P, I, P]),
         "nbo_hadamard_apply": (I, [P, I, P, P]),
+        "nbo_attend_head_raw": (I, [I, P, F, P, P, P, P, SZ, SZ, P]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -267,6 +268,23 @@ def product_raw(mode: int, bits: int, packed: np.ndarray, levels: np.ndarray, no
     xv = np.ascontiguousarray(x, dtype=np.float32)
     out = np.zeros(rows, dtype=np.float32)
     status = lib().nbo_product_raw(mode, bits, _ptr(p), _ptr(lv), _ptr(nm), rows, cols, _ptr(xv), _ptr(out), None)
+    if status != 0:
+        raise RuntimeError(lib().nbo_last_error().decode())
+    return out
+
+
+def attend_head_raw(mode: int, query: np.ndarray, query_scale: float, keys: np.ndarray, key_scales: np.ndarray,
+                    values: np.ndarray, value_scales: np.ndarray) -> np.ndarray:
+    """One head's attention over positions given directly (keys, values
+    [count][dim] int8; their scales [count])."""
+    q = np.ascontiguousarray(query, dtype=np.int8)
+    k = np.ascontiguousarray(keys, dtype=np.int8)
+    v = np.ascontiguousarray(values, dtype=np.int8)
+    ks = np.ascontiguousarray(key_scales, dtype=np.float32)
+    vs = np.ascontiguousarray(value_scales, dtype=np.float32)
+    count, dim = k.shape
+    out = np.zeros(dim, dtype=np.float32)
+    status = lib().nbo_attend_head_raw(mode, _ptr(q), float(query_scale), _ptr(k), _ptr(ks), _ptr(v), _ptr(vs), count, dim, _ptr(out))
     if status != 0:
         raise RuntimeError(lib().nbo_last_error().decode())
     return out

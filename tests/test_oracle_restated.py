@@ -1,0 +1,110 @@
+"""The C++ restatement (oracle/needle_oracle.cpp, INT mode) against a second,
+independent numpy restatement written from the reference's Rust
+(oracle/restated.py), on the composite paths that no reference test vector
+pins: codebook products with their per-group combine, one head's attention
+with 12-bit value weights, the Sinkhorn mixing and the grammar step's
+allowed statistics. Seeded random inputs; bit-exact. CPU only."""
+
+from fractions import Fraction
+
+import numpy as np
+import pytest
+
+from oracle import restated
+
+
+def _exact_f32(value: Fraction) -> np.float32:
+    """Round an exact rational to the nearest f32 (ties to even)."""
+    if value == 0:
+        return np.float32(0.0)
+    sign = -1 if value < 0 else 1
+    a = abs(value)
+    e = a.numerator.bit_length() - a.denominator.bit_length()
+    while Fraction(2) ** e > a:
+        e -= 1
+    while Fraction(2) ** (e + 1) <= a:
+        e += 1
+    k = max(e - 23, -149)  # the f32 spacing at this magnitude
+    q = a / Fraction(2) ** k
+    n = q.numerator // q.denominator
+    r = q - n
+    if r > Fraction(1, 2) or (r == Fraction(1, 2) and n % 2 == 1):
+        n += 1
+    return np.float32(sign * float(n * Fraction(2) ** k))
+
+
+def test_fused_multiply_add_rounds_once():
+    rng = np.random.default_rng(5)
+    a = rng.standard_normal(3000).astype(np.float32) * np.float32(1000)
+    b = rng.standard_normal(3000).astype(np.float32) * np.float32(1e-3)
+    c = rng.standard_normal(3000).astype(np.float32)
+    # halfway cases: c + (an exact f32 half-ulp) + a tiny product of the other sign
+    ulp = np.spacing(np.float32(1.0))
+    a[:4] = [np.float32(ulp / 2), np.float32(ulp / 2), np.float32(ulp / 2), np.float32(ulp / 2)]
+    b[:4] = [np.float32(1.0) + np.float32(2.0**-20), np.float32(1.0) - np.float32(2.0**-21), 1.0, -1.0]
+    c[:4] = [1.0, 1.0, 1.0, 1.0]
+    got = restated.fma_f32(a, b, c)
+    for i in range(a.size):
+        want = _exact_f32(Fraction(float(a[i])) * Fraction(float(b[i])) + Fraction(float(c[i])))
+        assert got[i] == want, (i, a[i], b[i], c[i], got[i], want)
+
+
+def _levels(rng, bits):
+    half = np.sort(np.abs(rng.standard_normal(1 << (bits - 1)))).astype(np.float32) + np.float32(0.05)
+    return np.concatenate([-half[::-1], half]).astype(np.float32)
+
+
+@pytest.mark.parametrize("bits,rows,cols", [(2, 96, 512), (2, 37, 1024), (4, 64, 512), (4, 33, 2048)])
+def test_codebook_products(oracle_lib, bits, rows, cols):
+    rng = np.random.default_rng(bits * 1000 + rows)
+    packed = rng.integers(0, 256, rows * cols * bits // 8, dtype=np.uint8)
+    levels = _levels(rng, bits)
+    norms = (rng.uniform(1e-3, 2e-2, rows * (cols // 128))).astype(np.float16).view(np.uint16)
+    for trial in range(3):
+        x = rng.standard_normal(cols).astype(np.float32) * np.float32(3.0 ** trial)
+        if trial == 2:
+            x[128:256] = 0.0  # a zero group: activation scale 1
+        want = oracle_lib.product_raw(oracle_lib.MODE_INT, bits, packed, levels, norms, rows, cols, x)
+        got = restated.product_int(bits, packed, levels, norms, rows, cols, x)
+        assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), (bits, trial, np.flatnonzero(got != want)[:5])
+
+
+@pytest.mark.parametrize("count", [1, 3, 4, 5, 63, 64, 257, 1000, 2048])
+def test_attention_head(oracle_lib, count):
+    rng = np.random.default_rng(count)
+    dim = 64
+    for trial in range(3):
+        q = rng.integers(-127, 128, dim).astype(np.int8)
+        keys = rng.integers(-127, 128, (count, dim)).astype(np.int8)
+        values = rng.integers(-127, 128, (count, dim)).astype(np.int8)
+        ks = rng.uniform(1e-3, 3e-2, count).astype(np.float32)
+        vs = rng.uniform(1e-3, 3e-2, count).astype(np.float32)
+        qs = np.float32(rng.uniform(1e-3, 2e-2) / 8.0)
+        if trial == 2:
+            ks[: count // 2] *= np.float32(10.0)  # a sharper softmax: many weights round to zero
+        want = oracle_lib.attend_head_raw(oracle_lib.MODE_INT, q, qs, keys, ks, values, vs)
+        got = restated.attend_head_int(q, qs, keys, ks, values, vs)
+        assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), (count, trial, np.flatnonzero(got != want)[:5])
+
+
+def test_sinkhorn(oracle_lib):
+    rng = np.random.default_rng(9)
+    for trial in range(20):
+        logits = (rng.standard_normal(16) * (0.5 + trial)).astype(np.float32)
+        want = oracle_lib.sinkhorn(logits, 4)
+        got = restated.sinkhorn(logits, 4)
+        assert np.array_equal(np.asarray(got).view(np.uint32), np.asarray(want, dtype=np.float32).view(np.uint32)), trial
+
+
+def test_allowed_statistics(oracle_lib):
+    rng = np.random.default_rng(13)
+    vocab = 8192
+    for trial in range(6):
+        logits = (rng.standard_normal(vocab) * (1.0 + 3 * trial)).astype(np.float32)
+        allowed = rng.random(vocab) < (0.05 if trial % 2 else 0.6)
+        allowed[rng.integers(0, vocab)] = True
+        ids = np.flatnonzero(allowed)
+        token = int(ids[rng.integers(0, ids.size)])
+        want = oracle_lib.allowed_statistics(logits, token, allowed)
+        got = restated.allowed_statistics(logits, token, allowed)
+        assert np.float32(want[0]) == got[0] and np.float32(want[1]) == got[1], (trial, want, got)
