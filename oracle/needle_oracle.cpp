@@ -2232,6 +2232,17 @@ int nbo_tensor_info(const nbo_model* model, int tensor, int64_t* o) {
   return OK;
 }
 
+int nbo_route(const nbo_model* model, int layer, int slot, const float* stream, float* input, float* post, float* residual) {
+  return guard([&] {
+    if (!model || !stream || !input || !post || !residual || layer < 0 || slot < 0)
+      throw Failure(ERR_ARGUMENT, "a route takes a model, a layer, a slot, the lane stream and three outputs");
+    Routing r = route(model, (size_t)layer, (size_t)slot, stream, model->archive->geo.d_model);
+    std::memcpy(input, r.input.data(), r.input.size() * sizeof(float));
+    std::memcpy(post, r.post.data(), r.post.size() * sizeof(float));
+    std::memcpy(residual, r.residual.data(), r.residual.size() * sizeof(float));
+  });
+}
+
 int nbo_hadamard_apply(const nbo_model* model, int layer, const float* input, float* out) {
   return guard([&] {
     const LayerW& W = model->weights->layers.at((size_t)layer);

@@ -124,6 +124,9 @@ int nbo_product_raw(int mode, uint32_t bits, const uint8_t* packed, const float*
    positions given directly: keys, values [count][dim] int8; scales [count]. */
 int nbo_attend_head_raw(int mode, const int8_t* query, float query_scale, const int8_t* keys, const float* key_scales,
                         const int8_t* values, const float* value_scales, size_t count, size_t dim, float* out);
+/* LaneWeights::route of one layer for the session in `slot` (crates/model/src/lanes.rs:45-80):
+   stream [lanes][d_model]; input [d_model], post [lanes], residual [lanes][lanes]. */
+int nbo_route(const nbo_model* model, int layer, int slot, const float* stream, float* input, float* post, float* residual);
 /* HadamardWeights::apply of one layer (crates/model/src/hadamard.rs:260-304). */
 int nbo_hadamard_apply(const nbo_model* model, int layer, const float* input, float* out);
 

@@ -174,6 +174,18 @@ class Model:
             raise OracleError(status)
         return out
 
+    def route(self, layer: int, slot: int, stream: np.ndarray):
+        """LaneWeights::route: (block input [d], post gates [lanes], residual mixing [lanes·lanes])."""
+        s = np.ascontiguousarray(stream, dtype=np.float32)
+        lanes = s.size // self.d_model
+        block_input = np.zeros(self.d_model, dtype=np.float32)
+        post = np.zeros(lanes, dtype=np.float32)
+        residual = np.zeros(lanes * lanes, dtype=np.float32)
+        status = lib().nbo_route(self._h, layer, slot, _ptr(s), _ptr(block_input), _ptr(post), _ptr(residual))
+        if status:
+            raise OracleError(status)
+        return block_input, post, residual
+
     def __del__(self):
         if getattr(self, "_h", None) and _lib is not None:
             _lib.nbo_model_free(self._h)

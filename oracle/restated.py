@@ -6,7 +6,10 @@ the C++ restatement in needle_oracle.cpp calls INT mode) and is used by
 tests/test_oracle_restated.py to cross-check that restatement on the paths
 no reference test vector pins: the codebook products with their per-group
 combine, one head's attention with its 12-bit value weights, the Sinkhorn
-mixing and the grammar step's allowed statistics. Every function names the
+mixing, the grammar step's allowed statistics, a layer's Hadamard block
+(condition softmax, modulation, three Kronecker factor pairs) and its lane
+routing (the phi products, the gates with the own-lane offsets). It reads
+the archive with its own reader. Every function names the
 reference lines it follows. Arithmetic is f32 throughout, one rounding per
 Rust operation, in the Rust order.
 """
@@ -274,3 +277,214 @@ def allowed_statistics(logits: np.ndarray, token: int, allowed: np.ndarray):
     probability = F32(fast_exp(np.array([x[token] - peak_allowed], dtype=np.float32))[0] / total_allowed)
     mass = F32(F32(total_allowed * fast_exp(np.array([peak_allowed - peak_all], dtype=np.float32))[0]) / total_all)
     return probability, mass
+
+
+# ------------------------------------------------------------ archive reader
+class Archive:
+    """The tensors of a .cact file, read with numpy (crates/cact/src/geometry.rs:41-90,
+    record.rs:38-50): 48 u32 header fields (the tensor count second, the
+    codebook length third) and the f32 rope theta, 196 bytes; the codebook
+    floats; one 44-byte record per tensor (kind u8, rank u8, u16, four u32
+    dims, u64 offset, u64 byte length, u32 group, u32 bits); tensor bytes at
+    their offsets. The tensors come in the order of crates/cact/src/layout.rs:
+    the embedding, then per layer norm_in, q/k/v, [3 conv taps], q_norm,
+    k_norm, gate_proj, out_proj, post_norm, attn_gate, pre_hada and 13
+    Hadamard tensors (:199-210), then the 9 lane tensors and the two
+    Hadamard permutations (:186-189)."""
+
+    HEADER_BYTES, RECORD_BYTES = 196, 44
+    SINGLE, CODEBOOK = 2, 3
+
+    def __init__(self, path: str):
+        import struct
+
+        with open(path, "rb") as f:
+            self.data = f.read()
+        fields = struct.unpack_from("<48I", self.data, 0)
+        self.count, codebook_len = fields[1], fields[2]
+        self.layers, self.d_model, self.lanes, self.conv_taps = fields[10], fields[7], fields[15], fields[19]
+        self.codebook = np.frombuffer(self.data, "<f4", codebook_len, self.HEADER_BYTES).astype(np.float32)
+        at = self.HEADER_BYTES + codebook_len * 4
+        self.records = [struct.unpack_from("<BBH4IQQII", self.data, at + self.RECORD_BYTES * i) for i in range(self.count)]
+
+    def floats(self, index: int) -> np.ndarray:
+        kind, rank, _, *rest = self.records[index]
+        offset, nbytes = rest[4], rest[5]
+        assert kind == self.SINGLE, (index, kind)
+        return np.frombuffer(self.data, "<f4", nbytes // 4, offset).astype(np.float32)
+
+    def codebook_matrix(self, index: int):
+        """(bits, packed [rows × row bytes], the 2^bits levels, fp16 norms, rows, columns)."""
+        kind, rank, _, rows, cols, _, _, offset, nbytes, group, bits = self.records[index]
+        assert kind == self.CODEBOOK and group == GROUP, (index, kind, group)
+        packed_len = rows * cols * bits // 8
+        packed = np.frombuffer(self.data, np.uint8, packed_len, offset)
+        norms = np.frombuffer(self.data, "<u2", (nbytes - packed_len) // 2, offset + packed_len)
+        first = {2: 0, 3: 4, 4: 12}[bits]  # two-, three-, four-bit levels (crates/kernels/src/codebook.rs:13-19)
+        return bits, packed, self.codebook[first:first + (1 << bits)], norms, rows, cols
+
+    def layer_base(self, layer: int) -> int:
+        return 1 + layer * (21 + (3 if self.conv_taps else 0) + 3)
+
+    def hadamard(self, layer: int):
+        base = self.layer_base(layer) + (14 if self.conv_taps else 11)
+        names = ("d1", "d2", "b2", "d3", "d4", "w1a", "w1b", "w2a", "w2b", "w3a", "w3b", "cond_v", "cond_u")
+        t = {name: self.floats(base + i) for i, name in enumerate(names)}
+        lanes = self.layer_base(self.layers)
+        t["perms"] = [self.floats(lanes + 9).astype(np.int64), self.floats(lanes + 10).astype(np.int64)]
+        return t
+
+    def lane_tensors(self):
+        base = self.layer_base(self.layers)
+        names = ("a_pre", "a_post", "a_res", "b_pre", "b_post", "b_res")
+        t = {name: self.floats(base + i) for i, name in enumerate(names)}
+        for i, name in enumerate(("phi_pre", "phi_post", "phi_res")):
+            t[name] = self.codebook_matrix(base + 6 + i)
+        return t
+
+
+# --------------------------------------------------------- Hadamard block
+def kronecker32(values: np.ndarray, left: np.ndarray, right: np.ndarray) -> np.ndarray:
+    """kronecker_apply_fixed::<32> (crates/kernels/src/ops.rs:143-163), the
+    form both architectures run when the left factor is not 32 wide: mixed
+    row i = Σ_j x[i][j] · right[j] in j order, then output row k =
+    Σ_i left[i][k] · mixed[i] in i order; every sum from +0.0, a multiply and
+    an add per term."""
+    R = 32
+    left_size = int(round(math.sqrt(left.size)))
+    x = np.asarray(values, dtype=np.float32).reshape(left_size, R)
+    rt = np.asarray(right, dtype=np.float32).reshape(R, R)
+    lf = np.asarray(left, dtype=np.float32).reshape(left_size, left_size)
+    mixed = np.zeros((left_size, R), dtype=np.float32)
+    for j in range(R):
+        mixed = (mixed + (x[:, j:j + 1] * rt[j][None, :]).astype(np.float32)).astype(np.float32)
+    out = np.zeros((left_size, R), dtype=np.float32)
+    for i in range(left_size):
+        out = (out + (lf[i][:, None] * mixed[i][None, :]).astype(np.float32)).astype(np.float32)
+    return out.reshape(-1)
+
+
+def silu(values: np.ndarray) -> np.ndarray:
+    """ops::silu (crates/kernels/src/ops.rs:74-76): x / (1 + fast_exp(-x))."""
+    v = np.asarray(values, dtype=np.float32)
+    return (v / (F32(1.0) + fast_exp(-v)).astype(np.float32)).astype(np.float32)
+
+
+def hadamard_apply(t: dict, x: np.ndarray) -> np.ndarray:
+    """HadamardWeights::apply (crates/model/src/hadamard.rs:55-99).
+
+    Condition weights: with rank 8, four chains (dimension d feeds chain
+    d mod 4, in order) of products with cond_v, then the chains added in
+    order; softmax_in_place (ops.rs:92-101) of them; the modulation
+    1 + Σ_rank weight · cond_u. The input padded to the factor size, times
+    d1, through factor pair 1, gathered by the first permutation,
+    silu(d2 · modulation · gathered + b2), factor pair 2, the second
+    permutation, times d3, factor pair 3, times d4, the first width kept."""
+    x = np.asarray(x, dtype=np.float32)
+    width, size = x.size, t["d1"].size
+    rank = t["cond_u"].size // size
+    cond_v = t["cond_v"].reshape(width, rank)
+    weights = np.zeros(rank, dtype=np.float32)
+    if rank == 8:
+        chains = np.zeros((4, rank), dtype=np.float32)
+        for d in range(width):
+            chains[d % 4] = (chains[d % 4] + (x[d] * cond_v[d]).astype(np.float32)).astype(np.float32)
+        for c in range(4):
+            weights = (weights + chains[c]).astype(np.float32)
+    else:
+        for d in range(width):
+            weights = (weights + (x[d] * cond_v[d]).astype(np.float32)).astype(np.float32)
+    peak = weights.max()
+    e = fast_exp((weights - peak).astype(np.float32))
+    total = F32(0.0)
+    for v in e:
+        total = F32(total + v)
+    weights = (e * F32(F32(1.0) / total)).astype(np.float32)
+    cond_u = t["cond_u"].reshape(rank, size)
+    modulation = np.ones(size, dtype=np.float32)
+    for r in range(rank):
+        modulation = (modulation + (weights[r] * cond_u[r]).astype(np.float32)).astype(np.float32)
+    padded = np.zeros(size, dtype=np.float32)
+    padded[:width] = x
+    first = kronecker32((padded * t["d1"]).astype(np.float32), t["w1a"], t["w1b"])
+    gathered = first[t["perms"][0]]
+    inner = (((t["d2"] * modulation).astype(np.float32) * gathered).astype(np.float32) + t["b2"]).astype(np.float32)
+    second = kronecker32(silu(inner), t["w2a"], t["w2b"])
+    third = kronecker32((second[t["perms"][1]] * t["d3"]).astype(np.float32), t["w3a"], t["w3b"])
+    return (third * t["d4"]).astype(np.float32)[:width]
+
+
+# ------------------------------------------------------------------ routing
+def sum_of_squares(values: np.ndarray) -> np.float32:
+    """ops::sum_of_squares (crates/kernels/src/ops.rs:7-17): eight lanes of
+    every eighth square, the lanes summed in order from -0.0, plus the tail."""
+    v = np.asarray(values, dtype=np.float32)
+    whole = v.size - v.size % 8
+    lanes = np.zeros(8, dtype=np.float32)
+    for i in range(0, whole, 8):
+        lanes = (lanes + (v[i:i + 8] * v[i:i + 8]).astype(np.float32)).astype(np.float32)
+    total = F32(-0.0)
+    for lane in lanes:
+        total = F32(total + lane)
+    tail = F32(-0.0)
+    for value in v[whole:]:
+        tail = F32(tail + F32(value * value))
+    return F32(total + tail)
+
+
+def unit_rms(values: np.ndarray) -> np.ndarray:
+    """ops::unit_rms (crates/kernels/src/ops.rs:60-66), epsilon 1e-6."""
+    v = np.asarray(values, dtype=np.float32)
+    mean_square = F32(sum_of_squares(v) / F32(v.size))
+    inverse = F32(F32(1.0) / np.sqrt(F32(mean_square + F32(1e-6))))
+    return (v * inverse).astype(np.float32)
+
+
+def fake_quantise_int8(values: np.ndarray) -> np.ndarray:
+    """ops::fake_quantise_int8 (crates/kernels/src/ops.rs:120-125)."""
+    v = np.asarray(values, dtype=np.float32)
+    peak = peak_magnitude(v)
+    scale = F32(peak / F32(127.0)) if peak > 0 else F32(1.0)
+    return (np.clip(np.rint((v / scale).astype(np.float32)), -128, 127).astype(np.float32) * scale).astype(np.float32)
+
+
+def sigmoid(value) -> np.float32:
+    """ops::sigmoid (crates/kernels/src/ops.rs:69-71) with libm's expf."""
+    return F32(F32(1.0) / F32(F32(1.0) + expf(-F32(value))))
+
+
+def product_rows(matrix, first_row: int, rows: int, x: np.ndarray) -> np.ndarray:
+    """Rows first_row.. of a codebook matrix times x (multiply_fused,
+    crates/kernels/src/matrix.rs:167-193, row by row as product_int)."""
+    bits, packed, levels, norms, all_rows, cols = matrix
+    row_bytes = cols * bits // 8
+    groups = cols // GROUP
+    return product_int(bits, packed[first_row * row_bytes:(first_row + rows) * row_bytes], levels,
+                       norms[first_row * groups:(first_row + rows) * groups], rows, cols, x)
+
+
+def route(lt: dict, lanes: int, layer: int, slot: int, stream: np.ndarray):
+    """LaneWeights::route (crates/model/src/lanes.rs:45-80): the stream
+    unit-normalised and fake-quantised; the phi products of this layer's
+    rows; the pre gates sigmoid(a_pre · pre + b_pre + offset) (own lane
+    8 - 4, others -4), the block input Σ_lane gate · lane from +0.0; the post
+    gates 2 · sigmoid(a_post · post + b_post + offset) (own lane 0, others
+    -4); the residual mixing a_res · r + b_res through the Sinkhorn."""
+    s = np.asarray(stream, dtype=np.float32)
+    width = s.size // lanes
+    normalised = fake_quantise_int8(unit_rms(s))
+    pre = product_rows(lt["phi_pre"], layer * lanes, lanes, normalised)
+    post = product_rows(lt["phi_post"], layer * lanes, lanes, normalised)
+    residual = product_rows(lt["phi_res"], layer * lanes * lanes, lanes * lanes, normalised)
+    own = slot % lanes
+    block_input = np.zeros(width, dtype=np.float32)
+    post_gates = np.zeros(lanes, dtype=np.float32)
+    for lane in range(lanes):
+        pre_offset = F32(8.0 + -4.0) if lane == own else F32(-4.0)
+        gate = sigmoid(F32(F32(F32(lt["a_pre"][layer] * pre[lane]) + lt["b_pre"][layer * lanes + lane]) + pre_offset))
+        block_input = (block_input + (gate * s[lane * width:(lane + 1) * width]).astype(np.float32)).astype(np.float32)
+        post_offset = F32(0.0) if lane == own else F32(-4.0)
+        post_gates[lane] = F32(2.0) * sigmoid(F32(F32(F32(lt["a_post"][layer] * post[lane]) + lt["b_post"][layer * lanes + lane]) + post_offset))
+    base = layer * lanes * lanes
+    mixed = ((lt["a_res"][layer] * residual).astype(np.float32) + lt["b_res"][base:base + lanes * lanes]).astype(np.float32)
+    return block_input, post_gates, sinkhorn(mixed, lanes)

@@ -2,8 +2,9 @@
 independent numpy restatement written from the reference's Rust
 (oracle/restated.py), on the composite paths that no reference test vector
 pins: codebook products with their per-group combine, one head's attention
-with 12-bit value weights, the Sinkhorn mixing and the grammar step's
-allowed statistics. Seeded random inputs; bit-exact. CPU only."""
+with 12-bit value weights, the Sinkhorn mixing, the grammar step's allowed
+statistics, and, with the archive's own weights, a layer's Hadamard block and
+its lane routing. Seeded random inputs; bit-exact. CPU only."""
 
 from fractions import Fraction
 
@@ -108,3 +109,44 @@ def test_allowed_statistics(oracle_lib):
         want = oracle_lib.allowed_statistics(logits, token, allowed)
         got = restated.allowed_statistics(logits, token, allowed)
         assert np.float32(want[0]) == got[0] and np.float32(want[1]) == got[1], (trial, want, got)
+
+
+def test_archive_reader_sees_the_layout(small_archive_path):
+    arch = restated.Archive(small_archive_path)
+    t = arch.hadamard(3)
+    n = t["d1"].size
+    assert n == 2048 and t["w1a"].size == 64 * 64 and t["w1b"].size == 32 * 32 and t["cond_v"].size == 512 * 8
+    assert t["cond_u"].size == 8 * n and sorted(t["perms"][0]) == list(range(n))
+    lt = arch.lane_tensors()
+    assert lt["a_pre"].size == arch.layers and lt["phi_res"][4] == arch.layers * arch.lanes * arch.lanes
+
+
+@pytest.mark.parametrize("layer", [0, 3])
+def test_hadamard_block(oracle_lib, small_archive_path, layer):
+    """HadamardWeights::apply with the archive's factors, read by each
+    restatement's own archive reader."""
+    arch = restated.Archive(small_archive_path)
+    model = oracle_lib.Model.open(small_archive_path, oracle_lib.MODE_INT)
+    rng = np.random.default_rng(40 + layer)
+    t = arch.hadamard(layer)
+    for trial in range(3):
+        x = (rng.standard_normal(arch.d_model) * (0.3 + trial)).astype(np.float32)
+        want = model.hadamard(layer, x)
+        got = restated.hadamard_apply(t, x)
+        assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), (layer, trial, np.flatnonzero(got != want)[:5])
+
+
+@pytest.mark.parametrize("layer,slot", [(0, 0), (1, 5), (3, 2)])
+def test_routing(oracle_lib, small_archive_path, layer, slot):
+    """LaneWeights::route: the phi products through the archive's 4-bit lane
+    maps, the gates with the session's own-lane offsets, the Sinkhorn."""
+    arch = restated.Archive(small_archive_path)
+    model = oracle_lib.Model.open(small_archive_path, oracle_lib.MODE_INT)
+    lt = arch.lane_tensors()
+    rng = np.random.default_rng(70 + layer * 8 + slot)
+    for trial in range(3):
+        stream = (rng.standard_normal(arch.lanes * arch.d_model) * (0.5 + trial)).astype(np.float32)
+        want = model.route(layer, slot, stream)
+        got = restated.route(lt, arch.lanes, layer, slot, stream)
+        for name, g, w in zip(("input", "post", "residual"), got, want):
+            assert np.array_equal(np.asarray(g, dtype=np.float32).view(np.uint32), w.view(np.uint32)), (name, trial)
