@@ -8,8 +8,10 @@ no reference test vector pins: the codebook products with their per-group
 combine, one head's attention with its 12-bit value weights, the Sinkhorn
 mixing, the grammar step's allowed statistics, a layer's Hadamard block
 (condition softmax, modulation, three Kronecker factor pairs) and its lane
-routing (the phi products, the gates with the own-lane offsets). It reads
-the archive with its own reader. Every function names the
+routing (the phi products, the gates with the own-lane offsets), and from
+them a whole token: Session::push (every layer's lane stream) and
+Session::logits. It reads the archive with its own reader. Every function
+names the
 reference lines it follows. Arithmetic is f32 throughout, one rounding per
 Rust operation, in the Rust order.
 """
@@ -488,3 +490,159 @@ def route(lt: dict, lanes: int, layer: int, slot: int, stream: np.ndarray):
     base = layer * lanes * lanes
     mixed = ((lt["a_res"][layer] * residual).astype(np.float32) + lt["b_res"][base:base + lanes * lanes]).astype(np.float32)
     return block_input, post_gates, sinkhorn(mixed, lanes)
+
+
+# ------------------------------------------------------------ a whole token
+_libm.sinf.restype = _libm.cosf.restype = _libm.powf.restype = ctypes.c_float
+_libm.sinf.argtypes = _libm.cosf.argtypes = [ctypes.c_float]
+_libm.powf.argtypes = [ctypes.c_float, ctypes.c_float]
+
+
+def zero_centred_norm(values: np.ndarray, gains: np.ndarray) -> np.ndarray:
+    """ops::zero_centred_norm (crates/kernels/src/ops.rs:44-58): (1 + gain) · x · inverse RMS."""
+    v = np.asarray(values, dtype=np.float32)
+    mean_square = F32(sum_of_squares(v) / F32(v.size))
+    inverse = F32(F32(1.0) / np.sqrt(F32(mean_square + F32(1e-6))))
+    return (((F32(1.0) + np.asarray(gains, dtype=np.float32)) * v).astype(np.float32) * inverse).astype(np.float32)
+
+
+def quantise_int8(values: np.ndarray):
+    """ops::quantise_int8 (crates/kernels/src/ops.rs:111-118): codes and scale."""
+    v = np.asarray(values, dtype=np.float32)
+    peak = peak_magnitude(v)
+    scale = F32(peak / F32(127.0)) if peak > 0 else F32(1.0)
+    return np.clip(np.rint((v / scale).astype(np.float32)), -128, 127).astype(np.int64), scale
+
+
+class Session:
+    """Session::push and Session::logits (crates/model/src/session.rs:78-175)
+    of an archive without engram sites, conv taps or probe heads, on the
+    integer kernels: the embedding row (dequantised and rotated back, times
+    sqrt(d)) in every lane; per layer the routing, the attention
+    (AttentionWeights::attend, crates/model/src/attention.rs:98-158, with the
+    cache's int8 keys and values), the gated residual, the Hadamard block,
+    the block delta and the lane combine (lanes.rs:82-104); the lane mean
+    through the final norm; the logits through the tied embedding."""
+
+    def __init__(self, archive: Archive):
+        import struct
+
+        a = self.archive = archive
+        fields = struct.unpack_from("<48I", a.data, 0)
+        self.heads, self.kv_heads, self.head_dim = fields[8], fields[9], fields[11]
+        self.sliding_window, self.global_layers = fields[16], fields[17] | fields[18] << 32
+        theta = F32(struct.unpack_from("<f", a.data, 192)[0])
+        half = self.head_dim // 2
+        self.frequencies = np.array(
+            [F32(F32(1.0) / F32(_libm.powf(float(theta), float(F32(F32(2.0 * i) / F32(self.head_dim)))))) for i in range(half)],
+            dtype=np.float32)
+        self.lane_weights = a.lane_tensors()
+        self.embedding = a.codebook_matrix(0)
+        self.final_norm = a.floats(a.layer_base(a.layers) + 11)
+        self.caches = [dict(keys=[], key_scales=[[] for _ in range(self.kv_heads)], values=[],
+                            value_scales=[[] for _ in range(self.kv_heads)]) for _ in range(a.layers)]
+        self.position = 0
+        self.hidden = None
+
+    def _embedding_row(self, token: int) -> np.ndarray:
+        """QuantisedMatrix::dequantise_row (crates/kernels/src/matrix.rs:140-152)."""
+        bits, packed, levels, norms, rows, cols = self.embedding
+        row_bytes = cols * bits // 8
+        codes = unpack_codes(packed[token * row_bytes:(token + 1) * row_bytes], bits, 1, cols)[0]
+        norm = half_to_f32(norms[token * (cols // GROUP):(token + 1) * (cols // GROUP)])
+        lv = np.asarray(levels, dtype=np.float32)
+        out = [walsh((lv[codes[g * GROUP:(g + 1) * GROUP]] * norm[g]).astype(np.float32)) for g in range(cols // GROUP)]
+        return np.concatenate(out)
+
+    def _rotary(self, head: np.ndarray, position: int) -> np.ndarray:
+        """ops::apply_rotary (crates/kernels/src/ops.rs:131-141) with libm sinf/cosf."""
+        half = head.size // 2
+        out = head.copy()
+        for i in range(half):
+            angle = F32(F32(position) * self.frequencies[i])
+            sin, cos = F32(_libm.sinf(float(angle))), F32(_libm.cosf(float(angle)))
+            a, b = head[i], head[half + i]
+            out[i] = F32(F32(a * cos) - F32(b * sin))
+            out[half + i] = F32(F32(b * cos) + F32(a * sin))
+        return out
+
+    def _attend(self, layer: int, hidden: np.ndarray) -> np.ndarray:
+        a, hd, H, KV = self.archive, self.head_dim, self.heads, self.kv_heads
+        base = a.layer_base(layer)
+        quantised = fake_quantise_int8(hidden)
+        q = product_rows(a.codebook_matrix(base + 1), 0, H * hd, quantised)
+        k = product_rows(a.codebook_matrix(base + 2), 0, KV * hd, quantised)
+        v = product_rows(a.codebook_matrix(base + 3), 0, KV * hd, quantised)
+        gate = product_rows(a.codebook_matrix(base + 6), 0, H * hd, quantised)
+        q_norm, k_norm = a.floats(base + 4), a.floats(base + 5)
+        cache = self.caches[layer]
+        query_codes, query_scales = [], []
+        for h in range(H):
+            head = self._rotary(zero_centred_norm(q[h * hd:(h + 1) * hd], q_norm), self.position)
+            codes, scale = quantise_int8(head)
+            query_codes.append(codes)
+            query_scales.append(scale)
+        keys, values = np.zeros((KV, hd), dtype=np.int64), np.zeros((KV, hd), dtype=np.int64)
+        for kv in range(KV):
+            head = self._rotary(zero_centred_norm(k[kv * hd:(kv + 1) * hd], k_norm), self.position)
+            keys[kv], scale = quantise_int8(head)
+            cache["key_scales"][kv].append(scale)
+        for kv in range(KV):
+            values[kv], scale = quantise_int8(v[kv * hd:(kv + 1) * hd])
+            cache["value_scales"][kv].append(scale)
+        cache["keys"].append(keys)
+        cache["values"].append(values)
+        total = self.position + 1
+        windowed = self.sliding_window > 0 and not (self.global_layers >> layer & 1)
+        first = max(0, total - self.sliding_window) if windowed else 0
+        all_keys, all_values = np.stack(cache["keys"])[first:], np.stack(cache["values"])[first:]
+        inverse_root = F32(F32(1.0) / np.sqrt(F32(hd)))
+        group = H // KV
+        attended = np.zeros(H * hd, dtype=np.float32)
+        for h in range(H):
+            kv = h // group
+            attended[h * hd:(h + 1) * hd] = attend_head_int(
+                query_codes[h], F32(query_scales[h] * inverse_root), all_keys[:, kv], np.array(cache["key_scales"][kv][first:], dtype=np.float32),
+                all_values[:, kv], np.array(cache["value_scales"][kv][first:], dtype=np.float32))
+        gates = np.array([sigmoid(g) for g in gate], dtype=np.float32)
+        gated = fake_quantise_int8((attended * gates).astype(np.float32))
+        out = a.codebook_matrix(base + 7)
+        return product_rows(out, 0, out[4], gated)
+
+    def push(self, token: int) -> np.ndarray:
+        """One token; returns the lane stream after every layer [layers][lanes·d]."""
+        a, lanes, d = self.archive, self.archive.lanes, self.archive.d_model
+        row = self._embedding_row(token)
+        stream = np.tile((row * np.sqrt(F32(d))).astype(np.float32), lanes)
+        trace = []
+        for layer in range(a.layers):
+            base = a.layer_base(layer)
+            block_input, post, residual = route(self.lane_weights, lanes, layer, layer, stream)
+            x = block_input.copy()
+            attended = zero_centred_norm(self._attend(layer, zero_centred_norm(x, a.floats(base))), a.floats(base + 8))
+            gate = sigmoid(a.floats(base + 9)[0])
+            x = (x + (gate * attended).astype(np.float32)).astype(np.float32)
+            mlp = hadamard_apply(a.hadamard(layer), zero_centred_norm(x, a.floats(base + 10)))
+            x = (x + mlp).astype(np.float32)
+            delta = (x - block_input).astype(np.float32)
+            mix = residual.reshape(lanes, lanes)
+            lanes_in = stream.reshape(lanes, d)
+            nxt = np.zeros((lanes, d), dtype=np.float32)
+            for lane in range(lanes):
+                for source in range(lanes):
+                    nxt[lane] = (nxt[lane] + (mix[lane, source] * lanes_in[source]).astype(np.float32)).astype(np.float32)
+                nxt[lane] = (nxt[lane] + (post[lane] * delta).astype(np.float32)).astype(np.float32)
+            stream = nxt.reshape(-1)
+            trace.append(stream.copy())
+        mean = np.zeros(d, dtype=np.float32)
+        for lane in stream.reshape(lanes, d):
+            mean = (mean + (lane / F32(lanes)).astype(np.float32)).astype(np.float32)
+        self.hidden = zero_centred_norm(mean, self.final_norm)
+        self.position += 1
+        return np.stack(trace)
+
+    def logits(self) -> np.ndarray:
+        """Session::logits (crates/model/src/session.rs:162-175): the fake-quantised
+        hidden row through the tied embedding."""
+        bits, packed, levels, norms, rows, cols = self.embedding
+        return product_int(bits, packed, levels, norms, rows, cols, fake_quantise_int8(self.hidden))

@@ -3,8 +3,9 @@ independent numpy restatement written from the reference's Rust
 (oracle/restated.py), on the composite paths that no reference test vector
 pins: codebook products with their per-group combine, one head's attention
 with 12-bit value weights, the Sinkhorn mixing, the grammar step's allowed
-statistics, and, with the archive's own weights, a layer's Hadamard block and
-its lane routing. Seeded random inputs; bit-exact. CPU only."""
+statistics, and, with the archive's own weights, a layer's Hadamard block,
+its lane routing and whole tokens (every layer's lane stream, then the
+logits). Seeded random inputs; bit-exact. CPU only."""
 
 from fractions import Fraction
 
@@ -150,3 +151,19 @@ def test_routing(oracle_lib, small_archive_path, layer, slot):
         got = restated.route(lt, arch.lanes, layer, slot, stream)
         for name, g, w in zip(("input", "post", "residual"), got, want):
             assert np.array_equal(np.asarray(g, dtype=np.float32).view(np.uint32), w.view(np.uint32)), (name, trial)
+
+
+def test_whole_tokens(oracle_lib, small_archive_path):
+    """Session::push and Session::logits end to end (4 layers): the lane
+    stream after every layer for six tokens, then the logits."""
+    arch = restated.Archive(small_archive_path)
+    model = oracle_lib.Model.open(small_archive_path, oracle_lib.MODE_INT)
+    ours, theirs = restated.Session(arch), oracle_lib.Session(model)
+    for position, token in enumerate([17, 300, 5000, 42, 9, 1234]):
+        want = theirs.push_traced(token)
+        got = ours.push(token)
+        for layer in range(arch.layers):
+            w, g = want[layer].reshape(-1), got[layer]
+            assert np.array_equal(g.view(np.uint32), w.view(np.uint32)), (position, layer, np.flatnonzero(g != w)[:5])
+    want, got = theirs.logits(), ours.logits()
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), np.flatnonzero(got != want)[:5]
