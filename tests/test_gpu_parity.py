@@ -179,6 +179,31 @@ def test_feed_matches_the_oracle_hidden_logits_and_cache(device_model, oracle_mo
     assert _bits_equal(s.logits(), o.logits()), _mismatch(s.logits(), o.logits())
 
 
+def test_device_matches_the_numpy_restatement(native_built, small_archive_path):
+    """The device against the second, numpy restatement (oracle/restated.py)
+    directly: a 4-layer archive, six pushed tokens with the logits after each,
+    then four greedy tokens chosen by the device's batch step."""
+    import rustyneedle_b200 as nb
+    from oracle import restated
+
+    model = nb.Model.open(small_archive_path, max_sessions=2)
+    s = nb.Session(model)
+    r = restated.Session(restated.Archive(small_archive_path))
+    for token in [17, 300, 5000, 42, 9, 1234]:
+        s.push(token)
+        r.push(token)
+        assert _bits_equal(s.logits(), r.logits()), _mismatch(s.logits(), r.logits())
+    batch = nb.Batch(model, [s])
+    for _ in range(4):
+        want = int(np.argmax(r.logits()))  # the first index of the maximum (generator.rs:147-152)
+        assert int(batch.step()[0]) == want
+        r.push(want)
+    batch.close()
+    assert _bits_equal(s.logits(), r.logits())
+    s.close()
+    model.close()
+
+
 def test_long_prefill_matches_the_oracle(device_model, oracle_model, oracle_lib):
     """A 600-token prompt in one pass (19 token blocks of the tcgen05 product, the last ragged)."""
     import rustyneedle_b200 as nb
