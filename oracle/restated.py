@@ -10,7 +10,9 @@ mixing, the grammar step's allowed statistics, a layer's Hadamard block
 (condition softmax, modulation, three Kronecker factor pairs) and its lane
 routing (the phi products, the gates with the own-lane offsets), and from
 them a whole token: Session::push (every layer's lane stream) and
-Session::logits. It reads the archive with its own reader. Every function
+Session::logits, with the Whistle cross attention (the cross memory and
+CrossState::apply) when a memory is given. It reads the archive with its
+own reader. Every function
 names the
 reference lines it follows. Arithmetic is f32 throughout, one rounding per
 Rust operation, in the Rust order.
@@ -609,8 +611,9 @@ class Session:
         out = a.codebook_matrix(base + 7)
         return product_rows(out, 0, out[4], gated)
 
-    def push(self, token: int) -> np.ndarray:
-        """One token; returns the lane stream after every layer [layers][lanes·d]."""
+    def push(self, token: int, memory: list | None = None) -> np.ndarray:
+        """One token (with a Whistle cross memory: Session::push_with and
+        CrossState); returns the lane stream after every layer [layers][lanes·d]."""
         a, lanes, d = self.archive, self.archive.lanes, self.archive.d_model
         row = self._embedding_row(token)
         stream = np.tile((row * np.sqrt(F32(d))).astype(np.float32), lanes)
@@ -622,6 +625,8 @@ class Session:
             attended = zero_centred_norm(self._attend(layer, zero_centred_norm(x, a.floats(base))), a.floats(base + 8))
             gate = sigmoid(a.floats(base + 9)[0])
             x = (x + (gate * attended).astype(np.float32)).astype(np.float32)
+            if memory is not None:  # the CrossAttention hook (session.rs:126-128)
+                x = cross_apply(a, memory, layer, x, self.heads, self.head_dim)
             mlp = hadamard_apply(a.hadamard(layer), zero_centred_norm(x, a.floats(base + 10)))
             x = (x + mlp).astype(np.float32)
             delta = (x - block_input).astype(np.float32)
@@ -644,5 +649,99 @@ class Session:
     def logits(self) -> np.ndarray:
         """Session::logits (crates/model/src/session.rs:162-175): the fake-quantised
         hidden row through the tied embedding."""
+        import struct
+
         bits, packed, levels, norms, rows, cols = self.embedding
-        return product_int(bits, packed, levels, norms, rows, cols, fake_quantise_int8(self.hidden))
+        out_vocab = struct.unpack_from("<48I", self.archive.data, 0)[6]
+        return product_int(bits, packed, levels, norms, rows, cols, fake_quantise_int8(self.hidden))[:out_vocab]
+
+
+# ------------------------------------------------------ Whistle cross attention
+_libm.logf.restype = ctypes.c_float
+_libm.logf.argtypes = [ctypes.c_float]
+
+
+def _cross_layer(archive: Archive, layer: int) -> dict:
+    """The 10 cross tensors of decoder layer `layer` (crates/cact/src/layout.rs:278-283),
+    after the audio manifest that follows the final norm."""
+    base = archive.layer_base(archive.layers) + 12 + 1 + 10 * layer
+    t = {name: base + i for i, name in enumerate(("norm", "q", "k", "v", "gate_proj", "out", "q_norm", "k_norm", "post_norm", "gate"))}
+    return t
+
+
+def cross_memory(archive: Archive, encoded: np.ndarray, heads: int, head_dim: int) -> list:
+    """CrossWeights::memory (crates/whistle/src/cross.rs:58-105): each frame
+    plus the gated sinusoidal position (angle t · exp(rate · j), rate =
+    -ln(10000) / (d/2 - 1); sin in the first half, cos in the second),
+    fake-quantised; per layer the key and value products of every frame,
+    the keys normed with k_norm, both quantised per (frame, head)."""
+    enc = np.asarray(encoded, dtype=np.float32)
+    frames, d = enc.shape
+    position_gate = archive.floats(archive.layer_base(archive.layers) + 12 + 1 + 10 * archive.layers)[0]
+    gate = sigmoid(position_gate)
+    half = d // 2
+    rate = F32(-F32(_libm.logf(10000.0)) / F32(half - 1.0))
+    memory = np.zeros((frames, d), dtype=np.float32)
+    for t in range(frames):
+        out = enc[t].copy()
+        for j in range(half):
+            angle = F32(F32(t) * F32(_libm.expf(float(F32(rate * F32(j))))))
+            out[j] = F32(enc[t, j] + F32(gate * F32(_libm.sinf(float(angle)))))
+            out[half + j] = F32(enc[t, half + j] + F32(gate * F32(_libm.cosf(float(angle)))))
+        memory[t] = fake_quantise_int8(out)
+    layers = []
+    for layer in range(archive.layers):
+        names = _cross_layer(archive, layer)
+        k_proj, v_proj = archive.codebook_matrix(names["k"]), archive.codebook_matrix(names["v"])
+        k_norm = archive.floats(names["k_norm"])
+        keys = np.zeros((frames, heads, head_dim), dtype=np.int64)
+        values = np.zeros_like(keys)
+        key_scales = np.zeros((frames, heads), dtype=np.float32)
+        value_scales = np.zeros_like(key_scales)
+        for t in range(frames):
+            k = product_rows(k_proj, 0, k_proj[4], memory[t])
+            v = product_rows(v_proj, 0, v_proj[4], memory[t])
+            for h in range(heads):
+                keys[t, h], key_scales[t, h] = quantise_int8(zero_centred_norm(k[h * head_dim:(h + 1) * head_dim], k_norm))
+                values[t, h], value_scales[t, h] = quantise_int8(v[h * head_dim:(h + 1) * head_dim])
+        layers.append(dict(keys=keys, key_scales=key_scales, values=values, value_scales=value_scales))
+    return layers
+
+
+def cross_apply(archive: Archive, memory: list, layer: int, x: np.ndarray, heads: int, head_dim: int) -> np.ndarray:
+    """CrossState::apply (crates/whistle/src/cross.rs:127-182): the query and
+    gate products of the normed, fake-quantised x; per head the normed,
+    quantised query; scores dot · key_scale · query_scale over the frames;
+    softmax_in_place; the context Σ_frame (value_scale · weight) · code in
+    frame order from +0.0; times sigmoid(gate), fake-quantised, the output
+    product, post-normed, added with the layer's sigmoid(gate) gain."""
+    names = _cross_layer(archive, layer)
+    m = memory[layer]
+    normed = fake_quantise_int8(zero_centred_norm(x, archive.floats(names["norm"])))
+    q = product_rows(archive.codebook_matrix(names["q"]), 0, heads * head_dim, normed)
+    gate = product_rows(archive.codebook_matrix(names["gate_proj"]), 0, heads * head_dim, normed)
+    q_norm = archive.floats(names["q_norm"])
+    inverse_root = F32(F32(1.0) / np.sqrt(F32(head_dim)))
+    context = np.zeros(heads * head_dim, dtype=np.float32)
+    for h in range(heads):
+        codes, scale = quantise_int8(zero_centred_norm(q[h * head_dim:(h + 1) * head_dim], q_norm))
+        query_scale = F32(scale * inverse_root)
+        dots = (m["keys"][:, h] @ codes).astype(np.float32)
+        scores = ((dots * m["key_scales"][:, h]).astype(np.float32) * query_scale).astype(np.float32)
+        e = fast_exp((scores - scores.max()).astype(np.float32))
+        total = F32(0.0)
+        for value in e:
+            total = F32(total + value)
+        weights = (e * F32(F32(1.0) / total)).astype(np.float32)
+        out = np.zeros(head_dim, dtype=np.float32)
+        codes_v = m["values"][:, h].astype(np.float32)
+        for f in range(weights.size):
+            s = F32(m["value_scales"][f, h] * weights[f])
+            out = (out + (s * codes_v[f]).astype(np.float32)).astype(np.float32)
+        context[h * head_dim:(h + 1) * head_dim] = out
+    gates = np.array([sigmoid(g) for g in gate], dtype=np.float32)
+    out_proj = archive.codebook_matrix(names["out"])
+    attended = product_rows(out_proj, 0, out_proj[4], fake_quantise_int8((context * gates).astype(np.float32)))
+    attended = zero_centred_norm(attended, archive.floats(names["post_norm"]))
+    gain = sigmoid(archive.floats(names["gate"])[0])
+    return (np.asarray(x, dtype=np.float32) + (gain * attended).astype(np.float32)).astype(np.float32)

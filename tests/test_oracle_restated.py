@@ -4,8 +4,9 @@ independent numpy restatement written from the reference's Rust
 pins: codebook products with their per-group combine, one head's attention
 with 12-bit value weights, the Sinkhorn mixing, the grammar step's allowed
 statistics, and, with the archive's own weights, a layer's Hadamard block,
-its lane routing and whole tokens (every layer's lane stream, then the
-logits). Seeded random inputs; bit-exact. CPU only."""
+its lane routing, whole tokens (every layer's lane stream, then the logits)
+and Whistle tokens with their cross memory. Seeded random inputs;
+bit-exact. CPU only."""
 
 from fractions import Fraction
 
@@ -167,3 +168,30 @@ def test_whole_tokens(oracle_lib, small_archive_path):
             assert np.array_equal(g.view(np.uint32), w.view(np.uint32)), (position, layer, np.flatnonzero(g != w)[:5])
     want, got = theirs.logits(), ours.logits()
     assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), np.flatnonzero(got != want)[:5]
+
+
+def test_whistle_cross_attention(oracle_lib):
+    """CrossWeights::memory and CrossState::apply inside Session::push_with on
+    a 4-layer synthetic Whistle archive: the logits after bos, a language
+    token and three text tokens, with a 48-frame encoder output."""
+    from rustyneedle_b200 import synthetic
+
+    path = synthetic.cached_archive(seed=19, geometry=synthetic.Geometry(num_layers=4, max_seq_len=512, text_vocab=8000))
+    arch = restated.Archive(path)
+    model = oracle_lib.Model.open(path, oracle_lib.MODE_INT)
+    encoded = np.random.default_rng(23).standard_normal((48, arch.d_model)).astype(np.float32)
+    ours = restated.Session(arch)
+    memory = restated.cross_memory(arch, encoded, ours.heads, ours.head_dim)
+    theirs = oracle_lib.Session(model)
+    theirs_memory = oracle_lib.CrossMemory(model, encoded)
+    for layer in (0, 3):  # the memory itself (keys, values and their scales)
+        k, ks, v, vs = theirs_memory.read(layer, ours.heads)
+        assert np.array_equal(np.asarray(k).reshape(memory[layer]["keys"].shape), memory[layer]["keys"])
+        assert np.array_equal(np.asarray(v).reshape(memory[layer]["values"].shape), memory[layer]["values"])
+        assert np.array_equal(np.asarray(ks, dtype=np.float32).reshape(-1).view(np.uint32), memory[layer]["key_scales"].reshape(-1).view(np.uint32))
+        assert np.array_equal(np.asarray(vs, dtype=np.float32).reshape(-1).view(np.uint32), memory[layer]["value_scales"].reshape(-1).view(np.uint32))
+    for token in [1, 8003, 17, 4242, 99]:
+        theirs.push_cross(token, theirs_memory)
+        ours.push(token, memory)
+        want, got = theirs.logits(), ours.logits()
+        assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), (token, np.flatnonzero(got != want)[:5])
