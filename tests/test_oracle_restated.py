@@ -195,3 +195,24 @@ def test_whistle_cross_attention(oracle_lib):
         ours.push(token, memory)
         want, got = theirs.logits(), ours.logits()
         assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), (token, np.flatnonzero(got != want)[:5])
+
+
+def test_prefill_against_pushes(oracle_lib, small_archive_path):
+    """Session::feed of 20 tokens (the prefill path, prefill.rs:10-99, in the
+    C++ restatement) against the numpy restatement pushing them one by one:
+    the logits and every layer's int8 cache."""
+    arch = restated.Archive(small_archive_path)
+    model = oracle_lib.Model.open(small_archive_path, oracle_lib.MODE_INT)
+    tokens = [int(t) for t in np.random.default_rng(3).integers(10, 8000, 20)]
+    theirs = oracle_lib.Session(model)
+    theirs.feed(tokens)
+    ours = restated.Session(arch)
+    for token in tokens:
+        ours.push(token)
+    assert np.array_equal(ours.logits().view(np.uint32), theirs.logits().view(np.uint32))
+    for layer in range(arch.layers):
+        keys, key_scales, values, value_scales = theirs.cache(layer)
+        cache = ours.caches[layer]
+        assert np.array_equal(np.stack(cache["keys"]), keys) and np.array_equal(np.stack(cache["values"]), values)
+        assert np.array_equal(np.array(cache["key_scales"], dtype=np.float32).view(np.uint32), key_scales.view(np.uint32))
+        assert np.array_equal(np.array(cache["value_scales"], dtype=np.float32).view(np.uint32), value_scales.view(np.uint32))
