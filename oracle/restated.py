@@ -518,8 +518,9 @@ def quantise_int8(values: np.ndarray):
 
 class Session:
     """Session::push and Session::logits (crates/model/src/session.rs:78-175)
-    of an archive without engram sites, conv taps or probe heads, on the
-    integer kernels: the embedding row (dequantised and rotated back, times
+    of an archive without engram sites or probe heads (q/k/v convolution taps
+    and sliding-window layers included), on the integer kernels: the
+    embedding row (dequantised and rotated back, times
     sqrt(d)) in every lane; per layer the routing, the attention
     (AttentionWeights::attend, crates/model/src/attention.rs:98-158, with the
     cache's int8 keys and values), the gated residual, the Hadamard block,
@@ -568,16 +569,41 @@ class Session:
             out[half + i] = F32(F32(b * cos) + F32(a * sin))
         return out
 
+    def _index(self, layer: int, name: str) -> int:
+        """A layer tensor's record (crates/cact/src/layout.rs:199-210): norm_in,
+        q/k/v, [three conv tap tensors], q_norm, k_norm, gate_proj, out_proj,
+        post_norm, attn_gate, pre_hada."""
+        a = self.archive
+        taps = 3 if a.conv_taps else 0
+        order = {"norm_in": 0, "q": 1, "k": 2, "v": 3, "taps": 4, "q_norm": 4 + taps, "k_norm": 5 + taps, "gate": 6 + taps,
+                 "out": 7 + taps, "post_norm": 8 + taps, "attn_gate": 9 + taps, "pre_hada": 10 + taps}
+        return a.layer_base(layer) + order[name]
+
     def _attend(self, layer: int, hidden: np.ndarray) -> np.ndarray:
         a, hd, H, KV = self.archive, self.head_dim, self.heads, self.kv_heads
-        base = a.layer_base(layer)
+        idx = lambda name: self._index(layer, name)  # noqa: E731
         quantised = fake_quantise_int8(hidden)
-        q = product_rows(a.codebook_matrix(base + 1), 0, H * hd, quantised)
-        k = product_rows(a.codebook_matrix(base + 2), 0, KV * hd, quantised)
-        v = product_rows(a.codebook_matrix(base + 3), 0, KV * hd, quantised)
-        gate = product_rows(a.codebook_matrix(base + 6), 0, H * hd, quantised)
-        q_norm, k_norm = a.floats(base + 4), a.floats(base + 5)
+        q = product_rows(a.codebook_matrix(idx("q")), 0, H * hd, quantised)
+        k = product_rows(a.codebook_matrix(idx("k")), 0, KV * hd, quantised)
+        v = product_rows(a.codebook_matrix(idx("v")), 0, KV * hd, quantised)
+        gate = product_rows(a.codebook_matrix(idx("gate")), 0, H * hd, quantised)
         cache = self.caches[layer]
+        if a.conv_taps:
+            # mix_taps (crates/model/src/attention.rs:83-93, 112-119): the raw
+            # projections newest first, then Σ over tap < min(taps, position + 1)
+            # of gain[tap] · history[tap] from +0.0
+            history = cache.setdefault("history", [])
+            history.insert(0, (q, k, v))
+            del history[a.conv_taps:]
+            mixed = []
+            for which in range(3):
+                gains = a.floats(idx("taps") + which).reshape(a.conv_taps, -1)
+                out = np.zeros_like(history[0][which])
+                for tap in range(min(a.conv_taps, self.position + 1)):
+                    out = (out + (gains[tap] * history[tap][which]).astype(np.float32)).astype(np.float32)
+                mixed.append(out)
+            q, k, v = mixed
+        q_norm, k_norm = a.floats(idx("q_norm")), a.floats(idx("k_norm"))
         query_codes, query_scales = [], []
         for h in range(H):
             head = self._rotary(zero_centred_norm(q[h * hd:(h + 1) * hd], q_norm), self.position)
@@ -608,7 +634,7 @@ class Session:
                 all_values[:, kv], np.array(cache["value_scales"][kv][first:], dtype=np.float32))
         gates = np.array([sigmoid(g) for g in gate], dtype=np.float32)
         gated = fake_quantise_int8((attended * gates).astype(np.float32))
-        out = a.codebook_matrix(base + 7)
+        out = a.codebook_matrix(idx("out"))
         return product_rows(out, 0, out[4], gated)
 
     def push(self, token: int, memory: list | None = None) -> np.ndarray:
@@ -619,15 +645,15 @@ class Session:
         stream = np.tile((row * np.sqrt(F32(d))).astype(np.float32), lanes)
         trace = []
         for layer in range(a.layers):
-            base = a.layer_base(layer)
+            idx = lambda name: self._index(layer, name)  # noqa: E731
             block_input, post, residual = route(self.lane_weights, lanes, layer, layer, stream)
             x = block_input.copy()
-            attended = zero_centred_norm(self._attend(layer, zero_centred_norm(x, a.floats(base))), a.floats(base + 8))
-            gate = sigmoid(a.floats(base + 9)[0])
+            attended = zero_centred_norm(self._attend(layer, zero_centred_norm(x, a.floats(idx("norm_in")))), a.floats(idx("post_norm")))
+            gate = sigmoid(a.floats(idx("attn_gate"))[0])
             x = (x + (gate * attended).astype(np.float32)).astype(np.float32)
             if memory is not None:  # the CrossAttention hook (session.rs:126-128)
                 x = cross_apply(a, memory, layer, x, self.heads, self.head_dim)
-            mlp = hadamard_apply(a.hadamard(layer), zero_centred_norm(x, a.floats(base + 10)))
+            mlp = hadamard_apply(a.hadamard(layer), zero_centred_norm(x, a.floats(idx("pre_hada"))))
             x = (x + mlp).astype(np.float32)
             delta = (x - block_input).astype(np.float32)
             mix = residual.reshape(lanes, lanes)

@@ -216,3 +216,26 @@ def test_prefill_against_pushes(oracle_lib, small_archive_path):
         assert np.array_equal(np.stack(cache["keys"]), keys) and np.array_equal(np.stack(cache["values"]), values)
         assert np.array_equal(np.array(cache["key_scales"], dtype=np.float32).view(np.uint32), key_scales.view(np.uint32))
         assert np.array_equal(np.array(cache["value_scales"], dtype=np.float32).view(np.uint32), value_scales.view(np.uint32))
+
+
+def test_conv_taps_and_sliding_window(oracle_lib):
+    """Whole tokens on an archive with 3-tap q/k/v convolutions and a 40-position
+    sliding window on every layer but the first and last (global): 50 tokens,
+    so the window and the taps' history both fill; every layer's lane stream
+    at every tenth token, then the logits."""
+    from rustyneedle_b200 import synthetic
+
+    geometry = synthetic.Geometry(num_layers=6, max_seq_len=512, conv_taps=3, sliding_window=40, global_layers=0b100001)
+    path = synthetic.cached_archive(seed=7, geometry=geometry)
+    arch = restated.Archive(path)
+    model = oracle_lib.Model.open(path, oracle_lib.MODE_INT)
+    ours, theirs = restated.Session(arch), oracle_lib.Session(model)
+    for position, token in enumerate(np.random.default_rng(5).integers(10, 8000, 50)):
+        want = theirs.push_traced(int(token))
+        got = ours.push(int(token))
+        if position % 10 == 9:
+            for layer in range(arch.layers):
+                w, g = want[layer].reshape(-1), got[layer]
+                assert np.array_equal(g.view(np.uint32), w.view(np.uint32)), (position, layer, np.flatnonzero(g != w)[:5])
+    want, got = theirs.logits(), ours.logits()
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), np.flatnonzero(got != want)[:5]
