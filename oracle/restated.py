@@ -307,6 +307,10 @@ class Archive:
         fields = struct.unpack_from("<48I", self.data, 0)
         self.count, codebook_len = fields[1], fields[2]
         self.layers, self.d_model, self.lanes, self.conv_taps = fields[10], fields[7], fields[15], fields[19]
+        # engram geometry (crates/cact/src/geometry.rs:66-82): slots, sub_dim, tables,
+        # conv taps, dilation, seed heads, the orders, the site layers
+        self.engram = dict(slots=fields[20], sub_dim=fields[21], tables=fields[22], conv_taps=fields[23], dilation=fields[24],
+                           seed_heads=fields[25], orders=list(fields[27:27 + fields[26]]), sites=list(fields[32:32 + fields[31]]))
         self.codebook = np.frombuffer(self.data, "<f4", codebook_len, self.HEADER_BYTES).astype(np.float32)
         at = self.HEADER_BYTES + codebook_len * 4
         self.records = [struct.unpack_from("<BBH4IQQII", self.data, at + self.RECORD_BYTES * i) for i in range(self.count)]
@@ -337,6 +341,16 @@ class Archive:
         lanes = self.layer_base(self.layers)
         t["perms"] = [self.floats(lanes + 9).astype(np.int64), self.floats(lanes + 10).astype(np.int64)]
         return t
+
+    def engram_tensors(self, site: int) -> dict:
+        """Site `site`'s tables, key_proj, value_proj and taps (layout.rs:231-234),
+        after the lane tensors and the two Hadamard permutations."""
+        base = self.layer_base(self.layers) + 11 + 4 * site
+        return dict(tables=self.codebook_matrix(base), key=self.codebook_matrix(base + 1), value=self.codebook_matrix(base + 2),
+                    taps=self.floats(base + 3))
+
+    def final_norm_index(self) -> int:
+        return self.layer_base(self.layers) + 11 + 4 * len(self.engram["sites"])
 
     def lane_tensors(self):
         base = self.layer_base(self.layers)
@@ -500,6 +514,37 @@ _libm.sinf.argtypes = _libm.cosf.argtypes = [ctypes.c_float]
 _libm.powf.argtypes = [ctypes.c_float, ctypes.c_float]
 
 
+def dequantise_row(matrix, row: int) -> np.ndarray:
+    """QuantisedMatrix::dequantise_row (crates/kernels/src/matrix.rs:140-152):
+    level × norm per element, then the Walsh transform per group."""
+    bits, packed, levels, norms, rows, cols = matrix
+    row_bytes = cols * bits // 8
+    codes = unpack_codes(packed[row * row_bytes:(row + 1) * row_bytes], bits, 1, cols)[0]
+    norm = half_to_f32(norms[row * (cols // GROUP):(row + 1) * (cols // GROUP)])
+    lv = np.asarray(levels, dtype=np.float32)
+    return np.concatenate([walsh((lv[codes[g * GROUP:(g + 1) * GROUP]] * norm[g]).astype(np.float32)) for g in range(cols // GROUP)])
+
+
+def engram_indices(cfg: dict, tokens: list, position: int) -> list:
+    """table_indices (crates/model/src/engram.rs:30-45): per order and head a
+    32-bit hash seeded by 0x9E3779B9 · (order_index · stride + head + 1), each
+    of the last `order` tokens (0 before the start) xored in and multiplied by
+    0x01000193, then xored with itself shifted right 15, modulo the slots."""
+    heads_per_order = cfg["tables"] // max(1, len(cfg["orders"]))
+    stride = heads_per_order if cfg["seed_heads"] == 0 else cfg["seed_heads"]
+    mask = 0xFFFFFFFF
+    out = []
+    for order_index, order in enumerate(cfg["orders"]):
+        for head in range(heads_per_order):
+            acc = (0x9E3779B9 * (order_index * stride + head + 1)) & mask
+            for back in range(order):
+                token = tokens[position - back] if position >= back else 0
+                acc = ((acc ^ token) * 0x01000193) & mask
+            acc ^= acc >> 15
+            out.append(acc % cfg["slots"])
+    return out
+
+
 def zero_centred_norm(values: np.ndarray, gains: np.ndarray) -> np.ndarray:
     """ops::zero_centred_norm (crates/kernels/src/ops.rs:44-58): (1 + gain) · x · inverse RMS."""
     v = np.asarray(values, dtype=np.float32)
@@ -518,8 +563,8 @@ def quantise_int8(values: np.ndarray):
 
 class Session:
     """Session::push and Session::logits (crates/model/src/session.rs:78-175)
-    of an archive without engram sites or probe heads (q/k/v convolution taps
-    and sliding-window layers included), on the integer kernels: the
+    of an archive without probe heads (q/k/v convolution taps, sliding-window
+    layers and engram sites included), on the integer kernels: the
     embedding row (dequantised and rotated back, times
     sqrt(d)) in every lane; per layer the routing, the attention
     (AttentionWeights::attend, crates/model/src/attention.rs:98-158, with the
@@ -541,21 +586,44 @@ class Session:
             dtype=np.float32)
         self.lane_weights = a.lane_tensors()
         self.embedding = a.codebook_matrix(0)
-        self.final_norm = a.floats(a.layer_base(a.layers) + 11)
+        self.final_norm = a.floats(a.final_norm_index())
+        self.tokens = []
+        self.engram_history = [[] for _ in a.engram["sites"]]
         self.caches = [dict(keys=[], key_scales=[[] for _ in range(self.kv_heads)], values=[],
                             value_scales=[[] for _ in range(self.kv_heads)]) for _ in range(a.layers)]
         self.position = 0
         self.hidden = None
 
     def _embedding_row(self, token: int) -> np.ndarray:
-        """QuantisedMatrix::dequantise_row (crates/kernels/src/matrix.rs:140-152)."""
-        bits, packed, levels, norms, rows, cols = self.embedding
-        row_bytes = cols * bits // 8
-        codes = unpack_codes(packed[token * row_bytes:(token + 1) * row_bytes], bits, 1, cols)[0]
-        norm = half_to_f32(norms[token * (cols // GROUP):(token + 1) * (cols // GROUP)])
-        lv = np.asarray(levels, dtype=np.float32)
-        out = [walsh((lv[codes[g * GROUP:(g + 1) * GROUP]] * norm[g]).astype(np.float32)) for g in range(cols // GROUP)]
-        return np.concatenate(out)
+        return dequantise_row(self.embedding, token)
+
+    def _engram(self, site: int, position: int) -> tuple:
+        """EngramSiteState::contribute (crates/model/src/engram.rs:67-100): the
+        tables' rows at the hashed indices (zeros while the position is shorter
+        than the order), fake-quantised, the key and raw value products, then the
+        value as the dilated causal convolution of the raw values."""
+        cfg, t = self.archive.engram, self.archive.engram_tensors(site)
+        heads_per_order = cfg["tables"] // max(1, len(cfg["orders"]))
+        gathered = []
+        for table, index in enumerate(engram_indices(cfg, self.tokens, position)):
+            order = cfg["orders"][table // heads_per_order]
+            if position + 1 >= order:
+                gathered.append(dequantise_row(t["tables"], table * cfg["slots"] + index))
+            else:
+                gathered.append(np.zeros(cfg["sub_dim"], dtype=np.float32))
+        gathered = fake_quantise_int8(np.concatenate(gathered))
+        key = product_rows(t["key"], 0, t["key"][4], gathered)
+        raw = product_rows(t["value"], 0, t["value"][4], gathered)
+        history = self.engram_history[site]
+        history.insert(0, raw)
+        del history[(cfg["conv_taps"] - 1) * cfg["dilation"] + 1:]
+        gains = t["taps"].reshape(cfg["conv_taps"], -1)
+        value = np.zeros_like(raw)
+        for tap in range(cfg["conv_taps"]):
+            back = tap * cfg["dilation"]
+            if position >= back:
+                value = (value + (gains[tap] * history[back]).astype(np.float32)).astype(np.float32)
+        return key, value
 
     def _rotary(self, head: np.ndarray, position: int) -> np.ndarray:
         """ops::apply_rotary (crates/kernels/src/ops.rs:131-141) with libm sinf/cosf."""
@@ -641,6 +709,8 @@ class Session:
         """One token (with a Whistle cross memory: Session::push_with and
         CrossState); returns the lane stream after every layer [layers][lanes·d]."""
         a, lanes, d = self.archive, self.archive.lanes, self.archive.d_model
+        self.tokens.append(int(token))
+        engram = [self._engram(site, self.position) for site in range(len(a.engram["sites"]))]
         row = self._embedding_row(token)
         stream = np.tile((row * np.sqrt(F32(d))).astype(np.float32), lanes)
         trace = []
@@ -648,6 +718,14 @@ class Session:
             idx = lambda name: self._index(layer, name)  # noqa: E731
             block_input, post, residual = route(self.lane_weights, lanes, layer, layer, stream)
             x = block_input.copy()
+            if layer in a.engram["sites"]:  # add_engram (crates/model/src/session.rs:178-188)
+                key, value = engram[a.engram["sites"].index(layer)]
+                products = (unit_rms(x) * unit_rms(key)).astype(np.float32)
+                dot = F32(-0.0)
+                for p in products:
+                    dot = F32(dot + p)
+                alpha = sigmoid(F32(dot / np.sqrt(F32(d))))
+                x = (x + (alpha * value).astype(np.float32)).astype(np.float32)
             attended = zero_centred_norm(self._attend(layer, zero_centred_norm(x, a.floats(idx("norm_in")))), a.floats(idx("post_norm")))
             gate = sigmoid(a.floats(idx("attn_gate"))[0])
             x = (x + (gate * attended).astype(np.float32)).astype(np.float32)
@@ -690,7 +768,7 @@ _libm.logf.argtypes = [ctypes.c_float]
 def _cross_layer(archive: Archive, layer: int) -> dict:
     """The 10 cross tensors of decoder layer `layer` (crates/cact/src/layout.rs:278-283),
     after the audio manifest that follows the final norm."""
-    base = archive.layer_base(archive.layers) + 12 + 1 + 10 * layer
+    base = archive.final_norm_index() + 1 + 1 + 10 * layer
     t = {name: base + i for i, name in enumerate(("norm", "q", "k", "v", "gate_proj", "out", "q_norm", "k_norm", "post_norm", "gate"))}
     return t
 
@@ -703,7 +781,7 @@ def cross_memory(archive: Archive, encoded: np.ndarray, heads: int, head_dim: in
     the keys normed with k_norm, both quantised per (frame, head)."""
     enc = np.asarray(encoded, dtype=np.float32)
     frames, d = enc.shape
-    position_gate = archive.floats(archive.layer_base(archive.layers) + 12 + 1 + 10 * archive.layers)[0]
+    position_gate = archive.floats(archive.final_norm_index() + 1 + 1 + 10 * archive.layers)[0]
     gate = sigmoid(position_gate)
     half = d // 2
     rate = F32(-F32(_libm.logf(10000.0)) / F32(half - 1.0))

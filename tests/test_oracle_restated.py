@@ -239,3 +239,29 @@ def test_conv_taps_and_sliding_window(oracle_lib):
                 assert np.array_equal(g.view(np.uint32), w.view(np.uint32)), (position, layer, np.flatnonzero(g != w)[:5])
     want, got = theirs.logits(), ours.logits()
     assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), np.flatnonzero(got != want)[:5]
+
+
+def test_engram_sites(oracle_lib):
+    """Whole tokens on an archive with engram sites at layers 1 and 4 (orders
+    2 and 3, two hashed tables per order, a 3-tap dilation-2 value
+    convolution) besides conv taps and sliding windows: 30 tokens, every
+    layer's lane stream at every fifth token, then the logits."""
+    from rustyneedle_b200 import synthetic
+
+    geometry = synthetic.Geometry(num_layers=6, max_seq_len=512, conv_taps=3, sliding_window=40, global_layers=0b100001,
+                                  engram_sites=(1, 4), engram_slots=512, engram_orders=(2, 3), engram_heads_per_order=2,
+                                  engram_conv_taps=3, engram_dilation=2)
+    path = synthetic.cached_archive(seed=11, geometry=geometry)
+    arch = restated.Archive(path)
+    assert arch.engram["sites"] == [1, 4] and arch.engram["orders"] == [2, 3]
+    model = oracle_lib.Model.open(path, oracle_lib.MODE_INT)
+    ours, theirs = restated.Session(arch), oracle_lib.Session(model)
+    for position, token in enumerate(np.random.default_rng(6).integers(10, 8000, 30)):
+        want = theirs.push_traced(int(token))
+        got = ours.push(int(token))
+        if position % 5 == 4 or position < 3:
+            for layer in range(arch.layers):
+                w, g = want[layer].reshape(-1), got[layer]
+                assert np.array_equal(g.view(np.uint32), w.view(np.uint32)), (position, layer, np.flatnonzero(g != w)[:5])
+    want, got = theirs.logits(), ours.logits()
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), np.flatnonzero(got != want)[:5]
