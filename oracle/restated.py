@@ -352,6 +352,30 @@ class Archive:
     def final_norm_index(self) -> int:
         return self.layer_base(self.layers) + 11 + 4 * len(self.engram["sites"])
 
+    def head_tensors(self) -> list:
+        """The probe heads (crates/cact/src/layout.rs:236-254): a half-precision
+        manifest of head codes after the final norm, then per head probes,
+        gain, query, row_bias, proj and bias (and a calibration for code 3)."""
+        at = self.final_norm_index() + 1
+        if at >= self.count or self.records[at][0] != 1:
+            return []
+        _, _, _, n, _, _, _, offset, nbytes, _, _ = self.records[at]
+        codes = np.frombuffer(self.data, "<f2", n, offset).astype(np.float32)
+        heads, at = [], at + 1
+        for code in codes:
+            heads.append(dict(code=int(code), probes=self.codebook_matrix(at), gain=self.floats(at + 1), query=self.codebook_matrix(at + 2),
+                              row_bias=self.floats(at + 3), proj=self.codebook_matrix(at + 4), bias=self.floats(at + 5)))
+            at += 6 + (1 if int(code) == 3 else 0)
+        return heads
+
+    def audio_index(self) -> int:
+        """The audio manifest's record: after the final norm and the probe heads."""
+        at = self.final_norm_index() + 1
+        if at < self.count and self.records[at][0] == 1:
+            codes = np.frombuffer(self.data, "<f2", self.records[at][3], self.records[at][7]).astype(np.float32)
+            at += 1 + sum(6 + (1 if int(c) == 3 else 0) for c in codes)
+        return at
+
     def lane_tensors(self):
         base = self.layer_base(self.layers)
         names = ("a_pre", "a_post", "a_res", "b_pre", "b_post", "b_res")
@@ -545,6 +569,84 @@ def engram_indices(cfg: dict, tokens: list, position: int) -> list:
     return out
 
 
+def lane_mean(stream: np.ndarray, lanes: int) -> np.ndarray:
+    """lane_mean (crates/model/src/session.rs:191-199): Σ_lane value / lanes from +0.0."""
+    s = np.asarray(stream, dtype=np.float32).reshape(lanes, -1)
+    mean = np.zeros(s.shape[1], dtype=np.float32)
+    for lane in s:
+        mean = (mean + (lane / F32(lanes)).astype(np.float32)).astype(np.float32)
+    return mean
+
+
+def dot_product(a: np.ndarray, b: np.ndarray) -> np.float32:
+    """ops::dot_product (crates/kernels/src/ops.rs:19-30): eight lanes of every
+    eighth product, the lanes summed in order from -0.0, plus the tail."""
+    x, y = np.asarray(a, dtype=np.float32), np.asarray(b, dtype=np.float32)
+    whole = x.size - x.size % 8
+    lanes = np.zeros(8, dtype=np.float32)
+    for i in range(0, whole, 8):
+        lanes = (lanes + (x[i:i + 8] * y[i:i + 8]).astype(np.float32)).astype(np.float32)
+    total = F32(-0.0)
+    for lane in lanes:
+        total = F32(total + lane)
+    tail = F32(-0.0)
+    for p, q in zip(x[whole:], y[whole:]):
+        tail = F32(tail + F32(p * q))
+    return F32(total + tail)
+
+
+class ProbeHead:
+    """ProbeHead (crates/model/src/heads.rs): the dense probe and query rows,
+    the running per-slot softmax pool of the cells (observe, :129-148), the
+    pooled readout (:88-117) and its projection (:119-127)."""
+
+    def __init__(self, t: dict, cells: int):
+        self.code = t["code"]
+        self.probes = np.stack([dequantise_row(t["probes"], r) for r in range(t["probes"][4])])
+        self.query = np.stack([dequantise_row(t["query"], r) for r in range(t["query"][4])])
+        self.gain, self.row_bias, self.proj, self.bias = t["gain"], t["row_bias"], t["proj"], t["bias"]
+        self.slots, self.width = self.probes.shape
+        self.per_cell = self.slots // cells
+        self.peak = np.full(self.slots, -np.inf, dtype=np.float32)
+        self.total = np.zeros(self.slots, dtype=np.float32)
+        self.weighted = np.zeros((self.slots, self.width), dtype=np.float32)
+
+    def observe(self, cells: list) -> None:
+        root = np.sqrt(F32(self.width))
+        for layer, cell in enumerate(cells):
+            for probe in range(self.per_cell):
+                slot = layer * self.per_cell + probe
+                score = F32(dot_product(cell, self.probes[slot]) / root)
+                peak = F32(max(self.peak[slot], score))
+                rescale = F32(0.0) if self.peak[slot] == -np.inf else expf(F32(self.peak[slot] - peak))
+                weight = expf(F32(score - peak))
+                self.total[slot] = F32(F32(self.total[slot] * rescale) + weight)
+                self.weighted[slot] = ((self.weighted[slot] * rescale).astype(np.float32) + (weight * cell).astype(np.float32)).astype(np.float32)
+                self.peak[slot] = peak
+
+    def pooled(self) -> np.ndarray:
+        readouts = np.zeros((self.slots, self.width), dtype=np.float32)
+        for slot in range(self.slots):
+            inverse = F32(F32(1.0) / self.total[slot])
+            readouts[slot] = (unit_rms((self.weighted[slot] * inverse).astype(np.float32)) * self.gain[slot]).astype(np.float32)
+        root = np.sqrt(F32(self.width))
+        out = np.zeros((self.query.shape[0], self.width), dtype=np.float32)
+        for q in range(self.query.shape[0]):
+            w = np.array([F32(F32(dot_product(readouts[slot], self.query[q]) / root) + self.row_bias[q * self.slots + slot])
+                          for slot in range(self.slots)], dtype=np.float32)
+            e = fast_exp((w - w.max()).astype(np.float32))
+            total = F32(0.0)
+            for v in e:
+                total = F32(total + v)
+            w = (e * F32(F32(1.0) / total)).astype(np.float32)
+            for slot in range(self.slots):
+                out[q] = (out[q] + (w[slot] * readouts[slot]).astype(np.float32)).astype(np.float32)
+        return out.reshape(-1)
+
+    def project(self, pooled: np.ndarray) -> np.ndarray:
+        return (product_rows(self.proj, 0, self.proj[4], pooled) + self.bias).astype(np.float32)
+
+
 def zero_centred_norm(values: np.ndarray, gains: np.ndarray) -> np.ndarray:
     """ops::zero_centred_norm (crates/kernels/src/ops.rs:44-58): (1 + gain) · x · inverse RMS."""
     v = np.asarray(values, dtype=np.float32)
@@ -563,8 +665,9 @@ def quantise_int8(values: np.ndarray):
 
 class Session:
     """Session::push and Session::logits (crates/model/src/session.rs:78-175)
-    of an archive without probe heads (q/k/v convolution taps, sliding-window
-    layers and engram sites included), on the integer kernels: the
+    of a Needle-3 archive with any of its features (q/k/v convolution taps,
+    sliding-window layers, engram sites, probe heads), on the integer
+    kernels: the
     embedding row (dequantised and rotated back, times
     sqrt(d)) in every lane; per layer the routing, the attention
     (AttentionWeights::attend, crates/model/src/attention.rs:98-158, with the
@@ -589,6 +692,7 @@ class Session:
         self.final_norm = a.floats(a.final_norm_index())
         self.tokens = []
         self.engram_history = [[] for _ in a.engram["sites"]]
+        self.heads_list = [ProbeHead(t, a.layers + 1) for t in a.head_tensors()]
         self.caches = [dict(keys=[], key_scales=[[] for _ in range(self.kv_heads)], values=[],
                             value_scales=[[] for _ in range(self.kv_heads)]) for _ in range(a.layers)]
         self.position = 0
@@ -714,6 +818,7 @@ class Session:
         row = self._embedding_row(token)
         stream = np.tile((row * np.sqrt(F32(d))).astype(np.float32), lanes)
         trace = []
+        cells = [lane_mean(stream, lanes)]
         for layer in range(a.layers):
             idx = lambda name: self._index(layer, name)  # noqa: E731
             block_input, post, residual = route(self.lane_weights, lanes, layer, layer, stream)
@@ -743,12 +848,22 @@ class Session:
                 nxt[lane] = (nxt[lane] + (post[lane] * delta).astype(np.float32)).astype(np.float32)
             stream = nxt.reshape(-1)
             trace.append(stream.copy())
-        mean = np.zeros(d, dtype=np.float32)
-        for lane in stream.reshape(lanes, d):
-            mean = (mean + (lane / F32(lanes)).astype(np.float32)).astype(np.float32)
-        self.hidden = zero_centred_norm(mean, self.final_norm)
+            cells.append(lane_mean(stream, lanes))
+        self.hidden = zero_centred_norm(lane_mean(stream, lanes), self.final_norm)
+        for head in self.heads_list:  # ProbeHead::observe of every cell (session.rs:144-147)
+            head.observe(cells)
         self.position += 1
         return np.stack(trace)
+
+    def pooled_readout(self, code: int):
+        """Session::pooled_readout (session.rs:156-160); None without that head."""
+        head = next((h for h in self.heads_list if h.code == code), None)
+        return None if head is None else head.pooled()
+
+    def head_output(self, code: int):
+        """Session::head_output (session.rs:150-154); None without that head."""
+        head = next((h for h in self.heads_list if h.code == code), None)
+        return None if head is None else head.project(head.pooled())
 
     def logits(self) -> np.ndarray:
         """Session::logits (crates/model/src/session.rs:162-175): the fake-quantised
@@ -768,7 +883,7 @@ _libm.logf.argtypes = [ctypes.c_float]
 def _cross_layer(archive: Archive, layer: int) -> dict:
     """The 10 cross tensors of decoder layer `layer` (crates/cact/src/layout.rs:278-283),
     after the audio manifest that follows the final norm."""
-    base = archive.final_norm_index() + 1 + 1 + 10 * layer
+    base = archive.audio_index() + 1 + 10 * layer
     t = {name: base + i for i, name in enumerate(("norm", "q", "k", "v", "gate_proj", "out", "q_norm", "k_norm", "post_norm", "gate"))}
     return t
 
@@ -781,7 +896,7 @@ def cross_memory(archive: Archive, encoded: np.ndarray, heads: int, head_dim: in
     the keys normed with k_norm, both quantised per (frame, head)."""
     enc = np.asarray(encoded, dtype=np.float32)
     frames, d = enc.shape
-    position_gate = archive.floats(archive.final_norm_index() + 1 + 1 + 10 * archive.layers)[0]
+    position_gate = archive.floats(archive.audio_index() + 1 + 10 * archive.layers)[0]
     gate = sigmoid(position_gate)
     half = d // 2
     rate = F32(-F32(_libm.logf(10000.0)) / F32(half - 1.0))

@@ -265,3 +265,31 @@ def test_engram_sites(oracle_lib):
                 assert np.array_equal(g.view(np.uint32), w.view(np.uint32)), (position, layer, np.flatnonzero(g != w)[:5])
     want, got = theirs.logits(), ours.logits()
     assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), np.flatnonzero(got != want)[:5]
+
+
+def test_probe_heads(oracle_lib):
+    """Probe heads (codes 2 and 3, two probes per cell, two queries, three
+    outputs) on the engram/taps/window archive: the pooled readout and the
+    head output after each of 12 tokens."""
+    from rustyneedle_b200 import synthetic
+
+    geometry = synthetic.Geometry(num_layers=6, max_seq_len=512, conv_taps=3, sliding_window=40, global_layers=0b100001,
+                                  engram_sites=(1, 4), engram_slots=512, engram_orders=(2, 3), engram_heads_per_order=2,
+                                  engram_conv_taps=3, engram_dilation=2, probe_heads=(2, 3), probes_per_layer=2, head_queries=2,
+                                  head_outputs=3)
+    path = synthetic.cached_archive(seed=16, geometry=geometry)
+    arch = restated.Archive(path)
+    model = oracle_lib.Model.open(path, oracle_lib.MODE_INT)
+    ours, theirs = restated.Session(arch), oracle_lib.Session(model)
+    assert [h.code for h in ours.heads_list] == [2, 3]
+    for position, token in enumerate(np.random.default_rng(8).integers(10, 8000, 12)):
+        theirs.push(int(token))
+        ours.push(int(token))
+        for code in (2, 3):
+            for name in ("pooled_readout", "head_output"):
+                want = np.asarray(getattr(theirs, name)(code), dtype=np.float32)
+                got = getattr(ours, name)(code)
+                assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), (position, code, name, np.flatnonzero(got != want)[:5])
+    assert ours.head_output(1) is None and theirs.head_output(1) is None
+    want, got = theirs.logits(), ours.logits()
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
