@@ -204,6 +204,38 @@ def test_device_matches_the_numpy_restatement(native_built, small_archive_path):
     model.close()
 
 
+def test_device_features_match_the_numpy_restatement(native_built):
+    """The same on an archive with every feature (3-tap q/k/v convolutions,
+    a 40-position window on the non-global layers, engram sites at layers 1
+    and 4, probe heads 2 and 3): a 12-token feed, then eight pushes, with the
+    logits and both heads' outputs after each push."""
+    import rustyneedle_b200 as nb
+    from oracle import restated
+    from rustyneedle_b200 import synthetic
+
+    geometry = synthetic.Geometry(num_layers=6, max_seq_len=512, conv_taps=3, sliding_window=40, global_layers=0b100001,
+                                  engram_sites=(1, 4), engram_slots=512, engram_orders=(2, 3), engram_heads_per_order=2,
+                                  engram_conv_taps=3, engram_dilation=2, probe_heads=(2, 3), probes_per_layer=2, head_queries=2,
+                                  head_outputs=3)
+    path = synthetic.cached_archive(seed=16, geometry=geometry)
+    model = nb.Model.open(path, max_sessions=2)
+    s = nb.Session(model)
+    r = restated.Session(restated.Archive(path))
+    tokens = [int(t) for t in np.random.default_rng(8).integers(10, 8000, 20)]
+    s.feed(tokens[:12])
+    for t in tokens[:12]:
+        r.push(t)
+    assert _bits_equal(s.logits(), r.logits()), _mismatch(s.logits(), r.logits())
+    for t in tokens[12:]:
+        s.push(t)
+        r.push(t)
+        assert _bits_equal(s.logits(), r.logits()), _mismatch(s.logits(), r.logits())
+        for code in (2, 3):
+            assert _bits_equal(s.head_output(code), r.head_output(code)), code
+    s.close()
+    model.close()
+
+
 def test_long_prefill_matches_the_oracle(device_model, oracle_model, oracle_lib):
     """A 600-token prompt in one pass (19 token blocks of the tcgen05 product, the last ragged)."""
     import rustyneedle_b200 as nb
