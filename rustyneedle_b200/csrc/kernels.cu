@@ -24,6 +24,7 @@
 #include <cmath>
 #include <cstdlib>
 #include <cstring>
+#include <map>
 #include <mutex>
 #include <type_traits>
 #include <utility>
@@ -2925,33 +2926,54 @@ size_t block_split_smem(const ModelDev& md) {
   return floats * 4;
 }
 
+// The dynamic shared memory a kernel may take is an attribute of the
+// function in the device's context, shared by every model open in the
+// process; a model that needs less (a shorter max_seq_len, a narrower d) must
+// not lower what an earlier one set. So the attribute only grows, per device
+// and kernel, to the most any open model needs.
+static std::mutex g_smem_mutex;
+static std::map<std::pair<int, const void*>, int> g_smem_allowed;
+
+template <typename K>
+static cudaError_t allow_smem(K* kernel, int bytes) {
+  int device = 0;
+  cudaError_t e = cudaGetDevice(&device);
+  if (e != cudaSuccess) return e;
+  std::lock_guard<std::mutex> lock(g_smem_mutex);
+  int& allowed = g_smem_allowed[{device, reinterpret_cast<const void*>(kernel)}];
+  if (bytes <= allowed) return cudaSuccess;
+  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess) allowed = bytes;
+  return e;
+}
+
 template <int G, int EPI>
 static cudaError_t attend_attributes(int smem) {
-  cudaError_t e = cudaFuncSetAttribute(k_attend<G, EPI, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  return e ? e : cudaFuncSetAttribute(k_attend<G, EPI, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  cudaError_t e = allow_smem(k_attend<G, EPI, false>, smem);
+  return e ? e : allow_smem(k_attend<G, EPI, true>, smem);
 }
 
 cudaError_t configure(const ModelDev& md, int t_cap) {
   cudaError_t e;
-  if ((e = cudaFuncSetAttribute(k_route, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)route_smem(md)))) return e;
+  if ((e = allow_smem(k_route, (int)route_smem(md)))) return e;
   const int att_smem = (int)attend_smem(md, t_cap);
   if ((e = attend_attributes<1, ATT_ROWS>(att_smem)) || (e = attend_attributes<1, ATT_LAST>(att_smem)) ||
       (e = attend_attributes<2, ATT_ROWS>(att_smem)) || (e = attend_attributes<2, ATT_CLUSTER>(att_smem)) ||
       (e = attend_attributes<2, ATT_LAST>(att_smem)) || (e = attend_attributes<4, ATT_ROWS>(att_smem)) ||
       (e = attend_attributes<4, ATT_CLUSTER>(att_smem)) || (e = attend_attributes<4, ATT_LAST>(att_smem)))
     return e;
-  if ((e = cudaFuncSetAttribute(k_block<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)block_smem(md)))) return e;
-  if ((e = cudaFuncSetAttribute(k_block<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)block_smem(md)))) return e;
+  if ((e = allow_smem(k_block<64>, (int)block_smem(md)))) return e;
+  if ((e = allow_smem(k_block<32>, (int)block_smem(md)))) return e;
   const int split_max = (int)(block_split_out_offset(block_split_smem(md) / 4) + FUSED_OUT_CODES + FUSED_OUT_SCALES);
-  if ((e = cudaFuncSetAttribute(k_block_split<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, split_max))) return e;
-  if ((e = cudaFuncSetAttribute(k_block_split<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, split_max))) return e;
-  if ((e = cudaFuncSetAttribute(k_stats, cudaFuncAttributeMaxDynamicSharedMemorySize, 2 * 8192 * 4))) return e;
-  if ((e = cudaFuncSetAttribute(k_cross_attend, cudaFuncAttributeMaxDynamicSharedMemorySize, 2 * MAX_CROSS_FRAMES * 4))) return e;
-  if ((e = cudaFuncSetAttribute(k_gemm<16, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gemm_smem<16>()))) return e;
-  if ((e = cudaFuncSetAttribute(k_gemm<32, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gemm_smem<32>()))) return e;
-  if ((e = cudaFuncSetAttribute(k_gemm<16, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gemm_smem<16>()))) return e;
-  if ((e = cudaFuncSetAttribute(k_gemm<32, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gemm_smem<32>()))) return e;
-  if ((e = cudaFuncSetAttribute(k_gemm_wide, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)wide_smem()))) return e;
+  if ((e = allow_smem(k_block_split<64>, split_max))) return e;
+  if ((e = allow_smem(k_block_split<32>, split_max))) return e;
+  if ((e = allow_smem(k_stats, 2 * 8192 * 4))) return e;
+  if ((e = allow_smem(k_cross_attend, 2 * MAX_CROSS_FRAMES * 4))) return e;
+  if ((e = allow_smem(k_gemm<16, 1>, (int)gemm_smem<16>()))) return e;
+  if ((e = allow_smem(k_gemm<32, 1>, (int)gemm_smem<32>()))) return e;
+  if ((e = allow_smem(k_gemm<16, 4>, (int)gemm_smem<16>()))) return e;
+  if ((e = allow_smem(k_gemm<32, 4>, (int)gemm_smem<32>()))) return e;
+  if ((e = allow_smem(k_gemm_wide, (int)wide_smem()))) return e;
 
   return cudaSuccess;
 }

@@ -236,6 +236,31 @@ def test_device_features_match_the_numpy_restatement(native_built):
     model.close()
 
 
+def test_a_shorter_model_opened_later_leaves_the_first_working(archive_path, oracle_model, oracle_lib):
+    """Models of different context lengths in one process: the kernels'
+    shared-memory limits are per-process function attributes, so opening a
+    512-position model after a 2048-position one must not shrink what the
+    first one's attention launches take."""
+    import rustyneedle_b200 as nb
+    from rustyneedle_b200 import synthetic
+
+    long_model = nb.Model.open(archive_path, max_sessions=2).with_depth(2)
+    short_model = nb.Model.open(synthetic.cached_archive(seed=19, geometry=synthetic.Geometry(num_layers=4, max_seq_len=512)),
+                                max_sessions=2)
+    ids = prompt_ids(13, 1500)
+    s = nb.Session(long_model)
+    s.feed(ids)
+    o = oracle_lib.Session(oracle_model.with_depth(2))
+    o.feed(ids)
+    assert _bits_equal(s.logits(), o.logits()), _mismatch(s.logits(), o.logits())
+    short = nb.Session(short_model)
+    short.feed(ids[:100])
+    s.close()
+    short.close()
+    short_model.close()
+    long_model.close()
+
+
 def test_long_prefill_matches_the_oracle(device_model, oracle_model, oracle_lib):
     """A 600-token prompt in one pass (19 token blocks of the tcgen05 product, the last ragged)."""
     import rustyneedle_b200 as nb
