@@ -894,12 +894,14 @@ std::shared_ptr<Engine> open_engine(const char* path, const nb_options* opt) {
   E->h_error.ensure(sizeof(int));
   E->d_logit_scale = A.alloc<float>((size_t)B * (d / GROUP));
   E->d_logits = A.alloc<float>((size_t)B * V);
-  E->d_slots = A.alloc<int32_t>(2 * (size_t)B);  // [slots][active flags]: one upload per step
+  // [slots][active flags][masks (B rows of V/32 words)]: a step's slots,
+  // flags and host masks arrive in one upload
+  E->d_slots = A.alloc<int32_t>(2 * (size_t)B + (size_t)B * (V / 32));
   E->d_active = E->d_slots + B;
+  E->d_mask = reinterpret_cast<uint32_t*>(E->d_slots + 2 * (size_t)B);
   E->d_next = A.alloc<uint32_t>(B);
   E->d_peaks = A.alloc<float>((size_t)2 * B);
   E->d_stats = A.alloc<float>((size_t)2 * B);
-  E->d_mask = A.alloc<uint32_t>((size_t)B * (V / 32));
   E->h_tokens.ensure((size_t)M * 4);
   E->h_meta.ensure((size_t)M * sizeof(TokenMeta));
   E->t_cap = (int)((g.max_seq_len + 3) / 4 * 4);
@@ -1037,7 +1039,7 @@ struct nb_batch {
   uint32_t* d_tokens = nullptr;           // the batch's token ids (= the chosen tokens)
   TokenMeta* d_meta = nullptr;
   int32_t* d_order = nullptr;             // per group: its sequences by decreasing context length
-  PinnedBuffer h_meta, h_mask, h_next, h_stats, h_active;
+  PinnedBuffer h_meta, h_next, h_stats, h_active;
   DeviceArena arena;
   cudaEvent_t fork = nullptr, join[MAX_STEP_GROUPS] = {};
   int groups = 1;  // independent chains of the step (sequences split in runs of whole 32-row tiles)
@@ -1724,7 +1726,6 @@ nb_status nb_batch_create(nb_model* model, nb_session* const* sessions, uint32_t
     b->h_next.ensure(count * 4);
     b->h_stats.ensure(count * 8);
     b->h_active.ensure(count * 4);
-    b->h_mask.ensure((size_t)count * (E.md.output_vocab / 32) * 4);
     NB_CUDA(cudaEventCreateWithFlags(&b->fork, cudaEventDisableTiming));
     for (cudaEvent_t& e : b->join) NB_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
     b->groups = step_groups(count);
@@ -1759,16 +1760,19 @@ void nb_batch_release(nb_batch* batch) {
 }
 
 // Host part of a step: which sequences can grow, their pages, their metadata.
-static uint32_t stage_step(nb_batch* b) {
+// mask_bits (host, B rows of output_vocab/32 words, or null) joins the upload
+// of the slots and flags.
+static uint32_t stage_step(nb_batch* b, const uint32_t* mask_bits = nullptr) {
   Engine& E = *b->engine;
   E.settle();
   const uint32_t B = (uint32_t)b->sessions.size();
   TokenMeta* hm = b->h_meta.as<TokenMeta>();
   int32_t* ha = b->h_active.as<int32_t>();
-  // the slots at [0, B), the active flags at [max_sessions, max_sessions + B):
-  // d_slots and d_active are one device array
-  const size_t flags = E.max_sessions;
-  E.h_misc.ensure((flags + B) * 4);
+  // the slots at [0, B), the active flags at [max_sessions, max_sessions + B)
+  // and the masks from 2 · max_sessions on: d_slots, d_active and d_mask are
+  // one device array
+  const size_t flags = E.max_sessions, words = E.md.output_vocab / 32;
+  E.h_misc.ensure((2 * flags + (size_t)B * words) * 4);
   int32_t* slots = E.h_misc.as<int32_t>();
   uint32_t live = 0;
   for (uint32_t i = 0; i < B; ++i) {
@@ -1785,7 +1789,12 @@ static uint32_t stage_step(nb_batch* b) {
   }
   E.flush_page_tables();
   std::memcpy(slots + flags, ha, B * 4);
-  NB_CUDA(cudaMemcpyAsync(E.d_slots, slots, (flags + B) * 4, cudaMemcpyHostToDevice, E.stream));
+  size_t upload = flags + B;
+  if (mask_bits) {
+    std::memcpy(slots + 2 * flags, mask_bits, (size_t)B * words * 4);
+    upload = 2 * flags + (size_t)B * words;
+  }
+  NB_CUDA(cudaMemcpyAsync(E.d_slots, slots, upload * 4, cudaMemcpyHostToDevice, E.stream));
   NB_CUDA(cudaMemcpyAsync(b->d_meta, hm, B * sizeof(TokenMeta), cudaMemcpyHostToDevice, E.stream));
   E.copies_in_flight = true;
   return live;
@@ -1833,11 +1842,7 @@ nb_status nb_batch_step(nb_batch* batch, const uint32_t* mask_bits, uint32_t* ne
     std::lock_guard<std::mutex> lock(E.mutex);
     NB_CUDA(cudaSetDevice(E.device));
     const uint32_t B = (uint32_t)batch->sessions.size(), words = E.md.output_vocab / 32;
-    stage_step(batch);
-    if (mask_bits) {
-      std::memcpy(batch->h_mask.p, mask_bits, (size_t)B * words * 4);
-      NB_CUDA(cudaMemcpyAsync(E.d_mask, batch->h_mask.p, (size_t)B * words * 4, cudaMemcpyHostToDevice, E.stream));
-    }
+    stage_step(batch, mask_bits);
     launch_step(batch, mask_bits != nullptr, stats != nullptr);
     NB_CUDA(cudaMemcpyAsync(batch->h_next.p, batch->d_tokens, B * 4, cudaMemcpyDeviceToHost, E.stream));
     if (stats) NB_CUDA(cudaMemcpyAsync(batch->h_stats.p, E.d_stats, (size_t)B * 8, cudaMemcpyDeviceToHost, E.stream));
