@@ -237,9 +237,10 @@ constexpr int PHI_ROWS = LANES + LANES + LANES * LANES;
 // Shared memory of k_route, in floats: this layer's phi rows (PHI_ROWS × n
 // bytes), the stream, a work row, the squares in chain-major order (8 chains
 // of n/8, stride n/8 + 4), the int8 codes, the phi norms and the norm_in gains.
-__host__ __device__ inline size_t route_floats(int d) {
+// Without the phi rows (LEAN: they are read through L2) the rest is the same.
+__host__ __device__ inline size_t route_floats(int d, bool lean = false) {
   const size_t n = (size_t)LANES * d, ng = n / GROUP;
-  return PHI_ROWS * n / 4 + 2 * n + 8 * (n / 8 + 4) + n / 4 + PHI_ROWS * ng + d;
+  return (lean ? 0 : PHI_ROWS * n / 4) + 2 * n + 8 * (n / 8 + 4) + n / 4 + PHI_ROWS * ng + d;
 }
 
 // Failure detection test hook: while g_expire_route > 0, each k_route CTA
@@ -269,13 +270,17 @@ __device__ __forceinline__ bool take_expiry() {
   return false;
 }
 
+// LEAN (large prefill passes): the phi rows stay in global memory and the
+// products read them through L2, so a CTA takes 33 KB of shared memory
+// instead of 81 KB and six CTAs fit an SM instead of two.
+template <bool LEAN>
 __global__ void __launch_bounds__(256) k_route(ModelDev md, LayerDev L, Work w, int M, int layer, int slot, int* error) {
   extern __shared__ __align__(16) float sm[];
   const int t = blockIdx.x;
   const int d = md.d_model, n = LANES * d, ng = n / GROUP, sqs = n / 8 + 4;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  uint8_t* s_phiw = reinterpret_cast<uint8_t*>(sm);              // PHI_ROWS × n bytes
-  float* s_stream = sm + PHI_ROWS * n / 4;                       // n
+  uint8_t* s_phiw = reinterpret_cast<uint8_t*>(sm);              // PHI_ROWS × n bytes (not LEAN)
+  float* s_stream = sm + (LEAN ? 0 : PHI_ROWS * n / 4);          // n
   float* s_work = s_stream + n;                                  // n: later x and the phi terms
   float* s_sq = s_work + n;                                      // 8 × sqs
   int8_t* s_codes = reinterpret_cast<int8_t*>(s_sq + 8 * sqs);  // n bytes
@@ -297,10 +302,12 @@ __global__ void __launch_bounds__(256) k_route(ModelDev md, LayerDev L, Work w, 
   // them instead of delaying them.
   __shared__ int s_expire;
   if (tid == 0) {
-    bulk_start(bar, PHI_ROWS * n + (PHI_ROWS * ng + d) * 4);
-    bulk_copy(s_phiw, md.phi_pre.codes + (size_t)layer * LANES * n, LANES * n, bar);
-    bulk_copy(s_phiw + (size_t)LANES * n, md.phi_post.codes + (size_t)layer * LANES * n, LANES * n, bar);
-    bulk_copy(s_phiw + (size_t)2 * LANES * n, md.phi_res.codes + (size_t)layer * LANES * LANES * n, LANES * LANES * n, bar);
+    bulk_start(bar, (LEAN ? 0 : PHI_ROWS * n) + (PHI_ROWS * ng + d) * 4);
+    if (!LEAN) {
+      bulk_copy(s_phiw, md.phi_pre.codes + (size_t)layer * LANES * n, LANES * n, bar);
+      bulk_copy(s_phiw + (size_t)LANES * n, md.phi_post.codes + (size_t)layer * LANES * n, LANES * n, bar);
+      bulk_copy(s_phiw + (size_t)2 * LANES * n, md.phi_res.codes + (size_t)layer * LANES * LANES * n, LANES * LANES * n, bar);
+    }
     bulk_copy(s_norms, md.phi_pre.scales + (size_t)layer * LANES * ng, LANES * ng * 4, bar);
     bulk_copy(s_norms + LANES * ng, md.phi_post.scales + (size_t)layer * LANES * ng, LANES * ng * 4, bar);
     bulk_copy(s_norms + 2 * LANES * ng, md.phi_res.scales + (size_t)layer * LANES * LANES * ng, LANES * LANES * ng * 4, bar);
@@ -414,13 +421,25 @@ __global__ void __launch_bounds__(256) k_route(ModelDev md, LayerDev L, Work w, 
     const float ls_pre = md.phi_pre.level_scale, ls_post = md.phi_post.level_scale, ls_res = md.phi_res.level_scale;
     for (int pair = tid; pair < PHI_ROWS * ng; pair += blockDim.x) {
       const int g = pair / PHI_ROWS, r = pair % PHI_ROWS;
-      const uint8_t* wrow = s_phiw + (size_t)r * n + g * GROUP;
+      const uint8_t* wrow;
+      if (LEAN)
+        wrow = reinterpret_cast<const uint8_t*>(r < LANES ? md.phi_pre.codes + ((size_t)layer * LANES + r) * n
+                          : (r < 2 * LANES ? md.phi_post.codes + ((size_t)layer * LANES + r - LANES) * n
+                                           : md.phi_res.codes + ((size_t)layer * LANES * LANES + r - 2 * LANES) * n)) +
+               g * GROUP;
+      else
+        wrow = s_phiw + (size_t)r * n + g * GROUP;
       const int8_t* arow = s_codes + g * GROUP;
       int acc0 = 0, acc1 = 0;
+      uint4 wl[8];
+      if (LEAN) {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) wl[k] = __ldg(reinterpret_cast<const uint4*>(wrow + ((k + tid) & 7) * 16));
+      }
 #pragma unroll
       for (int k = 0; k < 8; ++k) {
         const int kk = (k + tid) & 7;
-        const uint4 wv = *reinterpret_cast<const uint4*>(wrow + kk * 16);
+        const uint4 wv = LEAN ? wl[k] : *reinterpret_cast<const uint4*>(wrow + kk * 16);
         const uint4 a = *reinterpret_cast<const uint4*>(arow + kk * 16);
         acc0 = dp4a(wv.x, a.x, acc0);
         acc1 = dp4a(wv.y, a.y, acc1);
@@ -1333,16 +1352,20 @@ __device__ __forceinline__ void prep_token(const float* src, const float* gate, 
 }
 
 // ---------------------------------------------------------------- attention
-// grid (M, kv_heads), block 288: warps 0-7 score, weight and accumulate the
-// values of the kv head's query heads; warp 8 forms the softmax totals in the
-// reference's order (four running lanes, (l0+l1)+(l2+l3), then the tail;
-// neon.rs:277-307) while warps 0-7 accumulate. Every KV byte is read once.
+// grid (M, kv_heads), block W + 32: the W worker threads score, weight and
+// accumulate the values of the kv head's query heads; the last warp forms the
+// softmax totals in the reference's order (four running lanes,
+// (l0+l1)+(l2+l3), then the tail; neon.rs:277-307) while the workers
+// accumulate. Every KV byte is read once. W = 256 runs three CTAs per SM;
+// W = 128 (at most two query heads per kv head: the epilogue gives each of
+// the G·64 outputs a thread) runs five, for large prefill passes.
 constexpr int ATT_WORKERS = 256;
-constexpr int ATT_THREADS_ALL = ATT_WORKERS + 32;
+constexpr int ATT_WORKERS_NARROW = 128;
 constexpr int MAX_GROUP = 4;
-constexpr int ATT_SLICES = ATT_WORKERS / 16;
 constexpr int ATT_UNROLL = 8;
 constexpr int ATT_MAX_KV = 8;
+
+__host__ __device__ constexpr int att_min_blocks(int workers) { return workers == ATT_WORKERS ? 3 : 5; }
 
 __host__ __device__ constexpr int att_wstride(int t_cap) { return t_cap / 4 + 2; }
 
@@ -1361,8 +1384,8 @@ constexpr int ATT_ROWS = 0, ATT_CLUSTER = 1, ATT_LAST = 2;
 __device__ __forceinline__ void cluster_arrive_relaxed() { asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory"); }
 __device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.aligned;" ::: "memory"); }
 
-template <int G, int EPI, bool HEADS>
-__global__ void __launch_bounds__(ATT_THREADS_ALL, 3) k_attend(ModelDev md, LayerDev L, Work w, KvDev kv, int M, int layer, int t_cap) {
+template <int G, int EPI, bool HEADS, int W>
+__global__ void __launch_bounds__(W + 32, att_min_blocks(W)) k_attend(ModelDev md, LayerDev L, Work w, KvDev kv, int M, int layer, int t_cap) {
   constexpr bool PREP = EPI == ATT_CLUSTER;
   const int global = L.global;
   extern __shared__ float sm[];
@@ -1399,10 +1422,10 @@ __global__ void __launch_bounds__(ATT_THREADS_ALL, 3) k_attend(ModelDev md, Laye
   float* s_vs = sm + G * t_cap;                                 // [t_cap] value scales
   uint32_t* s_whi = reinterpret_cast<uint32_t*>(s_vs + t_cap);  // [G][ws]
   uint32_t* s_wlo = s_whi + G * ws;                             // [G][ws]
-  int* s_pv = reinterpret_cast<int*>(s_wlo + G * ws);           // [ATT_SLICES][G][64]
+  int* s_pv = reinterpret_cast<int*>(s_wlo + G * ws);           // [(W / 16)][G][64]
   __shared__ __align__(16) uint32_t s_q[MAX_GROUP][16];
   __shared__ float s_qs[MAX_GROUP], s_peak[MAX_GROUP], s_scale2[MAX_GROUP], s_total[MAX_GROUP];
-  __shared__ float s_red[MAX_GROUP][ATT_WORKERS / 32];
+  __shared__ float s_red[MAX_GROUP][W / 32];
   __shared__ float s_gsig[EPI == ATT_ROWS ? 1 : MAX_GROUP * HEAD_DIM];  // sigmoid of this CTA's gate values
   const PageGeometry& pg = md.page;
   if (HEADS) {
@@ -1423,23 +1446,23 @@ __global__ void __launch_bounds__(ATT_THREADS_ALL, 3) k_attend(ModelDev md, Laye
     // by the warps the head step leaves idle
     const int H = md.heads, KV = md.kv_heads, first_thread = HEADS ? (G + 2) * 32 : 0;
     const float* gsrc = w.proj + (size_t)t * (2 * H + 2 * KV) * HEAD_DIM + (H + 2 * KV) * HEAD_DIM + kvh * G * HEAD_DIM;
-    for (int i = tid - first_thread; i >= 0 && i < G * HEAD_DIM; i += ATT_THREADS_ALL - first_thread) s_gsig[i] = sigmoid(gsrc[i]);
+    for (int i = tid - first_thread; i >= 0 && i < G * HEAD_DIM; i += (W + 32) - first_thread) s_gsig[i] = sigmoid(gsrc[i]);
   }
   __syncthreads();  // the query codes, and with HEADS this position's key and value, are in place
 
-  if (tid < ATT_WORKERS) {
+  if (tid < W) {
     // pass 1: integer scores q·k, coefficients (s · key_scale) · query_scale, their
     // peak; the value scales are staged for pass 2. Two positions per thread
     // per round, both positions' loads in flight together.
     float lmax[G];
 #pragma unroll
     for (int h = 0; h < G; ++h) lmax[h] = -INFINITY;
-    for (int i0 = tid; i0 < count; i0 += 2 * ATT_WORKERS) {
+    for (int i0 = tid; i0 < count; i0 += 2 * W) {
       uint4 key[2][4];
       float ks[2], vs[2];
 #pragma unroll
       for (int u = 0; u < 2; ++u) {
-        const int i = min(i0 + u * ATT_WORKERS, count - 1);
+        const int i = min(i0 + u * W, count - 1);
         const int p = first + i, within = p % PAGE_POSITIONS;
         const uint8_t* page = s_page[p / PAGE_POSITIONS];
         const uint4* kp = reinterpret_cast<const uint4*>(page + ((size_t)kvh * PAGE_POSITIONS + within) * HEAD_DIM);
@@ -1450,7 +1473,7 @@ __global__ void __launch_bounds__(ATT_THREADS_ALL, 3) k_attend(ModelDev md, Laye
       }
 #pragma unroll
       for (int u = 0; u < 2; ++u) {
-        const int i = i0 + u * ATT_WORKERS;
+        const int i = i0 + u * W;
         if (i < count) {
           s_vs[i] = vs[u];
 #pragma unroll
@@ -1482,16 +1505,16 @@ __global__ void __launch_bounds__(ATT_THREADS_ALL, 3) k_attend(ModelDev md, Laye
   __syncthreads();
   if (tid < G) {
     float m = s_red[tid][0];
-    for (int k = 1; k < ATT_WORKERS / 32; ++k) m = fmaxf(m, s_red[tid][k]);
+    for (int k = 1; k < W / 32; ++k) m = fmaxf(m, s_red[tid][k]);
     s_peak[tid] = m;
   }
   __syncthreads();
-  if (tid < ATT_WORKERS) {
+  if (tid < W) {
     // pass 2: e = fast_exp(c - peak) and the peak of the weights e · value_scale
     float lmax[G];
 #pragma unroll
     for (int h = 0; h < G; ++h) lmax[h] = 0.0f;
-    for (int i = tid; i < count; i += ATT_WORKERS) {
+    for (int i = tid; i < count; i += W) {
       const float vs = s_vs[i];
 #pragma unroll
       for (int h = 0; h < G; ++h) {
@@ -1509,12 +1532,12 @@ __global__ void __launch_bounds__(ATT_THREADS_ALL, 3) k_attend(ModelDev md, Laye
   __syncthreads();
   if (tid < G) {
     float pk = s_red[tid][0];
-    for (int k = 1; k < ATT_WORKERS / 32; ++k) pk = fmaxf(pk, s_red[tid][k]);
+    for (int k = 1; k < W / 32; ++k) pk = fmaxf(pk, s_red[tid][k]);
     s_peak[tid] = pk;
     s_scale2[tid] = fdiv(pk, 2047.0f);
   }
   __syncthreads();
-  if (warp == ATT_WORKERS / 32) {
+  if (warp == W / 32) {
     // softmax totals in the order of neon.rs:294-305
     const int h = lane >> 2, j = lane & 3;
     const int vc = count - count % 4;
@@ -1543,7 +1566,7 @@ __global__ void __launch_bounds__(ATT_THREADS_ALL, 3) k_attend(ModelDev md, Laye
     // pass 3: 12-bit weights round(c / (peak / 2047)) (half away from zero) of
     // c = e · value_scale, split into 6-bit halves per absolute 4-position
     // block (attention.rs:294-310, neon.rs:348-365)
-    for (int b = tid; b < nblk; b += ATT_WORKERS) {
+    for (int b = tid; b < nblk; b += W) {
       const int pbase = (b0 + b) * 4;
 #pragma unroll
       for (int h = 0; h < G; ++h) {
@@ -1565,9 +1588,9 @@ __global__ void __launch_bounds__(ATT_THREADS_ALL, 3) k_attend(ModelDev md, Laye
         s_wlo[h * ws + b] = lo;
       }
     }
-    named_barrier(1, ATT_WORKERS);
+    named_barrier(1, W);
     // pass 4: exact integer sums over the value panels; thread (dq, slice) owns
-    // four dimensions and every ATT_SLICES-th block, ATT_UNROLL blocks per round
+    // four dimensions and every (W / 16)-th block, ATT_UNROLL blocks per round
     const int dq = tid & 15, slice = tid >> 4;
     int hi_acc[G][4], lo_acc[G][4];
 #pragma unroll
@@ -1575,17 +1598,17 @@ __global__ void __launch_bounds__(ATT_THREADS_ALL, 3) k_attend(ModelDev md, Laye
 #pragma unroll
       for (int k = 0; k < 4; ++k) hi_acc[h][k] = lo_acc[h][k] = 0;
     const size_t vbase = pg.value_offset + (size_t)kvh * PAGE_POSITIONS * HEAD_DIM + dq * 16;
-    for (int bb = slice; bb < nblk; bb += ATT_UNROLL * ATT_SLICES) {
+    for (int bb = slice; bb < nblk; bb += ATT_UNROLL * (W / 16)) {
       uint4 v[ATT_UNROLL];
 #pragma unroll
       for (int u = 0; u < ATT_UNROLL; ++u) {
-        const int b = min(bb + u * ATT_SLICES, nblk - 1);
+        const int b = min(bb + u * (W / 16), nblk - 1);
         const int p = (b0 + b) * 4;
         v[u] = *reinterpret_cast<const uint4*>(s_page[p / PAGE_POSITIONS] + vbase + ((p % PAGE_POSITIONS) / 4) * (HEAD_DIM * 4));
       }
 #pragma unroll
       for (int u = 0; u < ATT_UNROLL; ++u) {
-        const int b = bb + u * ATT_SLICES;
+        const int b = bb + u * (W / 16);
         if (b < nblk) {
 #pragma unroll
           for (int h = 0; h < G; ++h) {
@@ -1614,7 +1637,7 @@ __global__ void __launch_bounds__(ATT_THREADS_ALL, 3) k_attend(ModelDev md, Laye
     const int h = tid / HEAD_DIM, dim = tid % HEAD_DIM;
     int sum = 0;
 #pragma unroll
-    for (int s = 0; s < ATT_SLICES; ++s) sum += s_pv[(s * G + h) * HEAD_DIM + dim];
+    for (int s = 0; s < (W / 16); ++s) sum += s_pv[(s * G + h) * HEAD_DIM + dim];
     const float value = s_peak[h] > 0.0f ? fmul((float)sum, s_scale2[h]) : 0.0f;
     const float inverse = fdiv(1.0f, s_total[h]);
     out = fmul(value, inverse);
@@ -2062,8 +2085,13 @@ __device__ __forceinline__ float lane_out(const float* rw, const float* sv, int 
 
 // grid M, block 256. Post norm, gated residual (session.rs:121-125), the
 // Hadamard MLP (hadamard.rs:260-304) and the lane combine (lanes.rs:183-204).
-template <int LEFT>
-__global__ void __launch_bounds__(BLOCK_THREADS) k_block(ModelDev md, LayerDev L, Work w, int M, int* error) {
+// RES keeps all three Kronecker factor pairs resident and the lane combine's
+// operands in registers from the start (two CTAs per SM); without RES one
+// factor pair is staged per application and the operands load after the
+// Hadamard MLP (three CTAs per SM).
+template <int LEFT, bool RES>
+__device__ __forceinline__ void block_finish(const ModelDev& md, const LayerDev& L, const Work& w, int M, int* error) {
+  constexpr int F = RES ? 3 : 1;
   extern __shared__ float sm[];
   constexpr int N = LEFT * HADA_RIGHT;
   const int t = blockIdx.x;
@@ -2074,12 +2102,12 @@ __global__ void __launch_bounds__(BLOCK_THREADS) k_block(ModelDev md, LayerDev L
   float* buf0 = sm + 3 * MAX_D;           // N
   float* buf1 = buf0 + N;                 // N
   float* s_mod = buf1 + N;                // N
-  float* s_left = s_mod + N;                  // 3 × LEFT*LEFT: the three left factors
-  float* s_right = s_left + 3 * LEFT * LEFT;  // 3 × 32*32: the three right factors
+  float* s_left = s_mod + N;                  // F × LEFT*LEFT: the left factors
+  float* s_right = s_left + F * LEFT * LEFT;  // F × 32*32: the right factors
   // d*8 condition values, consumed before the first Kronecker stage: they
   // borrow buf1 and s_mod when they fit there
-  float* s_condv = d * COND_RANK <= 2 * N ? buf1 : s_right + 3 * HADA_RIGHT * HADA_RIGHT;
-  float* s_gpost = s_right + 3 * HADA_RIGHT * HADA_RIGHT + (d * COND_RANK <= 2 * N ? 0 : d * COND_RANK);  // d post_norm gains
+  float* s_condv = d * COND_RANK <= 2 * N ? buf1 : s_right + F * HADA_RIGHT * HADA_RIGHT;
+  float* s_gpost = s_right + F * HADA_RIGHT * HADA_RIGHT + (d * COND_RANK <= 2 * N ? 0 : d * COND_RANK);  // d post_norm gains
   float* s_gpre = s_gpost + MAX_D;                                                                         // d pre_hada gains
   const HadamardDev& Hd = L.hada;
 
@@ -2088,20 +2116,31 @@ __global__ void __launch_bounds__(BLOCK_THREADS) k_block(ModelDev md, LayerDev L
   // through the Hadamard MLP; one float4 column per thread (d <= 4 · 256)
   const float* route = w.route + (size_t)t * (LANES + LANES * LANES);
   float rw[LANES + LANES * LANES];
-#pragma unroll
-  for (int k = 0; k < LANES + LANES * LANES; ++k) rw[k] = __ldcg(route + k);
   const float* stream = w.stream + (size_t)t * LANES * d;
   float* next = w.next_stream + (size_t)t * LANES * d;
   const int i4 = tid;
   float4 sv[LANES], d4 = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-  if (i4 < d / 4) {
-    d4 = reinterpret_cast<const float4*>(Hd.d4)[i4];
+  if (RES) {
 #pragma unroll
-    for (int s = 0; s < LANES; ++s) sv[s] = __ldcg(reinterpret_cast<const float4*>(stream + s * d) + i4);
+    for (int k = 0; k < LANES + LANES * LANES; ++k) rw[k] = __ldcg(route + k);
+    if (i4 < d / 4) {
+      d4 = reinterpret_cast<const float4*>(Hd.d4)[i4];
+#pragma unroll
+      for (int s = 0; s < LANES; ++s) sv[s] = __ldcg(reinterpret_cast<const float4*>(stream + s * d) + i4);
+    }
   }
-  if (!block_front<LEFT, 3>(md, L, w, M, t, d, error, s_a, s_x, s_pre, s_condv, s_left, s_right, s_gpost, s_gpre, 0, 1)) return;
+  if (!block_front<LEFT, F>(md, L, w, M, t, d, error, s_a, s_x, s_pre, s_condv, s_left, s_right, s_gpost, s_gpre, 0, 1)) return;
   __syncthreads();
-  hadamard_core<LEFT, true>(md, Hd, d, s_pre, buf0, buf1, s_mod, s_left, s_right, s_condv);
+  hadamard_core<LEFT, RES>(md, Hd, d, s_pre, buf0, buf1, s_mod, s_left, s_right, s_condv);
+  if (!RES) {
+#pragma unroll
+    for (int k = 0; k < LANES + LANES * LANES; ++k) rw[k] = __ldcg(route + k);
+    if (i4 < d / 4) {
+      d4 = reinterpret_cast<const float4*>(Hd.d4)[i4];
+#pragma unroll
+      for (int s = 0; s < LANES; ++s) sv[s] = __ldcg(reinterpret_cast<const float4*>(stream + s * d) + i4);
+    }
+  }
   pdl_trigger();  // the lane combine overlaps the next kernel's prologue
   if (i4 < d / 4) {
     const float dv[4] = {d4.x, d4.y, d4.z, d4.w};
@@ -2124,6 +2163,15 @@ __global__ void __launch_bounds__(BLOCK_THREADS) k_block(ModelDev md, LayerDev L
       reinterpret_cast<float4*>(next + l * d)[i4] = make_float4(o[0], o[1], o[2], o[3]);
     }
   }
+}
+
+template <int LEFT>
+__global__ void __launch_bounds__(BLOCK_THREADS) k_block(ModelDev md, LayerDev L, Work w, int M, int* error) {
+  block_finish<LEFT, true>(md, L, w, M, error);
+}
+template <int LEFT>
+__global__ void __launch_bounds__(BLOCK_THREADS, 3) k_block_lean(ModelDev md, LayerDev L, Work w, int M, int* error) {
+  block_finish<LEFT, false>(md, L, w, M, error);
 }
 
 // ------------------------------------------------ block finish over a cluster
@@ -2908,14 +2956,14 @@ void set_exp_constants(const nbx::ExpConstants& constants, const nbx::ExceptionS
   cudaMemcpyToSymbolAsync(c_exceptions, &exceptions, sizeof exceptions, 0, cudaMemcpyHostToDevice, stream);
 }
 
-size_t route_smem(const ModelDev& md) { return route_floats((int)md.d_model) * 4; }
-size_t attend_smem(const ModelDev& md, int t_cap) {
+size_t route_smem(const ModelDev& md, bool lean = false) { return route_floats((int)md.d_model, lean) * 4; }
+size_t attend_smem(const ModelDev& md, int t_cap, int workers = ATT_WORKERS) {
   int G = md.heads / md.kv_heads;
-  return (size_t)(G + 1) * t_cap * 4 + 2 * (size_t)G * att_wstride(t_cap) * 4 + (size_t)ATT_SLICES * G * HEAD_DIM * 4;
+  return (size_t)(G + 1) * t_cap * 4 + 2 * (size_t)G * att_wstride(t_cap) * 4 + (size_t)(workers / 16) * G * HEAD_DIM * 4;
 }
-size_t block_smem(const ModelDev& md) {
+size_t block_smem(const ModelDev& md, int factors = 3) {
   int N = md.hada_left * HADA_RIGHT;
-  size_t floats = 3 * MAX_D + 3 * N + 3 * (md.hada_left * md.hada_left + HADA_RIGHT * HADA_RIGHT) + 2 * MAX_D;
+  size_t floats = 3 * MAX_D + 3 * N + factors * (md.hada_left * md.hada_left + HADA_RIGHT * HADA_RIGHT) + 2 * MAX_D;
   if ((int)md.d_model * COND_RANK > 2 * N) floats += (size_t)md.d_model * COND_RANK;
   return floats * 4;
 }
@@ -2949,13 +2997,19 @@ static cudaError_t allow_smem(K* kernel, int bytes) {
 
 template <int G, int EPI>
 static cudaError_t attend_attributes(int smem) {
-  cudaError_t e = allow_smem(k_attend<G, EPI, false>, smem);
-  return e ? e : allow_smem(k_attend<G, EPI, true>, smem);
+  cudaError_t e = allow_smem(k_attend<G, EPI, false, ATT_WORKERS>, smem);
+  if (!e) e = allow_smem(k_attend<G, EPI, true, ATT_WORKERS>, smem);
+  if constexpr (G <= 2) {
+    if (!e) e = allow_smem(k_attend<G, EPI, false, ATT_WORKERS_NARROW>, smem);
+    if (!e) e = allow_smem(k_attend<G, EPI, true, ATT_WORKERS_NARROW>, smem);
+  }
+  return e;
 }
 
 cudaError_t configure(const ModelDev& md, int t_cap) {
   cudaError_t e;
-  if ((e = allow_smem(k_route, (int)route_smem(md)))) return e;
+  if ((e = allow_smem(k_route<false>, (int)route_smem(md)))) return e;
+  if ((e = allow_smem(k_route<true>, (int)route_smem(md, true)))) return e;
   const int att_smem = (int)attend_smem(md, t_cap);
   if ((e = attend_attributes<1, ATT_ROWS>(att_smem)) || (e = attend_attributes<1, ATT_LAST>(att_smem)) ||
       (e = attend_attributes<2, ATT_ROWS>(att_smem)) || (e = attend_attributes<2, ATT_CLUSTER>(att_smem)) ||
@@ -2964,6 +3018,8 @@ cudaError_t configure(const ModelDev& md, int t_cap) {
     return e;
   if ((e = allow_smem(k_block<64>, (int)block_smem(md)))) return e;
   if ((e = allow_smem(k_block<32>, (int)block_smem(md)))) return e;
+  if ((e = allow_smem(k_block_lean<64>, (int)block_smem(md, 1)))) return e;
+  if ((e = allow_smem(k_block_lean<32>, (int)block_smem(md, 1)))) return e;
   const int split_max = (int)(block_split_out_offset(block_split_smem(md) / 4) + FUSED_OUT_CODES + FUSED_OUT_SCALES);
   if ((e = allow_smem(k_block_split<64>, split_max))) return e;
   if ((e = allow_smem(k_block_split<32>, split_max))) return e;
@@ -3139,6 +3195,10 @@ static bool fuse_out_product(const ModelDev& md, const LayerDev& L, int M, bool 
          L.out.rows == md.d_model && L.out.cols == (uint32_t)GEMM_K;
 }
 
+// the lean block finish from this many tokens on (prefill passes; the
+// 128-token decode chains keep two resident-factor CTAs per SM)
+constexpr int BLOCK_LEAN_MIN_TOKENS = 256;
+
 static void launch_block(const ModelDev& md, const LayerDev& L, const Work& w, int M, cudaStream_t st, bool fuse_out = false) {
   const int left = md.hada_left, W = 2 * BLOCK_THREADS / left, CL = HADA_RIGHT / W;
   if (block_split_path(md, M)) {
@@ -3147,10 +3207,24 @@ static void launch_block(const ModelDev& md, const LayerDev& L, const Work& w, i
     const size_t smem = fuse_out ? block_split_out_offset(split_floats) + FUSED_OUT_CODES + FUSED_OUT_SCALES : block_split_smem(md);
     launch_clustered(k, dim3(M * CL), BLOCK_THREADS, smem, st, dim3(CL, 1, 1), md, L, w, M, md.error, fuse_out ? 1 : 0, split_floats);
   } else {
-    auto k = left == 64 ? k_block<64> : k_block<32>;
-    launch(k, M, BLOCK_THREADS, block_smem(md), st, md, L, w, M, md.error);
+    // $NEEDLE_B200_BLOCK_LEAN=N: the lean block finish for passes of at least N tokens
+    static const int lean_from = [] {
+      const char* e = std::getenv("NEEDLE_B200_BLOCK_LEAN");
+      return e ? std::atoi(e) : BLOCK_LEAN_MIN_TOKENS;
+    }();
+    if (M >= lean_from) {
+      auto k = left == 64 ? k_block_lean<64> : k_block_lean<32>;
+      launch(k, M, BLOCK_THREADS, block_smem(md, 1), st, md, L, w, M, md.error);
+    } else {
+      auto k = left == 64 ? k_block<64> : k_block<32>;
+      launch(k, M, BLOCK_THREADS, block_smem(md), st, md, L, w, M, md.error);
+    }
   }
 }
+
+// the lean routing from this many tokens on (prefill passes; the decode
+// chains keep the phi rows in shared memory, off the token's L2 latency chain)
+constexpr int ROUTE_LEAN_MIN_TOKENS = 256;
 
 void launch_layer(const ModelDev& md, const LayerDev& L, const EngramDev* engram, const CrossLayerDev* cross, const Work& w,
                   const KvDev& kv, int M, int layer, int slot, int t_cap, bool distinct, cudaStream_t st) {
@@ -3161,7 +3235,15 @@ void launch_layer(const ModelDev& md, const LayerDev& L, const EngramDev* engram
     launch(k_engram_gather, M, 128, 0, st, md, *engram, w, M);
     project(engram->kv, w.act, w.act_scale, w.engram_kv, M, 2 * d, w.meta, st, md.error, (int)w.act_rows);
   }
-  launch(k_route, M, 256, route_smem(md), st, md, L, w, M, layer, slot, md.error);
+  // $NEEDLE_B200_ROUTE_LEAN=N: the lean routing for passes of at least N tokens
+  static const int route_lean_from = [] {
+    const char* e = std::getenv("NEEDLE_B200_ROUTE_LEAN");
+    return e ? std::atoi(e) : ROUTE_LEAN_MIN_TOKENS;
+  }();
+  if (M >= route_lean_from)
+    launch(k_route<true>, M, 256, route_smem(md, true), st, md, L, w, M, layer, slot, md.error);
+  else
+    launch(k_route<false>, M, 256, route_smem(md), st, md, L, w, M, layer, slot, md.error);
   project(L.qkvg, w.act, w.act_scale, w.proj, M, proj_stride, w.meta, st, md.error);
   // the head step runs inside the attention when each token of the pass
   // belongs to a different sequence; $NEEDLE_B200_FUSE_HEADS=0 keeps k_heads
@@ -3269,16 +3351,37 @@ void launch_advance(TokenMeta* meta, int B, cudaStream_t st) {
 // freedom there). False when k_prep must still run.
 // $NEEDLE_B200_FUSE_PREP=0 always leaves the activation step to k_prep.
 constexpr int FUSE_PREP_MAX_TOKENS = 64;
+// the narrow attention CTAs from this many tokens on: prefill passes, whose
+// many short contexts (a CTA per query token and kv head) are bound by the
+// fixed phases, which five CTAs per SM overlap better than three; the
+// 128-token decode chains, longer contexts on fewer CTAs, keep the wide ones
+constexpr int ATT_NARROW_MIN_TOKENS = 256;
 
 template <int G, int EPI>
 static void attend_variant(bool heads, const ModelDev& md, const LayerDev& L, const Work& w, const KvDev& kv, int M, int layer,
                            int t_cap, cudaStream_t st) {
+  // $NEEDLE_B200_ATT_NARROW=N: the narrow CTAs (G <= 2) for passes of at least N tokens
+  static const int narrow_from = [] {
+    const char* e = std::getenv("NEEDLE_B200_ATT_NARROW");
+    return e ? std::atoi(e) : ATT_NARROW_MIN_TOKENS;
+  }();
   const dim3 grid(M, md.kv_heads), cluster(1, EPI == ATT_CLUSTER ? md.kv_heads : 1, 1);
+  if constexpr (G <= 2) {
+    if (M >= narrow_from) {
+      constexpr int W = ATT_WORKERS_NARROW;
+      const size_t smem = attend_smem(md, t_cap, W);
+      if (heads)
+        launch_clustered(k_attend<G, EPI, true, W>, grid, W + 32, smem, st, cluster, md, L, w, kv, M, layer, t_cap);
+      else
+        launch_clustered(k_attend<G, EPI, false, W>, grid, W + 32, smem, st, cluster, md, L, w, kv, M, layer, t_cap);
+      return;
+    }
+  }
   const size_t smem = attend_smem(md, t_cap);
   if (heads)
-    launch_clustered(k_attend<G, EPI, true>, grid, ATT_THREADS_ALL, smem, st, cluster, md, L, w, kv, M, layer, t_cap);
+    launch_clustered(k_attend<G, EPI, true, ATT_WORKERS>, grid, ATT_WORKERS + 32, smem, st, cluster, md, L, w, kv, M, layer, t_cap);
   else
-    launch_clustered(k_attend<G, EPI, false>, grid, ATT_THREADS_ALL, smem, st, cluster, md, L, w, kv, M, layer, t_cap);
+    launch_clustered(k_attend<G, EPI, false, ATT_WORKERS>, grid, ATT_WORKERS + 32, smem, st, cluster, md, L, w, kv, M, layer, t_cap);
 }
 
 bool launch_attention(const ModelDev& md, const LayerDev& L, const Work& w, const KvDev& kv, int M, int layer, int t_cap, bool heads,
