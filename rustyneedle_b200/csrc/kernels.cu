@@ -1358,14 +1358,16 @@ __device__ __forceinline__ void prep_token(const float* src, const float* gate, 
 // (l0+l1)+(l2+l3), then the tail; neon.rs:277-307) while the workers
 // accumulate. Every KV byte is read once. W = 256 runs three CTAs per SM;
 // W = 128 (at most two query heads per kv head: the epilogue gives each of
-// the G·64 outputs a thread) runs five, for large prefill passes.
+// the G·64 outputs a thread) runs five, for large prefill passes; W = 512
+// runs one, for passes of a few tokens.
 constexpr int ATT_WORKERS = 256;
 constexpr int ATT_WORKERS_NARROW = 128;
+constexpr int ATT_WORKERS_WIDE = 512;
 constexpr int MAX_GROUP = 4;
 constexpr int ATT_UNROLL = 8;
 constexpr int ATT_MAX_KV = 8;
 
-__host__ __device__ constexpr int att_min_blocks(int workers) { return workers == ATT_WORKERS ? 3 : 5; }
+__host__ __device__ constexpr int att_min_blocks(int workers) { return workers == ATT_WORKERS ? 3 : (workers == ATT_WORKERS_NARROW ? 5 : 1); }
 
 __host__ __device__ constexpr int att_wstride(int t_cap) { return t_cap / 4 + 2; }
 
@@ -3002,6 +3004,9 @@ static cudaError_t attend_attributes(int smem) {
   if constexpr (G <= 2) {
     if (!e) e = allow_smem(k_attend<G, EPI, false, ATT_WORKERS_NARROW>, smem);
     if (!e) e = allow_smem(k_attend<G, EPI, true, ATT_WORKERS_NARROW>, smem);
+    const int wide = smem - (ATT_WORKERS / 16) * G * HEAD_DIM * 4 + (ATT_WORKERS_WIDE / 16) * G * HEAD_DIM * 4;
+    if (!e) e = allow_smem(k_attend<G, EPI, false, ATT_WORKERS_WIDE>, wide);
+    if (!e) e = allow_smem(k_attend<G, EPI, true, ATT_WORKERS_WIDE>, wide);
   }
   return e;
 }
@@ -3356,6 +3361,9 @@ constexpr int FUSE_PREP_MAX_TOKENS = 64;
 // fixed phases, which five CTAs per SM overlap better than three; the
 // 128-token decode chains, longer contexts on fewer CTAs, keep the wide ones
 constexpr int ATT_NARROW_MIN_TOKENS = 256;
+// the wide attention CTAs up to this many tokens: at batch 1 a token's four
+// kv-head CTAs are the whole launch, so each CTA's phases get a whole SM
+constexpr int ATT_WIDE_MAX_TOKENS = 8;
 
 template <int G, int EPI>
 static void attend_variant(bool heads, const ModelDev& md, const LayerDev& L, const Work& w, const KvDev& kv, int M, int layer,
@@ -3366,7 +3374,21 @@ static void attend_variant(bool heads, const ModelDev& md, const LayerDev& L, co
     return e ? std::atoi(e) : ATT_NARROW_MIN_TOKENS;
   }();
   const dim3 grid(M, md.kv_heads), cluster(1, EPI == ATT_CLUSTER ? md.kv_heads : 1, 1);
+  // $NEEDLE_B200_ATT_WIDE=N: the wide CTAs (G <= 2) for passes of at most N tokens
+  static const int wide_to = [] {
+    const char* e = std::getenv("NEEDLE_B200_ATT_WIDE");
+    return e ? std::atoi(e) : ATT_WIDE_MAX_TOKENS;
+  }();
   if constexpr (G <= 2) {
+    if (M <= wide_to) {
+      constexpr int W = ATT_WORKERS_WIDE;
+      const size_t smem = attend_smem(md, t_cap, W);
+      if (heads)
+        launch_clustered(k_attend<G, EPI, true, W>, grid, W + 32, smem, st, cluster, md, L, w, kv, M, layer, t_cap);
+      else
+        launch_clustered(k_attend<G, EPI, false, W>, grid, W + 32, smem, st, cluster, md, L, w, kv, M, layer, t_cap);
+      return;
+    }
     if (M >= narrow_from) {
       constexpr int W = ATT_WORKERS_NARROW;
       const size_t smem = attend_smem(md, t_cap, W);
